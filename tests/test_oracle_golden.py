@@ -1,0 +1,142 @@
+"""Pin the float64 oracle against golden vectors made by running the reference itself
+(tests/golden/make_golden.py): its Triton kernels under the CPU interpreter and its eager path.
+
+Tolerances: the reference's "float64" eager run still computes the controller projection and
+the write path in float32 (forward/control.py:131-163), and its Triton kernels run in float32,
+so agreement is expected at the float32 level, not float64. A formula error shows up as O(1).
+"""
+import numpy as np
+import pytest
+
+from oracle import sparc_oracle as O
+
+MIXER_CASES = ["mixer_b2_t64_w16", "mixer_b3_t37_w10", "mixer_b2_t96_w64_c32"]
+GRAD_NAMES = [k for k in O.PARAM_NAMES if k != "energy_response"]
+
+
+def _params(d):
+    return O.Params.from_mapping({k: d["p_" + k] for k in O.PARAM_NAMES})
+
+
+@pytest.mark.parametrize("name", MIXER_CASES)
+@pytest.mark.parametrize("src,tol", [("eager64", 2e-6), ("triton", 1e-5)])
+def test_mixer_forward_backward(golden, name, src, tol):
+    d = golden(name)
+    p = _params(d)
+    y, last, _ = O.sparc_forward(d["x"], p)
+    g = O.sparc_backward(d["x"], p, d["dy"])
+    assert O.rel_l2(y, d[src + "_y"]) < tol
+    assert O.rel_l2(g["x"], d[src + "_grad_x"]) < tol
+    for k in GRAD_NAMES:
+        assert O.rel_l2(g[k], d[src + "_grad_" + k]) < 3 * tol, k
+    assert np.all(g["energy_response"] == 0)
+    assert np.all(d[src + "_grad_energy_response"] == 0)
+
+
+@pytest.mark.parametrize("name", MIXER_CASES)
+def test_mixer_cache(golden, name):
+    d = golden(name)
+    _, last, _ = O.sparc_forward(d["x"], _params(d))
+    assert O.rel_l2(last[0], d["triton_cache_last_r"]) < 1e-5
+    assert O.rel_l2(last[1], d["triton_cache_last_i"]) < 1e-5
+
+
+def test_mixer_bf16_inputs(golden):
+    """bf16 activations: the oracle on the bf16 values matches the eager float64 run; the
+    reference's own bf16 Triton path sits within a few percent (its own rounding error)."""
+    d = golden("mixer_bf16_b2_t64_w32")
+    p = _params(d)
+    y, _, _ = O.sparc_forward(d["x"], p)
+    g = O.sparc_backward(d["x"], p, d["dy"])
+    assert O.rel_l2(y, d["eager64_y"]) < 2e-6
+    assert O.rel_l2(g["x"], d["eager64_grad_x"]) < 2e-6
+    assert O.rel_l2(y, d["triton_y"]) < 1e-2
+    assert O.rel_l2(g["x"], d["triton_grad_x"]) < 6e-2
+
+
+def test_decode(golden):
+    d = golden("decode")
+    p = _params(d)
+    st = (d["state0_r"], d["state0_i"])
+    ys = []
+    for s in range(d["xs"].shape[0]):
+        y, st = O.sparc_decode_step(d["xs"][s], p, st)
+        ys.append(y)
+    ys = np.stack(ys)
+    for src in ("fused", "eager"):
+        assert O.rel_l2(ys, d[src + "_ys"]) < 1e-5
+        assert O.rel_l2(st[0], d[src + "_last_r"]) < 1e-5
+        assert O.rel_l2(st[1], d[src + "_last_i"]) < 1e-5
+
+
+def test_decode_equals_sequence(golden):
+    """A chain of decode steps is the sequence scan of the stacked inputs."""
+    d = golden("decode")
+    p = _params(d)
+    xs = d["xs"]
+    st = (d["state0_r"], d["state0_i"])
+    ys = []
+    for s in range(xs.shape[0]):
+        y, st = O.sparc_decode_step(xs[s], p, st)
+        ys.append(y)
+    yseq, last, _ = O.sparc_forward(np.transpose(xs, (1, 0, 2)), p, h0=(d["state0_r"], d["state0_i"]))
+    np.testing.assert_allclose(np.transpose(np.stack(ys), (1, 0, 2)), yseq, rtol=0, atol=1e-12)
+    np.testing.assert_allclose(st[0], last[0], atol=1e-12)
+
+
+@pytest.mark.parametrize("src", ["chunk16", "serial"])
+def test_real_scan(golden, src):
+    d = golden("real")
+    out, last = O.real_scan_forward(d["a"], d["b"])
+    ga, gb = O.real_scan_backward(d["a"], d["b"], d["g"])
+    assert O.rel_l2(out, d[src + "_out"]) < 1e-6
+    assert O.rel_l2(ga, d[src + "_grad_a"]) < 1e-6
+    assert O.rel_l2(gb, d[src + "_grad_b"]) < 1e-6
+    assert O.rel_l2(last, d["with_last_last"]) < 1e-6
+
+
+def test_real_scan_bf16(golden):
+    d = golden("real")
+    out, _ = O.real_scan_forward(d["bf16_a"], d["bf16_b"])
+    ga, gb = O.real_scan_backward(d["bf16_a"], d["bf16_b"], d["g"])
+    assert O.rel_l2(out, d["bf16_chunk16_out"]) < 1e-2
+    assert O.rel_l2(ga, d["bf16_chunk16_grad_a"]) < 2e-2
+    assert O.rel_l2(gb, d["bf16_chunk16_grad_b"]) < 1e-2
+
+
+def test_h0_resets_and_grad_last(golden):
+    """h0, segment resets and grad of the last state, against _SPARCTiledSerialScan
+    (backward/scan.py:971-1070) run through the interpreter on the reference's own inputs."""
+    d = golden("tiled_h0_reset")
+    p = _params(d)
+    # the oracle's scan on the reference's own controls/writes
+    ar, ai, rho, z = O.transition(d["eta"], d["delta"], p)
+    reset = d["segment_pos"] == 0
+    hr, hi = O._scan(ar, ai, d["write_r"], d["write_i"], (d["h0_r"], d["h0_i"]), reset)
+    assert O.rel_l2(hr, d["out_r"]) < 1e-5 and O.rel_l2(hi, d["out_i"]) < 1e-5
+    assert O.rel_l2(hr[:, -1], d["last_r"]) < 1e-5
+    # the scan adjoint with h0, resets and grad_last
+    sc = O.scan_backward(d["eta"], d["delta"], p, hr, hi, d["d_out_r"], d["d_out_i"],
+                         h0=(d["h0_r"], d["h0_i"]), grad_last=(d["d_last_r"], d["d_last_i"]),
+                         reset=reset)
+    for mine, ref in (("lam_r", "grad_write_r"), ("lam_i", "grad_write_i"), ("eta", "grad_eta"),
+                      ("delta", "grad_delta"), ("nu_log", "grad_nu_log"),
+                      ("theta_log", "grad_theta_log"), ("h0_r", "grad_h0_r"), ("h0_i", "grad_h0_i")):
+        assert O.rel_l2(sc[mine], d[ref]) < 1e-5, mine
+    # the module-level forward with h0 and resets reproduces the reference states
+    _, last, S = O.sparc_forward(d["x"], p, h0=(d["h0_r"], d["h0_i"]), reset=reset)
+    assert O.rel_l2(S["hr"], d["out_r"]) < 1e-5 and O.rel_l2(S["hi"], d["out_i"]) < 1e-5
+
+
+def test_init_matches_reference(golden):
+    import torch
+
+    d = golden("init")
+    for W in (16, 64):
+        torch.manual_seed(0)
+        p = O.init_params(W, lambda n: torch.rand(n).numpy())
+        for k in O.PARAM_NAMES:
+            np.testing.assert_allclose(p[k], d[f"w{W}_{k}"], rtol=1e-6, atol=1e-7)
+    assert int(d["odd_raises"]) == 1
+    with pytest.raises(ValueError):
+        O.init_params(7, lambda n: np.zeros(n))
