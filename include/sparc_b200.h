@@ -1,0 +1,221 @@
+/*
+ * sparc_b200.h -- C ABI of the B200-native SPARC hot path (libsparc_b200.so).
+ *
+ * Plain pointers and sizes only. Every tensor pointer is a CUDA device pointer to a dense,
+ * row-major (last dimension fastest) array. Activations are float32 or bfloat16 (`dtype`);
+ * parameters, recurrent states and parameter gradients are float32. `stream` is a
+ * cudaStream_t passed as void*. All entry points only enqueue work on that stream (no host
+ * synchronisation) except sparc_read_status.
+ *
+ * Return value: SPARC_OK (0) or a negative SPARC_ERR_* code; sparc_last_error() then returns a
+ * message (thread-local). No entry point allocates memory: scratch comes from a caller-owned
+ * workspace whose size the *_workspace_bytes query returns. A workspace must be zero-filled
+ * once when it is allocated, and may then be reused by any number of launches that are
+ * ordered on one stream; calls that run concurrently need distinct workspaces.
+ *
+ * Chunk carries are passed between tiles by decoupled lookback; a tile composes whatever
+ * predecessor aggregates are ready, so the last bits of the carries (and of everything
+ * downstream) can vary run to run. With `deterministic` set a tile waits for its immediate
+ * predecessor's carry instead, which makes results bitwise reproducible. Parameter gradients
+ * are always reduced in a fixed order. Every wait is bounded by
+ * `max_spin` polls (0 selects the default, about a second); a wait that runs out sets the
+ * SPARC_STATUS_TIMEOUT bit in the workspace's status word, continues with a zero carry, and
+ * the launch still completes. sparc_read_status reads that word.
+ *
+ * Which reference interface each entry point replaces (paths inside Botwwt/sparc):
+ *   sparc_mixer_forward   SPARCMixer.forward -> run_sequence          sparc-kernal/sparc.py:90-91,
+ *                         forward/scan.py:1398-1603 (make_controls forward/control.py:129-139,
+ *                         latest_sparc_write backward/control.py:92-111,
+ *                         _SPARCChunkScan.forward backward/scan.py:1126-1372, cat+relu
+ *                         forward/scan.py:1598-1603; with return_cache the last state as in
+ *                         sparc_scan_with_last backward/scan.py:1857-1877; h0 as in
+ *                         _SPARCTiledSerialScan backward/scan.py:971-1070)
+ *   sparc_mixer_backward  autograd backward of the above: _SPARCChunkScan.backward
+ *                         backward/scan.py:1375-1640, _LatestSPARCWrite.backward
+ *                         backward/control.py:113-129, torch autograd of make_controls;
+ *                         grad of h0 / of the returned last state as in
+ *                         _SPARCTiledSerialScan.backward backward/scan.py:1034-1070
+ *   sparc_decode_step     SPARCMixer.step -> run_decode_step -> latest_sparc_decode
+ *                         sparc.py:122-123, forward/decode.py:273-306, 58-75 (kernel 11-55)
+ *   sparc_real_scan_forward   real_scan / real_chunk_scan / real_scan_with_last forward
+ *                         backward/scan.py:793-855, 1643-1650, 1821-1834
+ *   sparc_real_scan_backward  _RealScan.backward / _RealChunkScan.backward
+ *                         backward/scan.py:811-822, 857-884
+ */
+#ifndef SPARC_B200_H_
+#define SPARC_B200_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPARC_OK 0
+#define SPARC_ERR_ARG (-1)       /* null or inconsistent pointer arguments */
+#define SPARC_ERR_SHAPE (-2)     /* unsupported or invalid shape */
+#define SPARC_ERR_DTYPE (-3)     /* unsupported activation dtype */
+#define SPARC_ERR_WORKSPACE (-4) /* workspace missing or smaller than the query returned */
+#define SPARC_ERR_LAUNCH (-5)    /* CUDA launch / runtime error */
+
+#define SPARC_DTYPE_F32 0
+#define SPARC_DTYPE_BF16 1
+
+#define SPARC_STATUS_TIMEOUT 1u  /* a lookback wait ran out of polls */
+
+/* Forward of one SPARC mixer layer: y = relu([Re h, Im h]) for the recurrence
+ * h_t = a_t h_{t-1} + b_t over M = width/2 complex modes, with a_t, b_t computed from x_t
+ * and the parameters. `carry` receives the state at the end of every chunk of
+ * sparc_mixer_chunk_tokens() tokens ([batch, sparc_mixer_carry_chunks(length), M] complex,
+ * interleaved real/imag float32); the backward needs it. h0 (initial state) and last (final
+ * state) are optional pairs (NULL, NULL). */
+typedef struct SparcMixerFwdArgs {
+  const void* x;                       /* [batch, length, width]  activations (dtype) */
+  void* y;                             /* [batch, length, width]  output (dtype) */
+  const float* nu_log;                 /* [M] */
+  const float* theta_log;              /* [M] */
+  const float* phase_direction;        /* [width + 1] (last entry is the bias) */
+  const float* radial_direction;       /* [width + 1] */
+  const float* write_log_gain;         /* [M] */
+  const float* write_phase_response;   /* [M] */
+  const float* write_radial_response;  /* [M] */
+  const float* h0_r;                   /* [batch, M] or NULL */
+  const float* h0_i;                   /* [batch, M] or NULL */
+  float* last_r;                       /* [batch, M] or NULL */
+  float* last_i;                       /* [batch, M] or NULL */
+  float* carry;                        /* [batch, chunks, M, 2] */
+  void* workspace;
+  size_t workspace_bytes;
+  long long batch;
+  long long length;
+  int width;
+  int dtype;                           /* SPARC_DTYPE_* */
+  unsigned max_spin;                   /* 0 = default */
+  int deterministic;                   /* 1 = chained carries: bitwise reproducible, slower */
+  int inject_enable;                   /* test hook: 1 = tile inject_tile never publishes */
+  long long inject_tile;
+} SparcMixerFwdArgs;
+
+/* Backward of sparc_mixer_forward for the loss gradient dy on y (and optionally grad_last on
+ * the returned last state). Writes dx and every parameter gradient (energy_response's is 0:
+ * the reference multiplies that parameter by zero). Parameter gradients are reduced in a
+ * fixed order (deterministic run to run). */
+typedef struct SparcMixerBwdArgs {
+  const void* x;                       /* [batch, length, width] forward input (dtype) */
+  const void* dy;                      /* [batch, length, width] (dtype) */
+  void* dx;                            /* [batch, length, width] (dtype) */
+  const float* nu_log;
+  const float* theta_log;
+  const float* phase_direction;
+  const float* radial_direction;
+  const float* write_log_gain;
+  const float* write_phase_response;
+  const float* write_radial_response;
+  const float* h0_r;                   /* as given to the forward, or NULL */
+  const float* h0_i;
+  const float* grad_last_r;            /* [batch, M] or NULL */
+  const float* grad_last_i;
+  float* grad_h0_r;                    /* [batch, M] or NULL */
+  float* grad_h0_i;
+  const float* carry;                  /* the forward's carry output */
+  float* grad_nu_log;                  /* [M] */
+  float* grad_theta_log;               /* [M] */
+  float* grad_phase_direction;         /* [width + 1] */
+  float* grad_radial_direction;        /* [width + 1] */
+  float* grad_write_log_gain;          /* [M] */
+  float* grad_energy_response;         /* [M], written with zeros */
+  float* grad_write_phase_response;    /* [M] */
+  float* grad_write_radial_response;   /* [M] */
+  void* workspace;
+  size_t workspace_bytes;
+  long long batch;
+  long long length;
+  int width;
+  int dtype;
+  unsigned max_spin;
+  int deterministic;
+  int inject_enable;
+  long long inject_tile;
+} SparcMixerBwdArgs;
+
+/* One fused decode step (forward/decode.py:11-55): x [batch, width] (dtype), state
+ * [batch, M] float32 in; y [batch, width] (dtype), new state [batch, M] float32 out. The new
+ * state may not alias the old one. */
+typedef struct SparcDecodeArgs {
+  const void* x;
+  void* y;
+  const float* state_r;
+  const float* state_i;
+  float* new_state_r;
+  float* new_state_i;
+  const float* nu_log;
+  const float* theta_log;
+  const float* phase_direction;
+  const float* radial_direction;
+  const float* write_log_gain;
+  const float* write_phase_response;
+  const float* write_radial_response;
+  long long batch;
+  int width;
+  int dtype;
+} SparcDecodeArgs;
+
+/* Real diagonal scan h_t = a_t h_{t-1} + b_t over [batch, length, channels] (a, b, out in
+ * dtype; carries float32). `carry` ([batch, sparc_real_carry_chunks(length), channels]
+ * float32) receives the state at the end of each chunk for the backward; `last` ([batch,
+ * channels] float32) is optional. */
+typedef struct SparcRealFwdArgs {
+  const void* a;
+  const void* b;
+  void* out;
+  float* last;                         /* or NULL */
+  float* carry;
+  void* workspace;
+  size_t workspace_bytes;
+  long long batch;
+  long long length;
+  long long channels;
+  int dtype;
+  unsigned max_spin;
+} SparcRealFwdArgs;
+
+typedef struct SparcRealBwdArgs {
+  const void* a;
+  const void* b;
+  const void* grad_out;
+  const float* carry;                  /* the forward's carry output */
+  void* grad_a;
+  void* grad_b;
+  void* workspace;
+  size_t workspace_bytes;
+  long long batch;
+  long long length;
+  long long channels;
+  int dtype;
+  unsigned max_spin;
+} SparcRealBwdArgs;
+
+const char* sparc_last_error(void);
+
+long long sparc_mixer_chunk_tokens(void);
+long long sparc_mixer_carry_chunks(long long length);
+size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype);
+int sparc_mixer_forward(const SparcMixerFwdArgs* args, void* stream);
+int sparc_mixer_backward(const SparcMixerBwdArgs* args, void* stream);
+
+int sparc_decode_step(const SparcDecodeArgs* args, void* stream);
+
+long long sparc_real_carry_chunks(long long length);
+size_t sparc_real_workspace_bytes(long long batch, long long length, long long channels, int dtype);
+int sparc_real_scan_forward(const SparcRealFwdArgs* args, void* stream);
+int sparc_real_scan_backward(const SparcRealBwdArgs* args, void* stream);
+
+/* Status word of a workspace (SPARC_STATUS_* bits). Reads synchronise `stream`. */
+int sparc_read_status(const void* workspace, unsigned* status, void* stream);
+int sparc_clear_status(void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARC_B200_H_ */

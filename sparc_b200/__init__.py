@@ -1,0 +1,30 @@
+"""B200-native SPARC hot path: a drop-in for the reference ``sparc-kernal`` PyTorch API.
+
+    from sparc_b200 import SPARCMixer, real_scan, real_chunk_scan, real_scan_with_last
+
+All compute runs in the sm_100a kernels of ``libsparc_b200.so`` (C ABI in
+``include/sparc_b200.h``), loaded through ctypes on first use. There is no CPU path.
+"""
+from .mixer import SPARCMixer, sparc_decode_step, sparc_mixer
+from .real import real_chunk_scan, real_scan, real_scan_with_last
+from . import _lib
+
+
+def library_path() -> str:
+    return _lib.LIB_PATH
+
+
+def check_status(clear: bool = True) -> None:
+    """Raise if any kernel launch on a cached workspace recorded a lookback timeout.
+
+    Synchronises the streams that own the workspaces."""
+    for ws in _lib.WORKSPACES.all():
+        st = _lib.read_status(ws)
+        if st:
+            if clear:
+                _lib.clear_status(ws)
+            raise RuntimeError(f"sparc_b200: a chunk-carry wait timed out (status {st:#x})")
+
+
+__all__ = ["SPARCMixer", "sparc_mixer", "sparc_decode_step", "real_scan", "real_chunk_scan",
+           "real_scan_with_last", "check_status", "library_path"]

@@ -1,0 +1,197 @@
+"""ctypes binding of libsparc_b200.so (the C ABI declared in include/sparc_b200.h).
+
+This is the only place Python touches the library. Tensors cross the boundary as raw device
+pointers (``tensor.data_ptr()``) and the current CUDA stream as a ``cudaStream_t`` handle.
+There is no fallback: if the library or a CUDA device is missing, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libsparc_b200.so")
+
+OK = 0
+ERR_NAMES = {-1: "bad argument", -2: "bad shape", -3: "bad dtype", -4: "workspace", -5: "launch"}
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+STATUS_TIMEOUT = 1
+
+_vp = ctypes.c_void_p
+_ll = ctypes.c_longlong
+
+
+class MixerFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("y", _vp),
+        ("nu_log", _vp), ("theta_log", _vp), ("phase_direction", _vp), ("radial_direction", _vp),
+        ("write_log_gain", _vp), ("write_phase_response", _vp), ("write_radial_response", _vp),
+        ("h0_r", _vp), ("h0_i", _vp), ("last_r", _vp), ("last_i", _vp), ("carry", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
+        ("max_spin", ctypes.c_uint), ("deterministic", ctypes.c_int),
+        ("inject_enable", ctypes.c_int), ("inject_tile", _ll),
+    ]
+
+
+class MixerBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("dy", _vp), ("dx", _vp),
+        ("nu_log", _vp), ("theta_log", _vp), ("phase_direction", _vp), ("radial_direction", _vp),
+        ("write_log_gain", _vp), ("write_phase_response", _vp), ("write_radial_response", _vp),
+        ("h0_r", _vp), ("h0_i", _vp), ("grad_last_r", _vp), ("grad_last_i", _vp),
+        ("grad_h0_r", _vp), ("grad_h0_i", _vp), ("carry", _vp),
+        ("grad_nu_log", _vp), ("grad_theta_log", _vp), ("grad_phase_direction", _vp),
+        ("grad_radial_direction", _vp), ("grad_write_log_gain", _vp), ("grad_energy_response", _vp),
+        ("grad_write_phase_response", _vp), ("grad_write_radial_response", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
+        ("max_spin", ctypes.c_uint), ("deterministic", ctypes.c_int),
+        ("inject_enable", ctypes.c_int), ("inject_tile", _ll),
+    ]
+
+
+class DecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("y", _vp), ("state_r", _vp), ("state_i", _vp),
+        ("new_state_r", _vp), ("new_state_i", _vp),
+        ("nu_log", _vp), ("theta_log", _vp), ("phase_direction", _vp), ("radial_direction", _vp),
+        ("write_log_gain", _vp), ("write_phase_response", _vp), ("write_radial_response", _vp),
+        ("batch", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
+    ]
+
+
+class RealFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("a", _vp), ("b", _vp), ("out", _vp), ("last", _vp), ("carry", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("batch", _ll), ("length", _ll), ("channels", _ll), ("dtype", ctypes.c_int),
+        ("max_spin", ctypes.c_uint),
+    ]
+
+
+class RealBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("a", _vp), ("b", _vp), ("grad_out", _vp), ("carry", _vp), ("grad_a", _vp), ("grad_b", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("batch", _ll), ("length", _ll), ("channels", _ll), ("dtype", ctypes.c_int),
+        ("max_spin", ctypes.c_uint),
+    ]
+
+
+# every symbol declared in include/sparc_b200.h, with its ctypes signature
+SIGNATURES = {
+    "sparc_last_error": (ctypes.c_char_p, []),
+    "sparc_mixer_chunk_tokens": (_ll, []),
+    "sparc_mixer_carry_chunks": (_ll, [_ll]),
+    "sparc_mixer_workspace_bytes": (ctypes.c_size_t, [_ll, _ll, ctypes.c_int, ctypes.c_int]),
+    "sparc_mixer_forward": (ctypes.c_int, [ctypes.POINTER(MixerFwdArgs), _vp]),
+    "sparc_mixer_backward": (ctypes.c_int, [ctypes.POINTER(MixerBwdArgs), _vp]),
+    "sparc_decode_step": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
+    "sparc_real_carry_chunks": (_ll, [_ll]),
+    "sparc_real_workspace_bytes": (ctypes.c_size_t, [_ll, _ll, _ll, ctypes.c_int]),
+    "sparc_real_scan_forward": (ctypes.c_int, [ctypes.POINTER(RealFwdArgs), _vp]),
+    "sparc_real_scan_backward": (ctypes.c_int, [ctypes.POINTER(RealBwdArgs), _vp]),
+    "sparc_read_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint), _vp]),
+    "sparc_clear_status": (ctypes.c_int, [_vp, _vp]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library(path: str = LIB_PATH):
+    """Load (once) and return the CDLL. Raises if the library is missing."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(path):
+                raise RuntimeError(
+                    f"{path} is missing: build it with `python -m sparc_b200._build` "
+                    "(there is no CPU or Python fallback for the SPARC kernels)")
+            lib = ctypes.CDLL(path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def lib():
+    return load_library()
+
+
+def check(rc: int, what: str):
+    if rc != OK:
+        msg = lib().sparc_last_error()
+        msg = msg.decode() if msg else ""
+        raise RuntimeError(f"{what} failed ({ERR_NAMES.get(rc, rc)}): {msg}")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return DTYPE_F32
+    if dtype == torch.bfloat16:
+        return DTYPE_BF16
+    raise TypeError(f"sparc_b200 supports float32 and bfloat16 activations, got {dtype}")
+
+
+def require_cuda(t: torch.Tensor, name: str):
+    if not t.is_cuda:
+        raise RuntimeError(f"sparc_b200: {name} must be a CUDA tensor (there is no CPU path)")
+
+
+def deterministic() -> int:
+    """Chained (bitwise reproducible) chunk carries when torch's deterministic mode is on."""
+    return 1 if torch.are_deterministic_algorithms_enabled() else 0
+
+
+def ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _Workspaces:
+    """Zero-initialised scratch per (device, stream), grown on demand.
+
+    The library keeps its launch counters and lookback flags in the workspace, so one is
+    reused across launches on a stream; concurrent streams get their own."""
+
+    def __init__(self):
+        self._ws = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < nbytes:
+            size = max(nbytes, 1 << 20)
+            if ws is not None:
+                size = max(size, int(ws.numel() * 1.25))
+            ws = torch.zeros(size, dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
+
+    def all(self):
+        return list(self._ws.values())
+
+
+WORKSPACES = _Workspaces()
+
+
+def read_status(ws: torch.Tensor) -> int:
+    st = ctypes.c_uint(0)
+    check(lib().sparc_read_status(ws.data_ptr(), ctypes.byref(st), stream_handle(ws.device)),
+          "sparc_read_status")
+    return int(st.value)
+
+
+def clear_status(ws: torch.Tensor):
+    check(lib().sparc_clear_status(ws.data_ptr(), stream_handle(ws.device)), "sparc_clear_status")

@@ -1,0 +1,187 @@
+// Shared device helpers for the SPARC B200 kernels (sm_100a).
+//
+// * Activation I/O types (float / bfloat16) converted to float in registers.
+// * Transcendentals. The hardware approximations (ex2/rcp/sqrt/tanh .approx PTX
+//   instructions, documented in the PTX ISA) are used directly; the two functions that need
+//   more care are built here from textbook series:
+//     - tanh for |x| < 1/2 from its Maclaurin series (coefficients from the Bernoulli
+//       numbers, 2^{2n}(2^{2n}-1)B_{2n}/(2n)!), else 1 - 2/(e^{2|x|}+1);
+//     - -expm1(-u) for u < 1/4 from its Maclaurin series u - u^2/2 + u^3/6 - ...;
+//     - sin/cos on [-pi/2, pi/2] from their Maclaurin series (no range reduction needed:
+//       the per-token phase offset (1-rho)*delta is bounded by pi/2 in magnitude).
+// * Decoupled-lookback flags: a 32-bit word = (epoch << 2) | state. The epoch is bumped by
+//   the last CTA of every launch, so flags never need clearing between launches. Every wait
+//   is bounded; on timeout the kernel records an error bit in the launch status word and
+//   continues with a zero carry, so the launch still terminates.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sparc {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn16 = 2.772588722239781f;
+constexpr float kHalfPi = 1.5707963267948966f;
+constexpr float kInvLn16 = 0.36067376022224085f;   // 1 / ln 16
+constexpr float kInvHalfPi = 0.6366197723675814f;  // 2 / pi
+
+// ---------------------------------------------------------------- I/O types
+template <typename T> struct Io;
+template <> struct Io<float> {
+  static __device__ __forceinline__ float load(const float* p) { return __ldg(p); }
+  static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+};
+template <> struct Io<__nv_bfloat16> {
+  static __device__ __forceinline__ float load(const __nv_bfloat16* p) {
+    return __bfloat162float(__ldg(p));
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, float v) {
+    *p = __float2bfloat16_rn(v);
+  }
+};
+
+// ---------------------------------------------------------------- math
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// tanh accurate to a few float32 ulp: Maclaurin series below 1/2, exponential form above.
+__device__ __forceinline__ float tanh_accurate(float x) {
+  const float ax = fabsf(x);
+  const float e = ex2_approx(2.0f * kLog2e * ax);
+  const float big = 1.0f - 2.0f * rcp_approx(e + 1.0f);
+  const float x2 = x * x;
+  // 1, -1/3, 2/15, -17/315, 62/2835, -1382/155925, 21844/6081075, -929569/638512875
+  float p = -1.4558343870513183e-3f;
+  p = fmaf(p, x2, 3.5921280365724810e-3f);
+  p = fmaf(p, x2, -8.8632355299021966e-3f);
+  p = fmaf(p, x2, 2.1869488536155203e-2f);
+  p = fmaf(p, x2, -5.3968253968253968e-2f);
+  p = fmaf(p, x2, 1.3333333333333333e-1f);
+  p = fmaf(p, x2, -3.3333333333333333e-1f);
+  const float small = fmaf(p * x2, x, x);
+  return ax < 0.5f ? small : copysignf(big, x);
+}
+
+template <bool kFast>
+__device__ __forceinline__ float tanh_t(float x) {
+  if constexpr (kFast) return tanh_hw(x);
+  else return tanh_accurate(x);
+}
+
+// -expm1(-u) = 1 - e^{-u} for u >= 0, given w = e^{-u}. Series below 1/4 (cancellation-free).
+__device__ __forceinline__ float one_minus_exp_neg(float u, float w) {
+  // u - u^2/2 + u^3/6 - u^4/24 + u^5/120 - u^6/720
+  float p = -1.3888888888888889e-3f;
+  p = fmaf(p, u, 8.3333333333333333e-3f);
+  p = fmaf(p, u, -4.1666666666666667e-2f);
+  p = fmaf(p, u, 1.6666666666666667e-1f);
+  p = fmaf(p, u, -0.5f);
+  p = fmaf(p, u, 1.0f);
+  const float small = p * u;
+  return u < 0.25f ? small : 1.0f - w;
+}
+
+// sin and cos of |x| <= pi/2 (Maclaurin series through x^13 / x^12).
+__device__ __forceinline__ void sincos_halfpi(float x, float* s, float* c) {
+  const float x2 = x * x;
+  float ps = 1.6059043836821615e-10f;         // 1/13!
+  ps = fmaf(ps, x2, -2.5052108385441720e-8f);  // -1/11!
+  ps = fmaf(ps, x2, 2.7557319223985893e-6f);   // 1/9!
+  ps = fmaf(ps, x2, -1.9841269841269841e-4f);  // -1/7!
+  ps = fmaf(ps, x2, 8.3333333333333333e-3f);   // 1/5!
+  ps = fmaf(ps, x2, -1.6666666666666667e-1f);  // -1/3!
+  *s = fmaf(ps * x2, x, x);
+  float pc = 2.0876756987868099e-9f;           // 1/12!
+  pc = fmaf(pc, x2, -2.7557319223985891e-7f);  // -1/10!
+  pc = fmaf(pc, x2, 2.4801587301587302e-5f);   // 1/8!
+  pc = fmaf(pc, x2, -1.3888888888888889e-3f);  // -1/6!
+  pc = fmaf(pc, x2, 4.1666666666666667e-2f);   // 1/4!
+  pc = fmaf(pc, x2, -0.5f);
+  *c = fmaf(pc, x2, 1.0f);
+}
+
+// ---------------------------------------------------------------- launch state + lookback
+struct LaunchState {
+  unsigned epoch;   // bumped by the last CTA of each launch
+  unsigned ticket;  // dynamic tile counter, reset by the last CTA
+  unsigned done;    // CTAs finished in this launch
+  unsigned status;  // sticky error bits (kStatusTimeout ...)
+  unsigned pad[60];
+};
+static_assert(sizeof(LaunchState) == 256, "launch state is one 256-byte line");
+
+constexpr unsigned kStatusTimeout = 1u;
+constexpr unsigned kFlagAggregate = 1u;
+constexpr unsigned kFlagInclusive = 2u;
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Spin (bounded) until the flag carries this epoch and a state >= min_state. Returns the
+// state, or 0 after `max_spin` polls (the caller then records a timeout).
+__device__ __forceinline__ unsigned wait_flag(const unsigned* flag, unsigned epoch,
+                                              unsigned max_spin, unsigned min_state = 1u) {
+  for (unsigned it = 0; it < max_spin; ++it) {
+    const unsigned v = ld_acquire(flag);
+    if ((v >> 2) == (epoch & 0x3fffffffu) && (v & 3u) >= min_state) return v & 3u;
+    if (it > 8) __nanosleep(it < 64 ? 32 : 256);
+  }
+  return 0u;
+}
+
+__device__ __forceinline__ unsigned make_flag(unsigned epoch, unsigned state) {
+  return ((epoch & 0x3fffffffu) << 2) | state;
+}
+
+// Called once per CTA at the very end of a persistent kernel: the last CTA resets the ticket
+// and bumps the epoch so the next launch on this workspace starts clean.
+__device__ __forceinline__ void finish_launch(LaunchState* ls) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    const unsigned prev = atomicAdd(&ls->done, 1u);
+    if (prev == total - 1u) {
+      ls->ticket = 0u;
+      ls->done = 0u;
+      __threadfence();
+      atomicAdd(&ls->epoch, 1u);
+    }
+  }
+}
+
+// Complex helpers on float2 (x = real, y = imag).
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
+}
+__device__ __forceinline__ float2 cfma(float2 a, float2 b, float2 c) {  // a*b + c
+  return make_float2(fmaf(a.x, b.x, fmaf(-a.y, b.y, c.x)), fmaf(a.x, b.y, fmaf(a.y, b.x, c.y)));
+}
+
+}  // namespace sparc

@@ -1,0 +1,997 @@
+// SPARC mixer forward / backward for B200 (sm_100a).
+//
+// Work unit ("tile"): one batch row b and one chunk of C consecutive tokens, all M modes.
+// A tile is processed by one thread-block cluster of G CTAs; CTA g owns modes
+// [g*NT, g*NT + NT) with one thread per mode, so the cross-mode per-token reductions
+// (controller projection in the forward, the shared-control gradient in the backward) run
+// on-chip: warp transpose-reduce -> shared memory -> distributed shared memory across the
+// cluster.
+//
+// Kernels are persistent: clusters take tiles from a ticket counter in chunk-major order
+// (ticket = c*B + b forward, (chunks-1-c)*B + b backward), so a tile only ever waits on tiles
+// with smaller tickets, which are held by running clusters. Chunk carries are passed by
+// decoupled lookback: a tile publishes its aggregate affine map (A, B: out = A*in + B, per
+// mode) and, once it knows its carry-in, its inclusive state; successors compose aggregates
+// until they reach an inclusive state. The forward's inclusive states double as the saved
+// chunk carries that the backward replays from.
+//
+// Parity targets (reference paths inside Botwwt/sparc):
+//   controls  forward/control.py:129-139      write  forward/control.py:167-195
+//   scan      forward/scan.py:886-1003,1277-1354  (chunk summary / prefix / replay)
+//   backward  backward/scan.py:382-644 (reverse chunk kernels), backward/control.py:11-89
+//             (write backward), autograd of make_controls for the controller gradient.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "sparc_b200.h"
+
+namespace cg = cooperative_groups;
+
+namespace sparc {
+
+constexpr int kChunk = 16;  // tokens per tile; the carry layout depends on it
+
+struct ModeConst {
+  float nu;      // e^{nu_log}
+  float nl2e;    // nu * log2(e)
+  float ct, st;  // cos/sin theta
+  float theta;
+  float gconst;  // e^{write_log_gain} / sqrt(-expm1(-2 nu))
+  float stat;    // nu e^{-2nu} / -expm1(-2nu)
+  float wpr, wrr;
+  float d0r, d0i, d1r, d1i;  // controller directions at columns m and M+m
+};
+
+struct MixerParamPtrs {
+  const float* nu_log;
+  const float* theta_log;
+  const float* phase_dir;   // [W+1]
+  const float* radial_dir;  // [W+1]
+  const float* wlg;
+  const float* wpr;
+  const float* wrr;
+};
+
+__device__ __forceinline__ ModeConst load_mode(const MixerParamPtrs& pp, int m, int M, bool active) {
+  ModeConst mc;
+  const float nu_log = active ? pp.nu_log[m] : 0.0f;
+  const float theta_log = active ? pp.theta_log[m] : 0.0f;
+  mc.nu = expf(nu_log);
+  mc.nl2e = mc.nu * kLog2e;
+  mc.theta = expf(theta_log);
+  sincosf(mc.theta, &mc.st, &mc.ct);
+  const float den = -expm1f(-2.0f * mc.nu);
+  mc.gconst = active ? expf(pp.wlg[m]) * rsqrtf(den) : 0.0f;
+  mc.stat = mc.nu * expf(-2.0f * mc.nu) / den;
+  mc.wpr = active ? pp.wpr[m] : 0.0f;
+  mc.wrr = active ? pp.wrr[m] : 0.0f;
+  mc.d0r = active ? pp.phase_dir[m] : 0.0f;
+  mc.d0i = active ? pp.phase_dir[M + m] : 0.0f;
+  mc.d1r = active ? pp.radial_dir[m] : 0.0f;
+  mc.d1i = active ? pp.radial_dir[M + m] : 0.0f;
+  return mc;
+}
+
+struct TokenCoef {  // per-(token, mode) quantities shared by the forward and the backward
+  float z, rho;
+  float2 a;
+  float num, gate, gain;
+};
+
+template <bool kFast>
+__device__ __forceinline__ TokenCoef token_coef(const ModeConst& mc, float E, float delta,
+                                                float tau0, float tau1) {
+  TokenCoef k;
+  k.z = mc.nu * E;
+  k.rho = ex2_approx(-mc.nl2e * E);
+  float s, c;
+  sincos_halfpi(fmaf(-k.rho, delta, delta), &s, &c);  // (1 - rho) * delta, |.| <= pi/2
+  const float rct = k.rho * mc.ct, rst = k.rho * mc.st;
+  k.a = make_float2(fmaf(rct, c, -rst * s), fmaf(rst, c, rct * s));
+  k.num = one_minus_exp_neg(2.0f * k.z, k.rho * k.rho);
+  const float q = fmaf(tau0, mc.wpr, tau1 * mc.wrr);
+  if constexpr (kFast) {
+    k.gate = 1.0f + tanh_hw(0.5f * q);
+  } else {
+    k.gate = 2.0f * rcp_approx(1.0f + ex2_approx(-kLog2e * q));
+  }
+  k.gain = mc.gconst * sqrt_approx(k.num) * k.gate;
+  return k;
+}
+
+// Warp transpose-reduce of N values per lane (N a power of two, N <= 32). Afterwards lane l
+// holds the warp total of value l >> (5 - log2 N).
+template <int N>
+__device__ __forceinline__ float transpose_reduce(float (&v)[N], int lane) {
+  static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "N must be a power of two <= 32");
+  int n = N;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (n > 1) {
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) {
+        if (i < n / 2) {
+          const float send = upper ? v[i] : v[i + n / 2];
+          const float keep = upper ? v[i + n / 2] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      n >>= 1;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+  return v[0];
+}
+
+template <int N>
+__host__ __device__ constexpr int log2i() { return N <= 1 ? 0 : 1 + log2i<N / 2>(); }
+
+// Reduce N per-thread values over the whole cluster. Every CTA ends with the cluster totals
+// in out[0..N) (shared memory). s_warp: [NW][N], s_cta: [N] (peers read it).
+template <int N, int NT>
+__device__ __forceinline__ void cluster_reduce(float (&v)[N], float (*s_warp)[N], float* s_cta,
+                                               float* out, cg::cluster_group& cluster) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kShift = 5 - log2i<N>();
+  const float total = transpose_reduce<N>(v, lane);
+  if ((lane & ((1 << kShift) - 1)) == 0) s_warp[warp][lane >> kShift] = total;
+  __syncthreads();
+  if (threadIdx.x < N) {
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) s += s_warp[w][threadIdx.x];
+    s_cta[threadIdx.x] = s;
+  }
+  cluster.sync();
+  if (threadIdx.x < N) {
+    float s = 0.0f;
+    const unsigned G = cluster.num_blocks();
+    for (unsigned r = 0; r < G; ++r) s += cluster.map_shared_rank(s_cta, r)[threadIdx.x];
+    out[threadIdx.x] = s;
+  }
+  __syncthreads();
+}
+
+// Token controls from the reduced projections: eta, delta, e^eta, tanh values.
+template <int C>
+__device__ __forceinline__ void token_controls(const float* proj, float b0, float b1, float* s_E,
+                                               float* s_delta, float* s_tau0, float* s_tau1) {
+  if (threadIdx.x < C) {
+    const int t = threadIdx.x;
+    const float tau0 = tanh_accurate(proj[t] + b0);
+    const float tau1 = tanh_accurate(proj[C + t] + b1);
+    s_tau0[t] = tau0;
+    s_tau1[t] = tau1;
+    s_delta[t] = kHalfPi * tau0;
+    s_E[t] = expf(kLn16 * tau1);
+  }
+  __syncthreads();
+}
+
+// Decoupled lookback. The tile publishes `agg` (out = A*in + B) unless its predecessor is
+// already inclusive, walks back composing aggregates, and returns the carry-in.
+// pred_inclusive(j) loads the inclusive state of the tile `j` steps back.
+// Deterministic mode waits for the immediate predecessor's inclusive state instead (a chained
+// scan), so the carry's rounding does not depend on which predecessors were done first.
+struct LookbackCtx {
+  LaunchState* ls;
+  unsigned* flags;     // [tiles * G]
+  float4* agg;         // [tiles * Mp]
+  unsigned epoch;
+  unsigned max_spin;
+  int G;
+  int Mp;
+  long long B;         // ticket distance to the predecessor tile
+  bool deterministic;
+};
+
+template <typename InclFn>
+__device__ __forceinline__ float2 lookback(const LookbackCtx& lc, long long ticket, int g,
+                                           int steps_back_max, float2 A, float2 Bv, bool publish,
+                                           unsigned* s_state, InclFn pred_inclusive) {
+  const int tid = threadIdx.x;
+  const int mp = g * blockDim.x + tid;
+  long long pred = ticket - lc.B;
+  if (lc.deterministic) {
+    if (tid == 0) {
+      unsigned s = wait_flag(lc.flags + pred * lc.G + g, lc.epoch, lc.max_spin, kFlagInclusive);
+      if (s == 0u) atomicOr(&lc.ls->status, kStatusTimeout);
+      s_state[0] = s;
+    }
+    __syncthreads();
+    const unsigned state = s_state[0];
+    __syncthreads();
+    return state == kFlagInclusive ? pred_inclusive(1) : make_float2(0.0f, 0.0f);
+  }
+  if (tid == 0) s_state[0] = ld_acquire(lc.flags + pred * lc.G + g);
+  __syncthreads();
+  unsigned st = s_state[0];
+  const bool pred_ready = ((st >> 2) == (lc.epoch & 0x3fffffffu)) && (st & 3u) == kFlagInclusive;
+  if (!pred_ready && publish) {
+    lc.agg[ticket * lc.Mp + mp] = make_float4(A.x, A.y, Bv.x, Bv.y);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release(lc.flags + ticket * lc.G + g, make_flag(lc.epoch, kFlagAggregate));
+  }
+  float2 accA = make_float2(1.0f, 0.0f), accB = make_float2(0.0f, 0.0f);
+  for (int j = 1;; ++j) {
+    unsigned state;
+    if (j == 1 && pred_ready) {
+      state = kFlagInclusive;
+    } else {
+      if (tid == 0) {
+        unsigned s = wait_flag(lc.flags + pred * lc.G + g, lc.epoch, lc.max_spin);
+        if (s == 0u) atomicOr(&lc.ls->status, kStatusTimeout);
+        s_state[j & 1] = s;
+      }
+      __syncthreads();
+      state = s_state[j & 1];
+    }
+    if (state == kFlagInclusive) {
+      const float2 h = pred_inclusive(j);
+      return cfma(accA, h, accB);
+    }
+    if (state != kFlagAggregate || j >= steps_back_max) return accB;  // timeout: zero carry
+    const float4 ag = __ldcg(lc.agg + pred * lc.Mp + mp);
+    accB = cfma(accA, make_float2(ag.z, ag.w), accB);
+    accA = cmul(accA, make_float2(ag.x, ag.y));
+    pred -= lc.B;
+  }
+}
+
+// ------------------------------------------------------------------------------ forward
+struct FwdParams {
+  const void* x;
+  void* y;
+  MixerParamPtrs pp;
+  const float* h0_r;
+  const float* h0_i;
+  float* last_r;
+  float* last_i;
+  float2* carry;  // [B, chunks, M]
+  LaunchState* ls;
+  unsigned* flags;
+  float4* agg;
+  long long B, T;
+  int W, M, chunks;
+  long long tiles;
+  unsigned max_spin;
+  int deterministic;
+  long long inject_unpublished;
+};
+
+template <typename TIO, int NT, bool kFast>
+__global__ void __launch_bounds__(NT) mixer_fwd_kernel(const FwdParams p) {
+  constexpr int C = kChunk;
+  constexpr int NW = NT / 32;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int g = (int)cluster.block_rank();
+  const int G = (int)cluster.num_blocks();
+  const int tid = threadIdx.x;
+  const int M = p.M, W = p.W;
+  const int m = g * NT + tid;
+  const bool active = m < M;
+  const long long B = p.B, T = p.T;
+
+  __shared__ float s_warp[NW][2 * C];
+  __shared__ float s_cta[2 * C];
+  __shared__ float s_proj[2 * C];
+  __shared__ float s_E[C], s_delta[C], s_tau0[C], s_tau1[C];
+  __shared__ unsigned s_ticket;
+  __shared__ unsigned s_state[2];
+
+  const ModeConst mc = load_mode(p.pp, m, M, active);
+  const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
+  LookbackCtx lc{p.ls, p.flags, p.agg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, G, G * NT, B,
+                 p.deterministic != 0};
+
+  for (;;) {
+    if (g == 0 && tid == 0) s_ticket = atomicAdd(&p.ls->ticket, 1u);
+    cluster.sync();
+    const long long ticket = *cluster.map_shared_rank(&s_ticket, 0);
+    if (ticket >= p.tiles) {
+      cluster.sync();
+      break;
+    }
+    const long long b = ticket % B;
+    const int c = (int)(ticket / B);
+    const long long t0 = (long long)c * C;
+    const int nvalid = (int)(T - t0 < C ? T - t0 : C);
+    const TIO* xrow = static_cast<const TIO*>(p.x) + (b * T + t0) * W;
+
+    float xr[C], xi[C], v[2 * C];
+#pragma unroll
+    for (int t = 0; t < C; ++t) {
+      const bool ok = active && t < nvalid;
+      xr[t] = ok ? Io<TIO>::load(xrow + (long long)t * W + m) : 0.0f;
+      xi[t] = ok ? Io<TIO>::load(xrow + (long long)t * W + M + m) : 0.0f;
+      v[t] = fmaf(xr[t], mc.d0r, xi[t] * mc.d0i);
+      v[C + t] = fmaf(xr[t], mc.d1r, xi[t] * mc.d1i);
+    }
+    cluster_reduce<2 * C, NT>(v, s_warp, s_cta, s_proj, cluster);
+    token_controls<C>(s_proj, bias0, bias1, s_E, s_delta, s_tau0, s_tau1);
+
+    // pass 1: per-step transition and write, local state from zero, chunk product
+    float2 a[C], bw[C];
+    float2 P = make_float2(1.0f, 0.0f), Q = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int t = 0; t < C; ++t) {
+      if (t < nvalid) {
+        const TokenCoef k = token_coef<kFast>(mc, s_E[t], s_delta[t], s_tau0[t], s_tau1[t]);
+        a[t] = k.a;
+        bw[t] = make_float2(k.gain * tanh_t<kFast>(xr[t]), k.gain * tanh_t<kFast>(xi[t]));
+      } else {
+        a[t] = make_float2(1.0f, 0.0f);
+        bw[t] = make_float2(0.0f, 0.0f);
+      }
+      Q = cfma(a[t], Q, bw[t]);
+      P = cmul(a[t], P);
+    }
+
+    // chunk carry
+    float2 hin = make_float2(0.0f, 0.0f);
+    if (c == 0) {
+      if (p.h0_r != nullptr && active) hin = make_float2(p.h0_r[b * M + m], p.h0_i[b * M + m]);
+    } else {
+      const float2* carry = p.carry;
+      const int chunks = p.chunks;
+      hin = lookback(lc, ticket, g, c, P, Q, ticket != p.inject_unpublished, s_state, [&](int j) {
+        return active ? __ldcg(carry + (b * chunks + (c - j)) * M + m) : make_float2(0.0f, 0.0f);
+      });
+    }
+    const float2 hout = cfma(P, hin, Q);
+    if (ticket != p.inject_unpublished) {
+      if (active) p.carry[(b * p.chunks + c) * M + m] = hout;
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) st_release(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
+    }
+
+    // pass 2: replay from the carry, relu output
+    TIO* yrow = static_cast<TIO*>(p.y) + (b * T + t0) * W;
+    float2 h = hin;
+#pragma unroll
+    for (int t = 0; t < C; ++t) {
+      h = cfma(a[t], h, bw[t]);
+      if (active && t < nvalid) {
+        Io<TIO>::store(yrow + (long long)t * W + m, fmaxf(h.x, 0.0f));
+        Io<TIO>::store(yrow + (long long)t * W + M + m, fmaxf(h.y, 0.0f));
+      }
+    }
+    if (c == p.chunks - 1 && p.last_r != nullptr && active) {
+      p.last_r[b * M + m] = hout.x;
+      p.last_i[b * M + m] = hout.y;
+    }
+  }
+  finish_launch(p.ls);
+}
+
+// ------------------------------------------------------------------------------ backward
+constexpr int kPartModes = 9;  // nu, theta (sum of phase grads), wlg, wpr, wrr, D0r, D0i, D1r, D1i
+
+struct BwdParams {
+  const void* x;
+  const void* dy;
+  void* dx;
+  MixerParamPtrs pp;
+  const float* h0_r;
+  const float* h0_i;
+  const float* glast_r;
+  const float* glast_i;
+  float* gh0_r;
+  float* gh0_i;
+  const float2* carry;  // forward inclusive states [B, chunks, M]
+  LaunchState* ls;
+  unsigned* flags;
+  float4* agg;
+  float2* incl;         // reverse inclusive carries [tiles, Mp]
+  double* part;         // [clusters][kPartModes][Mp] then [clusters][2] bias partials
+  long long B, T;
+  int W, M, chunks;
+  long long tiles;
+  unsigned max_spin;
+  int deterministic;
+  long long inject_unpublished;
+};
+
+template <int C, int NT>
+struct BwdSmem {
+  float xr[C][NT], xi[C][NT];
+  float gr[C][NT], gi[C][NT];  // masked dy, later reused for nothing
+  float hr[C][NT], hi[C][NT];  // replayed states
+  float ar[C][NT], ai[C][NT];  // transitions, overwritten by the write-path dx
+};
+
+template <typename TIO, int NT, bool kFast>
+__global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
+  constexpr int C = kChunk;
+  constexpr int NW = NT / 32;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int g = (int)cluster.block_rank();
+  const int G = (int)cluster.num_blocks();
+  const int tid = threadIdx.x;
+  const int M = p.M, W = p.W;
+  const int m = g * NT + tid;
+  const int Mp = G * NT;
+  const bool active = m < M;
+  const long long B = p.B, T = p.T;
+  const int chunks = p.chunks;
+
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  BwdSmem<C, NT>& S = *reinterpret_cast<BwdSmem<C, NT>*>(smem_raw);
+  __shared__ float s_warp[NW][2 * C];
+  __shared__ float s_cta_ctl[2 * C];
+  __shared__ float s_cta_grad[2 * C];
+  __shared__ float s_proj[2 * C];
+  __shared__ float s_tot[2 * C];
+  __shared__ float s_E[C], s_delta[C], s_tau0[C], s_tau1[C], s_dp0[C], s_dp1[C];
+  __shared__ unsigned s_ticket;
+  __shared__ unsigned s_state[2];
+
+  const ModeConst mc = load_mode(p.pp, m, M, active);
+  const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
+  LookbackCtx lc{p.ls, p.flags, p.agg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, G, Mp, B,
+                 p.deterministic != 0};
+
+  double acc_nu = 0.0, acc_th = 0.0, acc_wlg = 0.0, acc_wpr = 0.0, acc_wrr = 0.0;
+  double acc_d0r = 0.0, acc_d0i = 0.0, acc_d1r = 0.0, acc_d1i = 0.0;
+  double acc_b0 = 0.0, acc_b1 = 0.0;
+
+  for (;;) {
+    if (g == 0 && tid == 0) s_ticket = atomicAdd(&p.ls->ticket, 1u);
+    cluster.sync();
+    const long long ticket = *cluster.map_shared_rank(&s_ticket, 0);
+    if (ticket >= p.tiles) {
+      cluster.sync();
+      break;
+    }
+    const long long b = ticket % B;
+    const int c = chunks - 1 - (int)(ticket / B);
+    const long long t0 = (long long)c * C;
+    const int nvalid = (int)(T - t0 < C ? T - t0 : C);
+    const long long row0 = (b * T + t0) * W;
+    const TIO* xrow = static_cast<const TIO*>(p.x) + row0;
+    const TIO* dyrow = static_cast<const TIO*>(p.dy) + row0;
+
+    float v[2 * C];
+#pragma unroll
+    for (int t = 0; t < C; ++t) {
+      const bool ok = active && t < nvalid;
+      const float xr = ok ? Io<TIO>::load(xrow + (long long)t * W + m) : 0.0f;
+      const float xi = ok ? Io<TIO>::load(xrow + (long long)t * W + M + m) : 0.0f;
+      S.xr[t][tid] = xr;
+      S.xi[t][tid] = xi;
+      S.gr[t][tid] = ok ? Io<TIO>::load(dyrow + (long long)t * W + m) : 0.0f;
+      S.gi[t][tid] = ok ? Io<TIO>::load(dyrow + (long long)t * W + M + m) : 0.0f;
+      v[t] = fmaf(xr, mc.d0r, xi * mc.d0i);
+      v[C + t] = fmaf(xr, mc.d1r, xi * mc.d1i);
+    }
+    cluster_reduce<2 * C, NT>(v, s_warp, s_cta_ctl, s_proj, cluster);
+    token_controls<C>(s_proj, bias0, bias1, s_E, s_delta, s_tau0, s_tau1);
+
+    // carry-in of this chunk from the forward
+    float2 hin = make_float2(0.0f, 0.0f);
+    if (active) {
+      if (c > 0) hin = p.carry[(b * chunks + c - 1) * M + m];
+      else if (p.h0_r != nullptr) hin = make_float2(p.h0_r[b * M + m], p.h0_i[b * M + m]);
+    }
+
+    // pass 0: replay states, relu masks, chunk product
+    float2 P = make_float2(1.0f, 0.0f);
+    {
+      float2 h = hin;
+#pragma unroll
+      for (int t = 0; t < C; ++t) {
+        float2 a = make_float2(1.0f, 0.0f);
+        if (t < nvalid) {
+          const TokenCoef k = token_coef<kFast>(mc, s_E[t], s_delta[t], s_tau0[t], s_tau1[t]);
+          a = k.a;
+          const float2 bw = make_float2(k.gain * tanh_t<kFast>(S.xr[t][tid]),
+                                        k.gain * tanh_t<kFast>(S.xi[t][tid]));
+          h = cfma(a, h, bw);
+          if (!(h.x > 0.0f)) S.gr[t][tid] = 0.0f;
+          if (!(h.y > 0.0f)) S.gi[t][tid] = 0.0f;
+        }
+        S.hr[t][tid] = h.x;
+        S.hi[t][tid] = h.y;
+        S.ar[t][tid] = a.x;
+        S.ai[t][tid] = a.y;
+        P = cmul(a, P);
+      }
+    }
+    // pass A: local reverse adjoint from zero -> aggregate (conj P, Qr)
+    float2 Qr = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int t = C - 1; t >= 0; --t) {
+      Qr.x += S.gr[t][tid];
+      Qr.y += S.gi[t][tid];
+      const float ar = S.ar[t][tid], ai = S.ai[t][tid];
+      Qr = make_float2(fmaf(ar, Qr.x, ai * Qr.y), fmaf(ar, Qr.y, -ai * Qr.x));
+    }
+    const float2 Pc = make_float2(P.x, -P.y);
+
+    float2 kin = make_float2(0.0f, 0.0f);
+    if (c == chunks - 1) {
+      if (p.glast_r != nullptr && active) kin = make_float2(p.glast_r[b * M + m], p.glast_i[b * M + m]);
+    } else {
+      const float2* incl = p.incl;
+      const long long Bq = B;
+      kin = lookback(lc, ticket, g, chunks - 1 - c, Pc, Qr, ticket != p.inject_unpublished, s_state, [&](int j) {
+        return __ldcg(incl + (ticket - j * Bq) * Mp + m);
+      });
+    }
+    const float2 kout = cfma(Pc, kin, Qr);
+    if (ticket != p.inject_unpublished) {
+      p.incl[ticket * Mp + m] = kout;
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) st_release(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
+    }
+    if (c == 0 && p.gh0_r != nullptr && active) {
+      p.gh0_r[b * M + m] = kout.x;
+      p.gh0_i[b * M + m] = kout.y;
+    }
+
+    // pass B: true adjoint, all gradients
+    float f_nu = 0.0f, f_th = 0.0f, f_wlg = 0.0f, f_wpr = 0.0f, f_wrr = 0.0f;
+    float2 lam = kin;
+#pragma unroll
+    for (int t = C - 1; t >= 0; --t) {
+      if (t < nvalid) {
+        lam.x += S.gr[t][tid];
+        lam.y += S.gi[t][tid];
+        const float2 prev = t > 0 ? make_float2(S.hr[t - 1][tid], S.hi[t - 1][tid]) : hin;
+        const float ar = S.ar[t][tid], ai = S.ai[t][tid];
+        const float gar = fmaf(lam.x, prev.x, lam.y * prev.y);
+        const float gai = fmaf(lam.y, prev.x, -lam.x * prev.y);
+        const float E = s_E[t], delta = s_delta[t];
+        const TokenCoef k = token_coef<kFast>(mc, E, delta, s_tau0[t], s_tau1[t]);
+        const float pg = fmaf(gai, ar, -gar * ai);
+        const float radial = k.z * fmaf(k.rho * delta, pg, -fmaf(gar, ar, gai * ai));
+        const float dscan = pg - k.rho * pg;
+        f_th += pg;
+        // write path
+        const float cr = tanh_t<kFast>(S.xr[t][tid]);
+        const float ci = tanh_t<kFast>(S.xi[t][tid]);
+        const float gg = k.gain * fmaf(lam.x, cr, lam.y * ci);
+        const float gq = gg * fmaf(-0.5f, k.gate, 1.0f);
+        const float dyn = k.z * k.rho * k.rho * rcp_approx(k.num);
+        v[t] = radial + fmaf(gg, dyn, gq * mc.wrr * kInvLn16);
+        v[C + t] = fmaf(gq * mc.wpr, kInvHalfPi, dscan);
+        f_nu += radial + gg * (dyn - mc.stat);
+        f_wlg += gg;
+        f_wpr = fmaf(gq, s_tau0[t], f_wpr);
+        f_wrr = fmaf(gq, s_tau1[t], f_wrr);
+        S.ar[t][tid] = lam.x * k.gain * fmaf(-cr, cr, 1.0f);
+        S.ai[t][tid] = lam.y * k.gain * fmaf(-ci, ci, 1.0f);
+        lam = make_float2(fmaf(ar, lam.x, ai * lam.y), fmaf(ar, lam.y, -ai * lam.x));
+      } else {
+        v[t] = 0.0f;
+        v[C + t] = 0.0f;
+      }
+    }
+    if (!active) {
+      f_nu = f_th = f_wlg = f_wpr = f_wrr = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 2 * C; ++i) v[i] = 0.0f;
+    }
+    acc_nu += f_nu;
+    acc_th += f_th;
+    acc_wlg += f_wlg;
+    acc_wpr += f_wpr;
+    acc_wrr += f_wrr;
+
+    cluster_reduce<2 * C, NT>(v, s_warp, s_cta_grad, s_tot, cluster);
+    if (tid < C) {
+      const int t = tid;
+      const float tau0 = s_tau0[t], tau1 = s_tau1[t];
+      s_dp1[t] = t < nvalid ? s_tot[t] * kLn16 * fmaf(-tau1, tau1, 1.0f) : 0.0f;
+      s_dp0[t] = t < nvalid ? s_tot[C + t] * kHalfPi * fmaf(-tau0, tau0, 1.0f) : 0.0f;
+    }
+    __syncthreads();
+    TIO* dxrow = static_cast<TIO*>(p.dx) + row0;
+    float f_d0r = 0.0f, f_d0i = 0.0f, f_d1r = 0.0f, f_d1i = 0.0f;
+#pragma unroll
+    for (int t = 0; t < C; ++t) {
+      if (t < nvalid) {
+        const float dp0 = s_dp0[t], dp1 = s_dp1[t];
+        const float xr = S.xr[t][tid], xi = S.xi[t][tid];
+        if (active) {
+          Io<TIO>::store(dxrow + (long long)t * W + m, fmaf(dp0, mc.d0r, fmaf(dp1, mc.d1r, S.ar[t][tid])));
+          Io<TIO>::store(dxrow + (long long)t * W + M + m,
+                         fmaf(dp0, mc.d0i, fmaf(dp1, mc.d1i, S.ai[t][tid])));
+        }
+        f_d0r = fmaf(xr, dp0, f_d0r);
+        f_d0i = fmaf(xi, dp0, f_d0i);
+        f_d1r = fmaf(xr, dp1, f_d1r);
+        f_d1i = fmaf(xi, dp1, f_d1i);
+      }
+    }
+    acc_d0r += f_d0r;
+    acc_d0i += f_d0i;
+    acc_d1r += f_d1r;
+    acc_d1i += f_d1i;
+    if (g == 0 && tid == 0) {
+      float s0 = 0.0f, s1 = 0.0f;
+      for (int t = 0; t < C; ++t) {
+        s0 += s_dp0[t];
+        s1 += s_dp1[t];
+      }
+      acc_b0 += s0;
+      acc_b1 += s1;
+    }
+  }
+  // per-cluster partial parameter gradients (reduced in a fixed order by mixer_reduce_kernel)
+  const long long k = blockIdx.y;
+  double* part = p.part + k * (long long)kPartModes * Mp;
+  const double vals[kPartModes] = {acc_nu, acc_th, acc_wlg, acc_wpr, acc_wrr,
+                                   acc_d0r, acc_d0i, acc_d1r, acc_d1i};
+#pragma unroll
+  for (int q = 0; q < kPartModes; ++q) part[(long long)q * Mp + m] = vals[q];
+  if (g == 0 && tid == 0) {
+    double* pb = p.part + (long long)gridDim.y * kPartModes * Mp + 2 * k;
+    pb[0] = acc_b0;
+    pb[1] = acc_b1;
+  }
+  finish_launch(p.ls);
+}
+
+struct ReduceParams {
+  const double* part;
+  int clusters, Mp, M, W;
+  const float* theta_log;
+  float* g_nu_log;
+  float* g_theta_log;
+  float* g_wlg;
+  float* g_wpr;
+  float* g_wrr;
+  float* g_energy;
+  float* g_phase_dir;   // [W+1]
+  float* g_radial_dir;  // [W+1]
+};
+
+__global__ void mixer_reduce_kernel(const ReduceParams r) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = (long long)kPartModes * r.Mp;
+  if (m < r.M) {
+    double s[kPartModes] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 0; k < r.clusters; ++k) {
+      const double* pk = r.part + k * stride + m;
+#pragma unroll
+      for (int q = 0; q < kPartModes; ++q) s[q] += pk[(long long)q * r.Mp];
+    }
+    r.g_nu_log[m] = (float)s[0];
+    r.g_theta_log[m] = (float)(s[1] * exp((double)r.theta_log[m]));
+    r.g_wlg[m] = (float)s[2];
+    r.g_wpr[m] = (float)s[3];
+    r.g_wrr[m] = (float)s[4];
+    r.g_energy[m] = 0.0f;
+    r.g_phase_dir[m] = (float)s[5];
+    r.g_phase_dir[r.M + m] = (float)s[6];
+    r.g_radial_dir[m] = (float)s[7];
+    r.g_radial_dir[r.M + m] = (float)s[8];
+  }
+  if (m == 0) {
+    double b0 = 0.0, b1 = 0.0;
+    const double* pb = r.part + (long long)r.clusters * stride;
+    for (int k = 0; k < r.clusters; ++k) {
+      b0 += pb[2 * k];
+      b1 += pb[2 * k + 1];
+    }
+    r.g_phase_dir[r.W] = (float)b0;
+    r.g_radial_dir[r.W] = (float)b1;
+  }
+}
+
+// ------------------------------------------------------------------------------ host side
+struct Plan {
+  int NT, G, Mp, chunks;
+  long long tiles;
+  int clusters_fwd, clusters_bwd;
+  size_t bwd_dyn_smem;
+};
+
+static thread_local char g_err[512];
+static void set_err(const char* msg) { snprintf(g_err, sizeof(g_err), "%s", msg); }
+
+template <typename K>
+static int max_clusters(K kernel, int G, int NT, size_t dyn_smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G, 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = dyn_smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = G;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+template <typename TIO, int NT>
+static int prepare_kernels(int G, size_t dyn, int* nf, int* nb) {
+  constexpr bool kFast = std::is_same<TIO, __nv_bfloat16>::value;
+  auto fk = mixer_fwd_kernel<TIO, NT, kFast>;
+  auto bk = mixer_bwd_kernel<TIO, NT, kFast>;
+  if (G > 8) {
+    cudaFuncSetAttribute(fk, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaFuncSetAttribute(bk, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  }
+  if (cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  *nf = max_clusters(fk, G, NT, 0);
+  *nb = max_clusters(bk, G, NT, dyn);
+  return (*nf > 0 && *nb > 0) ? 0 : -1;
+}
+
+static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
+  if (B <= 0 || T <= 0 || W <= 0) { set_err("batch, length and width must be positive"); return SPARC_ERR_SHAPE; }
+  if (W % 2) { set_err("SPARC rnn_width must be even"); return SPARC_ERR_SHAPE; }
+  if (dtype != SPARC_DTYPE_F32 && dtype != SPARC_DTYPE_BF16) { set_err("unsupported dtype"); return SPARC_ERR_DTYPE; }
+  const int M = W / 2;
+  int NT;
+  if (M <= 8 * 128) NT = 128;
+  else if (M <= 8 * 256) NT = 256;
+  else { set_err("width above 4096 is not supported"); return SPARC_ERR_SHAPE; }
+  pl->NT = NT;
+  pl->G = (M + NT - 1) / NT;
+  pl->Mp = pl->G * NT;
+  pl->chunks = (int)((T + kChunk - 1) / kChunk);
+  pl->tiles = B * pl->chunks;
+  if (pl->tiles >= (1LL << 31)) { set_err("too many tiles"); return SPARC_ERR_SHAPE; }
+  pl->bwd_dyn_smem = (NT == 128) ? sizeof(BwdSmem<kChunk, 128>) : sizeof(BwdSmem<kChunk, 256>);
+
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static int cache[64][2][2][2];  // [dev][dtype][NT idx][fwd/bwd]
+  static bool have[64][2][2];
+  std::lock_guard<std::mutex> lock(mu);
+  const int ni = NT == 128 ? 0 : 1;
+  const int di = dtype == SPARC_DTYPE_BF16 ? 1 : 0;
+  // occupancy is per cluster size; recompute if G differs from the cached one
+  static int cached_g[64][2][2];
+  if (dev < 64 && have[dev][di][ni] && cached_g[dev][di][ni] == pl->G) {
+    pl->clusters_fwd = cache[dev][di][ni][0];
+    pl->clusters_bwd = cache[dev][di][ni][1];
+  } else {
+    int nf = 0, nb = 0, rc;
+    if (dtype == SPARC_DTYPE_BF16) {
+      rc = NT == 128 ? prepare_kernels<__nv_bfloat16, 128>(pl->G, pl->bwd_dyn_smem, &nf, &nb)
+                     : prepare_kernels<__nv_bfloat16, 256>(pl->G, pl->bwd_dyn_smem, &nf, &nb);
+    } else {
+      rc = NT == 128 ? prepare_kernels<float, 128>(pl->G, pl->bwd_dyn_smem, &nf, &nb)
+                     : prepare_kernels<float, 256>(pl->G, pl->bwd_dyn_smem, &nf, &nb);
+    }
+    if (rc != 0) { set_err("cluster occupancy query failed"); return SPARC_ERR_LAUNCH; }
+    if (dev < 64) {
+      cache[dev][di][ni][0] = nf;
+      cache[dev][di][ni][1] = nb;
+      cached_g[dev][di][ni] = pl->G;
+      have[dev][di][ni] = true;
+    }
+    pl->clusters_fwd = nf;
+    pl->clusters_bwd = nb;
+  }
+  pl->clusters_fwd = (int)std::min<long long>(pl->clusters_fwd, pl->tiles);
+  pl->clusters_bwd = (int)std::min<long long>(pl->clusters_bwd, pl->tiles);
+  return SPARC_OK;
+}
+
+struct WsLayout {
+  size_t flags, agg, incl, part, total;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static WsLayout ws_layout(const Plan& pl) {
+  WsLayout L;
+  size_t off = align256(sizeof(LaunchState));
+  L.flags = off;
+  off = align256(off + (size_t)pl.tiles * pl.G * sizeof(unsigned));
+  L.agg = off;
+  off = align256(off + (size_t)pl.tiles * pl.Mp * sizeof(float4));
+  L.incl = off;
+  off = align256(off + (size_t)pl.tiles * pl.Mp * sizeof(float2));
+  L.part = off;
+  off = align256(off + ((size_t)pl.clusters_bwd * kPartModes * pl.Mp + 2 * (size_t)pl.clusters_bwd) * sizeof(double));
+  L.total = off;
+  return L;
+}
+
+template <typename K, typename P>
+static cudaError_t launch_cluster(K kernel, int G, int NT, int clusters, size_t dyn, cudaStream_t s,
+                                  const P& params) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G, clusters, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = dyn;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = G;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+}  // namespace sparc
+
+using namespace sparc;
+
+extern "C" {
+
+const char* sparc_last_error(void) { return g_err; }
+
+long long sparc_mixer_chunk_tokens(void) { return kChunk; }
+
+long long sparc_mixer_carry_chunks(long long length) { return (length + kChunk - 1) / kChunk; }
+
+size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype) {
+  Plan pl;
+  if (make_plan(batch, length, width, dtype, &pl) != SPARC_OK) return 0;
+  return ws_layout(pl).total;
+}
+
+int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
+  if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
+  Plan pl;
+  int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
+  if (rc != SPARC_OK) return rc;
+  const WsLayout L = ws_layout(pl);
+  if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
+  if (!a->x || !a->y || !a->carry || !a->nu_log || !a->theta_log || !a->phase_direction ||
+      !a->radial_direction || !a->write_log_gain || !a->write_phase_response || !a->write_radial_response) {
+    set_err("null tensor pointer"); return SPARC_ERR_ARG;
+  }
+  if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->last_r == nullptr) != (a->last_i == nullptr)) {
+    set_err("h0 / last pointers must be given in pairs"); return SPARC_ERR_ARG;
+  }
+  char* ws = static_cast<char*>(a->workspace);
+  FwdParams p;
+  p.x = a->x;
+  p.y = a->y;
+  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
+                        a->write_log_gain, a->write_phase_response, a->write_radial_response};
+  p.h0_r = a->h0_r;
+  p.h0_i = a->h0_i;
+  p.last_r = a->last_r;
+  p.last_i = a->last_i;
+  p.carry = reinterpret_cast<float2*>(a->carry);
+  p.ls = reinterpret_cast<LaunchState*>(ws);
+  p.flags = reinterpret_cast<unsigned*>(ws + L.flags);
+  p.agg = reinterpret_cast<float4*>(ws + L.agg);
+  p.B = a->batch;
+  p.T = a->length;
+  p.W = a->width;
+  p.M = a->width / 2;
+  p.chunks = pl.chunks;
+  p.tiles = pl.tiles;
+  p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
+  p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
+  p.deterministic = a->deterministic;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (a->dtype == SPARC_DTYPE_BF16) {
+    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 128, true>, pl.G, 128, pl.clusters_fwd, 0, s, p)
+                     : launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 256, true>, pl.G, 256, pl.clusters_fwd, 0, s, p);
+  } else {
+    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<float, 128, false>, pl.G, 128, pl.clusters_fwd, 0, s, p)
+                     : launch_cluster(mixer_fwd_kernel<float, 256, false>, pl.G, 256, pl.clusters_fwd, 0, s, p);
+  }
+  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  return SPARC_OK;
+}
+
+int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
+  if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
+  Plan pl;
+  int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
+  if (rc != SPARC_OK) return rc;
+  const WsLayout L = ws_layout(pl);
+  if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
+  if (!a->x || !a->dy || !a->dx || !a->carry || !a->grad_nu_log || !a->grad_theta_log ||
+      !a->grad_phase_direction || !a->grad_radial_direction || !a->grad_write_log_gain ||
+      !a->grad_energy_response || !a->grad_write_phase_response || !a->grad_write_radial_response) {
+    set_err("null tensor pointer"); return SPARC_ERR_ARG;
+  }
+  if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->grad_last_r == nullptr) != (a->grad_last_i == nullptr) ||
+      (a->grad_h0_r == nullptr) != (a->grad_h0_i == nullptr)) {
+    set_err("paired pointers must be given together"); return SPARC_ERR_ARG;
+  }
+  char* ws = static_cast<char*>(a->workspace);
+  BwdParams p;
+  p.x = a->x;
+  p.dy = a->dy;
+  p.dx = a->dx;
+  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
+                        a->write_log_gain, a->write_phase_response, a->write_radial_response};
+  p.h0_r = a->h0_r;
+  p.h0_i = a->h0_i;
+  p.glast_r = a->grad_last_r;
+  p.glast_i = a->grad_last_i;
+  p.gh0_r = a->grad_h0_r;
+  p.gh0_i = a->grad_h0_i;
+  p.carry = reinterpret_cast<const float2*>(a->carry);
+  p.ls = reinterpret_cast<LaunchState*>(ws);
+  p.flags = reinterpret_cast<unsigned*>(ws + L.flags);
+  p.agg = reinterpret_cast<float4*>(ws + L.agg);
+  p.incl = reinterpret_cast<float2*>(ws + L.incl);
+  p.part = reinterpret_cast<double*>(ws + L.part);
+  p.B = a->batch;
+  p.T = a->length;
+  p.W = a->width;
+  p.M = a->width / 2;
+  p.chunks = pl.chunks;
+  p.tiles = pl.tiles;
+  p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
+  p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
+  p.deterministic = a->deterministic;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  const size_t dyn = pl.bwd_dyn_smem;
+  if (a->dtype == SPARC_DTYPE_BF16) {
+    e = pl.NT == 128 ? launch_cluster(mixer_bwd_kernel<__nv_bfloat16, 128, true>, pl.G, 128, pl.clusters_bwd, dyn, s, p)
+                     : launch_cluster(mixer_bwd_kernel<__nv_bfloat16, 256, true>, pl.G, 256, pl.clusters_bwd, dyn, s, p);
+  } else {
+    e = pl.NT == 128 ? launch_cluster(mixer_bwd_kernel<float, 128, false>, pl.G, 128, pl.clusters_bwd, dyn, s, p)
+                     : launch_cluster(mixer_bwd_kernel<float, 256, false>, pl.G, 256, pl.clusters_bwd, dyn, s, p);
+  }
+  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  ReduceParams r;
+  r.part = p.part;
+  r.clusters = pl.clusters_bwd;
+  r.Mp = pl.Mp;
+  r.M = p.M;
+  r.W = p.W;
+  r.theta_log = a->theta_log;
+  r.g_nu_log = a->grad_nu_log;
+  r.g_theta_log = a->grad_theta_log;
+  r.g_wlg = a->grad_write_log_gain;
+  r.g_wpr = a->grad_write_phase_response;
+  r.g_wrr = a->grad_write_radial_response;
+  r.g_energy = a->grad_energy_response;
+  r.g_phase_dir = a->grad_phase_direction;
+  r.g_radial_dir = a->grad_radial_direction;
+  mixer_reduce_kernel<<<(p.M + 127) / 128, 128, 0, s>>>(r);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  return SPARC_OK;
+}
+
+int sparc_read_status(const void* workspace, unsigned* status, void* stream) {
+  if (workspace == nullptr || status == nullptr) { set_err("null pointer"); return SPARC_ERR_ARG; }
+  const LaunchState* ls = static_cast<const LaunchState*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(status, &ls->status, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  return SPARC_OK;
+}
+
+int sparc_clear_status(void* workspace, void* stream) {
+  if (workspace == nullptr) { set_err("null pointer"); return SPARC_ERR_ARG; }
+  LaunchState* ls = static_cast<LaunchState*>(workspace);
+  cudaError_t e = cudaMemsetAsync(&ls->status, 0, sizeof(unsigned), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  return SPARC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,100 @@
+"""The C-ABI library loads without a GPU and exports every function include/sparc_b200.h
+declares, with the signatures the Python binding uses. No compute call is made here."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "sparc_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(sparc_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from sparc_b200 import _build, _lib
+
+    _build.build()
+    return _lib.load_library()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    from sparc_b200 import _lib
+
+    names = _declared()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_struct_layouts_match_header():
+    """Field order of the ctypes structures equals the C structs' (parsed from the header)."""
+    from sparc_b200 import _lib
+
+    src = open(os.path.join(ROOT, "include", "sparc_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    for cname, py in (("SparcMixerFwdArgs", _lib.MixerFwdArgs), ("SparcMixerBwdArgs", _lib.MixerBwdArgs),
+                      ("SparcDecodeArgs", _lib.DecodeArgs), ("SparcRealFwdArgs", _lib.RealFwdArgs),
+                      ("SparcRealBwdArgs", _lib.RealBwdArgs)):
+        body = re.search(r"typedef struct %s \{(.*?)\}" % cname, src, flags=re.S).group(1)
+        fields = re.findall(r"(\w+)\s*;", body)
+        assert fields == [f[0] for f in py._fields_], cname
+
+
+def test_host_only_queries(lib):
+    assert lib.sparc_mixer_chunk_tokens() == 16
+    assert lib.sparc_mixer_carry_chunks(2048) == 128
+    assert lib.sparc_mixer_carry_chunks(37) == 3
+    assert lib.sparc_real_carry_chunks(17) == 2
+
+
+def test_no_cpu_fallback():
+    import torch
+
+    import sparc_b200
+
+    if torch.cuda.is_available():
+        pytest.skip("checks the no-GPU behaviour")
+    m = sparc_b200.SPARCMixer(8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.randn(1, 4, 8))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sparc_b200.real_scan(torch.rand(1, 4, 3), torch.rand(1, 4, 3))
+
+
+def test_module_api_matches_reference(golden):
+    """Constructor, parameter/buffer names and shapes, init values under manual_seed(0) and the
+    setters' validation, against the reference module (golden init.npz)."""
+    import numpy as np
+    import torch
+
+    import sparc_b200
+
+    d = golden("init")
+    for W in (16, 64):
+        torch.manual_seed(0)
+        m = sparc_b200.SPARCMixer(W)
+        sd = m.state_dict()
+        ref_keys = sorted(k[len(f"w{W}_"):] for k in d.files if k.startswith(f"w{W}_"))
+        assert sorted(sd.keys()) == ref_keys
+        for k in ref_keys:
+            np.testing.assert_array_equal(sd[k].double().numpy(), d[f"w{W}_{k}"])
+    with pytest.raises(ValueError):
+        sparc_b200.SPARCMixer(7)
+    m = sparc_b200.SPARCMixer(8)
+    with pytest.raises(ValueError):
+        m.set_tiled_training_block_size(48)
+    with pytest.raises(ValueError):
+        m.set_controller_projection_dtype("fp16")
+    with pytest.raises(ValueError):
+        m.set_decode_backend("blocked8")
+    m.set_scan_backend("chunk16")
+    m.set_decode_backend("fused")
+    m.prepare_inference()
+    assert m._inference_fused
