@@ -1,0 +1,578 @@
+"""Benchmark of the SPARC hot path on B200 (one JSON line on rank 0).
+
+Default workload (the configuration the metric is quoted on): one
+SPARCMixer(512) layer, forward + backward of sum(y * g), B=8 x T=2048 tokens per GPU, float32,
+parameters from the default init under torch.manual_seed(0), synthetic x, g ~ N(0, 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload layer|stack|real|decode]
+
+Multi-GPU: one process per GPU (torchrun), batch-sharded data parallelism (each rank runs the
+per-GPU batch: weak scaling), parameter gradients all-reduced over NCCL every step; timing is
+the max over ranks of per-step CUDA-event times.
+
+Timing: W untimed warm-up steps; the step is captured once in a CUDA graph and replayed. Before
+every timed step L2 is flushed by writing a 512 MiB buffer (the config-2 inputs fit in L2);
+CUDA events bracket the step only, and K steps are bracketed by a barrier and a device
+synchronise. `e2e` repeats the step through the public module API from pinned host buffers
+(host->device copies of x and g and the device->host read of the loss inside the timed region).
+
+`--impl reference` times the reference algorithm's CPU restatement (the oracle) on the host
+cores instead (the reference itself is Python/Triton with no CPU kernel for this path).
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import json
+import math
+import multiprocessing as mp
+import os
+import re
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "layer": dict(workload="sparc_mixer_layer_fwd_bwd", batch=8, seq_len=2048, width=512,
+                  dtype="float32", chunk=16, config_index=1),
+    "stack": dict(workload="sparc_4layer_rmsnorm_residual_stack_fwd_bwd", batch=64, seq_len=16384,
+                  width=2048, dtype="bfloat16", layers=4, config_index=4),
+    "real": dict(workload="real_scan_fwd_bwd", batch=16, seq_len=8192, channels=16384,
+                 dtype="bfloat16", config_index=2),
+    "decode": dict(workload="sparc_decode_step", batch=256, width=2048, steps=1024,
+                   dtype="bfloat16", config_index=3),
+}
+METRIC = "SPARC layer fwd+bwd tokens/sec and % HBM roofline at 1/2/4/8 B200"
+
+
+# ----------------------------------------------------------------------------- helpers
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if there is one."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU oracle
+def _oracle_rows(args):
+    """float64 oracle forward+backward of a block of batch rows (run in a worker process)."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+
+    from oracle import sparc_oracle as O
+
+    x, g, params = args
+    with threadpool_limits(1):
+        P = O.Params.from_mapping(params)
+        y, _, _ = O.sparc_forward(x, P)
+        grads = O.sparc_backward(x, P, g)
+    return float(np.abs(y).sum()), {k: grads[k] for k in O.PARAM_NAMES}
+
+
+class OraclePool:
+    """Spawned worker processes that run the float64 oracle forward+backward, one batch row of
+    the layer workload per task (the pool starts before any timing and before GPU work)."""
+
+    def __init__(self, batch, seq_len, width, workers, seed=0):
+        import numpy as np
+        import torch
+
+        from oracle import sparc_oracle as O
+
+        torch.manual_seed(seed)
+        params = O.init_params(width, lambda n: torch.rand(n).numpy())
+        rng = np.random.default_rng(seed)
+        self.rows = [(rng.standard_normal((1, seq_len, width)), rng.standard_normal((1, seq_len, width)), params)
+                     for _ in range(min(batch, workers))]
+        self.seq_len = seq_len
+        self.ex = cf.ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn"))
+        list(self.ex.map(_oracle_rows, self.rows[:1]))  # start the workers
+
+    def round(self):
+        """One round over the rows; returns (seconds, tokens)."""
+        t0 = time.perf_counter()
+        list(self.ex.map(_oracle_rows, self.rows))
+        return time.perf_counter() - t0, len(self.rows) * self.seq_len
+
+    def close(self):
+        self.ex.shutdown()
+
+
+def cpu_oracle_layer(batch, seq_len, width, workers, seconds, seed=0):
+    """Time the CPU oracle on the layer workload for about `seconds` (at least one round).
+    Returns (tokens/s, tokens processed, rows per round)."""
+    pool = OraclePool(batch, seq_len, width, workers, seed)
+    el, tokens = 0.0, 0
+    while True:
+        s, t = pool.round()
+        el += s
+        tokens += t
+        if el >= seconds:
+            break
+    pool.close()
+    return tokens / el, tokens, len(pool.rows)
+
+
+# ----------------------------------------------------------------------------- our arm
+def _dist():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def _time_steps(step_fn, steps, flush, world, device):
+    """Per-step CUDA event times (ms) of `step_fn`, L2 flushed before each step; max over
+    ranks of the summed time."""
+    import torch
+    import torch.distributed as dist
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    for i in range(steps):
+        flush()
+        starts[i].record()
+        step_fn()
+        ends[i].record()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total = torch.tensor([sum(per)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    return float(total.item()), per
+
+
+def run_layer(args, wl, world, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    import sparc_b200
+    from sparc_b200 import _lib
+    from sparc_b200.ddp import GradAllReduce
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    B, T, W = wl["batch"], wl["seq_len"], wl["width"]
+    dtype = getattr(torch, wl["dtype"])
+    torch.manual_seed(0)
+    model = sparc_b200.SPARCMixer(W).to(device)
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    x = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
+    g = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
+    reducer = GradAllReduce(model.parameters()) if world > 1 else None
+    flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+
+    def flush():
+        flush_buf.fill_(1)
+
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            model.zero_grad(set_to_none=True)
+            y, _ = model(x)
+            y.backward(g)
+    torch.cuda.current_stream(device).wait_stream(stream)
+    torch.cuda.synchronize(device)
+    model.zero_grad(set_to_none=True)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        y, _ = model(x)
+        y.backward(g)
+
+    def step():
+        graph.replay()
+        if reducer is not None:
+            reducer()
+
+    for _ in range(args.warmup):
+        flush()
+        step()
+    with ClockSampler(local) as clocks:
+        total_ms, per = _time_steps(step, args.steps, flush, world, device)
+    ms = total_ms / args.steps
+    tokens_step = B * T * world
+    value = tokens_step / (ms / 1e3)
+
+    # per-kernel timing through the C ABI (same inputs), for the roofline of the dominant kernel
+    s = 4 if dtype == torch.float32 else 2
+    peak, peak_kind = measured_peaks()
+    kern = {}
+    xr = x.clone().requires_grad_(True)
+    fwd_times, bwd_times = [], []
+    for _ in range(args.steps + 3):
+        flush()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        yy, _ = model(xr)
+        e1.record()
+        flush()
+        e1b = torch.cuda.Event(enable_timing=True)
+        e1b.record()
+        yy.backward(g)
+        e2.record()
+        torch.cuda.synchronize(device)
+        fwd_times.append(e0.elapsed_time(e1))
+        bwd_times.append(e1b.elapsed_time(e2))
+        xr.grad = None
+        model.zero_grad(set_to_none=True)
+    fwd_ms = sorted(fwd_times[3:])[len(fwd_times[3:]) // 2]
+    bwd_ms = sorted(bwd_times[3:])[len(bwd_times[3:]) // 2]
+    kern["mixer_fwd_kernel"] = dict(ms=fwd_ms, bytes=2 * W * s * B * T)
+    kern["mixer_bwd_kernel"] = dict(ms=bwd_ms, bytes=3 * W * s * B * T)
+    dom = max(kern, key=lambda k: kern[k]["ms"])
+    achieved = kern[dom]["bytes"] / (kern[dom]["ms"] / 1e3) / 1e9
+    traffic = profile_traffic(dom, "layer_b8_t2048_w512_fp32")
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": dom,
+                "peak_source": peak_kind,
+                "kernels": {k: {"ms": round(v["ms"], 4), "algorithmic_bytes": v["bytes"],
+                                "GBps": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1)} for k, v in kern.items()},
+                "step_frac": round(5 * W * s * B * T / (ms / 1e3) / 1e9 / peak, 4)}
+
+    # end to end through the public API with pinned host buffers
+    xh = x.cpu().pin_memory()
+    gh = g.cpu().pin_memory()
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        xd = xh.to(device, non_blocking=True)
+        gd = gh.to(device, non_blocking=True)
+        yy, _ = model(xd)
+        loss = (yy.float() * gd.float()).sum()
+        loss.backward()
+        loss_h.copy_(loss.detach(), non_blocking=True)
+        model.zero_grad(set_to_none=True)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        xd = xh.to(device, non_blocking=True)
+        gd = gh.to(device, non_blocking=True)
+        yy, _ = model(xd)
+        loss = (yy.float() * gd.float()).sum()
+        loss.backward()
+        if reducer is not None:
+            reducer()
+        loss_h.copy_(loss.detach(), non_blocking=True)
+        model.zero_grad(set_to_none=True)
+    ev1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+    e2e = {"value": round(tokens_step / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+           "h2d_bytes_per_step": int(2 * B * T * W * s), "d2h_bytes_per_step": 4,
+           "ms_per_step": round(e2e_ms, 4), "path": "SPARCMixer.forward/backward from pinned host x, g"}
+    sparc_b200.check_status()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        workers = min(8, os.cpu_count() or 1)
+        tps, toks, rows = cpu_oracle_layer(B, T, W, workers, seconds=args.cpu_seconds)
+        cpu = {"value": round(tps, 1), "unit": "tokens/s", "cores": workers, "kind": "port",
+               "sample": f"{toks} tokens: float64 numpy oracle fwd+bwd, {rows} batch rows of "
+                         f"T={T}, W={W} per round, one row per process"}
+    del graph
+    return dict(value=value, ms=ms, roofline=roofline, e2e=e2e, cpu=cpu, clocks=clocks.summary(),
+                launches=3 * args.steps, per_step_ms=per, tokens_step=tokens_step)
+
+
+def run_stack(args, wl, world, rank, local):
+    import torch
+
+    import sparc_b200
+    from sparc_b200.ddp import GradAllReduce
+    from sparc_b200.stack import SPARCStack
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    gb, T, W, L = wl["batch"], wl["seq_len"], wl["width"], wl["layers"]
+    B = gb // world
+    torch.manual_seed(0)
+    model = SPARCStack(W, L).to(device)
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    x = torch.randn(B, T, W, generator=gen, device=device).to(torch.bfloat16)
+    g = torch.randn(B, T, W, generator=gen, device=device).to(torch.bfloat16)
+    reducer = GradAllReduce(model.parameters()) if world > 1 else None
+
+    def step():
+        model.zero_grad(set_to_none=True)
+        out = model(x)
+        out.backward(g)
+        if reducer is not None:
+            reducer()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+
+    def noflush():
+        pass
+
+    with ClockSampler(local) as clocks:
+        total_ms, per = _time_steps(step, args.steps, noflush, world, device)
+    ms = total_ms / args.steps
+    value = gb * T / (ms / 1e3)
+    peak, kind = measured_peaks()
+    fused_min = L * 5 * W * 2 * gb * T / world
+    roofline = {"bound": "hbm", "achieved": round(fused_min / (ms / 1e3) / 1e9, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(fused_min / (ms / 1e3) / 1e9 / peak, 4), "traffic": None,
+                "kernel": "whole step (L*5*W*s bytes/token)", "peak_source": kind}
+    sparc_b200.check_status()
+    return dict(value=value, ms=ms, roofline=roofline, e2e=None, cpu=None, clocks=clocks.summary(),
+                launches=3 * L * args.steps, per_step_ms=per, tokens_step=gb * T)
+
+
+def run_real(args, wl, world, rank, local):
+    import torch
+
+    import sparc_b200
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    B, T, D = wl["batch"], wl["seq_len"], wl["channels"]
+    gen = torch.Generator(device=device).manual_seed(rank)
+    a = torch.sigmoid(torch.logit(0.9 + 0.099 * torch.rand(B, T, D, generator=gen, device=device))).to(torch.bfloat16)
+    b = (0.5 * torch.randn(B, T, D, generator=gen, device=device)).to(torch.bfloat16)
+    g = torch.randn(B, T, D, generator=gen, device=device).to(torch.bfloat16)
+    a.requires_grad_(True)
+    b.requires_grad_(True)
+
+    def step():
+        a.grad = None
+        b.grad = None
+        out = sparc_b200.real_chunk_scan(a, b, 128)
+        out.backward(g)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    with ClockSampler(local) as clocks:
+        total_ms, per = _time_steps(step, args.steps, lambda: None, world, device)
+    ms = total_ms / args.steps
+    peak, kind = measured_peaks()
+    byts = 16 * D * B * T
+    roofline = {"bound": "hbm", "achieved": round(byts / (ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(byts / (ms / 1e3) / 1e9 / peak, 4), "traffic": None, "kernel": "fwd+bwd",
+                "peak_source": kind}
+    return dict(value=B * T * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=None, cpu=None,
+                clocks=clocks.summary(), launches=2 * args.steps, per_step_ms=per, tokens_step=B * T * world)
+
+
+def run_decode(args, wl, world, rank, local):
+    import torch
+
+    import sparc_b200
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    B, W, S = wl["batch"], wl["width"], wl["steps"]
+    torch.manual_seed(0)
+    m = sparc_b200.SPARCMixer(W).to(device)
+    m.prepare_inference()
+    gen = torch.Generator(device=device).manual_seed(rank)
+    xs = torch.randn(S, B, W, generator=gen, device=device).to(torch.bfloat16)
+    st0 = (torch.zeros(B, W // 2, device=device), torch.zeros(B, W // 2, device=device))
+
+    def roll():
+        st = st0
+        for s in range(S):
+            _, st = m.step(xs[s], st, None)
+        return st
+
+    roll()
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        roll()
+    torch.cuda.current_stream(device).wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        roll()
+    for _ in range(args.warmup):
+        graph.replay()
+    with ClockSampler(local) as clocks:
+        total_ms, per = _time_steps(graph.replay, args.steps, lambda: None, world, device)
+    ms = total_ms / args.steps
+    us_step = ms * 1e3 / S
+    peak, kind = measured_peaks()
+    byts = 12 * W * B
+    roofline = {"bound": "hbm", "achieved": round(byts / (us_step / 1e6) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(byts / (us_step / 1e6) / 1e9 / peak, 4), "traffic": None,
+                "kernel": "decode_kernel", "peak_source": kind, "us_per_step": round(us_step, 3)}
+    del graph
+    return dict(value=B * S * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=None, cpu=None,
+                clocks=clocks.summary(), launches=S * args.steps, per_step_ms=per, tokens_step=B * S * world)
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args, wl):
+    """The reference algorithm on the host cores: the float64 oracle restatement, one batch row
+    per process over all host cores; each step is one round over min(cores, batch) rows."""
+    workers = os.cpu_count() or 1
+    B, T, W = wl["batch"], wl["seq_len"], wl["width"]
+    pool = OraclePool(B, T, W, min(workers, B))
+    times = []
+    for i in range(args.warmup + args.steps):
+        sec, toks = pool.round()
+        if i >= args.warmup:
+            times.append(sec)
+    pool.close()
+    ms = sum(times) / len(times) * 1e3
+    return toks / (ms / 1e3), ms, toks, len(pool.rows)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="layer")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    wl = WORKLOADS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        if args.workload != "layer":
+            print(json.dumps({"impl": "reference", "unavailable": "reference arm covers the layer workload"}))
+            return
+        value, ms, toks, cores = run_reference(args, wl)
+        line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+                "data": "synthetic", "impl": "reference",
+                "config": {"workload": wl["workload"], "global_batch": wl["batch"], "seq_len": wl["seq_len"],
+                           "width": wl["width"], "parallelism": "host cores"},
+                "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                 "sample": f"{toks} tokens per step: {cores} batch rows of T={wl['seq_len']}, "
+                                           f"W={wl['width']}, float64 numpy oracle fwd+bwd, one row per process"},
+                "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    world, rank, local = _dist()
+    runner = {"layer": run_layer, "stack": run_stack, "real": run_real, "decode": run_decode}[args.workload]
+    r = runner(args, wl, world, rank, local)
+    if rank == 0:
+        unit = "tokens/s"
+        cfg = {"workload": wl["workload"], "baseline_config": wl["config_index"],
+               "parallelism": f"dp{world}" if world > 1 else "single"}
+        for k in ("batch", "seq_len", "width", "channels", "layers", "steps", "chunk"):
+            if k in wl:
+                cfg["global_batch" if k == "batch" else k] = wl[k] * (world if k == "batch" and args.workload in ("layer", "real", "decode") else 1)
+        cfg["l2"] = ("flushed before every step (512 MiB write, outside the CUDA events)"
+                     if args.workload == "layer" else "inputs larger than L2")
+        cfg["timing"] = "per-step CUDA events, CUDA-graph replay" if args.workload in ("layer", "decode") else "per-step CUDA events"
+        line = {"metric": METRIC, "value": round(r["value"], 1), "unit": unit, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32" if wl["dtype"] == "float32" else "bf16", "data": "synthetic",
+                "config": cfg, "roofline": r["roofline"], "cpu_baseline": r["cpu"], "e2e": r["e2e"],
+                "clocks": r["clocks"], "gpu_launches": r["launches"]}
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
