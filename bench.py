@@ -100,6 +100,9 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 2.0:  # short regions: keep one sample
+                time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)

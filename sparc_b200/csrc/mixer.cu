@@ -174,9 +174,12 @@ __device__ __forceinline__ void token_controls(const float* proj, float b0, floa
   __syncthreads();
 }
 
-// Decoupled lookback. The tile publishes `agg` (out = A*in + B) unless its predecessor is
-// already inclusive, walks back composing aggregates, and returns the carry-in.
-// pred_inclusive(j) loads the inclusive state of the tile `j` steps back.
+// Decoupled lookback with a warp-wide window. The tile publishes its aggregate (out = A*in + B)
+// unless its predecessor is already inclusive. Warp 0 then polls up to 32 predecessors at once
+// (lane j reads the flag of the tile j+1 steps back) and picks the nearest inclusive one; the
+// aggregates in between are composed by every thread for its own mode (their loads are
+// independent, so the whole window costs about two round trips instead of one per
+// predecessor). pred_inclusive(j) loads the inclusive state of the tile j steps back.
 // Deterministic mode waits for the immediate predecessor's inclusive state instead (a chained
 // scan), so the carry's rounding does not depend on which predecessors were done first.
 struct LookbackCtx {
@@ -191,57 +194,87 @@ struct LookbackCtx {
   bool deterministic;
 };
 
+__device__ __forceinline__ void publish_flag(unsigned* flag, unsigned value) {
+  // every thread's payload stores precede the barrier; one release fence makes them visible
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    st_release(flag, value);
+  }
+}
+
 template <typename InclFn>
 __device__ __forceinline__ float2 lookback(const LookbackCtx& lc, long long ticket, int g,
                                            int steps_back_max, float2 A, float2 Bv, bool publish,
-                                           unsigned* s_state, InclFn pred_inclusive) {
+                                           unsigned pred_state, unsigned* s_win,
+                                           InclFn pred_inclusive) {
   const int tid = threadIdx.x;
   const int mp = g * blockDim.x + tid;
-  long long pred = ticket - lc.B;
+  const unsigned ep = lc.epoch & 0x3fffffffu;
   if (lc.deterministic) {
     if (tid == 0) {
-      unsigned s = wait_flag(lc.flags + pred * lc.G + g, lc.epoch, lc.max_spin, kFlagInclusive);
+      unsigned s = wait_flag(lc.flags + (ticket - lc.B) * lc.G + g, lc.epoch, lc.max_spin, kFlagInclusive);
       if (s == 0u) atomicOr(&lc.ls->status, kStatusTimeout);
-      s_state[0] = s;
+      s_win[0] = s;
     }
     __syncthreads();
-    const unsigned state = s_state[0];
+    const unsigned state = s_win[0];
     __syncthreads();
     return state == kFlagInclusive ? pred_inclusive(1) : make_float2(0.0f, 0.0f);
   }
-  if (tid == 0) s_state[0] = ld_acquire(lc.flags + pred * lc.G + g);
-  __syncthreads();
-  unsigned st = s_state[0];
-  const bool pred_ready = ((st >> 2) == (lc.epoch & 0x3fffffffu)) && (st & 3u) == kFlagInclusive;
-  if (!pred_ready && publish) {
+  const bool pred_ready = ((pred_state >> 2) == ep) && (pred_state & 3u) == kFlagInclusive;
+  if (pred_ready) return pred_inclusive(1);
+  if (publish) {
     lc.agg[ticket * lc.Mp + mp] = make_float4(A.x, A.y, Bv.x, Bv.y);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) st_release(lc.flags + ticket * lc.G + g, make_flag(lc.epoch, kFlagAggregate));
+    publish_flag(lc.flags + ticket * lc.G + g, make_flag(lc.epoch, kFlagAggregate));
   }
   float2 accA = make_float2(1.0f, 0.0f), accB = make_float2(0.0f, 0.0f);
-  for (int j = 1;; ++j) {
-    unsigned state;
-    if (j == 1 && pred_ready) {
-      state = kFlagInclusive;
-    } else {
-      if (tid == 0) {
-        unsigned s = wait_flag(lc.flags + pred * lc.G + g, lc.epoch, lc.max_spin);
-        if (s == 0u) atomicOr(&lc.ls->status, kStatusTimeout);
-        s_state[j & 1] = s;
+  int base = 0;  // window covers predecessors base+1 .. base+32
+  for (unsigned spin = 0;; ++spin) {
+    // s_win[0] = number of aggregates to compose, s_win[1] = 1 if an inclusive follows them
+    if (tid < 32) {
+      const int j = base + tid + 1;
+      unsigned st = 0u;
+      if (j <= steps_back_max) {
+        const unsigned v = ld_acquire(lc.flags + (ticket - (long long)j * lc.B) * lc.G + g);
+        st = ((v >> 2) == ep) ? (v & 3u) : 0u;
       }
-      __syncthreads();
-      state = s_state[j & 1];
+      const unsigned incl = __ballot_sync(0xffffffffu, st == kFlagInclusive);
+      const unsigned notready = __ballot_sync(0xffffffffu, st == 0u && j <= steps_back_max);
+      if (tid == 0) {
+        const int first_incl = incl ? __ffs(incl) - 1 : 32;
+        const int first_wait = notready ? __ffs(notready) - 1 : 32;
+        if (first_incl < first_wait) {            // aggregates, then an inclusive: done
+          s_win[0] = first_incl;
+          s_win[1] = 1u;
+        } else if (first_wait == 32) {            // a full window of aggregates
+          s_win[0] = 32;
+          s_win[1] = 0u;
+        } else {                                  // compose what is ready, wait for the rest
+          s_win[0] = first_wait;
+          s_win[1] = 0u;
+        }
+      }
     }
-    if (state == kFlagInclusive) {
-      const float2 h = pred_inclusive(j);
-      return cfma(accA, h, accB);
+    __syncthreads();
+    const int n = (int)s_win[0];
+    const bool done = s_win[1] != 0u;
+    __syncthreads();
+    for (int j = 0; j < n; ++j) {
+      const float4 ag = __ldcg(lc.agg + (ticket - (long long)(base + j + 1) * lc.B) * lc.Mp + mp);
+      accB = cfma(accA, make_float2(ag.z, ag.w), accB);
+      accA = cmul(accA, make_float2(ag.x, ag.y));
     }
-    if (state != kFlagAggregate || j >= steps_back_max) return accB;  // timeout: zero carry
-    const float4 ag = __ldcg(lc.agg + pred * lc.Mp + mp);
-    accB = cfma(accA, make_float2(ag.z, ag.w), accB);
-    accA = cmul(accA, make_float2(ag.x, ag.y));
-    pred -= lc.B;
+    base += n;
+    if (done) return cfma(accA, pred_inclusive(base + 1), accB);
+    if (base >= steps_back_max) return accB;  // only on a broken chain; the zero carry is flagged below
+    if (n == 0) {
+      if (spin >= lc.max_spin) {
+        if (tid == 0) atomicOr(&lc.ls->status, kStatusTimeout);
+        return accB;
+      }
+      if (spin > 8) __nanosleep(spin < 64 ? 32 : 256);
+    }
   }
 }
 
@@ -266,6 +299,37 @@ struct FwdParams {
   long long inject_unpublished;
 };
 
+template <typename TIO> struct OutPack;
+template <> struct OutPack<float> {
+  using T = float2;
+  static __device__ __forceinline__ T pack(float2 h) { return make_float2(fmaxf(h.x, 0.0f), fmaxf(h.y, 0.0f)); }
+  static __device__ __forceinline__ void store(float* row, int W, int M, int m, T v) {
+    row[m] = v.x;
+    row[M + m] = v.y;
+  }
+};
+template <> struct OutPack<__nv_bfloat16> {
+  using T = __nv_bfloat162;
+  static __device__ __forceinline__ T pack(float2 h) {
+    return __floats2bfloat162_rn(fmaxf(h.x, 0.0f), fmaxf(h.y, 0.0f));
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* row, int W, int M, int m, T v) {
+    row[m] = v.x;
+    row[M + m] = v.y;
+  }
+};
+
+template <int C, int NT>
+struct FwdSmem {
+  float4 ab[C][NT];  // (a.re, a.im, b.re, b.im) per token and mode, for the two-pass path
+};
+
+// Cluster rank 0 takes the next ticket; peers read it from rank 0's shared memory after the
+// next cluster barrier. Double-buffered by tile parity.
+__device__ __forceinline__ void take_ticket(LaunchState* ls, unsigned* s_ticket, int parity, int g) {
+  if (g == 0 && threadIdx.x == 0) s_ticket[parity] = atomicAdd(&ls->ticket, 1u);
+}
+
 template <typename TIO, int NT, bool kFast>
 __global__ void __launch_bounds__(NT) mixer_fwd_kernel(const FwdParams p) {
   constexpr int C = kChunk;
@@ -279,31 +343,37 @@ __global__ void __launch_bounds__(NT) mixer_fwd_kernel(const FwdParams p) {
   const bool active = m < M;
   const long long B = p.B, T = p.T;
 
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  FwdSmem<C, NT>& S = *reinterpret_cast<FwdSmem<C, NT>*>(smem_raw);
   __shared__ float s_warp[NW][2 * C];
   __shared__ float s_cta[2 * C];
   __shared__ float s_proj[2 * C];
   __shared__ float s_E[C], s_delta[C], s_tau0[C], s_tau1[C];
-  __shared__ unsigned s_ticket;
-  __shared__ unsigned s_state[2];
+  __shared__ unsigned s_ticket[2];
+  __shared__ unsigned s_win[2];
+  __shared__ unsigned s_pred;
 
   const ModeConst mc = load_mode(p.pp, m, M, active);
   const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
   LookbackCtx lc{p.ls, p.flags, p.agg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, G, G * NT, B,
                  p.deterministic != 0};
 
-  for (;;) {
-    if (g == 0 && tid == 0) s_ticket = atomicAdd(&p.ls->ticket, 1u);
-    cluster.sync();
-    const long long ticket = *cluster.map_shared_rank(&s_ticket, 0);
+  take_ticket(p.ls, s_ticket, 0, g);
+  cluster.sync();
+  long long ticket = *cluster.map_shared_rank(&s_ticket[0], 0);
+  for (int it = 0;; ++it) {
     if (ticket >= p.tiles) {
-      cluster.sync();
+      cluster.sync();  // no CTA leaves while a peer may still read its shared memory
       break;
     }
+    take_ticket(p.ls, s_ticket, (it + 1) & 1, g);  // next tile, read after the barrier below
     const long long b = ticket % B;
     const int c = (int)(ticket / B);
     const long long t0 = (long long)c * C;
     const int nvalid = (int)(T - t0 < C ? T - t0 : C);
     const TIO* xrow = static_cast<const TIO*>(p.x) + (b * T + t0) * W;
+    // peek the predecessor (one round trip, overlapped with the loads below)
+    if (tid == 0) s_pred = c > 0 ? ld_acquire(p.flags + (ticket - B) * G + g) : 0u;
 
     float xr[C], xi[C], v[2 * C];
 #pragma unroll
@@ -315,59 +385,80 @@ __global__ void __launch_bounds__(NT) mixer_fwd_kernel(const FwdParams p) {
       v[C + t] = fmaf(xr[t], mc.d1r, xi[t] * mc.d1i);
     }
     cluster_reduce<2 * C, NT>(v, s_warp, s_cta, s_proj, cluster);
+    const long long next = *cluster.map_shared_rank(&s_ticket[(it + 1) & 1], 0);
     token_controls<C>(s_proj, bias0, bias1, s_E, s_delta, s_tau0, s_tau1);
 
-    // pass 1: per-step transition and write, local state from zero, chunk product
-    float2 a[C], bw[C];
-    float2 P = make_float2(1.0f, 0.0f), Q = make_float2(0.0f, 0.0f);
-#pragma unroll
-    for (int t = 0; t < C; ++t) {
-      if (t < nvalid) {
-        const TokenCoef k = token_coef<kFast>(mc, s_E[t], s_delta[t], s_tau0[t], s_tau1[t]);
-        a[t] = k.a;
-        bw[t] = make_float2(k.gain * tanh_t<kFast>(xr[t]), k.gain * tanh_t<kFast>(xi[t]));
-      } else {
-        a[t] = make_float2(1.0f, 0.0f);
-        bw[t] = make_float2(0.0f, 0.0f);
+    const unsigned pst = s_pred;
+    const bool pred_ready = c == 0 || (!lc.deterministic && ((pst >> 2) == (lc.epoch & 0x3fffffffu)) &&
+                                       (pst & 3u) == kFlagInclusive);
+    const bool publish = ticket != p.inject_unpublished;
+    TIO* yrow = static_cast<TIO*>(p.y) + (b * T + t0) * W;
+    float2 hout;
+    if (pred_ready) {
+      // single pass: the carry-in is known, so no aggregate and nothing stored
+      float2 h = make_float2(0.0f, 0.0f);
+      if (active) {
+        if (c > 0) h = __ldcg(p.carry + (b * p.chunks + (c - 1)) * M + m);
+        else if (p.h0_r != nullptr) h = make_float2(p.h0_r[b * M + m], p.h0_i[b * M + m]);
       }
-      Q = cfma(a[t], Q, bw[t]);
-      P = cmul(a[t], P);
-    }
-
-    // chunk carry
-    float2 hin = make_float2(0.0f, 0.0f);
-    if (c == 0) {
-      if (p.h0_r != nullptr && active) hin = make_float2(p.h0_r[b * M + m], p.h0_i[b * M + m]);
+      typename OutPack<TIO>::T outv[C];
+#pragma unroll
+      for (int t = 0; t < C; ++t) {
+        if (t < nvalid) {
+          const TokenCoef k = token_coef<kFast>(mc, s_E[t], s_delta[t], s_tau0[t], s_tau1[t]);
+          const float2 bw = make_float2(k.gain * tanh_t<kFast>(xr[t]), k.gain * tanh_t<kFast>(xi[t]));
+          h = cfma(k.a, h, bw);
+        }
+        outv[t] = OutPack<TIO>::pack(h);
+      }
+      hout = h;
+      if (publish) {
+        if (active) p.carry[(b * p.chunks + c) * M + m] = hout;
+        publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
+      }
+      if (active) {
+#pragma unroll
+        for (int t = 0; t < C; ++t)
+          if (t < nvalid) OutPack<TIO>::store(yrow + (long long)t * W, W, M, m, outv[t]);
+      }
     } else {
+      // two passes around the lookback
+      float2 P = make_float2(1.0f, 0.0f), Q = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int t = 0; t < C; ++t) {
+        float2 a = make_float2(1.0f, 0.0f), bw = make_float2(0.0f, 0.0f);
+        if (t < nvalid) {
+          const TokenCoef k = token_coef<kFast>(mc, s_E[t], s_delta[t], s_tau0[t], s_tau1[t]);
+          a = k.a;
+          bw = make_float2(k.gain * tanh_t<kFast>(xr[t]), k.gain * tanh_t<kFast>(xi[t]));
+        }
+        S.ab[t][tid] = make_float4(a.x, a.y, bw.x, bw.y);
+        Q = cfma(a, Q, bw);
+        P = cmul(a, P);
+      }
       const float2* carry = p.carry;
       const int chunks = p.chunks;
-      hin = lookback(lc, ticket, g, c, P, Q, ticket != p.inject_unpublished, s_state, [&](int j) {
+      const float2 hin = lookback(lc, ticket, g, c, P, Q, publish, pst, s_win, [&](int j) {
         return active ? __ldcg(carry + (b * chunks + (c - j)) * M + m) : make_float2(0.0f, 0.0f);
       });
-    }
-    const float2 hout = cfma(P, hin, Q);
-    if (ticket != p.inject_unpublished) {
-      if (active) p.carry[(b * p.chunks + c) * M + m] = hout;
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) st_release(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-    }
-
-    // pass 2: replay from the carry, relu output
-    TIO* yrow = static_cast<TIO*>(p.y) + (b * T + t0) * W;
-    float2 h = hin;
+      hout = cfma(P, hin, Q);
+      if (publish) {
+        if (active) p.carry[(b * p.chunks + c) * M + m] = hout;
+        publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
+      }
+      float2 h = hin;
 #pragma unroll
-    for (int t = 0; t < C; ++t) {
-      h = cfma(a[t], h, bw[t]);
-      if (active && t < nvalid) {
-        Io<TIO>::store(yrow + (long long)t * W + m, fmaxf(h.x, 0.0f));
-        Io<TIO>::store(yrow + (long long)t * W + M + m, fmaxf(h.y, 0.0f));
+      for (int t = 0; t < C; ++t) {
+        const float4 ab = S.ab[t][tid];
+        h = cfma(make_float2(ab.x, ab.y), h, make_float2(ab.z, ab.w));
+        if (active && t < nvalid) OutPack<TIO>::store(yrow + (long long)t * W, W, M, m, OutPack<TIO>::pack(h));
       }
     }
     if (c == p.chunks - 1 && p.last_r != nullptr && active) {
       p.last_r[b * M + m] = hout.x;
       p.last_i[b * M + m] = hout.y;
     }
+    ticket = next;
   }
   finish_launch(p.ls);
 }
@@ -403,9 +494,10 @@ struct BwdParams {
 template <int C, int NT>
 struct BwdSmem {
   float xr[C][NT], xi[C][NT];
-  float gr[C][NT], gi[C][NT];  // masked dy, later reused for nothing
+  float gr[C][NT], gi[C][NT];  // dy, masked by the relu in pass 0
   float hr[C][NT], hi[C][NT];  // replayed states
-  float ar[C][NT], ai[C][NT];  // transitions, overwritten by the write-path dx
+  float ar[C][NT], ai[C][NT];  // transitions, overwritten by the write-path dx in pass B
+  double acc[kPartModes][NT];  // per-mode parameter-gradient accumulators across tiles
 };
 
 template <typename TIO, int NT, bool kFast>
@@ -431,26 +523,28 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
   __shared__ float s_proj[2 * C];
   __shared__ float s_tot[2 * C];
   __shared__ float s_E[C], s_delta[C], s_tau0[C], s_tau1[C], s_dp0[C], s_dp1[C];
-  __shared__ unsigned s_ticket;
-  __shared__ unsigned s_state[2];
+  __shared__ unsigned s_ticket[2];
+  __shared__ unsigned s_win[2];
+  __shared__ unsigned s_pred;
+  __shared__ double s_bias[2];
 
   const ModeConst mc = load_mode(p.pp, m, M, active);
   const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
   LookbackCtx lc{p.ls, p.flags, p.agg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, G, Mp, B,
                  p.deterministic != 0};
+#pragma unroll
+  for (int q = 0; q < kPartModes; ++q) S.acc[q][tid] = 0.0;
+  if (tid == 0) s_bias[0] = s_bias[1] = 0.0;
 
-  double acc_nu = 0.0, acc_th = 0.0, acc_wlg = 0.0, acc_wpr = 0.0, acc_wrr = 0.0;
-  double acc_d0r = 0.0, acc_d0i = 0.0, acc_d1r = 0.0, acc_d1i = 0.0;
-  double acc_b0 = 0.0, acc_b1 = 0.0;
-
-  for (;;) {
-    if (g == 0 && tid == 0) s_ticket = atomicAdd(&p.ls->ticket, 1u);
-    cluster.sync();
-    const long long ticket = *cluster.map_shared_rank(&s_ticket, 0);
+  take_ticket(p.ls, s_ticket, 0, g);
+  cluster.sync();
+  long long ticket = *cluster.map_shared_rank(&s_ticket[0], 0);
+  for (int it = 0;; ++it) {
     if (ticket >= p.tiles) {
       cluster.sync();
       break;
     }
+    take_ticket(p.ls, s_ticket, (it + 1) & 1, g);
     const long long b = ticket % B;
     const int c = chunks - 1 - (int)(ticket / B);
     const long long t0 = (long long)c * C;
@@ -458,6 +552,7 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
     const long long row0 = (b * T + t0) * W;
     const TIO* xrow = static_cast<const TIO*>(p.x) + row0;
     const TIO* dyrow = static_cast<const TIO*>(p.dy) + row0;
+    if (tid == 0) s_pred = c < chunks - 1 ? ld_acquire(p.flags + (ticket - B) * G + g) : 0u;
 
     float v[2 * C];
 #pragma unroll
@@ -473,6 +568,7 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
       v[C + t] = fmaf(xr, mc.d1r, xi * mc.d1i);
     }
     cluster_reduce<2 * C, NT>(v, s_warp, s_cta_ctl, s_proj, cluster);
+    const long long next = *cluster.map_shared_rank(&s_ticket[(it + 1) & 1], 0);
     token_controls<C>(s_proj, bias0, bias1, s_E, s_delta, s_tau0, s_tau1);
 
     // carry-in of this chunk from the forward
@@ -517,21 +613,20 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
     const float2 Pc = make_float2(P.x, -P.y);
 
     float2 kin = make_float2(0.0f, 0.0f);
+    const bool publish = ticket != p.inject_unpublished;
     if (c == chunks - 1) {
       if (p.glast_r != nullptr && active) kin = make_float2(p.glast_r[b * M + m], p.glast_i[b * M + m]);
     } else {
       const float2* incl = p.incl;
       const long long Bq = B;
-      kin = lookback(lc, ticket, g, chunks - 1 - c, Pc, Qr, ticket != p.inject_unpublished, s_state, [&](int j) {
+      kin = lookback(lc, ticket, g, chunks - 1 - c, Pc, Qr, publish, s_pred, s_win, [&](int j) {
         return __ldcg(incl + (ticket - j * Bq) * Mp + m);
       });
     }
     const float2 kout = cfma(Pc, kin, Qr);
-    if (ticket != p.inject_unpublished) {
+    if (publish) {
       p.incl[ticket * Mp + m] = kout;
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) st_release(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
+      publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
     }
     if (c == 0 && p.gh0_r != nullptr && active) {
       p.gh0_r[b * M + m] = kout.x;
@@ -556,7 +651,6 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
         const float radial = k.z * fmaf(k.rho * delta, pg, -fmaf(gar, ar, gai * ai));
         const float dscan = pg - k.rho * pg;
         f_th += pg;
-        // write path
         const float cr = tanh_t<kFast>(S.xr[t][tid]);
         const float ci = tanh_t<kFast>(S.xi[t][tid]);
         const float gg = k.gain * fmaf(lam.x, cr, lam.y * ci);
@@ -581,11 +675,11 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
 #pragma unroll
       for (int i = 0; i < 2 * C; ++i) v[i] = 0.0f;
     }
-    acc_nu += f_nu;
-    acc_th += f_th;
-    acc_wlg += f_wlg;
-    acc_wpr += f_wpr;
-    acc_wrr += f_wrr;
+    S.acc[0][tid] += f_nu;
+    S.acc[1][tid] += f_th;
+    S.acc[2][tid] += f_wlg;
+    S.acc[3][tid] += f_wpr;
+    S.acc[4][tid] += f_wrr;
 
     cluster_reduce<2 * C, NT>(v, s_warp, s_cta_grad, s_tot, cluster);
     if (tid < C) {
@@ -613,31 +707,30 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
         f_d1i = fmaf(xi, dp1, f_d1i);
       }
     }
-    acc_d0r += f_d0r;
-    acc_d0i += f_d0i;
-    acc_d1r += f_d1r;
-    acc_d1i += f_d1i;
+    S.acc[5][tid] += f_d0r;
+    S.acc[6][tid] += f_d0i;
+    S.acc[7][tid] += f_d1r;
+    S.acc[8][tid] += f_d1i;
     if (g == 0 && tid == 0) {
       float s0 = 0.0f, s1 = 0.0f;
       for (int t = 0; t < C; ++t) {
         s0 += s_dp0[t];
         s1 += s_dp1[t];
       }
-      acc_b0 += s0;
-      acc_b1 += s1;
+      s_bias[0] += s0;
+      s_bias[1] += s1;
     }
+    ticket = next;
   }
   // per-cluster partial parameter gradients (reduced in a fixed order by mixer_reduce_kernel)
   const long long k = blockIdx.y;
   double* part = p.part + k * (long long)kPartModes * Mp;
-  const double vals[kPartModes] = {acc_nu, acc_th, acc_wlg, acc_wpr, acc_wrr,
-                                   acc_d0r, acc_d0i, acc_d1r, acc_d1i};
 #pragma unroll
-  for (int q = 0; q < kPartModes; ++q) part[(long long)q * Mp + m] = vals[q];
+  for (int q = 0; q < kPartModes; ++q) part[(long long)q * Mp + m] = S.acc[q][tid];
   if (g == 0 && tid == 0) {
     double* pb = p.part + (long long)gridDim.y * kPartModes * Mp + 2 * k;
-    pb[0] = acc_b0;
-    pb[1] = acc_b1;
+    pb[0] = s_bias[0];
+    pb[1] = s_bias[1];
   }
   finish_launch(p.ls);
 }
@@ -656,36 +749,42 @@ struct ReduceParams {
   float* g_radial_dir;  // [W+1]
 };
 
-__global__ void mixer_reduce_kernel(const ReduceParams r) {
-  const int m = blockIdx.x * blockDim.x + threadIdx.x;
-  const long long stride = (long long)kPartModes * r.Mp;
-  if (m < r.M) {
-    double s[kPartModes] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
-    for (int k = 0; k < r.clusters; ++k) {
-      const double* pk = r.part + k * stride + m;
-#pragma unroll
-      for (int q = 0; q < kPartModes; ++q) s[q] += pk[(long long)q * r.Mp];
-    }
-    r.g_nu_log[m] = (float)s[0];
-    r.g_theta_log[m] = (float)(s[1] * exp((double)r.theta_log[m]));
-    r.g_wlg[m] = (float)s[2];
-    r.g_wpr[m] = (float)s[3];
-    r.g_wrr[m] = (float)s[4];
-    r.g_energy[m] = 0.0f;
-    r.g_phase_dir[m] = (float)s[5];
-    r.g_phase_dir[r.M + m] = (float)s[6];
-    r.g_radial_dir[m] = (float)s[7];
-    r.g_radial_dir[r.M + m] = (float)s[8];
+// grid (ceil(Mp/32), kPartModes), block (32, 8): warp w sums clusters w, w+8, ... for 32 modes
+// (coalesced), then warp 0 adds the eight partial sums in a fixed order.
+constexpr int kReduceWarps = 8;
+
+__global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const ReduceParams r) {
+  const int lane = threadIdx.x, w = threadIdx.y;
+  const int m = blockIdx.x * 32 + lane;
+  const int q = blockIdx.y;
+  __shared__ double sm[kReduceWarps][32];
+  double s = 0.0;
+  if (m < r.Mp) {
+    for (int k = w; k < r.clusters; k += kReduceWarps) s += r.part[((long long)k * kPartModes + q) * r.Mp + m];
   }
-  if (m == 0) {
-    double b0 = 0.0, b1 = 0.0;
-    const double* pb = r.part + (long long)r.clusters * stride;
-    for (int k = 0; k < r.clusters; ++k) {
-      b0 += pb[2 * k];
-      b1 += pb[2 * k + 1];
+  sm[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && m < r.M) {
+    double t = 0.0;
+#pragma unroll
+    for (int i = 0; i < kReduceWarps; ++i) t += sm[i][lane];
+    switch (q) {
+      case 0: r.g_nu_log[m] = (float)t; r.g_energy[m] = 0.0f; break;
+      case 1: r.g_theta_log[m] = (float)(t * exp((double)r.theta_log[m])); break;
+      case 2: r.g_wlg[m] = (float)t; break;
+      case 3: r.g_wpr[m] = (float)t; break;
+      case 4: r.g_wrr[m] = (float)t; break;
+      case 5: r.g_phase_dir[m] = (float)t; break;
+      case 6: r.g_phase_dir[r.M + m] = (float)t; break;
+      case 7: r.g_radial_dir[m] = (float)t; break;
+      default: r.g_radial_dir[r.M + m] = (float)t; break;
     }
-    r.g_phase_dir[r.W] = (float)b0;
-    r.g_radial_dir[r.W] = (float)b1;
+  }
+  if (blockIdx.x == 0 && q == 0 && w == 1 && lane < 2) {
+    const double* pb = r.part + (long long)r.clusters * kPartModes * r.Mp;
+    double t = 0.0;
+    for (int k = 0; k < r.clusters; ++k) t += pb[2 * k + lane];
+    (lane == 0 ? r.g_phase_dir : r.g_radial_dir)[r.W] = (float)t;
   }
 }
 
@@ -694,7 +793,7 @@ struct Plan {
   int NT, G, Mp, chunks;
   long long tiles;
   int clusters_fwd, clusters_bwd;
-  size_t bwd_dyn_smem;
+  size_t bwd_dyn_smem, fwd_dyn_smem;
 };
 
 static thread_local char g_err[512];
@@ -722,7 +821,7 @@ static int max_clusters(K kernel, int G, int NT, size_t dyn_smem) {
 }
 
 template <typename TIO, int NT>
-static int prepare_kernels(int G, size_t dyn, int* nf, int* nb) {
+static int prepare_kernels(int G, size_t dyn, size_t fdyn, int* nf, int* nb) {
   constexpr bool kFast = std::is_same<TIO, __nv_bfloat16>::value;
   auto fk = mixer_fwd_kernel<TIO, NT, kFast>;
   auto bk = mixer_bwd_kernel<TIO, NT, kFast>;
@@ -730,11 +829,12 @@ static int prepare_kernels(int G, size_t dyn, int* nf, int* nb) {
     cudaFuncSetAttribute(fk, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaFuncSetAttribute(bk, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   }
-  if (cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
+  if (cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess ||
+      cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fdyn) != cudaSuccess) {
     cudaGetLastError();
     return -1;
   }
-  *nf = max_clusters(fk, G, NT, 0);
+  *nf = max_clusters(fk, G, NT, fdyn);
   *nb = max_clusters(bk, G, NT, dyn);
   return (*nf > 0 && *nb > 0) ? 0 : -1;
 }
@@ -755,6 +855,7 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   pl->tiles = B * pl->chunks;
   if (pl->tiles >= (1LL << 31)) { set_err("too many tiles"); return SPARC_ERR_SHAPE; }
   pl->bwd_dyn_smem = (NT == 128) ? sizeof(BwdSmem<kChunk, 128>) : sizeof(BwdSmem<kChunk, 256>);
+  pl->fwd_dyn_smem = (NT == 128) ? sizeof(FwdSmem<kChunk, 128>) : sizeof(FwdSmem<kChunk, 256>);
 
   int dev = 0;
   cudaGetDevice(&dev);
@@ -772,11 +873,11 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   } else {
     int nf = 0, nb = 0, rc;
     if (dtype == SPARC_DTYPE_BF16) {
-      rc = NT == 128 ? prepare_kernels<__nv_bfloat16, 128>(pl->G, pl->bwd_dyn_smem, &nf, &nb)
-                     : prepare_kernels<__nv_bfloat16, 256>(pl->G, pl->bwd_dyn_smem, &nf, &nb);
+      rc = NT == 128 ? prepare_kernels<__nv_bfloat16, 128>(pl->G, pl->bwd_dyn_smem, pl->fwd_dyn_smem, &nf, &nb)
+                     : prepare_kernels<__nv_bfloat16, 256>(pl->G, pl->bwd_dyn_smem, pl->fwd_dyn_smem, &nf, &nb);
     } else {
-      rc = NT == 128 ? prepare_kernels<float, 128>(pl->G, pl->bwd_dyn_smem, &nf, &nb)
-                     : prepare_kernels<float, 256>(pl->G, pl->bwd_dyn_smem, &nf, &nb);
+      rc = NT == 128 ? prepare_kernels<float, 128>(pl->G, pl->bwd_dyn_smem, pl->fwd_dyn_smem, &nf, &nb)
+                     : prepare_kernels<float, 256>(pl->G, pl->bwd_dyn_smem, pl->fwd_dyn_smem, &nf, &nb);
     }
     if (rc != 0) { set_err("cluster occupancy query failed"); return SPARC_ERR_LAUNCH; }
     if (dev < 64) {
@@ -890,11 +991,11 @@ int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (a->dtype == SPARC_DTYPE_BF16) {
-    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 128, true>, pl.G, 128, pl.clusters_fwd, 0, s, p)
-                     : launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 256, true>, pl.G, 256, pl.clusters_fwd, 0, s, p);
+    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 128, true>, pl.G, 128, pl.clusters_fwd, pl.fwd_dyn_smem, s, p)
+                     : launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 256, true>, pl.G, 256, pl.clusters_fwd, pl.fwd_dyn_smem, s, p);
   } else {
-    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<float, 128, false>, pl.G, 128, pl.clusters_fwd, 0, s, p)
-                     : launch_cluster(mixer_fwd_kernel<float, 256, false>, pl.G, 256, pl.clusters_fwd, 0, s, p);
+    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<float, 128, false>, pl.G, 128, pl.clusters_fwd, pl.fwd_dyn_smem, s, p)
+                     : launch_cluster(mixer_fwd_kernel<float, 256, false>, pl.G, 256, pl.clusters_fwd, pl.fwd_dyn_smem, s, p);
   }
   if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
   return SPARC_OK;
@@ -970,7 +1071,7 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   r.g_energy = a->grad_energy_response;
   r.g_phase_dir = a->grad_phase_direction;
   r.g_radial_dir = a->grad_radial_direction;
-  mixer_reduce_kernel<<<(p.M + 127) / 128, 128, 0, s>>>(r);
+  mixer_reduce_kernel<<<dim3((pl.Mp + 31) / 32, kPartModes), dim3(32, kReduceWarps), 0, s>>>(r);
   e = cudaGetLastError();
   if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
   return SPARC_OK;
