@@ -203,6 +203,22 @@ size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width,
 int sparc_mixer_forward(const SparcMixerFwdArgs* args, void* stream);
 int sparc_mixer_backward(const SparcMixerBwdArgs* args, void* stream);
 
+/* No counterpart in the reference: an extra entry point of this library.
+ * sparc_mixer_forward_noalloc runs exactly the computation of sparc_mixer_forward but takes
+ * no workspace (args->workspace and args->workspace_bytes are ignored). It is for callers
+ * that cannot allocate device memory: for example a plugin bound through an FFI into a host
+ * process whose own memory pool has already claimed the GPU, or a serving loop that must not
+ * call cudaMalloc after start-up because it can block the whole device. Its scratch is a
+ * fixed array of sparc_mixer_noalloc_scratch_bytes() (32 MiB) inside the library, which every
+ * GPU that loads the library holds until the process exits; a problem that needs more
+ * (roughly batch * ceil(length/16) * width/2 * 16 bytes) is rejected with SPARC_ERR_WORKSPACE
+ * and a message. The first call on a device looks up that device's copy of the array
+ * (cudaGetSymbolAddress), so make it before any stream capture. All calls share the array:
+ * calls whose executions overlap on the GPU (other streams, other host threads) race and must
+ * be serialised by the caller. The caller still provides x, y, carry and the parameters. */
+size_t sparc_mixer_noalloc_scratch_bytes(void);
+int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* args, void* stream);
+
 int sparc_decode_step(const SparcDecodeArgs* args, void* stream);
 
 long long sparc_real_carry_chunks(long long length);

@@ -1077,6 +1077,110 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   return SPARC_OK;
 }
 
+// ------------------------------------------------------------------------------ no-alloc variant
+// sparc_mixer_forward_noalloc: the same forward kernel, with its scratch (launch counters,
+// lookback flags and chunk aggregates) in a fixed array that lives in the library itself, for
+// callers that cannot allocate device memory. See the declaration in sparc_b200.h.
+}  // extern "C"
+
+namespace sparc {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per GPU, held until exit
+
+// Zero-initialised when the library's module is loaded on a device. Host code must not use
+// this name as a device address: noalloc_scratch() looks the address up per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static void* noalloc_scratch(int dev) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    // the current device is `dev`: the lookup (and the lazy module load it may trigger) binds
+    // the array of this device
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    addr[dev] = ptr;
+  }
+  return addr[dev];
+}
+
+}  // namespace sparc
+
+extern "C" {
+
+size_t sparc_mixer_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
+  if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
+  Plan pl;
+  int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
+  if (rc != SPARC_OK) return rc;
+  const WsLayout L = ws_layout(pl);
+  // the forward uses the launch state, the flags and the aggregates (everything before incl)
+  const size_t need = L.incl;
+  if (need > kNoAllocScratchBytes) {
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "sparc_mixer_forward_noalloc: batch %lld x length %lld x width %d needs %zu bytes of "
+             "scratch, above the built-in %zu; use sparc_mixer_forward with a workspace",
+             a->batch, a->length, a->width, need, kNoAllocScratchBytes);
+    set_err(msg);
+    return SPARC_ERR_WORKSPACE;
+  }
+  if (!a->x || !a->y || !a->carry || !a->nu_log || !a->theta_log || !a->phase_direction ||
+      !a->radial_direction || !a->write_log_gain || !a->write_phase_response || !a->write_radial_response) {
+    set_err("null tensor pointer"); return SPARC_ERR_ARG;
+  }
+  if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->last_r == nullptr) != (a->last_i == nullptr)) {
+    set_err("h0 / last pointers must be given in pairs"); return SPARC_ERR_ARG;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); set_err("no current CUDA device"); return SPARC_ERR_LAUNCH; }
+  char* ws = static_cast<char*>(noalloc_scratch(dev));
+  if (ws == nullptr) { set_err("cudaGetSymbolAddress failed for the built-in scratch"); return SPARC_ERR_LAUNCH; }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the array keeps the previous call's contents: its flag words, laid out for another shape,
+  // could alias this launch's, so they start from zero on every call (a memset, no allocation)
+  cudaError_t e = cudaMemsetAsync(ws + L.flags, 0, (size_t)pl.tiles * pl.G * sizeof(unsigned), s);
+  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  FwdParams p;
+  p.x = a->x;
+  p.y = a->y;
+  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
+                        a->write_log_gain, a->write_phase_response, a->write_radial_response};
+  p.h0_r = a->h0_r;
+  p.h0_i = a->h0_i;
+  p.last_r = a->last_r;
+  p.last_i = a->last_i;
+  p.carry = reinterpret_cast<float2*>(a->carry);
+  p.ls = reinterpret_cast<LaunchState*>(ws);
+  p.flags = reinterpret_cast<unsigned*>(ws + L.flags);
+  p.agg = reinterpret_cast<float4*>(ws + L.agg);
+  p.B = a->batch;
+  p.T = a->length;
+  p.W = a->width;
+  p.M = a->width / 2;
+  p.chunks = pl.chunks;
+  p.tiles = pl.tiles;
+  p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
+  p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
+  p.deterministic = a->deterministic;
+  if (a->dtype == SPARC_DTYPE_BF16) {
+    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 128, true>, pl.G, 128, pl.clusters_fwd, pl.fwd_dyn_smem, s, p)
+                     : launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 256, true>, pl.G, 256, pl.clusters_fwd, pl.fwd_dyn_smem, s, p);
+  } else {
+    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<float, 128, false>, pl.G, 128, pl.clusters_fwd, pl.fwd_dyn_smem, s, p)
+                     : launch_cluster(mixer_fwd_kernel<float, 256, false>, pl.G, 256, pl.clusters_fwd, pl.fwd_dyn_smem, s, p);
+  }
+  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  return SPARC_OK;
+}
+
 int sparc_read_status(const void* workspace, unsigned* status, void* stream) {
   if (workspace == nullptr || status == nullptr) { set_err("null pointer"); return SPARC_ERR_ARG; }
   const LaunchState* ls = static_cast<const LaunchState*>(workspace);
