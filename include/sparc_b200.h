@@ -66,7 +66,7 @@ extern "C" {
 /* Forward of one SPARC mixer layer: y = relu([Re h, Im h]) for the recurrence
  * h_t = a_t h_{t-1} + b_t over M = width/2 complex modes, with a_t, b_t computed from x_t
  * and the parameters. `carry` receives the state at the end of every chunk of
- * sparc_mixer_chunk_tokens() tokens ([batch, sparc_mixer_carry_chunks(length), M] complex,
+ * sparc_mixer_chunk_tokens(dtype) tokens ([batch, sparc_mixer_carry_chunks(length, dtype), M] complex,
  * interleaved real/imag float32); the backward needs it. h0 (initial state) and last (final
  * state) are optional pairs (NULL, NULL). */
 typedef struct SparcMixerFwdArgs {
@@ -197,8 +197,8 @@ typedef struct SparcRealBwdArgs {
 
 const char* sparc_last_error(void);
 
-long long sparc_mixer_chunk_tokens(void);
-long long sparc_mixer_carry_chunks(long long length);
+long long sparc_mixer_chunk_tokens(int dtype);
+long long sparc_mixer_carry_chunks(long long length, int dtype);
 size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype);
 int sparc_mixer_forward(const SparcMixerFwdArgs* args, void* stream);
 int sparc_mixer_backward(const SparcMixerBwdArgs* args, void* stream);

@@ -86,8 +86,8 @@ class RealBwdArgs(ctypes.Structure):
 # every symbol declared in include/sparc_b200.h, with its ctypes signature
 SIGNATURES = {
     "sparc_last_error": (ctypes.c_char_p, []),
-    "sparc_mixer_chunk_tokens": (_ll, []),
-    "sparc_mixer_carry_chunks": (_ll, [_ll]),
+    "sparc_mixer_chunk_tokens": (_ll, [ctypes.c_int]),
+    "sparc_mixer_carry_chunks": (_ll, [_ll, ctypes.c_int]),
     "sparc_mixer_workspace_bytes": (ctypes.c_size_t, [_ll, _ll, ctypes.c_int, ctypes.c_int]),
     "sparc_mixer_forward": (ctypes.c_int, [ctypes.POINTER(MixerFwdArgs), _vp]),
     "sparc_mixer_backward": (ctypes.c_int, [ctypes.POINTER(MixerBwdArgs), _vp]),

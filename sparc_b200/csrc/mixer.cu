@@ -33,7 +33,12 @@ namespace cg = cooperative_groups;
 
 namespace sparc {
 
-constexpr int kChunk = 16;  // tokens per tile; the carry layout depends on it
+#ifndef SPARC_BF16_CHUNK
+#define SPARC_BF16_CHUNK 16
+#endif
+// Tokens per tile (the chunk of the saved carries): 16 for bfloat16, 8 for float32 (whose
+// shared-memory tiles are twice as large).
+__host__ __device__ constexpr int chunk_for(int dtype) { return dtype == SPARC_DTYPE_BF16 ? SPARC_BF16_CHUNK : 8; }
 
 struct ModeConst {
   float nu;      // e^{nu_log}
@@ -203,13 +208,12 @@ __device__ __forceinline__ void publish_flag(unsigned* flag, unsigned value) {
   }
 }
 
-template <typename InclFn>
-__device__ __forceinline__ float2 lookback(const LookbackCtx& lc, long long ticket, int g,
-                                           int steps_back_max, float2 A, float2 Bv, bool publish,
-                                           unsigned pred_state, unsigned* s_win,
-                                           InclFn pred_inclusive) {
+template <int MPT, typename InclFn>
+__device__ __forceinline__ void lookback(const LookbackCtx& lc, long long ticket, int g, int steps_back_max,
+                                         const float2 (&A)[MPT], const float2 (&Bv)[MPT], bool publish,
+                                         unsigned pred_state, unsigned* s_win, int mp0,
+                                         InclFn pred_inclusive, float2 (&carry)[MPT]) {
   const int tid = threadIdx.x;
-  const int mp = g * blockDim.x + tid;
   const unsigned ep = lc.epoch & 0x3fffffffu;
   if (lc.deterministic) {
     if (tid == 0) {
@@ -220,18 +224,32 @@ __device__ __forceinline__ float2 lookback(const LookbackCtx& lc, long long tick
     __syncthreads();
     const unsigned state = s_win[0];
     __syncthreads();
-    return state == kFlagInclusive ? pred_inclusive(1) : make_float2(0.0f, 0.0f);
+    if (state == kFlagInclusive) {
+      pred_inclusive(1, carry);
+    } else {
+#pragma unroll
+      for (int q = 0; q < MPT; ++q) carry[q] = make_float2(0.0f, 0.0f);
+    }
+    return;
   }
   const bool pred_ready = ((pred_state >> 2) == ep) && (pred_state & 3u) == kFlagInclusive;
-  if (pred_ready) return pred_inclusive(1);
+  if (pred_ready) {
+    pred_inclusive(1, carry);
+    return;
+  }
   if (publish) {
-    lc.agg[ticket * lc.Mp + mp] = make_float4(A.x, A.y, Bv.x, Bv.y);
+#pragma unroll
+    for (int q = 0; q < MPT; ++q) lc.agg[ticket * lc.Mp + mp0 + q] = make_float4(A[q].x, A[q].y, Bv[q].x, Bv[q].y);
     publish_flag(lc.flags + ticket * lc.G + g, make_flag(lc.epoch, kFlagAggregate));
   }
-  float2 accA = make_float2(1.0f, 0.0f), accB = make_float2(0.0f, 0.0f);
-  int base = 0;  // window covers predecessors base+1 .. base+32
+  float2 accA[MPT], accB[MPT];
+#pragma unroll
+  for (int q = 0; q < MPT; ++q) {
+    accA[q] = make_float2(1.0f, 0.0f);
+    accB[q] = make_float2(0.0f, 0.0f);
+  }
+  int base = 0;  // the window covers predecessors base+1 .. base+32
   for (unsigned spin = 0;; ++spin) {
-    // s_win[0] = number of aggregates to compose, s_win[1] = 1 if an inclusive follows them
     if (tid < 32) {
       const int j = base + tid + 1;
       unsigned st = 0u;
@@ -247,10 +265,7 @@ __device__ __forceinline__ float2 lookback(const LookbackCtx& lc, long long tick
         if (first_incl < first_wait) {            // aggregates, then an inclusive: done
           s_win[0] = first_incl;
           s_win[1] = 1u;
-        } else if (first_wait == 32) {            // a full window of aggregates
-          s_win[0] = 32;
-          s_win[1] = 0u;
-        } else {                                  // compose what is ready, wait for the rest
+        } else {                                  // compose what is ready; wait for the rest
           s_win[0] = first_wait;
           s_win[1] = 0u;
         }
@@ -260,69 +275,48 @@ __device__ __forceinline__ float2 lookback(const LookbackCtx& lc, long long tick
     const int n = (int)s_win[0];
     const bool done = s_win[1] != 0u;
     __syncthreads();
-    for (int j = 0; j < n; ++j) {
-      const float4 ag = __ldcg(lc.agg + (ticket - (long long)(base + j + 1) * lc.B) * lc.Mp + mp);
-      accB = cfma(accA, make_float2(ag.z, ag.w), accB);
-      accA = cmul(accA, make_float2(ag.x, ag.y));
+    // compose the n aggregates nearest first; loads are issued a batch at a time so their
+    // latencies overlap instead of adding up
+    constexpr int kBatch = 8 / MPT;
+    for (int j0 = 0; j0 < n; j0 += kBatch) {
+      float4 ag[kBatch][MPT];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        if (j0 + u < n) {
+          const float4* ap = lc.agg + (ticket - (long long)(base + j0 + u + 1) * lc.B) * lc.Mp + mp0;
+#pragma unroll
+          for (int q = 0; q < MPT; ++q) ag[u][q] = __ldcg(ap + q);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        if (j0 + u < n) {
+#pragma unroll
+          for (int q = 0; q < MPT; ++q) {
+            accB[q] = cfma(accA[q], make_float2(ag[u][q].z, ag[u][q].w), accB[q]);
+            accA[q] = cmul(accA[q], make_float2(ag[u][q].x, ag[u][q].y));
+          }
+        }
+      }
     }
     base += n;
-    if (done) return cfma(accA, pred_inclusive(base + 1), accB);
-    if (base >= steps_back_max) return accB;  // only on a broken chain; the zero carry is flagged below
-    if (n == 0) {
-      if (spin >= lc.max_spin) {
-        if (tid == 0) atomicOr(&lc.ls->status, kStatusTimeout);
-        return accB;
-      }
-      if (spin > 8) __nanosleep(spin < 64 ? 32 : 256);
+    if (done) {
+      float2 h[MPT];
+      pred_inclusive(base + 1, h);
+#pragma unroll
+      for (int q = 0; q < MPT; ++q) carry[q] = cfma(accA[q], h[q], accB[q]);
+      return;
     }
+    if (base >= steps_back_max || (n == 0 && spin >= lc.max_spin)) {
+      // a broken chain (a tile that never published): record it and continue with zero carry
+      if (tid == 0) atomicOr(&lc.ls->status, kStatusTimeout);
+#pragma unroll
+      for (int q = 0; q < MPT; ++q) carry[q] = accB[q];
+      return;
+    }
+    if (n == 0 && spin > 8) __nanosleep(spin < 64 ? 32 : 256);
   }
 }
-
-// ------------------------------------------------------------------------------ forward
-struct FwdParams {
-  const void* x;
-  void* y;
-  MixerParamPtrs pp;
-  const float* h0_r;
-  const float* h0_i;
-  float* last_r;
-  float* last_i;
-  float2* carry;  // [B, chunks, M]
-  LaunchState* ls;
-  unsigned* flags;
-  float4* agg;
-  long long B, T;
-  int W, M, chunks;
-  long long tiles;
-  unsigned max_spin;
-  int deterministic;
-  long long inject_unpublished;
-};
-
-template <typename TIO> struct OutPack;
-template <> struct OutPack<float> {
-  using T = float2;
-  static __device__ __forceinline__ T pack(float2 h) { return make_float2(fmaxf(h.x, 0.0f), fmaxf(h.y, 0.0f)); }
-  static __device__ __forceinline__ void store(float* row, int W, int M, int m, T v) {
-    row[m] = v.x;
-    row[M + m] = v.y;
-  }
-};
-template <> struct OutPack<__nv_bfloat16> {
-  using T = __nv_bfloat162;
-  static __device__ __forceinline__ T pack(float2 h) {
-    return __floats2bfloat162_rn(fmaxf(h.x, 0.0f), fmaxf(h.y, 0.0f));
-  }
-  static __device__ __forceinline__ void store(__nv_bfloat16* row, int W, int M, int m, T v) {
-    row[m] = v.x;
-    row[M + m] = v.y;
-  }
-};
-
-template <int C, int NT>
-struct FwdSmem {
-  float4 ab[C][NT];  // (a.re, a.im, b.re, b.im) per token and mode, for the two-pass path
-};
 
 // Cluster rank 0 takes the next ticket; peers read it from rank 0's shared memory after the
 // next cluster barrier. Double-buffered by tile parity.
@@ -330,138 +324,7 @@ __device__ __forceinline__ void take_ticket(LaunchState* ls, unsigned* s_ticket,
   if (g == 0 && threadIdx.x == 0) s_ticket[parity] = atomicAdd(&ls->ticket, 1u);
 }
 
-template <typename TIO, int NT, bool kFast>
-__global__ void __launch_bounds__(NT) mixer_fwd_kernel(const FwdParams p) {
-  constexpr int C = kChunk;
-  constexpr int NW = NT / 32;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int g = (int)cluster.block_rank();
-  const int G = (int)cluster.num_blocks();
-  const int tid = threadIdx.x;
-  const int M = p.M, W = p.W;
-  const int m = g * NT + tid;
-  const bool active = m < M;
-  const long long B = p.B, T = p.T;
-
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  FwdSmem<C, NT>& S = *reinterpret_cast<FwdSmem<C, NT>*>(smem_raw);
-  __shared__ float s_warp[NW][2 * C];
-  __shared__ float s_cta[2 * C];
-  __shared__ float s_proj[2 * C];
-  __shared__ float s_E[C], s_delta[C], s_tau0[C], s_tau1[C];
-  __shared__ unsigned s_ticket[2];
-  __shared__ unsigned s_win[2];
-  __shared__ unsigned s_pred;
-
-  const ModeConst mc = load_mode(p.pp, m, M, active);
-  const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
-  LookbackCtx lc{p.ls, p.flags, p.agg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, G, G * NT, B,
-                 p.deterministic != 0};
-
-  take_ticket(p.ls, s_ticket, 0, g);
-  cluster.sync();
-  long long ticket = *cluster.map_shared_rank(&s_ticket[0], 0);
-  for (int it = 0;; ++it) {
-    if (ticket >= p.tiles) {
-      cluster.sync();  // no CTA leaves while a peer may still read its shared memory
-      break;
-    }
-    take_ticket(p.ls, s_ticket, (it + 1) & 1, g);  // next tile, read after the barrier below
-    const long long b = ticket % B;
-    const int c = (int)(ticket / B);
-    const long long t0 = (long long)c * C;
-    const int nvalid = (int)(T - t0 < C ? T - t0 : C);
-    const TIO* xrow = static_cast<const TIO*>(p.x) + (b * T + t0) * W;
-    // peek the predecessor (one round trip, overlapped with the loads below)
-    if (tid == 0) s_pred = c > 0 ? ld_acquire(p.flags + (ticket - B) * G + g) : 0u;
-
-    float xr[C], xi[C], v[2 * C];
-#pragma unroll
-    for (int t = 0; t < C; ++t) {
-      const bool ok = active && t < nvalid;
-      xr[t] = ok ? Io<TIO>::load(xrow + (long long)t * W + m) : 0.0f;
-      xi[t] = ok ? Io<TIO>::load(xrow + (long long)t * W + M + m) : 0.0f;
-      v[t] = fmaf(xr[t], mc.d0r, xi[t] * mc.d0i);
-      v[C + t] = fmaf(xr[t], mc.d1r, xi[t] * mc.d1i);
-    }
-    cluster_reduce<2 * C, NT>(v, s_warp, s_cta, s_proj, cluster);
-    const long long next = *cluster.map_shared_rank(&s_ticket[(it + 1) & 1], 0);
-    token_controls<C>(s_proj, bias0, bias1, s_E, s_delta, s_tau0, s_tau1);
-
-    const unsigned pst = s_pred;
-    const bool pred_ready = c == 0 || (!lc.deterministic && ((pst >> 2) == (lc.epoch & 0x3fffffffu)) &&
-                                       (pst & 3u) == kFlagInclusive);
-    const bool publish = ticket != p.inject_unpublished;
-    TIO* yrow = static_cast<TIO*>(p.y) + (b * T + t0) * W;
-    float2 hout;
-    if (pred_ready) {
-      // single pass: the carry-in is known, so no aggregate and nothing stored
-      float2 h = make_float2(0.0f, 0.0f);
-      if (active) {
-        if (c > 0) h = __ldcg(p.carry + (b * p.chunks + (c - 1)) * M + m);
-        else if (p.h0_r != nullptr) h = make_float2(p.h0_r[b * M + m], p.h0_i[b * M + m]);
-      }
-      typename OutPack<TIO>::T outv[C];
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        if (t < nvalid) {
-          const TokenCoef k = token_coef<kFast>(mc, s_E[t], s_delta[t], s_tau0[t], s_tau1[t]);
-          const float2 bw = make_float2(k.gain * tanh_t<kFast>(xr[t]), k.gain * tanh_t<kFast>(xi[t]));
-          h = cfma(k.a, h, bw);
-        }
-        outv[t] = OutPack<TIO>::pack(h);
-      }
-      hout = h;
-      if (publish) {
-        if (active) p.carry[(b * p.chunks + c) * M + m] = hout;
-        publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-      }
-      if (active) {
-#pragma unroll
-        for (int t = 0; t < C; ++t)
-          if (t < nvalid) OutPack<TIO>::store(yrow + (long long)t * W, W, M, m, outv[t]);
-      }
-    } else {
-      // two passes around the lookback
-      float2 P = make_float2(1.0f, 0.0f), Q = make_float2(0.0f, 0.0f);
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        float2 a = make_float2(1.0f, 0.0f), bw = make_float2(0.0f, 0.0f);
-        if (t < nvalid) {
-          const TokenCoef k = token_coef<kFast>(mc, s_E[t], s_delta[t], s_tau0[t], s_tau1[t]);
-          a = k.a;
-          bw = make_float2(k.gain * tanh_t<kFast>(xr[t]), k.gain * tanh_t<kFast>(xi[t]));
-        }
-        S.ab[t][tid] = make_float4(a.x, a.y, bw.x, bw.y);
-        Q = cfma(a, Q, bw);
-        P = cmul(a, P);
-      }
-      const float2* carry = p.carry;
-      const int chunks = p.chunks;
-      const float2 hin = lookback(lc, ticket, g, c, P, Q, publish, pst, s_win, [&](int j) {
-        return active ? __ldcg(carry + (b * chunks + (c - j)) * M + m) : make_float2(0.0f, 0.0f);
-      });
-      hout = cfma(P, hin, Q);
-      if (publish) {
-        if (active) p.carry[(b * p.chunks + c) * M + m] = hout;
-        publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-      }
-      float2 h = hin;
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        const float4 ab = S.ab[t][tid];
-        h = cfma(make_float2(ab.x, ab.y), h, make_float2(ab.z, ab.w));
-        if (active && t < nvalid) OutPack<TIO>::store(yrow + (long long)t * W, W, M, m, OutPack<TIO>::pack(h));
-      }
-    }
-    if (c == p.chunks - 1 && p.last_r != nullptr && active) {
-      p.last_r[b * M + m] = hout.x;
-      p.last_i[b * M + m] = hout.y;
-    }
-    ticket = next;
-  }
-  finish_launch(p.ls);
-}
+#include "mixer_fwd.cuh"
 
 // ------------------------------------------------------------------------------ backward
 constexpr int kPartModes = 9;  // nu, theta (sum of phase grads), wlg, wpr, wrr, D0r, D0i, D1r, D1i
@@ -500,9 +363,8 @@ struct BwdSmem {
   double acc[kPartModes][NT];  // per-mode parameter-gradient accumulators across tiles
 };
 
-template <typename TIO, int NT, bool kFast>
+template <typename TIO, int NT, bool kFast, int C>
 __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
-  constexpr int C = kChunk;
   constexpr int NW = NT / 32;
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
@@ -515,7 +377,7 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
   const long long B = p.B, T = p.T;
   const int chunks = p.chunks;
 
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   BwdSmem<C, NT>& S = *reinterpret_cast<BwdSmem<C, NT>*>(smem_raw);
   __shared__ float s_warp[NW][2 * C];
   __shared__ float s_cta_ctl[2 * C];
@@ -536,15 +398,15 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
   for (int q = 0; q < kPartModes; ++q) S.acc[q][tid] = 0.0;
   if (tid == 0) s_bias[0] = s_bias[1] = 0.0;
 
-  take_ticket(p.ls, s_ticket, 0, g);
-  cluster.sync();
-  long long ticket = *cluster.map_shared_rank(&s_ticket[0], 0);
   for (int it = 0;; ++it) {
+    // take a ticket only when ready to start it (a held, unstarted ticket stalls successors)
+    take_ticket(p.ls, s_ticket, it & 1, g);
+    cluster.sync();
+    const long long ticket = *cluster.map_shared_rank(&s_ticket[it & 1], 0);
     if (ticket >= p.tiles) {
       cluster.sync();
       break;
     }
-    take_ticket(p.ls, s_ticket, (it + 1) & 1, g);
     const long long b = ticket % B;
     const int c = chunks - 1 - (int)(ticket / B);
     const long long t0 = (long long)c * C;
@@ -568,7 +430,6 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
       v[C + t] = fmaf(xr, mc.d1r, xi * mc.d1i);
     }
     cluster_reduce<2 * C, NT>(v, s_warp, s_cta_ctl, s_proj, cluster);
-    const long long next = *cluster.map_shared_rank(&s_ticket[(it + 1) & 1], 0);
     token_controls<C>(s_proj, bias0, bias1, s_E, s_delta, s_tau0, s_tau1);
 
     // carry-in of this chunk from the forward
@@ -619,9 +480,11 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
     } else {
       const float2* incl = p.incl;
       const long long Bq = B;
-      kin = lookback(lc, ticket, g, chunks - 1 - c, Pc, Qr, publish, s_pred, s_win, [&](int j) {
-        return __ldcg(incl + (ticket - j * Bq) * Mp + m);
-      });
+      const float2 A1[1] = {Pc}, B1[1] = {Qr};
+      float2 k1[1];
+      lookback<1>(lc, ticket, g, chunks - 1 - c, A1, B1, publish, s_pred, s_win, m,
+                  [&](int j, float2 (&h)[1]) { h[0] = __ldcg(incl + (ticket - j * Bq) * Mp + m); }, k1);
+      kin = k1[0];
     }
     const float2 kout = cfma(Pc, kin, Qr);
     if (publish) {
@@ -720,7 +583,6 @@ __global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
       s_bias[0] += s0;
       s_bias[1] += s1;
     }
-    ticket = next;
   }
   // per-cluster partial parameter gradients (reduced in a fixed order by mixer_reduce_kernel)
   const long long k = blockIdx.y;
@@ -790,10 +652,13 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
 
 // ------------------------------------------------------------------------------ host side
 struct Plan {
-  int NT, G, Mp, chunks;
+  int dtype, C, chunks;
   long long tiles;
-  int clusters_fwd, clusters_bwd;
-  size_t bwd_dyn_smem, fwd_dyn_smem;
+  int Gf, Mpf, clusters_fwd;  // forward: CTAs of 256 modes
+  size_t fwd_smem;
+  bool fvec, tma;
+  int NTb, Gb, Mpb, clusters_bwd;  // backward: CTAs of NTb modes
+  size_t bwd_smem;
 };
 
 static thread_local char g_err[512];
@@ -801,6 +666,11 @@ static void set_err(const char* msg) { snprintf(g_err, sizeof(g_err), "%s", msg)
 
 template <typename K>
 static int max_clusters(K kernel, int G, int NT, size_t dyn_smem) {
+  if (G > 8) cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G, 1, 1);
   cfg.blockDim = dim3(NT, 1, 1);
@@ -820,77 +690,73 @@ static int max_clusters(K kernel, int G, int NT, size_t dyn_smem) {
   return n;
 }
 
-template <typename TIO, int NT>
-static int prepare_kernels(int G, size_t dyn, size_t fdyn, int* nf, int* nb) {
-  constexpr bool kFast = std::is_same<TIO, __nv_bfloat16>::value;
-  auto fk = mixer_fwd_kernel<TIO, NT, kFast>;
-  auto bk = mixer_bwd_kernel<TIO, NT, kFast>;
-  if (G > 8) {
-    cudaFuncSetAttribute(fk, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    cudaFuncSetAttribute(bk, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+// Kernel instances: forward <TIO, C, fast math, vector pairs>, backward <TIO, NT, fast math, C>.
+template <typename TIO>
+struct Kernels {
+  static constexpr bool kFast = std::is_same<TIO, __nv_bfloat16>::value;
+  static constexpr int C = kFast ? SPARC_BF16_CHUNK : 8;
+  static void* fwd(bool vec) {
+    return vec ? (void*)mixer_fwd_kernel<TIO, C, kFast, true> : (void*)mixer_fwd_kernel<TIO, C, kFast, false>;
   }
-  if (cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess ||
-      cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fdyn) != cudaSuccess) {
-    cudaGetLastError();
-    return -1;
+  static void* bwd(int NT) {
+    return NT == 128 ? (void*)mixer_bwd_kernel<TIO, 128, kFast, C> : (void*)mixer_bwd_kernel<TIO, 256, kFast, C>;
   }
-  *nf = max_clusters(fk, G, NT, fdyn);
-  *nb = max_clusters(bk, G, NT, dyn);
-  return (*nf > 0 && *nb > 0) ? 0 : -1;
-}
+  static size_t fwd_smem() { return sizeof(FwdSmem<TIO, C, kFast>); }
+  static size_t bwd_smem(int NT) { return NT == 128 ? sizeof(BwdSmem<C, 128>) : sizeof(BwdSmem<C, 256>); }
+};
 
 static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   if (B <= 0 || T <= 0 || W <= 0) { set_err("batch, length and width must be positive"); return SPARC_ERR_SHAPE; }
   if (W % 2) { set_err("SPARC rnn_width must be even"); return SPARC_ERR_SHAPE; }
   if (dtype != SPARC_DTYPE_F32 && dtype != SPARC_DTYPE_BF16) { set_err("unsupported dtype"); return SPARC_ERR_DTYPE; }
   const int M = W / 2;
-  int NT;
-  if (M <= 8 * 128) NT = 128;
-  else if (M <= 8 * 256) NT = 256;
-  else { set_err("width above 4096 is not supported"); return SPARC_ERR_SHAPE; }
-  pl->NT = NT;
-  pl->G = (M + NT - 1) / NT;
-  pl->Mp = pl->G * NT;
-  pl->chunks = (int)((T + kChunk - 1) / kChunk);
+  if (M > 8 * kFwdModes) { set_err("width above 4096 is not supported"); return SPARC_ERR_SHAPE; }
+  pl->dtype = dtype;
+  pl->C = chunk_for(dtype);
+  pl->chunks = (int)((T + pl->C - 1) / pl->C);
   pl->tiles = B * pl->chunks;
   if (pl->tiles >= (1LL << 31)) { set_err("too many tiles"); return SPARC_ERR_SHAPE; }
-  pl->bwd_dyn_smem = (NT == 128) ? sizeof(BwdSmem<kChunk, 128>) : sizeof(BwdSmem<kChunk, 256>);
-  pl->fwd_dyn_smem = (NT == 128) ? sizeof(FwdSmem<kChunk, 128>) : sizeof(FwdSmem<kChunk, 256>);
+  pl->Gf = (M + kFwdModes - 1) / kFwdModes;
+  pl->Mpf = pl->Gf * kFwdModes;
+  pl->fvec = (M % 2) == 0;
+  const size_t s = dtype == SPARC_DTYPE_BF16 ? 2 : 4;
+  pl->tma = ((size_t)W * s) % 16 == 0 && ((size_t)M * s) % 16 == 0;
+  pl->NTb = M <= 8 * 128 ? 128 : 256;
+  pl->Gb = (M + pl->NTb - 1) / pl->NTb;
+  pl->Mpb = pl->Gb * pl->NTb;
 
   int dev = 0;
   cudaGetDevice(&dev);
+  struct Key { int dev, dtype, Gf, Gb, NTb, vec; int nf, nb; };
   static std::mutex mu;
-  static int cache[64][2][2][2];  // [dev][dtype][NT idx][fwd/bwd]
-  static bool have[64][2][2];
+  static Key cache[64];
+  static int ncache = 0;
   std::lock_guard<std::mutex> lock(mu);
-  const int ni = NT == 128 ? 0 : 1;
-  const int di = dtype == SPARC_DTYPE_BF16 ? 1 : 0;
-  // occupancy is per cluster size; recompute if G differs from the cached one
-  static int cached_g[64][2][2];
-  if (dev < 64 && have[dev][di][ni] && cached_g[dev][di][ni] == pl->G) {
-    pl->clusters_fwd = cache[dev][di][ni][0];
-    pl->clusters_bwd = cache[dev][di][ni][1];
-  } else {
-    int nf = 0, nb = 0, rc;
-    if (dtype == SPARC_DTYPE_BF16) {
-      rc = NT == 128 ? prepare_kernels<__nv_bfloat16, 128>(pl->G, pl->bwd_dyn_smem, pl->fwd_dyn_smem, &nf, &nb)
-                     : prepare_kernels<__nv_bfloat16, 256>(pl->G, pl->bwd_dyn_smem, pl->fwd_dyn_smem, &nf, &nb);
-    } else {
-      rc = NT == 128 ? prepare_kernels<float, 128>(pl->G, pl->bwd_dyn_smem, pl->fwd_dyn_smem, &nf, &nb)
-                     : prepare_kernels<float, 256>(pl->G, pl->bwd_dyn_smem, pl->fwd_dyn_smem, &nf, &nb);
+  int nf = -1, nb = -1;
+  for (int i = 0; i < ncache; ++i) {
+    const Key& k = cache[i];
+    if (k.dev == dev && k.dtype == dtype && k.Gf == pl->Gf && k.Gb == pl->Gb && k.NTb == pl->NTb && k.vec == (int)pl->fvec) {
+      nf = k.nf;
+      nb = k.nb;
     }
-    if (rc != 0) { set_err("cluster occupancy query failed"); return SPARC_ERR_LAUNCH; }
-    if (dev < 64) {
-      cache[dev][di][ni][0] = nf;
-      cache[dev][di][ni][1] = nb;
-      cached_g[dev][di][ni] = pl->G;
-      have[dev][di][ni] = true;
-    }
-    pl->clusters_fwd = nf;
-    pl->clusters_bwd = nb;
   }
-  pl->clusters_fwd = (int)std::min<long long>(pl->clusters_fwd, pl->tiles);
-  pl->clusters_bwd = (int)std::min<long long>(pl->clusters_bwd, pl->tiles);
+  if (dtype == SPARC_DTYPE_BF16) {
+    pl->fwd_smem = Kernels<__nv_bfloat16>::fwd_smem();
+    pl->bwd_smem = Kernels<__nv_bfloat16>::bwd_smem(pl->NTb);
+  } else {
+    pl->fwd_smem = Kernels<float>::fwd_smem();
+    pl->bwd_smem = Kernels<float>::bwd_smem(pl->NTb);
+  }
+  if (nf < 0) {
+    void* fk = dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::fwd(pl->fvec) : Kernels<float>::fwd(pl->fvec);
+    void* bk = dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::bwd(pl->NTb) : Kernels<float>::bwd(pl->NTb);
+    nf = max_clusters(fk, pl->Gf, kFwdThreads, pl->fwd_smem);
+    nb = max_clusters(bk, pl->Gb, pl->NTb, pl->bwd_smem);
+    if (nf <= 0 || nb <= 0) { set_err("cluster occupancy query failed"); return SPARC_ERR_LAUNCH; }
+    if (ncache < 64) cache[ncache++] = Key{dev, dtype, pl->Gf, pl->Gb, pl->NTb, (int)pl->fvec, nf, nb};
+  }
+  pl->clusters_fwd = (int)std::min<long long>(nf, pl->tiles);
+  pl->clusters_bwd = (int)std::min<long long>(nb, pl->tiles);
   return SPARC_OK;
 }
 
@@ -902,21 +768,23 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 static WsLayout ws_layout(const Plan& pl) {
   WsLayout L;
+  const int G = std::max(pl.Gf, pl.Gb);
+  const int Mp = std::max(pl.Mpf, pl.Mpb);
   size_t off = align256(sizeof(LaunchState));
   L.flags = off;
-  off = align256(off + (size_t)pl.tiles * pl.G * sizeof(unsigned));
+  off = align256(off + (size_t)pl.tiles * G * sizeof(unsigned));
   L.agg = off;
-  off = align256(off + (size_t)pl.tiles * pl.Mp * sizeof(float4));
+  off = align256(off + (size_t)pl.tiles * Mp * sizeof(float4));
   L.incl = off;
-  off = align256(off + (size_t)pl.tiles * pl.Mp * sizeof(float2));
+  off = align256(off + (size_t)pl.tiles * pl.Mpb * sizeof(float2));
   L.part = off;
-  off = align256(off + ((size_t)pl.clusters_bwd * kPartModes * pl.Mp + 2 * (size_t)pl.clusters_bwd) * sizeof(double));
+  off = align256(off + ((size_t)pl.clusters_bwd * kPartModes * pl.Mpb + 2 * (size_t)pl.clusters_bwd) * sizeof(double));
   L.total = off;
   return L;
 }
 
-template <typename K, typename P>
-static cudaError_t launch_cluster(K kernel, int G, int NT, int clusters, size_t dyn, cudaStream_t s,
+template <typename P>
+static cudaError_t launch_cluster(void* kernel, int G, int NT, int clusters, size_t dyn, cudaStream_t s,
                                   const P& params) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G, clusters, 1);
@@ -930,7 +798,49 @@ static cudaError_t launch_cluster(K kernel, int G, int NT, int clusters, size_t 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, params);
+  void* args[] = {const_cast<P*>(&params)};
+  return cudaLaunchKernelExC(&cfg, kernel, args);
+}
+
+// Validate the forward arguments and fill the kernel parameters (scratch at `ws`).
+static int forward_params(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayout& L, char* ws, FwdParams* p) {
+  if (!a->x || !a->y || !a->carry || !a->nu_log || !a->theta_log || !a->phase_direction ||
+      !a->radial_direction || !a->write_log_gain || !a->write_phase_response || !a->write_radial_response) {
+    set_err("null tensor pointer"); return SPARC_ERR_ARG;
+  }
+  if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->last_r == nullptr) != (a->last_i == nullptr)) {
+    set_err("h0 / last pointers must be given in pairs"); return SPARC_ERR_ARG;
+  }
+  p->x = a->x;
+  p->y = a->y;
+  p->pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
+                         a->write_log_gain, a->write_phase_response, a->write_radial_response};
+  p->h0_r = a->h0_r;
+  p->h0_i = a->h0_i;
+  p->last_r = a->last_r;
+  p->last_i = a->last_i;
+  p->carry = reinterpret_cast<float2*>(a->carry);
+  p->ls = reinterpret_cast<LaunchState*>(ws);
+  p->flags = reinterpret_cast<unsigned*>(ws + L.flags);
+  p->agg = reinterpret_cast<float4*>(ws + L.agg);
+  p->B = a->batch;
+  p->T = a->length;
+  p->W = a->width;
+  p->M = a->width / 2;
+  p->chunks = pl.chunks;
+  p->tiles = pl.tiles;
+  p->max_spin = a->max_spin ? a->max_spin : (1u << 20);
+  p->inject_unpublished = a->inject_enable ? a->inject_tile : -1;
+  p->deterministic = a->deterministic;
+  p->use_tma = pl.tma && (reinterpret_cast<uintptr_t>(a->x) % 16 == 0) ? 1 : 0;
+  return SPARC_OK;
+}
+
+static int launch_forward(const Plan& pl, const FwdParams& p, cudaStream_t s) {
+  void* k = pl.dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::fwd(pl.fvec) : Kernels<float>::fwd(pl.fvec);
+  const cudaError_t e = launch_cluster(k, pl.Gf, kFwdThreads, pl.clusters_fwd, pl.fwd_smem, s, p);
+  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  return SPARC_OK;
 }
 
 }  // namespace sparc
@@ -941,9 +851,12 @@ extern "C" {
 
 const char* sparc_last_error(void) { return g_err; }
 
-long long sparc_mixer_chunk_tokens(void) { return kChunk; }
+long long sparc_mixer_chunk_tokens(int dtype) { return chunk_for(dtype); }
 
-long long sparc_mixer_carry_chunks(long long length) { return (length + kChunk - 1) / kChunk; }
+long long sparc_mixer_carry_chunks(long long length, int dtype) {
+  const int C = chunk_for(dtype);
+  return (length + C - 1) / C;
+}
 
 size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype) {
   Plan pl;
@@ -958,47 +871,10 @@ int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
-  if (!a->x || !a->y || !a->carry || !a->nu_log || !a->theta_log || !a->phase_direction ||
-      !a->radial_direction || !a->write_log_gain || !a->write_phase_response || !a->write_radial_response) {
-    set_err("null tensor pointer"); return SPARC_ERR_ARG;
-  }
-  if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->last_r == nullptr) != (a->last_i == nullptr)) {
-    set_err("h0 / last pointers must be given in pairs"); return SPARC_ERR_ARG;
-  }
-  char* ws = static_cast<char*>(a->workspace);
   FwdParams p;
-  p.x = a->x;
-  p.y = a->y;
-  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
-                        a->write_log_gain, a->write_phase_response, a->write_radial_response};
-  p.h0_r = a->h0_r;
-  p.h0_i = a->h0_i;
-  p.last_r = a->last_r;
-  p.last_i = a->last_i;
-  p.carry = reinterpret_cast<float2*>(a->carry);
-  p.ls = reinterpret_cast<LaunchState*>(ws);
-  p.flags = reinterpret_cast<unsigned*>(ws + L.flags);
-  p.agg = reinterpret_cast<float4*>(ws + L.agg);
-  p.B = a->batch;
-  p.T = a->length;
-  p.W = a->width;
-  p.M = a->width / 2;
-  p.chunks = pl.chunks;
-  p.tiles = pl.tiles;
-  p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
-  p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
-  p.deterministic = a->deterministic;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
-  if (a->dtype == SPARC_DTYPE_BF16) {
-    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 128, true>, pl.G, 128, pl.clusters_fwd, pl.fwd_dyn_smem, s, p)
-                     : launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 256, true>, pl.G, 256, pl.clusters_fwd, pl.fwd_dyn_smem, s, p);
-  } else {
-    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<float, 128, false>, pl.G, 128, pl.clusters_fwd, pl.fwd_dyn_smem, s, p)
-                     : launch_cluster(mixer_fwd_kernel<float, 256, false>, pl.G, 256, pl.clusters_fwd, pl.fwd_dyn_smem, s, p);
-  }
-  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
-  return SPARC_OK;
+  rc = forward_params(a, pl, L, static_cast<char*>(a->workspace), &p);
+  if (rc != SPARC_OK) return rc;
+  return launch_forward(pl, p, static_cast<cudaStream_t>(stream));
 }
 
 int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
@@ -1046,20 +922,13 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
   p.deterministic = a->deterministic;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
-  const size_t dyn = pl.bwd_dyn_smem;
-  if (a->dtype == SPARC_DTYPE_BF16) {
-    e = pl.NT == 128 ? launch_cluster(mixer_bwd_kernel<__nv_bfloat16, 128, true>, pl.G, 128, pl.clusters_bwd, dyn, s, p)
-                     : launch_cluster(mixer_bwd_kernel<__nv_bfloat16, 256, true>, pl.G, 256, pl.clusters_bwd, dyn, s, p);
-  } else {
-    e = pl.NT == 128 ? launch_cluster(mixer_bwd_kernel<float, 128, false>, pl.G, 128, pl.clusters_bwd, dyn, s, p)
-                     : launch_cluster(mixer_bwd_kernel<float, 256, false>, pl.G, 256, pl.clusters_bwd, dyn, s, p);
-  }
+  void* k = a->dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::bwd(pl.NTb) : Kernels<float>::bwd(pl.NTb);
+  cudaError_t e = launch_cluster(k, pl.Gb, pl.NTb, pl.clusters_bwd, pl.bwd_smem, s, p);
   if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
   ReduceParams r;
   r.part = p.part;
   r.clusters = pl.clusters_bwd;
-  r.Mp = pl.Mp;
+  r.Mp = pl.Mpb;
   r.M = p.M;
   r.W = p.W;
   r.theta_log = a->theta_log;
@@ -1071,7 +940,7 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   r.g_energy = a->grad_energy_response;
   r.g_phase_dir = a->grad_phase_direction;
   r.g_radial_dir = a->grad_radial_direction;
-  mixer_reduce_kernel<<<dim3((pl.Mp + 31) / 32, kPartModes), dim3(32, kReduceWarps), 0, s>>>(r);
+  mixer_reduce_kernel<<<dim3((pl.Mpb + 31) / 32, kPartModes), dim3(32, kReduceWarps), 0, s>>>(r);
   e = cudaGetLastError();
   if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
   return SPARC_OK;
@@ -1132,53 +1001,19 @@ int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
     set_err(msg);
     return SPARC_ERR_WORKSPACE;
   }
-  if (!a->x || !a->y || !a->carry || !a->nu_log || !a->theta_log || !a->phase_direction ||
-      !a->radial_direction || !a->write_log_gain || !a->write_phase_response || !a->write_radial_response) {
-    set_err("null tensor pointer"); return SPARC_ERR_ARG;
-  }
-  if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->last_r == nullptr) != (a->last_i == nullptr)) {
-    set_err("h0 / last pointers must be given in pairs"); return SPARC_ERR_ARG;
-  }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); set_err("no current CUDA device"); return SPARC_ERR_LAUNCH; }
   char* ws = static_cast<char*>(noalloc_scratch(dev));
   if (ws == nullptr) { set_err("cudaGetSymbolAddress failed for the built-in scratch"); return SPARC_ERR_LAUNCH; }
+  FwdParams p;
+  rc = forward_params(a, pl, L, ws, &p);
+  if (rc != SPARC_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the array keeps the previous call's contents: its flag words, laid out for another shape,
   // could alias this launch's, so they start from zero on every call (a memset, no allocation)
-  cudaError_t e = cudaMemsetAsync(ws + L.flags, 0, (size_t)pl.tiles * pl.G * sizeof(unsigned), s);
+  const cudaError_t e = cudaMemsetAsync(ws + L.flags, 0, L.agg - L.flags, s);
   if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
-  FwdParams p;
-  p.x = a->x;
-  p.y = a->y;
-  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
-                        a->write_log_gain, a->write_phase_response, a->write_radial_response};
-  p.h0_r = a->h0_r;
-  p.h0_i = a->h0_i;
-  p.last_r = a->last_r;
-  p.last_i = a->last_i;
-  p.carry = reinterpret_cast<float2*>(a->carry);
-  p.ls = reinterpret_cast<LaunchState*>(ws);
-  p.flags = reinterpret_cast<unsigned*>(ws + L.flags);
-  p.agg = reinterpret_cast<float4*>(ws + L.agg);
-  p.B = a->batch;
-  p.T = a->length;
-  p.W = a->width;
-  p.M = a->width / 2;
-  p.chunks = pl.chunks;
-  p.tiles = pl.tiles;
-  p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
-  p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
-  p.deterministic = a->deterministic;
-  if (a->dtype == SPARC_DTYPE_BF16) {
-    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 128, true>, pl.G, 128, pl.clusters_fwd, pl.fwd_dyn_smem, s, p)
-                     : launch_cluster(mixer_fwd_kernel<__nv_bfloat16, 256, true>, pl.G, 256, pl.clusters_fwd, pl.fwd_dyn_smem, s, p);
-  } else {
-    e = pl.NT == 128 ? launch_cluster(mixer_fwd_kernel<float, 128, false>, pl.G, 128, pl.clusters_fwd, pl.fwd_dyn_smem, s, p)
-                     : launch_cluster(mixer_fwd_kernel<float, 256, false>, pl.G, 256, pl.clusters_fwd, pl.fwd_dyn_smem, s, p);
-  }
-  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
-  return SPARC_OK;
+  return launch_forward(pl, p, s);
 }
 
 int sparc_read_status(const void* workspace, unsigned* status, void* stream) {

@@ -49,7 +49,7 @@ class _SparcMixerFunction(torch.autograd.Function):
         if h0_r is not None:
             h0 = (_f32(h0_r), _f32(h0_i))
         y = torch.empty_like(x)
-        chunks = L.sparc_mixer_carry_chunks(T)
+        chunks = L.sparc_mixer_carry_chunks(T, dt)
         carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
         last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
         last_i = torch.empty((B, M), dtype=torch.float32, device=dev)

@@ -48,9 +48,12 @@ def test_struct_layouts_match_header():
 
 
 def test_host_only_queries(lib):
-    assert lib.sparc_mixer_chunk_tokens() == 16
-    assert lib.sparc_mixer_carry_chunks(2048) == 128
-    assert lib.sparc_mixer_carry_chunks(37) == 3
+    from sparc_b200 import _lib
+
+    assert lib.sparc_mixer_chunk_tokens(_lib.DTYPE_BF16) == 16
+    assert lib.sparc_mixer_chunk_tokens(_lib.DTYPE_F32) == 8
+    assert lib.sparc_mixer_carry_chunks(2048, _lib.DTYPE_BF16) == 128
+    assert lib.sparc_mixer_carry_chunks(37, _lib.DTYPE_F32) == 5
     assert lib.sparc_real_carry_chunks(17) == 2
 
 

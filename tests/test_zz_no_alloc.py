@@ -41,7 +41,7 @@ def _call(entry, x, params, workspace=None):
     B, T, W = x.shape
     M = W // 2
     y = torch.empty_like(x)
-    carry = torch.empty((B, L.sparc_mixer_carry_chunks(T), M, 2), device=x.device)
+    carry = torch.empty((B, L.sparc_mixer_carry_chunks(T, _lib.dtype_code(x.dtype)), M, 2), device=x.device)
     last_r = torch.empty((B, M), device=x.device)
     last_i = torch.empty((B, M), device=x.device)
     ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel())
