@@ -23,6 +23,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <cstdio>
 #include <mutex>
 
@@ -106,6 +107,15 @@ __device__ __forceinline__ TokenCoef token_coef(const ModeConst& mc, float E, fl
   }
   k.gain = mc.gconst * sqrt_approx(k.num) * k.gate;
   return k;
+}
+
+// Transition a = rho e^{i(theta + (1-rho) delta)} alone (the reverse local pass needs no write).
+__device__ __forceinline__ float2 token_transition(const ModeConst& mc, float E, float delta) {
+  const float rho = ex2_approx(-mc.nl2e * E);
+  float s, c;
+  sincos_halfpi(fmaf(-rho, delta, delta), &s, &c);
+  const float rct = rho * mc.ct, rst = rho * mc.st;
+  return make_float2(fmaf(rct, c, -rst * s), fmaf(rst, c, rct * s));
 }
 
 // Warp transpose-reduce of N values per lane (N a power of two, N <= 32). Afterwards lane l
@@ -326,276 +336,7 @@ __device__ __forceinline__ void take_ticket(LaunchState* ls, unsigned* s_ticket,
 
 #include "mixer_fwd.cuh"
 
-// ------------------------------------------------------------------------------ backward
-constexpr int kPartModes = 9;  // nu, theta (sum of phase grads), wlg, wpr, wrr, D0r, D0i, D1r, D1i
-
-struct BwdParams {
-  const void* x;
-  const void* dy;
-  void* dx;
-  MixerParamPtrs pp;
-  const float* h0_r;
-  const float* h0_i;
-  const float* glast_r;
-  const float* glast_i;
-  float* gh0_r;
-  float* gh0_i;
-  const float2* carry;  // forward inclusive states [B, chunks, M]
-  LaunchState* ls;
-  unsigned* flags;
-  float4* agg;
-  float2* incl;         // reverse inclusive carries [tiles, Mp]
-  double* part;         // [clusters][kPartModes][Mp] then [clusters][2] bias partials
-  long long B, T;
-  int W, M, chunks;
-  long long tiles;
-  unsigned max_spin;
-  int deterministic;
-  long long inject_unpublished;
-};
-
-template <int C, int NT>
-struct BwdSmem {
-  float xr[C][NT], xi[C][NT];
-  float gr[C][NT], gi[C][NT];  // dy, masked by the relu in pass 0
-  float hr[C][NT], hi[C][NT];  // replayed states
-  float ar[C][NT], ai[C][NT];  // transitions, overwritten by the write-path dx in pass B
-  double acc[kPartModes][NT];  // per-mode parameter-gradient accumulators across tiles
-};
-
-template <typename TIO, int NT, bool kFast, int C>
-__global__ void __launch_bounds__(NT) mixer_bwd_kernel(const BwdParams p) {
-  constexpr int NW = NT / 32;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int g = (int)cluster.block_rank();
-  const int G = (int)cluster.num_blocks();
-  const int tid = threadIdx.x;
-  const int M = p.M, W = p.W;
-  const int m = g * NT + tid;
-  const int Mp = G * NT;
-  const bool active = m < M;
-  const long long B = p.B, T = p.T;
-  const int chunks = p.chunks;
-
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  BwdSmem<C, NT>& S = *reinterpret_cast<BwdSmem<C, NT>*>(smem_raw);
-  __shared__ float s_warp[NW][2 * C];
-  __shared__ float s_cta_ctl[2 * C];
-  __shared__ float s_cta_grad[2 * C];
-  __shared__ float s_proj[2 * C];
-  __shared__ float s_tot[2 * C];
-  __shared__ float s_E[C], s_delta[C], s_tau0[C], s_tau1[C], s_dp0[C], s_dp1[C];
-  __shared__ unsigned s_ticket[2];
-  __shared__ unsigned s_win[2];
-  __shared__ unsigned s_pred;
-  __shared__ double s_bias[2];
-
-  const ModeConst mc = load_mode(p.pp, m, M, active);
-  const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
-  LookbackCtx lc{p.ls, p.flags, p.agg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, G, Mp, B,
-                 p.deterministic != 0};
-#pragma unroll
-  for (int q = 0; q < kPartModes; ++q) S.acc[q][tid] = 0.0;
-  if (tid == 0) s_bias[0] = s_bias[1] = 0.0;
-
-  for (int it = 0;; ++it) {
-    // take a ticket only when ready to start it (a held, unstarted ticket stalls successors)
-    take_ticket(p.ls, s_ticket, it & 1, g);
-    cluster.sync();
-    const long long ticket = *cluster.map_shared_rank(&s_ticket[it & 1], 0);
-    if (ticket >= p.tiles) {
-      cluster.sync();
-      break;
-    }
-    const long long b = ticket % B;
-    const int c = chunks - 1 - (int)(ticket / B);
-    const long long t0 = (long long)c * C;
-    const int nvalid = (int)(T - t0 < C ? T - t0 : C);
-    const long long row0 = (b * T + t0) * W;
-    const TIO* xrow = static_cast<const TIO*>(p.x) + row0;
-    const TIO* dyrow = static_cast<const TIO*>(p.dy) + row0;
-    if (tid == 0) s_pred = c < chunks - 1 ? ld_acquire(p.flags + (ticket - B) * G + g) : 0u;
-
-    float v[2 * C];
-#pragma unroll
-    for (int t = 0; t < C; ++t) {
-      const bool ok = active && t < nvalid;
-      const float xr = ok ? Io<TIO>::load(xrow + (long long)t * W + m) : 0.0f;
-      const float xi = ok ? Io<TIO>::load(xrow + (long long)t * W + M + m) : 0.0f;
-      S.xr[t][tid] = xr;
-      S.xi[t][tid] = xi;
-      S.gr[t][tid] = ok ? Io<TIO>::load(dyrow + (long long)t * W + m) : 0.0f;
-      S.gi[t][tid] = ok ? Io<TIO>::load(dyrow + (long long)t * W + M + m) : 0.0f;
-      v[t] = fmaf(xr, mc.d0r, xi * mc.d0i);
-      v[C + t] = fmaf(xr, mc.d1r, xi * mc.d1i);
-    }
-    cluster_reduce<2 * C, NT>(v, s_warp, s_cta_ctl, s_proj, cluster);
-    token_controls<C>(s_proj, bias0, bias1, s_E, s_delta, s_tau0, s_tau1);
-
-    // carry-in of this chunk from the forward
-    float2 hin = make_float2(0.0f, 0.0f);
-    if (active) {
-      if (c > 0) hin = p.carry[(b * chunks + c - 1) * M + m];
-      else if (p.h0_r != nullptr) hin = make_float2(p.h0_r[b * M + m], p.h0_i[b * M + m]);
-    }
-
-    // pass 0: replay states, relu masks, chunk product
-    float2 P = make_float2(1.0f, 0.0f);
-    {
-      float2 h = hin;
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        float2 a = make_float2(1.0f, 0.0f);
-        if (t < nvalid) {
-          const TokenCoef k = token_coef<kFast>(mc, s_E[t], s_delta[t], s_tau0[t], s_tau1[t]);
-          a = k.a;
-          const float2 bw = make_float2(k.gain * tanh_t<kFast>(S.xr[t][tid]),
-                                        k.gain * tanh_t<kFast>(S.xi[t][tid]));
-          h = cfma(a, h, bw);
-          if (!(h.x > 0.0f)) S.gr[t][tid] = 0.0f;
-          if (!(h.y > 0.0f)) S.gi[t][tid] = 0.0f;
-        }
-        S.hr[t][tid] = h.x;
-        S.hi[t][tid] = h.y;
-        S.ar[t][tid] = a.x;
-        S.ai[t][tid] = a.y;
-        P = cmul(a, P);
-      }
-    }
-    // pass A: local reverse adjoint from zero -> aggregate (conj P, Qr)
-    float2 Qr = make_float2(0.0f, 0.0f);
-#pragma unroll
-    for (int t = C - 1; t >= 0; --t) {
-      Qr.x += S.gr[t][tid];
-      Qr.y += S.gi[t][tid];
-      const float ar = S.ar[t][tid], ai = S.ai[t][tid];
-      Qr = make_float2(fmaf(ar, Qr.x, ai * Qr.y), fmaf(ar, Qr.y, -ai * Qr.x));
-    }
-    const float2 Pc = make_float2(P.x, -P.y);
-
-    float2 kin = make_float2(0.0f, 0.0f);
-    const bool publish = ticket != p.inject_unpublished;
-    if (c == chunks - 1) {
-      if (p.glast_r != nullptr && active) kin = make_float2(p.glast_r[b * M + m], p.glast_i[b * M + m]);
-    } else {
-      const float2* incl = p.incl;
-      const long long Bq = B;
-      const float2 A1[1] = {Pc}, B1[1] = {Qr};
-      float2 k1[1];
-      lookback<1>(lc, ticket, g, chunks - 1 - c, A1, B1, publish, s_pred, s_win, m,
-                  [&](int j, float2 (&h)[1]) { h[0] = __ldcg(incl + (ticket - j * Bq) * Mp + m); }, k1);
-      kin = k1[0];
-    }
-    const float2 kout = cfma(Pc, kin, Qr);
-    if (publish) {
-      p.incl[ticket * Mp + m] = kout;
-      publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-    }
-    if (c == 0 && p.gh0_r != nullptr && active) {
-      p.gh0_r[b * M + m] = kout.x;
-      p.gh0_i[b * M + m] = kout.y;
-    }
-
-    // pass B: true adjoint, all gradients
-    float f_nu = 0.0f, f_th = 0.0f, f_wlg = 0.0f, f_wpr = 0.0f, f_wrr = 0.0f;
-    float2 lam = kin;
-#pragma unroll
-    for (int t = C - 1; t >= 0; --t) {
-      if (t < nvalid) {
-        lam.x += S.gr[t][tid];
-        lam.y += S.gi[t][tid];
-        const float2 prev = t > 0 ? make_float2(S.hr[t - 1][tid], S.hi[t - 1][tid]) : hin;
-        const float ar = S.ar[t][tid], ai = S.ai[t][tid];
-        const float gar = fmaf(lam.x, prev.x, lam.y * prev.y);
-        const float gai = fmaf(lam.y, prev.x, -lam.x * prev.y);
-        const float E = s_E[t], delta = s_delta[t];
-        const TokenCoef k = token_coef<kFast>(mc, E, delta, s_tau0[t], s_tau1[t]);
-        const float pg = fmaf(gai, ar, -gar * ai);
-        const float radial = k.z * fmaf(k.rho * delta, pg, -fmaf(gar, ar, gai * ai));
-        const float dscan = pg - k.rho * pg;
-        f_th += pg;
-        const float cr = tanh_t<kFast>(S.xr[t][tid]);
-        const float ci = tanh_t<kFast>(S.xi[t][tid]);
-        const float gg = k.gain * fmaf(lam.x, cr, lam.y * ci);
-        const float gq = gg * fmaf(-0.5f, k.gate, 1.0f);
-        const float dyn = k.z * k.rho * k.rho * rcp_approx(k.num);
-        v[t] = radial + fmaf(gg, dyn, gq * mc.wrr * kInvLn16);
-        v[C + t] = fmaf(gq * mc.wpr, kInvHalfPi, dscan);
-        f_nu += radial + gg * (dyn - mc.stat);
-        f_wlg += gg;
-        f_wpr = fmaf(gq, s_tau0[t], f_wpr);
-        f_wrr = fmaf(gq, s_tau1[t], f_wrr);
-        S.ar[t][tid] = lam.x * k.gain * fmaf(-cr, cr, 1.0f);
-        S.ai[t][tid] = lam.y * k.gain * fmaf(-ci, ci, 1.0f);
-        lam = make_float2(fmaf(ar, lam.x, ai * lam.y), fmaf(ar, lam.y, -ai * lam.x));
-      } else {
-        v[t] = 0.0f;
-        v[C + t] = 0.0f;
-      }
-    }
-    if (!active) {
-      f_nu = f_th = f_wlg = f_wpr = f_wrr = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 2 * C; ++i) v[i] = 0.0f;
-    }
-    S.acc[0][tid] += f_nu;
-    S.acc[1][tid] += f_th;
-    S.acc[2][tid] += f_wlg;
-    S.acc[3][tid] += f_wpr;
-    S.acc[4][tid] += f_wrr;
-
-    cluster_reduce<2 * C, NT>(v, s_warp, s_cta_grad, s_tot, cluster);
-    if (tid < C) {
-      const int t = tid;
-      const float tau0 = s_tau0[t], tau1 = s_tau1[t];
-      s_dp1[t] = t < nvalid ? s_tot[t] * kLn16 * fmaf(-tau1, tau1, 1.0f) : 0.0f;
-      s_dp0[t] = t < nvalid ? s_tot[C + t] * kHalfPi * fmaf(-tau0, tau0, 1.0f) : 0.0f;
-    }
-    __syncthreads();
-    TIO* dxrow = static_cast<TIO*>(p.dx) + row0;
-    float f_d0r = 0.0f, f_d0i = 0.0f, f_d1r = 0.0f, f_d1i = 0.0f;
-#pragma unroll
-    for (int t = 0; t < C; ++t) {
-      if (t < nvalid) {
-        const float dp0 = s_dp0[t], dp1 = s_dp1[t];
-        const float xr = S.xr[t][tid], xi = S.xi[t][tid];
-        if (active) {
-          Io<TIO>::store(dxrow + (long long)t * W + m, fmaf(dp0, mc.d0r, fmaf(dp1, mc.d1r, S.ar[t][tid])));
-          Io<TIO>::store(dxrow + (long long)t * W + M + m,
-                         fmaf(dp0, mc.d0i, fmaf(dp1, mc.d1i, S.ai[t][tid])));
-        }
-        f_d0r = fmaf(xr, dp0, f_d0r);
-        f_d0i = fmaf(xi, dp0, f_d0i);
-        f_d1r = fmaf(xr, dp1, f_d1r);
-        f_d1i = fmaf(xi, dp1, f_d1i);
-      }
-    }
-    S.acc[5][tid] += f_d0r;
-    S.acc[6][tid] += f_d0i;
-    S.acc[7][tid] += f_d1r;
-    S.acc[8][tid] += f_d1i;
-    if (g == 0 && tid == 0) {
-      float s0 = 0.0f, s1 = 0.0f;
-      for (int t = 0; t < C; ++t) {
-        s0 += s_dp0[t];
-        s1 += s_dp1[t];
-      }
-      s_bias[0] += s0;
-      s_bias[1] += s1;
-    }
-  }
-  // per-cluster partial parameter gradients (reduced in a fixed order by mixer_reduce_kernel)
-  const long long k = blockIdx.y;
-  double* part = p.part + k * (long long)kPartModes * Mp;
-#pragma unroll
-  for (int q = 0; q < kPartModes; ++q) part[(long long)q * Mp + m] = S.acc[q][tid];
-  if (g == 0 && tid == 0) {
-    double* pb = p.part + (long long)gridDim.y * kPartModes * Mp + 2 * k;
-    pb[0] = s_bias[0];
-    pb[1] = s_bias[1];
-  }
-  finish_launch(p.ls);
-}
+#include "mixer_bwd.cuh"
 
 struct ReduceParams {
   const double* part;
@@ -657,7 +398,7 @@ struct Plan {
   int Gf, Mpf, clusters_fwd;  // forward: CTAs of 256 modes
   size_t fwd_smem;
   bool fvec, tma;
-  int NTb, Gb, Mpb, clusters_bwd;  // backward: CTAs of NTb modes
+  int Gb, Mpb, clusters_bwd;  // backward: CTAs of 256 modes
   size_t bwd_smem;
 };
 
@@ -698,11 +439,11 @@ struct Kernels {
   static void* fwd(bool vec) {
     return vec ? (void*)mixer_fwd_kernel<TIO, C, kFast, true> : (void*)mixer_fwd_kernel<TIO, C, kFast, false>;
   }
-  static void* bwd(int NT) {
-    return NT == 128 ? (void*)mixer_bwd_kernel<TIO, 128, kFast, C> : (void*)mixer_bwd_kernel<TIO, 256, kFast, C>;
+  static void* bwd(bool vec) {
+    return vec ? (void*)mixer_bwd_kernel<TIO, C, kFast, true> : (void*)mixer_bwd_kernel<TIO, C, kFast, false>;
   }
   static size_t fwd_smem() { return sizeof(FwdSmem<TIO, C, kFast>); }
-  static size_t bwd_smem(int NT) { return NT == 128 ? sizeof(BwdSmem<C, 128>) : sizeof(BwdSmem<C, 256>); }
+  static size_t bwd_smem() { return sizeof(BwdSmem<TIO, C>); }
 };
 
 static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
@@ -721,13 +462,12 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   pl->fvec = (M % 2) == 0;
   const size_t s = dtype == SPARC_DTYPE_BF16 ? 2 : 4;
   pl->tma = ((size_t)W * s) % 16 == 0 && ((size_t)M * s) % 16 == 0;
-  pl->NTb = M <= 8 * 128 ? 128 : 256;
-  pl->Gb = (M + pl->NTb - 1) / pl->NTb;
-  pl->Mpb = pl->Gb * pl->NTb;
+  pl->Gb = (M + kBwdModes - 1) / kBwdModes;
+  pl->Mpb = pl->Gb * kBwdModes;
 
   int dev = 0;
   cudaGetDevice(&dev);
-  struct Key { int dev, dtype, Gf, Gb, NTb, vec; int nf, nb; };
+  struct Key { int dev, dtype, Gf, Gb, vec; int nf, nb; };
   static std::mutex mu;
   static Key cache[64];
   static int ncache = 0;
@@ -735,25 +475,25 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   int nf = -1, nb = -1;
   for (int i = 0; i < ncache; ++i) {
     const Key& k = cache[i];
-    if (k.dev == dev && k.dtype == dtype && k.Gf == pl->Gf && k.Gb == pl->Gb && k.NTb == pl->NTb && k.vec == (int)pl->fvec) {
+    if (k.dev == dev && k.dtype == dtype && k.Gf == pl->Gf && k.Gb == pl->Gb && k.vec == (int)pl->fvec) {
       nf = k.nf;
       nb = k.nb;
     }
   }
   if (dtype == SPARC_DTYPE_BF16) {
     pl->fwd_smem = Kernels<__nv_bfloat16>::fwd_smem();
-    pl->bwd_smem = Kernels<__nv_bfloat16>::bwd_smem(pl->NTb);
+    pl->bwd_smem = Kernels<__nv_bfloat16>::bwd_smem();
   } else {
     pl->fwd_smem = Kernels<float>::fwd_smem();
-    pl->bwd_smem = Kernels<float>::bwd_smem(pl->NTb);
+    pl->bwd_smem = Kernels<float>::bwd_smem();
   }
   if (nf < 0) {
     void* fk = dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::fwd(pl->fvec) : Kernels<float>::fwd(pl->fvec);
-    void* bk = dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::bwd(pl->NTb) : Kernels<float>::bwd(pl->NTb);
+    void* bk = dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::bwd(pl->fvec) : Kernels<float>::bwd(pl->fvec);
     nf = max_clusters(fk, pl->Gf, kFwdThreads, pl->fwd_smem);
-    nb = max_clusters(bk, pl->Gb, pl->NTb, pl->bwd_smem);
+    nb = max_clusters(bk, pl->Gb, kBwdThreads, pl->bwd_smem);
     if (nf <= 0 || nb <= 0) { set_err("cluster occupancy query failed"); return SPARC_ERR_LAUNCH; }
-    if (ncache < 64) cache[ncache++] = Key{dev, dtype, pl->Gf, pl->Gb, pl->NTb, (int)pl->fvec, nf, nb};
+    if (ncache < 64) cache[ncache++] = Key{dev, dtype, pl->Gf, pl->Gb, (int)pl->fvec, nf, nb};
   }
   pl->clusters_fwd = (int)std::min<long long>(nf, pl->tiles);
   pl->clusters_bwd = (int)std::min<long long>(nb, pl->tiles);
@@ -921,9 +661,10 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
   p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
   p.deterministic = a->deterministic;
+  p.use_tma = pl.tma && (reinterpret_cast<uintptr_t>(a->x) % 16 == 0) && (reinterpret_cast<uintptr_t>(a->dy) % 16 == 0) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  void* k = a->dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::bwd(pl.NTb) : Kernels<float>::bwd(pl.NTb);
-  cudaError_t e = launch_cluster(k, pl.Gb, pl.NTb, pl.clusters_bwd, pl.bwd_smem, s, p);
+  void* k = a->dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::bwd(pl.fvec) : Kernels<float>::bwd(pl.fvec);
+  cudaError_t e = launch_cluster(k, pl.Gb, kBwdThreads, pl.clusters_bwd, pl.bwd_smem, s, p);
   if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
   ReduceParams r;
   r.part = p.part;

@@ -225,125 +225,132 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_kernel(const FwdParams 
       }
       __syncthreads();
     }
-    const unsigned pst = S.pred;
-    const bool pred_ready = c == 0 || (!lc.deterministic && ((pst >> 2) == (lc.epoch & 0x3fffffffu)) &&
-                                       (pst & 3u) == kFlagInclusive);
-    const bool publish = ticket != p.inject_unpublished;
-    TIO* yrow = static_cast<TIO*>(p.y) + (b * T + t0) * W;
-    float2 hout0, hout1;
-    if (pred_ready) {
-      float2 h0 = make_float2(0.0f, 0.0f), h1 = make_float2(0.0f, 0.0f);
-      if (c > 0) {
-        const float2* cp = p.carry + (b * p.chunks + (c - 1)) * M + m0;
-        if (act0) h0 = __ldcg(cp);
-        if (act1) h1 = __ldcg(cp + 1);
-      } else if (p.h0_r != nullptr) {
-        if (act0) h0 = make_float2(p.h0_r[b * M + m0], p.h0_i[b * M + m0]);
-        if (act1) h1 = make_float2(p.h0_r[b * M + m0 + 1], p.h0_i[b * M + m0 + 1]);
-      }
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        if (t < nvalid) {
-          const float4 k4 = S.ctl[t];
-          const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
-          const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-          const TokenCoef k0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
-          const TokenCoef k1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
-          h0 = cfma(k0.a, h0, make_float2(k0.gain * tanh_t<kFast>(xr.x), k0.gain * tanh_t<kFast>(xi.x)));
-          h1 = cfma(k1.a, h1, make_float2(k1.gain * tanh_t<kFast>(xr.y), k1.gain * tanh_t<kFast>(xi.y)));
-          store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, h0, h1);
+    // the tile body, instantiated branch-free for full chunks (so the compiler can interleave
+    // independent tokens) and with guards for the ragged last chunk
+    auto tile_body = [&](auto full_tag) {
+      constexpr bool kFull = decltype(full_tag)::value;
+      const unsigned pst = S.pred;
+      const bool pred_ready = c == 0 || (!lc.deterministic && ((pst >> 2) == (lc.epoch & 0x3fffffffu)) &&
+                                         (pst & 3u) == kFlagInclusive);
+      const bool publish = ticket != p.inject_unpublished;
+      TIO* yrow = static_cast<TIO*>(p.y) + (b * T + t0) * W;
+      float2 hout0, hout1;
+      if (pred_ready) {
+        float2 h0 = make_float2(0.0f, 0.0f), h1 = make_float2(0.0f, 0.0f);
+        if (c > 0) {
+          const float2* cp = p.carry + (b * p.chunks + (c - 1)) * M + m0;
+          if (act0) h0 = __ldcg(cp);
+          if (act1) h1 = __ldcg(cp + 1);
+        } else if (p.h0_r != nullptr) {
+          if (act0) h0 = make_float2(p.h0_r[b * M + m0], p.h0_i[b * M + m0]);
+          if (act1) h1 = make_float2(p.h0_r[b * M + m0 + 1], p.h0_i[b * M + m0 + 1]);
         }
-      }
-      hout0 = h0;
-      hout1 = h1;
-      if (publish) {
-        float2* cp = p.carry + (b * p.chunks + c) * M + m0;
-        if (act0) cp[0] = hout0;
-        if (act1) cp[1] = hout1;
-        publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-      }
-    } else {
-      float2 P0 = make_float2(1.0f, 0.0f), Q0 = make_float2(0.0f, 0.0f);
-      float2 P1 = P0, Q1 = Q0;
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        float2 a0 = make_float2(1.0f, 0.0f), a1 = a0, b0 = make_float2(0.0f, 0.0f), b1 = b0;
-        float g0 = 0.0f, g1 = 0.0f;
-        if (t < nvalid) {
-          const float4 k4 = S.ctl[t];
-          const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
-          const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-          const TokenCoef k0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
-          const TokenCoef k1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
-          a0 = k0.a;
-          a1 = k1.a;
-          g0 = k0.gain;
-          g1 = k1.gain;
-          b0 = make_float2(g0 * tanh_t<kFast>(xr.x), g0 * tanh_t<kFast>(xi.x));
-          b1 = make_float2(g1 * tanh_t<kFast>(xr.y), g1 * tanh_t<kFast>(xi.y));
-        }
-        *reinterpret_cast<float4*>(&S.a[t][2 * tid]) = make_float4(a0.x, a0.y, a1.x, a1.y);
-        if constexpr (kFast) {
-          *reinterpret_cast<float2*>(&S.w[t][2 * tid]) = make_float2(g0, g1);
-        } else {
-          *reinterpret_cast<float4*>(&S.w[t][4 * tid]) = make_float4(b0.x, b0.y, b1.x, b1.y);
-        }
-        Q0 = cfma(a0, Q0, b0);
-        P0 = cmul(a0, P0);
-        Q1 = cfma(a1, Q1, b1);
-        P1 = cmul(a1, P1);
-      }
-      const float2* carry = p.carry;
-      const int chunks = p.chunks;
-      float2 A[2] = {P0, P1}, Bv[2] = {Q0, Q1}, hin[2];
-      lookback<2>(lc, ticket, g, c, A, Bv, publish, pst, S.win, m0,
-                  [&](int j, float2 (&h)[2]) {
-                    const float2* cp = carry + (b * chunks + (c - j)) * M + m0;
-                    h[0] = act0 ? __ldcg(cp) : make_float2(0.0f, 0.0f);
-                    h[1] = act1 ? __ldcg(cp + 1) : make_float2(0.0f, 0.0f);
-                  },
-                  hin);
-      hout0 = cfma(P0, hin[0], Q0);
-      hout1 = cfma(P1, hin[1], Q1);
-      if (publish) {
-        float2* cp = p.carry + (b * p.chunks + c) * M + m0;
-        if (act0) cp[0] = hout0;
-        if (act1) cp[1] = hout1;
-        publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-      }
-      float2 h0 = hin[0], h1 = hin[1];
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        if (t < nvalid) {
-          const float4 a4 = *reinterpret_cast<const float4*>(&S.a[t][2 * tid]);
-          float2 b0, b1;
-          if constexpr (kFast) {
-            const float2 gg = *reinterpret_cast<const float2*>(&S.w[t][2 * tid]);
+  #pragma unroll
+        for (int t = 0; t < C; ++t) {
+          if (kFull || t < nvalid) {
+            const float4 k4 = S.ctl[t];
             const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
             const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-            b0 = make_float2(gg.x * tanh_t<kFast>(xr.x), gg.x * tanh_t<kFast>(xi.x));
-            b1 = make_float2(gg.y * tanh_t<kFast>(xr.y), gg.y * tanh_t<kFast>(xi.y));
-          } else {
-            const float4 w4 = *reinterpret_cast<const float4*>(&S.w[t][4 * tid]);
-            b0 = make_float2(w4.x, w4.y);
-            b1 = make_float2(w4.z, w4.w);
+            const TokenCoef k0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
+            const TokenCoef k1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
+            h0 = cfma(k0.a, h0, make_float2(k0.gain * tanh_t<kFast>(xr.x), k0.gain * tanh_t<kFast>(xi.x)));
+            h1 = cfma(k1.a, h1, make_float2(k1.gain * tanh_t<kFast>(xr.y), k1.gain * tanh_t<kFast>(xi.y)));
+            store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, h0, h1);
           }
-          h0 = cfma(make_float2(a4.x, a4.y), h0, b0);
-          h1 = cfma(make_float2(a4.z, a4.w), h1, b1);
-          store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, h0, h1);
+        }
+        hout0 = h0;
+        hout1 = h1;
+        if (publish) {
+          float2* cp = p.carry + (b * p.chunks + c) * M + m0;
+          if (act0) cp[0] = hout0;
+          if (act1) cp[1] = hout1;
+          publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
+        }
+      } else {
+        float2 P0 = make_float2(1.0f, 0.0f), Q0 = make_float2(0.0f, 0.0f);
+        float2 P1 = P0, Q1 = Q0;
+  #pragma unroll
+        for (int t = 0; t < C; ++t) {
+          float2 a0 = make_float2(1.0f, 0.0f), a1 = a0, b0 = make_float2(0.0f, 0.0f), b1 = b0;
+          float g0 = 0.0f, g1 = 0.0f;
+          if (kFull || t < nvalid) {
+            const float4 k4 = S.ctl[t];
+            const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
+            const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
+            const TokenCoef k0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
+            const TokenCoef k1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
+            a0 = k0.a;
+            a1 = k1.a;
+            g0 = k0.gain;
+            g1 = k1.gain;
+            b0 = make_float2(g0 * tanh_t<kFast>(xr.x), g0 * tanh_t<kFast>(xi.x));
+            b1 = make_float2(g1 * tanh_t<kFast>(xr.y), g1 * tanh_t<kFast>(xi.y));
+          }
+          *reinterpret_cast<float4*>(&S.a[t][2 * tid]) = make_float4(a0.x, a0.y, a1.x, a1.y);
+          if constexpr (kFast) {
+            *reinterpret_cast<float2*>(&S.w[t][2 * tid]) = make_float2(g0, g1);
+          } else {
+            *reinterpret_cast<float4*>(&S.w[t][4 * tid]) = make_float4(b0.x, b0.y, b1.x, b1.y);
+          }
+          Q0 = cfma(a0, Q0, b0);
+          P0 = cmul(a0, P0);
+          Q1 = cfma(a1, Q1, b1);
+          P1 = cmul(a1, P1);
+        }
+        const float2* carry = p.carry;
+        const int chunks = p.chunks;
+        float2 A[2] = {P0, P1}, Bv[2] = {Q0, Q1}, hin[2];
+        lookback<2>(lc, ticket, g, c, A, Bv, publish, pst, S.win, m0,
+                    [&](int j, float2 (&h)[2]) {
+                      const float2* cp = carry + (b * chunks + (c - j)) * M + m0;
+                      h[0] = act0 ? __ldcg(cp) : make_float2(0.0f, 0.0f);
+                      h[1] = act1 ? __ldcg(cp + 1) : make_float2(0.0f, 0.0f);
+                    },
+                    hin);
+        hout0 = cfma(P0, hin[0], Q0);
+        hout1 = cfma(P1, hin[1], Q1);
+        if (publish) {
+          float2* cp = p.carry + (b * p.chunks + c) * M + m0;
+          if (act0) cp[0] = hout0;
+          if (act1) cp[1] = hout1;
+          publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
+        }
+        float2 h0 = hin[0], h1 = hin[1];
+  #pragma unroll
+        for (int t = 0; t < C; ++t) {
+          if (kFull || t < nvalid) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&S.a[t][2 * tid]);
+            float2 b0, b1;
+            if constexpr (kFast) {
+              const float2 gg = *reinterpret_cast<const float2*>(&S.w[t][2 * tid]);
+              const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
+              const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
+              b0 = make_float2(gg.x * tanh_t<kFast>(xr.x), gg.x * tanh_t<kFast>(xi.x));
+              b1 = make_float2(gg.y * tanh_t<kFast>(xr.y), gg.y * tanh_t<kFast>(xi.y));
+            } else {
+              const float4 w4 = *reinterpret_cast<const float4*>(&S.w[t][4 * tid]);
+              b0 = make_float2(w4.x, w4.y);
+              b1 = make_float2(w4.z, w4.w);
+            }
+            h0 = cfma(make_float2(a4.x, a4.y), h0, b0);
+            h1 = cfma(make_float2(a4.z, a4.w), h1, b1);
+            store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, h0, h1);
+          }
         }
       }
-    }
-    if (c == p.chunks - 1 && p.last_r != nullptr) {
-      if (act0) {
-        p.last_r[b * M + m0] = hout0.x;
-        p.last_i[b * M + m0] = hout0.y;
+      if (c == p.chunks - 1 && p.last_r != nullptr) {
+        if (act0) {
+          p.last_r[b * M + m0] = hout0.x;
+          p.last_i[b * M + m0] = hout0.y;
+        }
+        if (act1) {
+          p.last_r[b * M + m0 + 1] = hout1.x;
+          p.last_i[b * M + m0 + 1] = hout1.y;
+        }
       }
-      if (act1) {
-        p.last_r[b * M + m0 + 1] = hout1.x;
-        p.last_i[b * M + m0 + 1] = hout1.y;
-      }
-    }
+    };
+    if (nvalid == C) tile_body(std::true_type{});
+    else tile_body(std::false_type{});
     __syncthreads();  // the buffer and the shared arrays are free for the next tile
   }
   if (timed_out && tid == 0) atomicOr(&p.ls->status, kStatusTimeout);
