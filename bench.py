@@ -527,9 +527,15 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="layer")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--batch", type=int, default=None, help="override the per-GPU batch (profiling runs)")
+    ap.add_argument("--seq-len", type=int, default=None, help="override the sequence length (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.batch is not None:
+        wl["batch"] = args.batch
+    if args.seq_len is not None:
+        wl["seq_len"] = args.seq_len
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
 

@@ -210,12 +210,10 @@ struct LookbackCtx {
 };
 
 __device__ __forceinline__ void publish_flag(unsigned* flag, unsigned value) {
-  // every thread's payload stores precede the barrier; one release fence makes them visible
+  // every thread's payload stores precede the barrier; thread 0's release store (cumulative
+  // over what the barrier ordered before it) makes them visible with the flag
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    st_release(flag, value);
-  }
+  if (threadIdx.x == 0) st_release(flag, value);
 }
 
 template <int MPT, typename InclFn>

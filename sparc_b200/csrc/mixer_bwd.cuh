@@ -35,6 +35,7 @@ struct BwdSmem {
   float part_ctl[2][2 * C];    // projection partials (peers read), by tile parity
   float part_grad[2][2 * C];   // dEta / dDelta partials (peers read), by tile parity
   float warp_part[kBwdThreads / 32][2 * C];
+  float vt[2 * C][kBwdThreads];   // per-thread dEta / dDelta partials of pass B, by token
   unsigned long long bar;
   long long ring[2];
   unsigned win[2];
@@ -210,6 +211,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
     // the tile body, instantiated branch-free for full chunks and with guards for the ragged last chunk
     auto tile_body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
+      constexpr int kU = kFull ? 4 : 1;  // partial unrolling keeps the kernel's code in the i-cache
       // pass 0: replay the states from the forward's carry; relu masks on dy; chunk product
       float2 hin0 = make_float2(0.0f, 0.0f), hin1 = hin0;
       if (c > 0) {
@@ -223,7 +225,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
       float2 P0 = make_float2(1.0f, 0.0f), P1 = P0;
       {
         float2 h0 = hin0, h1 = hin1;
-  #pragma unroll
+  #pragma unroll kU
         for (int t = 0; t < C; ++t) {
           if (kFull || t < nvalid) {
             const float4 k4 = S.ctl[t];
@@ -263,7 +265,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
       } else {
         // pass A: local reverse adjoint from zero -> aggregate (conj P, Qr)
         float2 q0 = make_float2(0.0f, 0.0f), q1 = q0;
-  #pragma unroll
+  #pragma unroll kU
         for (int t = C - 1; t >= 0; --t) {
           if (kFull || t < nvalid) {
             const float4 k4 = S.ctl[t];
@@ -303,12 +305,10 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
       float fa[2][5];
   #pragma unroll
       for (int q = 0; q < 5; ++q) fa[0][q] = fa[1][q] = 0.0f;
-      float v[2 * C];
       float2 lam0 = kin0, lam1 = kin1;
-  #pragma unroll
+  #pragma unroll kU
       for (int t = C - 1; t >= 0; --t) {
-        v[t] = 0.0f;
-        v[C + t] = 0.0f;
+        float ve = 0.0f, vd = 0.0f;
         if (kFull || t < nvalid) {
           const float4 k4 = S.ctl[t];
           const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
@@ -341,8 +341,8 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
             const float gg = k.gain * fmaf(lam.x, cr, lam.y * ci);
             const float gq = gg * fmaf(-0.5f, k.gate, 1.0f);
             const float dyn = k.z * k.rho * k.rho * rcp_approx(k.num);
-            v[t] += radial + fmaf(gg, dyn, gq * mc.wrr * kInvLn16);
-            v[C + t] += fmaf(gq * mc.wpr, kInvHalfPi, dscan);
+            ve += radial + fmaf(gg, dyn, gq * mc.wrr * kInvLn16);
+            vd += fmaf(gq * mc.wpr, kInvHalfPi, dscan);
             fa[q][0] += radial + gg * (dyn - mc.stat);
             fa[q][1] += pg;
             fa[q][2] += gg;
@@ -362,6 +362,8 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
           // h[t] was last read as `prev` at step t+1: its slot now holds the write-path dx
           *reinterpret_cast<float4*>(&S.h[t][2 * tid]) = dxc;
         }
+        S.vt[t][tid] = ve;
+        S.vt[C + t][tid] = vd;
       }
       if (!act0) {
         lam0 = make_float2(0.0f, 0.0f);
@@ -395,6 +397,9 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
       }
 
       // token sums over all modes -> controller gradients
+      float v[2 * C];
+#pragma unroll
+      for (int i = 0; i < 2 * C; ++i) v[i] = S.vt[i][tid];
       cluster_sum_2c<C>(v, S.warp_part, S.part_grad[par], S.tot, G, cluster);
       __syncthreads();
       if (tid < C) {
@@ -406,7 +411,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
       __syncthreads();
       TIO* dxrow = static_cast<TIO*>(p.dx) + row0;
       float fd[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-  #pragma unroll
+  #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < nvalid) {
           const float2 dp = S.dp[t];

@@ -229,6 +229,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_kernel(const FwdParams 
     // independent tokens) and with guards for the ragged last chunk
     auto tile_body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
+      constexpr int kU = kFull ? 4 : 1;  // partial unrolling keeps the kernel's code in the i-cache
       const unsigned pst = S.pred;
       const bool pred_ready = c == 0 || (!lc.deterministic && ((pst >> 2) == (lc.epoch & 0x3fffffffu)) &&
                                          (pst & 3u) == kFlagInclusive);
@@ -245,7 +246,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_kernel(const FwdParams 
           if (act0) h0 = make_float2(p.h0_r[b * M + m0], p.h0_i[b * M + m0]);
           if (act1) h1 = make_float2(p.h0_r[b * M + m0 + 1], p.h0_i[b * M + m0 + 1]);
         }
-  #pragma unroll
+  #pragma unroll kU
         for (int t = 0; t < C; ++t) {
           if (kFull || t < nvalid) {
             const float4 k4 = S.ctl[t];
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_kernel(const FwdParams 
       } else {
         float2 P0 = make_float2(1.0f, 0.0f), Q0 = make_float2(0.0f, 0.0f);
         float2 P1 = P0, Q1 = Q0;
-  #pragma unroll
+  #pragma unroll kU
         for (int t = 0; t < C; ++t) {
           float2 a0 = make_float2(1.0f, 0.0f), a1 = a0, b0 = make_float2(0.0f, 0.0f), b1 = b0;
           float g0 = 0.0f, g1 = 0.0f;
@@ -316,7 +317,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_kernel(const FwdParams 
           publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
         }
         float2 h0 = hin[0], h1 = hin[1];
-  #pragma unroll
+  #pragma unroll kU
         for (int t = 0; t < C; ++t) {
           if (kFull || t < nvalid) {
             const float4 a4 = *reinterpret_cast<const float4*>(&S.a[t][2 * tid]);

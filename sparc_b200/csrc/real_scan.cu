@@ -83,7 +83,6 @@ __device__ __forceinline__ void real_lookback(const RealParams& p, unsigned epoc
   if (!pred_ready) {
 #pragma unroll
     for (int v = 0; v < V; ++v) p.agg[ticket * p.Dp + dp0 + v] = make_float2(A[v], Bv[v]);
-    __threadfence();
     __syncthreads();
     if (tid == 0) st_release(p.flags + ticket, make_flag(epoch, kFlagAggregate));
   }
@@ -156,16 +155,25 @@ __global__ void __launch_bounds__(kRealThreads) real_fwd_kernel(const RealParams
     const TIO* pb = static_cast<const TIO*>(p.b) + base;
 
     float a[C][V], bv[C][V];
+    if (active && nvalid == C) {
+      // full chunk: unguarded loads, all in flight together
 #pragma unroll
-    for (int t = 0; t < C; ++t) {
-      if (active && t < nvalid) {
+      for (int t = 0; t < C; ++t) {
         VecIo<TIO, V>::load(pa + (long long)t * D, a[t]);
         VecIo<TIO, V>::load(pb + (long long)t * D, bv[t]);
-      } else {
+      }
+    } else {
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
-          a[t][v] = 1.0f;
-          bv[t][v] = 0.0f;
+      for (int t = 0; t < C; ++t) {
+        if (active && t < nvalid) {
+          VecIo<TIO, V>::load(pa + (long long)t * D, a[t]);
+          VecIo<TIO, V>::load(pb + (long long)t * D, bv[t]);
+        } else {
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            a[t][v] = 1.0f;
+            bv[t][v] = 0.0f;
+          }
         }
       }
     }
@@ -204,8 +212,7 @@ __global__ void __launch_bounds__(kRealThreads) real_fwd_kernel(const RealParams
 #pragma unroll
       for (int v = 0; v < V; ++v) p.carry[(b * p.chunks + c) * D + dp0 + v] = hout[v];
     }
-    __threadfence();
-    __syncthreads();
+    __syncthreads();  // thread 0's release store publishes what the barrier ordered before it
     if (tid == 0) st_release(p.flags + ticket, make_flag(epoch, kFlagInclusive));
 
     TIO* po = static_cast<TIO*>(p.out) + base;
@@ -263,25 +270,44 @@ __global__ void __launch_bounds__(kRealThreads) real_bwd_kernel(const RealParams
       float hh[V];
 #pragma unroll
       for (int v = 0; v < V; ++v) hh[v] = hin[v];
+      if (active && nvalid == C) {
+        // full chunk: unguarded loads, all in flight together
+        float bt[C][V];
 #pragma unroll
-      for (int t = 0; t < C; ++t) {
-        float bt[V];
-        if (active && t < nvalid) {
+        for (int t = 0; t < C; ++t) {
           VecIo<TIO, V>::load(pa + (long long)t * D, a[t]);
-          VecIo<TIO, V>::load(pb + (long long)t * D, bt);
+          VecIo<TIO, V>::load(pb + (long long)t * D, bt[t]);
           VecIo<TIO, V>::load(pg + (long long)t * D, g[t]);
-        } else {
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            a[t][v] = 1.0f;
-            bt[v] = 0.0f;
-            g[t][v] = 0.0f;
-          }
         }
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
-          hh[v] = fmaf(a[t][v], hh[v], bt[v]);
-          h[t][v] = hh[v];
+        for (int t = 0; t < C; ++t) {
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            hh[v] = fmaf(a[t][v], hh[v], bt[t][v]);
+            h[t][v] = hh[v];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < C; ++t) {
+          float bt[V];
+          if (active && t < nvalid) {
+            VecIo<TIO, V>::load(pa + (long long)t * D, a[t]);
+            VecIo<TIO, V>::load(pb + (long long)t * D, bt);
+            VecIo<TIO, V>::load(pg + (long long)t * D, g[t]);
+          } else {
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+              a[t][v] = 1.0f;
+              bt[v] = 0.0f;
+              g[t][v] = 0.0f;
+            }
+          }
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            hh[v] = fmaf(a[t][v], hh[v], bt[v]);
+            h[t][v] = hh[v];
+          }
         }
       }
     }
@@ -318,8 +344,7 @@ __global__ void __launch_bounds__(kRealThreads) real_bwd_kernel(const RealParams
 #pragma unroll
       for (int v = 0; v < V; ++v) p.incl[ticket * p.Dp + dp0 + v] = fmaf(P[v], kin[v], Qr[v]);
     }
-    __threadfence();
-    __syncthreads();
+    __syncthreads();  // thread 0's release store publishes what the barrier ordered before it
     if (tid == 0) st_release(p.flags + ticket, make_flag(epoch, kFlagInclusive));
 
     TIO* pga = static_cast<TIO*>(p.out) + base;
