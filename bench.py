@@ -313,8 +313,8 @@ def run_layer(args, wl, world, rank, local):
         model.zero_grad(set_to_none=True)
     fwd_ms = sorted(fwd_times[3:])[len(fwd_times[3:]) // 2]
     bwd_ms = sorted(bwd_times[3:])[len(bwd_times[3:]) // 2]
-    kern["mixer_fwd_kernel"] = dict(ms=fwd_ms, bytes=2 * W * s * B * T)
-    kern["mixer_bwd_kernel"] = dict(ms=bwd_ms, bytes=3 * W * s * B * T)
+    kern["mixer_forward"] = dict(ms=fwd_ms, bytes=2 * W * s * B * T)
+    kern["mixer_backward"] = dict(ms=bwd_ms, bytes=3 * W * s * B * T)
     dom = max(kern, key=lambda k: kern[k]["ms"])
     achieved = kern[dom]["bytes"] / (kern[dom]["ms"] / 1e3) / 1e9
     traffic = profile_traffic(dom, f"layer_b{B}_t{T}_w{W}_{'fp32' if s == 4 else 'bf16'}")

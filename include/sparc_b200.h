@@ -13,14 +13,15 @@
  * once when it is allocated, and may then be reused by any number of launches that are
  * ordered on one stream; calls that run concurrently need distinct workspaces.
  *
- * Chunk carries are passed between tiles by decoupled lookback; a tile composes whatever
+ * The mixer runs as chunk summaries -> a carry scan -> a replay. The carry scan passes the
+ * states between segments of chunks by decoupled lookback: a segment composes whatever
  * predecessor aggregates are ready, so the last bits of the carries (and of everything
- * downstream) can vary run to run. With `deterministic` set a tile waits for its immediate
+ * downstream) can vary run to run. With `deterministic` set a segment waits for its immediate
  * predecessor's carry instead, which makes results bitwise reproducible. Parameter gradients
- * are always reduced in a fixed order. Every wait is bounded by
- * `max_spin` polls (0 selects the default, about a second); a wait that runs out sets the
- * SPARC_STATUS_TIMEOUT bit in the workspace's status word, continues with a zero carry, and
- * the launch still completes. sparc_read_status reads that word.
+ * are always reduced in a fixed order. Every wait is bounded by `max_spin` polls (0 selects
+ * the default, about a second); a wait that runs out sets the SPARC_STATUS_TIMEOUT bit in the
+ * workspace's status word, continues with a zero carry, and the launch still completes.
+ * sparc_read_status reads that word.
  *
  * Which reference interface each entry point replaces (paths inside Botwwt/sparc):
  *   sparc_mixer_forward   SPARCMixer.forward -> run_sequence          sparc-kernal/sparc.py:90-91,
@@ -67,8 +68,9 @@ extern "C" {
  * h_t = a_t h_{t-1} + b_t over M = width/2 complex modes, with a_t, b_t computed from x_t
  * and the parameters. `carry` receives the state at the end of every chunk of
  * sparc_mixer_chunk_tokens(dtype) tokens ([batch, sparc_mixer_carry_chunks(length, dtype), M] complex,
- * interleaved real/imag float32); the backward needs it. h0 (initial state) and last (final
- * state) are optional pairs (NULL, NULL). */
+ * interleaved real/imag float32) and `controls` the per-token controls ([batch, length, 4]
+ * float32: e^eta, delta, tanh p0, tanh p1); the backward needs both, and y. h0 (initial
+ * state) and last (final state) are optional pairs (NULL, NULL). */
 typedef struct SparcMixerFwdArgs {
   const void* x;                       /* [batch, length, width]  activations (dtype) */
   void* y;                             /* [batch, length, width]  output (dtype) */
@@ -84,6 +86,7 @@ typedef struct SparcMixerFwdArgs {
   float* last_r;                       /* [batch, M] or NULL */
   float* last_i;                       /* [batch, M] or NULL */
   float* carry;                        /* [batch, chunks, M, 2] */
+  float* controls;                     /* [batch, length, 4] */
   void* workspace;
   size_t workspace_bytes;
   long long batch;
@@ -92,8 +95,8 @@ typedef struct SparcMixerFwdArgs {
   int dtype;                           /* SPARC_DTYPE_* */
   unsigned max_spin;                   /* 0 = default */
   int deterministic;                   /* 1 = chained carries: bitwise reproducible, slower */
-  int inject_enable;                   /* test hook: 1 = tile inject_tile never publishes */
-  long long inject_tile;
+  int inject_enable;                   /* test hook: 1 = carry-scan segment inject_tile */
+  long long inject_tile;               /*   never publishes (its successors time out) */
 } SparcMixerFwdArgs;
 
 /* Backward of sparc_mixer_forward for the loss gradient dy on y (and optionally grad_last on
@@ -102,6 +105,7 @@ typedef struct SparcMixerFwdArgs {
  * fixed order (deterministic run to run). */
 typedef struct SparcMixerBwdArgs {
   const void* x;                       /* [batch, length, width] forward input (dtype) */
+  const void* y;                       /* [batch, length, width] the forward's output (dtype) */
   const void* dy;                      /* [batch, length, width] (dtype) */
   void* dx;                            /* [batch, length, width] (dtype) */
   const float* nu_log;
@@ -118,6 +122,7 @@ typedef struct SparcMixerBwdArgs {
   float* grad_h0_r;                    /* [batch, M] or NULL */
   float* grad_h0_i;
   const float* carry;                  /* the forward's carry output */
+  const float* controls;               /* the forward's controls output */
   float* grad_nu_log;                  /* [M] */
   float* grad_theta_log;               /* [M] */
   float* grad_phase_direction;         /* [width + 1] */
@@ -211,12 +216,12 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* args, void* stream);
  * call cudaMalloc after start-up because it can block the whole device. Its scratch is a
  * fixed array of sparc_mixer_noalloc_scratch_bytes() (32 MiB) inside the library, which every
  * GPU that loads the library holds until the process exits; a problem that needs more
- * (roughly batch * ceil(length/C) * (width/2 rounded up to 256) * 16 bytes, with C = 16 tokens
- * for bfloat16 and 8 for float32) is rejected with SPARC_ERR_WORKSPACE
- * and a message. The first call on a device looks up that device's copy of the array
+ * (roughly batch * ceil(length/16) * (width/2 rounded up to 256) * 18 bytes) is rejected with
+ * SPARC_ERR_WORKSPACE and a message. The first call on a device looks up that device's copy of the array
  * (cudaGetSymbolAddress), so make it before any stream capture. All calls share the array:
  * calls whose executions overlap on the GPU (other streams, other host threads) race and must
- * be serialised by the caller. The caller still provides x, y, carry and the parameters. */
+ * be serialised by the caller. The caller still provides x, y, carry, controls and the
+ * parameters. */
 size_t sparc_mixer_noalloc_scratch_bytes(void);
 int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* args, void* stream);
 

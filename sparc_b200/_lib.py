@@ -31,6 +31,7 @@ class MixerFwdArgs(ctypes.Structure):
         ("nu_log", _vp), ("theta_log", _vp), ("phase_direction", _vp), ("radial_direction", _vp),
         ("write_log_gain", _vp), ("write_phase_response", _vp), ("write_radial_response", _vp),
         ("h0_r", _vp), ("h0_i", _vp), ("last_r", _vp), ("last_i", _vp), ("carry", _vp),
+        ("controls", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint), ("deterministic", ctypes.c_int),
@@ -40,11 +41,11 @@ class MixerFwdArgs(ctypes.Structure):
 
 class MixerBwdArgs(ctypes.Structure):
     _fields_ = [
-        ("x", _vp), ("dy", _vp), ("dx", _vp),
+        ("x", _vp), ("y", _vp), ("dy", _vp), ("dx", _vp),
         ("nu_log", _vp), ("theta_log", _vp), ("phase_direction", _vp), ("radial_direction", _vp),
         ("write_log_gain", _vp), ("write_phase_response", _vp), ("write_radial_response", _vp),
         ("h0_r", _vp), ("h0_i", _vp), ("grad_last_r", _vp), ("grad_last_i", _vp),
-        ("grad_h0_r", _vp), ("grad_h0_i", _vp), ("carry", _vp),
+        ("grad_h0_r", _vp), ("grad_h0_i", _vp), ("carry", _vp), ("controls", _vp),
         ("grad_nu_log", _vp), ("grad_theta_log", _vp), ("grad_phase_direction", _vp),
         ("grad_radial_direction", _vp), ("grad_write_log_gain", _vp), ("grad_energy_response", _vp),
         ("grad_write_phase_response", _vp), ("grad_write_radial_response", _vp),

@@ -42,6 +42,14 @@ template <> struct Io<__nv_bfloat16> {
   }
 };
 
+__device__ __forceinline__ float to_float(float v) { return v; }
+__device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T from_float(float v);
+template <> __device__ __forceinline__ float from_float<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -175,6 +183,12 @@ __device__ __forceinline__ void finish_launch(LaunchState* ls) {
     }
   }
 }
+
+// Programmatic dependent launch: kernels are launched so that they may start while the previous
+// kernel on the stream drains; this waits until that kernel has completed and its memory is
+// visible (a no-op when the launch had no programmatic dependency). Nothing the previous kernel
+// writes may be read before it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Complex helpers on float2 (x = real, y = imag).
 __device__ __forceinline__ float2 cmul(float2 a, float2 b) {

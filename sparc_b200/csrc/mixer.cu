@@ -1,19 +1,16 @@
 // SPARC mixer forward / backward for B200 (sm_100a).
 //
-// Work unit ("tile"): one batch row b and one chunk of C consecutive tokens, all M modes.
-// A tile is processed by one thread-block cluster of G CTAs; CTA g owns modes
-// [g*NT, g*NT + NT) with one thread per mode, so the cross-mode per-token reductions
-// (controller projection in the forward, the shared-control gradient in the backward) run
-// on-chip: warp transpose-reduce -> shared memory -> distributed shared memory across the
-// cluster.
-//
-// Kernels are persistent: clusters take tiles from a ticket counter in chunk-major order
-// (ticket = c*B + b forward, (chunks-1-c)*B + b backward), so a tile only ever waits on tiles
-// with smaller tickets, which are held by running clusters. Chunk carries are passed by
-// decoupled lookback: a tile publishes its aggregate affine map (A, B: out = A*in + B, per
-// mode) and, once it knows its carry-in, its inclusive state; successors compose aggregates
-// until they reach an inclusive state. The forward's inclusive states double as the saved
-// chunk carries that the backward replays from.
+// Work unit ("tile"): one batch row b and one chunk of C consecutive tokens, all M modes; CTA g
+// of a tile owns modes [g*256, g*256 + 256), two adjacent modes per thread. The forward is
+//   summary  (cluster of G CTAs per tile) token controls + each chunk's affine map
+//            h_out = P h_in + Q per mode,
+//   scan     the chunk carries: a decoupled-lookback scan over segments of chunks,
+//   replay   the recurrence inside every chunk from its carried-in state, y = relu(h);
+// the backward mirrors it (reverse summary from the relu mask of y, reverse scan of the
+// adjoint carries, gradient kernel) and ends with a fixed-order reduction of the per-cluster
+// parameter-gradient partials. The tile kernels are persistent with a static schedule and
+// never wait on each other; the only cross-CTA waits are the scan's bounded lookback polls.
+// The forward's chunk carries and per-token controls are outputs the backward reads back.
 //
 // Parity targets (reference paths inside Botwwt/sparc):
 //   controls  forward/control.py:129-139      write  forward/control.py:167-195
@@ -34,12 +31,9 @@ namespace cg = cooperative_groups;
 
 namespace sparc {
 
-#ifndef SPARC_BF16_CHUNK
-#define SPARC_BF16_CHUNK 16
-#endif
-// Tokens per tile (the chunk of the saved carries): 16 for bfloat16, 8 for float32 (whose
-// shared-memory tiles are twice as large).
-__host__ __device__ constexpr int chunk_for(int dtype) { return dtype == SPARC_DTYPE_BF16 ? SPARC_BF16_CHUNK : 8; }
+// Tokens per chunk (the granularity of the saved carries): 16 for bfloat16, 8 for float32
+// (whose shared-memory tiles are twice as large per token).
+__host__ __device__ constexpr int chunk_for(int dtype) { return dtype == SPARC_DTYPE_BF16 ? 16 : 8; }
 
 struct ModeConst {
   float nu;      // e^{nu_log}
@@ -146,48 +140,6 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[N], int lane) {
 
 template <int N>
 __host__ __device__ constexpr int log2i() { return N <= 1 ? 0 : 1 + log2i<N / 2>(); }
-
-// Reduce N per-thread values over the whole cluster. Every CTA ends with the cluster totals
-// in out[0..N) (shared memory). s_warp: [NW][N], s_cta: [N] (peers read it).
-template <int N, int NT>
-__device__ __forceinline__ void cluster_reduce(float (&v)[N], float (*s_warp)[N], float* s_cta,
-                                               float* out, cg::cluster_group& cluster) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int kShift = 5 - log2i<N>();
-  const float total = transpose_reduce<N>(v, lane);
-  if ((lane & ((1 << kShift) - 1)) == 0) s_warp[warp][lane >> kShift] = total;
-  __syncthreads();
-  if (threadIdx.x < N) {
-    float s = 0.0f;
-#pragma unroll
-    for (int w = 0; w < NT / 32; ++w) s += s_warp[w][threadIdx.x];
-    s_cta[threadIdx.x] = s;
-  }
-  cluster.sync();
-  if (threadIdx.x < N) {
-    float s = 0.0f;
-    const unsigned G = cluster.num_blocks();
-    for (unsigned r = 0; r < G; ++r) s += cluster.map_shared_rank(s_cta, r)[threadIdx.x];
-    out[threadIdx.x] = s;
-  }
-  __syncthreads();
-}
-
-// Token controls from the reduced projections: eta, delta, e^eta, tanh values.
-template <int C>
-__device__ __forceinline__ void token_controls(const float* proj, float b0, float b1, float* s_E,
-                                               float* s_delta, float* s_tau0, float* s_tau1) {
-  if (threadIdx.x < C) {
-    const int t = threadIdx.x;
-    const float tau0 = tanh_accurate(proj[t] + b0);
-    const float tau1 = tanh_accurate(proj[C + t] + b1);
-    s_tau0[t] = tau0;
-    s_tau1[t] = tau1;
-    s_delta[t] = kHalfPi * tau0;
-    s_E[t] = expf(kLn16 * tau1);
-  }
-  __syncthreads();
-}
 
 // Decoupled lookback with a warp-wide window. The tile publishes its aggregate (out = A*in + B)
 // unless its predecessor is already inclusive. Warp 0 then polls up to 32 predecessors at once
@@ -326,10 +278,118 @@ __device__ __forceinline__ void lookback(const LookbackCtx& lc, long long ticket
   }
 }
 
-// Cluster rank 0 takes the next ticket; peers read it from rank 0's shared memory after the
-// next cluster barrier. Double-buffered by tile parity.
-__device__ __forceinline__ void take_ticket(LaunchState* ls, unsigned* s_ticket, int parity, int g) {
-  if (g == 0 && threadIdx.x == 0) s_ticket[parity] = atomicAdd(&ls->ticket, 1u);
+// ------------------------------------------------------------------------------ carry scan
+// Per (row b, mode m): v_j = A_j v_{j-1} + B_j over the chunks j in processing order (forward:
+// chunk j; backward: chunk chunks-1-j), v_{-1} = init (h0, or the gradient of the returned last
+// state; else 0). out[chunk] receives every v; `final` (optional) the last one (the forward's
+// last state, the backward's gradient of h0). A CTA takes a segment of kScanSeg consecutive
+// chunks of one row and 256 modes, holds their maps in registers, composes the segment's map,
+// obtains the carry into the segment by decoupled lookback over the row's earlier segments,
+// publishes its own inclusive result and walks the segment writing every chunk's v. Segments
+// are taken in ticket order (segment-major), so a segment only waits on segments that running
+// CTAs hold.
+constexpr int kScanThreads = 256;
+constexpr int kScanSeg = 16;
+
+struct ScanParams {
+  const float4* agg;     // [B, chunks, Mp] per-chunk maps (A, B)
+  float2* out;           // [B, chunks, M]
+  const float* init_r;   // [B, M] or null
+  const float* init_i;
+  float* final_r;        // [B, M] or null
+  float* final_i;
+  LaunchState* ls;
+  unsigned* flags;       // [tiles]
+  float4* sagg;          // [tiles, 256] segment maps
+  float2* sincl;         // [tiles, 256] segment inclusive results
+  long long B;
+  int M, Mp, G, chunks, nseg;
+  long long tiles;       // nseg * B * G
+  int reverse;
+  unsigned max_spin;
+  int deterministic;
+  long long inject_unpublished;
+};
+
+__global__ void __launch_bounds__(kScanThreads, 2) mixer_carry_scan_kernel(const ScanParams p) {
+  __shared__ long long s_ticket;
+  __shared__ unsigned s_pred;
+  __shared__ unsigned s_win[2];
+  const int tid = threadIdx.x;
+  pdl_wait();  // the chunk maps (summary) are complete from here on
+  const long long rows = p.B * p.G;  // ticket distance to the previous segment of the same row
+  const LookbackCtx lc{p.ls, p.flags, p.sagg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, 1,
+                       kScanThreads, rows, p.deterministic != 0};
+  for (;;) {
+    if (tid == 0) {
+      const long long t = atomicAdd(&p.ls->ticket, 1u);
+      s_ticket = t;
+      s_pred = (t < p.tiles && t >= rows) ? ld_acquire(p.flags + (t - rows)) : 0u;
+    }
+    __syncthreads();
+    const long long ticket = s_ticket;
+    const unsigned pred = s_pred;
+    __syncthreads();  // s_ticket and s_pred are rewritten by the next iteration
+    if (ticket >= p.tiles) break;
+    const int seg = (int)(ticket / rows);
+    const long long rg = ticket - (long long)seg * rows;
+    const long long b = rg / p.G;
+    const int g = (int)(rg - b * p.G);
+    const int m = g * kScanThreads + tid;
+    const bool act = m < p.M;
+    const int j0 = seg * kScanSeg;
+
+    float4 a[kScanSeg];
+#pragma unroll
+    for (int u = 0; u < kScanSeg; ++u) {
+      const int j = j0 + u;
+      a[u] = make_float4(1.0f, 0.0f, 0.0f, 0.0f);
+      if (act && j < p.chunks) {
+        const int c = p.reverse ? p.chunks - 1 - j : j;
+        a[u] = __ldcg(p.agg + (b * p.chunks + c) * (long long)p.Mp + m);
+      }
+    }
+    float2 A = make_float2(1.0f, 0.0f), Bv = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int u = 0; u < kScanSeg; ++u) {
+      Bv = cfma(make_float2(a[u].x, a[u].y), Bv, make_float2(a[u].z, a[u].w));
+      A = cmul(make_float2(a[u].x, a[u].y), A);
+    }
+    const bool publish = ticket != p.inject_unpublished;
+    float2 cin = make_float2(0.0f, 0.0f);
+    if (seg == 0) {
+      if (p.init_r != nullptr && act) cin = make_float2(p.init_r[b * p.M + m], p.init_i[b * p.M + m]);
+    } else {
+      float2 Aa[1] = {A}, Ba[1] = {Bv}, cc[1];
+      const float2* sincl = p.sincl;
+      lookback<1>(lc, ticket, 0, seg, Aa, Ba, publish, pred, s_win, tid,
+                  [&](int jj, float2 (&h)[1]) {
+                    h[0] = __ldcg(sincl + (ticket - (long long)jj * rows) * kScanThreads + tid);
+                  },
+                  cc);
+      cin = cc[0];
+    }
+    if (publish) {
+      __stcg(p.sincl + ticket * kScanThreads + tid, cfma(A, cin, Bv));
+      publish_flag(p.flags + ticket, make_flag(lc.epoch, kFlagInclusive));
+    }
+    float2 v = cin;
+#pragma unroll
+    for (int u = 0; u < kScanSeg; ++u) {
+      const int j = j0 + u;
+      if (j < p.chunks) {
+        v = cfma(make_float2(a[u].x, a[u].y), v, make_float2(a[u].z, a[u].w));
+        const int c = p.reverse ? p.chunks - 1 - j : j;
+        if (act) p.out[(b * p.chunks + c) * (long long)p.M + m] = v;
+      }
+    }
+    if (p.final_r != nullptr && act && j0 + kScanSeg >= p.chunks) {
+      p.final_r[b * p.M + m] = v.x;
+      p.final_i[b * p.M + m] = v.y;
+    }
+    __syncthreads();
+  }
+  finish_launch(p.ls);
 }
 
 #include "mixer_fwd.cuh"
@@ -350,20 +410,45 @@ struct ReduceParams {
   float* g_radial_dir;  // [W+1]
 };
 
-// grid (ceil(Mp/32), kPartModes), block (32, 8): warp w sums clusters w, w+8, ... for 32 modes
-// (coalesced), then warp 0 adds the eight partial sums in a fixed order.
-constexpr int kReduceWarps = 8;
+// grid (ceil(Mp/32), kPartModes + 1), block (32, kReduceWarps). Rows q < kPartModes: warp w sums
+// clusters w, w + kReduceWarps, ... for 32 modes (coalesced, eight loads in flight), then warp 0
+// adds the warps' sums. Row kPartModes (block 0 only): warps 0 and 1 sum the two controller
+// biases over the clusters, lane-strided, then a shuffle tree. Every order is fixed.
+constexpr int kReduceWarps = 16;
+constexpr int kReduceUnroll = 8;
 
 __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const ReduceParams r) {
+  pdl_wait();  // the partials (gradient kernel) are complete from here on
   const int lane = threadIdx.x, w = threadIdx.y;
-  const int m = blockIdx.x * 32 + lane;
   const int q = blockIdx.y;
-  __shared__ double sm[kReduceWarps][32];
-  double s = 0.0;
-  if (m < r.Mp) {
-    for (int k = w; k < r.clusters; k += kReduceWarps) s += r.part[((long long)k * kPartModes + q) * r.Mp + m];
+  if (q == kPartModes) {
+    if (blockIdx.x != 0 || w >= 2) return;
+    const double* pb = r.part + (long long)r.clusters * kPartModes * r.Mp;
+    double t = 0.0;
+    for (int k = lane; k < r.clusters; k += 32) t += pb[2 * k + w];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) (w == 0 ? r.g_phase_dir : r.g_radial_dir)[r.W] = (float)t;
+    return;
   }
-  sm[w][lane] = s;
+  const int m = blockIdx.x * 32 + lane;
+  __shared__ double sm[kReduceWarps][32];
+  double s8[kReduceUnroll];
+#pragma unroll
+  for (int u = 0; u < kReduceUnroll; ++u) s8[u] = 0.0;
+  if (m < r.Mp) {
+    int k = w;
+    for (; k + (kReduceUnroll - 1) * kReduceWarps < r.clusters; k += kReduceUnroll * kReduceWarps) {
+#pragma unroll
+      for (int u = 0; u < kReduceUnroll; ++u)
+        s8[u] += r.part[((long long)(k + u * kReduceWarps) * kPartModes + q) * r.Mp + m];
+    }
+    for (; k < r.clusters; k += kReduceWarps) s8[0] += r.part[((long long)k * kPartModes + q) * r.Mp + m];
+  }
+  double sw = 0.0;
+#pragma unroll
+  for (int u = 0; u < kReduceUnroll; ++u) sw += s8[u];
+  sm[w][lane] = sw;
   __syncthreads();
   if (w == 0 && m < r.M) {
     double t = 0.0;
@@ -381,35 +466,35 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
       default: r.g_radial_dir[r.M + m] = (float)t; break;
     }
   }
-  if (blockIdx.x == 0 && q == 0 && w == 1 && lane < 2) {
-    const double* pb = r.part + (long long)r.clusters * kPartModes * r.Mp;
-    double t = 0.0;
-    for (int k = 0; k < r.clusters; ++k) t += pb[2 * k + lane];
-    (lane == 0 ? r.g_phase_dir : r.g_radial_dir)[r.W] = (float)t;
-  }
 }
 
 // ------------------------------------------------------------------------------ host side
 struct Plan {
   int dtype, C, chunks;
-  long long tiles;
-  int Gf, Mpf, clusters_fwd;  // forward: CTAs of 256 modes
-  size_t fwd_smem;
-  bool fvec, tma;
-  int Gb, Mpb, clusters_bwd;  // backward: CTAs of 256 modes
-  size_t bwd_smem;
+  long long tiles;         // B * chunks
+  int G, Mp;               // CTAs of 256 modes per tile; modes padded to G * 256
+  bool vec, tma;
+  int sum_clusters, rep_rows, rsum_rows, grad_clusters, scan_ctas;
+  size_t sum_smem, rep_smem, rsum_smem, grad_smem;
+  int nseg;                // carry-scan segments per row
+  long long scan_tiles;    // nseg * B * G
 };
 
 static thread_local char g_err[512];
 static void set_err(const char* msg) { snprintf(g_err, sizeof(g_err), "%s", msg); }
 
-template <typename K>
-static int max_clusters(K kernel, int G, int NT, size_t dyn_smem) {
-  if (G > 8) cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem) != cudaSuccess) {
+static bool set_smem(const void* kernel, size_t dyn) {
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
     cudaGetLastError();
-    return 0;
+    return false;
   }
+  return true;
+}
+
+// Resident clusters of G CTAs (whole GPU) for a cluster kernel.
+static int max_clusters(const void* kernel, int G, int NT, size_t dyn_smem) {
+  if (G > 8) cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (!set_smem(kernel, dyn_smem)) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G, 1, 1);
   cfg.blockDim = dim3(NT, 1, 1);
@@ -429,20 +514,49 @@ static int max_clusters(K kernel, int G, int NT, size_t dyn_smem) {
   return n;
 }
 
-// Kernel instances: forward <TIO, C, fast math, vector pairs>, backward <TIO, NT, fast math, C>.
+// Resident CTAs (whole GPU) for a plain kernel.
+static int max_blocks(const void* kernel, int NT, size_t dyn_smem) {
+  if (dyn_smem > 0 && !set_smem(kernel, dyn_smem)) return 0;
+  int per_sm = 0, dev = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, NT, dyn_smem) != cudaSuccess ||
+      cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return per_sm * sms;
+}
+
+// Kernel instances per activation type (bfloat16 uses the hardware tanh; float32 the accurate one).
 template <typename TIO>
 struct Kernels {
   static constexpr bool kFast = std::is_same<TIO, __nv_bfloat16>::value;
-  static constexpr int C = kFast ? SPARC_BF16_CHUNK : 8;
-  static void* fwd(bool vec) {
-    return vec ? (void*)mixer_fwd_kernel<TIO, C, kFast, true> : (void*)mixer_fwd_kernel<TIO, C, kFast, false>;
+  static constexpr int C = chunk_for(kFast ? SPARC_DTYPE_BF16 : SPARC_DTYPE_F32);
+  static const void* sum() { return (const void*)mixer_fwd_summary_kernel<TIO, C, kFast>; }
+  static const void* rep(bool vec) {
+    return vec ? (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, true>
+               : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false>;
   }
-  static void* bwd(bool vec) {
-    return vec ? (void*)mixer_bwd_kernel<TIO, C, kFast, true> : (void*)mixer_bwd_kernel<TIO, C, kFast, false>;
-  }
-  static size_t fwd_smem() { return sizeof(FwdSmem<TIO, C, kFast>); }
-  static size_t bwd_smem() { return sizeof(BwdSmem<TIO, C>); }
+  static const void* rsum() { return (const void*)mixer_bwd_summary_kernel<TIO, C>; }
+  static const void* grad() { return (const void*)mixer_bwd_grad_kernel<TIO, C, kFast>; }
+  static size_t sum_smem() { return sizeof(SumSmem<TIO, C>); }
+  static size_t rep_smem() { return sizeof(RepSmem<TIO, C>); }
+  static size_t rsum_smem() { return sizeof(RsumSmem<TIO, C>); }
+  static size_t grad_smem() { return sizeof(GradSmem<TIO, C>); }
 };
+
+template <typename TIO>
+static void plan_kernels(Plan* pl, const void** k) {
+  using K = Kernels<TIO>;
+  pl->sum_smem = K::sum_smem();
+  pl->rep_smem = K::rep_smem();
+  pl->rsum_smem = K::rsum_smem();
+  pl->grad_smem = K::grad_smem();
+  k[0] = K::sum();
+  k[1] = K::rep(pl->vec);
+  k[2] = K::rsum();
+  k[3] = K::grad();
+}
 
 static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   if (B <= 0 || T <= 0 || W <= 0) { set_err("batch, length and width must be positive"); return SPARC_ERR_SHAPE; }
@@ -455,130 +569,197 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   pl->chunks = (int)((T + pl->C - 1) / pl->C);
   pl->tiles = B * pl->chunks;
   if (pl->tiles >= (1LL << 31)) { set_err("too many tiles"); return SPARC_ERR_SHAPE; }
-  pl->Gf = (M + kFwdModes - 1) / kFwdModes;
-  pl->Mpf = pl->Gf * kFwdModes;
-  pl->fvec = (M % 2) == 0;
+  pl->G = (M + kFwdModes - 1) / kFwdModes;
+  pl->Mp = pl->G * kFwdModes;
+  pl->vec = (M % 2) == 0;
   const size_t s = dtype == SPARC_DTYPE_BF16 ? 2 : 4;
   pl->tma = ((size_t)W * s) % 16 == 0 && ((size_t)M * s) % 16 == 0;
-  pl->Gb = (M + kBwdModes - 1) / kBwdModes;
-  pl->Mpb = pl->Gb * kBwdModes;
+  pl->nseg = (pl->chunks + kScanSeg - 1) / kScanSeg;
+  pl->scan_tiles = (long long)pl->nseg * B * pl->G;
+
+  const void* k[4];
+  if (dtype == SPARC_DTYPE_BF16) plan_kernels<__nv_bfloat16>(pl, k);
+  else plan_kernels<float>(pl, k);
 
   int dev = 0;
   cudaGetDevice(&dev);
-  struct Key { int dev, dtype, Gf, Gb, vec; int nf, nb; };
+  struct Key { int dev, dtype, G, vec; int sum, rep, rsum, grad, scan; };
   static std::mutex mu;
   static Key cache[64];
   static int ncache = 0;
   std::lock_guard<std::mutex> lock(mu);
-  int nf = -1, nb = -1;
+  const Key* hit = nullptr;
   for (int i = 0; i < ncache; ++i) {
-    const Key& k = cache[i];
-    if (k.dev == dev && k.dtype == dtype && k.Gf == pl->Gf && k.Gb == pl->Gb && k.vec == (int)pl->fvec) {
-      nf = k.nf;
-      nb = k.nb;
-    }
+    const Key& kk = cache[i];
+    if (kk.dev == dev && kk.dtype == dtype && kk.G == pl->G && kk.vec == (int)pl->vec) hit = &kk;
   }
-  if (dtype == SPARC_DTYPE_BF16) {
-    pl->fwd_smem = Kernels<__nv_bfloat16>::fwd_smem();
-    pl->bwd_smem = Kernels<__nv_bfloat16>::bwd_smem();
+  Key key;
+  if (hit != nullptr) {
+    key = *hit;
   } else {
-    pl->fwd_smem = Kernels<float>::fwd_smem();
-    pl->bwd_smem = Kernels<float>::bwd_smem();
+    key = Key{dev, dtype, pl->G, (int)pl->vec, 0, 0, 0, 0, 0};
+    key.sum = max_clusters(k[0], pl->G, kFwdThreads, pl->sum_smem);
+    key.rep = max_blocks(k[1], kFwdThreads, pl->rep_smem);
+    key.rsum = max_blocks(k[2], kBwdThreads, pl->rsum_smem);
+    key.grad = max_clusters(k[3], pl->G, kBwdThreads, pl->grad_smem);
+    key.scan = max_blocks((const void*)mixer_carry_scan_kernel, kScanThreads, 0);
+    if (key.sum <= 0 || key.rep <= 0 || key.rsum <= 0 || key.grad <= 0 || key.scan <= 0) {
+      set_err("occupancy query failed");
+      return SPARC_ERR_LAUNCH;
+    }
+    if (ncache < 64) cache[ncache++] = key;
   }
-  if (nf < 0) {
-    void* fk = dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::fwd(pl->fvec) : Kernels<float>::fwd(pl->fvec);
-    void* bk = dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::bwd(pl->fvec) : Kernels<float>::bwd(pl->fvec);
-    nf = max_clusters(fk, pl->Gf, kFwdThreads, pl->fwd_smem);
-    nb = max_clusters(bk, pl->Gb, kBwdThreads, pl->bwd_smem);
-    if (nf <= 0 || nb <= 0) { set_err("cluster occupancy query failed"); return SPARC_ERR_LAUNCH; }
-    if (ncache < 64) cache[ncache++] = Key{dev, dtype, pl->Gf, pl->Gb, (int)pl->fvec, nf, nb};
-  }
-  pl->clusters_fwd = (int)std::min<long long>(nf, pl->tiles);
-  pl->clusters_bwd = (int)std::min<long long>(nb, pl->tiles);
+  auto clamp = [](long long n, long long hi) { return (int)std::max<long long>(1, std::min<long long>(n, hi)); };
+  pl->sum_clusters = clamp(key.sum, pl->tiles);
+  pl->rep_rows = clamp(key.rep / pl->G, pl->tiles);
+  pl->rsum_rows = clamp(key.rsum / pl->G, pl->tiles);
+  pl->grad_clusters = clamp(key.grad, pl->tiles);
+  pl->scan_ctas = clamp(key.scan, pl->scan_tiles);
   return SPARC_OK;
 }
 
 struct WsLayout {
-  size_t flags, agg, incl, part, total;
+  size_t flags, sagg, sincl, agg, kout, part, total;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-static WsLayout ws_layout(const Plan& pl) {
+static WsLayout ws_layout(const Plan& pl, long long B, int M) {
   WsLayout L;
-  const int G = std::max(pl.Gf, pl.Gb);
-  const int Mp = std::max(pl.Mpf, pl.Mpb);
   size_t off = align256(sizeof(LaunchState));
   L.flags = off;
-  off = align256(off + (size_t)pl.tiles * G * sizeof(unsigned));
+  off = align256(off + (size_t)pl.scan_tiles * sizeof(unsigned));
+  L.sagg = off;
+  off = align256(off + (size_t)pl.scan_tiles * kScanThreads * sizeof(float4));
+  L.sincl = off;
+  off = align256(off + (size_t)pl.scan_tiles * kScanThreads * sizeof(float2));
   L.agg = off;
-  off = align256(off + (size_t)pl.tiles * Mp * sizeof(float4));
-  L.incl = off;
-  off = align256(off + (size_t)pl.tiles * pl.Mpb * sizeof(float2));
+  off = align256(off + (size_t)pl.tiles * pl.Mp * sizeof(float4));
+  L.kout = off;
+  off = align256(off + (size_t)B * pl.chunks * M * sizeof(float2));
   L.part = off;
-  off = align256(off + ((size_t)pl.clusters_bwd * kPartModes * pl.Mpb + 2 * (size_t)pl.clusters_bwd) * sizeof(double));
+  off = align256(off + ((size_t)pl.grad_clusters * kPartModes * pl.Mp + 2 * (size_t)pl.grad_clusters) * sizeof(double));
   L.total = off;
   return L;
 }
 
+// Every mixer launch carries a programmatic-stream-serialisation attribute: it may be scheduled
+// while the previous kernel on the stream drains, and waits (pdl_wait) before reading that
+// kernel's outputs.
 template <typename P>
-static cudaError_t launch_cluster(void* kernel, int G, int NT, int clusters, size_t dyn, cudaStream_t s,
-                                  const P& params) {
+static cudaError_t launch_ex(const void* kernel, dim3 grid, dim3 block, int cluster_x, size_t dyn, cudaStream_t s,
+                             const P& params) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(G, clusters, 1);
-  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
   cfg.dynamicSmemBytes = dyn;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = G;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  ++na;
+  if (cluster_x > 0) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster_x;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = na;
   void* args[] = {const_cast<P*>(&params)};
   return cudaLaunchKernelExC(&cfg, kernel, args);
 }
 
-// Validate the forward arguments and fill the kernel parameters (scratch at `ws`).
-static int forward_params(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayout& L, char* ws, FwdParams* p) {
-  if (!a->x || !a->y || !a->carry || !a->nu_log || !a->theta_log || !a->phase_direction ||
+template <typename P>
+static cudaError_t launch_cluster(const void* kernel, int G, int NT, int clusters, size_t dyn, cudaStream_t s,
+                                  const P& params) {
+  return launch_ex(kernel, dim3(G, clusters, 1), dim3(NT, 1, 1), G, dyn, s, params);
+}
+
+template <typename P>
+static cudaError_t launch_plain(const void* kernel, dim3 grid, int NT, size_t dyn, cudaStream_t s, const P& params) {
+  return launch_ex(kernel, grid, dim3(NT, 1, 1), 0, dyn, s, params);
+}
+
+static bool aligned16(const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+static ScanParams scan_params(const Plan& pl, const WsLayout& L, char* ws, long long B, int M, int reverse,
+                              const float* init_r, const float* init_i, float* final_r, float* final_i,
+                              float2* out, unsigned max_spin, int deterministic, int inject_enable,
+                              long long inject_tile) {
+  ScanParams sp;
+  sp.agg = reinterpret_cast<const float4*>(ws + L.agg);
+  sp.out = out;
+  sp.init_r = init_r;
+  sp.init_i = init_i;
+  sp.final_r = final_r;
+  sp.final_i = final_i;
+  sp.ls = reinterpret_cast<LaunchState*>(ws);
+  sp.flags = reinterpret_cast<unsigned*>(ws + L.flags);
+  sp.sagg = reinterpret_cast<float4*>(ws + L.sagg);
+  sp.sincl = reinterpret_cast<float2*>(ws + L.sincl);
+  sp.B = B;
+  sp.M = M;
+  sp.Mp = pl.Mp;
+  sp.G = pl.G;
+  sp.chunks = pl.chunks;
+  sp.nseg = pl.nseg;
+  sp.tiles = pl.scan_tiles;
+  sp.reverse = reverse;
+  sp.max_spin = max_spin ? max_spin : (1u << 20);
+  sp.deterministic = deterministic;
+  sp.inject_unpublished = inject_enable ? inject_tile : -1;
+  return sp;
+}
+
+static int launch_error(cudaError_t e) {
+  if (e == cudaSuccess) return SPARC_OK;
+  set_err(cudaGetErrorString(e));
+  return SPARC_ERR_LAUNCH;
+}
+
+// Validate the forward arguments and enqueue summary -> scan -> replay (scratch at `ws`).
+static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayout& L, char* ws, cudaStream_t s) {
+  if (!a->x || !a->y || !a->carry || !a->controls || !a->nu_log || !a->theta_log || !a->phase_direction ||
       !a->radial_direction || !a->write_log_gain || !a->write_phase_response || !a->write_radial_response) {
     set_err("null tensor pointer"); return SPARC_ERR_ARG;
   }
   if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->last_r == nullptr) != (a->last_i == nullptr)) {
     set_err("h0 / last pointers must be given in pairs"); return SPARC_ERR_ARG;
   }
-  p->x = a->x;
-  p->y = a->y;
-  p->pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
-                         a->write_log_gain, a->write_phase_response, a->write_radial_response};
-  p->h0_r = a->h0_r;
-  p->h0_i = a->h0_i;
-  p->last_r = a->last_r;
-  p->last_i = a->last_i;
-  p->carry = reinterpret_cast<float2*>(a->carry);
-  p->ls = reinterpret_cast<LaunchState*>(ws);
-  p->flags = reinterpret_cast<unsigned*>(ws + L.flags);
-  p->agg = reinterpret_cast<float4*>(ws + L.agg);
-  p->B = a->batch;
-  p->T = a->length;
-  p->W = a->width;
-  p->M = a->width / 2;
-  p->chunks = pl.chunks;
-  p->tiles = pl.tiles;
-  p->max_spin = a->max_spin ? a->max_spin : (1u << 20);
-  p->inject_unpublished = a->inject_enable ? a->inject_tile : -1;
-  p->deterministic = a->deterministic;
-  p->use_tma = pl.tma && (reinterpret_cast<uintptr_t>(a->x) % 16 == 0) ? 1 : 0;
-  return SPARC_OK;
-}
-
-static int launch_forward(const Plan& pl, const FwdParams& p, cudaStream_t s) {
-  void* k = pl.dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::fwd(pl.fvec) : Kernels<float>::fwd(pl.fvec);
-  const cudaError_t e = launch_cluster(k, pl.Gf, kFwdThreads, pl.clusters_fwd, pl.fwd_smem, s, p);
-  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
-  return SPARC_OK;
+  FwdParams p;
+  p.x = a->x;
+  p.y = a->y;
+  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
+                        a->write_log_gain, a->write_phase_response, a->write_radial_response};
+  p.h0_r = a->h0_r;
+  p.h0_i = a->h0_i;
+  p.ctl = reinterpret_cast<float4*>(a->controls);
+  p.carry = reinterpret_cast<const float2*>(a->carry);
+  p.agg = reinterpret_cast<float4*>(ws + L.agg);
+  p.ls = reinterpret_cast<LaunchState*>(ws);
+  p.B = a->batch;
+  p.T = a->length;
+  p.W = a->width;
+  p.M = a->width / 2;
+  p.Mp = pl.Mp;
+  p.chunks = pl.chunks;
+  p.tiles = pl.tiles;
+  p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
+  p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->controls) && aligned16(a->carry) ? 1 : 0;
+  const bool bf = a->dtype == SPARC_DTYPE_BF16;
+  const void* ksum = bf ? Kernels<__nv_bfloat16>::sum() : Kernels<float>::sum();
+  const void* krep = bf ? Kernels<__nv_bfloat16>::rep(pl.vec) : Kernels<float>::rep(pl.vec);
+  int rc = launch_error(launch_cluster(ksum, pl.G, kFwdThreads, pl.sum_clusters, pl.sum_smem, s, p));
+  if (rc != SPARC_OK) return rc;
+  const ScanParams sp = scan_params(pl, L, ws, p.B, p.M, 0, a->h0_r, a->h0_i, a->last_r, a->last_i,
+                                    reinterpret_cast<float2*>(a->carry), a->max_spin, a->deterministic,
+                                    a->inject_enable, a->inject_tile);
+  rc = launch_error(launch_plain((const void*)mixer_carry_scan_kernel, dim3(pl.scan_ctas), kScanThreads, 0, s, sp));
+  if (rc != SPARC_OK) return rc;
+  return launch_error(launch_plain(krep, dim3(pl.G, pl.rep_rows), kFwdThreads, pl.rep_smem, s, p));
 }
 
 }  // namespace sparc
@@ -599,20 +780,17 @@ long long sparc_mixer_carry_chunks(long long length, int dtype) {
 size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype) {
   Plan pl;
   if (make_plan(batch, length, width, dtype, &pl) != SPARC_OK) return 0;
-  return ws_layout(pl).total;
+  return ws_layout(pl, batch, width / 2).total;
 }
 
 int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   Plan pl;
-  int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
+  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
   if (rc != SPARC_OK) return rc;
-  const WsLayout L = ws_layout(pl);
+  const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
-  FwdParams p;
-  rc = forward_params(a, pl, L, static_cast<char*>(a->workspace), &p);
-  if (rc != SPARC_OK) return rc;
-  return launch_forward(pl, p, static_cast<cudaStream_t>(stream));
+  return run_forward(a, pl, L, static_cast<char*>(a->workspace), static_cast<cudaStream_t>(stream));
 }
 
 int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
@@ -620,9 +798,9 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   Plan pl;
   int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
   if (rc != SPARC_OK) return rc;
-  const WsLayout L = ws_layout(pl);
+  const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
-  if (!a->x || !a->dy || !a->dx || !a->carry || !a->grad_nu_log || !a->grad_theta_log ||
+  if (!a->x || !a->y || !a->dy || !a->dx || !a->carry || !a->controls || !a->grad_nu_log || !a->grad_theta_log ||
       !a->grad_phase_direction || !a->grad_radial_direction || !a->grad_write_log_gain ||
       !a->grad_energy_response || !a->grad_write_phase_response || !a->grad_write_radial_response) {
     set_err("null tensor pointer"); return SPARC_ERR_ARG;
@@ -634,6 +812,7 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   char* ws = static_cast<char*>(a->workspace);
   BwdParams p;
   p.x = a->x;
+  p.y = a->y;
   p.dy = a->dy;
   p.dx = a->dx;
   p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
@@ -642,32 +821,39 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.h0_i = a->h0_i;
   p.glast_r = a->grad_last_r;
   p.glast_i = a->grad_last_i;
-  p.gh0_r = a->grad_h0_r;
-  p.gh0_i = a->grad_h0_i;
+  p.ctl = reinterpret_cast<const float4*>(a->controls);
   p.carry = reinterpret_cast<const float2*>(a->carry);
-  p.ls = reinterpret_cast<LaunchState*>(ws);
-  p.flags = reinterpret_cast<unsigned*>(ws + L.flags);
+  p.kout = reinterpret_cast<const float2*>(ws + L.kout);
   p.agg = reinterpret_cast<float4*>(ws + L.agg);
-  p.incl = reinterpret_cast<float2*>(ws + L.incl);
   p.part = reinterpret_cast<double*>(ws + L.part);
+  p.ls = reinterpret_cast<LaunchState*>(ws);
   p.B = a->batch;
   p.T = a->length;
   p.W = a->width;
   p.M = a->width / 2;
+  p.Mp = pl.Mp;
   p.chunks = pl.chunks;
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
-  p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
-  p.deterministic = a->deterministic;
-  p.use_tma = pl.tma && (reinterpret_cast<uintptr_t>(a->x) % 16 == 0) && (reinterpret_cast<uintptr_t>(a->dy) % 16 == 0) ? 1 : 0;
+  p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->y) && aligned16(a->dy) && aligned16(a->controls) &&
+                      aligned16(a->carry) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  void* k = a->dtype == SPARC_DTYPE_BF16 ? Kernels<__nv_bfloat16>::bwd(pl.fvec) : Kernels<float>::bwd(pl.fvec);
-  cudaError_t e = launch_cluster(k, pl.Gb, kBwdThreads, pl.clusters_bwd, pl.bwd_smem, s, p);
-  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
+  const bool bf = a->dtype == SPARC_DTYPE_BF16;
+  const void* krsum = bf ? Kernels<__nv_bfloat16>::rsum() : Kernels<float>::rsum();
+  const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad() : Kernels<float>::grad();
+  rc = launch_error(launch_plain(krsum, dim3(pl.G, pl.rsum_rows), kBwdThreads, pl.rsum_smem, s, p));
+  if (rc != SPARC_OK) return rc;
+  const ScanParams sp = scan_params(pl, L, ws, p.B, p.M, 1, a->grad_last_r, a->grad_last_i, a->grad_h0_r,
+                                    a->grad_h0_i, reinterpret_cast<float2*>(ws + L.kout), a->max_spin,
+                                    a->deterministic, a->inject_enable, a->inject_tile);
+  rc = launch_error(launch_plain((const void*)mixer_carry_scan_kernel, dim3(pl.scan_ctas), kScanThreads, 0, s, sp));
+  if (rc != SPARC_OK) return rc;
+  rc = launch_error(launch_cluster(kgrad, pl.G, kBwdThreads, pl.grad_clusters, pl.grad_smem, s, p));
+  if (rc != SPARC_OK) return rc;
   ReduceParams r;
   r.part = p.part;
-  r.clusters = pl.clusters_bwd;
-  r.Mp = pl.Mpb;
+  r.clusters = pl.grad_clusters;
+  r.Mp = pl.Mp;
   r.M = p.M;
   r.W = p.W;
   r.theta_log = a->theta_log;
@@ -679,16 +865,14 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   r.g_energy = a->grad_energy_response;
   r.g_phase_dir = a->grad_phase_direction;
   r.g_radial_dir = a->grad_radial_direction;
-  mixer_reduce_kernel<<<dim3((pl.Mpb + 31) / 32, kPartModes), dim3(32, kReduceWarps), 0, s>>>(r);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
-  return SPARC_OK;
+  return launch_error(launch_ex((const void*)mixer_reduce_kernel, dim3((pl.Mp + 31) / 32, kPartModes + 1),
+                               dim3(32, kReduceWarps), 0, 0, s, r));
 }
 
 // ------------------------------------------------------------------------------ no-alloc variant
-// sparc_mixer_forward_noalloc: the same forward kernel, with its scratch (launch counters,
-// lookback flags and chunk aggregates) in a fixed array that lives in the library itself, for
-// callers that cannot allocate device memory. See the declaration in sparc_b200.h.
+// sparc_mixer_forward_noalloc: the same forward launches, with their scratch (launch counters,
+// scan flags, segment and chunk aggregates) in a fixed array that lives in the library itself,
+// for callers that cannot allocate device memory. See the declaration in sparc_b200.h.
 }  // extern "C"
 
 namespace sparc {
@@ -726,11 +910,12 @@ size_t sparc_mixer_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   Plan pl;
-  int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
+  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
   if (rc != SPARC_OK) return rc;
-  const WsLayout L = ws_layout(pl);
-  // the forward uses the launch state, the flags and the aggregates (everything before incl)
-  const size_t need = L.incl;
+  const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
+  // the forward uses the launch state, the scan's flags and segment arrays, and the chunk
+  // aggregates (everything before the backward's adjoint carries)
+  const size_t need = L.kout;
   if (need > kNoAllocScratchBytes) {
     char msg[256];
     snprintf(msg, sizeof(msg),
@@ -744,15 +929,12 @@ int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
   if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); set_err("no current CUDA device"); return SPARC_ERR_LAUNCH; }
   char* ws = static_cast<char*>(noalloc_scratch(dev));
   if (ws == nullptr) { set_err("cudaGetSymbolAddress failed for the built-in scratch"); return SPARC_ERR_LAUNCH; }
-  FwdParams p;
-  rc = forward_params(a, pl, L, ws, &p);
-  if (rc != SPARC_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the array keeps the previous call's contents: its flag words, laid out for another shape,
   // could alias this launch's, so they start from zero on every call (a memset, no allocation)
-  const cudaError_t e = cudaMemsetAsync(ws + L.flags, 0, L.agg - L.flags, s);
+  const cudaError_t e = cudaMemsetAsync(ws + L.flags, 0, L.sagg - L.flags, s);
   if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
-  return launch_forward(pl, p, s);
+  return run_forward(a, pl, L, ws, s);
 }
 
 int sparc_read_status(const void* workspace, unsigned* status, void* stream) {

@@ -1,49 +1,63 @@
-// SPARC mixer backward kernel (included by mixer.cu, inside namespace sparc).
+// SPARC mixer backward kernels (included by mixer.cu, inside namespace sparc). Three launches
+// plus the fixed-order parameter-gradient reduction:
 //
-// Same tiling as the forward (a cluster of G CTAs per tile of C tokens x all M modes, two
-// adjacent modes per thread), walked in reverse chunk order. The x and dy tiles arrive in
-// shared memory by TMA bulk copies. Per tile:
-//   controls    the projections are recomputed from x (cluster reduction, as in the forward);
-//   pass 0      replay the states from the forward's chunk carry, keep them in shared memory and
-//               zero dy where the relu was inactive;
-//   carry       if the carry of the adjoint from the later chunk is already published, use it;
-//               otherwise run the local reverse pass from zero (pass A), publish the aggregate
-//               (conj(P), Qr) and resolve the carry by decoupled lookback;
-//   pass B      the true adjoint backwards through the chunk with every gradient: transition
-//               (dEta, dDelta per token, dNu, dTheta per mode), write path (dx of the content,
-//               dEta, dDelta, dNu, write-gain / response gradients); the write-path dx waits in
-//               the state slots the reverse walk has consumed;
-//   tokens      dEta, dDelta are summed over all modes (cluster reduction), turned into the
-//               controller gradients dp0, dp1, which finish dx and the direction gradients.
-// Per-mode parameter gradients accumulate in float64 per cluster; mixer_reduce_kernel sums the
-// clusters in a fixed order.
+//   mixer_bwd_summary_kernel  per tile: the relu-masked output gradient g_t = dy_t * [y_t > 0]
+//                             (y is the forward output, so no state replay is needed here), and
+//                             the chunk's reverse aggregate: with lambda_t = g_t + conj(a_{t+1})
+//                             lambda_{t+1} the adjoint, the carry leaving the chunk towards
+//                             earlier tokens is conj(a_t0) lambda_t0 = conj(P) k_in + q, with
+//                             P = prod a_t and q the same walk from k_in = 0.
+//   mixer_carry_scan_kernel   (mixer.cu) the same scan as the forward's, from the last chunk
+//                             backwards: the adjoint carry leaving every chunk.
+//   mixer_bwd_grad_kernel     per tile (cluster of G CTAs): pass 0 replays the states from the
+//                             forward's chunk carry into shared memory and masks dy; pass B
+//                             walks the true adjoint backwards with every gradient: transition
+//                             (dEta, dDelta per token, dNu, dTheta per mode), write path (dx of
+//                             the content, dEta, dDelta, dNu, write-gain / response gradients);
+//                             the write-path dx waits in the state slots the reverse walk has
+//                             consumed. dEta, dDelta are summed over all modes (warp
+//                             transpose-reduce per group of tokens during the walk, then shared
+//                             and distributed shared memory) into the controller gradients dp0,
+//                             dp1, which finish dx and the direction gradients.
+// One mode per thread, 256 threads per CTA (the tiles' shared memory then serves twice the warps
+// of a two-modes-per-thread layout). Per-mode parameter gradients accumulate in float64 per
+// cluster; mixer_reduce_kernel sums the clusters in a fixed order. The token controls come from
+// the forward (saved per token).
 
 // (included inside namespace sparc)
 
-constexpr int kBwdThreads = 128;
-constexpr int kBwdModes = 2 * kBwdThreads;
+constexpr int kBwdThreads = 256;
+constexpr int kBwdModes = kBwdThreads;  // one mode per thread
+constexpr int kBwdWarps = kBwdThreads / 32;
 constexpr int kPartModes = 9;  // nu, theta (sum of phase grads), wlg, wpr, wrr, D0r, D0i, D1r, D1i
+constexpr int kGroup = 4;      // tokens per unrolled group of the reverse walk
 
 template <typename TIO, int C>
-struct BwdSmem {
+struct RsumSmem {
+  TIO dy[2][C][2][kBwdModes];
+  TIO y[2][C][2][kBwdModes];
+  float4 ctl[2][C];
+  unsigned long long bar[2];
+};
+
+template <typename TIO, int C>
+struct GradSmem {
   TIO x[C][2][kBwdModes];
   TIO dy[C][2][kBwdModes];     // masked by the relu in pass 0
   float2 h[C][kBwdModes];      // replayed states, then the write-path dx (pass B)
+  float2 hin[kBwdModes];       // state entering the chunk
+  float2 kin[kBwdModes];       // adjoint carry entering the chunk from the later chunks
   float4 ctl[C];               // E, delta, tau0, tau1
   float2 dp[C];                // controller gradients dp0, dp1
-  float tot[2 * C];            // cluster totals of the current reduction
-  float part_ctl[2][2 * C];    // projection partials (peers read), by tile parity
-  float part_grad[2][2 * C];   // dEta / dDelta partials (peers read), by tile parity
-  float warp_part[kBwdThreads / 32][2 * C];
-  float vt[2 * C][kBwdThreads];   // per-thread dEta / dDelta partials of pass B, by token
+  float tot[2 * C];            // cluster totals of dEta / dDelta
+  float part_grad[2][2 * C];   // dEta / dDelta CTA partials (peers read), by tile parity
+  float warp_part[kBwdWarps][2 * C];
   unsigned long long bar;
-  long long ring[2];
-  unsigned win[2];
-  unsigned pred;
 };
 
 struct BwdParams {
   const void* x;
+  const void* y;
   const void* dy;
   void* dx;
   MixerParamPtrs pp;
@@ -51,105 +65,166 @@ struct BwdParams {
   const float* h0_i;
   const float* glast_r;
   const float* glast_i;
-  float* gh0_r;
-  float* gh0_i;
-  const float2* carry;  // forward inclusive states [B, chunks, M]
+  const float4* ctl;     // [B, T] forward token controls
+  const float2* carry;   // [B, chunks, M] forward inclusive states
+  const float2* kout;    // [B, chunks, M] adjoint carry leaving each chunk (scan output)
+  float4* agg;           // [B, chunks, Mp] reverse aggregates (summary output)
+  double* part;          // [clusters][kPartModes][Mp] then [clusters][2] bias partials
   LaunchState* ls;
-  unsigned* flags;
-  float4* agg;
-  float2* incl;         // reverse inclusive carries [tiles, Mp]
-  double* part;         // [clusters][kPartModes][Mp] then [clusters][2] bias partials
   long long B, T;
-  int W, M, chunks;
+  int W, M, Mp, chunks;
   long long tiles;
   unsigned max_spin;
-  int deterministic;
   int use_tma;
-  long long inject_unpublished;
 };
 
-// Cluster-wide sum of 2C per-thread values; every CTA gets the totals in `tot` (2C floats).
-template <int C>
-__device__ __forceinline__ void cluster_sum_2c(float (&v)[2 * C], float (*warp_part)[2 * C], float* part,
-                                               float* tot, int G, cg::cluster_group& cluster) {
-  constexpr int NW = kBwdThreads / 32;
-  constexpr int kShift = 5 - log2i<2 * C>();
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float total = transpose_reduce<2 * C>(v, lane);
-  if ((lane & ((1 << kShift) - 1)) == 0) warp_part[warp][lane >> kShift] = total;
-  __syncthreads();
-  if (tid < 2 * C) {
-    float sum = 0.0f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) sum += warp_part[w][tid];
-    part[tid] = sum;
-  }
-  cluster.sync();
-  if (tid < 2 * C) {
-    float q[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) q[r] = r < G ? cluster.map_shared_rank(part, r)[tid] : 0.0f;
-    float sum = 0.0f;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) sum += q[r];
-    tot[tid] = sum;
-  }
-}
-
+// ------------------------------------------------------------------------------ reverse summary
 template <typename TIO, int C>
-__device__ __forceinline__ void fetch_bwd_tile(const BwdParams& p, BwdSmem<TIO, C>& S, long long row0,
-                                               int nvalid, int g) {
+__global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const BwdParams p) {
+  const int g = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int M = p.M, W = p.W;
   const int mbase = g * kBwdModes;
-  const int ncols = min(kBwdModes, p.M - mbase);
-  const TIO* xs = static_cast<const TIO*>(p.x) + row0 + mbase;
-  const TIO* ds = static_cast<const TIO*>(p.dy) + row0 + mbase;
-  if (p.use_tma) {
-    if (threadIdx.x < 32) {
-      const unsigned bytes = (unsigned)(ncols * sizeof(TIO));
-      if (threadIdx.x == 0) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&S.bar, bytes * 4u * (unsigned)nvalid);
-      }
-      __syncwarp();
-      for (int t = threadIdx.x; t < nvalid; t += 32) {
-        const long long o = (long long)t * p.W;
-        bulk_copy_g2s(&S.x[t][0][0], xs + o, bytes, &S.bar);
-        bulk_copy_g2s(&S.x[t][1][0], xs + o + p.M, bytes, &S.bar);
-        bulk_copy_g2s(&S.dy[t][0][0], ds + o, bytes, &S.bar);
-        bulk_copy_g2s(&S.dy[t][1][0], ds + o + p.M, bytes, &S.bar);
-      }
-    }
-  } else {
-    for (int i = threadIdx.x; i < nvalid * 2 * ncols; i += kBwdThreads) {
-      const int t = i / (2 * ncols), r = i - t * 2 * ncols, half = r / ncols, mm = r - half * ncols;
-      const long long o = (long long)t * p.W + half * p.M + mm;
-      S.x[t][half][mm] = xs[o];
-      S.dy[t][half][mm] = ds[o];
-    }
+  const int m = mbase + tid;
+  const bool act = m < M;
+  const long long B = p.B, T = p.T;
+  const long long k0 = blockIdx.y, nk = gridDim.y;
+  pdl_wait();  // the first launch of the backward: dy comes from the previous kernel
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  RsumSmem<TIO, C>& S = *reinterpret_cast<RsumSmem<TIO, C>*>(smem_raw);
+
+  const ModeConst mc = load_mode(p.pp, m, M, act);
+
+  {  // columns past M are never copied: zero dy there (the walk then stays at zero)
+    unsigned* z = reinterpret_cast<unsigned*>(&S.dy[0][0][0][0]);
+    for (int i = tid; i < (int)(sizeof(S.dy) / 4); i += kBwdThreads) z[i] = 0u;
   }
+  if (tid == 0) {
+    mbar_init(&S.bar[0], 1);
+    mbar_init(&S.bar[1], 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+
+  auto issue = [&](long long i, int buf) {
+    const TileRef r = tile_ref(i, B, T, C);
+    const long long row0 = (r.b * T + r.t0) * W;
+    const TIO* dsrc = static_cast<const TIO*>(p.dy) + row0;
+    const TIO* ysrc = static_cast<const TIO*>(p.y) + row0;
+    const float4* csrc = p.ctl + r.b * T + r.t0;
+    if (p.use_tma) {
+      if (tid == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&S.bar[buf], 2u * act_bytes<TIO>(M, mbase, kBwdModes, r.nvalid) + 16u * (unsigned)r.nvalid);
+        tma_act_rows<TIO, kBwdModes>(dsrc, W, M, mbase, r.nvalid, S.dy[buf], &S.bar[buf]);
+        tma_act_rows<TIO, kBwdModes>(ysrc, W, M, mbase, r.nvalid, S.y[buf], &S.bar[buf]);
+        bulk_copy_g2s(&S.ctl[buf][0], csrc, 16u * (unsigned)r.nvalid, &S.bar[buf]);
+      }
+    } else {
+      load_act_rows<TIO, kBwdModes>(dsrc, W, M, mbase, r.nvalid, S.dy[buf], kBwdThreads);
+      load_act_rows<TIO, kBwdModes>(ysrc, W, M, mbase, r.nvalid, S.y[buf], kBwdThreads);
+      for (int t = tid; t < r.nvalid; t += kBwdThreads) S.ctl[buf][t] = csrc[t];
+    }
+  };
+  if (k0 < p.tiles) issue(k0, 0);
+  bool timed_out = false;
+
+  for (long long n = 0;; ++n) {
+    const long long i = k0 + n * nk;
+    if (i >= p.tiles) break;
+    const int buf = (int)(n & 1);
+    if (i + nk < p.tiles) issue(i + nk, buf ^ 1);
+    const TileRef r = tile_ref(i, B, T, C);
+    if (p.use_tma) {
+      if (!mbar_wait(&S.bar[buf], (unsigned)((n >> 1) & 1), p.max_spin << 4)) timed_out = true;
+    } else {
+      __syncthreads();
+    }
+    const TIO(*dyt)[2][kBwdModes] = S.dy[buf];
+    const TIO(*yt)[2][kBwdModes] = S.y[buf];
+    const float4* ctl = S.ctl[buf];
+    auto body = [&](auto full_tag) {
+      constexpr bool kFull = decltype(full_tag)::value;
+      constexpr int kU = kFull ? 4 : 1;
+      float2 q = make_float2(0.0f, 0.0f);
+      float2 P = make_float2(1.0f, 0.0f);
+#pragma unroll kU
+      for (int t = C - 1; t >= 0; --t) {
+        if (kFull || t < r.nvalid) {
+          const float4 k4 = ctl[t];
+          const float gr = to_float(dyt[t][0][tid]);
+          const float gi = to_float(dyt[t][1][tid]);
+          const float yr = to_float(yt[t][0][tid]);
+          const float yi = to_float(yt[t][1][tid]);
+          q.x += yr > 0.0f ? gr : 0.0f;
+          q.y += yi > 0.0f ? gi : 0.0f;
+          const float2 a = token_transition(mc, k4.x, k4.y);
+          q = make_float2(fmaf(a.x, q.x, a.y * q.y), fmaf(a.x, q.y, -a.y * q.x));
+          P = cmul(a, P);
+        }
+      }
+      if (act) __stcg(p.agg + (r.b * p.chunks + r.c) * (long long)p.Mp + m, make_float4(P.x, -P.y, q.x, q.y));
+    };
+    if (r.nvalid == C) body(std::true_type{});
+    else body(std::false_type{});
+    __syncthreads();
+  }
+  if (timed_out) atomicOr(&p.ls->status, kStatusTimeout);
 }
 
-template <typename TIO, int C, bool kFast, bool kVec>
-__global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams p) {
+// ------------------------------------------------------------------------------ gradients
+// Gradient contributions of one (token, mode): updates the adjoint lam in place (to conj(a)
+// lam) and returns the write-path dx of the content (real, imaginary); adds the token's dEta /
+// dDelta contributions to ve / vd and the per-mode parameter terms to fa.
+template <bool kFast>
+__device__ __forceinline__ float2 grad_step(const ModeConst& mc, const float4 k4, float2& lam, float2 pv,
+                                            float cx, float cy, float& ve, float& vd, float (&fa)[5]) {
+  const TokenCoef k = token_coef<kFast>(mc, k4.x, k4.y, k4.z, k4.w);
+  const float ar = k.a.x, ai = k.a.y;
+  const float gar = fmaf(lam.x, pv.x, lam.y * pv.y);
+  const float gai = fmaf(lam.y, pv.x, -lam.x * pv.y);
+  const float pg = fmaf(gai, ar, -gar * ai);
+  const float radial = k.z * fmaf(k.rho * k4.y, pg, -fmaf(gar, ar, gai * ai));
+  const float dscan = pg - k.rho * pg;
+  const float cr = tanh_t<kFast>(cx);
+  const float ci = tanh_t<kFast>(cy);
+  const float gg = k.gain * fmaf(lam.x, cr, lam.y * ci);
+  const float gq = gg * fmaf(-0.5f, k.gate, 1.0f);
+  const float dyn = k.z * k.rho * k.rho * rcp_approx(k.num);
+  ve = radial + fmaf(gg, dyn, gq * mc.wrr * kInvLn16);
+  vd = fmaf(gq * mc.wpr, kInvHalfPi, dscan);
+  fa[0] += radial + gg * (dyn - mc.stat);
+  fa[1] += pg;
+  fa[2] += gg;
+  fa[3] = fmaf(gq, k4.z, fa[3]);
+  fa[4] = fmaf(gq, k4.w, fa[4]);
+  const float2 dxc = make_float2(lam.x * k.gain * fmaf(-cr, cr, 1.0f), lam.y * k.gain * fmaf(-ci, ci, 1.0f));
+  lam = make_float2(fmaf(ar, lam.x, ai * lam.y), fmaf(ar, lam.y, -ai * lam.x));
+  return dxc;
+}
+
+template <typename TIO, int C, bool kFast>
+__global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const BwdParams p) {
+  static_assert(C % kGroup == 0, "the reverse walk runs in groups of kGroup tokens");
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
   const int G = (int)cluster.num_blocks();
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int M = p.M, W = p.W;
-  const int m0 = g * kBwdModes + 2 * tid;
-  const int Mp = G * kBwdModes;
-  const bool act0 = m0 < M, act1 = m0 + 1 < M;
+  const int mbase = g * kBwdModes;
+  const int m = mbase + tid;
+  const int Mp = p.Mp;
+  const bool act = m < M;
   const long long B = p.B, T = p.T;
   const int chunks = p.chunks;
+  const int ncols = min(kBwdModes, M - mbase);
+  const long long k0 = blockIdx.y, nk = gridDim.y;
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  BwdSmem<TIO, C>& S = *reinterpret_cast<BwdSmem<TIO, C>*>(smem_raw);
+  GradSmem<TIO, C>& S = *reinterpret_cast<GradSmem<TIO, C>*>(smem_raw);
 
-  const ModeConst mc0 = load_mode(p.pp, m0, M, act0);
-  const ModeConst mc1 = load_mode(p.pp, m0 + 1, M, act1);
-  const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
-  LookbackCtx lc{p.ls, p.flags, p.agg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, G, Mp, B,
-                 p.deterministic != 0};
+  const ModeConst mc = load_mode(p.pp, m, M, act);
 
   {
     unsigned* z = reinterpret_cast<unsigned*>(&S.x[0][0][0]);
@@ -161,246 +236,150 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
   }
   __syncthreads();
 
-  double acc[2][kPartModes];
+  double acc[kPartModes];
 #pragma unroll
-  for (int q = 0; q < kPartModes; ++q) acc[0][q] = acc[1][q] = 0.0;
+  for (int q = 0; q < kPartModes; ++q) acc[q] = 0.0;
   double acc_b0 = 0.0, acc_b1 = 0.0;
   bool timed_out = false;
+  pdl_wait();  // the adjoint carries (scan) are complete from here on
 
-  for (int it = 0;; ++it) {
-    const int par = it & 1;
-    if (tid == 0 && g == 0) S.ring[par] = atomicAdd(&p.ls->ticket, 1u);
-    cluster.sync();
-    if (tid == 0 && g != 0) S.ring[par] = *cluster.map_shared_rank(&S.ring[par], 0);
-    __syncthreads();
-    const long long ticket = S.ring[par];
-    if (ticket >= p.tiles) break;
-    const long long b = ticket % B;
-    const int c = chunks - 1 - (int)(ticket / B);
-    const long long t0 = (long long)c * C;
-    const int nvalid = (int)(T - t0 < C ? T - t0 : C);
-    const long long row0 = (b * T + t0) * W;
-    fetch_bwd_tile<TIO, C>(p, S, row0, nvalid, g);
-    if (tid == 0) S.pred = c < chunks - 1 ? ld_acquire(p.flags + (ticket - B) * G + g) : 0u;
-    if (p.use_tma) {
-      if (!mbar_wait(&S.bar, (unsigned)par, p.max_spin << 4)) timed_out = true;
-    } else {
-      __syncthreads();
-    }
-
-    // controls (recomputed from x)
+  for (long long n = 0;; ++n) {
+    const long long i = k0 + n * nk;
+    if (i >= p.tiles) break;
+    const int par = (int)(n & 1);
+    const TileRef r = tile_ref(i, B, T, C);
+    const long long b = r.b;
+    const int c = r.c;
+    const long long row0 = (b * T + r.t0) * W;
     {
-      float v[2 * C];
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
-        const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
-        v[t] = fmaf(xr.x, mc0.d0r, fmaf(xi.x, mc0.d0i, fmaf(xr.y, mc1.d0r, xi.y * mc1.d0i)));
-        v[C + t] = fmaf(xr.x, mc0.d1r, fmaf(xi.x, mc0.d1i, fmaf(xr.y, mc1.d1r, xi.y * mc1.d1i)));
+      const TIO* xs = static_cast<const TIO*>(p.x) + row0;
+      const TIO* ds = static_cast<const TIO*>(p.dy) + row0;
+      const float4* cs = p.ctl + b * T + r.t0;
+      const float2* hs = c > 0 ? p.carry + (b * chunks + (c - 1)) * (long long)M + mbase : nullptr;
+      const float2* ks = c < chunks - 1 ? p.kout + (b * chunks + (c + 1)) * (long long)M + mbase : nullptr;
+      if (p.use_tma) {
+        if (tid == 0) {
+          fence_proxy_async_smem();
+          unsigned bytes = 2u * act_bytes<TIO>(M, mbase, kBwdModes, r.nvalid) + 16u * (unsigned)r.nvalid;
+          if (hs != nullptr) bytes += (unsigned)ncols * 8u;
+          if (ks != nullptr) bytes += (unsigned)ncols * 8u;
+          mbar_arrive_expect_tx(&S.bar, bytes);
+          tma_act_rows<TIO, kBwdModes>(xs, W, M, mbase, r.nvalid, S.x, &S.bar);
+          tma_act_rows<TIO, kBwdModes>(ds, W, M, mbase, r.nvalid, S.dy, &S.bar);
+          bulk_copy_g2s(&S.ctl[0], cs, 16u * (unsigned)r.nvalid, &S.bar);
+          if (hs != nullptr) bulk_copy_g2s(&S.hin[0], hs, (unsigned)ncols * 8u, &S.bar);
+          if (ks != nullptr) bulk_copy_g2s(&S.kin[0], ks, (unsigned)ncols * 8u, &S.bar);
+        }
+        if (!mbar_wait(&S.bar, (unsigned)par, p.max_spin << 4)) timed_out = true;
+      } else {
+        load_act_rows<TIO, kBwdModes>(xs, W, M, mbase, r.nvalid, S.x, kBwdThreads);
+        load_act_rows<TIO, kBwdModes>(ds, W, M, mbase, r.nvalid, S.dy, kBwdThreads);
+        for (int t = tid; t < r.nvalid; t += kBwdThreads) S.ctl[t] = cs[t];
+        for (int mm = tid; mm < ncols; mm += kBwdThreads) {
+          if (hs != nullptr) S.hin[mm] = hs[mm];
+          if (ks != nullptr) S.kin[mm] = ks[mm];
+        }
+        __syncthreads();
       }
-      cluster_sum_2c<C>(v, S.warp_part, S.part_ctl[par], S.tot, G, cluster);
-      __syncthreads();
-      if (tid < C) {
-        const float tau0 = tanh_accurate(S.tot[tid] + bias0);
-        const float tau1 = tanh_accurate(S.tot[C + tid] + bias1);
-        S.ctl[tid] = make_float4(expf(kLn16 * tau1), kHalfPi * tau0, tau0, tau1);
-      }
-      __syncthreads();
     }
+    const int nvalid = r.nvalid;
 
     // the tile body, instantiated branch-free for full chunks and with guards for the ragged last chunk
     auto tile_body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr int kU = kFull ? 4 : 1;  // partial unrolling keeps the kernel's code in the i-cache
-      // pass 0: replay the states from the forward's carry; relu masks on dy; chunk product
-      float2 hin0 = make_float2(0.0f, 0.0f), hin1 = hin0;
+      // pass 0: replay the states from the forward's carry; relu masks on dy
+      float2 hin = make_float2(0.0f, 0.0f);
       if (c > 0) {
-        const float2* cp = p.carry + (b * chunks + (c - 1)) * M + m0;
-        if (act0) hin0 = cp[0];
-        if (act1) hin1 = cp[1];
-      } else if (p.h0_r != nullptr) {
-        if (act0) hin0 = make_float2(p.h0_r[b * M + m0], p.h0_i[b * M + m0]);
-        if (act1) hin1 = make_float2(p.h0_r[b * M + m0 + 1], p.h0_i[b * M + m0 + 1]);
+        if (act) hin = S.hin[tid];
+      } else if (p.h0_r != nullptr && act) {
+        hin = make_float2(p.h0_r[b * M + m], p.h0_i[b * M + m]);
       }
-      float2 P0 = make_float2(1.0f, 0.0f), P1 = P0;
       {
-        float2 h0 = hin0, h1 = hin1;
-  #pragma unroll kU
+        float2 h = hin;
+#pragma unroll kU
         for (int t = 0; t < C; ++t) {
           if (kFull || t < nvalid) {
             const float4 k4 = S.ctl[t];
-            const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
-            const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
-            const TokenCoef k0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
-            const TokenCoef k1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
-            h0 = cfma(k0.a, h0, make_float2(k0.gain * tanh_t<kFast>(xr.x), k0.gain * tanh_t<kFast>(xi.x)));
-            h1 = cfma(k1.a, h1, make_float2(k1.gain * tanh_t<kFast>(xr.y), k1.gain * tanh_t<kFast>(xi.y)));
-            P0 = cmul(k0.a, P0);
-            P1 = cmul(k1.a, P1);
-            *reinterpret_cast<float4*>(&S.h[t][2 * tid]) = make_float4(h0.x, h0.y, h1.x, h1.y);
-            const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
-            const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
-            Pair<TIO>::store(&S.dy[t][0][2 * tid], h0.x > 0.0f ? gr.x : 0.0f, h1.x > 0.0f ? gr.y : 0.0f);
-            Pair<TIO>::store(&S.dy[t][1][2 * tid], h0.y > 0.0f ? gi.x : 0.0f, h1.y > 0.0f ? gi.y : 0.0f);
+            const float xr = to_float(S.x[t][0][tid]);
+            const float xi = to_float(S.x[t][1][tid]);
+            const TokenCoef kc = token_coef<kFast>(mc, k4.x, k4.y, k4.z, k4.w);
+            h = cfma(kc.a, h, make_float2(kc.gain * tanh_t<kFast>(xr), kc.gain * tanh_t<kFast>(xi)));
+            S.h[t][tid] = h;
+            const float gr = to_float(S.dy[t][0][tid]);
+            const float gi = to_float(S.dy[t][1][tid]);
+            S.dy[t][0][tid] = from_float<TIO>(h.x > 0.0f ? gr : 0.0f);
+            S.dy[t][1][tid] = from_float<TIO>(h.y > 0.0f ? gi : 0.0f);
           }
         }
       }
 
-      // carry of the adjoint from the later chunks
-      const unsigned pst = S.pred;
-      const bool last_chunk = c == chunks - 1;
-      const bool pred_ready = last_chunk || (!lc.deterministic && ((pst >> 2) == (lc.epoch & 0x3fffffffu)) &&
-                                             (pst & 3u) == kFlagInclusive);
-      const bool publish = ticket != p.inject_unpublished;
-      float2 kin0 = make_float2(0.0f, 0.0f), kin1 = kin0;
-      if (last_chunk) {
-        if (p.glast_r != nullptr) {
-          if (act0) kin0 = make_float2(p.glast_r[b * M + m0], p.glast_i[b * M + m0]);
-          if (act1) kin1 = make_float2(p.glast_r[b * M + m0 + 1], p.glast_i[b * M + m0 + 1]);
-        }
-      } else if (pred_ready) {
-        const float2* ip = p.incl + (ticket - B) * Mp + m0;
-        kin0 = __ldcg(ip);
-        kin1 = __ldcg(ip + 1);
-      } else {
-        // pass A: local reverse adjoint from zero -> aggregate (conj P, Qr)
-        float2 q0 = make_float2(0.0f, 0.0f), q1 = q0;
-  #pragma unroll kU
-        for (int t = C - 1; t >= 0; --t) {
+      // adjoint carry entering the chunk from the later chunks
+      float2 lam = make_float2(0.0f, 0.0f);
+      if (c < chunks - 1) {
+        if (act) lam = S.kin[tid];
+      } else if (p.glast_r != nullptr && act) {
+        lam = make_float2(p.glast_r[b * M + m], p.glast_i[b * M + m]);
+      }
+
+      // pass B: the true adjoint with every gradient, kGroup tokens at a time; each group's
+      // dEta / dDelta are reduced over the warp at once (lane 4u+j holds value u of the group)
+      float fa[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+      for (int t1 = C - 1; t1 >= 0; t1 -= kGroup) {
+        float v[2 * kGroup];
+#pragma unroll
+        for (int u = 0; u < kGroup; ++u) {
+          const int t = t1 - u;
+          float ve = 0.0f, vd = 0.0f;
           if (kFull || t < nvalid) {
             const float4 k4 = S.ctl[t];
-            const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
-            const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
-            q0.x += gr.x;
-            q0.y += gi.x;
-            q1.x += gr.y;
-            q1.y += gi.y;
-            const float2 a0 = token_transition(mc0, k4.x, k4.y);
-            const float2 a1 = token_transition(mc1, k4.x, k4.y);
-            q0 = make_float2(fmaf(a0.x, q0.x, a0.y * q0.y), fmaf(a0.x, q0.y, -a0.y * q0.x));
-            q1 = make_float2(fmaf(a1.x, q1.x, a1.y * q1.y), fmaf(a1.x, q1.y, -a1.y * q1.x));
+            lam.x += to_float(S.dy[t][0][tid]);
+            lam.y += to_float(S.dy[t][1][tid]);
+            const float2 pv = t > 0 ? S.h[t - 1][tid] : hin;
+            const float cx = to_float(S.x[t][0][tid]);
+            const float cy = to_float(S.x[t][1][tid]);
+            // h[t] was last read as the previous state at step t+1: its slot now holds the
+            // write-path dx
+            S.h[t][tid] = grad_step<kFast>(mc, k4, lam, pv, cx, cy, ve, vd, fa);
           }
+          v[u] = ve;
+          v[kGroup + u] = vd;
         }
-        const float2* incl = p.incl;
-        float2 A[2] = {make_float2(P0.x, -P0.y), make_float2(P1.x, -P1.y)}, Bv[2] = {q0, q1}, kin[2];
-        lookback<2>(lc, ticket, g, chunks - 1 - c, A, Bv, publish, pst, S.win, m0,
-                    [&](int j, float2 (&hh)[2]) {
-                      const float2* ip = incl + (ticket - (long long)j * B) * Mp + m0;
-                      hh[0] = __ldcg(ip);
-                      hh[1] = __ldcg(ip + 1);
-                    },
-                    kin);
-        kin0 = kin[0];
-        kin1 = kin[1];
-        // publish the inclusive carry now (the fast path publishes it after pass B)
-        if (publish) {
-          const float2 o0 = cfma(make_float2(P0.x, -P0.y), kin0, q0);
-          const float2 o1 = cfma(make_float2(P1.x, -P1.y), kin1, q1);
-          *reinterpret_cast<float4*>(p.incl + ticket * Mp + m0) = make_float4(o0.x, o0.y, o1.x, o1.y);
-          publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
+        constexpr int kShift = 5 - log2i<2 * kGroup>();
+        const float total = transpose_reduce<2 * kGroup>(v, lane);
+        if ((lane & ((1 << kShift) - 1)) == 0) {
+          const int u = lane >> kShift;  // 0..2*kGroup-1: ve of tokens t1..t1-3, then vd
+          const int t = t1 - (u % kGroup);
+          S.warp_part[warp][(u < kGroup ? 0 : C) + t] = total;
         }
       }
-
-      // pass B: the true adjoint with every gradient
-      float fa[2][5];
-  #pragma unroll
-      for (int q = 0; q < 5; ++q) fa[0][q] = fa[1][q] = 0.0f;
-      float2 lam0 = kin0, lam1 = kin1;
-  #pragma unroll kU
-      for (int t = C - 1; t >= 0; --t) {
-        float ve = 0.0f, vd = 0.0f;
-        if (kFull || t < nvalid) {
-          const float4 k4 = S.ctl[t];
-          const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
-          const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
-          lam0.x += gr.x;
-          lam0.y += gi.x;
-          lam1.x += gr.y;
-          lam1.y += gi.y;
-          float4 prev;
-          if (t > 0) prev = *reinterpret_cast<const float4*>(&S.h[t - 1][2 * tid]);
-          else prev = make_float4(hin0.x, hin0.y, hin1.x, hin1.y);
-          const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
-          const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
-          float4 dxc;
-  #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const ModeConst& mc = q == 0 ? mc0 : mc1;
-            float2& lam = q == 0 ? lam0 : lam1;
-            const float2 pv = q == 0 ? make_float2(prev.x, prev.y) : make_float2(prev.z, prev.w);
-            const float cx = q == 0 ? xr.x : xr.y, cy = q == 0 ? xi.x : xi.y;
-            const TokenCoef k = token_coef<kFast>(mc, k4.x, k4.y, k4.z, k4.w);
-            const float ar = k.a.x, ai = k.a.y;
-            const float gar = fmaf(lam.x, pv.x, lam.y * pv.y);
-            const float gai = fmaf(lam.y, pv.x, -lam.x * pv.y);
-            const float pg = fmaf(gai, ar, -gar * ai);
-            const float radial = k.z * fmaf(k.rho * k4.y, pg, -fmaf(gar, ar, gai * ai));
-            const float dscan = pg - k.rho * pg;
-            const float cr = tanh_t<kFast>(cx);
-            const float ci = tanh_t<kFast>(cy);
-            const float gg = k.gain * fmaf(lam.x, cr, lam.y * ci);
-            const float gq = gg * fmaf(-0.5f, k.gate, 1.0f);
-            const float dyn = k.z * k.rho * k.rho * rcp_approx(k.num);
-            ve += radial + fmaf(gg, dyn, gq * mc.wrr * kInvLn16);
-            vd += fmaf(gq * mc.wpr, kInvHalfPi, dscan);
-            fa[q][0] += radial + gg * (dyn - mc.stat);
-            fa[q][1] += pg;
-            fa[q][2] += gg;
-            fa[q][3] = fmaf(gq, k4.z, fa[q][3]);
-            fa[q][4] = fmaf(gq, k4.w, fa[q][4]);
-            const float dr = lam.x * k.gain * fmaf(-cr, cr, 1.0f);
-            const float di = lam.y * k.gain * fmaf(-ci, ci, 1.0f);
-            if (q == 0) {
-              dxc.x = dr;
-              dxc.y = di;
-            } else {
-              dxc.z = dr;
-              dxc.w = di;
-            }
-            lam = make_float2(fmaf(ar, lam.x, ai * lam.y), fmaf(ar, lam.y, -ai * lam.x));
-          }
-          // h[t] was last read as `prev` at step t+1: its slot now holds the write-path dx
-          *reinterpret_cast<float4*>(&S.h[t][2 * tid]) = dxc;
-        }
-        S.vt[t][tid] = ve;
-        S.vt[C + t][tid] = vd;
+      if (!act) {
+#pragma unroll
+        for (int q = 0; q < 5; ++q) fa[q] = 0.0f;
       }
-      if (!act0) {
-        lam0 = make_float2(0.0f, 0.0f);
-  #pragma unroll
-        for (int q = 0; q < 5; ++q) fa[0][q] = 0.0f;
-      }
-      if (!act1) {
-        lam1 = make_float2(0.0f, 0.0f);
-  #pragma unroll
-        for (int q = 0; q < 5; ++q) fa[1][q] = 0.0f;
-      }
-      if (pred_ready && publish) {
-        // fast path: the carry toward the earlier chunk is conj(a_t0) lambda_t0 = lam now
-        *reinterpret_cast<float4*>(p.incl + ticket * Mp + m0) = make_float4(lam0.x, lam0.y, lam1.x, lam1.y);
-        publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-      }
-      if (c == 0 && p.gh0_r != nullptr) {
-        if (act0) {
-          p.gh0_r[b * M + m0] = lam0.x;
-          p.gh0_i[b * M + m0] = lam0.y;
-        }
-        if (act1) {
-          p.gh0_r[b * M + m0 + 1] = lam1.x;
-          p.gh0_i[b * M + m0 + 1] = lam1.y;
-        }
-      }
-  #pragma unroll
-      for (int q = 0; q < 5; ++q) {
-        acc[0][q] += fa[0][q];
-        acc[1][q] += fa[1][q];
-      }
+#pragma unroll
+      for (int q = 0; q < 5; ++q) acc[q] += fa[q];
 
       // token sums over all modes -> controller gradients
-      float v[2 * C];
+      __syncthreads();
+      if (tid < 2 * C) {
+        float sum = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 2 * C; ++i) v[i] = S.vt[i][tid];
-      cluster_sum_2c<C>(v, S.warp_part, S.part_grad[par], S.tot, G, cluster);
+        for (int w = 0; w < kBwdWarps; ++w) sum += S.warp_part[w][tid];
+        S.part_grad[par][tid] = sum;
+      }
+      if (G > 1) cluster.sync();
+      else __syncthreads();
+      if (tid < 2 * C) {
+        float q[8];
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) q[rr] = rr < G ? cluster.map_shared_rank(&S.part_grad[par][0], rr)[tid] : 0.0f;
+        float sum = 0.0f;
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) sum += q[rr];
+        S.tot[tid] = sum;
+      }
       __syncthreads();
       if (tid < C) {
         const float4 k4 = S.ctl[tid];
@@ -410,47 +389,27 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
       }
       __syncthreads();
       TIO* dxrow = static_cast<TIO*>(p.dx) + row0;
-      float fd[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-  #pragma unroll kU
+      float fd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < nvalid) {
           const float2 dp = S.dp[t];
-          const float4 dxc = *reinterpret_cast<const float4*>(&S.h[t][2 * tid]);
-          const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
-          const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
-          const float r0 = fmaf(dp.x, mc0.d0r, fmaf(dp.y, mc0.d1r, dxc.x));
-          const float i0 = fmaf(dp.x, mc0.d0i, fmaf(dp.y, mc0.d1i, dxc.y));
-          const float r1 = fmaf(dp.x, mc1.d0r, fmaf(dp.y, mc1.d1r, dxc.z));
-          const float i1 = fmaf(dp.x, mc1.d0i, fmaf(dp.y, mc1.d1i, dxc.w));
-          TIO* row = dxrow + (long long)t * W;
-          if (kVec && act1) {
-            Pair<TIO>::store(row + m0, r0, r1);
-            Pair<TIO>::store(row + M + m0, i0, i1);
-          } else {
-            if (act0) {
-              Io<TIO>::store(row + m0, r0);
-              Io<TIO>::store(row + M + m0, i0);
-            }
-            if (act1) {
-              Io<TIO>::store(row + m0 + 1, r1);
-              Io<TIO>::store(row + M + m0 + 1, i1);
-            }
+          const float2 dxc = S.h[t][tid];
+          const float xr = to_float(S.x[t][0][tid]);
+          const float xi = to_float(S.x[t][1][tid]);
+          if (act) {
+            TIO* row = dxrow + (long long)t * W;
+            Io<TIO>::store(row + m, fmaf(dp.x, mc.d0r, fmaf(dp.y, mc.d1r, dxc.x)));
+            Io<TIO>::store(row + M + m, fmaf(dp.x, mc.d0i, fmaf(dp.y, mc.d1i, dxc.y)));
           }
-          fd[0][0] = fmaf(xr.x, dp.x, fd[0][0]);
-          fd[0][1] = fmaf(xi.x, dp.x, fd[0][1]);
-          fd[0][2] = fmaf(xr.x, dp.y, fd[0][2]);
-          fd[0][3] = fmaf(xi.x, dp.y, fd[0][3]);
-          fd[1][0] = fmaf(xr.y, dp.x, fd[1][0]);
-          fd[1][1] = fmaf(xi.y, dp.x, fd[1][1]);
-          fd[1][2] = fmaf(xr.y, dp.y, fd[1][2]);
-          fd[1][3] = fmaf(xi.y, dp.y, fd[1][3]);
+          fd[0] = fmaf(xr, dp.x, fd[0]);
+          fd[1] = fmaf(xi, dp.x, fd[1]);
+          fd[2] = fmaf(xr, dp.y, fd[2]);
+          fd[3] = fmaf(xi, dp.y, fd[3]);
         }
       }
-  #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc[0][5 + q] += fd[0][q];
-        acc[1][5 + q] += fd[1][q];
-      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[5 + q] += fd[q];
     };
     if (nvalid == C) tile_body(std::true_type{});
     else tile_body(std::false_type{});
@@ -463,22 +422,18 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_kernel(const BwdParams 
       acc_b0 += s0;
       acc_b1 += s1;
     }
-    __syncthreads();
+    __syncthreads();  // every shared array is free for the next tile
   }
   // per-cluster partial parameter gradients (reduced in a fixed order by mixer_reduce_kernel)
-  const long long k = blockIdx.y;
-  double* part = p.part + k * (long long)kPartModes * Mp;
+  const long long kc = blockIdx.y;
+  double* part = p.part + kc * (long long)kPartModes * Mp;
 #pragma unroll
-  for (int q = 0; q < kPartModes; ++q) {
-    part[(long long)q * Mp + m0] = act0 ? acc[0][q] : 0.0;
-    part[(long long)q * Mp + m0 + 1] = act1 ? acc[1][q] : 0.0;
-  }
+  for (int q = 0; q < kPartModes; ++q) part[(long long)q * Mp + m] = act ? acc[q] : 0.0;
   if (g == 0 && tid == 0) {
-    double* pb = p.part + (long long)gridDim.y * kPartModes * Mp + 2 * k;
+    double* pb = p.part + (long long)gridDim.y * kPartModes * Mp + 2 * kc;
     pb[0] = acc_b0;
     pb[1] = acc_b1;
   }
-  if (timed_out && tid == 0) atomicOr(&p.ls->status, kStatusTimeout);
+  if (timed_out) atomicOr(&p.ls->status, kStatusTimeout);
   cluster.sync();
-  finish_launch(p.ls);
 }

@@ -1,38 +1,43 @@
-// SPARC mixer forward kernel (included by mixer.cu, which holds the shared helpers).
+// SPARC mixer forward kernels (included by mixer.cu, which holds the shared helpers and the
+// carry scan). The forward is three launches:
 //
-// One thread-block cluster of G CTAs processes a tile (batch row b, chunk of C tokens, all M
-// modes); CTA g owns modes [g*256, g*256+256), two adjacent modes per thread (vectorised
-// bf16x2 / float2 I/O, two independent recurrences per thread). The x tile of the CTA's
-// columns (C rows x (256 real + 256 imaginary) values) is brought into shared memory by TMA
-// bulk copies on an mbarrier (plain loads replace the copies when the shapes are not 16-byte
-// aligned). Clusters take tiles from a ticket counter, and a cluster takes its next ticket
-// only when it is ready to start that tile: a ticket held but not started would stall every
-// successor tile's lookback behind it. (Prefetching the next tile's copy into a second buffer
-// was measured slower: the extra shared memory costs a resident CTA per SM.)
+//   mixer_fwd_summary_kernel   per tile (batch row b, chunk of C tokens, all M modes): the
+//                              token controls (projection of x onto the two controller
+//                              directions, reduced over all modes: warp transpose-reduce ->
+//                              shared memory -> distributed shared memory across the cluster of
+//                              G CTAs that share the tile), saved per token for the replay and
+//                              the backward; then the chunk's aggregate affine map
+//                              h_out = P h_in + Q per mode (P = prod a_t, Q = the local scan).
+//   mixer_carry_scan_kernel    (mixer.cu) the inclusive chunk states from the aggregates.
+//   mixer_fwd_replay_kernel    per tile again: from the carried-in state, h_t = a_t h_{t-1} + b_t
+//                              and y = relu([Re h, Im h]).
 //
-// Per tile: control projections of the C tokens (warp transpose-reduce, shared memory, then
-// distributed shared memory across the cluster), then the recurrence. If the predecessor
-// tile's carry is already published the recurrence runs in one pass; otherwise pass 1 keeps
-// the transitions and writes (or write gains) in shared memory, the decoupled lookback
-// resolves the carry, and pass 2 replays from shared memory.
+// Both tile kernels are persistent with a static schedule (tile k, k + n, k + 2n, ... for the
+// k-th of n CTAs or clusters): tiles do not depend on each other, so nothing waits on another
+// CTA. x tiles (and the replay's controls and carried-in states) arrive in shared memory by
+// TMA bulk copies on an mbarrier, double-buffered so the next tile's copy overlaps this tile's
+// arithmetic. CTA g of a tile owns modes [g*256, g*256+256), two adjacent modes per thread.
 
 // (included inside namespace sparc)
 
 constexpr int kFwdThreads = 128;
 constexpr int kFwdModes = 2 * kFwdThreads;  // modes per CTA
 
-template <typename TIO, int C, bool kFast>
-struct FwdSmem {
-  TIO x[1][C][2][kFwdModes];                         // [buffer][token][re|im][mode]
-  float2 a[C][kFwdModes];                            // slow path: transitions
-  float w[C][kFwdModes * (kFast ? 1 : 2)];           // slow path: gains (bf16) or writes (fp32)
-  float4 ctl[C];                                     // E, delta, tau0, tau1 per token
-  float part[2][2 * C];                              // this CTA's projection partials (peers read)
+template <typename TIO, int C>
+struct SumSmem {
+  TIO x[2][C][2][kFwdModes];  // [buffer][token][re|im][mode]
+  float4 ctl[C];              // E, delta, tau0, tau1 per token
+  float part[2][2 * C];       // this CTA's projection partials (peers read), by tile parity
   float warp_part[kFwdThreads / 32][2 * C];
-  unsigned long long bar[1];
-  long long ring[2];                                 // tickets, by tile parity
-  unsigned win[2];
-  unsigned pred;
+  unsigned long long bar[2];
+};
+
+template <typename TIO, int C>
+struct RepSmem {
+  TIO x[2][C][2][kFwdModes];
+  float4 ctl[2][C];
+  float2 hin[2][kFwdModes];  // carried-in state of the tile's modes
+  unsigned long long bar[2];
 };
 
 struct FwdParams {
@@ -41,19 +46,15 @@ struct FwdParams {
   MixerParamPtrs pp;
   const float* h0_r;
   const float* h0_i;
-  float* last_r;
-  float* last_i;
-  float2* carry;  // [B, chunks, M]
+  float4* ctl;          // [B, T] token controls (E, delta, tau0, tau1)
+  const float2* carry;  // [B, chunks, M] inclusive chunk states (replay input)
+  float4* agg;          // [B, chunks, Mp] chunk aggregates (P, Q)
   LaunchState* ls;
-  unsigned* flags;
-  float4* agg;
   long long B, T;
-  int W, M, chunks;
+  int W, M, Mp, chunks;
   long long tiles;
   unsigned max_spin;
-  int deterministic;
   int use_tma;
-  long long inject_unpublished;
 };
 
 template <typename TIO> struct Pair;
@@ -92,91 +93,117 @@ __device__ __forceinline__ void store_y_pair(TIO* row, int M, int m, bool a0, bo
   }
 }
 
-// Copy (or load) the CTA's columns of x rows t0..t0+C-1 into buffer `buf`.
-template <typename TIO, int C>
-__device__ __forceinline__ void fetch_x_tile(const FwdParams& p, TIO (*dst)[2][kFwdModes],
-                                             unsigned long long* bar, long long ticket, int g) {
-  const long long b = ticket % p.B;
-  const long long t0 = (long long)(ticket / p.B) * C;
-  const int nvalid = (int)(p.T - t0 < C ? p.T - t0 : C);
-  const int mbase = g * kFwdModes;
-  const int ncols = min(kFwdModes, p.M - mbase);
-  const TIO* src = static_cast<const TIO*>(p.x) + (b * p.T + t0) * p.W + mbase;
-  if (p.use_tma) {
-    if (threadIdx.x < 32) {  // warp 0: lane 0 sets the byte count, lane t copies row t
-      const unsigned bytes = (unsigned)(ncols * sizeof(TIO));
-      if (threadIdx.x == 0) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(bar, bytes * 2u * (unsigned)nvalid);
-      }
-      __syncwarp();
-      for (int t = threadIdx.x; t < nvalid; t += 32) {
-        bulk_copy_g2s(&dst[t][0][0], src + (long long)t * p.W, bytes, bar);
-        bulk_copy_g2s(&dst[t][1][0], src + (long long)t * p.W + p.M, bytes, bar);
-      }
-    }
-  } else {
-    for (int i = threadIdx.x; i < nvalid * 2 * ncols; i += kFwdThreads) {
-      const int t = i / (2 * ncols), r = i - t * 2 * ncols, half = r / ncols, mm = r - half * ncols;
-      dst[t][half][mm] = src[(long long)t * p.W + half * p.M + mm];
-    }
+// Tile geometry shared by all tile kernels: tile i covers row b = i % B, chunk c = i / B.
+struct TileRef {
+  long long b;
+  int c;
+  long long t0;
+  int nvalid;
+};
+__device__ __forceinline__ TileRef tile_ref(long long i, long long B, long long T, int C) {
+  TileRef r;
+  r.b = i % B;
+  r.c = (int)(i / B);
+  r.t0 = (long long)r.c * C;
+  r.nvalid = (int)(T - r.t0 < C ? T - r.t0 : C);
+  return r;
+}
+
+// TMA: bulk copies of the CTA's columns of `nvalid` activation rows (real half, imaginary
+// half) into dst[t][re|im][mode], completing on `bar`. Returns the bytes in flight.
+template <typename TIO, int NM>
+__device__ __forceinline__ unsigned tma_act_rows(const TIO* src, int W, int M, int mbase, int nvalid,
+                                                 TIO (*dst)[2][NM], unsigned long long* bar) {
+  const int ncols = min(NM, M - mbase);
+  const TIO* s = src + mbase;
+  const unsigned bytes = (unsigned)(ncols * sizeof(TIO));
+  for (int t = 0; t < nvalid; ++t) {
+    bulk_copy_g2s(&dst[t][0][0], s + (long long)t * W, bytes, bar);
+    bulk_copy_g2s(&dst[t][1][0], s + (long long)t * W + M, bytes, bar);
+  }
+  return bytes * 2u * (unsigned)nvalid;
+}
+
+// The same rows by plain loads spread over the CTA (shapes that are not 16-byte aligned).
+template <typename TIO, int NM>
+__device__ __forceinline__ void load_act_rows(const TIO* src, int W, int M, int mbase, int nvalid,
+                                              TIO (*dst)[2][NM], int nthreads) {
+  const int ncols = min(NM, M - mbase);
+  const TIO* s = src + mbase;
+  for (int i = threadIdx.x; i < nvalid * 2 * ncols; i += nthreads) {
+    const int t = i / (2 * ncols), r = i - t * 2 * ncols, half = r / ncols, mm = r - half * ncols;
+    dst[t][half][mm] = s[(long long)t * W + half * M + mm];
   }
 }
 
-template <typename TIO, int C, bool kFast, bool kVec>
-__global__ void __launch_bounds__(kFwdThreads) mixer_fwd_kernel(const FwdParams p) {
+template <typename TIO>
+__device__ __forceinline__ unsigned act_bytes(int M, int mbase, int NM, int nvalid) {
+  return (unsigned)(min(NM, M - mbase) * sizeof(TIO)) * 2u * (unsigned)nvalid;
+}
+
+// ------------------------------------------------------------------------------ summary
+template <typename TIO, int C, bool kFast>
+__global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const FwdParams p) {
   constexpr int NW = kFwdThreads / 32;
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
   const int G = (int)cluster.num_blocks();
   const int tid = threadIdx.x;
   const int M = p.M, W = p.W;
-  const int m0 = g * kFwdModes + 2 * tid;  // this thread's modes: m0, m0 + 1
+  const int mbase = g * kFwdModes;
+  const int m0 = mbase + 2 * tid;  // this thread's modes: m0, m0 + 1
   const bool act0 = m0 < M, act1 = m0 + 1 < M;
   const long long B = p.B, T = p.T;
+  const long long k0 = blockIdx.y, nk = gridDim.y;
+  pdl_wait();  // the first launch of the forward: parameters may have just been updated
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  FwdSmem<TIO, C, kFast>& S = *reinterpret_cast<FwdSmem<TIO, C, kFast>*>(smem_raw);
+  SumSmem<TIO, C>& S = *reinterpret_cast<SumSmem<TIO, C>*>(smem_raw);
 
   const ModeConst mc0 = load_mode(p.pp, m0, M, act0);
   const ModeConst mc1 = load_mode(p.pp, m0 + 1, M, act1);
   const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
-  LookbackCtx lc{p.ls, p.flags, p.agg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, G, G * kFwdModes, B,
-                 p.deterministic != 0};
 
-  // zero the x buffer once: columns past M are never copied and must read as zeros
+  // columns past M are never copied and must read as zeros
   {
     unsigned* xs = reinterpret_cast<unsigned*>(&S.x[0][0][0][0]);
     for (int i = tid; i < (int)(sizeof(S.x) / 4); i += kFwdThreads) xs[i] = 0u;
   }
   if (tid == 0) {
     mbar_init(&S.bar[0], 1);
+    mbar_init(&S.bar[1], 1);
     mbar_init_fence();
   }
   __syncthreads();
+
+  auto issue = [&](long long i, int buf) {
+    const TileRef r = tile_ref(i, B, T, C);
+    const TIO* src = static_cast<const TIO*>(p.x) + (r.b * T + r.t0) * W;
+    if (p.use_tma) {
+      if (tid == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&S.bar[buf], act_bytes<TIO>(M, mbase, kFwdModes, r.nvalid));
+        tma_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], &S.bar[buf]);
+      }
+    } else {
+      load_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], kFwdThreads);
+    }
+  };
+  if (k0 < p.tiles) issue(k0, 0);
   bool timed_out = false;
 
-  for (int it = 0;; ++it) {
-    const int par = it & 1;
-    if (tid == 0 && g == 0) S.ring[par] = atomicAdd(&p.ls->ticket, 1u);
-    cluster.sync();  // also: every peer is done with the previous tile's shared data
-    if (tid == 0 && g != 0) S.ring[par] = *cluster.map_shared_rank(&S.ring[par], 0);
-    __syncthreads();
-    const long long ticket = S.ring[par];
-    if (ticket >= p.tiles) break;
-    fetch_x_tile<TIO, C>(p, S.x[0], &S.bar[0], ticket, g);
-    const int buf = par;
-    const long long b = ticket % B;
-    const int c = (int)(ticket / B);
-    const long long t0 = (long long)c * C;
-    const int nvalid = (int)(T - t0 < C ? T - t0 : C);
-    if (tid == 0) S.pred = c > 0 ? ld_acquire(p.flags + (ticket - B) * G + g) : 0u;
+  for (long long n = 0;; ++n) {
+    const long long i = k0 + n * nk;
+    if (i >= p.tiles) break;
+    const int buf = (int)(n & 1);
+    if (i + nk < p.tiles) issue(i + nk, buf ^ 1);
+    const TileRef r = tile_ref(i, B, T, C);
     if (p.use_tma) {
-      if (!mbar_wait(&S.bar[0], (unsigned)par, p.max_spin << 4)) timed_out = true;
+      if (!mbar_wait(&S.bar[buf], (unsigned)((n >> 1) & 1), p.max_spin << 4)) timed_out = true;
     } else {
       __syncthreads();
     }
-    const TIO(*xt)[2][kFwdModes] = S.x[0];
+    const TIO(*xt)[2][kFwdModes] = S.x[buf];
 
     // control projections: per-thread partials over its 4 columns, reduced over the cluster
     {
@@ -199,163 +226,164 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_kernel(const FwdParams 
         for (int w = 0; w < NW; ++w) sum += S.warp_part[w][tid];
         S.part[buf][tid] = sum;
       }
-      cluster.sync();
+      if (G > 1) cluster.sync();
+      else __syncthreads();
       if (tid < C) {
         // the peers' partials are read together (their latencies overlap)
         float q0[8], q1[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          if (r < G) {
-            const float* peer = cluster.map_shared_rank(&S.part[buf][0], r);
-            q0[r] = peer[tid];
-            q1[r] = peer[C + tid];
+        for (int rr = 0; rr < 8; ++rr) {
+          if (rr < G) {
+            const float* peer = cluster.map_shared_rank(&S.part[buf][0], rr);
+            q0[rr] = peer[tid];
+            q1[rr] = peer[C + tid];
           } else {
-            q0[r] = q1[r] = 0.0f;
+            q0[rr] = q1[rr] = 0.0f;
           }
         }
         float p0 = 0.0f, p1 = 0.0f;
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          p0 += q0[r];
-          p1 += q1[r];
+        for (int rr = 0; rr < 8; ++rr) {
+          p0 += q0[rr];
+          p1 += q1[rr];
         }
         const float tau0 = tanh_accurate(p0 + bias0);
         const float tau1 = tanh_accurate(p1 + bias1);
-        S.ctl[tid] = make_float4(expf(kLn16 * tau1), kHalfPi * tau0, tau0, tau1);
+        const float4 k4 = make_float4(expf(kLn16 * tau1), kHalfPi * tau0, tau0, tau1);
+        S.ctl[tid] = k4;
+        if (g == 0 && tid < r.nvalid) p.ctl[r.b * T + r.t0 + tid] = k4;
       }
       __syncthreads();
     }
-    // the tile body, instantiated branch-free for full chunks (so the compiler can interleave
-    // independent tokens) and with guards for the ragged last chunk
-    auto tile_body = [&](auto full_tag) {
+
+    // the chunk's aggregate map per mode
+    auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr int kU = kFull ? 4 : 1;  // partial unrolling keeps the kernel's code in the i-cache
-      const unsigned pst = S.pred;
-      const bool pred_ready = c == 0 || (!lc.deterministic && ((pst >> 2) == (lc.epoch & 0x3fffffffu)) &&
-                                         (pst & 3u) == kFlagInclusive);
-      const bool publish = ticket != p.inject_unpublished;
-      TIO* yrow = static_cast<TIO*>(p.y) + (b * T + t0) * W;
-      float2 hout0, hout1;
-      if (pred_ready) {
-        float2 h0 = make_float2(0.0f, 0.0f), h1 = make_float2(0.0f, 0.0f);
-        if (c > 0) {
-          const float2* cp = p.carry + (b * p.chunks + (c - 1)) * M + m0;
-          if (act0) h0 = __ldcg(cp);
-          if (act1) h1 = __ldcg(cp + 1);
-        } else if (p.h0_r != nullptr) {
-          if (act0) h0 = make_float2(p.h0_r[b * M + m0], p.h0_i[b * M + m0]);
-          if (act1) h1 = make_float2(p.h0_r[b * M + m0 + 1], p.h0_i[b * M + m0 + 1]);
-        }
-  #pragma unroll kU
-        for (int t = 0; t < C; ++t) {
-          if (kFull || t < nvalid) {
-            const float4 k4 = S.ctl[t];
-            const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
-            const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-            const TokenCoef k0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
-            const TokenCoef k1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
-            h0 = cfma(k0.a, h0, make_float2(k0.gain * tanh_t<kFast>(xr.x), k0.gain * tanh_t<kFast>(xi.x)));
-            h1 = cfma(k1.a, h1, make_float2(k1.gain * tanh_t<kFast>(xr.y), k1.gain * tanh_t<kFast>(xi.y)));
-            store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, h0, h1);
-          }
-        }
-        hout0 = h0;
-        hout1 = h1;
-        if (publish) {
-          float2* cp = p.carry + (b * p.chunks + c) * M + m0;
-          if (act0) cp[0] = hout0;
-          if (act1) cp[1] = hout1;
-          publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-        }
-      } else {
-        float2 P0 = make_float2(1.0f, 0.0f), Q0 = make_float2(0.0f, 0.0f);
-        float2 P1 = P0, Q1 = Q0;
-  #pragma unroll kU
-        for (int t = 0; t < C; ++t) {
-          float2 a0 = make_float2(1.0f, 0.0f), a1 = a0, b0 = make_float2(0.0f, 0.0f), b1 = b0;
-          float g0 = 0.0f, g1 = 0.0f;
-          if (kFull || t < nvalid) {
-            const float4 k4 = S.ctl[t];
-            const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
-            const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-            const TokenCoef k0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
-            const TokenCoef k1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
-            a0 = k0.a;
-            a1 = k1.a;
-            g0 = k0.gain;
-            g1 = k1.gain;
-            b0 = make_float2(g0 * tanh_t<kFast>(xr.x), g0 * tanh_t<kFast>(xi.x));
-            b1 = make_float2(g1 * tanh_t<kFast>(xr.y), g1 * tanh_t<kFast>(xi.y));
-          }
-          *reinterpret_cast<float4*>(&S.a[t][2 * tid]) = make_float4(a0.x, a0.y, a1.x, a1.y);
-          if constexpr (kFast) {
-            *reinterpret_cast<float2*>(&S.w[t][2 * tid]) = make_float2(g0, g1);
-          } else {
-            *reinterpret_cast<float4*>(&S.w[t][4 * tid]) = make_float4(b0.x, b0.y, b1.x, b1.y);
-          }
-          Q0 = cfma(a0, Q0, b0);
-          P0 = cmul(a0, P0);
-          Q1 = cfma(a1, Q1, b1);
-          P1 = cmul(a1, P1);
-        }
-        const float2* carry = p.carry;
-        const int chunks = p.chunks;
-        float2 A[2] = {P0, P1}, Bv[2] = {Q0, Q1}, hin[2];
-        lookback<2>(lc, ticket, g, c, A, Bv, publish, pst, S.win, m0,
-                    [&](int j, float2 (&h)[2]) {
-                      const float2* cp = carry + (b * chunks + (c - j)) * M + m0;
-                      h[0] = act0 ? __ldcg(cp) : make_float2(0.0f, 0.0f);
-                      h[1] = act1 ? __ldcg(cp + 1) : make_float2(0.0f, 0.0f);
-                    },
-                    hin);
-        hout0 = cfma(P0, hin[0], Q0);
-        hout1 = cfma(P1, hin[1], Q1);
-        if (publish) {
-          float2* cp = p.carry + (b * p.chunks + c) * M + m0;
-          if (act0) cp[0] = hout0;
-          if (act1) cp[1] = hout1;
-          publish_flag(p.flags + ticket * G + g, make_flag(lc.epoch, kFlagInclusive));
-        }
-        float2 h0 = hin[0], h1 = hin[1];
-  #pragma unroll kU
-        for (int t = 0; t < C; ++t) {
-          if (kFull || t < nvalid) {
-            const float4 a4 = *reinterpret_cast<const float4*>(&S.a[t][2 * tid]);
-            float2 b0, b1;
-            if constexpr (kFast) {
-              const float2 gg = *reinterpret_cast<const float2*>(&S.w[t][2 * tid]);
-              const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
-              const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-              b0 = make_float2(gg.x * tanh_t<kFast>(xr.x), gg.x * tanh_t<kFast>(xi.x));
-              b1 = make_float2(gg.y * tanh_t<kFast>(xr.y), gg.y * tanh_t<kFast>(xi.y));
-            } else {
-              const float4 w4 = *reinterpret_cast<const float4*>(&S.w[t][4 * tid]);
-              b0 = make_float2(w4.x, w4.y);
-              b1 = make_float2(w4.z, w4.w);
-            }
-            h0 = cfma(make_float2(a4.x, a4.y), h0, b0);
-            h1 = cfma(make_float2(a4.z, a4.w), h1, b1);
-            store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, h0, h1);
-          }
+      float2 P0 = make_float2(1.0f, 0.0f), Q0 = make_float2(0.0f, 0.0f);
+      float2 P1 = P0, Q1 = Q0;
+#pragma unroll kU
+      for (int t = 0; t < C; ++t) {
+        if (kFull || t < r.nvalid) {
+          const float4 k4 = S.ctl[t];
+          const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
+          const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
+          const TokenCoef c0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
+          const TokenCoef c1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
+          Q0 = cfma(c0.a, Q0, make_float2(c0.gain * tanh_t<kFast>(xr.x), c0.gain * tanh_t<kFast>(xi.x)));
+          Q1 = cfma(c1.a, Q1, make_float2(c1.gain * tanh_t<kFast>(xr.y), c1.gain * tanh_t<kFast>(xi.y)));
+          P0 = cmul(c0.a, P0);
+          P1 = cmul(c1.a, P1);
         }
       }
-      if (c == p.chunks - 1 && p.last_r != nullptr) {
-        if (act0) {
-          p.last_r[b * M + m0] = hout0.x;
-          p.last_i[b * M + m0] = hout0.y;
-        }
-        if (act1) {
-          p.last_r[b * M + m0 + 1] = hout1.x;
-          p.last_i[b * M + m0 + 1] = hout1.y;
+      float4* ap = p.agg + (r.b * p.chunks + r.c) * (long long)p.Mp + m0;
+      if (act0) __stcg(ap, make_float4(P0.x, P0.y, Q0.x, Q0.y));
+      if (act1) __stcg(ap + 1, make_float4(P1.x, P1.y, Q1.x, Q1.y));
+    };
+    if (r.nvalid == C) body(std::true_type{});
+    else body(std::false_type{});
+    __syncthreads();  // the buffer and the shared arrays are free for the tile after next
+  }
+  if (timed_out) atomicOr(&p.ls->status, kStatusTimeout);
+  cluster.sync();  // no CTA leaves while a peer may still read its shared memory
+}
+
+// ------------------------------------------------------------------------------ replay
+template <typename TIO, int C, bool kFast, bool kVec>
+__global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const FwdParams p) {
+  const int g = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int M = p.M, W = p.W;
+  const int mbase = g * kFwdModes;
+  const int m0 = mbase + 2 * tid;
+  const bool act0 = m0 < M, act1 = m0 + 1 < M;
+  const long long B = p.B, T = p.T;
+  const long long k0 = blockIdx.y, nk = gridDim.y;
+  const int ncols = min(kFwdModes, M - mbase);
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  RepSmem<TIO, C>& S = *reinterpret_cast<RepSmem<TIO, C>*>(smem_raw);
+
+  const ModeConst mc0 = load_mode(p.pp, m0, M, act0);
+  const ModeConst mc1 = load_mode(p.pp, m0 + 1, M, act1);
+
+  if (tid == 0) {
+    mbar_init(&S.bar[0], 1);
+    mbar_init(&S.bar[1], 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+
+  pdl_wait();  // the controls (summary) and the carries (scan) are complete from here on
+
+  // Tile inputs: x rows, the C token controls and (for c > 0) the carried-in chunk state.
+  auto issue = [&](long long i, int buf) {
+    const TileRef r = tile_ref(i, B, T, C);
+    const TIO* src = static_cast<const TIO*>(p.x) + (r.b * T + r.t0) * W;
+    const float4* csrc = p.ctl + r.b * T + r.t0;
+    const float2* hsrc = r.c > 0 ? p.carry + (r.b * p.chunks + (r.c - 1)) * (long long)M + mbase : nullptr;
+    if (p.use_tma) {
+      if (tid == 0) {
+        fence_proxy_async_smem();
+        unsigned bytes = act_bytes<TIO>(M, mbase, kFwdModes, r.nvalid) + 16u * (unsigned)r.nvalid;
+        if (hsrc != nullptr) bytes += (unsigned)ncols * 8u;
+        mbar_arrive_expect_tx(&S.bar[buf], bytes);
+        tma_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], &S.bar[buf]);
+        bulk_copy_g2s(&S.ctl[buf][0], csrc, 16u * (unsigned)r.nvalid, &S.bar[buf]);
+        if (hsrc != nullptr) bulk_copy_g2s(&S.hin[buf][0], hsrc, (unsigned)ncols * 8u, &S.bar[buf]);
+      }
+    } else {
+      load_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], kFwdThreads);
+      for (int t = tid; t < r.nvalid; t += kFwdThreads) S.ctl[buf][t] = csrc[t];
+      if (hsrc != nullptr)
+        for (int mm = tid; mm < ncols; mm += kFwdThreads) S.hin[buf][mm] = hsrc[mm];
+    }
+  };
+  if (k0 < p.tiles) issue(k0, 0);
+  bool timed_out = false;
+
+  for (long long n = 0;; ++n) {
+    const long long i = k0 + n * nk;
+    if (i >= p.tiles) break;
+    const int buf = (int)(n & 1);
+    if (i + nk < p.tiles) issue(i + nk, buf ^ 1);
+    const TileRef r = tile_ref(i, B, T, C);
+    if (p.use_tma) {
+      if (!mbar_wait(&S.bar[buf], (unsigned)((n >> 1) & 1), p.max_spin << 4)) timed_out = true;
+    } else {
+      __syncthreads();
+    }
+    const TIO(*xt)[2][kFwdModes] = S.x[buf];
+    const float4* ctl = S.ctl[buf];
+    float2 h0 = make_float2(0.0f, 0.0f), h1 = h0;
+    if (r.c > 0) {
+      if (act0) h0 = S.hin[buf][2 * tid];
+      if (act1) h1 = S.hin[buf][2 * tid + 1];
+    } else if (p.h0_r != nullptr) {
+      if (act0) h0 = make_float2(p.h0_r[r.b * M + m0], p.h0_i[r.b * M + m0]);
+      if (act1) h1 = make_float2(p.h0_r[r.b * M + m0 + 1], p.h0_i[r.b * M + m0 + 1]);
+    }
+    TIO* yrow = static_cast<TIO*>(p.y) + (r.b * T + r.t0) * W;
+    auto body = [&](auto full_tag) {
+      constexpr bool kFull = decltype(full_tag)::value;
+      constexpr int kU = kFull ? 4 : 1;
+#pragma unroll kU
+      for (int t = 0; t < C; ++t) {
+        if (kFull || t < r.nvalid) {
+          const float4 k4 = ctl[t];
+          const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
+          const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
+          const TokenCoef c0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
+          const TokenCoef c1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
+          h0 = cfma(c0.a, h0, make_float2(c0.gain * tanh_t<kFast>(xr.x), c0.gain * tanh_t<kFast>(xi.x)));
+          h1 = cfma(c1.a, h1, make_float2(c1.gain * tanh_t<kFast>(xr.y), c1.gain * tanh_t<kFast>(xi.y)));
+          store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, h0, h1);
         }
       }
     };
-    if (nvalid == C) tile_body(std::true_type{});
-    else tile_body(std::false_type{});
-    __syncthreads();  // the buffer and the shared arrays are free for the next tile
+    if (r.nvalid == C) body(std::true_type{});
+    else body(std::false_type{});
+    __syncthreads();  // the buffer is free for the tile after next
   }
-  if (timed_out && tid == 0) atomicOr(&p.ls->status, kStatusTimeout);
-  cluster.sync();  // no CTA leaves while a peer may still read its shared memory
-  finish_launch(p.ls);
+  if (timed_out) atomicOr(&p.ls->status, kStatusTimeout);
 }
-

@@ -32,7 +32,8 @@ class _SparcMixerFunction(torch.autograd.Function):
     """Autograd op around sparc_mixer_forward / sparc_mixer_backward.
 
     Outputs y [B, T, W] (x.dtype) and the final state (last_r, last_i) [B, M] float32; both
-    are differentiable. Saved for backward: x, the parameters and the per-chunk carries."""
+    are differentiable. Saved for backward: x, y, the parameters, the per-chunk carries and the
+    per-token controls."""
 
     @staticmethod
     def forward(ctx, x, nu_log, theta_log, phase_direction, radial_direction, write_log_gain,
@@ -51,6 +52,7 @@ class _SparcMixerFunction(torch.autograd.Function):
         y = torch.empty_like(x)
         chunks = L.sparc_mixer_carry_chunks(T, dt)
         carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
+        controls = torch.empty((B, T, 4), dtype=torch.float32, device=dev)
         last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
         last_i = torch.empty((B, M), dtype=torch.float32, device=dev)
         nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
@@ -60,12 +62,12 @@ class _SparcMixerFunction(torch.autograd.Function):
         a = _lib.MixerFwdArgs(
             x.data_ptr(), y.data_ptr(), *[p.data_ptr() for p in params],
             _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
-            last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(),
+            last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(),
             ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin, _lib.deterministic(),
             1 if inject_tile is not None else 0, inject_tile if inject_tile is not None else 0)
         _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_forward")
-        ctx.save_for_backward(x, *params, carry, *(h0 if h0 else (None, None)))
+        ctx.save_for_backward(x, y, *params, carry, controls, *(h0 if h0 else (None, None)))
         ctx.has_h0 = h0 is not None
         ctx.max_spin = max_spin
         ctx.set_materialize_grads(False)
@@ -74,7 +76,7 @@ class _SparcMixerFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy, dlast_r, dlast_i):
         L = _lib.lib()
-        x, nu_log, theta_log, pd, rd, wlg, wpr, wrr, carry, h0_r, h0_i = ctx.saved_tensors
+        x, y, nu_log, theta_log, pd, rd, wlg, wpr, wrr, carry, controls, h0_r, h0_i = ctx.saved_tensors
         B, T, W = x.shape
         M = W // 2
         dev = x.device
@@ -96,13 +98,13 @@ class _SparcMixerFunction(torch.autograd.Function):
         nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
         ws = _lib.WORKSPACES.get(dev, nbytes)
         a = _lib.MixerBwdArgs(
-            x.data_ptr(), dy.data_ptr(), dx.data_ptr(),
+            x.data_ptr(), y.data_ptr(), dy.data_ptr(), dx.data_ptr(),
             nu_log.data_ptr(), theta_log.data_ptr(), pd.data_ptr(), rd.data_ptr(),
             wlg.data_ptr(), wpr.data_ptr(), wrr.data_ptr(),
             _lib.ptr(h0_r), _lib.ptr(h0_i),
             _lib.ptr(gl[0] if gl else None), _lib.ptr(gl[1] if gl else None),
             _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
-            carry.data_ptr(),
+            carry.data_ptr(), controls.data_ptr(),
             *[g[n].data_ptr() for n in _PARAMS],
             ws.data_ptr(), ws.numel(), B, T, W, dt, ctx.max_spin, _lib.deterministic(), 0, 0)
         _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),

@@ -243,8 +243,9 @@ def test_backward_is_deterministic(deterministic):
 
 
 def test_lookback_timeout_sets_status():
-    """A tile that never publishes makes its successor's bounded wait run out: the kernel
-    records the timeout in the workspace status word and the launch still completes."""
+    """A carry-scan segment that never publishes makes its successor's bounded wait run out:
+    the kernel records the timeout in the workspace status word and the launch still
+    completes. (2048 tokens = 128 chunks = 8 segments per row; ticket 5 is row 1, segment 2.)"""
     import sparc_b200
     from sparc_b200 import _lib
     from sparc_b200.mixer import sparc_mixer
@@ -252,7 +253,7 @@ def test_lookback_timeout_sets_status():
     sparc_b200.check_status()  # clean slate
     params = _random_params(64, 4)
     m = _module(params, 64)
-    x = torch.randn(2, 256, 64, device="cuda")
+    x = torch.randn(2, 2048, 64, device="cuda")
     with torch.no_grad():
         y, _ = sparc_mixer(x, m._params(), max_spin=2000, inject_unpublished_tile=5)
     torch.cuda.synchronize()
