@@ -232,6 +232,17 @@ size_t sparc_real_workspace_bytes(long long batch, long long length, long long c
 int sparc_real_scan_forward(const SparcRealFwdArgs* args, void* stream);
 int sparc_real_scan_backward(const SparcRealBwdArgs* args, void* stream);
 
+/* Diagnostics: per-kernel device time. While enabled, every kernel launch of this library is
+ * bracketed by CUDA events on its stream (launches inside a stream capture are not timed).
+ * sparc_timing_read waits for the recorded launches, writes per-kernel totals (milliseconds) and
+ * launch counts for up to n kernel kinds (either pointer may be NULL), resets them, and returns
+ * the number of kernel kinds, SPARC_TIMING_KERNELS; sparc_timing_kernel_name names kind `id`.
+ * sparc_timing_enable returns the previous setting. */
+#define SPARC_TIMING_KERNELS 10
+int sparc_timing_enable(int on);
+const char* sparc_timing_kernel_name(int id);
+int sparc_timing_read(double* ms, long long* launches, int n);
+
 /* Status word of a workspace (SPARC_STATUS_* bits). Reads synchronise `stream`. */
 int sparc_read_status(const void* workspace, unsigned* status, void* stream);
 int sparc_clear_status(void* workspace, void* stream);

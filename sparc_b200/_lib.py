@@ -13,7 +13,8 @@ import threading
 import torch
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "libsparc_b200.so")
+# SPARC_B200_LIBRARY selects another build of the library (for example to compare two builds)
+LIB_PATH = os.environ.get("SPARC_B200_LIBRARY") or os.path.join(_PKG, "libsparc_b200.so")
 
 OK = 0
 ERR_NAMES = {-1: "bad argument", -2: "bad shape", -3: "bad dtype", -4: "workspace", -5: "launch"}
@@ -101,6 +102,10 @@ SIGNATURES = {
     "sparc_real_scan_backward": (ctypes.c_int, [ctypes.POINTER(RealBwdArgs), _vp]),
     "sparc_read_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint), _vp]),
     "sparc_clear_status": (ctypes.c_int, [_vp, _vp]),
+    "sparc_timing_enable": (ctypes.c_int, [ctypes.c_int]),
+    "sparc_timing_kernel_name": (ctypes.c_char_p, [ctypes.c_int]),
+    "sparc_timing_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong),
+                                         ctypes.c_int]),
 }
 
 _lib = None
@@ -198,3 +203,16 @@ def read_status(ws: torch.Tensor) -> int:
 
 def clear_status(ws: torch.Tensor):
     check(lib().sparc_clear_status(ws.data_ptr(), stream_handle(ws.device)), "sparc_clear_status")
+
+
+def kernel_times(reset_only: bool = False):
+    """Per-kernel device time recorded since the last call while timing was enabled
+    (sparc_timing_enable): {kernel name: (total ms, launches)} for kernels that ran."""
+    L = lib()
+    n = 16
+    ms = (ctypes.c_double * n)()
+    cnt = (ctypes.c_longlong * n)()
+    k = L.sparc_timing_read(ms, cnt, n)
+    if reset_only:
+        return {}
+    return {L.sparc_timing_kernel_name(i).decode(): (ms[i], cnt[i]) for i in range(k) if cnt[i] > 0}

@@ -15,6 +15,7 @@
 //   continues with a zero carry, so the launch still terminates.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -70,6 +71,13 @@ __device__ __forceinline__ float tanh_hw(float x) {
   float y;
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// sin / cos by the hardware approximations (sin.approx / cos.approx, absolute error about 1e-6
+// for the arguments used here): the bfloat16 path's transitions.
+__device__ __forceinline__ void sincos_hw(float x, float* s, float* c) {
+  asm("sin.approx.ftz.f32 %0, %1;" : "=f"(*s) : "f"(x));
+  asm("cos.approx.ftz.f32 %0, %1;" : "=f"(*c) : "f"(x));
 }
 
 // tanh accurate to a few float32 ulp: Maclaurin series below 1/2, exponential form above.
@@ -246,6 +254,18 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, unsign
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// TMA tile load of a 3-D box described by a tensor map (no multicast) into this CTA's shared
+// memory, completing on an mbarrier. The map must live in kernel-parameter space
+// (__grid_constant__); c0 is the innermost coordinate (its byte offset must be 16-aligned).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<unsigned long long>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
       : "memory");
 }
 

@@ -6,6 +6,7 @@
 // (a few KB per row), so the accurate libm functions are used throughout.
 #include "common.cuh"
 #include "sparc_b200.h"
+#include "timing.cuh"
 
 namespace sparc {
 
@@ -110,6 +111,7 @@ extern "C" int sparc_decode_step(const SparcDecodeArgs* a, void* stream) {
                  a->write_log_gain, a->write_phase_response, a->write_radial_response,
                  a->width, a->width / 2};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TimedLaunch tl(kTimeDecode, s);
   if (a->dtype == SPARC_DTYPE_BF16) {
     decode_kernel<__nv_bfloat16><<<(unsigned)a->batch, kDecodeThreads, 0, s>>>(p);
   } else if (a->dtype == SPARC_DTYPE_F32) {

@@ -18,6 +18,7 @@
 //   backward  backward/scan.py:382-644 (reverse chunk kernels), backward/control.py:11-89
 //             (write backward), autograd of make_controls for the controller gradient.
 #include <cooperative_groups.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <type_traits>
@@ -26,10 +27,18 @@
 
 #include "common.cuh"
 #include "sparc_b200.h"
+#include "timing.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace sparc {
+
+// Unrolling of the token loops of full chunks (0 = the whole chunk).
+#ifndef SPARC_TOKEN_UNROLL
+#define SPARC_TOKEN_UNROLL 4
+#endif
+template <int C>
+__host__ __device__ constexpr int token_unroll() { return SPARC_TOKEN_UNROLL == 0 ? C : SPARC_TOKEN_UNROLL; }
 
 // Tokens per chunk (the granularity of the saved carries): 16 for bfloat16, 8 for float32
 // (whose shared-memory tiles are twice as large per token).
@@ -82,21 +91,39 @@ struct TokenCoef {  // per-(token, mode) quantities shared by the forward and th
   float num, gate, gain;
 };
 
+// kFast (bfloat16 activations): the rotation e^{i phi} comes from the hardware sin / cos of the
+// whole angle phi = theta + (1 - rho) delta, -expm1 from a shorter series, and the gate from the
+// hardware tanh (2 sigma(q) = 1 + tanh(q / 2)). Otherwise (float32) every factor is accurate to
+// a few ulp: series sin / cos of (1 - rho) delta rotate the precomputed e^{i theta}.
+template <bool kFast>
+__device__ __forceinline__ float2 transition_of(const ModeConst& mc, float rho, float delta) {
+  float s, c;
+  if constexpr (kFast) {
+    sincos_hw(fmaf(-rho, delta, delta) + mc.theta, &s, &c);
+    return make_float2(rho * c, rho * s);
+  } else {
+    sincos_halfpi(fmaf(-rho, delta, delta), &s, &c);  // (1 - rho) * delta, |.| <= pi/2
+    const float rct = rho * mc.ct, rst = rho * mc.st;
+    return make_float2(fmaf(rct, c, -rst * s), fmaf(rst, c, rct * s));
+  }
+}
+
 template <bool kFast>
 __device__ __forceinline__ TokenCoef token_coef(const ModeConst& mc, float E, float delta,
                                                 float tau0, float tau1) {
   TokenCoef k;
   k.z = mc.nu * E;
   k.rho = ex2_approx(-mc.nl2e * E);
-  float s, c;
-  sincos_halfpi(fmaf(-k.rho, delta, delta), &s, &c);  // (1 - rho) * delta, |.| <= pi/2
-  const float rct = k.rho * mc.ct, rst = k.rho * mc.st;
-  k.a = make_float2(fmaf(rct, c, -rst * s), fmaf(rst, c, rct * s));
-  k.num = one_minus_exp_neg(2.0f * k.z, k.rho * k.rho);
+  k.a = transition_of<kFast>(mc, k.rho, delta);
   const float q = fmaf(tau0, mc.wpr, tau1 * mc.wrr);
   if constexpr (kFast) {
+    // -expm1(-2z): u - u^2/2 + u^3/6 - u^4/24 below 1/4 (truncation below 1e-4 relative)
+    const float u = 2.0f * k.z;
+    const float ser = u * fmaf(fmaf(fmaf(-4.1666666666666667e-2f, u, 1.6666666666666667e-1f), u, -0.5f), u, 1.0f);
+    k.num = u < 0.25f ? ser : fmaf(-k.rho, k.rho, 1.0f);
     k.gate = 1.0f + tanh_hw(0.5f * q);
   } else {
+    k.num = one_minus_exp_neg(2.0f * k.z, k.rho * k.rho);
     k.gate = 2.0f * rcp_approx(1.0f + ex2_approx(-kLog2e * q));
   }
   k.gain = mc.gconst * sqrt_approx(k.num) * k.gate;
@@ -104,12 +131,9 @@ __device__ __forceinline__ TokenCoef token_coef(const ModeConst& mc, float E, fl
 }
 
 // Transition a = rho e^{i(theta + (1-rho) delta)} alone (the reverse local pass needs no write).
+template <bool kFast>
 __device__ __forceinline__ float2 token_transition(const ModeConst& mc, float E, float delta) {
-  const float rho = ex2_approx(-mc.nl2e * E);
-  float s, c;
-  sincos_halfpi(fmaf(-rho, delta, delta), &s, &c);
-  const float rct = rho * mc.ct, rst = rho * mc.st;
-  return make_float2(fmaf(rct, c, -rst * s), fmaf(rst, c, rct * s));
+  return transition_of<kFast>(mc, ex2_approx(-mc.nl2e * E), delta);
 }
 
 // Warp transpose-reduce of N values per lane (N a power of two, N <= 32). Afterwards lane l
@@ -331,10 +355,12 @@ __global__ void __launch_bounds__(kScanThreads, 2) mixer_carry_scan_kernel(const
     const unsigned pred = s_pred;
     __syncthreads();  // s_ticket and s_pred are rewritten by the next iteration
     if (ticket >= p.tiles) break;
-    const int seg = (int)(ticket / rows);
-    const long long rg = ticket - (long long)seg * rows;
-    const long long b = rg / p.G;
-    const int g = (int)(rg - b * p.G);
+    // scan tickets stay below 2^31: 32-bit division
+    const unsigned uticket = (unsigned)ticket, urows = (unsigned)rows;
+    const int seg = (int)(uticket / urows);
+    const unsigned rg = uticket - (unsigned)seg * urows;
+    const long long b = rg / (unsigned)p.G;
+    const int g = (int)(rg - (unsigned)b * (unsigned)p.G);
     const int m = g * kScanThreads + tid;
     const bool act = m < p.M;
     const int j0 = seg * kScanSeg;
@@ -537,7 +563,7 @@ struct Kernels {
     return vec ? (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, true>
                : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false>;
   }
-  static const void* rsum() { return (const void*)mixer_bwd_summary_kernel<TIO, C>; }
+  static const void* rsum() { return (const void*)mixer_bwd_summary_kernel<TIO, C, kFast>; }
   static const void* grad() { return (const void*)mixer_bwd_grad_kernel<TIO, C, kFast>; }
   static size_t sum_smem() { return sizeof(SumSmem<TIO, C>); }
   static size_t rep_smem() { return sizeof(RepSmem<TIO, C>); }
@@ -573,7 +599,7 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   pl->Mp = pl->G * kFwdModes;
   pl->vec = (M % 2) == 0;
   const size_t s = dtype == SPARC_DTYPE_BF16 ? 2 : 4;
-  pl->tma = ((size_t)W * s) % 16 == 0 && ((size_t)M * s) % 16 == 0;
+  pl->tma = ((size_t)W * s) % 16 == 0 && ((size_t)M * s) % 16 == 0 && B * T < (1LL << 31);
   pl->nseg = (pl->chunks + kScanSeg - 1) / kScanSeg;
   pl->scan_tiles = (long long)pl->nseg * B * pl->G;
 
@@ -685,6 +711,40 @@ static cudaError_t launch_plain(const void* kernel, dim3 grid, int NT, size_t dy
 
 static bool aligned16(const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    } else {
+      cudaGetLastError();
+    }
+  });
+  return fn;
+}
+
+// Activations [rows, W] seen as [rows][re|im half][M]: dims {M, 2, rows}, byte strides
+// {M*s, W*s}; one box {256 modes, 2 halves, C rows} is a tile's shared-memory [C][2][256] array.
+static bool act_tensor_map(CUtensorMap* map, const void* base, int dtype, long long rows, int M, int W, int C) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr || base == nullptr) return false;
+  const cuuint64_t s = dtype == SPARC_DTYPE_BF16 ? 2 : 4;
+  const cuuint64_t dims[3] = {(cuuint64_t)M, 2, (cuuint64_t)rows};
+  const cuuint64_t strides[2] = {(cuuint64_t)M * s, (cuuint64_t)W * s};
+  const cuuint32_t box[3] = {(cuuint32_t)kFwdModes, 2, (cuuint32_t)C};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult r = enc(map, dtype == SPARC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                         3, const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static ScanParams scan_params(const Plan& pl, const WsLayout& L, char* ws, long long B, int M, int reverse,
                               const float* init_r, const float* init_i, float* final_r, float* final_i,
                               float2* out, unsigned max_spin, int deterministic, int inject_enable,
@@ -748,17 +808,26 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
   p.chunks = pl.chunks;
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
-  p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->controls) && aligned16(a->carry) ? 1 : 0;
+  p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->controls) && aligned16(a->carry) &&
+                      act_tensor_map(&p.map_x, a->x, a->dtype, p.B * p.T, p.M, p.W, pl.C) ? 1 : 0;
   const bool bf = a->dtype == SPARC_DTYPE_BF16;
   const void* ksum = bf ? Kernels<__nv_bfloat16>::sum() : Kernels<float>::sum();
   const void* krep = bf ? Kernels<__nv_bfloat16>::rep(pl.vec) : Kernels<float>::rep(pl.vec);
-  int rc = launch_error(launch_cluster(ksum, pl.G, kFwdThreads, pl.sum_clusters, pl.sum_smem, s, p));
+  int rc;
+  {
+    TimedLaunch tl(kTimeFwdSummary, s);
+    rc = launch_error(launch_cluster(ksum, pl.G, kFwdThreads, pl.sum_clusters, pl.sum_smem, s, p));
+  }
   if (rc != SPARC_OK) return rc;
   const ScanParams sp = scan_params(pl, L, ws, p.B, p.M, 0, a->h0_r, a->h0_i, a->last_r, a->last_i,
                                     reinterpret_cast<float2*>(a->carry), a->max_spin, a->deterministic,
                                     a->inject_enable, a->inject_tile);
-  rc = launch_error(launch_plain((const void*)mixer_carry_scan_kernel, dim3(pl.scan_ctas), kScanThreads, 0, s, sp));
+  {
+    TimedLaunch tl(kTimeFwdScan, s);
+    rc = launch_error(launch_plain((const void*)mixer_carry_scan_kernel, dim3(pl.scan_ctas), kScanThreads, 0, s, sp));
+  }
   if (rc != SPARC_OK) return rc;
+  TimedLaunch tl(kTimeFwdReplay, s);
   return launch_error(launch_plain(krep, dim3(pl.G, pl.rep_rows), kFwdThreads, pl.rep_smem, s, p));
 }
 
@@ -835,20 +904,32 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.chunks = pl.chunks;
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
+  const long long rows = p.B * p.T;
   p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->y) && aligned16(a->dy) && aligned16(a->controls) &&
-                      aligned16(a->carry) ? 1 : 0;
+                      aligned16(a->carry) && act_tensor_map(&p.map_x, a->x, a->dtype, rows, p.M, p.W, pl.C) &&
+                      act_tensor_map(&p.map_y, a->y, a->dtype, rows, p.M, p.W, pl.C) &&
+                      act_tensor_map(&p.map_dy, a->dy, a->dtype, rows, p.M, p.W, pl.C) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf = a->dtype == SPARC_DTYPE_BF16;
   const void* krsum = bf ? Kernels<__nv_bfloat16>::rsum() : Kernels<float>::rsum();
   const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad() : Kernels<float>::grad();
-  rc = launch_error(launch_plain(krsum, dim3(pl.G, pl.rsum_rows), kBwdThreads, pl.rsum_smem, s, p));
+  {
+    TimedLaunch tl(kTimeBwdSummary, s);
+    rc = launch_error(launch_plain(krsum, dim3(pl.G, pl.rsum_rows), kBwdThreads, pl.rsum_smem, s, p));
+  }
   if (rc != SPARC_OK) return rc;
   const ScanParams sp = scan_params(pl, L, ws, p.B, p.M, 1, a->grad_last_r, a->grad_last_i, a->grad_h0_r,
                                     a->grad_h0_i, reinterpret_cast<float2*>(ws + L.kout), a->max_spin,
                                     a->deterministic, a->inject_enable, a->inject_tile);
-  rc = launch_error(launch_plain((const void*)mixer_carry_scan_kernel, dim3(pl.scan_ctas), kScanThreads, 0, s, sp));
+  {
+    TimedLaunch tl(kTimeBwdScan, s);
+    rc = launch_error(launch_plain((const void*)mixer_carry_scan_kernel, dim3(pl.scan_ctas), kScanThreads, 0, s, sp));
+  }
   if (rc != SPARC_OK) return rc;
-  rc = launch_error(launch_cluster(kgrad, pl.G, kBwdThreads, pl.grad_clusters, pl.grad_smem, s, p));
+  {
+    TimedLaunch tl(kTimeBwdGrad, s);
+    rc = launch_error(launch_cluster(kgrad, pl.G, kBwdThreads, pl.grad_clusters, pl.grad_smem, s, p));
+  }
   if (rc != SPARC_OK) return rc;
   ReduceParams r;
   r.part = p.part;
@@ -865,6 +946,7 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   r.g_energy = a->grad_energy_response;
   r.g_phase_dir = a->grad_phase_direction;
   r.g_radial_dir = a->grad_radial_direction;
+  TimedLaunch tl(kTimeBwdReduce, s);
   return launch_error(launch_ex((const void*)mixer_reduce_kernel, dim3((pl.Mp + 31) / 32, kPartModes + 1),
                                dim3(32, kReduceWarps), 0, 0, s, r));
 }

@@ -56,6 +56,9 @@ struct GradSmem {
 };
 
 struct BwdParams {
+  CUtensorMap map_x;     // x, y, dy as [B*T rows][re|im][M], box {256, 2, C} (when use_tma)
+  CUtensorMap map_y;
+  CUtensorMap map_dy;
   const void* x;
   const void* y;
   const void* dy;
@@ -79,8 +82,8 @@ struct BwdParams {
 };
 
 // ------------------------------------------------------------------------------ reverse summary
-template <typename TIO, int C>
-__global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const BwdParams p) {
+template <typename TIO, int C, bool kFast>
+__global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __grid_constant__ BwdParams p) {
   const int g = blockIdx.x;
   const int tid = threadIdx.x;
   const int M = p.M, W = p.W;
@@ -116,9 +119,10 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const Bw
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&S.bar[buf], 2u * act_bytes<TIO>(M, mbase, kBwdModes, r.nvalid) + 16u * (unsigned)r.nvalid);
-        tma_act_rows<TIO, kBwdModes>(dsrc, W, M, mbase, r.nvalid, S.dy[buf], &S.bar[buf]);
-        tma_act_rows<TIO, kBwdModes>(ysrc, W, M, mbase, r.nvalid, S.y[buf], &S.bar[buf]);
+        mbar_arrive_expect_tx(&S.bar[buf], 2u * act_box_bytes<TIO, C, kBwdModes>() + 16u * (unsigned)r.nvalid);
+        const int row = (int)(r.b * T + r.t0);
+        tma_load_3d(&S.dy[buf][0][0][0], &p.map_dy, mbase, 0, row, &S.bar[buf]);
+        tma_load_3d(&S.y[buf][0][0][0], &p.map_y, mbase, 0, row, &S.bar[buf]);
         bulk_copy_g2s(&S.ctl[buf][0], csrc, 16u * (unsigned)r.nvalid, &S.bar[buf]);
       }
     } else {
@@ -146,7 +150,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const Bw
     const float4* ctl = S.ctl[buf];
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
-      constexpr int kU = kFull ? 4 : 1;
+      constexpr int kU = kFull ? token_unroll<C>() : 1;
       float2 q = make_float2(0.0f, 0.0f);
       float2 P = make_float2(1.0f, 0.0f);
 #pragma unroll kU
@@ -159,7 +163,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const Bw
           const float yi = to_float(yt[t][1][tid]);
           q.x += yr > 0.0f ? gr : 0.0f;
           q.y += yi > 0.0f ? gi : 0.0f;
-          const float2 a = token_transition(mc, k4.x, k4.y);
+          const float2 a = token_transition<kFast>(mc, k4.x, k4.y);
           q = make_float2(fmaf(a.x, q.x, a.y * q.y), fmaf(a.x, q.y, -a.y * q.x));
           P = cmul(a, P);
         }
@@ -205,7 +209,7 @@ __device__ __forceinline__ float2 grad_step(const ModeConst& mc, const float4 k4
 }
 
 template <typename TIO, int C, bool kFast>
-__global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const BwdParams p) {
+__global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __grid_constant__ BwdParams p) {
   static_assert(C % kGroup == 0, "the reverse walk runs in groups of kGroup tokens");
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
@@ -260,12 +264,13 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const BwdPa
       if (p.use_tma) {
         if (tid == 0) {
           fence_proxy_async_smem();
-          unsigned bytes = 2u * act_bytes<TIO>(M, mbase, kBwdModes, r.nvalid) + 16u * (unsigned)r.nvalid;
+          unsigned bytes = 2u * act_box_bytes<TIO, C, kBwdModes>() + 16u * (unsigned)r.nvalid;
           if (hs != nullptr) bytes += (unsigned)ncols * 8u;
           if (ks != nullptr) bytes += (unsigned)ncols * 8u;
           mbar_arrive_expect_tx(&S.bar, bytes);
-          tma_act_rows<TIO, kBwdModes>(xs, W, M, mbase, r.nvalid, S.x, &S.bar);
-          tma_act_rows<TIO, kBwdModes>(ds, W, M, mbase, r.nvalid, S.dy, &S.bar);
+          const int row = (int)(b * T + r.t0);
+          tma_load_3d(&S.x[0][0][0], &p.map_x, mbase, 0, row, &S.bar);
+          tma_load_3d(&S.dy[0][0][0], &p.map_dy, mbase, 0, row, &S.bar);
           bulk_copy_g2s(&S.ctl[0], cs, 16u * (unsigned)r.nvalid, &S.bar);
           if (hs != nullptr) bulk_copy_g2s(&S.hin[0], hs, (unsigned)ncols * 8u, &S.bar);
           if (ks != nullptr) bulk_copy_g2s(&S.kin[0], ks, (unsigned)ncols * 8u, &S.bar);
@@ -287,7 +292,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const BwdPa
     // the tile body, instantiated branch-free for full chunks and with guards for the ragged last chunk
     auto tile_body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
-      constexpr int kU = kFull ? 4 : 1;  // partial unrolling keeps the kernel's code in the i-cache
+      constexpr int kU = kFull ? token_unroll<C>() : 1;  // partial unrolling keeps the kernel's code in the i-cache
       // pass 0: replay the states from the forward's carry; relu masks on dy
       float2 hin = make_float2(0.0f, 0.0f);
       if (c > 0) {

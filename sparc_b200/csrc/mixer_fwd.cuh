@@ -41,6 +41,7 @@ struct RepSmem {
 };
 
 struct FwdParams {
+  CUtensorMap map_x;    // x as [B*T rows][re|im][M], box {256, 2, C} (when use_tma)
   const void* x;
   void* y;
   MixerParamPtrs pp;
@@ -93,7 +94,8 @@ __device__ __forceinline__ void store_y_pair(TIO* row, int M, int m, bool a0, bo
   }
 }
 
-// Tile geometry shared by all tile kernels: tile i covers row b = i % B, chunk c = i / B.
+// Tile geometry shared by all tile kernels: tile i covers row b = i % B, chunk c = i / B (tile
+// counts stay below 2^31, so the division is 32-bit).
 struct TileRef {
   long long b;
   int c;
@@ -102,26 +104,13 @@ struct TileRef {
 };
 __device__ __forceinline__ TileRef tile_ref(long long i, long long B, long long T, int C) {
   TileRef r;
-  r.b = i % B;
-  r.c = (int)(i / B);
+  const unsigned ui = (unsigned)i, ub = (unsigned)B;
+  const unsigned c = ui / ub;
+  r.c = (int)c;
+  r.b = (long long)(ui - c * ub);
   r.t0 = (long long)r.c * C;
   r.nvalid = (int)(T - r.t0 < C ? T - r.t0 : C);
   return r;
-}
-
-// TMA: bulk copies of the CTA's columns of `nvalid` activation rows (real half, imaginary
-// half) into dst[t][re|im][mode], completing on `bar`. Returns the bytes in flight.
-template <typename TIO, int NM>
-__device__ __forceinline__ unsigned tma_act_rows(const TIO* src, int W, int M, int mbase, int nvalid,
-                                                 TIO (*dst)[2][NM], unsigned long long* bar) {
-  const int ncols = min(NM, M - mbase);
-  const TIO* s = src + mbase;
-  const unsigned bytes = (unsigned)(ncols * sizeof(TIO));
-  for (int t = 0; t < nvalid; ++t) {
-    bulk_copy_g2s(&dst[t][0][0], s + (long long)t * W, bytes, bar);
-    bulk_copy_g2s(&dst[t][1][0], s + (long long)t * W + M, bytes, bar);
-  }
-  return bytes * 2u * (unsigned)nvalid;
 }
 
 // The same rows by plain loads spread over the CTA (shapes that are not 16-byte aligned).
@@ -136,14 +125,16 @@ __device__ __forceinline__ void load_act_rows(const TIO* src, int W, int M, int 
   }
 }
 
-template <typename TIO>
-__device__ __forceinline__ unsigned act_bytes(int M, int mbase, int NM, int nvalid) {
-  return (unsigned)(min(NM, M - mbase) * sizeof(TIO)) * 2u * (unsigned)nvalid;
+// Bytes of one activation box (the tensor-map copy always moves the whole box; columns past M
+// and rows past the tensor arrive as zeros).
+template <typename TIO, int C, int NM>
+__host__ __device__ constexpr unsigned act_box_bytes() {
+  return (unsigned)(NM * 2 * C * sizeof(TIO));
 }
 
 // ------------------------------------------------------------------------------ summary
 template <typename TIO, int C, bool kFast>
-__global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const FwdParams p) {
+__global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __grid_constant__ FwdParams p) {
   constexpr int NW = kFwdThreads / 32;
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
@@ -182,8 +173,8 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const Fw
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&S.bar[buf], act_bytes<TIO>(M, mbase, kFwdModes, r.nvalid));
-        tma_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], &S.bar[buf]);
+        mbar_arrive_expect_tx(&S.bar[buf], act_box_bytes<TIO, C, kFwdModes>());
+        tma_load_3d(&S.x[buf][0][0][0], &p.map_x, mbase, 0, (int)(r.b * T + r.t0), &S.bar[buf]);
       }
     } else {
       load_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], kFwdThreads);
@@ -259,7 +250,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const Fw
     // the chunk's aggregate map per mode
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
-      constexpr int kU = kFull ? 4 : 1;  // partial unrolling keeps the kernel's code in the i-cache
+      constexpr int kU = kFull ? token_unroll<C>() : 1;  // partial unrolling keeps the kernel's code in the i-cache
       float2 P0 = make_float2(1.0f, 0.0f), Q0 = make_float2(0.0f, 0.0f);
       float2 P1 = P0, Q1 = Q0;
 #pragma unroll kU
@@ -290,7 +281,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const Fw
 
 // ------------------------------------------------------------------------------ replay
 template <typename TIO, int C, bool kFast, bool kVec>
-__global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const FwdParams p) {
+__global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __grid_constant__ FwdParams p) {
   const int g = blockIdx.x;
   const int tid = threadIdx.x;
   const int M = p.M, W = p.W;
@@ -325,10 +316,10 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const Fwd
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        unsigned bytes = act_bytes<TIO>(M, mbase, kFwdModes, r.nvalid) + 16u * (unsigned)r.nvalid;
+        unsigned bytes = act_box_bytes<TIO, C, kFwdModes>() + 16u * (unsigned)r.nvalid;
         if (hsrc != nullptr) bytes += (unsigned)ncols * 8u;
         mbar_arrive_expect_tx(&S.bar[buf], bytes);
-        tma_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], &S.bar[buf]);
+        tma_load_3d(&S.x[buf][0][0][0], &p.map_x, mbase, 0, (int)(r.b * T + r.t0), &S.bar[buf]);
         bulk_copy_g2s(&S.ctl[buf][0], csrc, 16u * (unsigned)r.nvalid, &S.bar[buf]);
         if (hsrc != nullptr) bulk_copy_g2s(&S.hin[buf][0], hsrc, (unsigned)ncols * 8u, &S.bar[buf]);
       }
@@ -366,7 +357,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const Fwd
     TIO* yrow = static_cast<TIO*>(p.y) + (r.b * T + r.t0) * W;
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
-      constexpr int kU = kFull ? 4 : 1;
+      constexpr int kU = kFull ? token_unroll<C>() : 1;
 #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < r.nvalid) {

@@ -15,6 +15,7 @@
 
 #include "common.cuh"
 #include "sparc_b200.h"
+#include "timing.cuh"
 
 namespace sparc {
 
@@ -475,6 +476,7 @@ int sparc_real_scan_forward(const SparcRealFwdArgs* a, void* stream) {
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TimedLaunch tl(kTimeRealFwd, s);
   if (a->dtype == SPARC_DTYPE_F32) real_fwd_kernel<float, 1><<<pl.grid_fwd, kRealThreads, 0, s>>>(p);
   else if (pl.V == 2) real_fwd_kernel<__nv_bfloat16, 2><<<pl.grid_fwd, kRealThreads, 0, s>>>(p);
   else real_fwd_kernel<__nv_bfloat16, 1><<<pl.grid_fwd, kRealThreads, 0, s>>>(p);
@@ -510,6 +512,7 @@ int sparc_real_scan_backward(const SparcRealBwdArgs* a, void* stream) {
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TimedLaunch tl(kTimeRealBwd, s);
   if (a->dtype == SPARC_DTYPE_F32) real_bwd_kernel<float, 1><<<pl.grid_bwd, kRealThreads, 0, s>>>(p);
   else if (pl.V == 2) real_bwd_kernel<__nv_bfloat16, 2><<<pl.grid_bwd, kRealThreads, 0, s>>>(p);
   else real_bwd_kernel<__nv_bfloat16, 1><<<pl.grid_bwd, kRealThreads, 0, s>>>(p);
