@@ -68,8 +68,9 @@ extern "C" {
  * h_t = a_t h_{t-1} + b_t over M = width/2 complex modes, with a_t, b_t computed from x_t
  * and the parameters. `carry` receives the state at the end of every chunk of
  * sparc_mixer_chunk_tokens(dtype) tokens ([batch, sparc_mixer_carry_chunks(length, dtype), M] complex,
- * interleaved real/imag float32) and `controls` the per-token controls ([batch, length, 4]
- * float32: e^eta, delta, tanh p0, tanh p1); the backward needs both, and y. h0 (initial
+ * interleaved real/imag float32) and `controls` the per-token controls ([batch, length, 8]
+ * float32: e^eta, delta, tanh p0, tanh p1, each stored twice in the order e^eta, e^eta, delta,
+ * delta, tanh p0, tanh p0, tanh p1, tanh p1); the backward needs both, and y. h0 (initial
  * state) and last (final state) are optional pairs (NULL, NULL). */
 typedef struct SparcMixerFwdArgs {
   const void* x;                       /* [batch, length, width]  activations (dtype) */
@@ -86,7 +87,7 @@ typedef struct SparcMixerFwdArgs {
   float* last_r;                       /* [batch, M] or NULL */
   float* last_i;                       /* [batch, M] or NULL */
   float* carry;                        /* [batch, chunks, M, 2] */
-  float* controls;                     /* [batch, length, 4] */
+  float* controls;                     /* [batch, length, 8] */
   void* workspace;
   size_t workspace_bytes;
   long long batch;

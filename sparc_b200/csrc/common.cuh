@@ -192,6 +192,109 @@ __device__ __forceinline__ void finish_launch(LaunchState* ls) {
   }
 }
 
+// ---------------------------------------------------------------- packed float pairs
+// sm_100's f32x2 arithmetic applies one add / sub / mul / fma to both lanes of a register pair
+// in one instruction (here the lanes are the two modes a thread owns). The .rn forms round like
+// the scalar operations.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {  // a*b + c
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 bcast2(float v) { return make_float2(v, v); }
+
+// Two modes' complex numbers: re = (re0, re1), im = (im0, im1).
+struct Cx2 {
+  float2 re, im;
+};
+__device__ __forceinline__ Cx2 cx2(float2 re, float2 im) { return Cx2{re, im}; }
+__device__ __forceinline__ Cx2 cmul2(Cx2 a, Cx2 b) {
+  return Cx2{sub2(mul2(a.re, b.re), mul2(a.im, b.im)), fma2(a.re, b.im, mul2(a.im, b.re))};
+}
+__device__ __forceinline__ Cx2 cfma2(Cx2 a, Cx2 b, Cx2 c) {  // a*b + c
+  return Cx2{sub2(fma2(a.re, b.re, c.re), mul2(a.im, b.im)), fma2(a.re, b.im, fma2(a.im, b.re, c.im))};
+}
+
+// Per-lane hardware approximations on pairs.
+__device__ __forceinline__ float2 ex2_2(float2 v) { return make_float2(ex2_approx(v.x), ex2_approx(v.y)); }
+__device__ __forceinline__ float2 rcp_2(float2 v) { return make_float2(rcp_approx(v.x), rcp_approx(v.y)); }
+__device__ __forceinline__ float2 sqrt_2(float2 v) { return make_float2(sqrt_approx(v.x), sqrt_approx(v.y)); }
+__device__ __forceinline__ float2 tanh_hw2(float2 v) { return make_float2(tanh_hw(v.x), tanh_hw(v.y)); }
+
+// Packed forms of the series helpers above (same coefficients and branch points, per lane).
+__device__ __forceinline__ float2 tanh_accurate2(float2 x) {
+  const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 e = ex2_2(mul2(bcast2(2.0f * kLog2e), ax));
+  const float2 r = rcp_2(add2(e, bcast2(1.0f)));
+  const float2 big = fma2(bcast2(-2.0f), r, bcast2(1.0f));
+  const float2 x2 = mul2(x, x);
+  float2 p = bcast2(-1.4558343870513183e-3f);
+  p = fma2(p, x2, bcast2(3.5921280365724810e-3f));
+  p = fma2(p, x2, bcast2(-8.8632355299021966e-3f));
+  p = fma2(p, x2, bcast2(2.1869488536155203e-2f));
+  p = fma2(p, x2, bcast2(-5.3968253968253968e-2f));
+  p = fma2(p, x2, bcast2(1.3333333333333333e-1f));
+  p = fma2(p, x2, bcast2(-3.3333333333333333e-1f));
+  const float2 small = fma2(mul2(p, x2), x, x);
+  return make_float2(ax.x < 0.5f ? small.x : copysignf(big.x, x.x), ax.y < 0.5f ? small.y : copysignf(big.y, x.y));
+}
+template <bool kFast>
+__device__ __forceinline__ float2 tanh_t2(float2 x) {
+  if constexpr (kFast) return tanh_hw2(x);
+  else return tanh_accurate2(x);
+}
+__device__ __forceinline__ float2 one_minus_exp_neg2(float2 u, float2 w) {
+  float2 p = bcast2(-1.3888888888888889e-3f);
+  p = fma2(p, u, bcast2(8.3333333333333333e-3f));
+  p = fma2(p, u, bcast2(-4.1666666666666667e-2f));
+  p = fma2(p, u, bcast2(1.6666666666666667e-1f));
+  p = fma2(p, u, bcast2(-0.5f));
+  p = fma2(p, u, bcast2(1.0f));
+  const float2 small = mul2(p, u);
+  const float2 big = sub2(bcast2(1.0f), w);
+  return make_float2(u.x < 0.25f ? small.x : big.x, u.y < 0.25f ? small.y : big.y);
+}
+__device__ __forceinline__ void sincos_halfpi2(float2 x, float2* s, float2* c) {
+  const float2 x2 = mul2(x, x);
+  float2 ps = bcast2(1.6059043836821615e-10f);
+  ps = fma2(ps, x2, bcast2(-2.5052108385441720e-8f));
+  ps = fma2(ps, x2, bcast2(2.7557319223985893e-6f));
+  ps = fma2(ps, x2, bcast2(-1.9841269841269841e-4f));
+  ps = fma2(ps, x2, bcast2(8.3333333333333333e-3f));
+  ps = fma2(ps, x2, bcast2(-1.6666666666666667e-1f));
+  *s = fma2(mul2(ps, x2), x, x);
+  float2 pc = bcast2(2.0876756987868099e-9f);
+  pc = fma2(pc, x2, bcast2(-2.7557319223985891e-7f));
+  pc = fma2(pc, x2, bcast2(2.4801587301587302e-5f));
+  pc = fma2(pc, x2, bcast2(-1.3888888888888889e-3f));
+  pc = fma2(pc, x2, bcast2(4.1666666666666667e-2f));
+  pc = fma2(pc, x2, bcast2(-0.5f));
+  *c = fma2(pc, x2, bcast2(1.0f));
+}
+
 // Programmatic dependent launch: kernels are launched so that they may start while the previous
 // kernel on the stream drains; this waits until that kernel has completed and its memory is
 // visible (a no-op when the launch had no programmatic dependency). Nothing the previous kernel

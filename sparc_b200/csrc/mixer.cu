@@ -130,6 +130,75 @@ __device__ __forceinline__ TokenCoef token_coef(const ModeConst& mc, float E, fl
   return k;
 }
 
+// Two modes at once (the lanes are the thread's modes m and m+1): the arithmetic of token_coef
+// with the float operations packed into f32x2 instructions; the hardware approximations stay per
+// lane. The token's controls come as pairs (E, E), (delta, delta), (tau0, tau0), (tau1, tau1).
+struct ModeConst2 {
+  float2 nu, nl2e_neg, theta, ct, st, gconst, stat, wpr, wrr;
+  float2 wpr_h, wrr_l;  // wpr * 2/pi, wrr / ln 16 (the gate's chain factors in the backward)
+  float2 d0r, d0i, d1r, d1i;
+};
+__device__ __forceinline__ ModeConst2 pair_modes(const ModeConst& a, const ModeConst& b) {
+  ModeConst2 m;
+  m.nu = make_float2(a.nu, b.nu);
+  m.nl2e_neg = make_float2(-a.nl2e, -b.nl2e);
+  m.theta = make_float2(a.theta, b.theta);
+  m.ct = make_float2(a.ct, b.ct);
+  m.st = make_float2(a.st, b.st);
+  m.gconst = make_float2(a.gconst, b.gconst);
+  m.stat = make_float2(a.stat, b.stat);
+  m.wpr = make_float2(a.wpr, b.wpr);
+  m.wrr = make_float2(a.wrr, b.wrr);
+  m.wpr_h = make_float2(a.wpr * kInvHalfPi, b.wpr * kInvHalfPi);
+  m.wrr_l = make_float2(a.wrr * kInvLn16, b.wrr * kInvLn16);
+  m.d0r = make_float2(a.d0r, b.d0r);
+  m.d0i = make_float2(a.d0i, b.d0i);
+  m.d1r = make_float2(a.d1r, b.d1r);
+  m.d1i = make_float2(a.d1i, b.d1i);
+  return m;
+}
+
+struct TokenCoef2 {
+  float2 z, rho;
+  Cx2 a;
+  float2 num, gate, gain;
+};
+
+template <bool kFast>
+__device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0,
+                                                  float2 tau1) {
+  TokenCoef2 k;
+  k.z = mul2(mc.nu, E);
+  k.rho = ex2_2(mul2(mc.nl2e_neg, E));
+  if constexpr (kFast) {
+    const float2 ph = sub2(add2(delta, mc.theta), mul2(k.rho, delta));  // theta + (1 - rho) delta
+    float2 sn, cs;
+    sincos_hw(ph.x, &sn.x, &cs.x);
+    sincos_hw(ph.y, &sn.y, &cs.y);
+    k.a = Cx2{mul2(k.rho, cs), mul2(k.rho, sn)};
+  } else {
+    float2 sn, cs;
+    sincos_halfpi2(sub2(delta, mul2(k.rho, delta)), &sn, &cs);  // (1 - rho) delta, |.| <= pi/2
+    const float2 rct = mul2(k.rho, mc.ct), rst = mul2(k.rho, mc.st);
+    k.a = Cx2{sub2(mul2(rct, cs), mul2(rst, sn)), fma2(rst, cs, mul2(rct, sn))};
+  }
+  const float2 q = fma2(tau0, mc.wpr, mul2(tau1, mc.wrr));
+  const float2 u = add2(k.z, k.z);
+  if constexpr (kFast) {
+    const float2 ser = mul2(u, fma2(fma2(fma2(bcast2(-4.1666666666666667e-2f), u, bcast2(1.6666666666666667e-1f)), u,
+                                         bcast2(-0.5f)), u, bcast2(1.0f)));
+    const float2 big = sub2(bcast2(1.0f), mul2(k.rho, k.rho));
+    k.num = make_float2(u.x < 0.25f ? ser.x : big.x, u.y < 0.25f ? ser.y : big.y);
+    k.gate = add2(bcast2(1.0f), tanh_hw2(mul2(bcast2(0.5f), q)));
+  } else {
+    k.num = one_minus_exp_neg2(u, mul2(k.rho, k.rho));
+    const float2 r = rcp_2(add2(bcast2(1.0f), ex2_2(mul2(bcast2(-kLog2e), q))));
+    k.gate = add2(r, r);
+  }
+  k.gain = mul2(mul2(mc.gconst, sqrt_2(k.num)), k.gate);
+  return k;
+}
+
 // Transition a = rho e^{i(theta + (1-rho) delta)} alone (the reverse local pass needs no write).
 template <bool kFast>
 __device__ __forceinline__ float2 token_transition(const ModeConst& mc, float E, float delta) {
@@ -564,7 +633,10 @@ struct Kernels {
                : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false>;
   }
   static const void* rsum() { return (const void*)mixer_bwd_summary_kernel<TIO, C, kFast>; }
-  static const void* grad() { return (const void*)mixer_bwd_grad_kernel<TIO, C, kFast>; }
+  static const void* grad(bool vec) {
+    return vec ? (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, true>
+               : (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, false>;
+  }
   static size_t sum_smem() { return sizeof(SumSmem<TIO, C>); }
   static size_t rep_smem() { return sizeof(RepSmem<TIO, C>); }
   static size_t rsum_smem() { return sizeof(RsumSmem<TIO, C>); }
@@ -581,7 +653,7 @@ static void plan_kernels(Plan* pl, const void** k) {
   k[0] = K::sum();
   k[1] = K::rep(pl->vec);
   k[2] = K::rsum();
-  k[3] = K::grad();
+  k[3] = K::grad(pl->vec);
 }
 
 static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
@@ -627,7 +699,7 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
     key.sum = max_clusters(k[0], pl->G, kFwdThreads, pl->sum_smem);
     key.rep = max_blocks(k[1], kFwdThreads, pl->rep_smem);
     key.rsum = max_blocks(k[2], kBwdThreads, pl->rsum_smem);
-    key.grad = max_clusters(k[3], pl->G, kBwdThreads, pl->grad_smem);
+    key.grad = max_clusters(k[3], pl->G, kGradThreads, pl->grad_smem);
     key.scan = max_blocks((const void*)mixer_carry_scan_kernel, kScanThreads, 0);
     if (key.sum <= 0 || key.rep <= 0 || key.rsum <= 0 || key.grad <= 0 || key.scan <= 0) {
       set_err("occupancy query failed");
@@ -912,7 +984,7 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf = a->dtype == SPARC_DTYPE_BF16;
   const void* krsum = bf ? Kernels<__nv_bfloat16>::rsum() : Kernels<float>::rsum();
-  const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad() : Kernels<float>::grad();
+  const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad(pl.vec) : Kernels<float>::grad(pl.vec);
   {
     TimedLaunch tl(kTimeBwdSummary, s);
     rc = launch_error(launch_plain(krsum, dim3(pl.G, pl.rsum_rows), kBwdThreads, pl.rsum_smem, s, p));
@@ -928,7 +1000,7 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   if (rc != SPARC_OK) return rc;
   {
     TimedLaunch tl(kTimeBwdGrad, s);
-    rc = launch_error(launch_cluster(kgrad, pl.G, kBwdThreads, pl.grad_clusters, pl.grad_smem, s, p));
+    rc = launch_error(launch_cluster(kgrad, pl.G, kGradThreads, pl.grad_clusters, pl.grad_smem, s, p));
   }
   if (rc != SPARC_OK) return rc;
   ReduceParams r;

@@ -19,10 +19,10 @@
 //                             transpose-reduce per group of tokens during the walk, then shared
 //                             and distributed shared memory) into the controller gradients dp0,
 //                             dp1, which finish dx and the direction gradients.
-// One mode per thread, 256 threads per CTA (the tiles' shared memory then serves twice the warps
-// of a two-modes-per-thread layout). Per-mode parameter gradients accumulate in float64 per
-// cluster; mixer_reduce_kernel sums the clusters in a fixed order. The token controls come from
-// the forward (saved per token).
+// The reverse summary runs one mode per thread (256 threads per CTA); the gradient kernel two
+// adjacent modes per thread with packed f32x2 arithmetic (128 threads). Per-mode parameter
+// gradients accumulate per cluster; mixer_reduce_kernel sums the clusters in float64 in a fixed
+// order. The token controls come from the forward (saved per token, as pairs).
 
 // (included inside namespace sparc)
 
@@ -36,24 +36,10 @@ template <typename TIO, int C>
 struct RsumSmem {
   TIO dy[2][C][2][kBwdModes];
   TIO y[2][C][2][kBwdModes];
-  float4 ctl[2][C];
+  float4 ctl[2][C][2];         // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
   unsigned long long bar[2];
 };
 
-template <typename TIO, int C>
-struct GradSmem {
-  TIO x[C][2][kBwdModes];
-  TIO dy[C][2][kBwdModes];     // masked by the relu in pass 0
-  float2 h[C][kBwdModes];      // replayed states, then the write-path dx (pass B)
-  float2 hin[kBwdModes];       // state entering the chunk
-  float2 kin[kBwdModes];       // adjoint carry entering the chunk from the later chunks
-  float4 ctl[C];               // E, delta, tau0, tau1
-  float2 dp[C];                // controller gradients dp0, dp1
-  float tot[2 * C];            // cluster totals of dEta / dDelta
-  float part_grad[2][2 * C];   // dEta / dDelta CTA partials (peers read), by tile parity
-  float warp_part[kBwdWarps][2 * C];
-  unsigned long long bar;
-};
 
 struct BwdParams {
   CUtensorMap map_x;     // x, y, dy as [B*T rows][re|im][M], box {256, 2, C} (when use_tma)
@@ -68,7 +54,7 @@ struct BwdParams {
   const float* h0_i;
   const float* glast_r;
   const float* glast_i;
-  const float4* ctl;     // [B, T] forward token controls
+  const float4* ctl;     // [B, T, 2] forward token controls (pairs, as the forward saved them)
   const float2* carry;   // [B, chunks, M] forward inclusive states
   const float2* kout;    // [B, chunks, M] adjoint carry leaving each chunk (scan output)
   float4* agg;           // [B, chunks, Mp] reverse aggregates (summary output)
@@ -80,6 +66,9 @@ struct BwdParams {
   unsigned max_spin;
   int use_tma;
 };
+
+// (E, delta, tau0, tau1) of a token from its pair layout.
+__device__ __forceinline__ float4 ctl4(const float4 (&c)[2]) { return make_float4(c[0].x, c[0].z, c[1].x, c[1].z); }
 
 // ------------------------------------------------------------------------------ reverse summary
 template <typename TIO, int C, bool kFast>
@@ -115,20 +104,20 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
     const long long row0 = (r.b * T + r.t0) * W;
     const TIO* dsrc = static_cast<const TIO*>(p.dy) + row0;
     const TIO* ysrc = static_cast<const TIO*>(p.y) + row0;
-    const float4* csrc = p.ctl + r.b * T + r.t0;
+    const float4* csrc = p.ctl + 2 * (r.b * T + r.t0);
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&S.bar[buf], 2u * act_box_bytes<TIO, C, kBwdModes>() + 16u * (unsigned)r.nvalid);
+        mbar_arrive_expect_tx(&S.bar[buf], 2u * act_box_bytes<TIO, C, kBwdModes>() + 32u * (unsigned)r.nvalid);
         const int row = (int)(r.b * T + r.t0);
         tma_load_3d(&S.dy[buf][0][0][0], &p.map_dy, mbase, 0, row, &S.bar[buf]);
         tma_load_3d(&S.y[buf][0][0][0], &p.map_y, mbase, 0, row, &S.bar[buf]);
-        bulk_copy_g2s(&S.ctl[buf][0], csrc, 16u * (unsigned)r.nvalid, &S.bar[buf]);
+        bulk_copy_g2s(&S.ctl[buf][0][0], csrc, 32u * (unsigned)r.nvalid, &S.bar[buf]);
       }
     } else {
       load_act_rows<TIO, kBwdModes>(dsrc, W, M, mbase, r.nvalid, S.dy[buf], kBwdThreads);
       load_act_rows<TIO, kBwdModes>(ysrc, W, M, mbase, r.nvalid, S.y[buf], kBwdThreads);
-      for (int t = tid; t < r.nvalid; t += kBwdThreads) S.ctl[buf][t] = csrc[t];
+      for (int t = tid; t < 2 * r.nvalid; t += kBwdThreads) (&S.ctl[buf][0][0])[t] = csrc[t];
     }
   };
   if (k0 < p.tiles) issue(k0, 0);
@@ -147,7 +136,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
     }
     const TIO(*dyt)[2][kBwdModes] = S.dy[buf];
     const TIO(*yt)[2][kBwdModes] = S.y[buf];
-    const float4* ctl = S.ctl[buf];
+    const float4(*ctl)[2] = S.ctl[buf];
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr int kU = kFull ? token_unroll<C>() : 1;
@@ -156,14 +145,14 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
 #pragma unroll kU
       for (int t = C - 1; t >= 0; --t) {
         if (kFull || t < r.nvalid) {
-          const float4 k4 = ctl[t];
+          const float4 c0 = ctl[t][0];
           const float gr = to_float(dyt[t][0][tid]);
           const float gi = to_float(dyt[t][1][tid]);
           const float yr = to_float(yt[t][0][tid]);
           const float yi = to_float(yt[t][1][tid]);
           q.x += yr > 0.0f ? gr : 0.0f;
           q.y += yi > 0.0f ? gi : 0.0f;
-          const float2 a = token_transition<kFast>(mc, k4.x, k4.y);
+          const float2 a = token_transition<kFast>(mc, c0.x, c0.z);
           q = make_float2(fmaf(a.x, q.x, a.y * q.y), fmaf(a.x, q.y, -a.y * q.x));
           P = cmul(a, P);
         }
@@ -178,38 +167,64 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
 }
 
 // ------------------------------------------------------------------------------ gradients
-// Gradient contributions of one (token, mode): updates the adjoint lam in place (to conj(a)
-// lam) and returns the write-path dx of the content (real, imaginary); adds the token's dEta /
-// dDelta contributions to ve / vd and the per-mode parameter terms to fa.
+// Two adjacent modes per thread (128 threads, 256 modes per CTA): the per-mode arithmetic runs
+// in packed f32x2 lanes. The replayed states and, later, the write-path dx sit in separate
+// real / imaginary planes so that a thread's two modes load as one pair.
+constexpr int kGradThreads = 128;
+constexpr int kGradWarps = kGradThreads / 32;
+
+template <typename TIO, int C>
+struct GradSmem {
+  TIO x[C][2][kBwdModes];
+  TIO dy[C][2][kBwdModes];     // masked by the relu in pass 0
+  float hr[C][kBwdModes];      // replayed states (real plane), then the write-path dx (pass B)
+  float hi[C][kBwdModes];      // imaginary plane
+  float2 hin[kBwdModes];       // state entering the chunk, (re, im) per mode
+  float2 kin[kBwdModes];       // adjoint carry entering the chunk from the later chunks
+  float4 ctl[C][2];            // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
+  float4 dp[C];                // controller gradients per token as pairs (dp0, dp0, dp1, dp1)
+  float tot[2 * C];            // cluster totals of dEta / dDelta
+  float part_grad[2][2 * C];   // dEta / dDelta CTA partials (peers read), by tile parity
+  float warp_part[kGradWarps][2 * C];
+  unsigned long long bar;
+};
+
+__device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ void st2(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
+
+// Gradient contributions of one token for the thread's two modes: updates the adjoint lam in
+// place (to conj(a) lam) and returns the write-path dx of the content; returns the token's dEta /
+// dDelta contributions in ve / vd (per lane) and adds the per-mode parameter terms to fa.
 template <bool kFast>
-__device__ __forceinline__ float2 grad_step(const ModeConst& mc, const float4 k4, float2& lam, float2 pv,
-                                            float cx, float cy, float& ve, float& vd, float (&fa)[5]) {
-  const TokenCoef k = token_coef<kFast>(mc, k4.x, k4.y, k4.z, k4.w);
-  const float ar = k.a.x, ai = k.a.y;
-  const float gar = fmaf(lam.x, pv.x, lam.y * pv.y);
-  const float gai = fmaf(lam.y, pv.x, -lam.x * pv.y);
-  const float pg = fmaf(gai, ar, -gar * ai);
-  const float radial = k.z * fmaf(k.rho * k4.y, pg, -fmaf(gar, ar, gai * ai));
-  const float dscan = pg - k.rho * pg;
-  const float cr = tanh_t<kFast>(cx);
-  const float ci = tanh_t<kFast>(cy);
-  const float gg = k.gain * fmaf(lam.x, cr, lam.y * ci);
-  const float gq = gg * fmaf(-0.5f, k.gate, 1.0f);
-  const float dyn = k.z * k.rho * k.rho * rcp_approx(k.num);
-  ve = radial + fmaf(gg, dyn, gq * mc.wrr * kInvLn16);
-  vd = fmaf(gq * mc.wpr, kInvHalfPi, dscan);
-  fa[0] += radial + gg * (dyn - mc.stat);
-  fa[1] += pg;
-  fa[2] += gg;
-  fa[3] = fmaf(gq, k4.z, fa[3]);
-  fa[4] = fmaf(gq, k4.w, fa[4]);
-  const float2 dxc = make_float2(lam.x * k.gain * fmaf(-cr, cr, 1.0f), lam.y * k.gain * fmaf(-ci, ci, 1.0f));
-  lam = make_float2(fmaf(ar, lam.x, ai * lam.y), fmaf(ar, lam.y, -ai * lam.x));
+__device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0, float2 tau1,
+                                          Cx2& lam, Cx2 pv, float2 cx, float2 cy, float2& ve, float2& vd,
+                                          float2 (&fa)[5]) {
+  const TokenCoef2 k = token_coef2<kFast>(mc, E, delta, tau0, tau1);
+  const float2 gar = fma2(lam.re, pv.re, mul2(lam.im, pv.im));   // Re(lam conj(h_prev))
+  const float2 gai = sub2(mul2(lam.im, pv.re), mul2(lam.re, pv.im));  // Im(lam conj(h_prev))
+  const float2 pg = sub2(mul2(gai, k.a.re), mul2(gar, k.a.im));
+  const float2 radial = mul2(k.z, sub2(mul2(mul2(k.rho, delta), pg), fma2(gar, k.a.re, mul2(gai, k.a.im))));
+  const float2 dscan = sub2(pg, mul2(k.rho, pg));
+  const float2 cr = tanh_t2<kFast>(cx);
+  const float2 ci = tanh_t2<kFast>(cy);
+  const float2 gg = mul2(k.gain, fma2(lam.re, cr, mul2(lam.im, ci)));
+  const float2 gq = mul2(gg, fma2(bcast2(-0.5f), k.gate, bcast2(1.0f)));
+  const float2 dyn = mul2(mul2(k.z, mul2(k.rho, k.rho)), rcp_2(k.num));
+  ve = add2(radial, fma2(gg, dyn, mul2(gq, mc.wrr_l)));
+  vd = fma2(gq, mc.wpr_h, dscan);
+  fa[0] = add2(fa[0], fma2(gg, sub2(dyn, mc.stat), radial));
+  fa[1] = add2(fa[1], pg);
+  fa[2] = add2(fa[2], gg);
+  fa[3] = fma2(gq, tau0, fa[3]);
+  fa[4] = fma2(gq, tau1, fa[4]);
+  const Cx2 dxc = Cx2{mul2(mul2(lam.re, k.gain), sub2(bcast2(1.0f), mul2(cr, cr))),
+                      mul2(mul2(lam.im, k.gain), sub2(bcast2(1.0f), mul2(ci, ci)))};
+  lam = Cx2{fma2(k.a.re, lam.re, mul2(k.a.im, lam.im)), sub2(mul2(k.a.re, lam.im), mul2(k.a.im, lam.re))};
   return dxc;
 }
 
-template <typename TIO, int C, bool kFast>
-__global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __grid_constant__ BwdParams p) {
+template <typename TIO, int C, bool kFast, bool kVec>
+__global__ void __launch_bounds__(kGradThreads) mixer_bwd_grad_kernel(const __grid_constant__ BwdParams p) {
   static_assert(C % kGroup == 0, "the reverse walk runs in groups of kGroup tokens");
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
@@ -217,9 +232,9 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int M = p.M, W = p.W;
   const int mbase = g * kBwdModes;
-  const int m = mbase + tid;
+  const int m0 = mbase + 2 * tid;  // this thread's modes: m0, m0 + 1
   const int Mp = p.Mp;
-  const bool act = m < M;
+  const bool act0 = m0 < M, act1 = m0 + 1 < M;
   const long long B = p.B, T = p.T;
   const int chunks = p.chunks;
   const int ncols = min(kBwdModes, M - mbase);
@@ -228,11 +243,11 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
   extern __shared__ __align__(128) unsigned char smem_raw[];
   GradSmem<TIO, C>& S = *reinterpret_cast<GradSmem<TIO, C>*>(smem_raw);
 
-  const ModeConst mc = load_mode(p.pp, m, M, act);
+  const ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
 
   {
     unsigned* z = reinterpret_cast<unsigned*>(&S.x[0][0][0]);
-    for (int i = tid; i < (int)((sizeof(S.x) + sizeof(S.dy)) / 4); i += kBwdThreads) z[i] = 0u;
+    for (int i = tid; i < (int)((sizeof(S.x) + sizeof(S.dy)) / 4); i += kGradThreads) z[i] = 0u;
   }
   if (tid == 0) {
     mbar_init(&S.bar, 1);
@@ -240,9 +255,11 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
   }
   __syncthreads();
 
-  double acc[kPartModes];
+  // per-mode parameter-gradient sums of this cluster's tiles (float pairs; each tile adds its
+  // C-token sum, the fixed-order cross-cluster reduction runs in float64)
+  float2 acc[kPartModes];
 #pragma unroll
-  for (int q = 0; q < kPartModes; ++q) acc[q] = 0.0;
+  for (int q = 0; q < kPartModes; ++q) acc[q] = bcast2(0.0f);
   double acc_b0 = 0.0, acc_b1 = 0.0;
   bool timed_out = false;
   pdl_wait();  // the adjoint carries (scan) are complete from here on
@@ -258,29 +275,29 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
     {
       const TIO* xs = static_cast<const TIO*>(p.x) + row0;
       const TIO* ds = static_cast<const TIO*>(p.dy) + row0;
-      const float4* cs = p.ctl + b * T + r.t0;
+      const float4* cs = p.ctl + 2 * (b * T + r.t0);
       const float2* hs = c > 0 ? p.carry + (b * chunks + (c - 1)) * (long long)M + mbase : nullptr;
       const float2* ks = c < chunks - 1 ? p.kout + (b * chunks + (c + 1)) * (long long)M + mbase : nullptr;
       if (p.use_tma) {
         if (tid == 0) {
           fence_proxy_async_smem();
-          unsigned bytes = 2u * act_box_bytes<TIO, C, kBwdModes>() + 16u * (unsigned)r.nvalid;
+          unsigned bytes = 2u * act_box_bytes<TIO, C, kBwdModes>() + 32u * (unsigned)r.nvalid;
           if (hs != nullptr) bytes += (unsigned)ncols * 8u;
           if (ks != nullptr) bytes += (unsigned)ncols * 8u;
           mbar_arrive_expect_tx(&S.bar, bytes);
           const int row = (int)(b * T + r.t0);
           tma_load_3d(&S.x[0][0][0], &p.map_x, mbase, 0, row, &S.bar);
           tma_load_3d(&S.dy[0][0][0], &p.map_dy, mbase, 0, row, &S.bar);
-          bulk_copy_g2s(&S.ctl[0], cs, 16u * (unsigned)r.nvalid, &S.bar);
+          bulk_copy_g2s(&S.ctl[0][0], cs, 32u * (unsigned)r.nvalid, &S.bar);
           if (hs != nullptr) bulk_copy_g2s(&S.hin[0], hs, (unsigned)ncols * 8u, &S.bar);
           if (ks != nullptr) bulk_copy_g2s(&S.kin[0], ks, (unsigned)ncols * 8u, &S.bar);
         }
         if (!mbar_wait(&S.bar, (unsigned)par, p.max_spin << 4)) timed_out = true;
       } else {
-        load_act_rows<TIO, kBwdModes>(xs, W, M, mbase, r.nvalid, S.x, kBwdThreads);
-        load_act_rows<TIO, kBwdModes>(ds, W, M, mbase, r.nvalid, S.dy, kBwdThreads);
-        for (int t = tid; t < r.nvalid; t += kBwdThreads) S.ctl[t] = cs[t];
-        for (int mm = tid; mm < ncols; mm += kBwdThreads) {
+        load_act_rows<TIO, kBwdModes>(xs, W, M, mbase, r.nvalid, S.x, kGradThreads);
+        load_act_rows<TIO, kBwdModes>(ds, W, M, mbase, r.nvalid, S.dy, kGradThreads);
+        for (int t = tid; t < 2 * r.nvalid; t += kGradThreads) (&S.ctl[0][0])[t] = cs[t];
+        for (int mm = tid; mm < ncols; mm += kGradThreads) {
           if (hs != nullptr) S.hin[mm] = hs[mm];
           if (ks != nullptr) S.kin[mm] = ks[mm];
         }
@@ -294,42 +311,52 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr int kU = kFull ? token_unroll<C>() : 1;  // partial unrolling keeps the kernel's code in the i-cache
       // pass 0: replay the states from the forward's carry; relu masks on dy
-      float2 hin = make_float2(0.0f, 0.0f);
+      float2 hin0 = make_float2(0.0f, 0.0f), hin1 = hin0;
       if (c > 0) {
-        if (act) hin = S.hin[tid];
-      } else if (p.h0_r != nullptr && act) {
-        hin = make_float2(p.h0_r[b * M + m], p.h0_i[b * M + m]);
+        if (act0) hin0 = S.hin[2 * tid];
+        if (act1) hin1 = S.hin[2 * tid + 1];
+      } else if (p.h0_r != nullptr) {
+        if (act0) hin0 = make_float2(p.h0_r[b * M + m0], p.h0_i[b * M + m0]);
+        if (act1) hin1 = make_float2(p.h0_r[b * M + m0 + 1], p.h0_i[b * M + m0 + 1]);
       }
+      const Cx2 hin = cx2(make_float2(hin0.x, hin1.x), make_float2(hin0.y, hin1.y));
       {
-        float2 h = hin;
+        Cx2 h = hin;
 #pragma unroll kU
         for (int t = 0; t < C; ++t) {
           if (kFull || t < nvalid) {
-            const float4 k4 = S.ctl[t];
-            const float xr = to_float(S.x[t][0][tid]);
-            const float xi = to_float(S.x[t][1][tid]);
-            const TokenCoef kc = token_coef<kFast>(mc, k4.x, k4.y, k4.z, k4.w);
-            h = cfma(kc.a, h, make_float2(kc.gain * tanh_t<kFast>(xr), kc.gain * tanh_t<kFast>(xi)));
-            S.h[t][tid] = h;
-            const float gr = to_float(S.dy[t][0][tid]);
-            const float gi = to_float(S.dy[t][1][tid]);
-            S.dy[t][0][tid] = from_float<TIO>(h.x > 0.0f ? gr : 0.0f);
-            S.dy[t][1][tid] = from_float<TIO>(h.y > 0.0f ? gi : 0.0f);
+            const float4 c0 = S.ctl[t][0], c1 = S.ctl[t][1];
+            const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
+            const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
+            const TokenCoef2 k = token_coef2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
+                                                    make_float2(c1.x, c1.y), make_float2(c1.z, c1.w));
+            h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
+            st2(&S.hr[t][2 * tid], h.re);
+            st2(&S.hi[t][2 * tid], h.im);
+            const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
+            const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
+            Pair<TIO>::store(&S.dy[t][0][2 * tid], h.re.x > 0.0f ? gr.x : 0.0f, h.re.y > 0.0f ? gr.y : 0.0f);
+            Pair<TIO>::store(&S.dy[t][1][2 * tid], h.im.x > 0.0f ? gi.x : 0.0f, h.im.y > 0.0f ? gi.y : 0.0f);
           }
         }
       }
 
       // adjoint carry entering the chunk from the later chunks
-      float2 lam = make_float2(0.0f, 0.0f);
+      float2 kin0 = make_float2(0.0f, 0.0f), kin1 = kin0;
       if (c < chunks - 1) {
-        if (act) lam = S.kin[tid];
-      } else if (p.glast_r != nullptr && act) {
-        lam = make_float2(p.glast_r[b * M + m], p.glast_i[b * M + m]);
+        if (act0) kin0 = S.kin[2 * tid];
+        if (act1) kin1 = S.kin[2 * tid + 1];
+      } else if (p.glast_r != nullptr) {
+        if (act0) kin0 = make_float2(p.glast_r[b * M + m0], p.glast_i[b * M + m0]);
+        if (act1) kin1 = make_float2(p.glast_r[b * M + m0 + 1], p.glast_i[b * M + m0 + 1]);
       }
+      Cx2 lam = cx2(make_float2(kin0.x, kin1.x), make_float2(kin0.y, kin1.y));
 
       // pass B: the true adjoint with every gradient, kGroup tokens at a time; each group's
       // dEta / dDelta are reduced over the warp at once (lane 4u+j holds value u of the group)
-      float fa[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      float2 fa[5];
+#pragma unroll
+      for (int q = 0; q < 5; ++q) fa[q] = bcast2(0.0f);
 #pragma unroll 1
       for (int t1 = C - 1; t1 >= 0; t1 -= kGroup) {
         float v[2 * kGroup];
@@ -338,15 +365,22 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
           const int t = t1 - u;
           float ve = 0.0f, vd = 0.0f;
           if (kFull || t < nvalid) {
-            const float4 k4 = S.ctl[t];
-            lam.x += to_float(S.dy[t][0][tid]);
-            lam.y += to_float(S.dy[t][1][tid]);
-            const float2 pv = t > 0 ? S.h[t - 1][tid] : hin;
-            const float cx = to_float(S.x[t][0][tid]);
-            const float cy = to_float(S.x[t][1][tid]);
-            // h[t] was last read as the previous state at step t+1: its slot now holds the
+            const float4 c0 = S.ctl[t][0], c1 = S.ctl[t][1];
+            lam.re = add2(lam.re, Pair<TIO>::load(&S.dy[t][0][2 * tid]));
+            lam.im = add2(lam.im, Pair<TIO>::load(&S.dy[t][1][2 * tid]));
+            const Cx2 pv = t > 0 ? cx2(ld2(&S.hr[t - 1][2 * tid]), ld2(&S.hi[t - 1][2 * tid])) : hin;
+            const float2 cx = Pair<TIO>::load(&S.x[t][0][2 * tid]);
+            const float2 cy = Pair<TIO>::load(&S.x[t][1][2 * tid]);
+            float2 ve2, vd2;
+            const Cx2 dxc = grad_step2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
+                                              make_float2(c1.x, c1.y), make_float2(c1.z, c1.w), lam, pv, cx, cy,
+                                              ve2, vd2, fa);
+            // h[t] was last read as the previous state at step t+1: its slots now hold the
             // write-path dx
-            S.h[t][tid] = grad_step<kFast>(mc, k4, lam, pv, cx, cy, ve, vd, fa);
+            st2(&S.hr[t][2 * tid], dxc.re);
+            st2(&S.hi[t][2 * tid], dxc.im);
+            ve = (act0 ? ve2.x : 0.0f) + (act1 ? ve2.y : 0.0f);
+            vd = (act0 ? vd2.x : 0.0f) + (act1 ? vd2.y : 0.0f);
           }
           v[u] = ve;
           v[kGroup + u] = vd;
@@ -359,19 +393,15 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
           S.warp_part[warp][(u < kGroup ? 0 : C) + t] = total;
         }
       }
-      if (!act) {
 #pragma unroll
-        for (int q = 0; q < 5; ++q) fa[q] = 0.0f;
-      }
-#pragma unroll
-      for (int q = 0; q < 5; ++q) acc[q] += fa[q];
+      for (int q = 0; q < 5; ++q) acc[q] = add2(acc[q], fa[q]);
 
       // token sums over all modes -> controller gradients
       __syncthreads();
       if (tid < 2 * C) {
         float sum = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kBwdWarps; ++w) sum += S.warp_part[w][tid];
+        for (int w = 0; w < kGradWarps; ++w) sum += S.warp_part[w][tid];
         S.part_grad[par][tid] = sum;
       }
       if (G > 1) cluster.sync();
@@ -387,34 +417,45 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
       }
       __syncthreads();
       if (tid < C) {
-        const float4 k4 = S.ctl[tid];
+        const float4 k4 = ctl4(S.ctl[tid]);
         const float dp1 = tid < nvalid ? S.tot[tid] * kLn16 * fmaf(-k4.w, k4.w, 1.0f) : 0.0f;
         const float dp0 = tid < nvalid ? S.tot[C + tid] * kHalfPi * fmaf(-k4.z, k4.z, 1.0f) : 0.0f;
-        S.dp[tid] = make_float2(dp0, dp1);
+        S.dp[tid] = make_float4(dp0, dp0, dp1, dp1);
       }
       __syncthreads();
       TIO* dxrow = static_cast<TIO*>(p.dx) + row0;
-      float fd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      float2 fd[4] = {bcast2(0.0f), bcast2(0.0f), bcast2(0.0f), bcast2(0.0f)};
 #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < nvalid) {
-          const float2 dp = S.dp[t];
-          const float2 dxc = S.h[t][tid];
-          const float xr = to_float(S.x[t][0][tid]);
-          const float xi = to_float(S.x[t][1][tid]);
-          if (act) {
-            TIO* row = dxrow + (long long)t * W;
-            Io<TIO>::store(row + m, fmaf(dp.x, mc.d0r, fmaf(dp.y, mc.d1r, dxc.x)));
-            Io<TIO>::store(row + M + m, fmaf(dp.x, mc.d0i, fmaf(dp.y, mc.d1i, dxc.y)));
+          const float4 dpv = S.dp[t];
+          const float2 dp0 = make_float2(dpv.x, dpv.y), dp1 = make_float2(dpv.z, dpv.w);
+          const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
+          const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
+          const float2 dre = fma2(dp0, mc.d0r, fma2(dp1, mc.d1r, ld2(&S.hr[t][2 * tid])));
+          const float2 dim = fma2(dp0, mc.d0i, fma2(dp1, mc.d1i, ld2(&S.hi[t][2 * tid])));
+          TIO* row = dxrow + (long long)t * W;
+          if (kVec && act1) {
+            Pair<TIO>::store(row + m0, dre.x, dre.y);
+            Pair<TIO>::store(row + M + m0, dim.x, dim.y);
+          } else {
+            if (act0) {
+              Io<TIO>::store(row + m0, dre.x);
+              Io<TIO>::store(row + M + m0, dim.x);
+            }
+            if (act1) {
+              Io<TIO>::store(row + m0 + 1, dre.y);
+              Io<TIO>::store(row + M + m0 + 1, dim.y);
+            }
           }
-          fd[0] = fmaf(xr, dp.x, fd[0]);
-          fd[1] = fmaf(xi, dp.x, fd[1]);
-          fd[2] = fmaf(xr, dp.y, fd[2]);
-          fd[3] = fmaf(xi, dp.y, fd[3]);
+          fd[0] = fma2(xr, dp0, fd[0]);
+          fd[1] = fma2(xi, dp0, fd[1]);
+          fd[2] = fma2(xr, dp1, fd[2]);
+          fd[3] = fma2(xi, dp1, fd[3]);
         }
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[5 + q] += fd[q];
+      for (int q = 0; q < 4; ++q) acc[5 + q] = add2(acc[5 + q], fd[q]);
     };
     if (nvalid == C) tile_body(std::true_type{});
     else tile_body(std::false_type{});
@@ -422,7 +463,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
       float s0 = 0.0f, s1 = 0.0f;
       for (int t = 0; t < C; ++t) {
         s0 += S.dp[t].x;
-        s1 += S.dp[t].y;
+        s1 += S.dp[t].z;
       }
       acc_b0 += s0;
       acc_b1 += s1;
@@ -433,7 +474,10 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_grad_kernel(const __gri
   const long long kc = blockIdx.y;
   double* part = p.part + kc * (long long)kPartModes * Mp;
 #pragma unroll
-  for (int q = 0; q < kPartModes; ++q) part[(long long)q * Mp + m] = act ? acc[q] : 0.0;
+  for (int q = 0; q < kPartModes; ++q) {
+    part[(long long)q * Mp + m0] = act0 ? (double)acc[q].x : 0.0;
+    part[(long long)q * Mp + m0 + 1] = act1 ? (double)acc[q].y : 0.0;
+  }
   if (g == 0 && tid == 0) {
     double* pb = p.part + (long long)gridDim.y * kPartModes * Mp + 2 * kc;
     pb[0] = acc_b0;

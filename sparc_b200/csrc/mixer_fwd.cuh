@@ -26,7 +26,7 @@ constexpr int kFwdModes = 2 * kFwdThreads;  // modes per CTA
 template <typename TIO, int C>
 struct SumSmem {
   TIO x[2][C][2][kFwdModes];  // [buffer][token][re|im][mode]
-  float4 ctl[C];              // E, delta, tau0, tau1 per token
+  float4 ctl[C][2];           // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
   float part[2][2 * C];       // this CTA's projection partials (peers read), by tile parity
   float warp_part[kFwdThreads / 32][2 * C];
   unsigned long long bar[2];
@@ -35,7 +35,7 @@ struct SumSmem {
 template <typename TIO, int C>
 struct RepSmem {
   TIO x[2][C][2][kFwdModes];
-  float4 ctl[2][C];
+  float4 ctl[2][C][2];       // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
   float2 hin[2][kFwdModes];  // carried-in state of the tile's modes
   unsigned long long bar[2];
 };
@@ -47,7 +47,7 @@ struct FwdParams {
   MixerParamPtrs pp;
   const float* h0_r;
   const float* h0_i;
-  float4* ctl;          // [B, T] token controls (E, delta, tau0, tau1)
+  float4* ctl;          // [B, T, 2] token controls as pairs (E, E, delta, delta), (tau0, tau0, tau1, tau1)
   const float2* carry;  // [B, chunks, M] inclusive chunk states (replay input)
   float4* agg;          // [B, chunks, Mp] chunk aggregates (P, Q)
   LaunchState* ls;
@@ -151,8 +151,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
   extern __shared__ __align__(128) unsigned char smem_raw[];
   SumSmem<TIO, C>& S = *reinterpret_cast<SumSmem<TIO, C>*>(smem_raw);
 
-  const ModeConst mc0 = load_mode(p.pp, m0, M, act0);
-  const ModeConst mc1 = load_mode(p.pp, m0 + 1, M, act1);
+  const ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
   const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
 
   // columns past M are never copied and must read as zeros
@@ -203,8 +202,10 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
       for (int t = 0; t < C; ++t) {
         const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
         const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-        v[t] = fmaf(xr.x, mc0.d0r, fmaf(xi.x, mc0.d0i, fmaf(xr.y, mc1.d0r, xi.y * mc1.d0i)));
-        v[C + t] = fmaf(xr.x, mc0.d1r, fmaf(xi.x, mc0.d1i, fmaf(xr.y, mc1.d1r, xi.y * mc1.d1i)));
+        const float2 v0 = fma2(xr, mc.d0r, mul2(xi, mc.d0i));
+        const float2 v1 = fma2(xr, mc.d1r, mul2(xi, mc.d1i));
+        v[t] = v0.x + v0.y;
+        v[C + t] = v1.x + v1.y;
       }
       constexpr int kShift = 5 - log2i<2 * C>();
       const int lane = tid & 31, warp = tid >> 5;
@@ -240,36 +241,39 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
         }
         const float tau0 = tanh_accurate(p0 + bias0);
         const float tau1 = tanh_accurate(p1 + bias1);
-        const float4 k4 = make_float4(expf(kLn16 * tau1), kHalfPi * tau0, tau0, tau1);
-        S.ctl[tid] = k4;
-        if (g == 0 && tid < r.nvalid) p.ctl[r.b * T + r.t0 + tid] = k4;
+        const float E = expf(kLn16 * tau1), delta = kHalfPi * tau0;
+        const float4 c0 = make_float4(E, E, delta, delta), c1 = make_float4(tau0, tau0, tau1, tau1);
+        S.ctl[tid][0] = c0;
+        S.ctl[tid][1] = c1;
+        if (g == 0 && tid < r.nvalid) {
+          float4* cp = p.ctl + 2 * (r.b * T + r.t0 + tid);
+          cp[0] = c0;
+          cp[1] = c1;
+        }
       }
       __syncthreads();
     }
 
-    // the chunk's aggregate map per mode
+    // the chunk's aggregate map per mode (both of the thread's modes in packed lanes)
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr int kU = kFull ? token_unroll<C>() : 1;  // partial unrolling keeps the kernel's code in the i-cache
-      float2 P0 = make_float2(1.0f, 0.0f), Q0 = make_float2(0.0f, 0.0f);
-      float2 P1 = P0, Q1 = Q0;
+      Cx2 P = cx2(bcast2(1.0f), bcast2(0.0f)), Q = cx2(bcast2(0.0f), bcast2(0.0f));
 #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < r.nvalid) {
-          const float4 k4 = S.ctl[t];
+          const float4 c0 = S.ctl[t][0], c1 = S.ctl[t][1];
           const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-          const TokenCoef c0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
-          const TokenCoef c1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
-          Q0 = cfma(c0.a, Q0, make_float2(c0.gain * tanh_t<kFast>(xr.x), c0.gain * tanh_t<kFast>(xi.x)));
-          Q1 = cfma(c1.a, Q1, make_float2(c1.gain * tanh_t<kFast>(xr.y), c1.gain * tanh_t<kFast>(xi.y)));
-          P0 = cmul(c0.a, P0);
-          P1 = cmul(c1.a, P1);
+          const TokenCoef2 k = token_coef2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
+                                                  make_float2(c1.x, c1.y), make_float2(c1.z, c1.w));
+          Q = cfma2(k.a, Q, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
+          P = cmul2(k.a, P);
         }
       }
       float4* ap = p.agg + (r.b * p.chunks + r.c) * (long long)p.Mp + m0;
-      if (act0) __stcg(ap, make_float4(P0.x, P0.y, Q0.x, Q0.y));
-      if (act1) __stcg(ap + 1, make_float4(P1.x, P1.y, Q1.x, Q1.y));
+      if (act0) __stcg(ap, make_float4(P.re.x, P.im.x, Q.re.x, Q.im.x));
+      if (act1) __stcg(ap + 1, make_float4(P.re.y, P.im.y, Q.re.y, Q.im.y));
     };
     if (r.nvalid == C) body(std::true_type{});
     else body(std::false_type{});
@@ -295,8 +299,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
   extern __shared__ __align__(128) unsigned char smem_raw[];
   RepSmem<TIO, C>& S = *reinterpret_cast<RepSmem<TIO, C>*>(smem_raw);
 
-  const ModeConst mc0 = load_mode(p.pp, m0, M, act0);
-  const ModeConst mc1 = load_mode(p.pp, m0 + 1, M, act1);
+  const ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
 
   if (tid == 0) {
     mbar_init(&S.bar[0], 1);
@@ -311,21 +314,21 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
   auto issue = [&](long long i, int buf) {
     const TileRef r = tile_ref(i, B, T, C);
     const TIO* src = static_cast<const TIO*>(p.x) + (r.b * T + r.t0) * W;
-    const float4* csrc = p.ctl + r.b * T + r.t0;
+    const float4* csrc = p.ctl + 2 * (r.b * T + r.t0);
     const float2* hsrc = r.c > 0 ? p.carry + (r.b * p.chunks + (r.c - 1)) * (long long)M + mbase : nullptr;
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        unsigned bytes = act_box_bytes<TIO, C, kFwdModes>() + 16u * (unsigned)r.nvalid;
+        unsigned bytes = act_box_bytes<TIO, C, kFwdModes>() + 32u * (unsigned)r.nvalid;
         if (hsrc != nullptr) bytes += (unsigned)ncols * 8u;
         mbar_arrive_expect_tx(&S.bar[buf], bytes);
         tma_load_3d(&S.x[buf][0][0][0], &p.map_x, mbase, 0, (int)(r.b * T + r.t0), &S.bar[buf]);
-        bulk_copy_g2s(&S.ctl[buf][0], csrc, 16u * (unsigned)r.nvalid, &S.bar[buf]);
+        bulk_copy_g2s(&S.ctl[buf][0][0], csrc, 32u * (unsigned)r.nvalid, &S.bar[buf]);
         if (hsrc != nullptr) bulk_copy_g2s(&S.hin[buf][0], hsrc, (unsigned)ncols * 8u, &S.bar[buf]);
       }
     } else {
       load_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], kFwdThreads);
-      for (int t = tid; t < r.nvalid; t += kFwdThreads) S.ctl[buf][t] = csrc[t];
+      for (int t = tid; t < 2 * r.nvalid; t += kFwdThreads) (&S.ctl[buf][0][0])[t] = csrc[t];
       if (hsrc != nullptr)
         for (int mm = tid; mm < ncols; mm += kFwdThreads) S.hin[buf][mm] = hsrc[mm];
     }
@@ -345,7 +348,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
       __syncthreads();
     }
     const TIO(*xt)[2][kFwdModes] = S.x[buf];
-    const float4* ctl = S.ctl[buf];
+    const float4(*ctl)[2] = S.ctl[buf];
     float2 h0 = make_float2(0.0f, 0.0f), h1 = h0;
     if (r.c > 0) {
       if (act0) h0 = S.hin[buf][2 * tid];
@@ -354,6 +357,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
       if (act0) h0 = make_float2(p.h0_r[r.b * M + m0], p.h0_i[r.b * M + m0]);
       if (act1) h1 = make_float2(p.h0_r[r.b * M + m0 + 1], p.h0_i[r.b * M + m0 + 1]);
     }
+    Cx2 h = cx2(make_float2(h0.x, h1.x), make_float2(h0.y, h1.y));
     TIO* yrow = static_cast<TIO*>(p.y) + (r.b * T + r.t0) * W;
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
@@ -361,14 +365,14 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
 #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < r.nvalid) {
-          const float4 k4 = ctl[t];
+          const float4 c0 = ctl[t][0], c1 = ctl[t][1];
           const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-          const TokenCoef c0 = token_coef<kFast>(mc0, k4.x, k4.y, k4.z, k4.w);
-          const TokenCoef c1 = token_coef<kFast>(mc1, k4.x, k4.y, k4.z, k4.w);
-          h0 = cfma(c0.a, h0, make_float2(c0.gain * tanh_t<kFast>(xr.x), c0.gain * tanh_t<kFast>(xi.x)));
-          h1 = cfma(c1.a, h1, make_float2(c1.gain * tanh_t<kFast>(xr.y), c1.gain * tanh_t<kFast>(xi.y)));
-          store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, h0, h1);
+          const TokenCoef2 k = token_coef2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
+                                                  make_float2(c1.x, c1.y), make_float2(c1.z, c1.w));
+          h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
+          store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, make_float2(h.re.x, h.im.x),
+                                  make_float2(h.re.y, h.im.y));
         }
       }
     };

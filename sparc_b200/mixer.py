@@ -52,7 +52,7 @@ class _SparcMixerFunction(torch.autograd.Function):
         y = torch.empty_like(x)
         chunks = L.sparc_mixer_carry_chunks(T, dt)
         carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
-        controls = torch.empty((B, T, 4), dtype=torch.float32, device=dev)
+        controls = torch.empty((B, T, 8), dtype=torch.float32, device=dev)
         last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
         last_i = torch.empty((B, M), dtype=torch.float32, device=dev)
         nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)

@@ -44,7 +44,7 @@ def _call(entry, x, params, workspace=None):
     carry = torch.empty((B, L.sparc_mixer_carry_chunks(T, _lib.dtype_code(x.dtype)), M, 2), device=x.device)
     last_r = torch.empty((B, M), device=x.device)
     last_i = torch.empty((B, M), device=x.device)
-    controls = torch.empty((B, T, 4), device=x.device)
+    controls = torch.empty((B, T, 8), device=x.device)
     ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel())
     a = _lib.MixerFwdArgs(x.data_ptr(), y.data_ptr(), *[p.data_ptr() for p in params], None, None,
                           last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), ws_ptr, ws_bytes,
