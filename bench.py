@@ -40,9 +40,9 @@ if ROOT not in sys.path:
 
 WORKLOADS = {
     "layer": dict(workload="sparc_mixer_layer_fwd_bwd", batch=8, seq_len=2048, width=512,
-                  dtype="float32", chunk=16, config_index=1),
+                  dtype="float32", config_index=1),
     "layer5": dict(workload="sparc_mixer_layer_fwd_bwd_config5_share", batch=8, seq_len=16384, width=2048,
-                   dtype="bfloat16", chunk=16, config_index=4),
+                   dtype="bfloat16", config_index=4),
     "stack": dict(workload="sparc_4layer_rmsnorm_residual_stack_fwd_bwd", batch=64, seq_len=16384,
                   width=2048, dtype="bfloat16", layers=4, config_index=4),
     "real": dict(workload="real_scan_fwd_bwd", batch=16, seq_len=8192, channels=16384,
@@ -61,6 +61,30 @@ def measured_peaks():
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+# Kernels one mixer fwd+bwd launches: fwd summary, carry scan, replay; bwd summary, carry scan,
+# gradients, parameter-gradient reduction.
+MIXER_LAUNCHES = 7
+
+
+def mixer_kernel_bytes(B, T, W, s, chunk):
+    """Algorithmic DRAM bytes of each mixer kernel per launch: every input it must read once and
+    every output it must write once (activations W*s bytes per token, saved controls 32 bytes
+    per token, chunk maps 16 bytes and chunk states 8 bytes per chunk and mode)."""
+    M = W // 2
+    bt = B * T
+    chunks = -(-T // chunk)
+    act = W * s * bt
+    ctl = 32 * bt
+    agg = 16 * B * chunks * M
+    car = 8 * B * chunks * M
+    return {"mixer_fwd_summary_kernel": act + ctl + agg,
+            "mixer_carry_scan_kernel(fwd)": agg + car,
+            "mixer_fwd_replay_kernel": 2 * act + ctl + car,
+            "mixer_bwd_summary_kernel": 2 * act + ctl + agg,
+            "mixer_carry_scan_kernel(bwd)": agg + car,
+            "mixer_bwd_grad_kernel": 3 * act + ctl + 2 * car}
 
 
 def profile_traffic(kernel: str, workload: str):
@@ -290,39 +314,41 @@ def run_layer(args, wl, world, rank, local):
     tokens_step = B * T * world
     value = tokens_step / (ms / 1e3)
 
-    # per-kernel timing through the C ABI (same inputs), for the roofline of the dominant kernel
+    # per-kernel device time from the library's CUDA-event timing (sparc_timing_*), same inputs,
+    # outside the graph; the roofline line is the dominant kernel's
     peak, peak_kind = measured_peaks()
-    kern = {}
+    L = _lib.lib()
+    chunk = int(L.sparc_mixer_chunk_tokens(_lib.dtype_code(dtype)))
+    kbytes = mixer_kernel_bytes(B, T, W, s, chunk)
     xr = x.clone().requires_grad_(True)
-    fwd_times, bwd_times = [], []
-    for _ in range(args.steps + 3):
-        flush()
-        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        e0.record()
+    for _ in range(2):
         yy, _ = model(xr)
-        e1.record()
-        flush()
-        e1b = torch.cuda.Event(enable_timing=True)
-        e1b.record()
         yy.backward(g)
-        e2.record()
-        torch.cuda.synchronize(device)
-        fwd_times.append(e0.elapsed_time(e1))
-        bwd_times.append(e1b.elapsed_time(e2))
+    torch.cuda.synchronize(device)
+    L.sparc_timing_enable(1)
+    _lib.kernel_times(reset_only=True)
+    for _ in range(args.steps):
+        flush()
+        yy, _ = model(xr)
+        flush()
+        yy.backward(g)
         xr.grad = None
         model.zero_grad(set_to_none=True)
-    fwd_ms = sorted(fwd_times[3:])[len(fwd_times[3:]) // 2]
-    bwd_ms = sorted(bwd_times[3:])[len(bwd_times[3:]) // 2]
-    kern["mixer_forward"] = dict(ms=fwd_ms, bytes=2 * W * s * B * T)
-    kern["mixer_backward"] = dict(ms=bwd_ms, bytes=3 * W * s * B * T)
+    torch.cuda.synchronize(device)
+    times = _lib.kernel_times()
+    L.sparc_timing_enable(0)
+    kern = {}
+    for name, (tot, cnt) in times.items():
+        kms = tot / cnt
+        kb = kbytes.get(name)
+        kern[name] = {"ms": round(kms, 4), "launches_per_step": round(cnt / args.steps, 2), "algorithmic_bytes": kb,
+                      "GBps": round(kb / (kms / 1e3) / 1e9, 1) if kb else None}
     dom = max(kern, key=lambda k: kern[k]["ms"])
-    achieved = kern[dom]["bytes"] / (kern[dom]["ms"] / 1e3) / 1e9
+    achieved = kern[dom]["GBps"]
     traffic = profile_traffic(dom, f"layer_b{B}_t{T}_w{W}_{'fp32' if s == 4 else 'bf16'}")
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": dom,
-                "peak_source": peak_kind,
-                "kernels": {k: {"ms": round(v["ms"], 4), "algorithmic_bytes": v["bytes"],
-                                "GBps": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1)} for k, v in kern.items()},
+                "peak_source": peak_kind, "kernels": kern,
                 "step_frac": round(5 * W * s * B * T / (ms / 1e3) / 1e9 / peak, 4)}
 
     # end to end through the public API with pinned host buffers
@@ -372,7 +398,7 @@ def run_layer(args, wl, world, rank, local):
                          f"T={T}, W={W} per round, one row per process"}
     del graph
     return dict(value=value, ms=ms, roofline=roofline, e2e=e2e, cpu=cpu, clocks=clocks.summary(),
-                launches=3 * args.steps, per_step_ms=per, tokens_step=tokens_step)
+                launches=MIXER_LAUNCHES * args.steps, per_step_ms=per, tokens_step=tokens_step, chunk=chunk)
 
 
 def run_stack(args, wl, world, rank, local):
@@ -417,7 +443,7 @@ def run_stack(args, wl, world, rank, local):
                 "kernel": "whole step (L*5*W*s bytes/token)", "peak_source": kind}
     sparc_b200.check_status()
     return dict(value=value, ms=ms, roofline=roofline, e2e=None, cpu=None, clocks=clocks.summary(),
-                launches=3 * L * args.steps, per_step_ms=per, tokens_step=gb * T)
+                launches=MIXER_LAUNCHES * L * args.steps, per_step_ms=per, tokens_step=gb * T)
 
 
 def run_real(args, wl, world, rank, local):
@@ -568,6 +594,8 @@ def main():
         unit = "tokens/s"
         cfg = {"workload": wl["workload"], "baseline_config": wl["config_index"],
                "parallelism": f"dp{world}" if world > 1 else "single"}
+        if "chunk" in r:
+            wl["chunk"] = r["chunk"]
         for k in ("batch", "seq_len", "width", "channels", "layers", "steps", "chunk"):
             if k in wl:
                 cfg["global_batch" if k == "batch" else k] = wl[k] * (world if k == "batch" and args.workload in ("layer", "layer5", "real", "decode") else 1)
