@@ -217,7 +217,8 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* args, void* stream);
  * call cudaMalloc after start-up because it can block the whole device. Its scratch is a
  * fixed array of sparc_mixer_noalloc_scratch_bytes() (32 MiB) inside the library, which every
  * GPU that loads the library holds until the process exits; a problem that needs more
- * (roughly batch * ceil(length/16) * (width/2 rounded up to 256) * 18 bytes) is rejected with
+ * (roughly batch * ceil(length/C) * (width/2 rounded up to 256) * 18 bytes, C = 16 tokens for
+ * bfloat16 and 8 for float32) is rejected with
  * SPARC_ERR_WORKSPACE and a message. The first call on a device looks up that device's copy of the array
  * (cudaGetSymbolAddress), so make it before any stream capture. All calls share the array:
  * calls whose executions overlap on the GPU (other streams, other host threads) race and must
