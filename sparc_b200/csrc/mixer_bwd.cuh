@@ -177,8 +177,10 @@ template <typename TIO, int C>
 struct GradSmem {
   TIO x[C][2][kBwdModes];
   TIO dy[C][2][kBwdModes];     // masked by the relu in pass 0
-  float hr[C][kBwdModes];      // replayed states (real plane), then the write-path dx (pass B)
-  float hi[C][kBwdModes];      // imaginary plane
+  TIO hr[C][kBwdModes];        // replayed states (real plane), then the write-path dx (pass B);
+  TIO hi[C][kBwdModes];        // imaginary plane. In the activation dtype: for bfloat16 that keeps
+                               // the CTA within four per SM (the reference's bf16 path likewise
+                               // saves its states in bf16); float32 keeps them exact
   float2 hin[kBwdModes];       // state entering the chunk, (re, im) per mode
   float2 kin[kBwdModes];       // adjoint carry entering the chunk from the later chunks
   float4 ctl[C][2];            // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
@@ -224,7 +226,7 @@ __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, float2 E, float2
 }
 
 template <typename TIO, int C, bool kFast, bool kVec>
-__global__ void __launch_bounds__(kGradThreads) mixer_bwd_grad_kernel(const __grid_constant__ BwdParams p) {
+__global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const __grid_constant__ BwdParams p) {
   static_assert(C % kGroup == 0, "the reverse walk runs in groups of kGroup tokens");
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
@@ -331,8 +333,8 @@ __global__ void __launch_bounds__(kGradThreads) mixer_bwd_grad_kernel(const __gr
             const TokenCoef2 k = token_coef2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
                                                     make_float2(c1.x, c1.y), make_float2(c1.z, c1.w));
             h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
-            st2(&S.hr[t][2 * tid], h.re);
-            st2(&S.hi[t][2 * tid], h.im);
+            Pair<TIO>::store(&S.hr[t][2 * tid], h.re.x, h.re.y);
+            Pair<TIO>::store(&S.hi[t][2 * tid], h.im.x, h.im.y);
             const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
             const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
             Pair<TIO>::store(&S.dy[t][0][2 * tid], h.re.x > 0.0f ? gr.x : 0.0f, h.re.y > 0.0f ? gr.y : 0.0f);
@@ -368,7 +370,8 @@ __global__ void __launch_bounds__(kGradThreads) mixer_bwd_grad_kernel(const __gr
             const float4 c0 = S.ctl[t][0], c1 = S.ctl[t][1];
             lam.re = add2(lam.re, Pair<TIO>::load(&S.dy[t][0][2 * tid]));
             lam.im = add2(lam.im, Pair<TIO>::load(&S.dy[t][1][2 * tid]));
-            const Cx2 pv = t > 0 ? cx2(ld2(&S.hr[t - 1][2 * tid]), ld2(&S.hi[t - 1][2 * tid])) : hin;
+            const Cx2 pv = t > 0 ? cx2(Pair<TIO>::load(&S.hr[t - 1][2 * tid]), Pair<TIO>::load(&S.hi[t - 1][2 * tid]))
+                                 : hin;
             const float2 cx = Pair<TIO>::load(&S.x[t][0][2 * tid]);
             const float2 cy = Pair<TIO>::load(&S.x[t][1][2 * tid]);
             float2 ve2, vd2;
@@ -377,8 +380,8 @@ __global__ void __launch_bounds__(kGradThreads) mixer_bwd_grad_kernel(const __gr
                                               ve2, vd2, fa);
             // h[t] was last read as the previous state at step t+1: its slots now hold the
             // write-path dx
-            st2(&S.hr[t][2 * tid], dxc.re);
-            st2(&S.hi[t][2 * tid], dxc.im);
+            Pair<TIO>::store(&S.hr[t][2 * tid], dxc.re.x, dxc.re.y);
+            Pair<TIO>::store(&S.hi[t][2 * tid], dxc.im.x, dxc.im.y);
             ve = (act0 ? ve2.x : 0.0f) + (act1 ? ve2.y : 0.0f);
             vd = (act0 ? vd2.x : 0.0f) + (act1 ? vd2.y : 0.0f);
           }
@@ -432,8 +435,8 @@ __global__ void __launch_bounds__(kGradThreads) mixer_bwd_grad_kernel(const __gr
           const float2 dp0 = make_float2(dpv.x, dpv.y), dp1 = make_float2(dpv.z, dpv.w);
           const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
-          const float2 dre = fma2(dp0, mc.d0r, fma2(dp1, mc.d1r, ld2(&S.hr[t][2 * tid])));
-          const float2 dim = fma2(dp0, mc.d0i, fma2(dp1, mc.d1i, ld2(&S.hi[t][2 * tid])));
+          const float2 dre = fma2(dp0, mc.d0r, fma2(dp1, mc.d1r, Pair<TIO>::load(&S.hr[t][2 * tid])));
+          const float2 dim = fma2(dp0, mc.d0i, fma2(dp1, mc.d1i, Pair<TIO>::load(&S.hi[t][2 * tid])));
           TIO* row = dxrow + (long long)t * W;
           if (kVec && act1) {
             Pair<TIO>::store(row + m0, dre.x, dre.y);
