@@ -292,6 +292,8 @@ def run_layer(args, wl, world, rank, local):
             model.zero_grad(set_to_none=True)
             y, _ = model(x)
             y.backward(g)
+            if reducer is not None:
+                reducer()  # also initialises the NCCL communicator before the graph capture
     torch.cuda.current_stream(device).wait_stream(stream)
     torch.cuda.synchronize(device)
     model.zero_grad(set_to_none=True)
@@ -299,11 +301,11 @@ def run_layer(args, wl, world, rank, local):
     with torch.cuda.graph(graph, stream=stream):
         y, _ = model(x)
         y.backward(g)
+        if reducer is not None:
+            reducer()  # the one exchange step (NCCL all-reduce of the parameter gradients)
 
     def step():
         graph.replay()
-        if reducer is not None:
-            reducer()
 
     for _ in range(args.warmup):
         flush()
