@@ -68,10 +68,13 @@ extern "C" {
  * h_t = a_t h_{t-1} + b_t over M = width/2 complex modes, with a_t, b_t computed from x_t
  * and the parameters. `carry` receives the state at the end of every chunk of
  * sparc_mixer_chunk_tokens(dtype) tokens ([batch, sparc_mixer_carry_chunks(length, dtype), M] complex,
- * interleaved real/imag float32) and `controls` the per-token controls ([batch, length, 8]
- * float32: e^eta, delta, tanh p0, tanh p1, each stored twice in the order e^eta, e^eta, delta,
- * delta, tanh p0, tanh p0, tanh p1, tanh p1); the backward needs both, and y. h0 (initial
- * state) and last (final state) are optional pairs (NULL, NULL). */
+ * interleaved real/imag float32) and `controls` the per-token controls ([batch, length, 12]
+ * float32: e^eta, e^eta, delta, delta, tanh p0, tanh p0, tanh p1, tanh p1, keep, keep, 0, 0, with
+ * keep 0 at a reset token); the backward needs both, and y. h0 (initial state) and last (final
+ * state) are optional pairs (NULL, NULL). `reset` (optional, [batch, length] bytes) marks the
+ * tokens where a new segment starts: there the transition is zero, so the state restarts from
+ * the token's write, as with segment_pos == 0 (or reset_first at t = 0) in the reference's
+ * tiled serial scan (forward/scan.py:807-854, common.py:219-268). */
 typedef struct SparcMixerFwdArgs {
   const void* x;                       /* [batch, length, width]  activations (dtype) */
   void* y;                             /* [batch, length, width]  output (dtype) */
@@ -87,7 +90,8 @@ typedef struct SparcMixerFwdArgs {
   float* last_r;                       /* [batch, M] or NULL */
   float* last_i;                       /* [batch, M] or NULL */
   float* carry;                        /* [batch, chunks, M, 2] */
-  float* controls;                     /* [batch, length, 8] */
+  float* controls;                     /* [batch, length, 12] */
+  const unsigned char* reset;          /* [batch, length] (nonzero = segment start) or NULL */
   void* workspace;
   size_t workspace_bytes;
   long long batch;

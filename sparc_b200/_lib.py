@@ -32,7 +32,7 @@ class MixerFwdArgs(ctypes.Structure):
         ("nu_log", _vp), ("theta_log", _vp), ("phase_direction", _vp), ("radial_direction", _vp),
         ("write_log_gain", _vp), ("write_phase_response", _vp), ("write_radial_response", _vp),
         ("h0_r", _vp), ("h0_i", _vp), ("last_r", _vp), ("last_i", _vp), ("carry", _vp),
-        ("controls", _vp),
+        ("controls", _vp), ("reset", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint), ("deterministic", ctypes.c_int),

@@ -158,6 +158,16 @@ __device__ __forceinline__ ModeConst2 pair_modes(const ModeConst& a, const ModeC
   return m;
 }
 
+// Per-token controls as the forward saves them (48 bytes): every value twice, so that a
+// thread's two modes load them as packed pairs; keep is 0 at a token where a segment reset cuts
+// the recurrence (its transition is zero), else 1.
+struct TokenCtl {
+  float4 ed;    // E, E, delta, delta   (E = e^eta)
+  float4 tau;   // tau0, tau0, tau1, tau1
+  float4 keep;  // keep, keep, 0, 0
+};
+static_assert(sizeof(TokenCtl) == 48, "token controls are three 16-byte words");
+
 struct TokenCoef2 {
   float2 z, rho;
   Cx2 a;
@@ -166,20 +176,21 @@ struct TokenCoef2 {
 
 template <bool kFast>
 __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0,
-                                                  float2 tau1) {
+                                                  float2 tau1, float2 keep) {
   TokenCoef2 k;
   k.z = mul2(mc.nu, E);
   k.rho = ex2_2(mul2(mc.nl2e_neg, E));
+  const float2 rk = mul2(k.rho, keep);  // the transition's radius (0 at a reset)
   if constexpr (kFast) {
     const float2 ph = sub2(add2(delta, mc.theta), mul2(k.rho, delta));  // theta + (1 - rho) delta
     float2 sn, cs;
     sincos_hw(ph.x, &sn.x, &cs.x);
     sincos_hw(ph.y, &sn.y, &cs.y);
-    k.a = Cx2{mul2(k.rho, cs), mul2(k.rho, sn)};
+    k.a = Cx2{mul2(rk, cs), mul2(rk, sn)};
   } else {
     float2 sn, cs;
     sincos_halfpi2(sub2(delta, mul2(k.rho, delta)), &sn, &cs);  // (1 - rho) delta, |.| <= pi/2
-    const float2 rct = mul2(k.rho, mc.ct), rst = mul2(k.rho, mc.st);
+    const float2 rct = mul2(rk, mc.ct), rst = mul2(rk, mc.st);
     k.a = Cx2{sub2(mul2(rct, cs), mul2(rst, sn)), fma2(rst, cs, mul2(rct, sn))};
   }
   const float2 q = fma2(tau0, mc.wpr, mul2(tau1, mc.wrr));
@@ -199,10 +210,19 @@ __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E
   return k;
 }
 
+// The same from a saved controls record.
+template <bool kFast>
+__device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, const TokenCtl& c) {
+  return token_coef2<kFast>(mc, make_float2(c.ed.x, c.ed.y), make_float2(c.ed.z, c.ed.w),
+                            make_float2(c.tau.x, c.tau.y), make_float2(c.tau.z, c.tau.w),
+                            make_float2(c.keep.x, c.keep.y));
+}
+
 // Transition a = rho e^{i(theta + (1-rho) delta)} alone (the reverse local pass needs no write).
 template <bool kFast>
-__device__ __forceinline__ float2 token_transition(const ModeConst& mc, float E, float delta) {
-  return transition_of<kFast>(mc, ex2_approx(-mc.nl2e * E), delta);
+__device__ __forceinline__ float2 token_transition(const ModeConst& mc, float E, float delta, float keep) {
+  const float2 a = transition_of<kFast>(mc, ex2_approx(-mc.nl2e * E), delta);
+  return make_float2(a.x * keep, a.y * keep);
 }
 
 // Warp transpose-reduce of N values per lane (N a power of two, N <= 32). Afterwards lane l
@@ -868,7 +888,8 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
                         a->write_log_gain, a->write_phase_response, a->write_radial_response};
   p.h0_r = a->h0_r;
   p.h0_i = a->h0_i;
-  p.ctl = reinterpret_cast<float4*>(a->controls);
+  p.ctl = reinterpret_cast<TokenCtl*>(a->controls);
+  p.reset = a->reset;
   p.carry = reinterpret_cast<const float2*>(a->carry);
   p.agg = reinterpret_cast<float4*>(ws + L.agg);
   p.ls = reinterpret_cast<LaunchState*>(ws);
@@ -962,7 +983,7 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.h0_i = a->h0_i;
   p.glast_r = a->grad_last_r;
   p.glast_i = a->grad_last_i;
-  p.ctl = reinterpret_cast<const float4*>(a->controls);
+  p.ctl = reinterpret_cast<const TokenCtl*>(a->controls);
   p.carry = reinterpret_cast<const float2*>(a->carry);
   p.kout = reinterpret_cast<const float2*>(ws + L.kout);
   p.agg = reinterpret_cast<float4*>(ws + L.agg);

@@ -36,7 +36,7 @@ template <typename TIO, int C>
 struct RsumSmem {
   TIO dy[2][C][2][kBwdModes];
   TIO y[2][C][2][kBwdModes];
-  float4 ctl[2][C][2];         // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
+  TokenCtl ctl[2][C];
   unsigned long long bar[2];
 };
 
@@ -54,7 +54,7 @@ struct BwdParams {
   const float* h0_i;
   const float* glast_r;
   const float* glast_i;
-  const float4* ctl;     // [B, T, 2] forward token controls (pairs, as the forward saved them)
+  const TokenCtl* ctl;   // [B, T] forward token controls
   const float2* carry;   // [B, chunks, M] forward inclusive states
   const float2* kout;    // [B, chunks, M] adjoint carry leaving each chunk (scan output)
   float4* agg;           // [B, chunks, Mp] reverse aggregates (summary output)
@@ -67,8 +67,7 @@ struct BwdParams {
   int use_tma;
 };
 
-// (E, delta, tau0, tau1) of a token from its pair layout.
-__device__ __forceinline__ float4 ctl4(const float4 (&c)[2]) { return make_float4(c[0].x, c[0].z, c[1].x, c[1].z); }
+
 
 // ------------------------------------------------------------------------------ reverse summary
 template <typename TIO, int C, bool kFast>
@@ -104,20 +103,21 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
     const long long row0 = (r.b * T + r.t0) * W;
     const TIO* dsrc = static_cast<const TIO*>(p.dy) + row0;
     const TIO* ysrc = static_cast<const TIO*>(p.y) + row0;
-    const float4* csrc = p.ctl + 2 * (r.b * T + r.t0);
+    const TokenCtl* csrc = p.ctl + r.b * T + r.t0;
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&S.bar[buf], 2u * act_box_bytes<TIO, C, kBwdModes>() + 32u * (unsigned)r.nvalid);
+        mbar_arrive_expect_tx(&S.bar[buf], 2u * act_box_bytes<TIO, C, kBwdModes>() +
+                                               (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid);
         const int row = (int)(r.b * T + r.t0);
         tma_load_3d(&S.dy[buf][0][0][0], &p.map_dy, mbase, 0, row, &S.bar[buf]);
         tma_load_3d(&S.y[buf][0][0][0], &p.map_y, mbase, 0, row, &S.bar[buf]);
-        bulk_copy_g2s(&S.ctl[buf][0][0], csrc, 32u * (unsigned)r.nvalid, &S.bar[buf]);
+        bulk_copy_g2s(&S.ctl[buf][0], csrc, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar[buf]);
       }
     } else {
       load_act_rows<TIO, kBwdModes>(dsrc, W, M, mbase, r.nvalid, S.dy[buf], kBwdThreads);
       load_act_rows<TIO, kBwdModes>(ysrc, W, M, mbase, r.nvalid, S.y[buf], kBwdThreads);
-      for (int t = tid; t < 2 * r.nvalid; t += kBwdThreads) (&S.ctl[buf][0][0])[t] = csrc[t];
+      for (int t = tid; t < r.nvalid; t += kBwdThreads) S.ctl[buf][t] = csrc[t];
     }
   };
   if (k0 < p.tiles) issue(k0, 0);
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
     }
     const TIO(*dyt)[2][kBwdModes] = S.dy[buf];
     const TIO(*yt)[2][kBwdModes] = S.y[buf];
-    const float4(*ctl)[2] = S.ctl[buf];
+    const TokenCtl* ctl = S.ctl[buf];
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr int kU = kFull ? token_unroll<C>() : 1;
@@ -145,14 +145,14 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
 #pragma unroll kU
       for (int t = C - 1; t >= 0; --t) {
         if (kFull || t < r.nvalid) {
-          const float4 c0 = ctl[t][0];
+          const TokenCtl& tc = ctl[t];
           const float gr = to_float(dyt[t][0][tid]);
           const float gi = to_float(dyt[t][1][tid]);
           const float yr = to_float(yt[t][0][tid]);
           const float yi = to_float(yt[t][1][tid]);
           q.x += yr > 0.0f ? gr : 0.0f;
           q.y += yi > 0.0f ? gi : 0.0f;
-          const float2 a = token_transition<kFast>(mc, c0.x, c0.z);
+          const float2 a = token_transition<kFast>(mc, tc.ed.x, tc.ed.z, tc.keep.x);
           q = make_float2(fmaf(a.x, q.x, a.y * q.y), fmaf(a.x, q.y, -a.y * q.x));
           P = cmul(a, P);
         }
@@ -183,7 +183,7 @@ struct GradSmem {
                                // saves its states in bf16); float32 keeps them exact
   float2 hin[kBwdModes];       // state entering the chunk, (re, im) per mode
   float2 kin[kBwdModes];       // adjoint carry entering the chunk from the later chunks
-  float4 ctl[C][2];            // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
+  TokenCtl ctl[C];
   float4 dp[C];                // controller gradients per token as pairs (dp0, dp0, dp1, dp1)
   float tot[2 * C];            // cluster totals of dEta / dDelta
   float part_grad[2][2 * C];   // dEta / dDelta CTA partials (peers read), by tile parity
@@ -198,10 +198,12 @@ __device__ __forceinline__ void st2(float* p, float2 v) { *reinterpret_cast<floa
 // place (to conj(a) lam) and returns the write-path dx of the content; returns the token's dEta /
 // dDelta contributions in ve / vd (per lane) and adds the per-mode parameter terms to fa.
 template <bool kFast>
-__device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0, float2 tau1,
-                                          Cx2& lam, Cx2 pv, float2 cx, float2 cy, float2& ve, float2& vd,
-                                          float2 (&fa)[5]) {
-  const TokenCoef2 k = token_coef2<kFast>(mc, E, delta, tau0, tau1);
+__device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& tc, Cx2& lam, Cx2 pv, float2 cx,
+                                          float2 cy, float2& ve, float2& vd, float2 (&fa)[5]) {
+  const float2 delta = make_float2(tc.ed.z, tc.ed.w), tau0 = make_float2(tc.tau.x, tc.tau.y),
+               tau1 = make_float2(tc.tau.z, tc.tau.w);
+  // with a reset the transition (k.a) is zero, so every transition-gradient term below vanishes
+  const TokenCoef2 k = token_coef2<kFast>(mc, tc);
   const float2 gar = fma2(lam.re, pv.re, mul2(lam.im, pv.im));   // Re(lam conj(h_prev))
   const float2 gai = sub2(mul2(lam.im, pv.re), mul2(lam.re, pv.im));  // Im(lam conj(h_prev))
   const float2 pg = sub2(mul2(gai, k.a.re), mul2(gar, k.a.im));
@@ -277,20 +279,20 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
     {
       const TIO* xs = static_cast<const TIO*>(p.x) + row0;
       const TIO* ds = static_cast<const TIO*>(p.dy) + row0;
-      const float4* cs = p.ctl + 2 * (b * T + r.t0);
+      const TokenCtl* cs = p.ctl + b * T + r.t0;
       const float2* hs = c > 0 ? p.carry + (b * chunks + (c - 1)) * (long long)M + mbase : nullptr;
       const float2* ks = c < chunks - 1 ? p.kout + (b * chunks + (c + 1)) * (long long)M + mbase : nullptr;
       if (p.use_tma) {
         if (tid == 0) {
           fence_proxy_async_smem();
-          unsigned bytes = 2u * act_box_bytes<TIO, C, kBwdModes>() + 32u * (unsigned)r.nvalid;
+          unsigned bytes = 2u * act_box_bytes<TIO, C, kBwdModes>() + (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
           if (hs != nullptr) bytes += (unsigned)ncols * 8u;
           if (ks != nullptr) bytes += (unsigned)ncols * 8u;
           mbar_arrive_expect_tx(&S.bar, bytes);
           const int row = (int)(b * T + r.t0);
           tma_load_3d(&S.x[0][0][0], &p.map_x, mbase, 0, row, &S.bar);
           tma_load_3d(&S.dy[0][0][0], &p.map_dy, mbase, 0, row, &S.bar);
-          bulk_copy_g2s(&S.ctl[0][0], cs, 32u * (unsigned)r.nvalid, &S.bar);
+          bulk_copy_g2s(&S.ctl[0], cs, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar);
           if (hs != nullptr) bulk_copy_g2s(&S.hin[0], hs, (unsigned)ncols * 8u, &S.bar);
           if (ks != nullptr) bulk_copy_g2s(&S.kin[0], ks, (unsigned)ncols * 8u, &S.bar);
         }
@@ -298,7 +300,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       } else {
         load_act_rows<TIO, kBwdModes>(xs, W, M, mbase, r.nvalid, S.x, kGradThreads);
         load_act_rows<TIO, kBwdModes>(ds, W, M, mbase, r.nvalid, S.dy, kGradThreads);
-        for (int t = tid; t < 2 * r.nvalid; t += kGradThreads) (&S.ctl[0][0])[t] = cs[t];
+        for (int t = tid; t < r.nvalid; t += kGradThreads) S.ctl[t] = cs[t];
         for (int mm = tid; mm < ncols; mm += kGradThreads) {
           if (hs != nullptr) S.hin[mm] = hs[mm];
           if (ks != nullptr) S.kin[mm] = ks[mm];
@@ -327,11 +329,9 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
 #pragma unroll kU
         for (int t = 0; t < C; ++t) {
           if (kFull || t < nvalid) {
-            const float4 c0 = S.ctl[t][0], c1 = S.ctl[t][1];
             const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
             const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
-            const TokenCoef2 k = token_coef2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
-                                                    make_float2(c1.x, c1.y), make_float2(c1.z, c1.w));
+            const TokenCoef2 k = token_coef2<kFast>(mc, S.ctl[t]);
             h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
             Pair<TIO>::store(&S.hr[t][2 * tid], h.re.x, h.re.y);
             Pair<TIO>::store(&S.hi[t][2 * tid], h.im.x, h.im.y);
@@ -367,7 +367,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
           const int t = t1 - u;
           float ve = 0.0f, vd = 0.0f;
           if (kFull || t < nvalid) {
-            const float4 c0 = S.ctl[t][0], c1 = S.ctl[t][1];
+            const TokenCtl& tc = S.ctl[t];
             lam.re = add2(lam.re, Pair<TIO>::load(&S.dy[t][0][2 * tid]));
             lam.im = add2(lam.im, Pair<TIO>::load(&S.dy[t][1][2 * tid]));
             const Cx2 pv = t > 0 ? cx2(Pair<TIO>::load(&S.hr[t - 1][2 * tid]), Pair<TIO>::load(&S.hi[t - 1][2 * tid]))
@@ -375,9 +375,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
             const float2 cx = Pair<TIO>::load(&S.x[t][0][2 * tid]);
             const float2 cy = Pair<TIO>::load(&S.x[t][1][2 * tid]);
             float2 ve2, vd2;
-            const Cx2 dxc = grad_step2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
-                                              make_float2(c1.x, c1.y), make_float2(c1.z, c1.w), lam, pv, cx, cy,
-                                              ve2, vd2, fa);
+            const Cx2 dxc = grad_step2<kFast>(mc, tc, lam, pv, cx, cy, ve2, vd2, fa);
             // h[t] was last read as the previous state at step t+1: its slots now hold the
             // write-path dx
             Pair<TIO>::store(&S.hr[t][2 * tid], dxc.re.x, dxc.re.y);
@@ -420,9 +418,9 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       }
       __syncthreads();
       if (tid < C) {
-        const float4 k4 = ctl4(S.ctl[tid]);
-        const float dp1 = tid < nvalid ? S.tot[tid] * kLn16 * fmaf(-k4.w, k4.w, 1.0f) : 0.0f;
-        const float dp0 = tid < nvalid ? S.tot[C + tid] * kHalfPi * fmaf(-k4.z, k4.z, 1.0f) : 0.0f;
+        const float tau0 = S.ctl[tid].tau.x, tau1 = S.ctl[tid].tau.z;
+        const float dp1 = tid < nvalid ? S.tot[tid] * kLn16 * fmaf(-tau1, tau1, 1.0f) : 0.0f;
+        const float dp0 = tid < nvalid ? S.tot[C + tid] * kHalfPi * fmaf(-tau0, tau0, 1.0f) : 0.0f;
         S.dp[tid] = make_float4(dp0, dp0, dp1, dp1);
       }
       __syncthreads();

@@ -26,7 +26,7 @@ constexpr int kFwdModes = 2 * kFwdThreads;  // modes per CTA
 template <typename TIO, int C>
 struct SumSmem {
   TIO x[2][C][2][kFwdModes];  // [buffer][token][re|im][mode]
-  float4 ctl[C][2];           // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
+  TokenCtl ctl[C];
   float part[2][2 * C];       // this CTA's projection partials (peers read), by tile parity
   float warp_part[kFwdThreads / 32][2 * C];
   unsigned long long bar[2];
@@ -35,7 +35,7 @@ struct SumSmem {
 template <typename TIO, int C>
 struct RepSmem {
   TIO x[2][C][2][kFwdModes];
-  float4 ctl[2][C][2];       // per token (E, E, delta, delta), (tau0, tau0, tau1, tau1)
+  TokenCtl ctl[2][C];
   float2 hin[2][kFwdModes];  // carried-in state of the tile's modes
   unsigned long long bar[2];
 };
@@ -47,7 +47,8 @@ struct FwdParams {
   MixerParamPtrs pp;
   const float* h0_r;
   const float* h0_i;
-  float4* ctl;          // [B, T, 2] token controls as pairs (E, E, delta, delta), (tau0, tau0, tau1, tau1)
+  TokenCtl* ctl;        // [B, T] token controls (written by the summary)
+  const unsigned char* reset;  // [B, T] 1 where a segment reset zeroes the transition, or null
   const float2* carry;  // [B, chunks, M] inclusive chunk states (replay input)
   float4* agg;          // [B, chunks, Mp] chunk aggregates (P, Q)
   LaunchState* ls;
@@ -242,14 +243,13 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
         const float tau0 = tanh_accurate(p0 + bias0);
         const float tau1 = tanh_accurate(p1 + bias1);
         const float E = expf(kLn16 * tau1), delta = kHalfPi * tau0;
-        const float4 c0 = make_float4(E, E, delta, delta), c1 = make_float4(tau0, tau0, tau1, tau1);
-        S.ctl[tid][0] = c0;
-        S.ctl[tid][1] = c1;
-        if (g == 0 && tid < r.nvalid) {
-          float4* cp = p.ctl + 2 * (r.b * T + r.t0 + tid);
-          cp[0] = c0;
-          cp[1] = c1;
-        }
+        const float keep = (p.reset != nullptr && tid < r.nvalid && p.reset[r.b * T + r.t0 + tid]) ? 0.0f : 1.0f;
+        TokenCtl tc;
+        tc.ed = make_float4(E, E, delta, delta);
+        tc.tau = make_float4(tau0, tau0, tau1, tau1);
+        tc.keep = make_float4(keep, keep, 0.0f, 0.0f);
+        S.ctl[tid] = tc;
+        if (g == 0 && tid < r.nvalid) p.ctl[r.b * T + r.t0 + tid] = tc;
       }
       __syncthreads();
     }
@@ -262,11 +262,9 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
 #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < r.nvalid) {
-          const float4 c0 = S.ctl[t][0], c1 = S.ctl[t][1];
           const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-          const TokenCoef2 k = token_coef2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
-                                                  make_float2(c1.x, c1.y), make_float2(c1.z, c1.w));
+          const TokenCoef2 k = token_coef2<kFast>(mc, S.ctl[t]);
           Q = cfma2(k.a, Q, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
           P = cmul2(k.a, P);
         }
@@ -314,21 +312,21 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
   auto issue = [&](long long i, int buf) {
     const TileRef r = tile_ref(i, B, T, C);
     const TIO* src = static_cast<const TIO*>(p.x) + (r.b * T + r.t0) * W;
-    const float4* csrc = p.ctl + 2 * (r.b * T + r.t0);
+    const TokenCtl* csrc = p.ctl + r.b * T + r.t0;
     const float2* hsrc = r.c > 0 ? p.carry + (r.b * p.chunks + (r.c - 1)) * (long long)M + mbase : nullptr;
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        unsigned bytes = act_box_bytes<TIO, C, kFwdModes>() + 32u * (unsigned)r.nvalid;
+        unsigned bytes = act_box_bytes<TIO, C, kFwdModes>() + (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
         if (hsrc != nullptr) bytes += (unsigned)ncols * 8u;
         mbar_arrive_expect_tx(&S.bar[buf], bytes);
         tma_load_3d(&S.x[buf][0][0][0], &p.map_x, mbase, 0, (int)(r.b * T + r.t0), &S.bar[buf]);
-        bulk_copy_g2s(&S.ctl[buf][0][0], csrc, 32u * (unsigned)r.nvalid, &S.bar[buf]);
+        bulk_copy_g2s(&S.ctl[buf][0], csrc, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar[buf]);
         if (hsrc != nullptr) bulk_copy_g2s(&S.hin[buf][0], hsrc, (unsigned)ncols * 8u, &S.bar[buf]);
       }
     } else {
       load_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], kFwdThreads);
-      for (int t = tid; t < 2 * r.nvalid; t += kFwdThreads) (&S.ctl[buf][0][0])[t] = csrc[t];
+      for (int t = tid; t < r.nvalid; t += kFwdThreads) S.ctl[buf][t] = csrc[t];
       if (hsrc != nullptr)
         for (int mm = tid; mm < ncols; mm += kFwdThreads) S.hin[buf][mm] = hsrc[mm];
     }
@@ -348,7 +346,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
       __syncthreads();
     }
     const TIO(*xt)[2][kFwdModes] = S.x[buf];
-    const float4(*ctl)[2] = S.ctl[buf];
+    const TokenCtl* ctl = S.ctl[buf];
     float2 h0 = make_float2(0.0f, 0.0f), h1 = h0;
     if (r.c > 0) {
       if (act0) h0 = S.hin[buf][2 * tid];
@@ -365,11 +363,9 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
 #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < r.nvalid) {
-          const float4 c0 = ctl[t][0], c1 = ctl[t][1];
           const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-          const TokenCoef2 k = token_coef2<kFast>(mc, make_float2(c0.x, c0.y), make_float2(c0.z, c0.w),
-                                                  make_float2(c1.x, c1.y), make_float2(c1.z, c1.w));
+          const TokenCoef2 k = token_coef2<kFast>(mc, ctl[t]);
           h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
           store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, make_float2(h.re.x, h.im.x),
                                   make_float2(h.re.y, h.im.y));

@@ -6,9 +6,12 @@ and setters as sparc.py:58-123. Every call runs the sm_100a kernels of libsparc_
 its C ABI; the backend setters are validated like the reference's but select nothing, since
 there is exactly one code path.
 
-Extension over the reference: ``forward(..., state=(h_r, h_i))`` starts the recurrence from a
-given state (the semantics of the reference's tiled serial scan with an initial state,
-backward/scan.py:971-1070), and its gradient flows back to that state.
+Extensions over the reference module (both follow the reference's tiled serial scan,
+``sparc_training_scan_dispatch`` backward/scan.py:1754-1818 -> forward/scan.py:807-854):
+``forward(..., state=(h_r, h_i))`` starts the recurrence from a given state, and its gradient
+flows back to that state; ``forward(..., segment_pos=pos)`` restarts the recurrence at every token
+with ``pos == 0`` (packed sequences), ``reset_first=True`` at the first token when no
+``segment_pos`` is given (common.py:219-268).
 """
 from __future__ import annotations
 
@@ -38,7 +41,7 @@ class _SparcMixerFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, nu_log, theta_log, phase_direction, radial_direction, write_log_gain,
                 energy_response, write_phase_response, write_radial_response, h0_r, h0_i,
-                max_spin, inject_tile):
+                max_spin, inject_tile, reset=None):
         L = _lib.lib()
         B, T, W = x.shape
         M = W // 2
@@ -52,7 +55,7 @@ class _SparcMixerFunction(torch.autograd.Function):
         y = torch.empty_like(x)
         chunks = L.sparc_mixer_carry_chunks(T, dt)
         carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
-        controls = torch.empty((B, T, 8), dtype=torch.float32, device=dev)
+        controls = torch.empty((B, T, 12), dtype=torch.float32, device=dev)
         last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
         last_i = torch.empty((B, M), dtype=torch.float32, device=dev)
         nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
@@ -62,7 +65,7 @@ class _SparcMixerFunction(torch.autograd.Function):
         a = _lib.MixerFwdArgs(
             x.data_ptr(), y.data_ptr(), *[p.data_ptr() for p in params],
             _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
-            last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(),
+            last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
             ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin, _lib.deterministic(),
             1 if inject_tile is not None else 0, inject_tile if inject_tile is not None else 0)
         _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
@@ -110,14 +113,31 @@ class _SparcMixerFunction(torch.autograd.Function):
         _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_backward")
         return (dx, *[g[n] for n in _PARAMS],
-                gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None)
+                gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None)
 
 
-def sparc_mixer(x, params, state=None, max_spin: int = 0, inject_unpublished_tile=None):
+def reset_mask(segment_pos, reset_first: bool, shape, device):
+    """The [B, T] byte mask of tokens whose transition is zeroed: segment_pos == 0 where
+    segment_pos is given, else the first token when reset_first (common.py:219-268)."""
+    B, T = shape
+    if segment_pos is not None:
+        if segment_pos.shape != (B, T):
+            raise ValueError(f"segment_pos must have shape [batch, length] = {(B, T)}")
+        return (segment_pos.to(device) == 0).to(torch.uint8).contiguous()
+    if reset_first:
+        m = torch.zeros((B, T), dtype=torch.uint8, device=device)
+        m[:, 0] = 1
+        return m
+    return None
+
+
+def sparc_mixer(x, params, state=None, max_spin: int = 0, inject_unpublished_tile=None,
+                segment_pos=None, reset_first: bool = False):
     """Functional form: (y, (last_r, last_i)) for parameters given as a mapping."""
     h0_r, h0_i = (None, None) if state is None else state
+    reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
     y, lr, li = _SparcMixerFunction.apply(
-        x, *[params[n] for n in _PARAMS], h0_r, h0_i, int(max_spin), inject_unpublished_tile)
+        x, *[params[n] for n in _PARAMS], h0_r, h0_i, int(max_spin), inject_unpublished_tile, reset)
     return y, (lr, li)
 
 
@@ -183,7 +203,8 @@ class SPARCMixer(nn.Module):
     def _params(self):
         return {n: getattr(self, n) for n in _PARAMS}
 
-    def forward(self, x: torch.Tensor, return_cache: bool = False, state=None):
+    def forward(self, x: torch.Tensor, return_cache: bool = False, state=None, segment_pos=None,
+                reset_first: bool = False):
         _lib.require_cuda(x, "x")
         if x.dim() != 3 or x.shape[-1] != self.width:
             raise ValueError(f"SPARCMixer expects x of shape [batch, length, {self.width}]")
@@ -193,7 +214,8 @@ class SPARCMixer(nn.Module):
             B = x.shape[0]
             if state[0].shape != (B, self.modes) or state[1].shape != (B, self.modes):
                 raise ValueError("initial SPARC states must have shape [B, M]")
-        y, cache = sparc_mixer(x.contiguous(), self._params(), state, self.max_spin)
+        y, cache = sparc_mixer(x.contiguous(), self._params(), state, self.max_spin,
+                               segment_pos=segment_pos, reset_first=reset_first)
         return y, (cache if return_cache else None)
 
     # the reference's backend switches (sparc.py:93-120): validated, one code path behind them

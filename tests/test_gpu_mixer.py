@@ -41,9 +41,9 @@ def _random_params(W, seed):
     return {k: np.asarray(v, dtype=np.float32).astype(np.float64) for k, v in p.items()}
 
 
-def _run(m, x, dy, state=None, dlast=None):
+def _run(m, x, dy, state=None, dlast=None, **kw):
     x = x.clone().requires_grad_(True)
-    y, cache = m(x, return_cache=True, state=state)
+    y, cache = m(x, return_cache=True, state=state, **kw)
     loss = (y.double() * dy.double()).sum()
     if dlast is not None:
         loss = loss + (cache[0].double() * dlast[0]).sum() + (cache[1].double() * dlast[1]).sum()
@@ -138,6 +138,89 @@ def test_initial_state_and_last_state_grads():
     assert O.rel_l2(cache[0].double().cpu().numpy(), last_ref[0]) < 1e-4
     assert O.rel_l2(st[0].grad.double().cpu().numpy(), g_ref["h0_r"]) < 1e-3
     assert O.rel_l2(st[1].grad.double().cpu().numpy(), g_ref["h0_i"]) < 1e-3
+
+
+def _segment_positions(B, T, gen, n_starts=4):
+    """Position within its segment for every token (0 where a segment starts)."""
+    pos = torch.empty(B, T, dtype=torch.int64)
+    for b in range(B):
+        starts = {int(v) for v in torch.randint(1, T, (n_starts,), generator=gen)}
+        if b == 0:
+            starts.add(0)  # row 0 also restarts at its first token (h0 ignored there)
+        last = -1  # rows without a start at t = 0 continue the sequence h0 came from
+        for t in range(T):
+            if t in starts:
+                last = t
+            pos[b, t] = t - last
+    return pos
+
+
+@pytest.mark.parametrize("dtype,B,T,W,fwd_tol,bwd_tol", [
+    (torch.float32, 3, 100, 64, 1e-4, 1e-3),
+    (torch.float32, 2, 37, 10, 1e-4, 1e-3),
+    (torch.bfloat16, 2, 300, 512, 2e-2, 2e-2),
+])
+def test_segment_resets_match_oracle(dtype, B, T, W, fwd_tol, bwd_tol):
+    """segment_pos == 0 restarts the recurrence (the reference's tiled serial scan semantics),
+    with h0 and a gradient on the last state, forward and backward."""
+    params = _random_params(W, 21 + W)
+    gen = torch.Generator().manual_seed(22 + W)
+    M = W // 2
+    x = torch.randn(B, T, W, generator=gen).to(dtype)
+    dy = torch.randn(B, T, W, generator=gen).to(dtype).double()
+    state = (torch.randn(B, M, generator=gen) * 0.5, torch.randn(B, M, generator=gen) * 0.5)
+    dlast = (torch.randn(B, M, generator=gen).double(), torch.randn(B, M, generator=gen).double())
+    pos = _segment_positions(B, T, gen)
+    reset = (pos == 0).numpy()
+    assert reset.sum() >= B  # every row restarts somewhere
+    P = O.Params.from_mapping(params)
+    xo = x.double().numpy()
+    h0 = (state[0].double().numpy(), state[1].double().numpy())
+    gl = (dlast[0].numpy(), dlast[1].numpy())
+    y_ref, last_ref, _ = O.sparc_forward(xo, P, h0=h0, reset=reset)
+    g_ref = O.sparc_backward(xo, P, dy.numpy(), h0=h0, grad_last=gl, reset=reset)
+    m = _module(params, W)
+    st = (state[0].cuda().requires_grad_(True), state[1].cuda().requires_grad_(True))
+    y, cache, g = _run(m, x.cuda(), dy.cuda(), state=st, dlast=(dlast[0].cuda(), dlast[1].cuda()),
+                       segment_pos=pos.cuda())
+    _compare(y, g, y_ref, g_ref, fwd_tol, bwd_tol, f"resets {dtype} B{B} T{T} W{W}")
+    assert O.rel_l2(cache[0].double().cpu().numpy(), last_ref[0]) < fwd_tol
+    assert O.rel_l2(st[0].grad.double().cpu().numpy(), g_ref["h0_r"]) < bwd_tol
+    assert O.rel_l2(st[1].grad.double().cpu().numpy(), g_ref["h0_i"]) < bwd_tol
+
+
+def test_segment_resets_golden(golden):
+    """The module with h0 and segment_pos reproduces the reference's own tiled serial scan
+    (_SPARCTiledSerialScan, run by the fixture generator) on the same inputs."""
+    d = golden("tiled_h0_reset")
+    params = {k: d["p_" + k] for k in O.PARAM_NAMES}
+    W = d["x"].shape[-1]
+    m = _module(params, W)
+    x = torch.as_tensor(d["x"], dtype=torch.float32).cuda()
+    st = (torch.as_tensor(d["h0_r"]).float().cuda(), torch.as_tensor(d["h0_i"]).float().cuda())
+    with torch.no_grad():
+        y, (lr, li) = m(x, return_cache=True, state=st, segment_pos=torch.as_tensor(d["segment_pos"]).cuda())
+    ref = np.maximum(np.concatenate((d["out_r"], d["out_i"]), axis=-1), 0.0)
+    assert O.rel_l2(y.double().cpu().numpy(), ref) < 1e-4
+    assert O.rel_l2(lr.double().cpu().numpy(), d["last_r"]) < 1e-4
+    assert O.rel_l2(li.double().cpu().numpy(), d["last_i"]) < 1e-4
+
+
+def test_reset_first_ignores_the_initial_state():
+    """reset_first restarts at t = 0 (the reference's RESET_FIRST): the output and the last state
+    do not depend on h0, and equal segment_pos with a single segment."""
+    params = _random_params(64, 5)
+    m = _module(params, 64)
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 50, 64, generator=gen).cuda()
+    st = (torch.randn(2, 32, generator=gen).cuda(), torch.randn(2, 32, generator=gen).cuda())
+    pos = torch.arange(50).repeat(2, 1).cuda()
+    with torch.no_grad():
+        y0, c0 = m(x, return_cache=True)
+        y1, c1 = m(x, return_cache=True, state=st, reset_first=True)
+        y2, c2 = m(x, return_cache=True, state=st, segment_pos=pos)
+    assert torch.allclose(y1, y0, rtol=1e-5, atol=1e-6) and torch.allclose(c1[0], c0[0], rtol=1e-5, atol=1e-6)
+    assert torch.equal(y1, y2) and torch.equal(c1[1], c2[1])
 
 
 def test_decode_matches_oracle_and_sequence(golden):
