@@ -68,13 +68,20 @@ extern "C" {
  * h_t = a_t h_{t-1} + b_t over M = width/2 complex modes, with a_t, b_t computed from x_t
  * and the parameters. `carry` receives the state at the end of every chunk of
  * sparc_mixer_chunk_tokens(dtype) tokens ([batch, sparc_mixer_carry_chunks(length, dtype), M] complex,
- * interleaved real/imag float32) and `controls` the per-token controls ([batch, length, 12]
- * float32: e^eta, e^eta, delta, delta, tanh p0, tanh p0, tanh p1, tanh p1, keep, keep, 0, 0, with
- * keep 0 at a reset token); the backward needs both, and y. h0 (initial state) and last (final
+ * interleaved real/imag float32) and `controls` the per-token controls ([batch, length,
+ * sparc_mixer_controls_floats()] float32: e^eta, delta, tanh p0, tanh p1, keep (0 at a reset
+ * token), the block's norm scale and the raw projections, laid out as pairs for the kernels);
+ * the backward needs both, and y. h0 (initial state) and last (final
  * state) are optional pairs (NULL, NULL). `reset` (optional, [batch, length] bytes) marks the
  * tokens where a new segment starts: there the transition is zero, so the state restarts from
  * the token's write, as with segment_pos == 0 (or reset_first at t = 0) in the reference's
  * tiled serial scan (forward/scan.py:807-854, common.py:219-268). */
+/* Block mode (norm_weight given): one layer of the config-5 stack, out = x + relu([Re h, Im h])
+ * where the mixer runs on n = RMSNorm(x) = x * r * norm_weight, r = (mean(x^2) + norm_eps)^(-1/2)
+ * per token, computed inside the mixer kernels (no separate norm or residual pass); y receives
+ * `out`, and relu_mask the bits of relu(h) > 0 that the backward needs in place of y. The
+ * backward then returns the block input's gradient in dx (the residual path included) and the
+ * norm weight's in grad_norm_weight. */
 typedef struct SparcMixerFwdArgs {
   const void* x;                       /* [batch, length, width]  activations (dtype) */
   void* y;                             /* [batch, length, width]  output (dtype) */
@@ -90,8 +97,11 @@ typedef struct SparcMixerFwdArgs {
   float* last_r;                       /* [batch, M] or NULL */
   float* last_i;                       /* [batch, M] or NULL */
   float* carry;                        /* [batch, chunks, M, 2] */
-  float* controls;                     /* [batch, length, 12] */
+  float* controls;                     /* [batch, length, sparc_mixer_controls_floats()] */
   const unsigned char* reset;          /* [batch, length] (nonzero = segment start) or NULL */
+  const float* norm_weight;            /* [width]: the call is a block (below), or NULL */
+  float norm_eps;                      /* block: RMSNorm epsilon */
+  unsigned* relu_mask;                 /* block: [batch, length, sparc_mixer_mask_words(width)] out */
   void* workspace;
   size_t workspace_bytes;
   long long batch;
@@ -128,6 +138,9 @@ typedef struct SparcMixerBwdArgs {
   float* grad_h0_i;
   const float* carry;                  /* the forward's carry output */
   const float* controls;               /* the forward's controls output */
+  const float* norm_weight;            /* block: as given to the forward, else NULL */
+  const unsigned* relu_mask;           /* block: the forward's relu_mask output */
+  float* grad_norm_weight;             /* block: [width] */
   float* grad_nu_log;                  /* [M] */
   float* grad_theta_log;               /* [M] */
   float* grad_phase_direction;         /* [width + 1] */
@@ -209,6 +222,10 @@ const char* sparc_last_error(void);
 
 long long sparc_mixer_chunk_tokens(int dtype);
 long long sparc_mixer_carry_chunks(long long length, int dtype);
+/* Floats per token of the forward's controls output (16). */
+int sparc_mixer_controls_floats(void);
+/* 32-bit words per token of a block's relu_mask (four per 64 modes, whole CTAs of 256 modes). */
+int sparc_mixer_mask_words(int width);
 size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype);
 int sparc_mixer_forward(const SparcMixerFwdArgs* args, void* stream);
 int sparc_mixer_backward(const SparcMixerBwdArgs* args, void* stream);

@@ -319,6 +319,34 @@ def rms_norm(x, weight, eps=1e-6):
     return x * r * _f64(weight)
 
 
+def block_forward(x, P: Params, norm_weight, eps=1e-6, h0=None, reset=None):
+    """One config-5 stack block: out = x + SPARCMixer(RMSNorm(x)), RMSNorm(x) = x r w with
+    r = (mean(x^2) + eps)^(-1/2) per token (the stack's norm; no reference counterpart, the
+    reference ships the mixer only). Returns (out, (last_r, last_i))."""
+    x = _f64(x)
+    n = rms_norm(x, norm_weight, eps)
+    y, last, _ = sparc_forward(n, P, h0, reset)
+    return x + y, last
+
+
+def block_backward(x, P: Params, norm_weight, d_out, eps=1e-6, h0=None, grad_last=None, reset=None):
+    """Adjoint of block_forward: the mixer's adjoint (sparc_backward) at the normalised input,
+    then RMSNorm's, plus the residual path. Returns the mixer's gradients with 'x' replaced by
+    the block input's gradient and 'norm_weight' added."""
+    x = _f64(x)
+    d_out = _f64(d_out)
+    w = _f64(norm_weight)
+    W = x.shape[-1]
+    r = 1.0 / np.sqrt((x * x).mean(-1, keepdims=True) + eps)
+    n = x * r * w
+    g = sparc_backward(n, P, d_out, h0, grad_last, reset)
+    dn = g["x"]
+    s = (x * w * dn).sum(-1, keepdims=True)
+    g["x"] = d_out + r * w * dn - (r ** 3 / W) * x * s
+    g["norm_weight"] = (dn * x * r).sum((0, 1))
+    return g
+
+
 def init_params(width: int, rand_fn):
     """SPARCMixer.__init__ parameter construction, sparc.py:59-88.
 

@@ -5,7 +5,8 @@
 All compute runs in the sm_100a kernels of ``libsparc_b200.so`` (C ABI in
 ``include/sparc_b200.h``), loaded through ctypes on first use. There is no CPU path.
 """
-from .mixer import SPARCMixer, sparc_decode_step, sparc_mixer
+from .mixer import SPARCMixer, sparc_block, sparc_decode_step, sparc_mixer
+from .stack import SPARCBlock, SPARCStack
 from .real import real_chunk_scan, real_scan, real_scan_with_last
 from . import _lib
 
@@ -26,5 +27,5 @@ def check_status(clear: bool = True) -> None:
             raise RuntimeError(f"sparc_b200: a chunk-carry wait timed out (status {st:#x})")
 
 
-__all__ = ["SPARCMixer", "sparc_mixer", "sparc_decode_step", "real_scan", "real_chunk_scan",
-           "real_scan_with_last", "check_status", "library_path"]
+__all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack", "sparc_decode_step",
+           "real_scan", "real_chunk_scan", "real_scan_with_last", "check_status", "library_path"]

@@ -33,6 +33,7 @@ class MixerFwdArgs(ctypes.Structure):
         ("write_log_gain", _vp), ("write_phase_response", _vp), ("write_radial_response", _vp),
         ("h0_r", _vp), ("h0_i", _vp), ("last_r", _vp), ("last_i", _vp), ("carry", _vp),
         ("controls", _vp), ("reset", _vp),
+        ("norm_weight", _vp), ("norm_eps", ctypes.c_float), ("relu_mask", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint), ("deterministic", ctypes.c_int),
@@ -47,6 +48,7 @@ class MixerBwdArgs(ctypes.Structure):
         ("write_log_gain", _vp), ("write_phase_response", _vp), ("write_radial_response", _vp),
         ("h0_r", _vp), ("h0_i", _vp), ("grad_last_r", _vp), ("grad_last_i", _vp),
         ("grad_h0_r", _vp), ("grad_h0_i", _vp), ("carry", _vp), ("controls", _vp),
+        ("norm_weight", _vp), ("relu_mask", _vp), ("grad_norm_weight", _vp),
         ("grad_nu_log", _vp), ("grad_theta_log", _vp), ("grad_phase_direction", _vp),
         ("grad_radial_direction", _vp), ("grad_write_log_gain", _vp), ("grad_energy_response", _vp),
         ("grad_write_phase_response", _vp), ("grad_write_radial_response", _vp),
@@ -90,6 +92,8 @@ SIGNATURES = {
     "sparc_last_error": (ctypes.c_char_p, []),
     "sparc_mixer_chunk_tokens": (_ll, [ctypes.c_int]),
     "sparc_mixer_carry_chunks": (_ll, [_ll, ctypes.c_int]),
+    "sparc_mixer_mask_words": (ctypes.c_int, [ctypes.c_int]),
+    "sparc_mixer_controls_floats": (ctypes.c_int, []),
     "sparc_mixer_workspace_bytes": (ctypes.c_size_t, [_ll, _ll, ctypes.c_int, ctypes.c_int]),
     "sparc_mixer_forward": (ctypes.c_int, [ctypes.POINTER(MixerFwdArgs), _vp]),
     "sparc_mixer_backward": (ctypes.c_int, [ctypes.POINTER(MixerBwdArgs), _vp]),

@@ -137,6 +137,7 @@ struct ModeConst2 {
   float2 nu, nl2e_neg, theta, ct, st, gconst, stat, wpr, wrr;
   float2 wpr_h, wrr_l;  // wpr * 2/pi, wrr / ln 16 (the gate's chain factors in the backward)
   float2 d0r, d0i, d1r, d1i;
+  float2 wre, wim;      // RMSNorm weight at the modes' real / imaginary columns (1 outside a block)
 };
 __device__ __forceinline__ ModeConst2 pair_modes(const ModeConst& a, const ModeConst& b) {
   ModeConst2 m;
@@ -155,7 +156,14 @@ __device__ __forceinline__ ModeConst2 pair_modes(const ModeConst& a, const ModeC
   m.d0i = make_float2(a.d0i, b.d0i);
   m.d1r = make_float2(a.d1r, b.d1r);
   m.d1i = make_float2(a.d1i, b.d1i);
+  m.wre = m.wim = make_float2(1.0f, 1.0f);
   return m;
+}
+
+// The RMSNorm weight of a block at the thread's modes (columns m, m+1 and M+m, M+m+1).
+__device__ __forceinline__ void load_norm_weight(ModeConst2& mc, const float* w, int m0, int M, bool a0, bool a1) {
+  mc.wre = make_float2(a0 ? w[m0] : 0.0f, a1 ? w[m0 + 1] : 0.0f);
+  mc.wim = make_float2(a0 ? w[M + m0] : 0.0f, a1 ? w[M + m0 + 1] : 0.0f);
 }
 
 // Per-token controls as the forward saves them (48 bytes): every value twice, so that a
@@ -164,9 +172,10 @@ __device__ __forceinline__ ModeConst2 pair_modes(const ModeConst& a, const ModeC
 struct TokenCtl {
   float4 ed;    // E, E, delta, delta   (E = e^eta)
   float4 tau;   // tau0, tau0, tau1, tau1
-  float4 keep;  // keep, keep, 0, 0
+  float4 keep;  // keep, keep, r, r     (r: the token's RMSNorm scale in a block, else 1)
+  float4 proj;  // q0, q1, 0, 0         (the projections before the scale r: the norm's backward)
 };
-static_assert(sizeof(TokenCtl) == 48, "token controls are three 16-byte words");
+static_assert(sizeof(TokenCtl) == 64, "token controls are four 16-byte words");
 
 struct TokenCoef2 {
   float2 z, rho;
@@ -523,6 +532,7 @@ struct ReduceParams {
   float* g_energy;
   float* g_phase_dir;   // [W+1]
   float* g_radial_dir;  // [W+1]
+  float* g_norm_w;      // [W] (block) or null
 };
 
 // grid (ceil(Mp/32), kPartModes + 1), block (32, kReduceWarps). Rows q < kPartModes: warp w sums
@@ -578,7 +588,9 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
       case 5: r.g_phase_dir[m] = (float)t; break;
       case 6: r.g_phase_dir[r.M + m] = (float)t; break;
       case 7: r.g_radial_dir[m] = (float)t; break;
-      default: r.g_radial_dir[r.M + m] = (float)t; break;
+      case 8: r.g_radial_dir[r.M + m] = (float)t; break;
+      case 9: if (r.g_norm_w) r.g_norm_w[m] = (float)t; break;
+      default: if (r.g_norm_w) r.g_norm_w[r.M + m] = (float)t; break;
     }
   }
 }
@@ -586,6 +598,7 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
 // ------------------------------------------------------------------------------ host side
 struct Plan {
   int dtype, C, chunks;
+  bool block;              // RMSNorm + mixer + residual kernels
   long long tiles;         // B * chunks
   int G, Mp;               // CTAs of 256 modes per tile; modes padded to G * 256
   bool vec, tma;
@@ -647,15 +660,26 @@ template <typename TIO>
 struct Kernels {
   static constexpr bool kFast = std::is_same<TIO, __nv_bfloat16>::value;
   static constexpr int C = chunk_for(kFast ? SPARC_DTYPE_BF16 : SPARC_DTYPE_F32);
-  static const void* sum() { return (const void*)mixer_fwd_summary_kernel<TIO, C, kFast>; }
-  static const void* rep(bool vec) {
-    return vec ? (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, true>
-               : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false>;
+  // block = RMSNorm + mixer + residual (norm weight given)
+  static const void* sum(bool block) {
+    return block ? (const void*)mixer_fwd_summary_kernel<TIO, C, kFast, true>
+                 : (const void*)mixer_fwd_summary_kernel<TIO, C, kFast, false>;
   }
-  static const void* rsum() { return (const void*)mixer_bwd_summary_kernel<TIO, C, kFast>; }
-  static const void* grad(bool vec) {
-    return vec ? (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, true>
-               : (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, false>;
+  static const void* rep(bool vec, bool block) {
+    if (block) return vec ? (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, true, true>
+                          : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false, true>;
+    return vec ? (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, true, false>
+               : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false, false>;
+  }
+  static const void* rsum(bool block) {
+    return block ? (const void*)mixer_bwd_summary_kernel<TIO, C, kFast, true>
+                 : (const void*)mixer_bwd_summary_kernel<TIO, C, kFast, false>;
+  }
+  static const void* grad(bool vec, bool block) {
+    if (block) return vec ? (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, true, true>
+                          : (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, false, true>;
+    return vec ? (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, true, false>
+               : (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, false, false>;
   }
   static size_t sum_smem() { return sizeof(SumSmem<TIO, C>); }
   static size_t rep_smem() { return sizeof(RepSmem<TIO, C>); }
@@ -670,19 +694,20 @@ static void plan_kernels(Plan* pl, const void** k) {
   pl->rep_smem = K::rep_smem();
   pl->rsum_smem = K::rsum_smem();
   pl->grad_smem = K::grad_smem();
-  k[0] = K::sum();
-  k[1] = K::rep(pl->vec);
-  k[2] = K::rsum();
-  k[3] = K::grad(pl->vec);
+  k[0] = K::sum(pl->block);
+  k[1] = K::rep(pl->vec, pl->block);
+  k[2] = K::rsum(pl->block);
+  k[3] = K::grad(pl->vec, pl->block);
 }
 
-static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
+static int make_plan(long long B, long long T, int W, int dtype, bool block, Plan* pl) {
   if (B <= 0 || T <= 0 || W <= 0) { set_err("batch, length and width must be positive"); return SPARC_ERR_SHAPE; }
   if (W % 2) { set_err("SPARC rnn_width must be even"); return SPARC_ERR_SHAPE; }
   if (dtype != SPARC_DTYPE_F32 && dtype != SPARC_DTYPE_BF16) { set_err("unsupported dtype"); return SPARC_ERR_DTYPE; }
   const int M = W / 2;
   if (M > 8 * kFwdModes) { set_err("width above 4096 is not supported"); return SPARC_ERR_SHAPE; }
   pl->dtype = dtype;
+  pl->block = block;
   pl->C = chunk_for(dtype);
   pl->chunks = (int)((T + pl->C - 1) / pl->C);
   pl->tiles = B * pl->chunks;
@@ -701,7 +726,7 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
 
   int dev = 0;
   cudaGetDevice(&dev);
-  struct Key { int dev, dtype, G, vec; int sum, rep, rsum, grad, scan; };
+  struct Key { int dev, dtype, G, vec, block; int sum, rep, rsum, grad, scan; };
   static std::mutex mu;
   static Key cache[64];
   static int ncache = 0;
@@ -709,13 +734,13 @@ static int make_plan(long long B, long long T, int W, int dtype, Plan* pl) {
   const Key* hit = nullptr;
   for (int i = 0; i < ncache; ++i) {
     const Key& kk = cache[i];
-    if (kk.dev == dev && kk.dtype == dtype && kk.G == pl->G && kk.vec == (int)pl->vec) hit = &kk;
+    if (kk.dev == dev && kk.dtype == dtype && kk.G == pl->G && kk.vec == (int)pl->vec && kk.block == (int)block) hit = &kk;
   }
   Key key;
   if (hit != nullptr) {
     key = *hit;
   } else {
-    key = Key{dev, dtype, pl->G, (int)pl->vec, 0, 0, 0, 0, 0};
+    key = Key{dev, dtype, pl->G, (int)pl->vec, (int)block, 0, 0, 0, 0, 0};
     key.sum = max_clusters(k[0], pl->G, kFwdThreads, pl->sum_smem);
     key.rep = max_blocks(k[1], kFwdThreads, pl->rep_smem);
     key.rsum = max_blocks(k[2], kBwdThreads, pl->rsum_smem);
@@ -881,7 +906,14 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
   if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->last_r == nullptr) != (a->last_i == nullptr)) {
     set_err("h0 / last pointers must be given in pairs"); return SPARC_ERR_ARG;
   }
+  if (pl.block && (a->relu_mask == nullptr || !(a->norm_eps >= 0.0f))) {
+    set_err("a block (norm_weight given) needs relu_mask and a non-negative norm_eps"); return SPARC_ERR_ARG;
+  }
   FwdParams p;
+  p.norm_w = a->norm_weight;
+  p.norm_eps = a->norm_eps;
+  p.mask = a->relu_mask;
+  p.mask_words = pl.G * 16;
   p.x = a->x;
   p.y = a->y;
   p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
@@ -904,8 +936,8 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
   p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->controls) && aligned16(a->carry) &&
                       act_tensor_map(&p.map_x, a->x, a->dtype, p.B * p.T, p.M, p.W, pl.C) ? 1 : 0;
   const bool bf = a->dtype == SPARC_DTYPE_BF16;
-  const void* ksum = bf ? Kernels<__nv_bfloat16>::sum() : Kernels<float>::sum();
-  const void* krep = bf ? Kernels<__nv_bfloat16>::rep(pl.vec) : Kernels<float>::rep(pl.vec);
+  const void* ksum = bf ? Kernels<__nv_bfloat16>::sum(pl.block) : Kernels<float>::sum(pl.block);
+  const void* krep = bf ? Kernels<__nv_bfloat16>::rep(pl.vec, pl.block) : Kernels<float>::rep(pl.vec, pl.block);
   int rc;
   {
     TimedLaunch tl(kTimeFwdSummary, s);
@@ -940,15 +972,27 @@ long long sparc_mixer_carry_chunks(long long length, int dtype) {
 }
 
 size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype) {
-  Plan pl;
-  if (make_plan(batch, length, width, dtype, &pl) != SPARC_OK) return 0;
-  return ws_layout(pl, batch, width / 2).total;
+  // one size for the plain mixer and the block (their gradient kernels' occupancy may differ)
+  size_t total = 0;
+  for (int block = 0; block < 2; ++block) {
+    Plan pl;
+    if (make_plan(batch, length, width, dtype, block != 0, &pl) != SPARC_OK) return 0;
+    total = std::max(total, ws_layout(pl, batch, width / 2).total);
+  }
+  return total;
+}
+
+int sparc_mixer_controls_floats(void) { return (int)(sizeof(TokenCtl) / sizeof(float)); }
+
+int sparc_mixer_mask_words(int width) {
+  if (width <= 0 || width % 2) return 0;
+  return ((width / 2 + kFwdModes - 1) / kFwdModes) * 16;
 }
 
 int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   Plan pl;
-  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
+  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, a->norm_weight != nullptr, &pl);
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
@@ -958,11 +1002,16 @@ int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
 int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   Plan pl;
-  int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
+  const bool block = a->norm_weight != nullptr;
+  int rc = make_plan(a->batch, a->length, a->width, a->dtype, block, &pl);
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
-  if (!a->x || !a->y || !a->dy || !a->dx || !a->carry || !a->controls || !a->grad_nu_log || !a->grad_theta_log ||
+  if (block ? (a->relu_mask == nullptr || a->grad_norm_weight == nullptr) : a->y == nullptr) {
+    set_err(block ? "a block needs relu_mask and grad_norm_weight" : "the forward's output y is needed");
+    return SPARC_ERR_ARG;
+  }
+  if (!a->x || !a->dy || !a->dx || !a->carry || !a->controls || !a->grad_nu_log || !a->grad_theta_log ||
       !a->grad_phase_direction || !a->grad_radial_direction || !a->grad_write_log_gain ||
       !a->grad_energy_response || !a->grad_write_phase_response || !a->grad_write_radial_response) {
     set_err("null tensor pointer"); return SPARC_ERR_ARG;
@@ -984,6 +1033,9 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.glast_r = a->grad_last_r;
   p.glast_i = a->grad_last_i;
   p.ctl = reinterpret_cast<const TokenCtl*>(a->controls);
+  p.norm_w = a->norm_weight;
+  p.mask = a->relu_mask;
+  p.mask_words = pl.G * 16;
   p.carry = reinterpret_cast<const float2*>(a->carry);
   p.kout = reinterpret_cast<const float2*>(ws + L.kout);
   p.agg = reinterpret_cast<float4*>(ws + L.agg);
@@ -998,14 +1050,16 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
   const long long rows = p.B * p.T;
+  // (a block reads no y: its relu mask comes as bits)
   p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->y) && aligned16(a->dy) && aligned16(a->controls) &&
-                      aligned16(a->carry) && act_tensor_map(&p.map_x, a->x, a->dtype, rows, p.M, p.W, pl.C) &&
-                      act_tensor_map(&p.map_y, a->y, a->dtype, rows, p.M, p.W, pl.C) &&
+                      aligned16(a->carry) && aligned16(a->relu_mask) &&
+                      act_tensor_map(&p.map_x, a->x, a->dtype, rows, p.M, p.W, pl.C) &&
+                      (block || act_tensor_map(&p.map_y, a->y, a->dtype, rows, p.M, p.W, pl.C)) &&
                       act_tensor_map(&p.map_dy, a->dy, a->dtype, rows, p.M, p.W, pl.C) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf = a->dtype == SPARC_DTYPE_BF16;
-  const void* krsum = bf ? Kernels<__nv_bfloat16>::rsum() : Kernels<float>::rsum();
-  const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad(pl.vec) : Kernels<float>::grad(pl.vec);
+  const void* krsum = bf ? Kernels<__nv_bfloat16>::rsum(block) : Kernels<float>::rsum(block);
+  const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad(pl.vec, block) : Kernels<float>::grad(pl.vec, block);
   {
     TimedLaunch tl(kTimeBwdSummary, s);
     rc = launch_error(launch_plain(krsum, dim3(pl.G, pl.rsum_rows), kBwdThreads, pl.rsum_smem, s, p));
@@ -1039,6 +1093,7 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   r.g_energy = a->grad_energy_response;
   r.g_phase_dir = a->grad_phase_direction;
   r.g_radial_dir = a->grad_radial_direction;
+  r.g_norm_w = block ? a->grad_norm_weight : nullptr;
   TimedLaunch tl(kTimeBwdReduce, s);
   return launch_error(launch_ex((const void*)mixer_reduce_kernel, dim3((pl.Mp + 31) / 32, kPartModes + 1),
                                dim3(32, kReduceWarps), 0, 0, s, r));
@@ -1085,7 +1140,7 @@ size_t sparc_mixer_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   Plan pl;
-  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, &pl);
+  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, a->norm_weight != nullptr, &pl);
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   // the forward uses the launch state, the scan's flags and segment arrays, and the chunk

@@ -29,14 +29,16 @@
 constexpr int kBwdThreads = 256;
 constexpr int kBwdModes = kBwdThreads;  // one mode per thread
 constexpr int kBwdWarps = kBwdThreads / 32;
-constexpr int kPartModes = 9;  // nu, theta (sum of phase grads), wlg, wpr, wrr, D0r, D0i, D1r, D1i
+constexpr int kPartModes = 11;  // nu, theta (sum of phase grads), wlg, wpr, wrr, D0r, D0i, D1r, D1i,
+                                // norm weight at the real / imaginary column (blocks only)
 constexpr int kGroup = 4;      // tokens per unrolled group of the reverse walk
 
 template <typename TIO, int C>
 struct RsumSmem {
   TIO dy[2][C][2][kBwdModes];
-  TIO y[2][C][2][kBwdModes];
+  TIO y[2][C][2][kBwdModes];     // the forward's output (not used by blocks)
   TokenCtl ctl[2][C];
+  unsigned mask[2][C][16];        // a block's relu bits for the CTA's 256 modes
   unsigned long long bar[2];
 };
 
@@ -55,6 +57,9 @@ struct BwdParams {
   const float* glast_r;
   const float* glast_i;
   const TokenCtl* ctl;   // [B, T] forward token controls
+  const float* norm_w;   // [W] RMSNorm weight of a block (kBlock kernels)
+  const unsigned* mask;  // [B*T, mask_words] relu bits of a block's mixer output (kBlock)
+  int mask_words;
   const float2* carry;   // [B, chunks, M] forward inclusive states
   const float2* kout;    // [B, chunks, M] adjoint carry leaving each chunk (scan output)
   float4* agg;           // [B, chunks, Mp] reverse aggregates (summary output)
@@ -70,7 +75,7 @@ struct BwdParams {
 
 
 // ------------------------------------------------------------------------------ reverse summary
-template <typename TIO, int C, bool kFast>
+template <typename TIO, int C, bool kFast, bool kBlock>
 __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __grid_constant__ BwdParams p) {
   const int g = blockIdx.x;
   const int tid = threadIdx.x;
@@ -104,19 +109,30 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
     const TIO* dsrc = static_cast<const TIO*>(p.dy) + row0;
     const TIO* ysrc = static_cast<const TIO*>(p.y) + row0;
     const TokenCtl* csrc = p.ctl + r.b * T + r.t0;
+    const unsigned* msrc = kBlock ? p.mask + (r.b * T + r.t0) * (long long)p.mask_words + (mbase >> 6) * 4 : nullptr;
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&S.bar[buf], 2u * act_box_bytes<TIO, C, kBwdModes>() +
-                                               (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid);
+        mbar_arrive_expect_tx(&S.bar[buf], (kBlock ? 1u : 2u) * act_box_bytes<TIO, C, kBwdModes>() +
+                                               (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid +
+                                               (kBlock ? 64u * (unsigned)r.nvalid : 0u));
         const int row = (int)(r.b * T + r.t0);
         tma_load_3d(&S.dy[buf][0][0][0], &p.map_dy, mbase, 0, row, &S.bar[buf]);
-        tma_load_3d(&S.y[buf][0][0][0], &p.map_y, mbase, 0, row, &S.bar[buf]);
+        if constexpr (kBlock) {
+          for (int t = 0; t < r.nvalid; ++t)
+            bulk_copy_g2s(&S.mask[buf][t][0], msrc + (long long)t * p.mask_words, 64u, &S.bar[buf]);
+        } else {
+          tma_load_3d(&S.y[buf][0][0][0], &p.map_y, mbase, 0, row, &S.bar[buf]);
+        }
         bulk_copy_g2s(&S.ctl[buf][0], csrc, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar[buf]);
       }
     } else {
       load_act_rows<TIO, kBwdModes>(dsrc, W, M, mbase, r.nvalid, S.dy[buf], kBwdThreads);
-      load_act_rows<TIO, kBwdModes>(ysrc, W, M, mbase, r.nvalid, S.y[buf], kBwdThreads);
+      if constexpr (kBlock) {
+        for (int j = tid; j < 16 * r.nvalid; j += kBwdThreads) S.mask[buf][j >> 4][j & 15] = msrc[(long long)(j >> 4) * p.mask_words + (j & 15)];
+      } else {
+        load_act_rows<TIO, kBwdModes>(ysrc, W, M, mbase, r.nvalid, S.y[buf], kBwdThreads);
+      }
       for (int t = tid; t < r.nvalid; t += kBwdThreads) S.ctl[buf][t] = csrc[t];
     }
   };
@@ -148,10 +164,18 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
           const TokenCtl& tc = ctl[t];
           const float gr = to_float(dyt[t][0][tid]);
           const float gi = to_float(dyt[t][1][tid]);
-          const float yr = to_float(yt[t][0][tid]);
-          const float yi = to_float(yt[t][1][tid]);
-          q.x += yr > 0.0f ? gr : 0.0f;
-          q.y += yi > 0.0f ? gi : 0.0f;
+          bool on_r, on_i;
+          if constexpr (kBlock) {  // bit (mode % 64) / 2 of word 4 (mode / 64) + mode % 2 (+2: imaginary)
+            const unsigned* mw = &S.mask[buf][t][(tid >> 6) * 4 + (tid & 1)];
+            const unsigned bit = 1u << ((tid & 63) >> 1);
+            on_r = (mw[0] & bit) != 0u;
+            on_i = (mw[2] & bit) != 0u;
+          } else {
+            on_r = to_float(yt[t][0][tid]) > 0.0f;
+            on_i = to_float(yt[t][1][tid]) > 0.0f;
+          }
+          q.x += on_r ? gr : 0.0f;
+          q.y += on_i ? gi : 0.0f;
           const float2 a = token_transition<kFast>(mc, tc.ed.x, tc.ed.z, tc.keep.x);
           q = make_float2(fmaf(a.x, q.x, a.y * q.y), fmaf(a.x, q.y, -a.y * q.x));
           P = cmul(a, P);
@@ -176,7 +200,7 @@ constexpr int kGradWarps = kGradThreads / 32;
 template <typename TIO, int C>
 struct GradSmem {
   TIO x[C][2][kBwdModes];
-  TIO dy[C][2][kBwdModes];     // masked by the relu in pass 0
+  TIO dy[C][2][kBwdModes];     // the output gradient as given (the relu mask applies in pass B)
   TIO hr[C][kBwdModes];        // replayed states (real plane), then the write-path dx (pass B);
   TIO hi[C][kBwdModes];        // imaginary plane. In the activation dtype: for bfloat16 that keeps
                                // the CTA within four per SM (the reference's bf16 path likewise
@@ -185,9 +209,10 @@ struct GradSmem {
   float2 kin[kBwdModes];       // adjoint carry entering the chunk from the later chunks
   TokenCtl ctl[C];
   float4 dp[C];                // controller gradients per token as pairs (dp0, dp0, dp1, dp1)
-  float tot[2 * C];            // cluster totals of dEta / dDelta
-  float part_grad[2][2 * C];   // dEta / dDelta CTA partials (peers read), by tile parity
-  float warp_part[kGradWarps][2 * C];
+  float2 kap[C];               // a block's RMSNorm backward coefficient r^3/W sum(x w dn), as a pair
+  float tot[3 * C];            // cluster totals of dEta / dDelta (and sum x w dxc in a block)
+  float part_grad[2][3 * C];   // CTA partials (peers read), by tile parity
+  float warp_part[kGradWarps][3 * C];
   unsigned long long bar;
 };
 
@@ -227,7 +252,11 @@ __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& 
   return dxc;
 }
 
-template <typename TIO, int C, bool kFast, bool kVec>
+
+// In a block (kBlock) the mixer's input is n = x r w (RMSNorm) and the output gradient also
+// flows straight to x (residual): dx = dy + r w dn - (r^3 / W) x sum_j(x_j w_j dn_j), with dn the
+// mixer's input gradient; the weight's gradient sums x r dn per column.
+template <typename TIO, int C, bool kFast, bool kVec, bool kBlock>
 __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const __grid_constant__ BwdParams p) {
   static_assert(C % kGroup == 0, "the reverse walk runs in groups of kGroup tokens");
   cg::cluster_group cluster = cg::this_cluster();
@@ -243,11 +272,13 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
   const int chunks = p.chunks;
   const int ncols = min(kBwdModes, M - mbase);
   const long long k0 = blockIdx.y, nk = gridDim.y;
+  constexpr int kVals = kBlock ? 3 * C : 2 * C;  // reduced per-token values
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   GradSmem<TIO, C>& S = *reinterpret_cast<GradSmem<TIO, C>*>(smem_raw);
 
-  const ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
+  ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
+  if constexpr (kBlock) load_norm_weight(mc, p.norm_w, m0, M, act0, act1);
 
   {
     unsigned* z = reinterpret_cast<unsigned*>(&S.x[0][0][0]);
@@ -314,7 +345,18 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
     auto tile_body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr int kU = kFull ? token_unroll<C>() : 1;  // partial unrolling keeps the kernel's code in the i-cache
-      // pass 0: replay the states from the forward's carry; relu masks on dy
+      // the mixer's input of token t: x, or x r w in a block
+      auto mixer_in = [&](int t, float2 xr, float2 xi, float2& nr, float2& ni) {
+        if constexpr (kBlock) {
+          const float2 rr = make_float2(S.ctl[t].keep.z, S.ctl[t].keep.w);
+          nr = mul2(xr, mul2(rr, mc.wre));
+          ni = mul2(xi, mul2(rr, mc.wim));
+        } else {
+          nr = xr;
+          ni = xi;
+        }
+      };
+      // pass 0: replay the states from the forward's carry
       float2 hin0 = make_float2(0.0f, 0.0f), hin1 = hin0;
       if (c > 0) {
         if (act0) hin0 = S.hin[2 * tid];
@@ -329,16 +371,12 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
 #pragma unroll kU
         for (int t = 0; t < C; ++t) {
           if (kFull || t < nvalid) {
-            const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
-            const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
+            float2 nr, ni;
+            mixer_in(t, Pair<TIO>::load(&S.x[t][0][2 * tid]), Pair<TIO>::load(&S.x[t][1][2 * tid]), nr, ni);
             const TokenCoef2 k = token_coef2<kFast>(mc, S.ctl[t]);
-            h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
+            h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(nr)), mul2(k.gain, tanh_t2<kFast>(ni))));
             Pair<TIO>::store(&S.hr[t][2 * tid], h.re.x, h.re.y);
             Pair<TIO>::store(&S.hi[t][2 * tid], h.im.x, h.im.y);
-            const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
-            const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
-            Pair<TIO>::store(&S.dy[t][0][2 * tid], h.re.x > 0.0f ? gr.x : 0.0f, h.re.y > 0.0f ? gr.y : 0.0f);
-            Pair<TIO>::store(&S.dy[t][1][2 * tid], h.im.x > 0.0f ? gi.x : 0.0f, h.im.y > 0.0f ? gi.y : 0.0f);
           }
         }
       }
@@ -355,51 +393,71 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       Cx2 lam = cx2(make_float2(kin0.x, kin1.x), make_float2(kin0.y, kin1.y));
 
       // pass B: the true adjoint with every gradient, kGroup tokens at a time; each group's
-      // dEta / dDelta are reduced over the warp at once (lane 4u+j holds value u of the group)
+      // per-token sums are reduced over the warp at once (lane 4u+j holds value u of the group)
       float2 fa[5];
 #pragma unroll
       for (int q = 0; q < 5; ++q) fa[q] = bcast2(0.0f);
 #pragma unroll 1
       for (int t1 = C - 1; t1 >= 0; t1 -= kGroup) {
         float v[2 * kGroup];
+        float v3[kGroup];
 #pragma unroll
         for (int u = 0; u < kGroup; ++u) {
           const int t = t1 - u;
-          float ve = 0.0f, vd = 0.0f;
+          float ve = 0.0f, vd = 0.0f, vs = 0.0f;
           if (kFull || t < nvalid) {
             const TokenCtl& tc = S.ctl[t];
-            lam.re = add2(lam.re, Pair<TIO>::load(&S.dy[t][0][2 * tid]));
-            lam.im = add2(lam.im, Pair<TIO>::load(&S.dy[t][1][2 * tid]));
+            // relu mask of the output gradient from this token's state (the slot still holds h_t)
+            const float2 hcr = Pair<TIO>::load(&S.hr[t][2 * tid]);
+            const float2 hci = Pair<TIO>::load(&S.hi[t][2 * tid]);
+            const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
+            const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
+            lam.re = add2(lam.re, make_float2(hcr.x > 0.0f ? gr.x : 0.0f, hcr.y > 0.0f ? gr.y : 0.0f));
+            lam.im = add2(lam.im, make_float2(hci.x > 0.0f ? gi.x : 0.0f, hci.y > 0.0f ? gi.y : 0.0f));
             const Cx2 pv = t > 0 ? cx2(Pair<TIO>::load(&S.hr[t - 1][2 * tid]), Pair<TIO>::load(&S.hi[t - 1][2 * tid]))
                                  : hin;
-            const float2 cx = Pair<TIO>::load(&S.x[t][0][2 * tid]);
-            const float2 cy = Pair<TIO>::load(&S.x[t][1][2 * tid]);
+            const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
+            const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
+            float2 nr, ni;
+            mixer_in(t, xr, xi, nr, ni);
             float2 ve2, vd2;
-            const Cx2 dxc = grad_step2<kFast>(mc, tc, lam, pv, cx, cy, ve2, vd2, fa);
-            // h[t] was last read as the previous state at step t+1: its slots now hold the
-            // write-path dx
+            const Cx2 dxc = grad_step2<kFast>(mc, tc, lam, pv, nr, ni, ve2, vd2, fa);
+            // h[t] was last read as the previous state at step t+1 and as this step's mask: its
+            // slots now hold the write-path dx
             Pair<TIO>::store(&S.hr[t][2 * tid], dxc.re.x, dxc.re.y);
             Pair<TIO>::store(&S.hi[t][2 * tid], dxc.im.x, dxc.im.y);
             ve = (act0 ? ve2.x : 0.0f) + (act1 ? ve2.y : 0.0f);
             vd = (act0 ? vd2.x : 0.0f) + (act1 ? vd2.y : 0.0f);
+            if constexpr (kBlock) {  // sum_j x_j w_j dxc_j (the norm backward's write-path part)
+              const float2 sx = fma2(mul2(xr, mc.wre), dxc.re, mul2(mul2(xi, mc.wim), dxc.im));
+              vs = (act0 ? sx.x : 0.0f) + (act1 ? sx.y : 0.0f);
+            }
           }
           v[u] = ve;
           v[kGroup + u] = vd;
+          v3[u] = vs;
         }
-        constexpr int kShift = 5 - log2i<2 * kGroup>();
-        const float total = transpose_reduce<2 * kGroup>(v, lane);
-        if ((lane & ((1 << kShift) - 1)) == 0) {
-          const int u = lane >> kShift;  // 0..2*kGroup-1: ve of tokens t1..t1-3, then vd
-          const int t = t1 - (u % kGroup);
-          S.warp_part[warp][(u < kGroup ? 0 : C) + t] = total;
+        {
+          constexpr int kShift = 5 - log2i<2 * kGroup>();
+          const float total = transpose_reduce<2 * kGroup>(v, lane);
+          if ((lane & ((1 << kShift) - 1)) == 0) {
+            const int u = lane >> kShift;  // 0..2*kGroup-1: ve of tokens t1..t1-3, then vd
+            const int t = t1 - (u % kGroup);
+            S.warp_part[warp][(u < kGroup ? 0 : C) + t] = total;
+          }
+        }
+        if constexpr (kBlock) {
+          constexpr int kShift = 5 - log2i<kGroup>();
+          const float total = transpose_reduce<kGroup>(v3, lane);
+          if ((lane & ((1 << kShift) - 1)) == 0) S.warp_part[warp][2 * C + t1 - (lane >> kShift)] = total;
         }
       }
 #pragma unroll
       for (int q = 0; q < 5; ++q) acc[q] = add2(acc[q], fa[q]);
 
-      // token sums over all modes -> controller gradients
+      // token sums over all modes -> controller gradients (and the norm's coefficient)
       __syncthreads();
-      if (tid < 2 * C) {
+      if (tid < kVals) {
         float sum = 0.0f;
 #pragma unroll
         for (int w = 0; w < kGradWarps; ++w) sum += S.warp_part[w][tid];
@@ -407,7 +465,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       }
       if (G > 1) cluster.sync();
       else __syncthreads();
-      if (tid < 2 * C) {
+      if (tid < kVals) {
         float q[8];
 #pragma unroll
         for (int rr = 0; rr < 8; ++rr) q[rr] = rr < G ? cluster.map_shared_rank(&S.part_grad[par][0], rr)[tid] : 0.0f;
@@ -418,14 +476,23 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       }
       __syncthreads();
       if (tid < C) {
-        const float tau0 = S.ctl[tid].tau.x, tau1 = S.ctl[tid].tau.z;
+        const TokenCtl& tc = S.ctl[tid];
+        const float tau0 = tc.tau.x, tau1 = tc.tau.z;
         const float dp1 = tid < nvalid ? S.tot[tid] * kLn16 * fmaf(-tau1, tau1, 1.0f) : 0.0f;
         const float dp0 = tid < nvalid ? S.tot[C + tid] * kHalfPi * fmaf(-tau0, tau0, 1.0f) : 0.0f;
         S.dp[tid] = make_float4(dp0, dp0, dp1, dp1);
+        if constexpr (kBlock) {
+          // sum_j x_j w_j dn_j = sum x w dxc + dp0 q0 + dp1 q1 (q: the projections before r)
+          const float rs = tc.keep.z;
+          const float sxn = fmaf(dp0, tc.proj.x, fmaf(dp1, tc.proj.y, S.tot[2 * C + tid]));
+          const float kappa = tid < nvalid ? rs * rs * rs * sxn / (float)W : 0.0f;
+          S.kap[tid] = make_float2(kappa, kappa);
+        }
       }
       __syncthreads();
       TIO* dxrow = static_cast<TIO*>(p.dx) + row0;
       float2 fd[4] = {bcast2(0.0f), bcast2(0.0f), bcast2(0.0f), bcast2(0.0f)};
+      float2 fw[2] = {bcast2(0.0f), bcast2(0.0f)};
 #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < nvalid) {
@@ -433,8 +500,26 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
           const float2 dp0 = make_float2(dpv.x, dpv.y), dp1 = make_float2(dpv.z, dpv.w);
           const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
-          const float2 dre = fma2(dp0, mc.d0r, fma2(dp1, mc.d1r, Pair<TIO>::load(&S.hr[t][2 * tid])));
-          const float2 dim = fma2(dp0, mc.d0i, fma2(dp1, mc.d1i, Pair<TIO>::load(&S.hi[t][2 * tid])));
+          // the mixer's input gradient
+          const float2 dnr = fma2(dp0, mc.d0r, fma2(dp1, mc.d1r, Pair<TIO>::load(&S.hr[t][2 * tid])));
+          const float2 dni = fma2(dp0, mc.d0i, fma2(dp1, mc.d1i, Pair<TIO>::load(&S.hi[t][2 * tid])));
+          float2 dre, dim, nr, ni;
+          if constexpr (kBlock) {
+            const float2 rr = make_float2(S.ctl[t].keep.z, S.ctl[t].keep.w);
+            const float2 kap = S.kap[t];
+            const float2 rwr = mul2(rr, mc.wre), rwi = mul2(rr, mc.wim);
+            dre = sub2(fma2(rwr, dnr, Pair<TIO>::load(&S.dy[t][0][2 * tid])), mul2(kap, xr));
+            dim = sub2(fma2(rwi, dni, Pair<TIO>::load(&S.dy[t][1][2 * tid])), mul2(kap, xi));
+            nr = mul2(xr, rwr);
+            ni = mul2(xi, rwi);
+            fw[0] = fma2(mul2(xr, rr), dnr, fw[0]);
+            fw[1] = fma2(mul2(xi, rr), dni, fw[1]);
+          } else {
+            dre = dnr;
+            dim = dni;
+            nr = xr;
+            ni = xi;
+          }
           TIO* row = dxrow + (long long)t * W;
           if (kVec && act1) {
             Pair<TIO>::store(row + m0, dre.x, dre.y);
@@ -449,14 +534,18 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
               Io<TIO>::store(row + M + m0 + 1, dim.y);
             }
           }
-          fd[0] = fma2(xr, dp0, fd[0]);
-          fd[1] = fma2(xi, dp0, fd[1]);
-          fd[2] = fma2(xr, dp1, fd[2]);
-          fd[3] = fma2(xi, dp1, fd[3]);
+          fd[0] = fma2(nr, dp0, fd[0]);
+          fd[1] = fma2(ni, dp0, fd[1]);
+          fd[2] = fma2(nr, dp1, fd[2]);
+          fd[3] = fma2(ni, dp1, fd[3]);
         }
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[5 + q] = add2(acc[5 + q], fd[q]);
+      if constexpr (kBlock) {
+        acc[9] = add2(acc[9], fw[0]);
+        acc[10] = add2(acc[10], fw[1]);
+      }
     };
     if (nvalid == C) tile_body(std::true_type{});
     else tile_body(std::false_type{});

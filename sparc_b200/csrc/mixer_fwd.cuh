@@ -27,8 +27,8 @@ template <typename TIO, int C>
 struct SumSmem {
   TIO x[2][C][2][kFwdModes];  // [buffer][token][re|im][mode]
   TokenCtl ctl[C];
-  float part[2][2 * C];       // this CTA's projection partials (peers read), by tile parity
-  float warp_part[kFwdThreads / 32][2 * C];
+  float part[2][3 * C];       // this CTA's projection / sum-of-squares partials (peers read), by tile parity
+  float warp_part[kFwdThreads / 32][3 * C];
   unsigned long long bar[2];
 };
 
@@ -49,6 +49,10 @@ struct FwdParams {
   const float* h0_i;
   TokenCtl* ctl;        // [B, T] token controls (written by the summary)
   const unsigned char* reset;  // [B, T] 1 where a segment reset zeroes the transition, or null
+  const float* norm_w;  // [W] RMSNorm weight of a block (kBlock kernels), else null
+  float norm_eps;
+  unsigned* mask;       // [B*T, mask_words] relu bits of the block's mixer output (kBlock)
+  int mask_words;       // 16 per CTA of 256 modes: four words per 64 modes (store_relu_bits)
   const float2* carry;  // [B, chunks, M] inclusive chunk states (replay input)
   float4* agg;          // [B, chunks, Mp] chunk aggregates (P, Q)
   LaunchState* ls;
@@ -95,6 +99,37 @@ __device__ __forceinline__ void store_y_pair(TIO* row, int M, int m, bool a0, bo
   }
 }
 
+// Block output x + relu(h) for the pair of modes (m, m+1) of one token row.
+template <typename TIO, bool kVec>
+__device__ __forceinline__ void store_sum_pair(TIO* row, int M, int m, bool a0, bool a1, float2 xr, float2 xi,
+                                               const Cx2& h) {
+  const float r0 = xr.x + fmaxf(h.re.x, 0.0f), r1 = xr.y + fmaxf(h.re.y, 0.0f);
+  const float i0 = xi.x + fmaxf(h.im.x, 0.0f), i1 = xi.y + fmaxf(h.im.y, 0.0f);
+  if (kVec && a1) {
+    Pair<TIO>::store(row + m, r0, r1);
+    Pair<TIO>::store(row + M + m, i0, i1);
+    return;
+  }
+  if (a0) {
+    Io<TIO>::store(row + m, r0);
+    Io<TIO>::store(row + M + m, i0);
+  }
+  if (a1) {
+    Io<TIO>::store(row + m + 1, r1);
+    Io<TIO>::store(row + M + m + 1, i1);
+  }
+}
+
+// Relu bits of one token for the warp's 64 modes (lane l owns modes 2l, 2l+1): four words,
+// [real of even modes, real of odd modes, imaginary of even, imaginary of odd], bit l each.
+__device__ __forceinline__ void store_relu_bits(unsigned* dst, const Cx2& h, int lane) {
+  const unsigned w0 = __ballot_sync(0xffffffffu, h.re.x > 0.0f);
+  const unsigned w1 = __ballot_sync(0xffffffffu, h.re.y > 0.0f);
+  const unsigned w2 = __ballot_sync(0xffffffffu, h.im.x > 0.0f);
+  const unsigned w3 = __ballot_sync(0xffffffffu, h.im.y > 0.0f);
+  if (lane == 0) *reinterpret_cast<uint4*>(dst) = make_uint4(w0, w1, w2, w3);
+}
+
 // Tile geometry shared by all tile kernels: tile i covers row b = i % B, chunk c = i / B (tile
 // counts stay below 2^31, so the division is 32-bit).
 struct TileRef {
@@ -134,7 +169,7 @@ __host__ __device__ constexpr unsigned act_box_bytes() {
 }
 
 // ------------------------------------------------------------------------------ summary
-template <typename TIO, int C, bool kFast>
+template <typename TIO, int C, bool kFast, bool kBlock>
 __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __grid_constant__ FwdParams p) {
   constexpr int NW = kFwdThreads / 32;
   cg::cluster_group cluster = cg::this_cluster();
@@ -152,8 +187,12 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
   extern __shared__ __align__(128) unsigned char smem_raw[];
   SumSmem<TIO, C>& S = *reinterpret_cast<SumSmem<TIO, C>*>(smem_raw);
 
-  const ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
+  ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
+  if constexpr (kBlock) load_norm_weight(mc, p.norm_w, m0, M, act0, act1);
   const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
+  // projection directions seen by raw x: D w (the norm's weight), scaled by r after the reduction
+  const float2 d0r = mul2(mc.d0r, mc.wre), d0i = mul2(mc.d0i, mc.wim);
+  const float2 d1r = mul2(mc.d1r, mc.wre), d1i = mul2(mc.d1i, mc.wim);
 
   // columns past M are never copied and must read as zeros
   {
@@ -196,24 +235,38 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
     }
     const TIO(*xt)[2][kFwdModes] = S.x[buf];
 
-    // control projections: per-thread partials over its 4 columns, reduced over the cluster
+    // control projections (and, in a block, the sum of squares for the norm): per-thread
+    // partials over its 4 columns, reduced over the cluster
     {
+      const int lane = tid & 31, warp = tid >> 5;
       float v[2 * C];
+      float vs[C];
 #pragma unroll
       for (int t = 0; t < C; ++t) {
         const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
         const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-        const float2 v0 = fma2(xr, mc.d0r, mul2(xi, mc.d0i));
-        const float2 v1 = fma2(xr, mc.d1r, mul2(xi, mc.d1i));
+        const float2 v0 = fma2(xr, d0r, mul2(xi, d0i));
+        const float2 v1 = fma2(xr, d1r, mul2(xi, d1i));
         v[t] = v0.x + v0.y;
         v[C + t] = v1.x + v1.y;
+        if constexpr (kBlock) {
+          const float2 sq = fma2(xr, xr, mul2(xi, xi));
+          vs[t] = sq.x + sq.y;
+        }
       }
-      constexpr int kShift = 5 - log2i<2 * C>();
-      const int lane = tid & 31, warp = tid >> 5;
-      const float total = transpose_reduce<2 * C>(v, lane);
-      if ((lane & ((1 << kShift) - 1)) == 0) S.warp_part[warp][lane >> kShift] = total;
+      {
+        constexpr int kShift = 5 - log2i<2 * C>();
+        const float total = transpose_reduce<2 * C>(v, lane);
+        if ((lane & ((1 << kShift) - 1)) == 0) S.warp_part[warp][lane >> kShift] = total;
+      }
+      if constexpr (kBlock) {
+        constexpr int kShift = 5 - log2i<C>();
+        const float total = transpose_reduce<C>(vs, lane);
+        if ((lane & ((1 << kShift) - 1)) == 0) S.warp_part[warp][2 * C + (lane >> kShift)] = total;
+      }
+      constexpr int kVals = kBlock ? 3 * C : 2 * C;
       __syncthreads();
-      if (tid < 2 * C) {
+      if (tid < kVals) {
         float sum = 0.0f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) sum += S.warp_part[w][tid];
@@ -223,31 +276,36 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
       else __syncthreads();
       if (tid < C) {
         // the peers' partials are read together (their latencies overlap)
-        float q0[8], q1[8];
+        float q0[8], q1[8], qs[8];
 #pragma unroll
         for (int rr = 0; rr < 8; ++rr) {
           if (rr < G) {
             const float* peer = cluster.map_shared_rank(&S.part[buf][0], rr);
             q0[rr] = peer[tid];
             q1[rr] = peer[C + tid];
+            qs[rr] = kBlock ? peer[2 * C + tid] : 0.0f;
           } else {
-            q0[rr] = q1[rr] = 0.0f;
+            q0[rr] = q1[rr] = qs[rr] = 0.0f;
           }
         }
-        float p0 = 0.0f, p1 = 0.0f;
+        float p0 = 0.0f, p1 = 0.0f, ss = 0.0f;
 #pragma unroll
         for (int rr = 0; rr < 8; ++rr) {
           p0 += q0[rr];
           p1 += q1[rr];
+          ss += qs[rr];
         }
-        const float tau0 = tanh_accurate(p0 + bias0);
-        const float tau1 = tanh_accurate(p1 + bias1);
+        // RMSNorm scale of the token (block): r = (mean x^2 + eps)^(-1/2)
+        const float rs = kBlock ? rsqrtf(fmaf(ss, 1.0f / (float)W, p.norm_eps)) : 1.0f;
+        const float tau0 = tanh_accurate(fmaf(rs, p0, bias0));
+        const float tau1 = tanh_accurate(fmaf(rs, p1, bias1));
         const float E = expf(kLn16 * tau1), delta = kHalfPi * tau0;
         const float keep = (p.reset != nullptr && tid < r.nvalid && p.reset[r.b * T + r.t0 + tid]) ? 0.0f : 1.0f;
         TokenCtl tc;
         tc.ed = make_float4(E, E, delta, delta);
         tc.tau = make_float4(tau0, tau0, tau1, tau1);
-        tc.keep = make_float4(keep, keep, 0.0f, 0.0f);
+        tc.keep = make_float4(keep, keep, rs, rs);
+        tc.proj = make_float4(p0, p1, 0.0f, 0.0f);
         S.ctl[tid] = tc;
         if (g == 0 && tid < r.nvalid) p.ctl[r.b * T + r.t0 + tid] = tc;
       }
@@ -262,8 +320,13 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
 #pragma unroll kU
       for (int t = 0; t < C; ++t) {
         if (kFull || t < r.nvalid) {
-          const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
-          const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
+          float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
+          float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
+          if constexpr (kBlock) {  // the mixer's input is the normalised token x r w
+            const float2 rr = make_float2(S.ctl[t].keep.z, S.ctl[t].keep.w);
+            xr = mul2(xr, mul2(rr, mc.wre));
+            xi = mul2(xi, mul2(rr, mc.wim));
+          }
           const TokenCoef2 k = token_coef2<kFast>(mc, S.ctl[t]);
           Q = cfma2(k.a, Q, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
           P = cmul2(k.a, P);
@@ -282,7 +345,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
 }
 
 // ------------------------------------------------------------------------------ replay
-template <typename TIO, int C, bool kFast, bool kVec>
+template <typename TIO, int C, bool kFast, bool kVec, bool kBlock>
 __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __grid_constant__ FwdParams p) {
   const int g = blockIdx.x;
   const int tid = threadIdx.x;
@@ -297,7 +360,9 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
   extern __shared__ __align__(128) unsigned char smem_raw[];
   RepSmem<TIO, C>& S = *reinterpret_cast<RepSmem<TIO, C>*>(smem_raw);
 
-  const ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
+  ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
+  if constexpr (kBlock) load_norm_weight(mc, p.norm_w, m0, M, act0, act1);
+  const int lane = tid & 31, warp = tid >> 5;
 
   if (tid == 0) {
     mbar_init(&S.bar[0], 1);
@@ -366,9 +431,19 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
           const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
           const TokenCoef2 k = token_coef2<kFast>(mc, ctl[t]);
-          h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
-          store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, make_float2(h.re.x, h.im.x),
-                                  make_float2(h.re.y, h.im.y));
+          if constexpr (kBlock) {
+            // mixer input x r w; block output x + relu(h); relu bits for the backward
+            const float2 rr = make_float2(ctl[t].keep.z, ctl[t].keep.w);
+            const float2 nr = mul2(xr, mul2(rr, mc.wre)), ni = mul2(xi, mul2(rr, mc.wim));
+            h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(nr)), mul2(k.gain, tanh_t2<kFast>(ni))));
+            store_sum_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, xr, xi, h);
+            store_relu_bits(p.mask + (r.b * T + r.t0 + t) * (long long)p.mask_words + (mbase >> 6) * 4 + warp * 4,
+                            h, lane);
+          } else {
+            h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
+            store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, make_float2(h.re.x, h.im.x),
+                                    make_float2(h.re.y, h.im.y));
+          }
         }
       }
     };

@@ -36,12 +36,13 @@ class _SparcMixerFunction(torch.autograd.Function):
 
     Outputs y [B, T, W] (x.dtype) and the final state (last_r, last_i) [B, M] float32; both
     are differentiable. Saved for backward: x, y, the parameters, the per-chunk carries and the
-    per-token controls."""
+    per-token controls. With a norm weight the call is a block: y = x + mixer(RMSNorm(x)) in the
+    same kernels, and the relu bits are saved instead of y."""
 
     @staticmethod
     def forward(ctx, x, nu_log, theta_log, phase_direction, radial_direction, write_log_gain,
                 energy_response, write_phase_response, write_radial_response, h0_r, h0_i,
-                max_spin, inject_tile, reset=None):
+                max_spin, inject_tile, reset=None, norm_weight=None, norm_eps=1e-6):
         L = _lib.lib()
         B, T, W = x.shape
         M = W // 2
@@ -53,9 +54,13 @@ class _SparcMixerFunction(torch.autograd.Function):
         if h0_r is not None:
             h0 = (_f32(h0_r), _f32(h0_i))
         y = torch.empty_like(x)
+        block = norm_weight is not None
+        nw = _f32(norm_weight) if block else None
+        mask = (torch.empty((B, T, L.sparc_mixer_mask_words(W)), dtype=torch.int32, device=dev)
+                if block else None)
         chunks = L.sparc_mixer_carry_chunks(T, dt)
         carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
-        controls = torch.empty((B, T, 12), dtype=torch.float32, device=dev)
+        controls = torch.empty((B, T, L.sparc_mixer_controls_floats()), dtype=torch.float32, device=dev)
         last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
         last_i = torch.empty((B, M), dtype=torch.float32, device=dev)
         nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
@@ -66,11 +71,13 @@ class _SparcMixerFunction(torch.autograd.Function):
             x.data_ptr(), y.data_ptr(), *[p.data_ptr() for p in params],
             _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
             last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
+            _lib.ptr(nw), float(norm_eps), _lib.ptr(mask),
             ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin, _lib.deterministic(),
             1 if inject_tile is not None else 0, inject_tile if inject_tile is not None else 0)
         _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_forward")
-        ctx.save_for_backward(x, y, *params, carry, controls, *(h0 if h0 else (None, None)))
+        ctx.save_for_backward(x, None if block else y, *params, carry, controls, *(h0 if h0 else (None, None)),
+                              nw, mask)
         ctx.has_h0 = h0 is not None
         ctx.max_spin = max_spin
         ctx.set_materialize_grads(False)
@@ -79,7 +86,7 @@ class _SparcMixerFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy, dlast_r, dlast_i):
         L = _lib.lib()
-        x, y, nu_log, theta_log, pd, rd, wlg, wpr, wrr, carry, controls, h0_r, h0_i = ctx.saved_tensors
+        x, y, nu_log, theta_log, pd, rd, wlg, wpr, wrr, carry, controls, h0_r, h0_i, nw, mask = ctx.saved_tensors
         B, T, W = x.shape
         M = W // 2
         dev = x.device
@@ -94,6 +101,7 @@ class _SparcMixerFunction(torch.autograd.Function):
         g = {n: torch.empty(M, dtype=torch.float32, device=dev) for n in _PARAMS}
         g["phase_direction"] = torch.empty(W + 1, dtype=torch.float32, device=dev)
         g["radial_direction"] = torch.empty(W + 1, dtype=torch.float32, device=dev)
+        gnw = torch.empty(W, dtype=torch.float32, device=dev) if nw is not None else None
         gh0 = None
         if ctx.has_h0:
             gh0 = (torch.empty((B, M), dtype=torch.float32, device=dev),
@@ -101,19 +109,19 @@ class _SparcMixerFunction(torch.autograd.Function):
         nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
         ws = _lib.WORKSPACES.get(dev, nbytes)
         a = _lib.MixerBwdArgs(
-            x.data_ptr(), y.data_ptr(), dy.data_ptr(), dx.data_ptr(),
+            x.data_ptr(), _lib.ptr(y), dy.data_ptr(), dx.data_ptr(),
             nu_log.data_ptr(), theta_log.data_ptr(), pd.data_ptr(), rd.data_ptr(),
             wlg.data_ptr(), wpr.data_ptr(), wrr.data_ptr(),
             _lib.ptr(h0_r), _lib.ptr(h0_i),
             _lib.ptr(gl[0] if gl else None), _lib.ptr(gl[1] if gl else None),
             _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
-            carry.data_ptr(), controls.data_ptr(),
+            carry.data_ptr(), controls.data_ptr(), _lib.ptr(nw), _lib.ptr(mask), _lib.ptr(gnw),
             *[g[n].data_ptr() for n in _PARAMS],
             ws.data_ptr(), ws.numel(), B, T, W, dt, ctx.max_spin, _lib.deterministic(), 0, 0)
         _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_backward")
         return (dx, *[g[n] for n in _PARAMS],
-                gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None)
+                gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None, gnw, None)
 
 
 def reset_mask(segment_pos, reset_first: bool, shape, device):
@@ -138,6 +146,21 @@ def sparc_mixer(x, params, state=None, max_spin: int = 0, inject_unpublished_til
     reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
     y, lr, li = _SparcMixerFunction.apply(
         x, *[params[n] for n in _PARAMS], h0_r, h0_i, int(max_spin), inject_unpublished_tile, reset)
+    return y, (lr, li)
+
+
+def sparc_block(x, params, norm_weight, eps: float = 1e-6, state=None, segment_pos=None,
+                reset_first: bool = False, max_spin: int = 0):
+    """One block of the config-5 stack in the mixer's own kernels: (x + mixer(RMSNorm(x)),
+    (last_r, last_i)), RMSNorm(x) = x * (mean(x^2) + eps)^(-1/2) * norm_weight per token."""
+    _lib.require_cuda(x, "x")
+    if norm_weight.shape != (x.shape[-1],):
+        raise ValueError("norm_weight must have shape [width]")
+    h0_r, h0_i = (None, None) if state is None else state
+    reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
+    y, lr, li = _SparcMixerFunction.apply(
+        x.contiguous(), *[params[n] for n in _PARAMS], h0_r, h0_i, int(max_spin), None, reset, norm_weight,
+        float(eps))
     return y, (lr, li)
 
 

@@ -362,3 +362,77 @@ def test_bad_inputs_raise():
         m(torch.randn(2, 8, 16))
     with pytest.raises(ValueError):
         sparc_b200.SPARCMixer(7)
+
+
+@pytest.mark.parametrize("dtype,B,T,W,fwd_tol,bwd_tol", [
+    (torch.float32, 2, 100, 64, 1e-4, 1e-3),
+    (torch.float32, 3, 37, 10, 1e-4, 1e-3),
+    (torch.float32, 2, 40, 600, 1e-4, 1e-3),
+    (torch.bfloat16, 2, 300, 2048, 2e-2, 2e-2),
+])
+def test_block_matches_oracle(dtype, B, T, W, fwd_tol, bwd_tol):
+    """The fused block x + mixer(RMSNorm(x)) (config-5 layer) against the oracle's composition,
+    forward and backward including the norm weight's gradient, with resets and h0."""
+    from sparc_b200 import sparc_block
+
+    params = _random_params(W, 40 + W)
+    gen = torch.Generator().manual_seed(41 + W)
+    M = W // 2
+    x = (torch.randn(B, T, W, generator=gen) * 2.0).to(dtype)
+    d = torch.randn(B, T, W, generator=gen).to(dtype).double()
+    w = (1.0 + 0.3 * torch.randn(W, generator=gen)).float()
+    state = (torch.randn(B, M, generator=gen) * 0.5, torch.randn(B, M, generator=gen) * 0.5)
+    pos = _segment_positions(B, T, gen, n_starts=2)
+    P = O.Params.from_mapping(params)
+    xo = x.double().numpy()
+    h0 = (state[0].double().numpy(), state[1].double().numpy())
+    reset = (pos == 0).numpy()
+    out_ref, last_ref = O.block_forward(xo, P, w.double().numpy(), 1e-6, h0=h0, reset=reset)
+    g_ref = O.block_backward(xo, P, w.double().numpy(), d.numpy(), 1e-6, h0=h0, reset=reset)
+    m = _module(params, W)
+    xs = x.cuda().requires_grad_(True)
+    wg = w.cuda().requires_grad_(True)
+    st = (state[0].cuda().requires_grad_(True), state[1].cuda().requires_grad_(True))
+    out, (lr, li) = sparc_block(xs, m._params(), wg, 1e-6, state=st, segment_pos=pos.cuda())
+    (out.double() * d.cuda()).sum().backward()
+    e = O.rel_l2(out.detach().double().cpu().numpy(), out_ref)
+    assert e < fwd_tol, f"block out rel-l2 {e:.3e}"
+    assert O.rel_l2(lr.detach().double().cpu().numpy(), last_ref[0]) < fwd_tol
+    e = O.rel_l2(xs.grad.double().cpu().numpy(), g_ref["x"])
+    assert e < bwd_tol, f"block dx rel-l2 {e:.3e}"
+    e = O.rel_l2(wg.grad.double().cpu().numpy(), g_ref["norm_weight"])
+    assert e < bwd_tol, f"norm weight grad rel-l2 {e:.3e}"
+    for k in GRADS:
+        e = O.rel_l2(getattr(m, k).grad.double().cpu().numpy(), g_ref[k])
+        assert e < bwd_tol, f"block grad {k} rel-l2 {e:.3e}"
+    assert O.rel_l2(st[0].grad.double().cpu().numpy(), g_ref["h0_r"]) < bwd_tol
+
+
+def test_fused_stack_matches_unfused():
+    """SPARCStack with fused blocks equals the composition of torch RMSNorm, the mixer and the
+    residual add (float32, two layers), forward and all parameter gradients."""
+    from sparc_b200 import SPARCStack
+
+    torch.manual_seed(0)
+    fused = SPARCStack(256, 2).cuda()
+    plain = SPARCStack(256, 2, fused=False).cuda()
+    plain.load_state_dict(fused.state_dict())
+    with torch.no_grad():
+        for mod in (fused, plain):
+            for i, n in enumerate(mod.norms):
+                n.weight.copy_(1.0 + 0.1 * torch.arange(256, device="cuda") / 256.0 + 0.05 * i)
+    x = torch.randn(2, 300, 256, device="cuda")
+    g = torch.randn(2, 300, 256, device="cuda")
+    outs = []
+    for mod in (fused, plain):
+        xx = x.clone().requires_grad_(True)
+        out = mod(xx)
+        out.backward(g)
+        outs.append((out.detach(), xx.grad, {k: v.grad for k, v in mod.named_parameters()}))
+    (o1, dx1, g1), (o2, dx2, g2) = outs
+    assert O.rel_l2(o1.double().cpu().numpy(), o2.double().cpu().numpy()) < 1e-5
+    assert O.rel_l2(dx1.double().cpu().numpy(), dx2.double().cpu().numpy()) < 1e-4
+    for k in g1:
+        if k.endswith("energy_response"):
+            continue
+        assert O.rel_l2(g1[k].double().cpu().numpy(), g2[k].double().cpu().numpy()) < 1e-4, k
