@@ -13,14 +13,13 @@
  * once when it is allocated, and may then be reused by any number of launches that are
  * ordered on one stream; calls that run concurrently need distinct workspaces.
  *
- * The mixer runs as chunk summaries -> a carry scan -> a replay. The carry scan passes the
- * states between segments of chunks by decoupled lookback: a segment composes whatever
- * predecessor aggregates are ready, so the last bits of the carries (and of everything
- * downstream) can vary run to run. With `deterministic` set a segment waits for its immediate
- * predecessor's carry instead, which makes results bitwise reproducible. Parameter gradients
- * are always reduced in a fixed order. Every wait is bounded by `max_spin` polls (0 selects
- * the default, about a second); a wait that runs out sets the SPARC_STATUS_TIMEOUT bit in the
- * workspace's status word, continues with a zero carry, and the launch still completes.
+ * The mixer runs as chunk summaries -> a carry scan (one thread-block cluster per row, spans of
+ * chunks composed in a fixed order) -> a replay; every result, parameter gradients included,
+ * is bitwise reproducible run to run. The real-mode scan passes its carries by decoupled
+ * lookback (a tile composes whatever predecessor aggregates are ready). Every wait is bounded
+ * by `max_spin` polls (0 selects the default, about a second): the lookback's and the TMA
+ * copies'; a wait that runs out sets the SPARC_STATUS_TIMEOUT bit in the workspace's status
+ * word, continues (with a zero carry in the lookback), and the launch still completes.
  * sparc_read_status reads that word.
  *
  * Which reference interface each entry point replaces (paths inside Botwwt/sparc):
@@ -108,10 +107,7 @@ typedef struct SparcMixerFwdArgs {
   long long length;
   int width;
   int dtype;                           /* SPARC_DTYPE_* */
-  unsigned max_spin;                   /* 0 = default */
-  int deterministic;                   /* 1 = chained carries: bitwise reproducible, slower */
-  int inject_enable;                   /* test hook: 1 = carry-scan segment inject_tile */
-  long long inject_tile;               /*   never publishes (its successors time out) */
+  unsigned max_spin;                   /* bound of the TMA waits (0 = default) */
 } SparcMixerFwdArgs;
 
 /* Backward of sparc_mixer_forward for the loss gradient dy on y (and optionally grad_last on
@@ -156,9 +152,6 @@ typedef struct SparcMixerBwdArgs {
   int width;
   int dtype;
   unsigned max_spin;
-  int deterministic;
-  int inject_enable;
-  long long inject_tile;
 } SparcMixerBwdArgs;
 
 /* One fused decode step (forward/decode.py:11-55): x [batch, width] (dtype), state
@@ -200,6 +193,8 @@ typedef struct SparcRealFwdArgs {
   long long channels;
   int dtype;
   unsigned max_spin;
+  int inject_enable;                   /* test hook: 1 = tile inject_tile never publishes */
+  long long inject_tile;               /*   (its successor's bounded wait runs out) */
 } SparcRealFwdArgs;
 
 typedef struct SparcRealBwdArgs {

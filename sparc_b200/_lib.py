@@ -36,8 +36,7 @@ class MixerFwdArgs(ctypes.Structure):
         ("norm_weight", _vp), ("norm_eps", ctypes.c_float), ("relu_mask", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
-        ("max_spin", ctypes.c_uint), ("deterministic", ctypes.c_int),
-        ("inject_enable", ctypes.c_int), ("inject_tile", _ll),
+        ("max_spin", ctypes.c_uint),
     ]
 
 
@@ -54,8 +53,7 @@ class MixerBwdArgs(ctypes.Structure):
         ("grad_write_phase_response", _vp), ("grad_write_radial_response", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
-        ("max_spin", ctypes.c_uint), ("deterministic", ctypes.c_int),
-        ("inject_enable", ctypes.c_int), ("inject_tile", _ll),
+        ("max_spin", ctypes.c_uint),
     ]
 
 
@@ -75,6 +73,7 @@ class RealFwdArgs(ctypes.Structure):
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("channels", _ll), ("dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint),
+        ("inject_enable", ctypes.c_int), ("inject_tile", _ll),
     ]
 
 
@@ -158,9 +157,6 @@ def require_cuda(t: torch.Tensor, name: str):
         raise RuntimeError(f"sparc_b200: {name} must be a CUDA tensor (there is no CPU path)")
 
 
-def deterministic() -> int:
-    """Chained (bitwise reproducible) chunk carries when torch's deterministic mode is on."""
-    return 1 if torch.are_deterministic_algorithms_enabled() else 0
 
 
 def ptr(t):

@@ -263,155 +263,22 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[N], int lane) {
 template <int N>
 __host__ __device__ constexpr int log2i() { return N <= 1 ? 0 : 1 + log2i<N / 2>(); }
 
-// Decoupled lookback with a warp-wide window. The tile publishes its aggregate (out = A*in + B)
-// unless its predecessor is already inclusive. Warp 0 then polls up to 32 predecessors at once
-// (lane j reads the flag of the tile j+1 steps back) and picks the nearest inclusive one; the
-// aggregates in between are composed by every thread for its own mode (their loads are
-// independent, so the whole window costs about two round trips instead of one per
-// predecessor). pred_inclusive(j) loads the inclusive state of the tile j steps back.
-// Deterministic mode waits for the immediate predecessor's inclusive state instead (a chained
-// scan), so the carry's rounding does not depend on which predecessors were done first.
-struct LookbackCtx {
-  LaunchState* ls;
-  unsigned* flags;     // [tiles * G]
-  float4* agg;         // [tiles * Mp]
-  unsigned epoch;
-  unsigned max_spin;
-  int G;
-  int Mp;
-  long long B;         // ticket distance to the predecessor tile
-  bool deterministic;
-};
-
-__device__ __forceinline__ void publish_flag(unsigned* flag, unsigned value) {
-  // every thread's payload stores precede the barrier; thread 0's release store (cumulative
-  // over what the barrier ordered before it) makes them visible with the flag
-  __syncthreads();
-  if (threadIdx.x == 0) st_release(flag, value);
-}
-
-template <int MPT, typename InclFn>
-__device__ __forceinline__ void lookback(const LookbackCtx& lc, long long ticket, int g, int steps_back_max,
-                                         const float2 (&A)[MPT], const float2 (&Bv)[MPT], bool publish,
-                                         unsigned pred_state, unsigned* s_win, int mp0,
-                                         InclFn pred_inclusive, float2 (&carry)[MPT]) {
-  const int tid = threadIdx.x;
-  const unsigned ep = lc.epoch & 0x3fffffffu;
-  if (lc.deterministic) {
-    if (tid == 0) {
-      unsigned s = wait_flag(lc.flags + (ticket - lc.B) * lc.G + g, lc.epoch, lc.max_spin, kFlagInclusive);
-      if (s == 0u) atomicOr(&lc.ls->status, kStatusTimeout);
-      s_win[0] = s;
-    }
-    __syncthreads();
-    const unsigned state = s_win[0];
-    __syncthreads();
-    if (state == kFlagInclusive) {
-      pred_inclusive(1, carry);
-    } else {
-#pragma unroll
-      for (int q = 0; q < MPT; ++q) carry[q] = make_float2(0.0f, 0.0f);
-    }
-    return;
-  }
-  const bool pred_ready = ((pred_state >> 2) == ep) && (pred_state & 3u) == kFlagInclusive;
-  if (pred_ready) {
-    pred_inclusive(1, carry);
-    return;
-  }
-  if (publish) {
-#pragma unroll
-    for (int q = 0; q < MPT; ++q) lc.agg[ticket * lc.Mp + mp0 + q] = make_float4(A[q].x, A[q].y, Bv[q].x, Bv[q].y);
-    publish_flag(lc.flags + ticket * lc.G + g, make_flag(lc.epoch, kFlagAggregate));
-  }
-  float2 accA[MPT], accB[MPT];
-#pragma unroll
-  for (int q = 0; q < MPT; ++q) {
-    accA[q] = make_float2(1.0f, 0.0f);
-    accB[q] = make_float2(0.0f, 0.0f);
-  }
-  int base = 0;  // the window covers predecessors base+1 .. base+32
-  for (unsigned spin = 0;; ++spin) {
-    if (tid < 32) {
-      const int j = base + tid + 1;
-      unsigned st = 0u;
-      if (j <= steps_back_max) {
-        const unsigned v = ld_acquire(lc.flags + (ticket - (long long)j * lc.B) * lc.G + g);
-        st = ((v >> 2) == ep) ? (v & 3u) : 0u;
-      }
-      const unsigned incl = __ballot_sync(0xffffffffu, st == kFlagInclusive);
-      const unsigned notready = __ballot_sync(0xffffffffu, st == 0u && j <= steps_back_max);
-      if (tid == 0) {
-        const int first_incl = incl ? __ffs(incl) - 1 : 32;
-        const int first_wait = notready ? __ffs(notready) - 1 : 32;
-        if (first_incl < first_wait) {            // aggregates, then an inclusive: done
-          s_win[0] = first_incl;
-          s_win[1] = 1u;
-        } else {                                  // compose what is ready; wait for the rest
-          s_win[0] = first_wait;
-          s_win[1] = 0u;
-        }
-      }
-    }
-    __syncthreads();
-    const int n = (int)s_win[0];
-    const bool done = s_win[1] != 0u;
-    __syncthreads();
-    // compose the n aggregates nearest first; loads are issued a batch at a time so their
-    // latencies overlap instead of adding up
-    constexpr int kBatch = 8 / MPT;
-    for (int j0 = 0; j0 < n; j0 += kBatch) {
-      float4 ag[kBatch][MPT];
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        if (j0 + u < n) {
-          const float4* ap = lc.agg + (ticket - (long long)(base + j0 + u + 1) * lc.B) * lc.Mp + mp0;
-#pragma unroll
-          for (int q = 0; q < MPT; ++q) ag[u][q] = __ldcg(ap + q);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        if (j0 + u < n) {
-#pragma unroll
-          for (int q = 0; q < MPT; ++q) {
-            accB[q] = cfma(accA[q], make_float2(ag[u][q].z, ag[u][q].w), accB[q]);
-            accA[q] = cmul(accA[q], make_float2(ag[u][q].x, ag[u][q].y));
-          }
-        }
-      }
-    }
-    base += n;
-    if (done) {
-      float2 h[MPT];
-      pred_inclusive(base + 1, h);
-#pragma unroll
-      for (int q = 0; q < MPT; ++q) carry[q] = cfma(accA[q], h[q], accB[q]);
-      return;
-    }
-    if (base >= steps_back_max || (n == 0 && spin >= lc.max_spin)) {
-      // a broken chain (a tile that never published): record it and continue with zero carry
-      if (tid == 0) atomicOr(&lc.ls->status, kStatusTimeout);
-#pragma unroll
-      for (int q = 0; q < MPT; ++q) carry[q] = accB[q];
-      return;
-    }
-    if (n == 0 && spin > 8) __nanosleep(spin < 64 ? 32 : 256);
-  }
-}
-
 // ------------------------------------------------------------------------------ carry scan
 // Per (row b, mode m): v_j = A_j v_{j-1} + B_j over the chunks j in processing order (forward:
 // chunk j; backward: chunk chunks-1-j), v_{-1} = init (h0, or the gradient of the returned last
 // state; else 0). out[chunk] receives every v; `final` (optional) the last one (the forward's
-// last state, the backward's gradient of h0). A CTA takes a segment of kScanSeg consecutive
-// chunks of one row and 256 modes, holds their maps in registers, composes the segment's map,
-// obtains the carry into the segment by decoupled lookback over the row's earlier segments,
-// publishes its own inclusive result and walks the segment writing every chunk's v. Segments
-// are taken in ticket order (segment-major), so a segment only waits on segments that running
-// CTAs hold.
+// last state, the backward's gradient of h0).
+//
+// One thread-block cluster of kScanQ CTAs per (row, 256 modes): CTA q owns the span of chunks
+// [q L, (q+1) L), L = ceil(chunks / kScanQ), and one mode per thread. It composes its span's maps
+// (loads batched kScanBatch at a time so their latencies overlap), leaves the span's map in
+// shared memory, and after one cluster barrier composes the maps of the spans before it, read
+// from the peers' shared memory in order, into its carry-in; then it walks its span again
+// writing every chunk's v. No CTA waits on anything but the cluster barrier, and the composition
+// order is fixed, so the carries are bitwise reproducible.
 constexpr int kScanThreads = 256;
-constexpr int kScanSeg = 16;
+constexpr int kScanQ = 8;        // CTAs per row (portable cluster size)
+constexpr int kScanBatch = 16;   // chunk maps in flight per thread
 
 struct ScanParams {
   const float4* agg;     // [B, chunks, Mp] per-chunk maps (A, B)
@@ -420,100 +287,73 @@ struct ScanParams {
   const float* init_i;
   float* final_r;        // [B, M] or null
   float* final_i;
-  LaunchState* ls;
-  unsigned* flags;       // [tiles]
-  float4* sagg;          // [tiles, 256] segment maps
-  float2* sincl;         // [tiles, 256] segment inclusive results
-  long long B;
-  int M, Mp, G, chunks, nseg;
-  long long tiles;       // nseg * B * G
+  int G;                 // 256-mode groups per row
+  int M, Mp, chunks, span;
   int reverse;
-  unsigned max_spin;
-  int deterministic;
-  long long inject_unpublished;
 };
 
-__global__ void __launch_bounds__(kScanThreads, 2) mixer_carry_scan_kernel(const ScanParams p) {
-  __shared__ long long s_ticket;
-  __shared__ unsigned s_pred;
-  __shared__ unsigned s_win[2];
+__global__ void __launch_bounds__(kScanThreads) mixer_carry_scan_kernel(const ScanParams p) {
+  __shared__ float4 s_map[kScanThreads];  // this span's map per mode (peers read it)
+  cg::cluster_group cluster = cg::this_cluster();
+  const int q = (int)cluster.block_rank();
   const int tid = threadIdx.x;
+  const long long row = blockIdx.y;
+  const long long b = row / p.G;
+  const int g = (int)(row - b * p.G);
+  const int m = g * kScanThreads + tid;
+  const bool act = m < p.M;
+  const int j0 = min(q * p.span, p.chunks), j1 = min(j0 + p.span, p.chunks);
+  auto map_at = [&](int j) {  // chunk map of processing index j (identity for idle lanes)
+    const int c = p.reverse ? p.chunks - 1 - j : j;
+    return act ? __ldcg(p.agg + (b * p.chunks + c) * (long long)p.Mp + m) : make_float4(1.0f, 0.0f, 0.0f, 0.0f);
+  };
   pdl_wait();  // the chunk maps (summary) are complete from here on
-  const long long rows = p.B * p.G;  // ticket distance to the previous segment of the same row
-  const LookbackCtx lc{p.ls, p.flags, p.sagg, *(volatile unsigned*)&p.ls->epoch, p.max_spin, 1,
-                       kScanThreads, rows, p.deterministic != 0};
-  for (;;) {
-    if (tid == 0) {
-      const long long t = atomicAdd(&p.ls->ticket, 1u);
-      s_ticket = t;
-      s_pred = (t < p.tiles && t >= rows) ? ld_acquire(p.flags + (t - rows)) : 0u;
-    }
-    __syncthreads();
-    const long long ticket = s_ticket;
-    const unsigned pred = s_pred;
-    __syncthreads();  // s_ticket and s_pred are rewritten by the next iteration
-    if (ticket >= p.tiles) break;
-    // scan tickets stay below 2^31: 32-bit division
-    const unsigned uticket = (unsigned)ticket, urows = (unsigned)rows;
-    const int seg = (int)(uticket / urows);
-    const unsigned rg = uticket - (unsigned)seg * urows;
-    const long long b = rg / (unsigned)p.G;
-    const int g = (int)(rg - (unsigned)b * (unsigned)p.G);
-    const int m = g * kScanThreads + tid;
-    const bool act = m < p.M;
-    const int j0 = seg * kScanSeg;
 
-    float4 a[kScanSeg];
+  // the span's map
+  float2 A = make_float2(1.0f, 0.0f), Bv = make_float2(0.0f, 0.0f);
+  for (int j = j0; j < j1; j += kScanBatch) {
+    float4 a[kScanBatch];
 #pragma unroll
-    for (int u = 0; u < kScanSeg; ++u) {
-      const int j = j0 + u;
-      a[u] = make_float4(1.0f, 0.0f, 0.0f, 0.0f);
-      if (act && j < p.chunks) {
-        const int c = p.reverse ? p.chunks - 1 - j : j;
-        a[u] = __ldcg(p.agg + (b * p.chunks + c) * (long long)p.Mp + m);
-      }
-    }
-    float2 A = make_float2(1.0f, 0.0f), Bv = make_float2(0.0f, 0.0f);
+    for (int u = 0; u < kScanBatch; ++u) a[u] = j + u < j1 ? map_at(j + u) : make_float4(1.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-    for (int u = 0; u < kScanSeg; ++u) {
+    for (int u = 0; u < kScanBatch; ++u) {
       Bv = cfma(make_float2(a[u].x, a[u].y), Bv, make_float2(a[u].z, a[u].w));
       A = cmul(make_float2(a[u].x, a[u].y), A);
     }
-    const bool publish = ticket != p.inject_unpublished;
-    float2 cin = make_float2(0.0f, 0.0f);
-    if (seg == 0) {
-      if (p.init_r != nullptr && act) cin = make_float2(p.init_r[b * p.M + m], p.init_i[b * p.M + m]);
-    } else {
-      float2 Aa[1] = {A}, Ba[1] = {Bv}, cc[1];
-      const float2* sincl = p.sincl;
-      lookback<1>(lc, ticket, 0, seg, Aa, Ba, publish, pred, s_win, tid,
-                  [&](int jj, float2 (&h)[1]) {
-                    h[0] = __ldcg(sincl + (ticket - (long long)jj * rows) * kScanThreads + tid);
-                  },
-                  cc);
-      cin = cc[0];
-    }
-    if (publish) {
-      __stcg(p.sincl + ticket * kScanThreads + tid, cfma(A, cin, Bv));
-      publish_flag(p.flags + ticket, make_flag(lc.epoch, kFlagInclusive));
-    }
-    float2 v = cin;
+  }
+  s_map[tid] = make_float4(A.x, A.y, Bv.x, Bv.y);
+  cluster.sync();
+
+  // carry into the span: init, then the earlier spans' maps in order
+  float2 v = make_float2(0.0f, 0.0f);
+  if (p.init_r != nullptr && act) v = make_float2(p.init_r[b * p.M + m], p.init_i[b * p.M + m]);
+  {
+    float4 mk[kScanQ];
 #pragma unroll
-    for (int u = 0; u < kScanSeg; ++u) {
-      const int j = j0 + u;
-      if (j < p.chunks) {
+    for (int k = 0; k < kScanQ; ++k) mk[k] = k < q ? cluster.map_shared_rank(s_map, k)[tid] : make_float4(1.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int k = 0; k < kScanQ; ++k) v = cfma(make_float2(mk[k].x, mk[k].y), v, make_float2(mk[k].z, mk[k].w));
+  }
+
+  // walk the span
+  for (int j = j0; j < j1; j += kScanBatch) {
+    float4 a[kScanBatch];
+#pragma unroll
+    for (int u = 0; u < kScanBatch; ++u) a[u] = j + u < j1 ? map_at(j + u) : make_float4(1.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int u = 0; u < kScanBatch; ++u) {
+      if (j + u < j1) {
         v = cfma(make_float2(a[u].x, a[u].y), v, make_float2(a[u].z, a[u].w));
-        const int c = p.reverse ? p.chunks - 1 - j : j;
+        const int c = p.reverse ? p.chunks - 1 - (j + u) : j + u;
         if (act) p.out[(b * p.chunks + c) * (long long)p.M + m] = v;
       }
     }
-    if (p.final_r != nullptr && act && j0 + kScanSeg >= p.chunks) {
-      p.final_r[b * p.M + m] = v.x;
-      p.final_i[b * p.M + m] = v.y;
-    }
-    __syncthreads();
   }
-  finish_launch(p.ls);
+  if (p.final_r != nullptr && act && j0 < j1 && j1 == p.chunks) {
+    p.final_r[b * p.M + m] = v.x;
+    p.final_i[b * p.M + m] = v.y;
+  }
+  cluster.sync();  // no CTA leaves while a peer may still read its span map
 }
 
 #include "mixer_fwd.cuh"
@@ -602,10 +442,10 @@ struct Plan {
   long long tiles;         // B * chunks
   int G, Mp;               // CTAs of 256 modes per tile; modes padded to G * 256
   bool vec, tma;
-  int sum_clusters, rep_rows, rsum_rows, grad_clusters, scan_ctas;
+  int sum_clusters, rep_rows, rsum_rows, grad_clusters;
   size_t sum_smem, rep_smem, rsum_smem, grad_smem;
-  int nseg;                // carry-scan segments per row
-  long long scan_tiles;    // nseg * B * G
+  long long scan_rows;     // carry-scan clusters: B * G
+  int scan_span;           // chunks per carry-scan CTA
 };
 
 static thread_local char g_err[512];
@@ -717,8 +557,9 @@ static int make_plan(long long B, long long T, int W, int dtype, bool block, Pla
   pl->vec = (M % 2) == 0;
   const size_t s = dtype == SPARC_DTYPE_BF16 ? 2 : 4;
   pl->tma = ((size_t)W * s) % 16 == 0 && ((size_t)M * s) % 16 == 0 && B * T < (1LL << 31);
-  pl->nseg = (pl->chunks + kScanSeg - 1) / kScanSeg;
-  pl->scan_tiles = (long long)pl->nseg * B * pl->G;
+  pl->scan_rows = B * pl->G;
+  pl->scan_span = (pl->chunks + kScanQ - 1) / kScanQ;
+  if (pl->scan_rows > 65535) { set_err("batch x width too large for the carry scan's grid"); return SPARC_ERR_SHAPE; }
 
   const void* k[4];
   if (dtype == SPARC_DTYPE_BF16) plan_kernels<__nv_bfloat16>(pl, k);
@@ -726,7 +567,7 @@ static int make_plan(long long B, long long T, int W, int dtype, bool block, Pla
 
   int dev = 0;
   cudaGetDevice(&dev);
-  struct Key { int dev, dtype, G, vec, block; int sum, rep, rsum, grad, scan; };
+  struct Key { int dev, dtype, G, vec, block; int sum, rep, rsum, grad; };
   static std::mutex mu;
   static Key cache[64];
   static int ncache = 0;
@@ -740,13 +581,12 @@ static int make_plan(long long B, long long T, int W, int dtype, bool block, Pla
   if (hit != nullptr) {
     key = *hit;
   } else {
-    key = Key{dev, dtype, pl->G, (int)pl->vec, (int)block, 0, 0, 0, 0, 0};
+    key = Key{dev, dtype, pl->G, (int)pl->vec, (int)block, 0, 0, 0, 0};
     key.sum = max_clusters(k[0], pl->G, kFwdThreads, pl->sum_smem);
     key.rep = max_blocks(k[1], kFwdThreads, pl->rep_smem);
     key.rsum = max_blocks(k[2], kBwdThreads, pl->rsum_smem);
     key.grad = max_clusters(k[3], pl->G, kGradThreads, pl->grad_smem);
-    key.scan = max_blocks((const void*)mixer_carry_scan_kernel, kScanThreads, 0);
-    if (key.sum <= 0 || key.rep <= 0 || key.rsum <= 0 || key.grad <= 0 || key.scan <= 0) {
+    if (key.sum <= 0 || key.rep <= 0 || key.rsum <= 0 || key.grad <= 0) {
       set_err("occupancy query failed");
       return SPARC_ERR_LAUNCH;
     }
@@ -757,12 +597,11 @@ static int make_plan(long long B, long long T, int W, int dtype, bool block, Pla
   pl->rep_rows = clamp(key.rep / pl->G, pl->tiles);
   pl->rsum_rows = clamp(key.rsum / pl->G, pl->tiles);
   pl->grad_clusters = clamp(key.grad, pl->tiles);
-  pl->scan_ctas = clamp(key.scan, pl->scan_tiles);
   return SPARC_OK;
 }
 
 struct WsLayout {
-  size_t flags, sagg, sincl, agg, kout, part, total;
+  size_t agg, kout, part, total;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -770,12 +609,6 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 static WsLayout ws_layout(const Plan& pl, long long B, int M) {
   WsLayout L;
   size_t off = align256(sizeof(LaunchState));
-  L.flags = off;
-  off = align256(off + (size_t)pl.scan_tiles * sizeof(unsigned));
-  L.sagg = off;
-  off = align256(off + (size_t)pl.scan_tiles * kScanThreads * sizeof(float4));
-  L.sincl = off;
-  off = align256(off + (size_t)pl.scan_tiles * kScanThreads * sizeof(float2));
   L.agg = off;
   off = align256(off + (size_t)pl.tiles * pl.Mp * sizeof(float4));
   L.kout = off;
@@ -862,10 +695,9 @@ static bool act_tensor_map(CUtensorMap* map, const void* base, int dtype, long l
   return r == CUDA_SUCCESS;
 }
 
-static ScanParams scan_params(const Plan& pl, const WsLayout& L, char* ws, long long B, int M, int reverse,
+static ScanParams scan_params(const Plan& pl, const WsLayout& L, char* ws, int M, int reverse,
                               const float* init_r, const float* init_i, float* final_r, float* final_i,
-                              float2* out, unsigned max_spin, int deterministic, int inject_enable,
-                              long long inject_tile) {
+                              float2* out) {
   ScanParams sp;
   sp.agg = reinterpret_cast<const float4*>(ws + L.agg);
   sp.out = out;
@@ -873,22 +705,17 @@ static ScanParams scan_params(const Plan& pl, const WsLayout& L, char* ws, long 
   sp.init_i = init_i;
   sp.final_r = final_r;
   sp.final_i = final_i;
-  sp.ls = reinterpret_cast<LaunchState*>(ws);
-  sp.flags = reinterpret_cast<unsigned*>(ws + L.flags);
-  sp.sagg = reinterpret_cast<float4*>(ws + L.sagg);
-  sp.sincl = reinterpret_cast<float2*>(ws + L.sincl);
-  sp.B = B;
+  sp.G = pl.G;
   sp.M = M;
   sp.Mp = pl.Mp;
-  sp.G = pl.G;
   sp.chunks = pl.chunks;
-  sp.nseg = pl.nseg;
-  sp.tiles = pl.scan_tiles;
+  sp.span = pl.scan_span;
   sp.reverse = reverse;
-  sp.max_spin = max_spin ? max_spin : (1u << 20);
-  sp.deterministic = deterministic;
-  sp.inject_unpublished = inject_enable ? inject_tile : -1;
   return sp;
+}
+
+static cudaError_t launch_scan(const Plan& pl, const ScanParams& sp, cudaStream_t s) {
+  return launch_cluster((const void*)mixer_carry_scan_kernel, kScanQ, kScanThreads, (int)pl.scan_rows, 0, s, sp);
 }
 
 static int launch_error(cudaError_t e) {
@@ -944,12 +771,11 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
     rc = launch_error(launch_cluster(ksum, pl.G, kFwdThreads, pl.sum_clusters, pl.sum_smem, s, p));
   }
   if (rc != SPARC_OK) return rc;
-  const ScanParams sp = scan_params(pl, L, ws, p.B, p.M, 0, a->h0_r, a->h0_i, a->last_r, a->last_i,
-                                    reinterpret_cast<float2*>(a->carry), a->max_spin, a->deterministic,
-                                    a->inject_enable, a->inject_tile);
+  const ScanParams sp = scan_params(pl, L, ws, p.M, 0, a->h0_r, a->h0_i, a->last_r, a->last_i,
+                                    reinterpret_cast<float2*>(a->carry));
   {
     TimedLaunch tl(kTimeFwdScan, s);
-    rc = launch_error(launch_plain((const void*)mixer_carry_scan_kernel, dim3(pl.scan_ctas), kScanThreads, 0, s, sp));
+    rc = launch_error(launch_scan(pl, sp, s));
   }
   if (rc != SPARC_OK) return rc;
   TimedLaunch tl(kTimeFwdReplay, s);
@@ -1065,12 +891,11 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
     rc = launch_error(launch_plain(krsum, dim3(pl.G, pl.rsum_rows), kBwdThreads, pl.rsum_smem, s, p));
   }
   if (rc != SPARC_OK) return rc;
-  const ScanParams sp = scan_params(pl, L, ws, p.B, p.M, 1, a->grad_last_r, a->grad_last_i, a->grad_h0_r,
-                                    a->grad_h0_i, reinterpret_cast<float2*>(ws + L.kout), a->max_spin,
-                                    a->deterministic, a->inject_enable, a->inject_tile);
+  const ScanParams sp = scan_params(pl, L, ws, p.M, 1, a->grad_last_r, a->grad_last_i, a->grad_h0_r,
+                                    a->grad_h0_i, reinterpret_cast<float2*>(ws + L.kout));
   {
     TimedLaunch tl(kTimeBwdScan, s);
-    rc = launch_error(launch_plain((const void*)mixer_carry_scan_kernel, dim3(pl.scan_ctas), kScanThreads, 0, s, sp));
+    rc = launch_error(launch_scan(pl, sp, s));
   }
   if (rc != SPARC_OK) return rc;
   {
@@ -1160,10 +985,6 @@ int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
   char* ws = static_cast<char*>(noalloc_scratch(dev));
   if (ws == nullptr) { set_err("cudaGetSymbolAddress failed for the built-in scratch"); return SPARC_ERR_LAUNCH; }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // the array keeps the previous call's contents: its flag words, laid out for another shape,
-  // could alias this launch's, so they start from zero on every call (a memset, no allocation)
-  const cudaError_t e = cudaMemsetAsync(ws + L.flags, 0, L.sagg - L.flags, s);
-  if (e != cudaSuccess) { set_err(cudaGetErrorString(e)); return SPARC_ERR_LAUNCH; }
   return run_forward(a, pl, L, ws, s);
 }
 

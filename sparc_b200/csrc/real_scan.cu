@@ -67,6 +67,7 @@ struct RealParams {
   int chunks, nDB, Dp;
   long long tiles;
   unsigned max_spin;
+  long long inject_unpublished;  // test hook: this forward tile never publishes (-1: none)
 };
 
 // Lookback over real affine maps out = A*in + B (one per channel). Returns the carry-in.
@@ -74,14 +75,14 @@ template <int V, typename InclFn>
 __device__ __forceinline__ void real_lookback(const RealParams& p, unsigned epoch, long long ticket,
                                               long long dist, int steps_max, const float (&A)[V],
                                               const float (&Bv)[V], long long dp0, unsigned* s_state,
-                                              InclFn pred_inclusive, float (&carry)[V]) {
+                                              InclFn pred_inclusive, float (&carry)[V], bool publish = true) {
   const int tid = threadIdx.x;
   long long pred = ticket - dist;
   if (tid == 0) s_state[0] = ld_acquire(p.flags + pred);
   __syncthreads();
   const unsigned st0 = s_state[0];
   const bool pred_ready = ((st0 >> 2) == (epoch & 0x3fffffffu)) && (st0 & 3u) == kFlagInclusive;
-  if (!pred_ready) {
+  if (!pred_ready && publish) {
 #pragma unroll
     for (int v = 0; v < V; ++v) p.agg[ticket * p.Dp + dp0 + v] = make_float2(A[v], Bv[v]);
     __syncthreads();
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(kRealThreads) real_fwd_kernel(const RealParams
                          for (int v = 0; v < V; ++v)
                            h[v] = active ? __ldcg(carry + (b * chunks + (c - j)) * D + dp0 + v) : 0.0f;
                        },
-                       hin);
+                       hin, ticket != p.inject_unpublished);
     }
     float hout[V];
 #pragma unroll
@@ -214,7 +215,7 @@ __global__ void __launch_bounds__(kRealThreads) real_fwd_kernel(const RealParams
       for (int v = 0; v < V; ++v) p.carry[(b * p.chunks + c) * D + dp0 + v] = hout[v];
     }
     __syncthreads();  // thread 0's release store publishes what the barrier ordered before it
-    if (tid == 0) st_release(p.flags + ticket, make_flag(epoch, kFlagInclusive));
+    if (tid == 0 && ticket != p.inject_unpublished) st_release(p.flags + ticket, make_flag(epoch, kFlagInclusive));
 
     TIO* po = static_cast<TIO*>(p.out) + base;
     float h[V];
@@ -475,6 +476,7 @@ int sparc_real_scan_forward(const SparcRealFwdArgs* a, void* stream) {
   p.Dp = pl.Dp;
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
+  p.inject_unpublished = a->inject_enable ? a->inject_tile : -1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   TimedLaunch tl(kTimeRealFwd, s);
   if (a->dtype == SPARC_DTYPE_F32) real_fwd_kernel<float, 1><<<pl.grid_fwd, kRealThreads, 0, s>>>(p);
@@ -511,6 +513,7 @@ int sparc_real_scan_backward(const SparcRealBwdArgs* a, void* stream) {
   p.Dp = pl.Dp;
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
+  p.inject_unpublished = -1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   TimedLaunch tl(kTimeRealBwd, s);
   if (a->dtype == SPARC_DTYPE_F32) real_bwd_kernel<float, 1><<<pl.grid_bwd, kRealThreads, 0, s>>>(p);

@@ -42,7 +42,7 @@ class _SparcMixerFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, nu_log, theta_log, phase_direction, radial_direction, write_log_gain,
                 energy_response, write_phase_response, write_radial_response, h0_r, h0_i,
-                max_spin, inject_tile, reset=None, norm_weight=None, norm_eps=1e-6):
+                max_spin, reset=None, norm_weight=None, norm_eps=1e-6):
         L = _lib.lib()
         B, T, W = x.shape
         M = W // 2
@@ -72,8 +72,7 @@ class _SparcMixerFunction(torch.autograd.Function):
             _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
             last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
             _lib.ptr(nw), float(norm_eps), _lib.ptr(mask),
-            ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin, _lib.deterministic(),
-            1 if inject_tile is not None else 0, inject_tile if inject_tile is not None else 0)
+            ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin)
         _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_forward")
         ctx.save_for_backward(x, None if block else y, *params, carry, controls, *(h0 if h0 else (None, None)),
@@ -117,11 +116,11 @@ class _SparcMixerFunction(torch.autograd.Function):
             _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
             carry.data_ptr(), controls.data_ptr(), _lib.ptr(nw), _lib.ptr(mask), _lib.ptr(gnw),
             *[g[n].data_ptr() for n in _PARAMS],
-            ws.data_ptr(), ws.numel(), B, T, W, dt, ctx.max_spin, _lib.deterministic(), 0, 0)
+            ws.data_ptr(), ws.numel(), B, T, W, dt, ctx.max_spin)
         _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_backward")
         return (dx, *[g[n] for n in _PARAMS],
-                gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None, gnw, None)
+                gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, gnw, None)
 
 
 def reset_mask(segment_pos, reset_first: bool, shape, device):
@@ -139,13 +138,12 @@ def reset_mask(segment_pos, reset_first: bool, shape, device):
     return None
 
 
-def sparc_mixer(x, params, state=None, max_spin: int = 0, inject_unpublished_tile=None,
-                segment_pos=None, reset_first: bool = False):
+def sparc_mixer(x, params, state=None, max_spin: int = 0, segment_pos=None, reset_first: bool = False):
     """Functional form: (y, (last_r, last_i)) for parameters given as a mapping."""
     h0_r, h0_i = (None, None) if state is None else state
     reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
     y, lr, li = _SparcMixerFunction.apply(
-        x, *[params[n] for n in _PARAMS], h0_r, h0_i, int(max_spin), inject_unpublished_tile, reset)
+        x, *[params[n] for n in _PARAMS], h0_r, h0_i, int(max_spin), reset)
     return y, (lr, li)
 
 
@@ -159,7 +157,7 @@ def sparc_block(x, params, norm_weight, eps: float = 1e-6, state=None, segment_p
     h0_r, h0_i = (None, None) if state is None else state
     reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
     y, lr, li = _SparcMixerFunction.apply(
-        x.contiguous(), *[params[n] for n in _PARAMS], h0_r, h0_i, int(max_spin), None, reset, norm_weight,
+        x.contiguous(), *[params[n] for n in _PARAMS], h0_r, h0_i, int(max_spin), reset, norm_weight,
         float(eps))
     return y, (lr, li)
 

@@ -21,7 +21,7 @@ def _check(a, b, what):
     _lib.require_cuda(b, "b")
 
 
-def _forward(a, b, want_last, max_spin=0):
+def _forward(a, b, want_last, max_spin=0, inject_tile=None):
     L = _lib.lib()
     dtype = b.dtype
     a = a.to(dtype).contiguous()
@@ -36,7 +36,8 @@ def _forward(a, b, want_last, max_spin=0):
         _lib.check(-2, "sparc_real_workspace_bytes")
     ws = _lib.WORKSPACES.get(b.device, nbytes)
     args = _lib.RealFwdArgs(a.data_ptr(), b.data_ptr(), out.data_ptr(), _lib.ptr(last), carry.data_ptr(),
-                            ws.data_ptr(), ws.numel(), B, T, D, dt, max_spin)
+                            ws.data_ptr(), ws.numel(), B, T, D, dt, max_spin,
+                            1 if inject_tile is not None else 0, inject_tile if inject_tile is not None else 0)
     _lib.check(L.sparc_real_scan_forward(ctypes.byref(args), _lib.stream_handle(b.device)),
                "sparc_real_scan_forward")
     return a, b, out, carry, last

@@ -275,8 +275,9 @@ def deterministic():
 
 def test_split_sequence_equals_whole_large(deterministic):
     """Size-independent property at a config-5 layer shape: running the second half from the
-    first half's final state reproduces the whole-sequence output and state (bf16). With
-    chained (deterministic) carries the shared prefix is bitwise identical."""
+    first half's final state reproduces the whole-sequence output and state (bf16). (The carry
+    scan's spans depend on the sequence length, so the shared prefix agrees to rounding, not
+    bitwise; each result is bitwise reproducible for the same input.)"""
     params = _random_params(2048, 11)
     m = _module(params, 2048)
     gen = torch.Generator(device="cuda").manual_seed(3)
@@ -285,27 +286,30 @@ def test_split_sequence_equals_whole_large(deterministic):
         y, (lr, li) = m(x, return_cache=True)
         y1, (ar, ai) = m(x[:, :6000], return_cache=True)
         y2, (br, bi) = m(x[:, 6000:], return_cache=True, state=(ar, ai))
-    assert torch.equal(y1, y[:, :6000])
+    scale = y.float().abs().max().item()
+    assert (y1.float() - y[:, :6000].float()).abs().max().item() < 1e-2 * scale
     d = (y2.float() - y[:, 6000:].float()).abs().max().item()
     assert d < 2e-2 * y.float().abs().max().item()
     assert torch.allclose(br, lr, rtol=1e-3, atol=1e-3)
     assert torch.allclose(bi, li, rtol=1e-3, atol=1e-3)
 
 
-def test_fast_mode_matches_deterministic_mode():
-    """The default (decoupled lookback) carries differ from the chained ones only by rounding."""
+def test_forward_is_bitwise_reproducible():
+    """The carry scan composes its spans in a fixed order: repeated forwards agree bitwise,
+    with or without torch's deterministic mode."""
     params = _random_params(512, 9)
     m = _module(params, 512)
     gen = torch.Generator(device="cuda").manual_seed(2)
     x = torch.randn(8, 2048, 512, generator=gen, device="cuda")
     with torch.no_grad():
-        y_fast, _ = m(x)
+        y1, _ = m(x)
         torch.use_deterministic_algorithms(True)
         try:
-            y_det, _ = m(x)
+            y2, _ = m(x)
         finally:
             torch.use_deterministic_algorithms(False)
-    assert (y_fast - y_det).abs().max().item() < 1e-5 * y_det.abs().max().item()
+        y3, _ = m(x)
+    assert torch.equal(y1, y2) and torch.equal(y1, y3)
 
 
 def test_backward_is_deterministic(deterministic):
@@ -323,31 +327,6 @@ def test_backward_is_deterministic(deterministic):
         outs.append([xx.grad.clone()] + [getattr(m, k).grad.clone() for k in O.PARAM_NAMES])
     for a, b in zip(*outs):
         assert torch.equal(a, b)
-
-
-def test_lookback_timeout_sets_status():
-    """A carry-scan segment that never publishes makes its successor's bounded wait run out:
-    the kernel records the timeout in the workspace status word and the launch still
-    completes. (2048 tokens = 128 chunks = 8 segments per row; ticket 5 is row 1, segment 2.)"""
-    import sparc_b200
-    from sparc_b200 import _lib
-    from sparc_b200.mixer import sparc_mixer
-
-    sparc_b200.check_status()  # clean slate
-    params = _random_params(64, 4)
-    m = _module(params, 64)
-    x = torch.randn(2, 2048, 64, device="cuda")
-    with torch.no_grad():
-        y, _ = sparc_mixer(x, m._params(), max_spin=2000, inject_unpublished_tile=5)
-    torch.cuda.synchronize()
-    with pytest.raises(RuntimeError, match="timed out"):
-        sparc_b200.check_status()
-    # the context is still usable and a normal launch is clean afterwards
-    with torch.no_grad():
-        y2, _ = m(x)
-    sparc_b200.check_status()
-    assert torch.isfinite(y2).all()
-    assert _lib.STATUS_TIMEOUT == 1
 
 
 def test_bad_inputs_raise():

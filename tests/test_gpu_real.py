@@ -80,3 +80,27 @@ def test_real_large_split_property():
     _, last_tail = sparc_b200.real_scan_with_last(a2, b2)
     assert torch.allclose(last_tail, h, rtol=2e-3, atol=2e-3)
     assert torch.isfinite(out.float()).all()
+
+
+def test_lookback_timeout_sets_status():
+    """A real-scan tile that never publishes (host-chosen test hook) makes its successor's
+    bounded lookback wait run out: the kernel records the timeout in the workspace status word,
+    the launch completes, and the context stays usable. (B=2, 256 tokens of 16-token chunks,
+    64 channels: two tiles per chunk, so ticket 4 is chunk 2 of row 0 and chunk 3 waits on it.)"""
+    import sparc_b200
+    from sparc_b200 import _lib
+    from sparc_b200.real import _forward
+
+    sparc_b200.check_status()  # clean slate
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.rand(2, 256, 64, generator=gen, device="cuda") * 0.5 + 0.4
+    b = torch.randn(2, 256, 64, generator=gen, device="cuda")
+    _forward(a, b, False, max_spin=2000, inject_tile=4)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="timed out"):
+        sparc_b200.check_status()
+    out = sparc_b200.real_scan(a, b)  # a normal launch afterwards is clean
+    sparc_b200.check_status()
+    ref, _ = O.real_scan_forward(a.double().cpu().numpy(), b.double().cpu().numpy())
+    assert O.rel_l2(out.double().cpu().numpy(), ref) < 1e-4
+    assert _lib.STATUS_TIMEOUT == 1
