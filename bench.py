@@ -303,6 +303,7 @@ def run_layer(args, wl, world, rank, local):
         y.backward(g)
         if reducer is not None:
             reducer()  # the one exchange step (NCCL all-reduce of the parameter gradients)
+    del y  # drop the captured autograd graph (its gradient-accumulation nodes belong to `stream`)
 
     def step():
         graph.replay()
