@@ -81,6 +81,17 @@ extern "C" {
  * `out`, and relu_mask the bits of relu(h) > 0 that the backward needs in place of y. The
  * backward then returns the block input's gradient in dx (the residual path included) and the
  * norm weight's in grad_norm_weight. */
+/* Projection mode (projections given): the recurrence core of the projection variant, the JAX
+ * sequence layer and RTRL cell of sparc-impl (recurrence.py:20-63, layers.py:156-194), whose
+ * content and controls come from matrix products the caller computes: x is the content input
+ * u = [x_in content_real, x_in content_imag] ([batch, length, width], width = 2M), projections
+ * the per-token controller projections p = [x_in, 1] phase_controller / retention_controller
+ * ([batch, length, 2] float32, bias included), and y receives the states [Re h, Im h] with no
+ * relu (the caller's readout follows). The content is tanh(u), or u with content_linear
+ * (content_activation "linear"). The directions are not read (may be NULL). The backward takes
+ * dy on the states and returns the content input's gradient in dx and the projections' in
+ * grad_projections; the caller finishes x_in's and the matrices' gradients with the transposed
+ * products. */
 typedef struct SparcMixerFwdArgs {
   const void* x;                       /* [batch, length, width]  activations (dtype) */
   void* y;                             /* [batch, length, width]  output (dtype) */
@@ -101,6 +112,8 @@ typedef struct SparcMixerFwdArgs {
   const float* norm_weight;            /* [width]: the call is a block (below), or NULL */
   float norm_eps;                      /* block: RMSNorm epsilon */
   unsigned* relu_mask;                 /* block: [batch, length, sparc_mixer_mask_words(width)] out */
+  const float* projections;            /* [batch, length, 2]: projection mode (above), or NULL */
+  int content_linear;                  /* projection mode: content u instead of tanh(u) */
   void* workspace;
   size_t workspace_bytes;
   long long batch;
@@ -116,7 +129,8 @@ typedef struct SparcMixerFwdArgs {
  * fixed order (deterministic run to run). */
 typedef struct SparcMixerBwdArgs {
   const void* x;                       /* [batch, length, width] forward input (dtype) */
-  const void* y;                       /* [batch, length, width] the forward's output (dtype) */
+  const void* y;                       /* [batch, length, width] the forward's output (dtype);
+                                          not read by a block or in projection mode */
   const void* dy;                      /* [batch, length, width] (dtype) */
   void* dx;                            /* [batch, length, width] (dtype) */
   const float* nu_log;
@@ -139,12 +153,14 @@ typedef struct SparcMixerBwdArgs {
   float* grad_norm_weight;             /* block: [width] */
   float* grad_nu_log;                  /* [M] */
   float* grad_theta_log;               /* [M] */
-  float* grad_phase_direction;         /* [width + 1] */
-  float* grad_radial_direction;        /* [width + 1] */
+  float* grad_phase_direction;         /* [width + 1] (NULL in projection mode) */
+  float* grad_radial_direction;        /* [width + 1] (NULL in projection mode) */
   float* grad_write_log_gain;          /* [M] */
   float* grad_energy_response;         /* [M], written with zeros */
   float* grad_write_phase_response;    /* [M] */
   float* grad_write_radial_response;   /* [M] */
+  float* grad_projections;             /* projection mode: [batch, length, 2] out, else NULL */
+  int content_linear;                  /* projection mode: as given to the forward */
   void* workspace;
   size_t workspace_bytes;
   long long batch;

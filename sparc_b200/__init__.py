@@ -7,6 +7,7 @@ All compute runs in the sm_100a kernels of ``libsparc_b200.so`` (C ABI in
 """
 from .mixer import SPARCMixer, sparc_block, sparc_decode_step, sparc_mixer
 from .stack import SPARCBlock, SPARCStack
+from .projection import SPARCSequenceLayer, sparc_projection_states, sparc_sequence_layer
 from .real import real_chunk_scan, real_scan, real_scan_with_last
 from . import _lib
 
@@ -28,4 +29,5 @@ def check_status(clear: bool = True) -> None:
 
 
 __all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack", "sparc_decode_step",
+           "SPARCSequenceLayer", "sparc_sequence_layer", "sparc_projection_states",
            "real_scan", "real_chunk_scan", "real_scan_with_last", "check_status", "library_path"]

@@ -34,6 +34,7 @@ class MixerFwdArgs(ctypes.Structure):
         ("h0_r", _vp), ("h0_i", _vp), ("last_r", _vp), ("last_i", _vp), ("carry", _vp),
         ("controls", _vp), ("reset", _vp),
         ("norm_weight", _vp), ("norm_eps", ctypes.c_float), ("relu_mask", _vp),
+        ("projections", _vp), ("content_linear", ctypes.c_int),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint),
@@ -51,6 +52,7 @@ class MixerBwdArgs(ctypes.Structure):
         ("grad_nu_log", _vp), ("grad_theta_log", _vp), ("grad_phase_direction", _vp),
         ("grad_radial_direction", _vp), ("grad_write_log_gain", _vp), ("grad_energy_response", _vp),
         ("grad_write_phase_response", _vp), ("grad_write_radial_response", _vp),
+        ("grad_projections", _vp), ("content_linear", ctypes.c_int),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint),

@@ -44,6 +44,23 @@ __host__ __device__ constexpr int token_unroll() { return SPARC_TOKEN_UNROLL == 
 // (whose shared-memory tiles are twice as large per token).
 __host__ __device__ constexpr int chunk_for(int dtype) { return dtype == SPARC_DTYPE_BF16 ? 16 : 8; }
 
+// What the tile kernels compute (their kMode template argument):
+constexpr int kModePlain = 0;  // y = relu(SPARC(x)), controls projected from x (the torch module)
+constexpr int kModeBlock = 1;  // y = x + relu(SPARC(RMSNorm(x))) (a pre-norm residual block)
+constexpr int kModeProj = 2;   // h = SPARC states from a content input u [B, T, 2M] and given
+                               // per-token controller projections p [B, T, 2] (the projection
+                               // variant: u = x Wc and p = [x, 1] c come from matrix products)
+
+// Content of a token: tanh(u), or u itself for a projection-mode layer with a linear content
+// activation (lin, uniform over the launch).
+template <bool kFast, int kMode>
+__device__ __forceinline__ float2 content2(float2 u, bool lin) {
+  if constexpr (kMode == kModeProj) {
+    if (lin) return u;
+  }
+  return tanh_t2<kFast>(u);
+}
+
 struct ModeConst {
   float nu;      // e^{nu_log}
   float nl2e;    // nu * log2(e)
@@ -78,10 +95,12 @@ __device__ __forceinline__ ModeConst load_mode(const MixerParamPtrs& pp, int m, 
   mc.stat = mc.nu * expf(-2.0f * mc.nu) / den;
   mc.wpr = active ? pp.wpr[m] : 0.0f;
   mc.wrr = active ? pp.wrr[m] : 0.0f;
-  mc.d0r = active ? pp.phase_dir[m] : 0.0f;
-  mc.d0i = active ? pp.phase_dir[M + m] : 0.0f;
-  mc.d1r = active ? pp.radial_dir[m] : 0.0f;
-  mc.d1i = active ? pp.radial_dir[M + m] : 0.0f;
+  // (a projection-mode launch has no controller directions: its controls come precomputed)
+  const bool dirs = active && pp.phase_dir != nullptr;
+  mc.d0r = dirs ? pp.phase_dir[m] : 0.0f;
+  mc.d0i = dirs ? pp.phase_dir[M + m] : 0.0f;
+  mc.d1r = dirs ? pp.radial_dir[m] : 0.0f;
+  mc.d1i = dirs ? pp.radial_dir[M + m] : 0.0f;
   return mc;
 }
 
@@ -370,8 +389,8 @@ struct ReduceParams {
   float* g_wpr;
   float* g_wrr;
   float* g_energy;
-  float* g_phase_dir;   // [W+1]
-  float* g_radial_dir;  // [W+1]
+  float* g_phase_dir;   // [W+1], or null (projection mode)
+  float* g_radial_dir;  // [W+1], or null (projection mode)
   float* g_norm_w;      // [W] (block) or null
 };
 
@@ -387,7 +406,7 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
   const int lane = threadIdx.x, w = threadIdx.y;
   const int q = blockIdx.y;
   if (q == kPartModes) {
-    if (blockIdx.x != 0 || w >= 2) return;
+    if (blockIdx.x != 0 || w >= 2 || r.g_phase_dir == nullptr) return;
     const double* pb = r.part + (long long)r.clusters * kPartModes * r.Mp;
     double t = 0.0;
     for (int k = lane; k < r.clusters; k += 32) t += pb[2 * k + w];
@@ -425,10 +444,10 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
       case 2: r.g_wlg[m] = (float)t; break;
       case 3: r.g_wpr[m] = (float)t; break;
       case 4: r.g_wrr[m] = (float)t; break;
-      case 5: r.g_phase_dir[m] = (float)t; break;
-      case 6: r.g_phase_dir[r.M + m] = (float)t; break;
-      case 7: r.g_radial_dir[m] = (float)t; break;
-      case 8: r.g_radial_dir[r.M + m] = (float)t; break;
+      case 5: if (r.g_phase_dir) r.g_phase_dir[m] = (float)t; break;
+      case 6: if (r.g_phase_dir) r.g_phase_dir[r.M + m] = (float)t; break;
+      case 7: if (r.g_radial_dir) r.g_radial_dir[m] = (float)t; break;
+      case 8: if (r.g_radial_dir) r.g_radial_dir[r.M + m] = (float)t; break;
       case 9: if (r.g_norm_w) r.g_norm_w[m] = (float)t; break;
       default: if (r.g_norm_w) r.g_norm_w[r.M + m] = (float)t; break;
     }
@@ -438,7 +457,7 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
 // ------------------------------------------------------------------------------ host side
 struct Plan {
   int dtype, C, chunks;
-  bool block;              // RMSNorm + mixer + residual kernels
+  int mode;                // kModePlain, kModeBlock or kModeProj
   long long tiles;         // B * chunks
   int G, Mp;               // CTAs of 256 modes per tile; modes padded to G * 256
   bool vec, tma;
@@ -495,31 +514,37 @@ static int max_blocks(const void* kernel, int NT, size_t dyn_smem) {
   return per_sm * sms;
 }
 
-// Kernel instances per activation type (bfloat16 uses the hardware tanh; float32 the accurate one).
+// Kernel instances per activation type (bfloat16 uses the hardware tanh; float32 the accurate
+// one) and mode (kModePlain, kModeBlock, kModeProj).
 template <typename TIO>
 struct Kernels {
   static constexpr bool kFast = std::is_same<TIO, __nv_bfloat16>::value;
   static constexpr int C = chunk_for(kFast ? SPARC_DTYPE_BF16 : SPARC_DTYPE_F32);
-  // block = RMSNorm + mixer + residual (norm weight given)
-  static const void* sum(bool block) {
-    return block ? (const void*)mixer_fwd_summary_kernel<TIO, C, kFast, true>
-                 : (const void*)mixer_fwd_summary_kernel<TIO, C, kFast, false>;
+  template <int kM>
+  static const void* sum_m() { return (const void*)mixer_fwd_summary_kernel<TIO, C, kFast, kM>; }
+  template <int kM>
+  static const void* rep_m(bool vec) {
+    return vec ? (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, true, kM>
+               : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false, kM>;
   }
-  static const void* rep(bool vec, bool block) {
-    if (block) return vec ? (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, true, true>
-                          : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false, true>;
-    return vec ? (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, true, false>
-               : (const void*)mixer_fwd_replay_kernel<TIO, C, kFast, false, false>;
+  template <int kM>
+  static const void* rsum_m() { return (const void*)mixer_bwd_summary_kernel<TIO, C, kFast, kM>; }
+  template <int kM>
+  static const void* grad_m(bool vec) {
+    return vec ? (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, true, kM>
+               : (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, false, kM>;
   }
-  static const void* rsum(bool block) {
-    return block ? (const void*)mixer_bwd_summary_kernel<TIO, C, kFast, true>
-                 : (const void*)mixer_bwd_summary_kernel<TIO, C, kFast, false>;
+  static const void* sum(int mode) {
+    return mode == kModeBlock ? sum_m<kModeBlock>() : mode == kModeProj ? sum_m<kModeProj>() : sum_m<kModePlain>();
   }
-  static const void* grad(bool vec, bool block) {
-    if (block) return vec ? (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, true, true>
-                          : (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, false, true>;
-    return vec ? (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, true, false>
-               : (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, false, false>;
+  static const void* rep(bool vec, int mode) {
+    return mode == kModeBlock ? rep_m<kModeBlock>(vec) : mode == kModeProj ? rep_m<kModeProj>(vec) : rep_m<kModePlain>(vec);
+  }
+  static const void* rsum(int mode) {
+    return mode == kModeBlock ? rsum_m<kModeBlock>() : mode == kModeProj ? rsum_m<kModeProj>() : rsum_m<kModePlain>();
+  }
+  static const void* grad(bool vec, int mode) {
+    return mode == kModeBlock ? grad_m<kModeBlock>(vec) : mode == kModeProj ? grad_m<kModeProj>(vec) : grad_m<kModePlain>(vec);
   }
   static size_t sum_smem() { return sizeof(SumSmem<TIO, C>); }
   static size_t rep_smem() { return sizeof(RepSmem<TIO, C>); }
@@ -534,20 +559,20 @@ static void plan_kernels(Plan* pl, const void** k) {
   pl->rep_smem = K::rep_smem();
   pl->rsum_smem = K::rsum_smem();
   pl->grad_smem = K::grad_smem();
-  k[0] = K::sum(pl->block);
-  k[1] = K::rep(pl->vec, pl->block);
-  k[2] = K::rsum(pl->block);
-  k[3] = K::grad(pl->vec, pl->block);
+  k[0] = K::sum(pl->mode);
+  k[1] = K::rep(pl->vec, pl->mode);
+  k[2] = K::rsum(pl->mode);
+  k[3] = K::grad(pl->vec, pl->mode);
 }
 
-static int make_plan(long long B, long long T, int W, int dtype, bool block, Plan* pl) {
+static int make_plan(long long B, long long T, int W, int dtype, int mode, Plan* pl) {
   if (B <= 0 || T <= 0 || W <= 0) { set_err("batch, length and width must be positive"); return SPARC_ERR_SHAPE; }
   if (W % 2) { set_err("SPARC rnn_width must be even"); return SPARC_ERR_SHAPE; }
   if (dtype != SPARC_DTYPE_F32 && dtype != SPARC_DTYPE_BF16) { set_err("unsupported dtype"); return SPARC_ERR_DTYPE; }
   const int M = W / 2;
   if (M > 8 * kFwdModes) { set_err("width above 4096 is not supported"); return SPARC_ERR_SHAPE; }
   pl->dtype = dtype;
-  pl->block = block;
+  pl->mode = mode;
   pl->C = chunk_for(dtype);
   pl->chunks = (int)((T + pl->C - 1) / pl->C);
   pl->tiles = B * pl->chunks;
@@ -567,7 +592,7 @@ static int make_plan(long long B, long long T, int W, int dtype, bool block, Pla
 
   int dev = 0;
   cudaGetDevice(&dev);
-  struct Key { int dev, dtype, G, vec, block; int sum, rep, rsum, grad; };
+  struct Key { int dev, dtype, G, vec, mode; int sum, rep, rsum, grad; };
   static std::mutex mu;
   static Key cache[64];
   static int ncache = 0;
@@ -575,13 +600,13 @@ static int make_plan(long long B, long long T, int W, int dtype, bool block, Pla
   const Key* hit = nullptr;
   for (int i = 0; i < ncache; ++i) {
     const Key& kk = cache[i];
-    if (kk.dev == dev && kk.dtype == dtype && kk.G == pl->G && kk.vec == (int)pl->vec && kk.block == (int)block) hit = &kk;
+    if (kk.dev == dev && kk.dtype == dtype && kk.G == pl->G && kk.vec == (int)pl->vec && kk.mode == mode) hit = &kk;
   }
   Key key;
   if (hit != nullptr) {
     key = *hit;
   } else {
-    key = Key{dev, dtype, pl->G, (int)pl->vec, (int)block, 0, 0, 0, 0};
+    key = Key{dev, dtype, pl->G, (int)pl->vec, mode, 0, 0, 0, 0};
     key.sum = max_clusters(k[0], pl->G, kFwdThreads, pl->sum_smem);
     key.rep = max_blocks(k[1], kFwdThreads, pl->rep_smem);
     key.rsum = max_blocks(k[2], kBwdThreads, pl->rsum_smem);
@@ -724,16 +749,24 @@ static int launch_error(cudaError_t e) {
   return SPARC_ERR_LAUNCH;
 }
 
+// The kernels' mode from which optional inputs are given (-1: both a norm weight and projections).
+static int fwd_mode(const SparcMixerFwdArgs* a) {
+  if (a->projections != nullptr) return a->norm_weight != nullptr ? -1 : kModeProj;
+  return a->norm_weight != nullptr ? kModeBlock : kModePlain;
+}
+
 // Validate the forward arguments and enqueue summary -> scan -> replay (scratch at `ws`).
 static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayout& L, char* ws, cudaStream_t s) {
-  if (!a->x || !a->y || !a->carry || !a->controls || !a->nu_log || !a->theta_log || !a->phase_direction ||
-      !a->radial_direction || !a->write_log_gain || !a->write_phase_response || !a->write_radial_response) {
+  const bool proj = pl.mode == kModeProj;
+  if (!a->x || !a->y || !a->carry || !a->controls || !a->nu_log || !a->theta_log ||
+      (!proj && (!a->phase_direction || !a->radial_direction)) || !a->write_log_gain ||
+      !a->write_phase_response || !a->write_radial_response) {
     set_err("null tensor pointer"); return SPARC_ERR_ARG;
   }
   if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->last_r == nullptr) != (a->last_i == nullptr)) {
     set_err("h0 / last pointers must be given in pairs"); return SPARC_ERR_ARG;
   }
-  if (pl.block && (a->relu_mask == nullptr || !(a->norm_eps >= 0.0f))) {
+  if (pl.mode == kModeBlock && (a->relu_mask == nullptr || !(a->norm_eps >= 0.0f))) {
     set_err("a block (norm_weight given) needs relu_mask and a non-negative norm_eps"); return SPARC_ERR_ARG;
   }
   FwdParams p;
@@ -743,8 +776,11 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
   p.mask_words = pl.G * 16;
   p.x = a->x;
   p.y = a->y;
-  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
-                        a->write_log_gain, a->write_phase_response, a->write_radial_response};
+  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, proj ? nullptr : a->phase_direction,
+                        proj ? nullptr : a->radial_direction, a->write_log_gain, a->write_phase_response,
+                        a->write_radial_response};
+  p.proj_in = reinterpret_cast<const float2*>(a->projections);
+  p.content_linear = a->content_linear;
   p.h0_r = a->h0_r;
   p.h0_i = a->h0_i;
   p.ctl = reinterpret_cast<TokenCtl*>(a->controls);
@@ -763,8 +799,8 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
   p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->controls) && aligned16(a->carry) &&
                       act_tensor_map(&p.map_x, a->x, a->dtype, p.B * p.T, p.M, p.W, pl.C) ? 1 : 0;
   const bool bf = a->dtype == SPARC_DTYPE_BF16;
-  const void* ksum = bf ? Kernels<__nv_bfloat16>::sum(pl.block) : Kernels<float>::sum(pl.block);
-  const void* krep = bf ? Kernels<__nv_bfloat16>::rep(pl.vec, pl.block) : Kernels<float>::rep(pl.vec, pl.block);
+  const void* ksum = bf ? Kernels<__nv_bfloat16>::sum(pl.mode) : Kernels<float>::sum(pl.mode);
+  const void* krep = bf ? Kernels<__nv_bfloat16>::rep(pl.vec, pl.mode) : Kernels<float>::rep(pl.vec, pl.mode);
   int rc;
   {
     TimedLaunch tl(kTimeFwdSummary, s);
@@ -798,11 +834,11 @@ long long sparc_mixer_carry_chunks(long long length, int dtype) {
 }
 
 size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype) {
-  // one size for the plain mixer and the block (their gradient kernels' occupancy may differ)
+  // one size for every mode (their gradient kernels' occupancy may differ)
   size_t total = 0;
-  for (int block = 0; block < 2; ++block) {
+  for (int mode = kModePlain; mode <= kModeProj; ++mode) {
     Plan pl;
-    if (make_plan(batch, length, width, dtype, block != 0, &pl) != SPARC_OK) return 0;
+    if (make_plan(batch, length, width, dtype, mode, &pl) != SPARC_OK) return 0;
     total = std::max(total, ws_layout(pl, batch, width / 2).total);
   }
   return total;
@@ -817,8 +853,10 @@ int sparc_mixer_mask_words(int width) {
 
 int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
+  const int mode = fwd_mode(a);
+  if (mode < 0) { set_err("norm_weight and projections exclude each other"); return SPARC_ERR_ARG; }
   Plan pl;
-  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, a->norm_weight != nullptr, &pl);
+  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, mode, &pl);
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
@@ -829,17 +867,21 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   Plan pl;
   const bool block = a->norm_weight != nullptr;
-  int rc = make_plan(a->batch, a->length, a->width, a->dtype, block, &pl);
+  const bool proj = a->grad_projections != nullptr;
+  if (block && proj) { set_err("norm_weight and grad_projections exclude each other"); return SPARC_ERR_ARG; }
+  int rc = make_plan(a->batch, a->length, a->width, a->dtype, proj ? kModeProj : block ? kModeBlock : kModePlain, &pl);
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
-  if (block ? (a->relu_mask == nullptr || a->grad_norm_weight == nullptr) : a->y == nullptr) {
+  if (block ? (a->relu_mask == nullptr || a->grad_norm_weight == nullptr) : (!proj && a->y == nullptr)) {
     set_err(block ? "a block needs relu_mask and grad_norm_weight" : "the forward's output y is needed");
     return SPARC_ERR_ARG;
   }
   if (!a->x || !a->dy || !a->dx || !a->carry || !a->controls || !a->grad_nu_log || !a->grad_theta_log ||
-      !a->grad_phase_direction || !a->grad_radial_direction || !a->grad_write_log_gain ||
-      !a->grad_energy_response || !a->grad_write_phase_response || !a->grad_write_radial_response) {
+      (!proj && (!a->grad_phase_direction || !a->grad_radial_direction || !a->phase_direction ||
+                 !a->radial_direction)) ||
+      !a->grad_write_log_gain || !a->grad_energy_response || !a->grad_write_phase_response ||
+      !a->grad_write_radial_response) {
     set_err("null tensor pointer"); return SPARC_ERR_ARG;
   }
   if ((a->h0_r == nullptr) != (a->h0_i == nullptr) || (a->grad_last_r == nullptr) != (a->grad_last_i == nullptr) ||
@@ -852,8 +894,11 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.y = a->y;
   p.dy = a->dy;
   p.dx = a->dx;
-  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
-                        a->write_log_gain, a->write_phase_response, a->write_radial_response};
+  p.pp = MixerParamPtrs{a->nu_log, a->theta_log, proj ? nullptr : a->phase_direction,
+                        proj ? nullptr : a->radial_direction, a->write_log_gain, a->write_phase_response,
+                        a->write_radial_response};
+  p.dp_out = reinterpret_cast<float2*>(a->grad_projections);
+  p.content_linear = a->content_linear;
   p.h0_r = a->h0_r;
   p.h0_i = a->h0_i;
   p.glast_r = a->grad_last_r;
@@ -876,16 +921,16 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.tiles = pl.tiles;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
   const long long rows = p.B * p.T;
-  // (a block reads no y: its relu mask comes as bits)
+  // (a block reads no y: its relu mask comes as bits; the projection mode has no relu)
   p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->y) && aligned16(a->dy) && aligned16(a->controls) &&
                       aligned16(a->carry) && aligned16(a->relu_mask) &&
                       act_tensor_map(&p.map_x, a->x, a->dtype, rows, p.M, p.W, pl.C) &&
-                      (block || act_tensor_map(&p.map_y, a->y, a->dtype, rows, p.M, p.W, pl.C)) &&
+                      (block || proj || act_tensor_map(&p.map_y, a->y, a->dtype, rows, p.M, p.W, pl.C)) &&
                       act_tensor_map(&p.map_dy, a->dy, a->dtype, rows, p.M, p.W, pl.C) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf = a->dtype == SPARC_DTYPE_BF16;
-  const void* krsum = bf ? Kernels<__nv_bfloat16>::rsum(block) : Kernels<float>::rsum(block);
-  const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad(pl.vec, block) : Kernels<float>::grad(pl.vec, block);
+  const void* krsum = bf ? Kernels<__nv_bfloat16>::rsum(pl.mode) : Kernels<float>::rsum(pl.mode);
+  const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad(pl.vec, pl.mode) : Kernels<float>::grad(pl.vec, pl.mode);
   {
     TimedLaunch tl(kTimeBwdSummary, s);
     rc = launch_error(launch_plain(krsum, dim3(pl.G, pl.rsum_rows), kBwdThreads, pl.rsum_smem, s, p));
@@ -916,8 +961,8 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   r.g_wpr = a->grad_write_phase_response;
   r.g_wrr = a->grad_write_radial_response;
   r.g_energy = a->grad_energy_response;
-  r.g_phase_dir = a->grad_phase_direction;
-  r.g_radial_dir = a->grad_radial_direction;
+  r.g_phase_dir = proj ? nullptr : a->grad_phase_direction;
+  r.g_radial_dir = proj ? nullptr : a->grad_radial_direction;
   r.g_norm_w = block ? a->grad_norm_weight : nullptr;
   TimedLaunch tl(kTimeBwdReduce, s);
   return launch_error(launch_ex((const void*)mixer_reduce_kernel, dim3((pl.Mp + 31) / 32, kPartModes + 1),
@@ -964,8 +1009,10 @@ size_t sparc_mixer_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 
 int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
+  const int mode = fwd_mode(a);
+  if (mode < 0) { set_err("norm_weight and projections exclude each other"); return SPARC_ERR_ARG; }
   Plan pl;
-  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, a->norm_weight != nullptr, &pl);
+  const int rc = make_plan(a->batch, a->length, a->width, a->dtype, mode, &pl);
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   // the forward uses the launch state, the scan's flags and segment arrays, and the chunk

@@ -64,6 +64,8 @@ struct BwdParams {
   const float2* kout;    // [B, chunks, M] adjoint carry leaving each chunk (scan output)
   float4* agg;           // [B, chunks, Mp] reverse aggregates (summary output)
   double* part;          // [clusters][kPartModes][Mp] then [clusters][2] bias partials
+  float2* dp_out;        // [B*T] controller-projection gradients (dp0, dp1) (kModeProj)
+  int content_linear;    // kModeProj: the content is u itself instead of tanh(u)
   LaunchState* ls;
   long long B, T;
   int W, M, Mp, chunks;
@@ -75,8 +77,9 @@ struct BwdParams {
 
 
 // ------------------------------------------------------------------------------ reverse summary
-template <typename TIO, int C, bool kFast, bool kBlock>
+template <typename TIO, int C, bool kFast, int kMode>
 __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __grid_constant__ BwdParams p) {
+  constexpr bool kBlock = kMode == kModeBlock, kProj = kMode == kModeProj;  // (projection mode: no relu)
   const int g = blockIdx.x;
   const int tid = threadIdx.x;
   const int M = p.M, W = p.W;
@@ -113,7 +116,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
     if (p.use_tma) {
       if (tid == 0) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&S.bar[buf], (kBlock ? 1u : 2u) * act_box_bytes<TIO, C, kBwdModes>() +
+        mbar_arrive_expect_tx(&S.bar[buf], (kBlock || kProj ? 1u : 2u) * act_box_bytes<TIO, C, kBwdModes>() +
                                                (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid +
                                                (kBlock ? 64u * (unsigned)r.nvalid : 0u));
         const int row = (int)(r.b * T + r.t0);
@@ -121,7 +124,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
         if constexpr (kBlock) {
           for (int t = 0; t < r.nvalid; ++t)
             bulk_copy_g2s(&S.mask[buf][t][0], msrc + (long long)t * p.mask_words, 64u, &S.bar[buf]);
-        } else {
+        } else if constexpr (!kProj) {
           tma_load_3d(&S.y[buf][0][0][0], &p.map_y, mbase, 0, row, &S.bar[buf]);
         }
         bulk_copy_g2s(&S.ctl[buf][0], csrc, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar[buf]);
@@ -130,7 +133,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
       load_act_rows<TIO, kBwdModes>(dsrc, W, M, mbase, r.nvalid, S.dy[buf], kBwdThreads);
       if constexpr (kBlock) {
         for (int j = tid; j < 16 * r.nvalid; j += kBwdThreads) S.mask[buf][j >> 4][j & 15] = msrc[(long long)(j >> 4) * p.mask_words + (j & 15)];
-      } else {
+      } else if constexpr (!kProj) {
         load_act_rows<TIO, kBwdModes>(ysrc, W, M, mbase, r.nvalid, S.y[buf], kBwdThreads);
       }
       for (int t = tid; t < r.nvalid; t += kBwdThreads) S.ctl[buf][t] = csrc[t];
@@ -165,7 +168,9 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
           const float gr = to_float(dyt[t][0][tid]);
           const float gi = to_float(dyt[t][1][tid]);
           bool on_r, on_i;
-          if constexpr (kBlock) {  // bit (mode % 64) / 2 of word 4 (mode / 64) + mode % 2 (+2: imaginary)
+          if constexpr (kProj) {
+            on_r = on_i = true;
+          } else if constexpr (kBlock) {  // bit (mode % 64) / 2 of word 4 (mode / 64) + mode % 2 (+2: imaginary)
             const unsigned* mw = &S.mask[buf][t][(tid >> 6) * 4 + (tid & 1)];
             const unsigned bit = 1u << ((tid & 63) >> 1);
             on_r = (mw[0] & bit) != 0u;
@@ -222,9 +227,9 @@ __device__ __forceinline__ void st2(float* p, float2 v) { *reinterpret_cast<floa
 // Gradient contributions of one token for the thread's two modes: updates the adjoint lam in
 // place (to conj(a) lam) and returns the write-path dx of the content; returns the token's dEta /
 // dDelta contributions in ve / vd (per lane) and adds the per-mode parameter terms to fa.
-template <bool kFast>
+template <bool kFast, int kMode>
 __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& tc, Cx2& lam, Cx2 pv, float2 cx,
-                                          float2 cy, float2& ve, float2& vd, float2 (&fa)[5]) {
+                                          float2 cy, float2& ve, float2& vd, float2 (&fa)[5], bool lin) {
   const float2 delta = make_float2(tc.ed.z, tc.ed.w), tau0 = make_float2(tc.tau.x, tc.tau.y),
                tau1 = make_float2(tc.tau.z, tc.tau.w);
   // with a reset the transition (k.a) is zero, so every transition-gradient term below vanishes
@@ -234,8 +239,8 @@ __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& 
   const float2 pg = sub2(mul2(gai, k.a.re), mul2(gar, k.a.im));
   const float2 radial = mul2(k.z, sub2(mul2(mul2(k.rho, delta), pg), fma2(gar, k.a.re, mul2(gai, k.a.im))));
   const float2 dscan = sub2(pg, mul2(k.rho, pg));
-  const float2 cr = tanh_t2<kFast>(cx);
-  const float2 ci = tanh_t2<kFast>(cy);
+  const float2 cr = content2<kFast, kMode>(cx, lin);
+  const float2 ci = content2<kFast, kMode>(cy, lin);
   const float2 gg = mul2(k.gain, fma2(lam.re, cr, mul2(lam.im, ci)));
   const float2 gq = mul2(gg, fma2(bcast2(-0.5f), k.gate, bcast2(1.0f)));
   const float2 dyn = mul2(mul2(k.z, mul2(k.rho, k.rho)), rcp_2(k.num));
@@ -246,8 +251,10 @@ __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& 
   fa[2] = add2(fa[2], gg);
   fa[3] = fma2(gq, tau0, fa[3]);
   fa[4] = fma2(gq, tau1, fa[4]);
-  const Cx2 dxc = Cx2{mul2(mul2(lam.re, k.gain), sub2(bcast2(1.0f), mul2(cr, cr))),
-                      mul2(mul2(lam.im, k.gain), sub2(bcast2(1.0f), mul2(ci, ci)))};
+  // the content's slope: 1 - tanh^2, or 1 for a linear content
+  const float2 sr = lin ? bcast2(1.0f) : sub2(bcast2(1.0f), mul2(cr, cr));
+  const float2 si = lin ? bcast2(1.0f) : sub2(bcast2(1.0f), mul2(ci, ci));
+  const Cx2 dxc = Cx2{mul2(mul2(lam.re, k.gain), sr), mul2(mul2(lam.im, k.gain), si)};
   lam = Cx2{fma2(k.a.re, lam.re, mul2(k.a.im, lam.im)), sub2(mul2(k.a.re, lam.im), mul2(k.a.im, lam.re))};
   return dxc;
 }
@@ -256,9 +263,11 @@ __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& 
 // In a block (kBlock) the mixer's input is n = x r w (RMSNorm) and the output gradient also
 // flows straight to x (residual): dx = dy + r w dn - (r^3 / W) x sum_j(x_j w_j dn_j), with dn the
 // mixer's input gradient; the weight's gradient sums x r dn per column.
-template <typename TIO, int C, bool kFast, bool kVec, bool kBlock>
+template <typename TIO, int C, bool kFast, bool kVec, int kMode>
 __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const __grid_constant__ BwdParams p) {
   static_assert(C % kGroup == 0, "the reverse walk runs in groups of kGroup tokens");
+  constexpr bool kBlock = kMode == kModeBlock, kProj = kMode == kModeProj;
+  const bool lin = kProj && p.content_linear != 0;
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
   const int G = (int)cluster.num_blocks();
@@ -374,7 +383,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
             float2 nr, ni;
             mixer_in(t, Pair<TIO>::load(&S.x[t][0][2 * tid]), Pair<TIO>::load(&S.x[t][1][2 * tid]), nr, ni);
             const TokenCoef2 k = token_coef2<kFast>(mc, S.ctl[t]);
-            h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(nr)), mul2(k.gain, tanh_t2<kFast>(ni))));
+            h = cfma2(k.a, h, cx2(mul2(k.gain, content2<kFast, kMode>(nr, lin)), mul2(k.gain, content2<kFast, kMode>(ni, lin))));
             Pair<TIO>::store(&S.hr[t][2 * tid], h.re.x, h.re.y);
             Pair<TIO>::store(&S.hi[t][2 * tid], h.im.x, h.im.y);
           }
@@ -412,8 +421,13 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
             const float2 hci = Pair<TIO>::load(&S.hi[t][2 * tid]);
             const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
             const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
-            lam.re = add2(lam.re, make_float2(hcr.x > 0.0f ? gr.x : 0.0f, hcr.y > 0.0f ? gr.y : 0.0f));
-            lam.im = add2(lam.im, make_float2(hci.x > 0.0f ? gi.x : 0.0f, hci.y > 0.0f ? gi.y : 0.0f));
+            if constexpr (kProj) {  // the states are the output: no relu
+              lam.re = add2(lam.re, gr);
+              lam.im = add2(lam.im, gi);
+            } else {
+              lam.re = add2(lam.re, make_float2(hcr.x > 0.0f ? gr.x : 0.0f, hcr.y > 0.0f ? gr.y : 0.0f));
+              lam.im = add2(lam.im, make_float2(hci.x > 0.0f ? gi.x : 0.0f, hci.y > 0.0f ? gi.y : 0.0f));
+            }
             const Cx2 pv = t > 0 ? cx2(Pair<TIO>::load(&S.hr[t - 1][2 * tid]), Pair<TIO>::load(&S.hi[t - 1][2 * tid]))
                                  : hin;
             const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
@@ -421,7 +435,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
             float2 nr, ni;
             mixer_in(t, xr, xi, nr, ni);
             float2 ve2, vd2;
-            const Cx2 dxc = grad_step2<kFast>(mc, tc, lam, pv, nr, ni, ve2, vd2, fa);
+            const Cx2 dxc = grad_step2<kFast, kMode>(mc, tc, lam, pv, nr, ni, ve2, vd2, fa, lin);
             // h[t] was last read as the previous state at step t+1 and as this step's mask: its
             // slots now hold the write-path dx
             Pair<TIO>::store(&S.hr[t][2 * tid], dxc.re.x, dxc.re.y);
@@ -481,6 +495,9 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
         const float dp1 = tid < nvalid ? S.tot[tid] * kLn16 * fmaf(-tau1, tau1, 1.0f) : 0.0f;
         const float dp0 = tid < nvalid ? S.tot[C + tid] * kHalfPi * fmaf(-tau0, tau0, 1.0f) : 0.0f;
         S.dp[tid] = make_float4(dp0, dp0, dp1, dp1);
+        if constexpr (kProj) {  // the projections' gradient (finished by the caller's matrix products)
+          if (g == 0 && tid < nvalid) p.dp_out[b * T + r.t0 + tid] = make_float2(dp0, dp1);
+        }
         if constexpr (kBlock) {
           // sum_j x_j w_j dn_j = sum x w dxc + dp0 q0 + dp1 q1 (q: the projections before r)
           const float rs = tc.keep.z;
@@ -534,10 +551,12 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
               Io<TIO>::store(row + M + m0 + 1, dim.y);
             }
           }
-          fd[0] = fma2(nr, dp0, fd[0]);
-          fd[1] = fma2(ni, dp0, fd[1]);
-          fd[2] = fma2(nr, dp1, fd[2]);
-          fd[3] = fma2(ni, dp1, fd[3]);
+          if constexpr (!kProj) {  // (projection mode: the directions' gradient is the caller's)
+            fd[0] = fma2(nr, dp0, fd[0]);
+            fd[1] = fma2(ni, dp0, fd[1]);
+            fd[2] = fma2(nr, dp1, fd[2]);
+            fd[3] = fma2(ni, dp1, fd[3]);
+          }
         }
       }
 #pragma unroll

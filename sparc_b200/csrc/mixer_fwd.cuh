@@ -55,6 +55,8 @@ struct FwdParams {
   int mask_words;       // 16 per CTA of 256 modes: four words per 64 modes (store_relu_bits)
   const float2* carry;  // [B, chunks, M] inclusive chunk states (replay input)
   float4* agg;          // [B, chunks, Mp] chunk aggregates (P, Q)
+  const float2* proj_in;  // [B*T] controller projections (p0, p1), bias included (kModeProj)
+  int content_linear;     // kModeProj: the content is u itself instead of tanh(u)
   LaunchState* ls;
   long long B, T;
   int W, M, Mp, chunks;
@@ -79,9 +81,25 @@ template <> struct Pair<__nv_bfloat16> {
   }
 };
 
-// Store the relu'd pair of states of modes (m, m+1) for one token row.
-template <typename TIO, bool kVec>
+// Store the relu'd (kRelu) or raw pair of states of modes (m, m+1) for one token row.
+template <typename TIO, bool kVec, bool kRelu = true>
 __device__ __forceinline__ void store_y_pair(TIO* row, int M, int m, bool a0, bool a1, float2 h0, float2 h1) {
+  if constexpr (!kRelu) {
+    if (kVec && a1) {
+      Pair<TIO>::store(row + m, h0.x, h1.x);
+      Pair<TIO>::store(row + M + m, h0.y, h1.y);
+      return;
+    }
+    if (a0) {
+      Io<TIO>::store(row + m, h0.x);
+      Io<TIO>::store(row + M + m, h0.y);
+    }
+    if (a1) {
+      Io<TIO>::store(row + m + 1, h1.x);
+      Io<TIO>::store(row + M + m + 1, h1.y);
+    }
+    return;
+  }
   if (kVec) {
     if (a1) {
       Pair<TIO>::store(row + m, fmaxf(h0.x, 0.0f), fmaxf(h1.x, 0.0f));
@@ -169,9 +187,10 @@ __host__ __device__ constexpr unsigned act_box_bytes() {
 }
 
 // ------------------------------------------------------------------------------ summary
-template <typename TIO, int C, bool kFast, bool kBlock>
+template <typename TIO, int C, bool kFast, int kMode>
 __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __grid_constant__ FwdParams p) {
   constexpr int NW = kFwdThreads / 32;
+  constexpr bool kBlock = kMode == kModeBlock, kProj = kMode == kModeProj;
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
   const int G = (int)cluster.num_blocks();
@@ -189,7 +208,8 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
 
   ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
   if constexpr (kBlock) load_norm_weight(mc, p.norm_w, m0, M, act0, act1);
-  const float bias0 = p.pp.phase_dir[W], bias1 = p.pp.radial_dir[W];
+  const float bias0 = kProj ? 0.0f : p.pp.phase_dir[W], bias1 = kProj ? 0.0f : p.pp.radial_dir[W];
+  const bool lin = kProj && p.content_linear != 0;
   // projection directions seen by raw x: D w (the norm's weight), scaled by r after the reduction
   const float2 d0r = mul2(mc.d0r, mc.wre), d0i = mul2(mc.d0i, mc.wim);
   const float2 d1r = mul2(mc.d1r, mc.wre), d1i = mul2(mc.d1i, mc.wim);
@@ -236,8 +256,15 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
     const TIO(*xt)[2][kFwdModes] = S.x[buf];
 
     // control projections (and, in a block, the sum of squares for the norm): per-thread
-    // partials over its 4 columns, reduced over the cluster
-    {
+    // partials over its 4 columns, reduced over the cluster; given per token in projection mode
+    float p0 = 0.0f, p1 = 0.0f, rs = 1.0f;  // (threads tid < C: token tid's values)
+    if constexpr (kProj) {
+      if (tid < r.nvalid) {
+        const float2 pj = p.proj_in[r.b * T + r.t0 + tid];
+        p0 = pj.x;
+        p1 = pj.y;
+      }
+    } else {
       const int lane = tid & 31, warp = tid >> 5;
       float v[2 * C];
       float vs[C];
@@ -288,7 +315,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
             q0[rr] = q1[rr] = qs[rr] = 0.0f;
           }
         }
-        float p0 = 0.0f, p1 = 0.0f, ss = 0.0f;
+        float ss = 0.0f;
 #pragma unroll
         for (int rr = 0; rr < 8; ++rr) {
           p0 += q0[rr];
@@ -296,7 +323,11 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
           ss += qs[rr];
         }
         // RMSNorm scale of the token (block): r = (mean x^2 + eps)^(-1/2)
-        const float rs = kBlock ? rsqrtf(fmaf(ss, 1.0f / (float)W, p.norm_eps)) : 1.0f;
+        if constexpr (kBlock) rs = rsqrtf(fmaf(ss, 1.0f / (float)W, p.norm_eps));
+      }
+    }
+    {
+      if (tid < C) {
         const float tau0 = tanh_accurate(fmaf(rs, p0, bias0));
         const float tau1 = tanh_accurate(fmaf(rs, p1, bias1));
         const float E = expf(kLn16 * tau1), delta = kHalfPi * tau0;
@@ -328,7 +359,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
             xi = mul2(xi, mul2(rr, mc.wim));
           }
           const TokenCoef2 k = token_coef2<kFast>(mc, S.ctl[t]);
-          Q = cfma2(k.a, Q, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
+          Q = cfma2(k.a, Q, cx2(mul2(k.gain, content2<kFast, kMode>(xr, lin)), mul2(k.gain, content2<kFast, kMode>(xi, lin))));
           P = cmul2(k.a, P);
         }
       }
@@ -345,8 +376,10 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
 }
 
 // ------------------------------------------------------------------------------ replay
-template <typename TIO, int C, bool kFast, bool kVec, bool kBlock>
+template <typename TIO, int C, bool kFast, bool kVec, int kMode>
 __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __grid_constant__ FwdParams p) {
+  constexpr bool kBlock = kMode == kModeBlock, kProj = kMode == kModeProj;
+  const bool lin = kProj && p.content_linear != 0;
   const int g = blockIdx.x;
   const int tid = threadIdx.x;
   const int M = p.M, W = p.W;
@@ -440,8 +473,8 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
             store_relu_bits(p.mask + (r.b * T + r.t0 + t) * (long long)p.mask_words + (mbase >> 6) * 4 + warp * 4,
                             h, lane);
           } else {
-            h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(xr)), mul2(k.gain, tanh_t2<kFast>(xi))));
-            store_y_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, make_float2(h.re.x, h.im.x),
+            h = cfma2(k.a, h, cx2(mul2(k.gain, content2<kFast, kMode>(xr, lin)), mul2(k.gain, content2<kFast, kMode>(xi, lin))));
+            store_y_pair<TIO, kVec, !kProj>(yrow + (long long)t * W, M, m0, act0, act1, make_float2(h.re.x, h.im.x),
                                     make_float2(h.re.y, h.im.y));
           }
         }

@@ -71,7 +71,7 @@ class _SparcMixerFunction(torch.autograd.Function):
             x.data_ptr(), y.data_ptr(), *[p.data_ptr() for p in params],
             _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
             last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
-            _lib.ptr(nw), float(norm_eps), _lib.ptr(mask),
+            _lib.ptr(nw), float(norm_eps), _lib.ptr(mask), None, 0,
             ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin)
         _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_forward")
@@ -115,7 +115,7 @@ class _SparcMixerFunction(torch.autograd.Function):
             _lib.ptr(gl[0] if gl else None), _lib.ptr(gl[1] if gl else None),
             _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
             carry.data_ptr(), controls.data_ptr(), _lib.ptr(nw), _lib.ptr(mask), _lib.ptr(gnw),
-            *[g[n].data_ptr() for n in _PARAMS],
+            *[g[n].data_ptr() for n in _PARAMS], None, 0,
             ws.data_ptr(), ws.numel(), B, T, W, dt, ctx.max_spin)
         _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_backward")

@@ -1,0 +1,206 @@
+"""The projection variant of SPARC on B200: the sequence layer of the JAX package ``sparc-impl``
+(``SPARCSequenceLayer``, layers.py:156-194 over recurrence.py:20-63) as a torch module.
+
+Unlike the torch ``SPARCMixer`` (whose content is x's two halves and whose output is
+relu([Re h, Im h])), this layer writes a content u = x content_{real,imag} into M modes of any
+count and reads the states out through a complex readout plus a skip:
+
+    p = [x, 1] (phase_controller, retention_controller)        controller projections [B, T, 2]
+    u = x [content_real | content_imag]                          content input [B, T, 2M]
+    h = SPARC states from (u, p)                                 libsparc_b200, projection mode
+    y = Re(h (readout_real + i readout_imag)^T) + skip * x
+
+The recurrence (controls, transition, write gain, scan and their adjoints) runs in the sm_100a
+kernels of libsparc_b200 in projection mode (``projections`` / ``grad_projections`` of the C
+ABI); the content, projection and readout products are the layer's matrix products around it.
+Parameter names and shapes are the JAX layer's; its initializers' distributions are reproduced
+(initialization.py:5-39) with torch's generator, since JAX's PRNG draws cannot be.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+from torch import nn
+
+from . import _lib
+from .mixer import reset_mask
+
+_CORE_PARAMS = ("decay_log", "frequency_log", "write_log_gain", "write_phase_response",
+                "write_retention_response")
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    return t.detach().to(torch.float32).contiguous()
+
+
+class _SparcCoreFunction(torch.autograd.Function):
+    """Autograd op around sparc_mixer_forward / _backward in projection mode.
+
+    Inputs: the content input u [B, T, 2M] (float32 or bfloat16), the controller projections
+    p [B, T, 2] float32 (bias included) and the five modal parameters. Outputs the states
+    h = [Re h, Im h] [B, T, 2M] (u.dtype) and the last state (last_r, last_i) [B, M] float32."""
+
+    @staticmethod
+    def forward(ctx, u, p, decay_log, frequency_log, write_log_gain, write_phase_response,
+                write_retention_response, h0_r, h0_i, max_spin, reset, content_linear):
+        L = _lib.lib()
+        B, T, W = u.shape
+        M = W // 2
+        dt = _lib.dtype_code(u.dtype)
+        dev = u.device
+        params = [_f32(t) for t in (decay_log, frequency_log, write_log_gain, write_phase_response,
+                                    write_retention_response)]
+        p = _f32(p)
+        h0 = None if h0_r is None else (_f32(h0_r), _f32(h0_i))
+        h = torch.empty_like(u)
+        chunks = L.sparc_mixer_carry_chunks(T, dt)
+        carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
+        controls = torch.empty((B, T, L.sparc_mixer_controls_floats()), dtype=torch.float32, device=dev)
+        last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
+        last_i = torch.empty((B, M), dtype=torch.float32, device=dev)
+        nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
+        if nbytes == 0:
+            _lib.check(-2, "sparc_mixer_workspace_bytes")
+        ws = _lib.WORKSPACES.get(dev, nbytes)
+        a = _lib.MixerFwdArgs(
+            u.data_ptr(), h.data_ptr(), params[0].data_ptr(), params[1].data_ptr(), None, None,
+            params[2].data_ptr(), params[3].data_ptr(), params[4].data_ptr(),
+            _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
+            last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
+            None, 0.0, None, p.data_ptr(), int(content_linear),
+            ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin)
+        _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
+                   "sparc_mixer_forward (projection mode)")
+        ctx.save_for_backward(u, *params, carry, controls, *(h0 if h0 else (None, None)))
+        ctx.has_h0 = h0 is not None
+        ctx.max_spin = max_spin
+        ctx.content_linear = int(content_linear)
+        ctx.set_materialize_grads(False)
+        return h, last_r, last_i
+
+    @staticmethod
+    def backward(ctx, dh, dlast_r, dlast_i):
+        L = _lib.lib()
+        u, dlog, flog, wlg, wpr, wrr, carry, controls, h0_r, h0_i = ctx.saved_tensors
+        B, T, W = u.shape
+        M = W // 2
+        dev = u.device
+        dt = _lib.dtype_code(u.dtype)
+        dh = torch.zeros_like(u) if dh is None else dh.to(u.dtype).contiguous()
+        if dlast_r is None and dlast_i is None:
+            gl = None
+        else:
+            gl = (torch.zeros((B, M), device=dev) if dlast_r is None else _f32(dlast_r),
+                  torch.zeros((B, M), device=dev) if dlast_i is None else _f32(dlast_i))
+        du = torch.empty_like(u)
+        dp = torch.empty((B, T, 2), dtype=torch.float32, device=dev)
+        g = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(6)]  # (+ energy slot)
+        gh0 = None
+        if ctx.has_h0:
+            gh0 = (torch.empty((B, M), dtype=torch.float32, device=dev),
+                   torch.empty((B, M), dtype=torch.float32, device=dev))
+        ws = _lib.WORKSPACES.get(dev, L.sparc_mixer_workspace_bytes(B, T, W, dt))
+        a = _lib.MixerBwdArgs(
+            u.data_ptr(), None, dh.data_ptr(), du.data_ptr(),
+            dlog.data_ptr(), flog.data_ptr(), None, None, wlg.data_ptr(), wpr.data_ptr(), wrr.data_ptr(),
+            _lib.ptr(h0_r), _lib.ptr(h0_i),
+            _lib.ptr(gl[0] if gl else None), _lib.ptr(gl[1] if gl else None),
+            _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
+            carry.data_ptr(), controls.data_ptr(), None, None, None,
+            g[0].data_ptr(), g[1].data_ptr(), None, None, g[2].data_ptr(), g[5].data_ptr(),
+            g[3].data_ptr(), g[4].data_ptr(), dp.data_ptr(), ctx.content_linear,
+            ws.data_ptr(), ws.numel(), B, T, W, dt, ctx.max_spin)
+        _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
+                   "sparc_mixer_backward (projection mode)")
+        return (du, dp, g[0], g[1], g[2], g[3], g[4],
+                gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None)
+
+
+def _check_activation(content_activation: str) -> bool:
+    if content_activation not in ("tanh", "linear"):
+        raise ValueError(content_activation)  # recurrence.py:41-48
+    return content_activation == "linear"
+
+
+def sparc_projection_states(x, params, content_activation: str = "tanh", state=None, segment_pos=None,
+                            reset_first: bool = False, max_spin: int = 0):
+    """The recurrent core of the projection variant: ((h_r, h_i) [B, T, M] each in x.dtype,
+    (last_r, last_i) [B, M] float32) for x [B, T, W] and a mapping holding the JAX layer's
+    recurrent parameters (content_real/imag [W, M], the two controllers [W+1], the five modal
+    vectors [M])."""
+    _lib.require_cuda(x, "x")
+    lin = _check_activation(content_activation)
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"supported activations are float32 and bfloat16, got {x.dtype}")
+    W = x.shape[-1]
+    M = params["decay_log"].shape[0]
+    wc = torch.cat((params["content_real"], params["content_imag"]), dim=1)  # [W, 2M]
+    u = torch.matmul(x, wc.to(x.dtype)).contiguous()
+    ctl = torch.stack((params["phase_controller"], params["retention_controller"]), dim=1)  # [W+1, 2]
+    p = torch.addmm(ctl[W], x.reshape(-1, W).float(), ctl[:W]).reshape(*x.shape[:2], 2)
+    h0_r, h0_i = (None, None) if state is None else state
+    reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
+    h, lr, li = _SparcCoreFunction.apply(
+        u, p, *[params[n] for n in _CORE_PARAMS], h0_r, h0_i, int(max_spin), reset, lin)
+    return (h[..., :M], h[..., M:]), (lr, li)
+
+
+def sparc_sequence_layer(x, params, content_activation: str = "tanh", state=None, segment_pos=None,
+                         reset_first: bool = False, max_spin: int = 0):
+    """Functional SPARCSequenceLayer: (y [B, T, W], (last_r, last_i))."""
+    (hr, hi), last = sparc_projection_states(x, params, content_activation, state, segment_pos,
+                                             reset_first, max_spin)
+    ro = torch.cat((params["readout_real"], -params["readout_imag"]), dim=1).to(x.dtype)  # [W, 2M]
+    h = torch.cat((hr, hi), dim=-1)
+    y = torch.addcmul(torch.matmul(h, ro.t()), params["skip"].to(x.dtype), x)
+    return y, last
+
+
+class SPARCSequenceLayer(nn.Module):
+    """Torch counterpart of ``SPARCSequenceLayer`` (sparc-impl/sparc/layers.py:156-194).
+
+    ``forward(x)`` returns y [B, T, model_width] like the JAX layer's ``__call__``; the optional
+    ``state`` / ``segment_pos`` / ``reset_first`` / ``return_cache`` arguments mirror
+    ``SPARCMixer.forward`` (initial state with gradient, packed-sequence resets, last state)."""
+
+    def __init__(self, model_width: int, modes: int, r_min: float = 0.9, r_max: float = 0.999,
+                 max_phase: float = 6.28, content_activation: str = "tanh"):
+        super().__init__()
+        _check_activation(content_activation)
+        self.model_width = W = model_width
+        self.modes = M = modes
+        self.content_activation = content_activation
+        self.max_spin = 0
+        # draw order of _parameters (layers.py:86-115), then the readout and skip (180-192)
+        u = torch.rand(M)
+        frequency_log = torch.log(max_phase * u)
+        u = torch.rand(M)
+        decay_log = torch.log(-0.5 * torch.log(u * (r_max ** 2 - r_min ** 2) + r_min ** 2))
+        self.frequency_log = nn.Parameter(frequency_log)
+        self.decay_log = nn.Parameter(decay_log)
+        self.content_real = nn.Parameter(torch.randn(W, M) / math.sqrt(2.0 * W))
+        self.content_imag = nn.Parameter(torch.randn(W, M) / math.sqrt(2.0 * W))
+        self.phase_controller = nn.Parameter(torch.zeros(W + 1))
+        self.retention_controller = nn.Parameter(torch.zeros(W + 1))
+        # write_log_gain_initializer: log sqrt(1 - |exp(-nu + i theta)|^2)
+        self.write_log_gain = nn.Parameter(torch.log(torch.sqrt(1.0 - torch.exp(-2.0 * torch.exp(decay_log)))))
+        self.write_phase_response = nn.Parameter(torch.zeros(M))
+        self.write_retention_response = nn.Parameter(torch.zeros(M))
+        self.readout_real = nn.Parameter(torch.randn(W, M) / math.sqrt(M))
+        self.readout_imag = nn.Parameter(torch.randn(W, M) / math.sqrt(M))
+        self.skip = nn.Parameter(torch.randn(W))
+
+    def parameters_dict(self):
+        return {n: getattr(self, n) for n, _ in self.named_parameters()}
+
+    def forward(self, x: torch.Tensor, state=None, segment_pos=None, reset_first: bool = False,
+                return_cache: bool = False):
+        if x.shape[-1] != self.model_width:
+            raise ValueError((x.shape[-1], self.model_width))  # layers.py:166-167
+        if x.dim() != 3:
+            raise ValueError("SPARCSequenceLayer expects x of shape [batch, length, model_width]")
+        y, last = sparc_sequence_layer(x.contiguous(), self.parameters_dict(), self.content_activation,
+                                       state, segment_pos, reset_first, self.max_spin)
+        return (y, last) if return_cache else y

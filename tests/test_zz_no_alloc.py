@@ -48,7 +48,7 @@ def _call(entry, x, params, workspace=None):
     ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel())
     a = _lib.MixerFwdArgs(x.data_ptr(), y.data_ptr(), *[p.data_ptr() for p in params], None, None,
                           last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), None, None, 0.0, None,
-                          ws_ptr, ws_bytes,
+                          None, 0, ws_ptr, ws_bytes,
                           B, T, W, _lib.dtype_code(x.dtype), 0)
     rc = getattr(L, entry)(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
     return rc, y, last_r, last_i, carry
