@@ -281,6 +281,62 @@ int sparc_timing_read(double* ms, long long* launches, int n);
 int sparc_read_status(const void* workspace, unsigned* status, void* stream);
 int sparc_clear_status(void* workspace, void* stream);
 
+/* RTRL online traces of the SPARC cell (sparc-impl/sparc/training/rtrl.py:154-240, replaces the
+ * JAX _trace_step / stored_rtrl_step). Traces and states are complex, stored as interleaved
+ * float32 pairs (the layout of complex64): trace index 0-4 the modal parameters decay_log,
+ * frequency_log, write_log_gain, write_phase_response, write_retention_response [batch, M];
+ * 5, 6 content_real, content_imag [batch, input_size, M]; 7, 8 phase_controller,
+ * retention_controller [batch, input_size + 1, M]. `content` is the caller's product
+ * [x content_real, x content_imag] ([batch, 2M] float32) and `projections` [x, 1] phase_controller,
+ * [x, 1] retention_controller ([batch, 2] float32). Where reset[b] is nonzero the carried state
+ * and traces of row b are zeroed before the step (_reset_carry, rtrl.py:142-151). new_traces may
+ * alias traces (each element is read and written by the same thread). `saved`
+ * ([batch, M, sparc_rtrl_saved_floats()] float32) receives what sparc_rtrl_grad needs. */
+typedef struct SparcRtrlStepArgs {
+  const float* x;                      /* [batch, input_size] */
+  const float* content;                /* [batch, 2M] */
+  const float* projections;            /* [batch, 2] */
+  const unsigned char* reset;          /* [batch] or NULL */
+  const float* state;                  /* [batch, M] complex */
+  float* new_state;                    /* [batch, M] complex out */
+  const float* decay_log;              /* [M] */
+  const float* frequency_log;          /* [M] */
+  const float* write_log_gain;         /* [M] */
+  const float* write_phase_response;   /* [M] */
+  const float* write_retention_response; /* [M] */
+  const float* traces[9];
+  float* new_traces[9];
+  float* saved;
+  long long batch;                     /* at most 65535 */
+  int input_size;
+  int modes;
+  int content_linear;                  /* content_activation "linear": content u, else tanh(u) */
+} SparcRtrlStepArgs;
+
+/* Gradients of a loss on the step's new state (stored_rtrl_step's backward, rtrl.py:220-240):
+ * grad_state holds (dL/dRe h', dL/dIm h') per mode; every parameter's gradient is
+ * sum_b (dL/dRe h' Re(trace) + dL/dIm h' Im(trace)) over the step's NEW traces (summed over the
+ * modes too for the controllers; grad_params in the trace order, shapes [M], [input_size, M],
+ * [input_size + 1]); grad_content [batch, 2M] and grad_projections [batch, 2] are the one-step
+ * gradients of the step's content and projection inputs (the caller's products finish the
+ * input's). Sums run in a fixed order. */
+typedef struct SparcRtrlGradArgs {
+  const float* grad_state;             /* [batch, M] complex */
+  const float* traces[9];              /* the step's new traces */
+  const float* saved;                  /* the step's saved output */
+  float* grad_params[9];
+  float* grad_content;                 /* [batch, 2M] out */
+  float* grad_projections;             /* [batch, 2] out */
+  long long batch;
+  int input_size;
+  int modes;
+} SparcRtrlGradArgs;
+
+int sparc_rtrl_saved_floats(void);
+int sparc_rtrl_step(const SparcRtrlStepArgs* args, void* stream);
+int sparc_rtrl_grad(const SparcRtrlGradArgs* args, void* stream);
+const char* sparc_rtrl_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,7 @@ All compute runs in the sm_100a kernels of ``libsparc_b200.so`` (C ABI in
 from .mixer import SPARCMixer, sparc_block, sparc_decode_step, sparc_mixer
 from .stack import SPARCBlock, SPARCStack
 from .projection import SPARCSequenceLayer, sparc_projection_states, sparc_sequence_layer
+from .rtrl import SPARCRTRLCell, initialize_carry, initialize_traces, rtrl_step
 from .real import real_chunk_scan, real_scan, real_scan_with_last
 from . import _lib
 
@@ -30,4 +31,5 @@ def check_status(clear: bool = True) -> None:
 
 __all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack", "sparc_decode_step",
            "SPARCSequenceLayer", "sparc_sequence_layer", "sparc_projection_states",
+           "SPARCRTRLCell", "rtrl_step", "initialize_carry", "initialize_traces",
            "real_scan", "real_chunk_scan", "real_scan_with_last", "check_status", "library_path"]

@@ -88,6 +88,23 @@ class RealBwdArgs(ctypes.Structure):
     ]
 
 
+class RtrlStepArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("content", _vp), ("projections", _vp), ("reset", _vp), ("state", _vp), ("new_state", _vp),
+        ("decay_log", _vp), ("frequency_log", _vp), ("write_log_gain", _vp), ("write_phase_response", _vp),
+        ("write_retention_response", _vp), ("traces", _vp * 9), ("new_traces", _vp * 9), ("saved", _vp),
+        ("batch", _ll), ("input_size", ctypes.c_int), ("modes", ctypes.c_int), ("content_linear", ctypes.c_int),
+    ]
+
+
+class RtrlGradArgs(ctypes.Structure):
+    _fields_ = [
+        ("grad_state", _vp), ("traces", _vp * 9), ("saved", _vp), ("grad_params", _vp * 9),
+        ("grad_content", _vp), ("grad_projections", _vp),
+        ("batch", _ll), ("input_size", ctypes.c_int), ("modes", ctypes.c_int),
+    ]
+
+
 # every symbol declared in include/sparc_b200.h, with its ctypes signature
 SIGNATURES = {
     "sparc_last_error": (ctypes.c_char_p, []),
@@ -107,6 +124,10 @@ SIGNATURES = {
     "sparc_real_scan_backward": (ctypes.c_int, [ctypes.POINTER(RealBwdArgs), _vp]),
     "sparc_read_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint), _vp]),
     "sparc_clear_status": (ctypes.c_int, [_vp, _vp]),
+    "sparc_rtrl_saved_floats": (ctypes.c_int, []),
+    "sparc_rtrl_step": (ctypes.c_int, [ctypes.POINTER(RtrlStepArgs), _vp]),
+    "sparc_rtrl_grad": (ctypes.c_int, [ctypes.POINTER(RtrlGradArgs), _vp]),
+    "sparc_rtrl_last_error": (ctypes.c_char_p, []),
     "sparc_timing_enable": (ctypes.c_int, [ctypes.c_int]),
     "sparc_timing_kernel_name": (ctypes.c_char_p, [ctypes.c_int]),
     "sparc_timing_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong),

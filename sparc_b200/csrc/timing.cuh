@@ -16,6 +16,8 @@ enum KernelId {
   kTimeRealFwd,
   kTimeRealBwd,
   kTimeDecode,
+  kTimeRtrlStep,
+  kTimeRtrlGrad,
   kTimeKernels
 };
 

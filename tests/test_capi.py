@@ -41,9 +41,10 @@ def test_struct_layouts_match_header():
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     for cname, py in (("SparcMixerFwdArgs", _lib.MixerFwdArgs), ("SparcMixerBwdArgs", _lib.MixerBwdArgs),
                       ("SparcDecodeArgs", _lib.DecodeArgs), ("SparcRealFwdArgs", _lib.RealFwdArgs),
-                      ("SparcRealBwdArgs", _lib.RealBwdArgs)):
+                      ("SparcRealBwdArgs", _lib.RealBwdArgs), ("SparcRtrlStepArgs", _lib.RtrlStepArgs),
+                      ("SparcRtrlGradArgs", _lib.RtrlGradArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\}" % cname, src, flags=re.S).group(1)
-        fields = re.findall(r"(\w+)\s*;", body)
+        fields = re.findall(r"(\w+)\s*(?:\[\d+\])?\s*;", body)
         assert fields == [f[0] for f in py._fields_], cname
 
 
@@ -58,6 +59,7 @@ def test_host_only_queries(lib):
     assert lib.sparc_mixer_controls_floats() == 16  # the per-token record the kernels write
     assert lib.sparc_mixer_mask_words(2048) == 64 and lib.sparc_mixer_mask_words(600) == 32
     assert lib.sparc_mixer_mask_words(7) == 0
+    assert lib.sparc_rtrl_saved_floats() == 8
 
 
 def test_no_cpu_fallback():
