@@ -5,7 +5,7 @@ SPARCMixer(512) layer, forward + backward of sum(y * g), B=8 x T=2048 tokens per
 parameters from the default init under torch.manual_seed(0), synthetic x, g ~ N(0, 1).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload layer|stack|real|decode]
+                    [--workload layer|layer5|stack|real|decode|projection|rtrl]
 
 Multi-GPU: one process per GPU (torchrun), batch-sharded data parallelism (each rank runs the
 per-GPU batch: weak scaling), parameter gradients all-reduced over NCCL every step; timing is
@@ -49,6 +49,12 @@ WORKLOADS = {
                  dtype="bfloat16", config_index=2),
     "decode": dict(workload="sparc_decode_step", batch=256, width=2048, steps=1024,
                    dtype="bfloat16", config_index=3),
+    # the projection variant (JAX sequence layer) at config 2's token count and state size
+    "projection": dict(workload="sparc_sequence_layer_fwd_bwd", batch=8, seq_len=2048, width=512, modes=256,
+                       dtype="float32", config_index=0),
+    # one RTRL cell step (trace update + trace gradients) at a size whose traces exceed L2
+    "rtrl": dict(workload="sparc_rtrl_cell_step_fwd_bwd", batch=64, width=512, modes=512,
+                 dtype="float32", config_index=0),
 }
 METRIC = "SPARC layer fwd+bwd tokens/sec and % HBM roofline at 1/2/4/8 B200"
 
@@ -354,34 +360,53 @@ def run_layer(args, wl, world, rank, local):
                 "peak_source": peak_kind, "kernels": kern,
                 "step_frac": round(5 * W * s * B * T / (ms / 1e3) / 1e9 / peak, 4)}
 
-    # end to end through the public API with pinned host buffers
+    # end to end through the public API: every step copies its x and g from pinned host memory
+    # (on a copy stream, double-buffered, so that step i+1's copy overlaps step i's compute) and
+    # reads its loss back to pinned host memory
     xh = x.cpu().pin_memory()
     gh = g.cpu().pin_memory()
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
-    for _ in range(2):
-        xd = xh.to(device, non_blocking=True)
-        gd = gh.to(device, non_blocking=True)
-        yy, _ = model(xd)
-        loss = (yy.float() * gd.float()).sum()
-        loss.backward()
-        loss_h.copy_(loss.detach(), non_blocking=True)
-        model.zero_grad(set_to_none=True)
+    main = torch.cuda.current_stream(device)
+    copy_stream = torch.cuda.Stream(device)
+    bufs = [(torch.empty_like(x), torch.empty_like(g)) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for e in free:
+        e.record(main)
+
+    def h2d(i):
+        k = i % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[k])
+            bufs[k][0].copy_(xh, non_blocking=True)
+            bufs[k][1].copy_(gh, non_blocking=True)
+            copied[k].record(copy_stream)
+
+    def e2e_steps(n):
+        h2d(0)
+        for i in range(n):
+            if i + 1 < n:
+                h2d(i + 1)
+            k = i % 2
+            main.wait_event(copied[k])
+            xd, gd = bufs[k]
+            yy, _ = model(xd)
+            loss = (yy.float() * gd.float()).sum()
+            loss.backward()
+            if reducer is not None:
+                reducer()
+            free[k].record(main)
+            loss_h.copy_(loss.detach(), non_blocking=True)
+            model.zero_grad(set_to_none=True)
+
+    e2e_steps(2)
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(args.steps):
-        xd = xh.to(device, non_blocking=True)
-        gd = gh.to(device, non_blocking=True)
-        yy, _ = model(xd)
-        loss = (yy.float() * gd.float()).sum()
-        loss.backward()
-        if reducer is not None:
-            reducer()
-        loss_h.copy_(loss.detach(), non_blocking=True)
-        model.zero_grad(set_to_none=True)
-    ev1.record()
+    ev0.record(main)
+    e2e_steps(args.steps)
+    ev1.record(main)
     torch.cuda.synchronize(device)
     e2e_ms = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=device, dtype=torch.float64)
     if world > 1:
@@ -389,7 +414,8 @@ def run_layer(args, wl, world, rank, local):
     e2e_ms = float(e2e_ms.item())
     e2e = {"value": round(tokens_step / (e2e_ms / 1e3), 1), "unit": "tokens/s",
            "h2d_bytes_per_step": int(2 * B * T * W * s), "d2h_bytes_per_step": 4,
-           "ms_per_step": round(e2e_ms, 4), "path": "SPARCMixer.forward/backward from pinned host x, g"}
+           "ms_per_step": round(e2e_ms, 4),
+           "path": "SPARCMixer.forward/backward from pinned host x, g (copies double-buffered on a copy stream)"}
     sparc_b200.check_status()
 
     cpu = None
@@ -530,6 +556,129 @@ def run_decode(args, wl, world, rank, local):
                 clocks=clocks.summary(), launches=S * args.steps, per_step_ms=per, tokens_step=B * S * world)
 
 
+def run_projection(args, wl, world, rank, local):
+    """SPARCSequenceLayer forward + backward (content / projection / readout products and the
+    recurrence in the mixer kernels' projection mode), captured in a CUDA graph."""
+    import torch
+
+    import sparc_b200
+    from sparc_b200 import _lib
+    from sparc_b200.ddp import GradAllReduce
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    B, T, W, M = wl["batch"], wl["seq_len"], wl["width"], wl["modes"]
+    torch.manual_seed(0)
+    layer = sparc_b200.SPARCSequenceLayer(W, M).to(device)
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    x = torch.randn(B, T, W, generator=gen, device=device)
+    g = torch.randn(B, T, W, generator=gen, device=device)
+    reducer = GradAllReduce(layer.parameters()) if world > 1 else None
+    flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            layer.zero_grad(set_to_none=True)
+            layer(x).backward(g)
+            if reducer is not None:
+                reducer()
+    torch.cuda.current_stream(device).wait_stream(stream)
+    torch.cuda.synchronize(device)
+    layer.zero_grad(set_to_none=True)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        layer(x).backward(g)
+        if reducer is not None:
+            reducer()
+    for _ in range(args.warmup):
+        flush_buf.fill_(1)
+        graph.replay()
+    with ClockSampler(local) as clocks:
+        total_ms, per = _time_steps(graph.replay, args.steps, lambda: flush_buf.fill_(1), world, device)
+    ms = total_ms / args.steps
+    # per-kernel times of the recurrence (library timing, outside the graph)
+    L = _lib.lib()
+    L.sparc_timing_enable(1)
+    _lib.kernel_times(reset_only=True)
+    for _ in range(args.steps):
+        flush_buf.fill_(1)
+        layer(x).backward(g)
+        layer.zero_grad(set_to_none=True)
+    torch.cuda.synchronize(device)
+    times = _lib.kernel_times()
+    L.sparc_timing_enable(0)
+    kern = {k: round(t / n, 4) for k, (t, n) in times.items()}
+    peak, kind = measured_peaks()
+    # the recurrence's algorithmic bytes: content u (2M floats per token) read by the forward
+    # summary and replay, states h written; u, dh read and du written by the backward
+    byts = 5 * 2 * M * 4 * B * T
+    rec_ms = sum(kern.values())
+    roofline = {"bound": "hbm", "achieved": round(byts / (rec_ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(byts / (rec_ms / 1e3) / 1e9 / peak, 4), "traffic": None,
+                "kernel": "the seven recurrence kernels (projection mode), 5 x 2M x 4 bytes per token",
+                "peak_source": kind, "kernels_ms": kern, "recurrence_ms": round(rec_ms, 4)}
+    del graph
+    return dict(value=B * T * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=None, cpu=None,
+                clocks=clocks.summary(), launches=MIXER_LAUNCHES * args.steps, per_step_ms=per,
+                tokens_step=B * T * world)
+
+
+def run_rtrl(args, wl, world, rank, local):
+    """One SPARCRTRLCell step with a loss on its output (trace update, trace gradients and the
+    content / projection products), batch rows as tokens; traces live in HBM (> L2)."""
+    import torch
+
+    import sparc_b200
+    from sparc_b200 import _lib
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    B, W, M = wl["batch"], wl["width"], wl["modes"]
+    torch.manual_seed(0)
+    cell = sparc_b200.SPARCRTRLCell(W, M).to(device)
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    xs = torch.randn(8, B, W, generator=gen, device=device)
+    w = torch.randn(B, 2 * M, generator=gen, device=device)
+    carry = cell.initial_carry(B)
+    state = {"carry": carry, "i": 0}
+
+    def step():
+        cell.zero_grad(set_to_none=True)
+        nxt, out = cell(state["carry"], xs[state["i"] % 8])
+        (out * w).sum().backward()
+        state["carry"] = nxt
+        state["i"] += 1
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    with ClockSampler(local) as clocks:
+        total_ms, per = _time_steps(step, args.steps, lambda: None, world, device)
+    ms = total_ms / args.steps
+    L = _lib.lib()
+    L.sparc_timing_enable(1)
+    _lib.kernel_times(reset_only=True)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize(device)
+    times = _lib.kernel_times()
+    L.sparc_timing_enable(0)
+    kern = {k: round(t / n, 4) for k, (t, n) in times.items()}
+    peak, kind = measured_peaks()
+    # step kernel: four [B, W(+1), M] complex traces read and written (64 bytes per (b, j, m)),
+    # five modal traces; gradient kernel: the nine new traces read once (32 bytes per (b, j, m))
+    step_bytes = 64 * B * W * M + 32 * B * M + 80 * B * M
+    grad_bytes = 32 * B * W * M + 40 * B * M
+    st_ms = kern.get("rtrl_step_kernel")
+    gr_ms = kern.get("rtrl_grad_kernel")
+    roofline = {"bound": "hbm", "achieved": round(step_bytes / (st_ms / 1e3) / 1e9, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(step_bytes / (st_ms / 1e3) / 1e9 / peak, 4), "traffic": None,
+                "kernel": "rtrl_step_kernel", "peak_source": kind, "kernels_ms": kern,
+                "grad_kernel_GBps": round(grad_bytes / (gr_ms / 1e3) / 1e9, 1) if gr_ms else None}
+    return dict(value=B * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=None, cpu=None,
+                clocks=clocks.summary(), launches=2 * args.steps, per_step_ms=per, tokens_step=B * world)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, wl):
     """The reference algorithm on the host cores: the float64 oracle restatement, one batch row
@@ -591,7 +740,7 @@ def main():
 
     world, rank, local = _dist()
     runner = {"layer": run_layer, "layer5": run_layer, "stack": run_stack, "real": run_real,
-              "decode": run_decode}[args.workload]
+              "decode": run_decode, "projection": run_projection, "rtrl": run_rtrl}[args.workload]
     r = runner(args, wl, world, rank, local)
     if rank == 0:
         unit = "tokens/s"
@@ -599,13 +748,13 @@ def main():
                "parallelism": f"dp{world}" if world > 1 else "single"}
         if "chunk" in r:
             wl["chunk"] = r["chunk"]
-        for k in ("batch", "seq_len", "width", "channels", "layers", "steps", "chunk"):
+        for k in ("batch", "seq_len", "width", "modes", "channels", "layers", "steps", "chunk"):
             if k in wl:
-                cfg["global_batch" if k == "batch" else k] = wl[k] * (world if k == "batch" and args.workload in ("layer", "layer5", "real", "decode") else 1)
+                cfg["global_batch" if k == "batch" else k] = wl[k] * (world if k == "batch" and args.workload in ("layer", "layer5", "real", "decode", "projection", "rtrl") else 1)
         cfg["l2"] = ("flushed before every step (512 MiB write, outside the CUDA events)"
-                     if args.workload == "layer" else "inputs larger than L2")
-        cfg["timing"] = ("per-step CUDA events, CUDA-graph replay" if args.workload in ("layer", "layer5", "decode")
-                         else "per-step CUDA events")
+                     if args.workload in ("layer", "projection") else "inputs larger than L2")
+        cfg["timing"] = ("per-step CUDA events, CUDA-graph replay"
+                         if args.workload in ("layer", "layer5", "decode", "projection") else "per-step CUDA events")
         line = {"metric": METRIC, "value": round(r["value"], 1), "unit": unit, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

@@ -32,6 +32,8 @@ namespace sparc {
 constexpr int kRtrlThreads = 128;  // one mode per thread
 constexpr int kRtrlUnroll = 4;     // trace rows in flight per thread
 constexpr int kRtrlSavedFloats = 8;
+constexpr int kRtrlGradThreads = 256;
+static_assert(kRtrlUnroll == 4, "the gradient kernel combines four partial sums");
 
 struct RtrlStepParams {
   const float* x;
@@ -196,17 +198,17 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   float t = 0.0f;
 #pragma unroll
-  for (int w = 0; w < kRtrlThreads / 32; ++w) t += red[w];
+  for (int w = 0; w < kRtrlGradThreads / 32; ++w) t += red[w];
   return t;
 }
 
-// grid (W + 1 + B + mblocks): CTA j < W + 1 reduces trace row j over the batch (content
-// gradients of row j for every mode; for the controllers also over the modes); the next B CTAs
-// one batch row each (the content input's gradient and the projections'); the last mblocks
-// CTAs 128 modes each (modal gradients). Every sum runs in a fixed order.
-__global__ void __launch_bounds__(kRtrlThreads) rtrl_grad_kernel(const __grid_constant__ RtrlGradParams p) {
+// grid (W + 1 + B + mblocks), 256 threads: CTA j < W + 1 reduces trace row j over the batch
+// (content gradients of row j for every mode; for the controllers also over the modes); the
+// next B CTAs one batch row each (the content input's gradient and the projections'); the last
+// mblocks CTAs 256 modes each (modal gradients). Every sum runs in a fixed order.
+__global__ void __launch_bounds__(kRtrlGradThreads) rtrl_grad_kernel(const __grid_constant__ RtrlGradParams p) {
   pdl_wait();
-  __shared__ float red[kRtrlThreads / 32];
+  __shared__ float red[kRtrlGradThreads / 32];
   const int W = p.W, M = p.M;
   const long long B = p.B;
   const int tid = threadIdx.x;
@@ -214,24 +216,47 @@ __global__ void __launch_bounds__(kRtrlThreads) rtrl_grad_kernel(const __grid_co
   if (role <= W) {
     const int j = (int)role;
     float sph = 0.0f, sret = 0.0f;
-    for (int m = tid; m < M; m += kRtrlThreads) {
-      float cr = 0.0f, ci = 0.0f;
-      for (long long b = 0; b < B; ++b) {
-        const float2 g = p.g[b * M + m];
-        if (j < W) {
-          const long long ci_ = (b * W + j) * (long long)M + m;
-          const float2 t0 = p.tr[5][ci_], t1 = p.tr[6][ci_];
-          cr = fmaf(g.x, t0.x, fmaf(g.y, t0.y, cr));
-          ci = fmaf(g.x, t1.x, fmaf(g.y, t1.y, ci));
+    for (int m = tid; m < M; m += kRtrlGradThreads) {
+      // kRtrlUnroll batch rows at a time, their loads issued together; one partial sum per
+      // unrolled slot, combined in a fixed order
+      float cr[kRtrlUnroll] = {}, ci[kRtrlUnroll] = {}, sp[kRtrlUnroll] = {}, sr[kRtrlUnroll] = {};
+      for (long long b0 = 0; b0 < B; b0 += kRtrlUnroll) {
+        float2 g[kRtrlUnroll], t[kRtrlUnroll][4];
+#pragma unroll
+        for (int u = 0; u < kRtrlUnroll; ++u) {
+          const long long b = b0 + u;
+          if (b < B) {
+            g[u] = p.g[b * M + m];
+            if (j < W) {
+              const long long ci_ = (b * W + j) * (long long)M + m;
+              t[u][0] = p.tr[5][ci_];
+              t[u][1] = p.tr[6][ci_];
+            }
+            const long long ki = (b * (W + 1) + j) * (long long)M + m;
+            t[u][2] = p.tr[7][ki];
+            t[u][3] = p.tr[8][ki];
+          }
         }
-        const long long ki = (b * (W + 1) + j) * (long long)M + m;
-        const float2 t2 = p.tr[7][ki], t3 = p.tr[8][ki];
-        sph = fmaf(g.x, t2.x, fmaf(g.y, t2.y, sph));
-        sret = fmaf(g.x, t3.x, fmaf(g.y, t3.y, sret));
+#pragma unroll
+        for (int u = 0; u < kRtrlUnroll; ++u) {
+          if (b0 + u < B) {
+            if (j < W) {
+              cr[u] = fmaf(g[u].x, t[u][0].x, fmaf(g[u].y, t[u][0].y, cr[u]));
+              ci[u] = fmaf(g[u].x, t[u][1].x, fmaf(g[u].y, t[u][1].y, ci[u]));
+            }
+            sp[u] = fmaf(g[u].x, t[u][2].x, fmaf(g[u].y, t[u][2].y, sp[u]));
+            sr[u] = fmaf(g[u].x, t[u][3].x, fmaf(g[u].y, t[u][3].y, sr[u]));
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kRtrlUnroll; ++u) {
+        sph += sp[u];
+        sret += sr[u];
       }
       if (j < W) {
-        p.grad[5][(long long)j * M + m] = cr;
-        p.grad[6][(long long)j * M + m] = ci;
+        p.grad[5][(long long)j * M + m] = (cr[0] + cr[1]) + (cr[2] + cr[3]);
+        p.grad[6][(long long)j * M + m] = (ci[0] + ci[1]) + (ci[2] + ci[3]);
       }
     }
     sph = block_sum(sph, red);
@@ -245,7 +270,7 @@ __global__ void __launch_bounds__(kRtrlThreads) rtrl_grad_kernel(const __grid_co
   if (role <= W + B) {
     const long long b = role - W - 1;
     float s0 = 0.0f, s1 = 0.0f;
-    for (int m = tid; m < M; m += kRtrlThreads) {
+    for (int m = tid; m < M; m += kRtrlGradThreads) {
       const float2 g = p.g[b * M + m];
       const float4 v0 = p.saved[(b * M + m) * 2], v1 = p.saved[(b * M + m) * 2 + 1];
       float* gu = reinterpret_cast<float*>(p.grad_u) + b * 2 * M;
@@ -259,7 +284,7 @@ __global__ void __launch_bounds__(kRtrlThreads) rtrl_grad_kernel(const __grid_co
     if (tid == 0) p.grad_proj[b] = make_float2(s0, s1);
     return;
   }
-  const int m = (int)(role - W - 1 - B) * kRtrlThreads + tid;
+  const int m = (int)(role - W - 1 - B) * kRtrlGradThreads + tid;
   if (m >= M) return;
   float acc[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
   for (long long b = 0; b < B; ++b) {
@@ -282,10 +307,10 @@ static int rtrl_fail(int code, const char* msg) {
 }
 
 template <typename P>
-static cudaError_t launch_pdl(const void* kernel, dim3 grid, cudaStream_t s, const P& params) {
+static cudaError_t launch_pdl(const void* kernel, dim3 grid, int threads, cudaStream_t s, const P& params) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kRtrlThreads, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -359,7 +384,7 @@ int sparc_rtrl_step(const SparcRtrlStepArgs* a, void* stream) {
   const int nz = (rows + p.rows_per_z - 1) / p.rows_per_z;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   TimedLaunch tl(kTimeRtrlStep, s);
-  const cudaError_t e = launch_pdl((const void*)rtrl_step_kernel, dim3(mblocks, (unsigned)a->batch, nz), s, p);
+  const cudaError_t e = launch_pdl((const void*)rtrl_step_kernel, dim3(mblocks, (unsigned)a->batch, nz), kRtrlThreads, s, p);
   return e == cudaSuccess ? SPARC_OK : rtrl_fail(SPARC_ERR_LAUNCH, cudaGetErrorString(e));
 }
 
@@ -382,12 +407,12 @@ int sparc_rtrl_grad(const SparcRtrlGradArgs* a, void* stream) {
   p.B = a->batch;
   p.W = a->input_size;
   p.M = a->modes;
-  p.mblocks = (a->modes + kRtrlThreads - 1) / kRtrlThreads;
+  p.mblocks = (a->modes + kRtrlGradThreads - 1) / kRtrlGradThreads;
   const long long grid = (long long)a->input_size + 1 + a->batch + p.mblocks;
   if (grid >= (1LL << 31)) return rtrl_fail(SPARC_ERR_SHAPE, "too many trace rows");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   TimedLaunch tl(kTimeRtrlGrad, s);
-  const cudaError_t e = launch_pdl((const void*)rtrl_grad_kernel, dim3((unsigned)grid), s, p);
+  const cudaError_t e = launch_pdl((const void*)rtrl_grad_kernel, dim3((unsigned)grid), kRtrlGradThreads, s, p);
   return e == cudaSuccess ? SPARC_OK : rtrl_fail(SPARC_ERR_LAUNCH, cudaGetErrorString(e));
 }
 
