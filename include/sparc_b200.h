@@ -337,6 +337,33 @@ int sparc_rtrl_step(const SparcRtrlStepArgs* args, void* stream);
 int sparc_rtrl_grad(const SparcRtrlGradArgs* args, void* stream);
 const char* sparc_rtrl_last_error(void);
 
+/* Tensor-core product of the projection variant (content, readout and their adjoints; the JAX
+ * layer's x @ content_real/imag and states @ readout^T, recurrence.py:39-40, layers.py:193-194):
+ *   out[m, n] = sum_k a[m, k] b[n, k] (+ skip[n] x[m, n]) (+ dp[m, 0] c0[n] + dp[m, 1] c1[n])
+ * a [rows, k] and b [n, k] row-major bfloat16 (k a multiple of 8, 16-byte aligned bases),
+ * float32 accumulation, out [rows, n] bfloat16 (or float32 with out_f32). x (bfloat16,
+ * [rows, n]) with skip ([n] float32), and dp ([rows, 2] float32) with c0, c1 ([n] float32),
+ * are optional fused terms. `status` (device word) is or'ed with 4 if a bounded wait ran out. */
+typedef struct SparcProjGemmArgs {
+  const void* a;
+  const void* b;
+  void* out;
+  const void* x;
+  const float* skip;
+  const float* dp;
+  const float* c0;
+  const float* c1;
+  unsigned* status;
+  long long rows;
+  int n;
+  int k;
+  int out_f32;
+  unsigned max_spin;                   /* bound of the mbarrier waits (0 = default) */
+} SparcProjGemmArgs;
+
+int sparc_proj_gemm(const SparcProjGemmArgs* args, void* stream);
+const char* sparc_proj_gemm_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif

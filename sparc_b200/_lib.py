@@ -105,6 +105,14 @@ class RtrlGradArgs(ctypes.Structure):
     ]
 
 
+class ProjGemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("a", _vp), ("b", _vp), ("out", _vp), ("x", _vp), ("skip", _vp), ("dp", _vp), ("c0", _vp), ("c1", _vp),
+        ("status", _vp), ("rows", _ll), ("n", ctypes.c_int), ("k", ctypes.c_int), ("out_f32", ctypes.c_int),
+        ("max_spin", ctypes.c_uint),
+    ]
+
+
 # every symbol declared in include/sparc_b200.h, with its ctypes signature
 SIGNATURES = {
     "sparc_last_error": (ctypes.c_char_p, []),
@@ -128,6 +136,8 @@ SIGNATURES = {
     "sparc_rtrl_step": (ctypes.c_int, [ctypes.POINTER(RtrlStepArgs), _vp]),
     "sparc_rtrl_grad": (ctypes.c_int, [ctypes.POINTER(RtrlGradArgs), _vp]),
     "sparc_rtrl_last_error": (ctypes.c_char_p, []),
+    "sparc_proj_gemm": (ctypes.c_int, [ctypes.POINTER(ProjGemmArgs), _vp]),
+    "sparc_proj_gemm_last_error": (ctypes.c_char_p, []),
     "sparc_timing_enable": (ctypes.c_int, [ctypes.c_int]),
     "sparc_timing_kernel_name": (ctypes.c_char_p, [ctypes.c_int]),
     "sparc_timing_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong),

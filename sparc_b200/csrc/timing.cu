@@ -27,7 +27,8 @@ const char* const kNames[kTimeKernels] = {
     "mixer_fwd_summary_kernel", "mixer_carry_scan_kernel(fwd)", "mixer_fwd_replay_kernel",
     "mixer_bwd_summary_kernel", "mixer_carry_scan_kernel(bwd)", "mixer_bwd_grad_kernel",
     "mixer_reduce_kernel",      "real_fwd_kernel",              "real_bwd_kernel",
-    "decode_kernel",            "rtrl_step_kernel",             "rtrl_grad_kernel"};
+    "decode_kernel",            "rtrl_step_kernel",             "rtrl_grad_kernel",
+    "proj_gemm_kernel"};
 
 cudaEvent_t take_event() {
   if (!g_pool.empty()) {

@@ -18,6 +18,7 @@ enum KernelId {
   kTimeDecode,
   kTimeRtrlStep,
   kTimeRtrlGrad,
+  kTimeProjGemm,
   kTimeKernels
 };
 
