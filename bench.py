@@ -5,7 +5,7 @@ SPARCMixer(512) layer, forward + backward of sum(y * g), B=8 x T=2048 tokens per
 parameters from the default init under torch.manual_seed(0), synthetic x, g ~ N(0, 1).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload layer|layer5|stack|real|decode|projection|rtrl]
+                    [--workload layer|layer5|stack|real|decode|projection|projection16|rtrl]
 
 Multi-GPU: one process per GPU (torchrun), batch-sharded data parallelism (each rank runs the
 per-GPU batch: weak scaling), parameter gradients all-reduced over NCCL every step; timing is
@@ -52,6 +52,9 @@ WORKLOADS = {
     # the projection variant (JAX sequence layer) at config 2's token count and state size
     "projection": dict(workload="sparc_sequence_layer_fwd_bwd", batch=8, seq_len=2048, width=512, modes=256,
                        dtype="float32", config_index=0),
+    # the same in bfloat16: the products on the tensor cores (tcgen05)
+    "projection16": dict(workload="sparc_sequence_layer_fwd_bwd_bf16", batch=8, seq_len=16384, width=2048,
+                         modes=1024, dtype="bfloat16", config_index=0),
     # one RTRL cell step (trace update + trace gradients) at a size whose traces exceed L2
     "rtrl": dict(workload="sparc_rtrl_cell_step_fwd_bwd", batch=64, width=512, modes=512,
                  dtype="float32", config_index=0),
@@ -67,6 +70,14 @@ def measured_peaks():
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def _bf16_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
 
 
 # Kernels one mixer fwd+bwd launches: fwd summary, carry scan, replay; bwd summary, carry scan,
@@ -571,8 +582,9 @@ def run_projection(args, wl, world, rank, local):
     torch.manual_seed(0)
     layer = sparc_b200.SPARCSequenceLayer(W, M).to(device)
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
-    x = torch.randn(B, T, W, generator=gen, device=device)
-    g = torch.randn(B, T, W, generator=gen, device=device)
+    dtype = getattr(torch, wl["dtype"])
+    x = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
+    g = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
     reducer = GradAllReduce(layer.parameters()) if world > 1 else None
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.Stream(device)
@@ -610,14 +622,19 @@ def run_projection(args, wl, world, rank, local):
     L.sparc_timing_enable(0)
     kern = {k: round(t / n, 4) for k, (t, n) in times.items()}
     peak, kind = measured_peaks()
-    # the recurrence's algorithmic bytes: content u (2M floats per token) read by the forward
+    # the recurrence's algorithmic bytes: content u (2M values per token) read by the forward
     # summary and replay, states h written; u, dh read and du written by the backward
-    byts = 5 * 2 * M * 4 * B * T
+    byts = 5 * 2 * M * x.element_size() * B * T
     rec_ms = sum(kern.values())
     roofline = {"bound": "hbm", "achieved": round(byts / (rec_ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(byts / (rec_ms / 1e3) / 1e9 / peak, 4), "traffic": None,
-                "kernel": "the seven recurrence kernels (projection mode), 5 x 2M x 4 bytes per token",
+                "kernel": "the seven recurrence kernels (projection mode), 5 x 2M x s bytes per token",
                 "peak_source": kind, "kernels_ms": kern, "recurrence_ms": round(rec_ms, 4)}
+    if "proj_gemm_kernel" in kern:  # tensor-core products: 2 x 2M x W flops per token each, four per step
+        gms = kern["proj_gemm_kernel"]
+        tf = 2.0 * 2 * M * W * B * T / (gms / 1e3) / 1e12
+        roofline["tensor"] = {"kernel": "proj_gemm_kernel", "ms_per_launch": gms, "TFLOPs": round(tf, 1),
+                              "peak_TFLOPs": _bf16_peak(), "frac": round(tf / _bf16_peak(), 4)}
     del graph
     return dict(value=B * T * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=None, cpu=None,
                 clocks=clocks.summary(), launches=MIXER_LAUNCHES * args.steps, per_step_ms=per,
@@ -740,7 +757,8 @@ def main():
 
     world, rank, local = _dist()
     runner = {"layer": run_layer, "layer5": run_layer, "stack": run_stack, "real": run_real,
-              "decode": run_decode, "projection": run_projection, "rtrl": run_rtrl}[args.workload]
+              "decode": run_decode, "projection": run_projection, "projection16": run_projection,
+              "rtrl": run_rtrl}[args.workload]
     r = runner(args, wl, world, rank, local)
     if rank == 0:
         unit = "tokens/s"
@@ -750,11 +768,12 @@ def main():
             wl["chunk"] = r["chunk"]
         for k in ("batch", "seq_len", "width", "modes", "channels", "layers", "steps", "chunk"):
             if k in wl:
-                cfg["global_batch" if k == "batch" else k] = wl[k] * (world if k == "batch" and args.workload in ("layer", "layer5", "real", "decode", "projection", "rtrl") else 1)
+                cfg["global_batch" if k == "batch" else k] = wl[k] * (world if k == "batch" and args.workload in ("layer", "layer5", "real", "decode", "projection", "projection16", "rtrl") else 1)
         cfg["l2"] = ("flushed before every step (512 MiB write, outside the CUDA events)"
                      if args.workload in ("layer", "projection") else "inputs larger than L2")
         cfg["timing"] = ("per-step CUDA events, CUDA-graph replay"
-                         if args.workload in ("layer", "layer5", "decode", "projection") else "per-step CUDA events")
+                         if args.workload in ("layer", "layer5", "decode", "projection", "projection16")
+                         else "per-step CUDA events")
         line = {"metric": METRIC, "value": round(r["value"], 1), "unit": unit, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

@@ -35,8 +35,87 @@ def _f32(t: torch.Tensor) -> torch.Tensor:
     return t.detach().to(torch.float32).contiguous()
 
 
+class _CoreSaved:
+    """What the recurrence's backward needs from its forward."""
+
+    def __init__(self, u, params, carry, controls, h0, lin, max_spin):
+        self.u, self.params, self.carry, self.controls = u, params, carry, controls
+        self.h0, self.lin, self.max_spin = h0, lin, max_spin
+
+
+def _core_forward(u, p, modal, h0, reset, lin, max_spin):
+    """sparc_mixer_forward in projection mode: states h [B, T, 2M] (u.dtype) and the last state
+    from the content input u [B, T, 2M] and the projections p [B, T, 2] float32."""
+    L = _lib.lib()
+    B, T, W = u.shape
+    M = W // 2
+    dt = _lib.dtype_code(u.dtype)
+    dev = u.device
+    params = [_f32(t) for t in modal]
+    p = _f32(p)
+    h0 = None if h0 is None else (_f32(h0[0]), _f32(h0[1]))
+    h = torch.empty_like(u)
+    chunks = L.sparc_mixer_carry_chunks(T, dt)
+    carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
+    controls = torch.empty((B, T, L.sparc_mixer_controls_floats()), dtype=torch.float32, device=dev)
+    last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
+    last_i = torch.empty((B, M), dtype=torch.float32, device=dev)
+    nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
+    if nbytes == 0:
+        _lib.check(-2, "sparc_mixer_workspace_bytes")
+    ws = _lib.WORKSPACES.get(dev, nbytes)
+    a = _lib.MixerFwdArgs(
+        u.data_ptr(), h.data_ptr(), params[0].data_ptr(), params[1].data_ptr(), None, None,
+        params[2].data_ptr(), params[3].data_ptr(), params[4].data_ptr(),
+        _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
+        last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
+        None, 0.0, None, p.data_ptr(), int(lin),
+        ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin)
+    _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
+               "sparc_mixer_forward (projection mode)")
+    return h, last_r, last_i, _CoreSaved(u, params, carry, controls, h0, int(lin), max_spin)
+
+
+def _core_backward(sv: _CoreSaved, dh, dlast_r, dlast_i):
+    """sparc_mixer_backward in projection mode: (du, dp, five modal gradients, gh0 or None)."""
+    L = _lib.lib()
+    u = sv.u
+    B, T, W = u.shape
+    M = W // 2
+    dev = u.device
+    dt = _lib.dtype_code(u.dtype)
+    dh = torch.zeros_like(u) if dh is None else dh.to(u.dtype).contiguous()
+    if dlast_r is None and dlast_i is None:
+        gl = None
+    else:
+        gl = (torch.zeros((B, M), device=dev) if dlast_r is None else _f32(dlast_r),
+              torch.zeros((B, M), device=dev) if dlast_i is None else _f32(dlast_i))
+    du = torch.empty_like(u)
+    dp = torch.empty((B, T, 2), dtype=torch.float32, device=dev)
+    g = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(6)]  # (+ energy slot)
+    gh0 = None
+    if sv.h0 is not None:
+        gh0 = (torch.empty((B, M), dtype=torch.float32, device=dev),
+               torch.empty((B, M), dtype=torch.float32, device=dev))
+    dlog, flog, wlg, wpr, wrr = sv.params
+    ws = _lib.WORKSPACES.get(dev, L.sparc_mixer_workspace_bytes(B, T, W, dt))
+    a = _lib.MixerBwdArgs(
+        u.data_ptr(), None, dh.data_ptr(), du.data_ptr(),
+        dlog.data_ptr(), flog.data_ptr(), None, None, wlg.data_ptr(), wpr.data_ptr(), wrr.data_ptr(),
+        _lib.ptr(sv.h0[0] if sv.h0 else None), _lib.ptr(sv.h0[1] if sv.h0 else None),
+        _lib.ptr(gl[0] if gl else None), _lib.ptr(gl[1] if gl else None),
+        _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
+        sv.carry.data_ptr(), sv.controls.data_ptr(), None, None, None,
+        g[0].data_ptr(), g[1].data_ptr(), None, None, g[2].data_ptr(), g[5].data_ptr(),
+        g[3].data_ptr(), g[4].data_ptr(), dp.data_ptr(), sv.lin,
+        ws.data_ptr(), ws.numel(), B, T, W, dt, sv.max_spin)
+    _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
+               "sparc_mixer_backward (projection mode)")
+    return du, dp, g[:5], gh0
+
+
 class _SparcCoreFunction(torch.autograd.Function):
-    """Autograd op around sparc_mixer_forward / _backward in projection mode.
+    """Autograd op around the recurrence in projection mode.
 
     Inputs: the content input u [B, T, 2M] (float32 or bfloat16), the controller projections
     p [B, T, 2] float32 (bias included) and the five modal parameters. Outputs the states
@@ -45,77 +124,82 @@ class _SparcCoreFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, u, p, decay_log, frequency_log, write_log_gain, write_phase_response,
                 write_retention_response, h0_r, h0_i, max_spin, reset, content_linear):
-        L = _lib.lib()
-        B, T, W = u.shape
-        M = W // 2
-        dt = _lib.dtype_code(u.dtype)
-        dev = u.device
-        params = [_f32(t) for t in (decay_log, frequency_log, write_log_gain, write_phase_response,
-                                    write_retention_response)]
-        p = _f32(p)
-        h0 = None if h0_r is None else (_f32(h0_r), _f32(h0_i))
-        h = torch.empty_like(u)
-        chunks = L.sparc_mixer_carry_chunks(T, dt)
-        carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
-        controls = torch.empty((B, T, L.sparc_mixer_controls_floats()), dtype=torch.float32, device=dev)
-        last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
-        last_i = torch.empty((B, M), dtype=torch.float32, device=dev)
-        nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
-        if nbytes == 0:
-            _lib.check(-2, "sparc_mixer_workspace_bytes")
-        ws = _lib.WORKSPACES.get(dev, nbytes)
-        a = _lib.MixerFwdArgs(
-            u.data_ptr(), h.data_ptr(), params[0].data_ptr(), params[1].data_ptr(), None, None,
-            params[2].data_ptr(), params[3].data_ptr(), params[4].data_ptr(),
-            _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
-            last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
-            None, 0.0, None, p.data_ptr(), int(content_linear),
-            ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin)
-        _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
-                   "sparc_mixer_forward (projection mode)")
-        ctx.save_for_backward(u, *params, carry, controls, *(h0 if h0 else (None, None)))
-        ctx.has_h0 = h0 is not None
-        ctx.max_spin = max_spin
-        ctx.content_linear = int(content_linear)
+        h0 = None if h0_r is None else (h0_r, h0_i)
+        h, lr, li, sv = _core_forward(u, p, (decay_log, frequency_log, write_log_gain, write_phase_response,
+                                             write_retention_response), h0, reset, content_linear, max_spin)
+        ctx.sv = sv
         ctx.set_materialize_grads(False)
-        return h, last_r, last_i
+        return h, lr, li
 
     @staticmethod
     def backward(ctx, dh, dlast_r, dlast_i):
-        L = _lib.lib()
-        u, dlog, flog, wlg, wpr, wrr, carry, controls, h0_r, h0_i = ctx.saved_tensors
-        B, T, W = u.shape
-        M = W // 2
-        dev = u.device
-        dt = _lib.dtype_code(u.dtype)
-        dh = torch.zeros_like(u) if dh is None else dh.to(u.dtype).contiguous()
-        if dlast_r is None and dlast_i is None:
-            gl = None
+        du, dp, g, gh0 = _core_backward(ctx.sv, dh, dlast_r, dlast_i)
+        ctx.sv = None
+        return (du, dp, *g, gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None)
+
+
+class _SequenceLayerTC(torch.autograd.Function):
+    """The whole layer for bfloat16 activations with the products on the tensor cores
+    (sparc_proj_gemm, tcgen05): u = x Wc and the readout with its fused skip in the forward;
+    dh = dy Ro and dx = du Wc^T + dp c^T + skip dy (one fused product) in the backward. The
+    weight gradients (x^T du, dy^T h) and the two controller projections stay torch products
+    (float32 for the projections, whose tanh sets every mode's controls)."""
+
+    @staticmethod
+    def forward(ctx, x, content_real, content_imag, phase_controller, retention_controller, decay_log,
+                frequency_log, write_log_gain, write_phase_response, write_retention_response, readout_real,
+                readout_imag, skip, h0_r, h0_i, reset, lin, max_spin):
+        from . import gemm
+
+        B, T, W = x.shape
+        M = content_real.shape[1]
+        xf = x.reshape(B * T, W)
+        wc = torch.cat((content_real, content_imag), dim=1).detach()               # [W, 2M]
+        ro = torch.cat((readout_real, -readout_imag), dim=1).detach()              # [W, 2M]
+        ctl = torch.stack((phase_controller, retention_controller), dim=1).detach().float()  # [W+1, 2]
+        u = gemm.proj_gemm(xf, wc.t().to(torch.bfloat16).contiguous()).view(B, T, 2 * M)
+        p = torch.addmm(ctl[W], xf.float(), ctl[:W]).view(B, T, 2)
+        h0 = None if h0_r is None else (h0_r, h0_i)
+        h, lr, li, sv = _core_forward(u, p, (decay_log, frequency_log, write_log_gain, write_phase_response,
+                                             write_retention_response), h0, reset, lin, max_spin)
+        ro16 = ro.to(torch.bfloat16).contiguous()
+        y = gemm.proj_gemm(h.view(B * T, 2 * M), ro16, x=xf, skip=skip).view(B, T, W)
+        ctx.sv = sv
+        ctx.save_for_backward(x, h, wc, ro16, ctl, skip.detach().float())
+        ctx.set_materialize_grads(False)
+        return y, lr, li
+
+    @staticmethod
+    def backward(ctx, dy, dlast_r, dlast_i):
+        from . import gemm
+
+        x, h, wc, ro16, ctl, skip = ctx.saved_tensors
+        B, T, W = x.shape
+        M2 = h.shape[-1]
+        xf = x.reshape(B * T, W)
+        hf = h.reshape(B * T, M2)
+        dyf = None if dy is None else dy.to(torch.bfloat16).reshape(B * T, W).contiguous()
+        dh = None if dyf is None else gemm.proj_gemm(dyf, ro16.t().contiguous()).view(B, T, M2)
+        du, dp, g, gh0 = _core_backward(ctx.sv, dh, dlast_r, dlast_i)
+        ctx.sv = None
+        du2 = du.view(B * T, M2)
+        dp2 = dp.view(B * T, 2)
+        wc16 = wc.to(torch.bfloat16).contiguous()
+        if dyf is not None:
+            dx = gemm.proj_gemm(du2, wc16, x=dyf, skip=skip, dp=dp2, c0=ctl[:W, 0], c1=ctl[:W, 1])
+            dro = (dyf.t() @ hf).float()                                           # [W, 2M]
+            dskip = (dyf.float() * xf.float()).sum(0)
         else:
-            gl = (torch.zeros((B, M), device=dev) if dlast_r is None else _f32(dlast_r),
-                  torch.zeros((B, M), device=dev) if dlast_i is None else _f32(dlast_i))
-        du = torch.empty_like(u)
-        dp = torch.empty((B, T, 2), dtype=torch.float32, device=dev)
-        g = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(6)]  # (+ energy slot)
-        gh0 = None
-        if ctx.has_h0:
-            gh0 = (torch.empty((B, M), dtype=torch.float32, device=dev),
-                   torch.empty((B, M), dtype=torch.float32, device=dev))
-        ws = _lib.WORKSPACES.get(dev, L.sparc_mixer_workspace_bytes(B, T, W, dt))
-        a = _lib.MixerBwdArgs(
-            u.data_ptr(), None, dh.data_ptr(), du.data_ptr(),
-            dlog.data_ptr(), flog.data_ptr(), None, None, wlg.data_ptr(), wpr.data_ptr(), wrr.data_ptr(),
-            _lib.ptr(h0_r), _lib.ptr(h0_i),
-            _lib.ptr(gl[0] if gl else None), _lib.ptr(gl[1] if gl else None),
-            _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
-            carry.data_ptr(), controls.data_ptr(), None, None, None,
-            g[0].data_ptr(), g[1].data_ptr(), None, None, g[2].data_ptr(), g[5].data_ptr(),
-            g[3].data_ptr(), g[4].data_ptr(), dp.data_ptr(), ctx.content_linear,
-            ws.data_ptr(), ws.numel(), B, T, W, dt, ctx.max_spin)
-        _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
-                   "sparc_mixer_backward (projection mode)")
-        return (du, dp, g[0], g[1], g[2], g[3], g[4],
-                gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None)
+            dx = gemm.proj_gemm(du2, wc16, dp=dp2, c0=ctl[:W, 0], c1=ctl[:W, 1])
+            dro = torch.zeros((W, M2), dtype=torch.float32, device=x.device)
+            dskip = torch.zeros(W, dtype=torch.float32, device=x.device)
+        dwc = (xf.t() @ du2).float()                                               # [W, 2M]
+        dctl = torch.empty((W + 1, 2), dtype=torch.float32, device=x.device)
+        dctl[:W] = xf.float().t() @ dp2
+        dctl[W] = dp2.sum(0)
+        M = M2 // 2
+        return (dx.view(B, T, W), dwc[:, :M], dwc[:, M:], dctl[:, 0], dctl[:, 1], *g, dro[:, :M], -dro[:, M:],
+                dskip, gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None)
 
 
 def _check_activation(content_activation: str) -> bool:
@@ -149,7 +233,23 @@ def sparc_projection_states(x, params, content_activation: str = "tanh", state=N
 
 def sparc_sequence_layer(x, params, content_activation: str = "tanh", state=None, segment_pos=None,
                          reset_first: bool = False, max_spin: int = 0):
-    """Functional SPARCSequenceLayer: (y [B, T, W], (last_r, last_i))."""
+    """Functional SPARCSequenceLayer: (y [B, T, W], (last_r, last_i)). For bfloat16 activations
+    (widths in whole 16-byte rows) the products run on the tensor cores (_SequenceLayerTC);
+    otherwise they are torch products around the same recurrence kernels."""
+    from . import gemm
+
+    W = x.shape[-1]
+    M = params["decay_log"].shape[0]
+    if x.dtype == torch.bfloat16 and gemm.supported(W, 2 * M):
+        _lib.require_cuda(x, "x")
+        lin = _check_activation(content_activation)
+        h0_r, h0_i = (None, None) if state is None else state
+        reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
+        y, lr, li = _SequenceLayerTC.apply(
+            x.contiguous(), params["content_real"], params["content_imag"], params["phase_controller"],
+            params["retention_controller"], *[params[n] for n in _CORE_PARAMS], params["readout_real"],
+            params["readout_imag"], params["skip"], h0_r, h0_i, reset, lin, int(max_spin))
+        return y, (lr, li)
     (hr, hi), last = sparc_projection_states(x, params, content_activation, state, segment_pos,
                                              reset_first, max_spin)
     ro = torch.cat((params["readout_real"], -params["readout_imag"]), dim=1).to(x.dtype)  # [W, 2M]
