@@ -6,38 +6,42 @@
 //   C[m, n] = sum_k A[m, k] B[n, k]  (+ skip[n] X[m, n]) (+ dp[m, 0] c0[n] + dp[m, 1] c1[n])
 //
 // A [rows, K] and B [N, K] are row-major bfloat16 (both K-major); C is bfloat16 or float32.
-// One CTA computes a 128 x 128 tile of C with tcgen05.mma (kind::f16, bf16 inputs, float32
-// accumulators in tensor memory):
-//   warp 0      TMA producer: 128 x 64 tiles of A and B (128-byte swizzle) into a 3-stage ring
-//               of shared memory, completing on the stage's `full` mbarrier;
-//   warp 1      allocates 128 TMEM columns, then one thread issues four 128x128x16 MMAs per
-//               stage and tcgen05.commit's the stage's `empty` mbarrier (the stage is free once
-//               those MMAs have read it), and after the last stage the `done` mbarrier;
-//   warps 2-5   epilogue: each reads its 32 TMEM lanes (rows) with tcgen05.ld, adds the fused
-//               terms and stores its rows.
-// Two CTAs fit on an SM (96 KB of stages each), so one CTA's epilogue overlaps the other's
-// main loop. Every mbarrier wait is bounded (max_spin polls); a wait that runs out or's 4 into
-// *status, and every role still reaches the end, where the TMEM is released. No multicast.
+// Persistent: one CTA per SM walks the 128 x 256 output tiles t = blockIdx.x, + gridDim.x, ...
+// (n fastest, so the CTAs running at once share their A row panels in L2), with
+// tcgen05.mma (kind::f16, bf16 inputs, float32 accumulators in tensor memory):
+//   warp 0      TMA producer: 128 x 64 tiles of A and 256 x 64 tiles of B (128-byte swizzle)
+//               into a 4-stage ring of shared memory (`full` mbarriers);
+//   warp 1      allocates all 512 TMEM columns (two 256-column accumulators); one thread issues
+//               four 128x256x16 MMAs per stage, tcgen05.commit's the stage's `empty` barrier,
+//               and after a tile's last stage the accumulator's `tmem_full` barrier;
+//   warps 2-5   epilogue: each reads its 32 TMEM lanes (rows) of the finished accumulator with
+//               tcgen05.ld, releases it (`tmem_empty`) and adds the fused terms while storing,
+// so a tile's epilogue overlaps the next tile's main loop. Every mbarrier wait is bounded
+// (max_spin polls); a wait that runs out or's 4 into *status and its role stops, every role
+// still reaches the end, where the TMEM is released. No multicast.
 #include "common.cuh"
 #include "sparc_b200.h"
 #include "timing.cuh"
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
 namespace sparc {
 
-constexpr int kGemmBM = 128, kGemmBN = 128, kGemmBK = 64;  // BK: 64 bf16 = one 128-byte swizzle row
-constexpr int kGemmStages = 3;
+constexpr int kGemmBM = 128, kGemmBN = 256, kGemmBK = 64;  // BK: 64 bf16 = one 128-byte swizzle row
+constexpr int kGemmStages = 4;
 constexpr int kGemmThreads = 192;
-constexpr unsigned kGemmTileBytes = kGemmBM * kGemmBK * 2;  // 16 KB (A and B tiles alike)
+constexpr int kGemmAccs = 2;                                   // TMEM accumulators (2 x 256 columns)
+constexpr unsigned kGemmABytes = kGemmBM * kGemmBK * 2;        // 16 KB
+constexpr unsigned kGemmBBytes = kGemmBN * kGemmBK * 2;        // 32 KB
 constexpr unsigned kStatusGemmTimeout = 4u;
 
 struct GemmParams {
   CUtensorMap map_a;   // A [rows, K] bf16, box {64, 128}, 128-byte swizzle
-  CUtensorMap map_b;   // B [N, K] bf16, same box
+  CUtensorMap map_b;   // B [N, K] bf16, box {64, 256}
   void* out;           // [rows, N]
   int out_f32;
   const __nv_bfloat16* x;  // [rows, N] (skip term) or null
@@ -46,16 +50,18 @@ struct GemmParams {
   const float* c0;         // [N]
   const float* c1;         // [N]
   int rows, N, K;
+  int mtiles, ntiles;
   unsigned max_spin;
   unsigned* status;
 };
 
 struct __align__(1024) GemmSmem {
-  __nv_bfloat16 a[kGemmStages][kGemmBM * kGemmBK];  // each 16 KB, 1024-byte aligned (swizzle atoms)
+  __nv_bfloat16 a[kGemmStages][kGemmBM * kGemmBK];  // 1024-byte aligned tiles (swizzle atoms)
   __nv_bfloat16 b[kGemmStages][kGemmBN * kGemmBK];
   unsigned long long full[kGemmStages];
   unsigned long long empty[kGemmStages];
-  unsigned long long done;
+  unsigned long long tmem_full[kGemmAccs];
+  unsigned long long tmem_empty[kGemmAccs];
   unsigned tmem_base;
 };
 
@@ -65,6 +71,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
           smem_addr(dst)),
       "l"(map), "r"(c0), "r"(c1), "r"(smem_addr(bar))
       : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major tile with 128-byte swizzle: rows of 128 bytes,
@@ -109,13 +119,64 @@ __device__ __forceinline__ void tmem_ld16(unsigned taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(kGemmThreads) proj_gemm_kernel(const __grid_constant__ GemmParams p) {
+// 16 columns of one output row: fused terms, then the store (vectorised when aligned).
+__device__ __forceinline__ void gemm_store16(const GemmParams& p, int row, int n0, float (&v)[16], float d0, float d1) {
+  const int nn = min(16, p.N - n0);
+  const long long base = (long long)row * p.N + n0;
+  const bool vec = nn == 16 && (base & 7) == 0;
+  if (p.x != nullptr) {
+    float xv[16];
+    if (vec) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + base);
+      uint4 w[2] = {__ldg(src), __ldg(src + 1)};
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        xv[2 * i] = f.x;
+        xv[2 * i + 1] = f.y;
+      }
+    } else {
+      for (int i = 0; i < 16; ++i) xv[i] = i < nn ? __bfloat162float(p.x[base + i]) : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = fmaf(i < nn ? __ldg(p.skip + n0 + i) : 0.0f, xv[i], v[i]);
+  }
+  if (p.dp != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i < nn) v[i] = fmaf(d0, __ldg(p.c0 + n0 + i), fmaf(d1, __ldg(p.c1 + n0 + i), v[i]));
+  }
+  if (p.out_f32) {
+    float* o = static_cast<float*>(p.out) + base;
+    if (nn == 16 && (base & 3) == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+      for (int i = 0; i < nn; ++i) o[i] = v[i];
+    }
+  } else {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + base;
+    if (vec) {
+      uint4 w[2];
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      reinterpret_cast<uint4*>(o)[0] = w[0];
+      reinterpret_cast<uint4*>(o)[1] = w[1];
+    } else {
+      for (int i = 0; i < nn; ++i) o[i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1) proj_gemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) unsigned char gemm_smem_raw[];
   // the dynamic shared memory window is only 16-byte aligned: round up to the swizzle atom
   GemmSmem& S = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile_n = blockIdx.x, tile_m = blockIdx.y;
   const int kblocks = (p.K + kGemmBK - 1) / kGemmBK;
+  const int tiles = p.mtiles * p.ntiles;
   bool timed_out = false;
 
   if (threadIdx.x == 0) {
@@ -123,12 +184,15 @@ __global__ void __launch_bounds__(kGemmThreads) proj_gemm_kernel(const __grid_co
       mbar_init(&S.full[s], 1);
       mbar_init(&S.empty[s], 1);
     }
-    mbar_init(&S.done, 1);
+    for (int c = 0; c < kGemmAccs; ++c) {
+      mbar_init(&S.tmem_full[c], 1);
+      mbar_init(&S.tmem_empty[c], 4);  // one arrive per epilogue warp
+    }
     mbar_init_fence();
   }
   if (warp == 1) {  // the whole warp allocates (sync.aligned); the address lands in shared memory
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&S.tmem_base)),
-                 "r"(kGemmBN)
+                 "r"(kGemmAccs * kGemmBN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -140,84 +204,82 @@ __global__ void __launch_bounds__(kGemmThreads) proj_gemm_kernel(const __grid_co
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kb = 0; kb < kblocks && !timed_out; ++kb) {
-        const int s = kb % kGemmStages;
-        const unsigned round = (unsigned)(kb / kGemmStages);
-        if (round > 0 && !mbar_wait(&S.empty[s], (round - 1) & 1u, p.max_spin)) {
-          timed_out = true;
-          break;
+      unsigned it = 0;
+      for (int t = blockIdx.x; t < tiles && !timed_out; t += gridDim.x) {
+        const int tm = t / p.ntiles, tn = t - tm * p.ntiles;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = (int)(it % kGemmStages);
+          const unsigned round = it / kGemmStages;
+          if (round > 0 && !mbar_wait(&S.empty[s], (round - 1) & 1u, p.max_spin)) {
+            timed_out = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&S.full[s], kGemmABytes + kGemmBBytes);
+          tma_load_2d(S.a[s], &p.map_a, kb * kGemmBK, tm * kGemmBM, &S.full[s]);
+          tma_load_2d(S.b[s], &p.map_b, kb * kGemmBK, tn * kGemmBN, &S.full[s]);
         }
-        mbar_arrive_expect_tx(&S.full[s], 2 * kGemmTileBytes);
-        tma_load_2d(S.a[s], &p.map_a, kb * kGemmBK, tile_m * kGemmBM, &S.full[s]);
-        tma_load_2d(S.b[s], &p.map_b, kb * kGemmBK, tile_n * kGemmBN, &S.full[s]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % kGemmStages;
-        if (!mbar_wait(&S.full[s], (unsigned)(kb / kGemmStages) & 1u, p.max_spin)) {
+      unsigned it = 0, lt = 0;
+      for (int t = blockIdx.x; t < tiles && !timed_out; t += gridDim.x, ++lt) {
+        const unsigned acc = lt % kGemmAccs, use = lt / kGemmAccs;
+        if (use > 0 && !mbar_wait(&S.tmem_empty[acc], (use - 1) & 1u, p.max_spin)) {
           timed_out = true;
           break;
         }
         tc_fence_after();
-        const unsigned long long ad = smem_desc_sw128(S.a[s]);
-        const unsigned long long bd = smem_desc_sw128(S.b[s]);
+        const unsigned d = tmem + acc * kGemmBN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = (int)(it % kGemmStages);
+          if (!mbar_wait(&S.full[s], (it / kGemmStages) & 1u, p.max_spin)) {
+            timed_out = true;
+            break;
+          }
+          tc_fence_after();
+          const unsigned long long ad = smem_desc_sw128(S.a[s]);
+          const unsigned long long bd = smem_desc_sw128(S.b[s]);
 #pragma unroll
-        for (int k = 0; k < kGemmBK / 16; ++k)  // 16 bf16 = 32 bytes = 2 descriptor address units
-          umma_bf16(tmem, ad + 2ull * k, bd + 2ull * k, (kb > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&S.empty[s]);
+          for (int k = 0; k < kGemmBK / 16; ++k)  // 16 bf16 = 32 bytes = 2 descriptor address units
+            umma_bf16(d, ad + 2ull * k, bd + 2ull * k, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&S.empty[s]);
+        }
+        umma_commit(&S.tmem_full[acc]);  // arrives once the tile's MMAs have completed
       }
-      umma_commit(&S.done);  // arrives once every MMA issued above has completed
     }
   } else {
     // epilogue: warp w reads TMEM lanes [32 (w % 4), +32) = rows of the tile
     const int q = warp & 3;
-    if (!mbar_wait(&S.done, 0u, p.max_spin)) timed_out = true;
-    tc_fence_after();
-    const int row = tile_m * kGemmBM + q * 32 + lane;
-    const bool row_ok = row < p.rows;
-    float d0 = 0.0f, d1 = 0.0f;
-    if (p.dp != nullptr && row_ok) {
-      d0 = p.dp[2 * (long long)row];
-      d1 = p.dp[2 * (long long)row + 1];
-    }
+    unsigned lt = 0;
+    for (int t = blockIdx.x; t < tiles && !timed_out; t += gridDim.x, ++lt) {
+      const int tm = t / p.ntiles, tn = t - tm * p.ntiles;
+      const unsigned acc = lt % kGemmAccs, use = lt / kGemmAccs;
+      if (!mbar_wait(&S.tmem_full[acc], use & 1u, p.max_spin)) {
+        timed_out = true;
+        break;
+      }
+      tc_fence_after();
+      const int row = tm * kGemmBM + q * 32 + lane;
+      const bool row_ok = row < p.rows;
+      float d0 = 0.0f, d1 = 0.0f;
+      if (p.dp != nullptr && row_ok) {
+        d0 = p.dp[2 * (long long)row];
+        d1 = p.dp[2 * (long long)row + 1];
+      }
+      const unsigned taddr = tmem + acc * kGemmBN + ((unsigned)(q * 32) << 16);
 #pragma unroll 1
-    for (int c = 0; c < kGemmBN; c += 16) {
-      float v[16];
-      __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
-      tmem_ld16(tmem + ((unsigned)(q * 32) << 16) + (unsigned)c, v);
-      const int n0 = tile_n * kGemmBN + c;
-      if (!row_ok || n0 >= p.N) continue;
-      const int nn = min(16, p.N - n0);
-      const long long base = (long long)row * p.N + n0;
-      if (p.x != nullptr) {
-        for (int i = 0; i < nn; ++i) v[i] = fmaf(p.skip[n0 + i], __bfloat162float(p.x[base + i]), v[i]);
+      for (int c = 0; c < kGemmBN; c += 16) {
+        float v[16];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+        tmem_ld16(taddr + (unsigned)c, v);
+        const int n0 = tn * kGemmBN + c;
+        if (row_ok && n0 < p.N) gemm_store16(p, row, n0, v, d0, d1);
       }
-      if (p.dp != nullptr) {
-        for (int i = 0; i < nn; ++i) v[i] = fmaf(d0, p.c0[n0 + i], fmaf(d1, p.c1[n0 + i], v[i]));
-      }
-      if (p.out_f32) {
-        float* o = static_cast<float*>(p.out) + base;
-        if (nn == 16 && (base & 3) == 0) {
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-        } else {
-          for (int i = 0; i < nn; ++i) o[i] = v[i];
-        }
-      } else {
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + base;
-        if (nn == 16 && (base & 7) == 0) {
-          uint4 w[2];
-          __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(w);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-          reinterpret_cast<uint4*>(o)[0] = w[0];
-          reinterpret_cast<uint4*>(o)[1] = w[1];
-        } else {
-          for (int i = 0; i < nn; ++i) o[i] = __float2bfloat16_rn(v[i]);
-        }
-      }
+      // this warp's reads of the accumulator are complete (tcgen05.wait::ld): release it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.tmem_empty[acc]);
     }
   }
   if (timed_out) atomicOr(p.status, kStatusGemmTimeout);
@@ -225,7 +287,8 @@ __global__ void __launch_bounds__(kGemmThreads) proj_gemm_kernel(const __grid_co
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmBN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmAccs * kGemmBN)
+                 : "memory");
   }
 }
 
@@ -245,13 +308,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 gemm_map_encoder() {
   return fn;
 }
 
-// [rows, K] bf16 row-major as a 2-D map with a {64, 128} box and 128-byte swizzle.
-static bool kmajor_map(CUtensorMap* map, const void* base, long long rows, int K) {
+// [rows, K] bf16 row-major as a 2-D map with a {64, box_rows} box and 128-byte swizzle.
+static bool kmajor_map(CUtensorMap* map, const void* base, long long rows, int K, int box_rows) {
   const PFN_cuTensorMapEncodeTiled_v12000 enc = gemm_map_encoder();
   if (enc == nullptr) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)kGemmBM};
+  const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)box_rows};
   const cuuint32_t estride[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estride,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -281,11 +344,11 @@ int sparc_proj_gemm(const SparcProjGemmArgs* a, void* stream) {
   if ((a->x != nullptr) != (a->skip != nullptr) || (a->dp != nullptr && (!a->c0 || !a->c1)))
     return gemm_fail(SPARC_ERR_ARG, "x / skip and dp / c0 / c1 go together");
   const long long mt = (a->rows + kGemmBM - 1) / kGemmBM, nt = (a->n + kGemmBN - 1) / kGemmBN;
-  if (mt > 65535 || nt > 0x7fffffffLL) return gemm_fail(SPARC_ERR_SHAPE, "too many row tiles");
+  if (mt * nt >= (1LL << 31)) return gemm_fail(SPARC_ERR_SHAPE, "too many output tiles");
   if (reinterpret_cast<uintptr_t>(a->a) % 16 || reinterpret_cast<uintptr_t>(a->b) % 16)
     return gemm_fail(SPARC_ERR_ARG, "a and b must be 16-byte aligned");
   GemmParams p;
-  if (!kmajor_map(&p.map_a, a->a, a->rows, a->k) || !kmajor_map(&p.map_b, a->b, a->n, a->k))
+  if (!kmajor_map(&p.map_a, a->a, a->rows, a->k, kGemmBM) || !kmajor_map(&p.map_b, a->b, a->n, a->k, kGemmBN))
     return gemm_fail(SPARC_ERR_ARG, "tensor map encoding failed");
   p.out = a->out;
   p.out_f32 = a->out_f32;
@@ -297,6 +360,8 @@ int sparc_proj_gemm(const SparcProjGemmArgs* a, void* stream) {
   p.rows = (int)a->rows;
   p.N = a->n;
   p.K = a->k;
+  p.mtiles = (int)mt;
+  p.ntiles = (int)nt;
   p.max_spin = a->max_spin ? a->max_spin : (1u << 22);
   p.status = a->status;
   const size_t smem = sizeof(GemmSmem) + 1024;
@@ -308,7 +373,12 @@ int sparc_proj_gemm(const SparcProjGemmArgs* a, void* stream) {
   if (attr_err != cudaSuccess) return gemm_fail(SPARC_ERR_LAUNCH, cudaGetErrorString(attr_err));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)nt, (unsigned)mt, 1);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  cfg.gridDim = dim3((unsigned)std::min<long long>(mt * nt, sms), 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
