@@ -14,8 +14,10 @@
 //   warp 1      allocates all 512 TMEM columns (two 256-column accumulators); one thread issues
 //               four 128x256x16 MMAs per stage, tcgen05.commit's the stage's `empty` barrier,
 //               and after a tile's last stage the accumulator's `tmem_full` barrier;
-//   warps 2-5   epilogue: each reads its 32 TMEM lanes (rows) of the finished accumulator with
-//               tcgen05.ld, releases it (`tmem_empty`) and adds the fused terms while storing,
+//   warps 2-9   epilogue: warp w reads TMEM lanes [32 (w % 4), +32) (rows) and one half of the
+//               columns of the finished accumulator with tcgen05.ld (the fused skip term's
+//               loads issued first, so their latency overlaps the TMEM reads), releases it
+//               (`tmem_empty`) and stores,
 // so a tile's epilogue overlaps the next tile's main loop. Every mbarrier wait is bounded
 // (max_spin polls); a wait that runs out or's 4 into *status and its role stops, every role
 // still reaches the end, where the TMEM is released. No multicast.
@@ -33,7 +35,8 @@ namespace sparc {
 
 constexpr int kGemmBM = 128, kGemmBN = 256, kGemmBK = 64;  // BK: 64 bf16 = one 128-byte swizzle row
 constexpr int kGemmStages = 4;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmEpiWarps = 8;                               // two per TMEM lane quadrant
+constexpr int kGemmThreads = 64 + 32 * kGemmEpiWarps;
 constexpr int kGemmAccs = 2;                                   // TMEM accumulators (2 x 256 columns)
 constexpr unsigned kGemmABytes = kGemmBM * kGemmBK * 2;        // 16 KB
 constexpr unsigned kGemmBBytes = kGemmBN * kGemmBK * 2;        // 32 KB
@@ -107,40 +110,57 @@ __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld16(unsigned taddr, float (&v)[16]) {
-  unsigned r[16];
+// 16 consecutive columns of this thread's TMEM lane (no wait: see tmem_wait16).
+__device__ __forceinline__ void tmem_ld16(unsigned taddr, unsigned (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// tcgen05.wait::ld for two 16-column loads; the registers are operands, so no use of them can be
+// scheduled before the wait.
+__device__ __forceinline__ void tmem_wait32(unsigned (&a)[16], unsigned (&b)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                 "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]),
+                 "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
+                 "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15])
+               :
+               : "memory");
+}
+
+// The skip term's 16 bf16 of one row (raw, as two 16-byte words; zero past N or the rows).
+__device__ __forceinline__ void gemm_load_x16(const GemmParams& p, int row, int n0, bool ok, uint4 (&w)[2]) {
+  w[0] = w[1] = make_uint4(0u, 0u, 0u, 0u);
+  if (p.x == nullptr || !ok || n0 >= p.N) return;
+  const int nn = min(16, p.N - n0);
+  const long long base = (long long)row * p.N + n0;
+  if (nn == 16 && (base & 7) == 0) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + base);
+    w[0] = __ldg(src);
+    w[1] = __ldg(src + 1);
+  } else {
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(w);
+    for (int i = 0; i < nn; ++i) h[i] = p.x[base + i];
+  }
 }
 
 // 16 columns of one output row: fused terms, then the store (vectorised when aligned).
-__device__ __forceinline__ void gemm_store16(const GemmParams& p, int row, int n0, float (&v)[16], float d0, float d1) {
+__device__ __forceinline__ void gemm_store16(const GemmParams& p, int row, int n0, float (&v)[16], float d0, float d1,
+                                             const uint4 (&xw)[2]) {
   const int nn = min(16, p.N - n0);
   const long long base = (long long)row * p.N + n0;
   const bool vec = nn == 16 && (base & 7) == 0;
   if (p.x != nullptr) {
-    float xv[16];
-    if (vec) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.x + base);
-      uint4 w[2] = {__ldg(src), __ldg(src + 1)};
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(w);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(xw);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        xv[2 * i] = f.x;
-        xv[2 * i + 1] = f.y;
-      }
-    } else {
-      for (int i = 0; i < 16; ++i) xv[i] = i < nn ? __bfloat162float(p.x[base + i]) : 0.0f;
+    for (int i = 0; i < 8; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      if (2 * i < nn) v[2 * i] = fmaf(__ldg(p.skip + n0 + 2 * i), f.x, v[2 * i]);
+      if (2 * i + 1 < nn) v[2 * i + 1] = fmaf(__ldg(p.skip + n0 + 2 * i + 1), f.y, v[2 * i + 1]);
     }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = fmaf(i < nn ? __ldg(p.skip + n0 + i) : 0.0f, xv[i], v[i]);
   }
   if (p.dp != nullptr) {
 #pragma unroll
@@ -186,7 +206,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_gemm_kernel(const __grid
     }
     for (int c = 0; c < kGemmAccs; ++c) {
       mbar_init(&S.tmem_full[c], 1);
-      mbar_init(&S.tmem_empty[c], 4);  // one arrive per epilogue warp
+      mbar_init(&S.tmem_empty[c], kGemmEpiWarps);  // one arrive per epilogue warp
     }
     mbar_init_fence();
   }
@@ -249,8 +269,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_gemm_kernel(const __grid
       }
     }
   } else {
-    // epilogue: warp w reads TMEM lanes [32 (w % 4), +32) = rows of the tile
+    // epilogue: warp w reads TMEM lanes [32 (w % 4), +32) = rows of the tile, columns
+    // [half * 128, +128)
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     unsigned lt = 0;
     for (int t = blockIdx.x; t < tiles && !timed_out; t += gridDim.x, ++lt) {
       const int tm = t / p.ntiles, tn = t - tm * p.ntiles;
@@ -268,13 +290,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) proj_gemm_kernel(const __grid
         d1 = p.dp[2 * (long long)row + 1];
       }
       const unsigned taddr = tmem + acc * kGemmBN + ((unsigned)(q * 32) << 16);
+      constexpr int kCols = kGemmBN / 2;
 #pragma unroll 1
-      for (int c = 0; c < kGemmBN; c += 16) {
-        float v[16];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
-        tmem_ld16(taddr + (unsigned)c, v);
+      for (int c = half * kCols; c < (half + 1) * kCols; c += 32) {
         const int n0 = tn * kGemmBN + c;
-        if (row_ok && n0 < p.N) gemm_store16(p, row, n0, v, d0, d1);
+        uint4 xa[2], xb[2];  // the skip term's loads first: in flight during the TMEM reads
+        gemm_load_x16(p, row, n0, row_ok, xa);
+        gemm_load_x16(p, row, n0 + 16, row_ok, xb);
+        unsigned ra[16], rb[16];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+        tmem_ld16(taddr + (unsigned)c, ra);
+        tmem_ld16(taddr + (unsigned)(c + 16), rb);
+        tmem_wait32(ra, rb);
+        float va[16], vb[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          va[i] = __uint_as_float(ra[i]);
+          vb[i] = __uint_as_float(rb[i]);
+        }
+        if (row_ok && n0 < p.N) gemm_store16(p, row, n0, va, d0, d1, xa);
+        if (row_ok && n0 + 16 < p.N) gemm_store16(p, row, n0 + 16, vb, d0, d1, xb);
       }
       // this warp's reads of the accumulator are complete (tcgen05.wait::ld): release it
       tc_fence_before();
