@@ -364,6 +364,41 @@ typedef struct SparcProjGemmArgs {
 int sparc_proj_gemm(const SparcProjGemmArgs* args, void* stream);
 const char* sparc_proj_gemm_last_error(void);
 
+/* Parameter-gradient all-reduce over NVLink peer memory (batch-sharded data parallelism: the
+ * one exchange step; replaces the NCCL all-reduce of the concatenated gradients). Each rank
+ * allocates one buffer of sparc_peer_buffer_bytes(world, total) bytes (sparc_peer_buffer_alloc,
+ * zeroed, with its CUDA IPC handle), the handles are exchanged by the caller (any host
+ * collective), and each rank opens the others' (sparc_peer_buffer_open). sparc_peer_allreduce
+ * then sums the float32 gradient segments (in order, `total` floats) over the ranks in place:
+ * every rank gets the identical sum in rank order, times `scale`. One kernel: each CTA pushes
+ * its slice into every rank's buffer, publishes an epoch flag per rank and waits (bounded by
+ * max_spin polls; a wait that runs out or's 8 into *status) for every rank's slice. Every rank
+ * must call it the same number of times with the same total. inject_skip_publish (tests only)
+ * withholds this rank's flags so that the peers' waits run out. */
+#define SPARC_PEER_MAX_RANKS 8
+#define SPARC_PEER_MAX_SEGMENTS 64
+typedef struct SparcPeerAllreduceArgs {
+  float* segments[SPARC_PEER_MAX_SEGMENTS];
+  long long counts[SPARC_PEER_MAX_SEGMENTS];
+  int nseg;
+  long long total;
+  void* buffers[SPARC_PEER_MAX_RANKS]; /* every rank's buffer as mapped in this process (own included) */
+  int world;
+  int rank;
+  float scale;
+  unsigned max_spin;
+  unsigned* status;
+  int inject_skip_publish;
+} SparcPeerAllreduceArgs;
+
+size_t sparc_peer_buffer_bytes(int world, long long total);
+int sparc_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle /* 64 bytes out */);
+int sparc_peer_buffer_open(const void* ipc_handle, void** ptr);
+int sparc_peer_buffer_close(void* ptr);
+int sparc_peer_buffer_free(void* ptr);
+int sparc_peer_allreduce(const SparcPeerAllreduceArgs* args, void* stream);
+const char* sparc_peer_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif

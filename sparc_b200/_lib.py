@@ -113,6 +113,14 @@ class ProjGemmArgs(ctypes.Structure):
     ]
 
 
+class PeerAllreduceArgs(ctypes.Structure):
+    _fields_ = [
+        ("segments", _vp * 64), ("counts", _ll * 64), ("nseg", ctypes.c_int), ("total", _ll),
+        ("buffers", _vp * 8), ("world", ctypes.c_int), ("rank", ctypes.c_int), ("scale", ctypes.c_float),
+        ("max_spin", ctypes.c_uint), ("status", _vp), ("inject_skip_publish", ctypes.c_int),
+    ]
+
+
 # every symbol declared in include/sparc_b200.h, with its ctypes signature
 SIGNATURES = {
     "sparc_last_error": (ctypes.c_char_p, []),
@@ -138,6 +146,13 @@ SIGNATURES = {
     "sparc_rtrl_last_error": (ctypes.c_char_p, []),
     "sparc_proj_gemm": (ctypes.c_int, [ctypes.POINTER(ProjGemmArgs), _vp]),
     "sparc_proj_gemm_last_error": (ctypes.c_char_p, []),
+    "sparc_peer_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int, _ll]),
+    "sparc_peer_buffer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
+    "sparc_peer_buffer_open": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    "sparc_peer_buffer_close": (ctypes.c_int, [_vp]),
+    "sparc_peer_buffer_free": (ctypes.c_int, [_vp]),
+    "sparc_peer_allreduce": (ctypes.c_int, [ctypes.POINTER(PeerAllreduceArgs), _vp]),
+    "sparc_peer_last_error": (ctypes.c_char_p, []),
     "sparc_timing_enable": (ctypes.c_int, [ctypes.c_int]),
     "sparc_timing_kernel_name": (ctypes.c_char_p, [ctypes.c_int]),
     "sparc_timing_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong),

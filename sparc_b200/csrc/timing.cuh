@@ -19,6 +19,7 @@ enum KernelId {
   kTimeRtrlStep,
   kTimeRtrlGrad,
   kTimeProjGemm,
+  kTimePeerAllreduce,
   kTimeKernels
 };
 

@@ -42,9 +42,10 @@ def test_struct_layouts_match_header():
     for cname, py in (("SparcMixerFwdArgs", _lib.MixerFwdArgs), ("SparcMixerBwdArgs", _lib.MixerBwdArgs),
                       ("SparcDecodeArgs", _lib.DecodeArgs), ("SparcRealFwdArgs", _lib.RealFwdArgs),
                       ("SparcRealBwdArgs", _lib.RealBwdArgs), ("SparcRtrlStepArgs", _lib.RtrlStepArgs),
-                      ("SparcRtrlGradArgs", _lib.RtrlGradArgs), ("SparcProjGemmArgs", _lib.ProjGemmArgs)):
+                      ("SparcRtrlGradArgs", _lib.RtrlGradArgs), ("SparcProjGemmArgs", _lib.ProjGemmArgs),
+                      ("SparcPeerAllreduceArgs", _lib.PeerAllreduceArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\}" % cname, src, flags=re.S).group(1)
-        fields = re.findall(r"(\w+)\s*(?:\[\d+\])?\s*;", body)
+        fields = re.findall(r"(\w+)\s*(?:\[\w+\])?\s*;", body)
         assert fields == [f[0] for f in py._fields_], cname
 
 
