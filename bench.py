@@ -8,8 +8,9 @@ parameters from the default init under torch.manual_seed(0), synthetic x, g ~ N(
                     [--workload layer|layer5|stack|real|decode|projection|projection16|rtrl]
 
 Multi-GPU: one process per GPU (torchrun), batch-sharded data parallelism (each rank runs the
-per-GPU batch: weak scaling), parameter gradients all-reduced over NCCL every step; timing is
-the max over ranks of per-step CUDA-event times.
+per-GPU batch: weak scaling), parameter gradients summed every step by the library's
+peer-memory all-reduce kernel over NVLink (`--allreduce nccl`: NCCL's all-reduce instead);
+timing is the max over ranks of per-step CUDA-event times.
 
 Timing: W untimed warm-up steps; the step is captured once in a CUDA graph and replayed. Before
 every timed step L2 is flushed by writing a 512 MiB buffer (the config-2 inputs fit in L2);
@@ -174,6 +175,26 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+_REDUCERS = []
+
+
+def make_reducer(args, params):
+    """The per-step exchange of the parameter gradients for N > 1: the library's peer-memory
+    all-reduce kernel (default), or NCCL's all-reduce of the packed gradients (--allreduce nccl)."""
+    import torch.distributed as dist
+
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return None
+    from sparc_b200.ddp import GradAllReduce, PeerGradAllReduce
+
+    params = [p for p in params if p.requires_grad]
+    if args.allreduce == "peer" and dist.get_world_size() <= 8 and len(params) <= 64:
+        r = PeerGradAllReduce(params)
+        _REDUCERS.append(r)
+        return r
+    return GradAllReduce(params)
+
+
 # ----------------------------------------------------------------------------- CPU oracle
 def _oracle_rows(args):
     """float64 oracle forward+backward of a block of batch rows (run in a worker process)."""
@@ -282,7 +303,6 @@ def run_layer(args, wl, world, rank, local):
 
     import sparc_b200
     from sparc_b200 import _lib
-    from sparc_b200.ddp import GradAllReduce
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -293,7 +313,7 @@ def run_layer(args, wl, world, rank, local):
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
     x = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
     g = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
-    reducer = GradAllReduce(model.parameters()) if world > 1 else None
+    reducer = make_reducer(args, model.parameters())
     s = 4 if dtype == torch.float32 else 2
     small = 2 * B * T * W * s < (256 << 20)  # inputs that could sit in the 126 MB L2
     flush_buf = torch.empty(512 << 20 if small else 16, dtype=torch.uint8, device=device)
@@ -445,7 +465,6 @@ def run_stack(args, wl, world, rank, local):
     import torch
 
     import sparc_b200
-    from sparc_b200.ddp import GradAllReduce
     from sparc_b200.stack import SPARCStack
 
     device = torch.device("cuda", local)
@@ -457,7 +476,7 @@ def run_stack(args, wl, world, rank, local):
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
     x = torch.randn(B, T, W, generator=gen, device=device).to(torch.bfloat16)
     g = torch.randn(B, T, W, generator=gen, device=device).to(torch.bfloat16)
-    reducer = GradAllReduce(model.parameters()) if world > 1 else None
+    reducer = make_reducer(args, model.parameters())
 
     def step():
         model.zero_grad(set_to_none=True)
@@ -574,7 +593,6 @@ def run_projection(args, wl, world, rank, local):
 
     import sparc_b200
     from sparc_b200 import _lib
-    from sparc_b200.ddp import GradAllReduce
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -585,7 +603,7 @@ def run_projection(args, wl, world, rank, local):
     dtype = getattr(torch, wl["dtype"])
     x = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
     g = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
-    reducer = GradAllReduce(layer.parameters()) if world > 1 else None
+    reducer = make_reducer(args, layer.parameters())
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
@@ -722,6 +740,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="layer")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: gradient exchange by the peer-memory kernel or by NCCL")
     ap.add_argument("--batch", type=int, default=None, help="override the per-GPU batch (profiling runs)")
     ap.add_argument("--seq-len", type=int, default=None, help="override the sequence length (profiling runs)")
     args = ap.parse_args()
@@ -764,6 +784,9 @@ def main():
         unit = "tokens/s"
         cfg = {"workload": wl["workload"], "baseline_config": wl["config_index"],
                "parallelism": f"dp{world}" if world > 1 else "single"}
+        if world > 1:
+            cfg["gradient_exchange"] = ("peer-memory all-reduce kernel (NVLink, CUDA IPC)" if args.allreduce == "peer"
+                                        else "NCCL all-reduce of the packed gradients")
         if "chunk" in r:
             wl["chunk"] = r["chunk"]
         for k in ("batch", "seq_len", "width", "modes", "channels", "layers", "steps", "chunk"):
@@ -784,6 +807,8 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        for r in _REDUCERS:
+            r.close()
         dist.barrier()
         dist.destroy_process_group()
 
