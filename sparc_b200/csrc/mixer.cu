@@ -296,8 +296,14 @@ __host__ __device__ constexpr int log2i() { return N <= 1 ? 0 : 1 + log2i<N / 2>
 // writing every chunk's v. No CTA waits on anything but the cluster barrier, and the composition
 // order is fixed, so the carries are bitwise reproducible.
 constexpr int kScanThreads = 256;
-constexpr int kScanQ = 8;        // CTAs per row (portable cluster size)
-constexpr int kScanBatch = 16;   // chunk maps in flight per thread
+#ifndef SPARC_SCAN_Q
+#define SPARC_SCAN_Q 8
+#endif
+#ifndef SPARC_SCAN_BATCH
+#define SPARC_SCAN_BATCH 16
+#endif
+constexpr int kScanQ = SPARC_SCAN_Q;          // CTAs per row (portable cluster size)
+constexpr int kScanBatch = SPARC_SCAN_BATCH;  // chunk maps in flight per thread
 
 struct ScanParams {
   const float4* agg;     // [B, chunks, Mp] per-chunk maps (A, B)
