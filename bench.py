@@ -9,7 +9,8 @@ parameters from the default init under torch.manual_seed(0), synthetic x, g ~ N(
 
 Multi-GPU: one process per GPU (torchrun), batch-sharded data parallelism (each rank runs the
 per-GPU batch: weak scaling), parameter gradients summed every step by the library's
-peer-memory all-reduce kernel over NVLink (`--allreduce nccl`: NCCL's all-reduce instead);
+gradient reduction kernel, which also sums them over the ranks through NVLink peer memory
+(`--allreduce peer`: a separate peer-memory all-reduce kernel; `nccl`: NCCL's all-reduce);
 timing is the max over ranks of per-step CUDA-event times.
 
 Timing: W untimed warm-up steps; the step is captured once in a CUDA graph and replayed. Before
@@ -178,17 +179,25 @@ class ClockSampler:
 _REDUCERS = []
 
 
-def make_reducer(args, params):
-    """The per-step exchange of the parameter gradients for N > 1: the library's peer-memory
-    all-reduce kernel (default), or NCCL's all-reduce of the packed gradients (--allreduce nccl)."""
+def make_reducer(args, params, fused_ok=False):
+    """The per-step exchange of the parameter gradients for N > 1: inside the mixer kernels'
+    gradient reduction (`fused`, the default where every parameter is a mixer / block parameter),
+    the library's peer-memory all-reduce kernel after the backward (`peer`), or NCCL's all-reduce
+    of the packed gradients (`nccl`). Returns the callable to run after the backward, or None."""
     import torch.distributed as dist
 
     if not dist.is_initialized() or dist.get_world_size() == 1:
         return None
-    from sparc_b200.ddp import GradAllReduce, PeerGradAllReduce
+    from sparc_b200.ddp import FusedGradExchange, GradAllReduce, PeerGradAllReduce
 
     params = [p for p in params if p.requires_grad]
-    if args.allreduce == "peer" and dist.get_world_size() <= 8 and len(params) <= 64:
+    mode = args.allreduce
+    if mode == "fused" and not fused_ok:
+        mode = "peer"
+    if mode == "fused" and dist.get_world_size() <= 8:
+        _REDUCERS.append(FusedGradExchange())
+        return None
+    if mode == "peer" and dist.get_world_size() <= 8 and len(params) <= 64:
         r = PeerGradAllReduce(params)
         _REDUCERS.append(r)
         return r
@@ -313,7 +322,7 @@ def run_layer(args, wl, world, rank, local):
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
     x = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
     g = torch.randn(B, T, W, generator=gen, device=device).to(dtype)
-    reducer = make_reducer(args, model.parameters())
+    reducer = make_reducer(args, model.parameters(), fused_ok=True)
     s = 4 if dtype == torch.float32 else 2
     small = 2 * B * T * W * s < (256 << 20)  # inputs that could sit in the 126 MB L2
     flush_buf = torch.empty(512 << 20 if small else 16, dtype=torch.uint8, device=device)
@@ -476,7 +485,7 @@ def run_stack(args, wl, world, rank, local):
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
     x = torch.randn(B, T, W, generator=gen, device=device).to(torch.bfloat16)
     g = torch.randn(B, T, W, generator=gen, device=device).to(torch.bfloat16)
-    reducer = make_reducer(args, model.parameters())
+    reducer = make_reducer(args, model.parameters(), fused_ok=True)
 
     def step():
         model.zero_grad(set_to_none=True)
@@ -740,8 +749,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="layer")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
-                    help="N > 1: gradient exchange by the peer-memory kernel or by NCCL")
+    ap.add_argument("--allreduce", choices=["fused", "peer", "nccl"], default="fused",
+                    help="N > 1: gradient exchange fused into the gradient reduction kernel, by the "
+                         "peer-memory all-reduce kernel, or by NCCL")
     ap.add_argument("--batch", type=int, default=None, help="override the per-GPU batch (profiling runs)")
     ap.add_argument("--seq-len", type=int, default=None, help="override the sequence length (profiling runs)")
     args = ap.parse_args()
@@ -785,8 +795,11 @@ def main():
         cfg = {"workload": wl["workload"], "baseline_config": wl["config_index"],
                "parallelism": f"dp{world}" if world > 1 else "single"}
         if world > 1:
-            cfg["gradient_exchange"] = ("peer-memory all-reduce kernel (NVLink, CUDA IPC)" if args.allreduce == "peer"
-                                        else "NCCL all-reduce of the packed gradients")
+            cfg["gradient_exchange"] = {
+                "fused": "in the gradient reduction kernel over NVLink peer memory (CUDA IPC)",
+                "peer": "peer-memory all-reduce kernel (NVLink, CUDA IPC)",
+                "nccl": "NCCL all-reduce of the packed gradients"}[
+                    args.allreduce if args.allreduce != "fused" or args.workload in ("layer", "layer5", "stack") else "peer"]
         if "chunk" in r:
             wl["chunk"] = r["chunk"]
         for k in ("batch", "seq_len", "width", "modes", "channels", "layers", "steps", "chunk"):

@@ -161,6 +161,10 @@ typedef struct SparcMixerBwdArgs {
   float* grad_write_radial_response;   /* [M] */
   float* grad_projections;             /* projection mode: [batch, length, 2] out, else NULL */
   int content_linear;                  /* projection mode: as given to the forward */
+  void* exchange_buffers[8];           /* data parallelism: every rank's exchange buffer (below) */
+  int exchange_world;                  /* > 1: the parameter gradients are summed over the ranks */
+  int exchange_rank;
+  unsigned* exchange_status;           /* device word, or'ed with 16 if an exchange wait ran out */
   void* workspace;
   size_t workspace_bytes;
   long long batch;
@@ -169,6 +173,16 @@ typedef struct SparcMixerBwdArgs {
   int dtype;
   unsigned max_spin;
 } SparcMixerBwdArgs;
+
+/* Fused cross-GPU gradient sum (batch-sharded data parallelism, up to 8 ranks of one node):
+ * with exchange_world > 1 the backward's parameter-gradient reduction kernel also sums every
+ * gradient over the ranks through NVLink peer memory before writing it, so the gradients it
+ * returns are already the group's sums (no separate all-reduce). Each rank allocates one buffer
+ * of sparc_exchange_buffer_bytes(world) bytes with sparc_peer_buffer_alloc (zeroed, with its
+ * IPC handle), the handles are exchanged by the caller and opened with sparc_peer_buffer_open;
+ * exchange_buffers[r] is rank r's buffer as mapped in this process. Every rank must make the
+ * same sequence of backward calls with the same shapes. */
+size_t sparc_exchange_buffer_bytes(int world);
 
 /* One fused decode step (forward/decode.py:11-55): x [batch, width] (dtype), state
  * [batch, M] float32 in; y [batch, width] (dtype), new state [batch, M] float32 out. The new

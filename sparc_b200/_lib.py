@@ -53,6 +53,8 @@ class MixerBwdArgs(ctypes.Structure):
         ("grad_radial_direction", _vp), ("grad_write_log_gain", _vp), ("grad_energy_response", _vp),
         ("grad_write_phase_response", _vp), ("grad_write_radial_response", _vp),
         ("grad_projections", _vp), ("content_linear", ctypes.c_int),
+        ("exchange_buffers", _vp * 8), ("exchange_world", ctypes.c_int), ("exchange_rank", ctypes.c_int),
+        ("exchange_status", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint),
@@ -146,6 +148,7 @@ SIGNATURES = {
     "sparc_rtrl_last_error": (ctypes.c_char_p, []),
     "sparc_proj_gemm": (ctypes.c_int, [ctypes.POINTER(ProjGemmArgs), _vp]),
     "sparc_proj_gemm_last_error": (ctypes.c_char_p, []),
+    "sparc_exchange_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int]),
     "sparc_peer_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int, _ll]),
     "sparc_peer_buffer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
     "sparc_peer_buffer_open": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),

@@ -380,4 +380,79 @@ __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- peer exchange (N GPUs)
+// One warp's values summed over the ranks of a data-parallel group through NVLink peer memory,
+// inside the kernel that computed them (the parameter-gradient reduction). Every rank holds an
+// exchange buffer mapped into every rank (CUDA IPC):
+//   flags [8][kXchgSlots] u32, epoch [kXchgSlots] u32, inbox [2][world][kXchgSlots][32] f32.
+// A slot is one warp-sized group of values of one launch geometry; its epoch counts the
+// launches that used it. The warp stores its 32 values into inbox[e & 1][rank][slot] of every
+// rank, publishes e in every rank's flags[rank][slot] (release, system scope), waits (bounded)
+// until every rank's flag for the slot reaches e (acquire), and sums the ranks' values in rank
+// order: every rank gets the identical sum. A peer can run one exchange ahead on a slot (the
+// parity double-buffers the inbox) but not two (it needs this rank's next push first).
+constexpr int kXchgSlots = 1024;
+constexpr int kXchgMaxRanks = 8;
+constexpr unsigned kStatusXchgTimeout = 16u;
+
+struct PeerExchange {
+  unsigned char* base[kXchgMaxRanks];  // every rank's exchange buffer, as mapped here
+  int world, rank;                     // world <= 1: no exchange
+  unsigned* status;
+  unsigned max_spin;
+};
+
+__host__ __device__ constexpr size_t xchg_flags_bytes() { return (size_t)kXchgMaxRanks * kXchgSlots * 4; }
+__host__ __device__ constexpr size_t xchg_inbox_offset() { return xchg_flags_bytes() + (size_t)kXchgSlots * 4; }
+__host__ __device__ constexpr size_t xchg_buffer_bytes(int world) {
+  return xchg_inbox_offset() + 2 * (size_t)world * kXchgSlots * 32 * 4;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Called by all 32 lanes of one warp with the lane's value; returns the sum over the ranks.
+__device__ __forceinline__ float warp_exchange(const PeerExchange& x, int slot, float val) {
+  const int lane = threadIdx.x & 31;
+  unsigned* flags_own = reinterpret_cast<unsigned*>(x.base[x.rank]);
+  unsigned* epoch = reinterpret_cast<unsigned*>(x.base[x.rank] + xchg_flags_bytes()) + slot;
+  unsigned e = 0;
+  if (lane == 0) e = *epoch + 1u;
+  e = __shfl_sync(0xffffffffu, e, 0);
+  const long long par = e & 1u;
+  for (int r = 0; r < x.world; ++r) {
+    float* in = reinterpret_cast<float*>(x.base[r] + xchg_inbox_offset());
+    in[((par * x.world + x.rank) * kXchgSlots + slot) * 32 + lane] = val;
+  }
+  __syncwarp();  // the warp's peer stores precede the release below (cumulativity)
+  if (lane < x.world)
+    st_release_sys(reinterpret_cast<unsigned*>(x.base[lane]) + (long long)x.rank * kXchgSlots + slot, e);
+  bool late = false;
+  if (lane < x.world) {
+    const unsigned* f = flags_own + (long long)lane * kXchgSlots + slot;
+    unsigned it = 0;
+    while ((int)(ld_acquire_sys(f) - e) < 0) {
+      if (++it >= x.max_spin) {
+        late = true;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  if (late) atomicOr(x.status, kStatusXchgTimeout);
+  __syncwarp();
+  const float* own = reinterpret_cast<const float*>(x.base[x.rank] + xchg_inbox_offset());
+  float s = 0.0f;
+  for (int r = 0; r < x.world; ++r) s += __ldcv(own + ((par * x.world + r) * kXchgSlots + slot) * 32 + lane);
+  if (lane == 0) *epoch = e;
+  return s;
+}
+
 }  // namespace sparc
+

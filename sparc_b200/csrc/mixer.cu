@@ -398,12 +398,16 @@ struct ReduceParams {
   float* g_phase_dir;   // [W+1], or null (projection mode)
   float* g_radial_dir;  // [W+1], or null (projection mode)
   float* g_norm_w;      // [W] (block) or null
+  PeerExchange xchg;    // world > 1: sum every gradient over the ranks before writing it
 };
 
 // grid (ceil(Mp/32), kPartModes + 1), block (32, kReduceWarps). Rows q < kPartModes: warp w sums
 // clusters w, w + kReduceWarps, ... for 32 modes (coalesced, eight loads in flight), then warp 0
 // adds the warps' sums. Row kPartModes (block 0 only): warps 0 and 1 sum the two controller
-// biases over the clusters, lane-strided, then a shuffle tree. Every order is fixed.
+// biases over the clusters, lane-strided, then a shuffle tree. Every order is fixed. With an
+// exchange group (N GPUs of batch-sharded data parallelism), warp 0 of every CTA then sums its
+// values over the ranks through NVLink peer memory (warp_exchange) before writing them: the
+// gradient reduction and the cross-GPU all-reduce are one kernel.
 constexpr int kReduceWarps = 16;
 constexpr int kReduceUnroll = 8;
 
@@ -411,16 +415,30 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
   pdl_wait();  // the partials (gradient kernel) are complete from here on
   const int lane = threadIdx.x, w = threadIdx.y;
   const int q = blockIdx.y;
+  const bool xchg = r.xchg.world > 1;
+  const int slot = blockIdx.y * gridDim.x + blockIdx.x;  // this CTA's exchange slot
   if (q == kPartModes) {
-    if (blockIdx.x != 0 || w >= 2 || r.g_phase_dir == nullptr) return;
-    const double* pb = r.part + (long long)r.clusters * kPartModes * r.Mp;
-    double t = 0.0;
-    for (int k = lane; k < r.clusters; k += 32) t += pb[2 * k + w];
+    // (uniform per CTA, and across the ranks, which all run the same configuration)
+    if (blockIdx.x != 0 || r.g_phase_dir == nullptr) return;
+    __shared__ float sb[2];
+    if (w < 2) {
+      const double* pb = r.part + (long long)r.clusters * kPartModes * r.Mp;
+      double t = 0.0;
+      for (int k = lane; k < r.clusters; k += 32) t += pb[2 * k + w];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (lane == 0) (w == 0 ? r.g_phase_dir : r.g_radial_dir)[r.W] = (float)t;
+      for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (lane == 0) sb[w] = (float)t;
+    }
+    __syncthreads();
+    if (w == 0) {
+      float v = lane < 2 ? sb[lane] : 0.0f;
+      if (xchg) v = warp_exchange(r.xchg, slot, v);
+      if (lane < 2) (lane == 0 ? r.g_phase_dir : r.g_radial_dir)[r.W] = v;
+    }
     return;
   }
+  // rows without a destination (directions in projection mode, norm weight outside a block)
+  if ((q >= 5 && q <= 8 && r.g_phase_dir == nullptr) || (q >= 9 && r.g_norm_w == nullptr)) return;
   const int m = blockIdx.x * 32 + lane;
   __shared__ double sm[kReduceWarps][32];
   double s8[kReduceUnroll];
@@ -440,23 +458,30 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
   for (int u = 0; u < kReduceUnroll; ++u) sw += s8[u];
   sm[w][lane] = sw;
   __syncthreads();
-  if (w == 0 && m < r.M) {
+  if (w != 0) return;
+  const bool ok = m < r.M;
+  float v = 0.0f;
+  if (ok) {
     double t = 0.0;
 #pragma unroll
     for (int i = 0; i < kReduceWarps; ++i) t += sm[i][lane];
-    switch (q) {
-      case 0: r.g_nu_log[m] = (float)t; r.g_energy[m] = 0.0f; break;
-      case 1: r.g_theta_log[m] = (float)(t * exp((double)r.theta_log[m])); break;
-      case 2: r.g_wlg[m] = (float)t; break;
-      case 3: r.g_wpr[m] = (float)t; break;
-      case 4: r.g_wrr[m] = (float)t; break;
-      case 5: if (r.g_phase_dir) r.g_phase_dir[m] = (float)t; break;
-      case 6: if (r.g_phase_dir) r.g_phase_dir[r.M + m] = (float)t; break;
-      case 7: if (r.g_radial_dir) r.g_radial_dir[m] = (float)t; break;
-      case 8: if (r.g_radial_dir) r.g_radial_dir[r.M + m] = (float)t; break;
-      case 9: if (r.g_norm_w) r.g_norm_w[m] = (float)t; break;
-      default: if (r.g_norm_w) r.g_norm_w[r.M + m] = (float)t; break;
-    }
+    v = q == 1 ? (float)(t * exp((double)r.theta_log[m])) : (float)t;
+  }
+  // N ranks: the whole warp exchanges its 32 values over peer memory; every rank gets the sum
+  if (xchg) v = warp_exchange(r.xchg, slot, v);
+  if (!ok) return;
+  switch (q) {
+    case 0: r.g_nu_log[m] = v; r.g_energy[m] = 0.0f; break;
+    case 1: r.g_theta_log[m] = v; break;
+    case 2: r.g_wlg[m] = v; break;
+    case 3: r.g_wpr[m] = v; break;
+    case 4: r.g_wrr[m] = v; break;
+    case 5: r.g_phase_dir[m] = v; break;
+    case 6: r.g_phase_dir[r.M + m] = v; break;
+    case 7: r.g_radial_dir[m] = v; break;
+    case 8: r.g_radial_dir[r.M + m] = v; break;
+    case 9: r.g_norm_w[m] = v; break;
+    default: r.g_norm_w[r.M + m] = v; break;
   }
 }
 
@@ -852,6 +877,10 @@ size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width,
 
 int sparc_mixer_controls_floats(void) { return (int)(sizeof(TokenCtl) / sizeof(float)); }
 
+size_t sparc_exchange_buffer_bytes(int world) {
+  return world >= 1 && world <= kXchgMaxRanks ? xchg_buffer_bytes(world) : 0;
+}
+
 int sparc_mixer_mask_words(int width) {
   if (width <= 0 || width % 2) return 0;
   return ((width / 2 + kFwdModes - 1) / kFwdModes) * 16;
@@ -970,6 +999,26 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   r.g_phase_dir = proj ? nullptr : a->grad_phase_direction;
   r.g_radial_dir = proj ? nullptr : a->grad_radial_direction;
   r.g_norm_w = block ? a->grad_norm_weight : nullptr;
+  r.xchg = PeerExchange{};
+  r.xchg.world = a->exchange_world > 1 ? a->exchange_world : 1;
+  if (r.xchg.world > 1) {
+    if (r.xchg.world > kXchgMaxRanks || a->exchange_rank < 0 || a->exchange_rank >= r.xchg.world ||
+        a->exchange_status == nullptr) {
+      set_err("exchange_world must be 2..8 with a rank in [0, world) and a status word");
+      return SPARC_ERR_ARG;
+    }
+    if ((long long)((pl.Mp + 31) / 32) * (kPartModes + 1) > kXchgSlots) {
+      set_err("width too large for the gradient exchange's slots");
+      return SPARC_ERR_SHAPE;
+    }
+    for (int i = 0; i < r.xchg.world; ++i) {
+      if (a->exchange_buffers[i] == nullptr) { set_err("null exchange buffer"); return SPARC_ERR_ARG; }
+      r.xchg.base[i] = static_cast<unsigned char*>(a->exchange_buffers[i]);
+    }
+    r.xchg.rank = a->exchange_rank;
+    r.xchg.status = a->exchange_status;
+    r.xchg.max_spin = 1u << 24;
+  }
   TimedLaunch tl(kTimeBwdReduce, s);
   return launch_error(launch_ex((const void*)mixer_reduce_kernel, dim3((pl.Mp + 31) / 32, kPartModes + 1),
                                dim3(32, kReduceWarps), 0, 0, s, r));

@@ -65,15 +65,6 @@ struct PeerParams {
   int skip_publish;                // failure test: do not publish (peers' waits run out)
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const __grid_constant__ PeerParams p) {
   pdl_wait();  // the gradients come from the previous kernels
   const int c = blockIdx.x, tid = threadIdx.x;

@@ -8,6 +8,10 @@ times the width per layer), so the exchange is latency-bound, not bandwidth-boun
   (`sparc_peer_allreduce`) reads the gradient tensors, pushes them into every rank's buffer over
   NVLink (CUDA IPC mappings), waits for the peers' pushes and writes the rank-ordered sum back:
   one launch per step, no packing copies, identical results on every rank.
+* FusedGradExchange (CUDA, up to 8 ranks): while active, the SPARC mixer / block backward itself
+  sums its parameter gradients over the ranks: the gradient reduction kernel exchanges its
+  results through NVLink peer memory before writing them (compute and collective in one kernel).
+  SPARCMixer, SPARCBlock and SPARCStack parameters then need no further all-reduce.
 * GradAllReduce (any backend; gloo on CPU): packs every gradient into one buffer, issues a
   single all-reduce on the current stream and unpacks it.
 """
@@ -74,23 +78,7 @@ class PeerGradAllReduce:
         device = self.params[0].device
         with torch.cuda.device(device):
             nbytes = L.sparc_peer_buffer_bytes(self.world, self.total)
-            handle = (ctypes.c_ubyte * 64)()
-            own = ctypes.c_void_p()
-            self._check(L.sparc_peer_buffer_alloc(nbytes, ctypes.byref(own), handle), "sparc_peer_buffer_alloc")
-            self._own = own.value
-            handles = [None] * self.world
-            dist.all_gather_object(handles, bytes(handle), group=group)
-            self._opened = []
-            self.buffers = []
-            for r, h in enumerate(handles):
-                if r == self.rank:
-                    self.buffers.append(self._own)
-                    continue
-                ptr = ctypes.c_void_p()
-                hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
-                self._check(L.sparc_peer_buffer_open(hb, ctypes.byref(ptr)), "sparc_peer_buffer_open")
-                self._opened.append(ptr.value)
-                self.buffers.append(ptr.value)
+            self._own, self._opened, self.buffers = _map_peer_buffers(L, nbytes, group, self._check)
             self.status = torch.zeros(1, dtype=torch.int32, device=device)
             torch.cuda.synchronize(device)
         dist.barrier(group=group)
@@ -139,6 +127,86 @@ class PeerGradAllReduce:
             return
         torch.cuda.synchronize(self.params[0].device)
         dist.barrier(group=self.group)  # no rank may still push into a buffer being freed
+        for ptr in self._opened:
+            self._L.sparc_peer_buffer_close(ctypes.c_void_p(ptr))
+        self._opened = []
+        dist.barrier(group=self.group)
+        self._L.sparc_peer_buffer_free(ctypes.c_void_p(self._own))
+        self._own = None
+
+
+def _map_peer_buffers(L, nbytes, group, check):
+    """Allocate this rank's zeroed buffer, exchange CUDA IPC handles over `group` and open the
+    others': (own pointer, [opened pointers], [every rank's pointer in rank order])."""
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    handle = (ctypes.c_ubyte * 64)()
+    own = ctypes.c_void_p()
+    check(L.sparc_peer_buffer_alloc(nbytes, ctypes.byref(own), handle), "sparc_peer_buffer_alloc")
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(handle), group=group)
+    opened, buffers = [], []
+    for r, h in enumerate(handles):
+        if r == rank:
+            buffers.append(own.value)
+            continue
+        ptr = ctypes.c_void_p()
+        check(L.sparc_peer_buffer_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(ptr)),
+              "sparc_peer_buffer_open")
+        opened.append(ptr.value)
+        buffers.append(ptr.value)
+    return own.value, opened, buffers
+
+
+_ACTIVE = {}
+
+
+def active_exchange(device):
+    """The FusedGradExchange active on `device`, or None."""
+    d = torch.device(device)
+    return _ACTIVE.get(d.index if d.index is not None else torch.cuda.current_device())
+
+
+class FusedGradExchange:
+    """Make the SPARC mixer / block backward on this rank's GPU return gradients already summed
+    over the process group (the reduction kernel's peer-memory exchange). Construction is
+    collective; `close()` (collective) deactivates it and releases the buffers. Every rank must
+    run the same sequence of backward passes while it is active."""
+
+    def __init__(self, group=None, device=None):
+        from . import _lib
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 2 <= self.world <= 8:
+            raise ValueError("FusedGradExchange needs 2..8 ranks of one node")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self._L = _lib.lib()
+        with torch.cuda.device(self.device):
+            nbytes = self._L.sparc_exchange_buffer_bytes(self.world)
+            self._own, self._opened, self.buffers = _map_peer_buffers(self._L, nbytes, group, self._check)
+            self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+        _ACTIVE[self.device.index] = self
+
+    def _check(self, rc, what):
+        from . import _lib
+
+        if rc != _lib.OK:
+            msg = self._L.sparc_peer_last_error()
+            raise RuntimeError(f"{what} failed ({_lib.ERR_NAMES.get(rc, rc)}): {msg.decode() if msg else ''}")
+
+    def timed_out(self) -> bool:
+        return bool(int(self.status.item()) & 16)
+
+    def close(self):
+        if self._own is None:
+            return
+        if _ACTIVE.get(self.device.index) is self:
+            del _ACTIVE[self.device.index]
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
         for ptr in self._opened:
             self._L.sparc_peer_buffer_close(ctypes.c_void_p(ptr))
         self._opened = []

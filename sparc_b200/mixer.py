@@ -31,6 +31,21 @@ def _f32(t: torch.Tensor) -> torch.Tensor:
     return t.detach().to(torch.float32).contiguous()
 
 
+def _exchange_fields(a, device):
+    """Fill the backward's fused cross-GPU gradient sum from the active exchange group of this
+    device (sparc_b200.ddp.FusedGradExchange), if any."""
+    from . import ddp
+
+    ex = ddp.active_exchange(device)
+    if ex is None:
+        return
+    for r, b in enumerate(ex.buffers):
+        a.exchange_buffers[r] = b
+    a.exchange_world = ex.world
+    a.exchange_rank = ex.rank
+    a.exchange_status = ex.status.data_ptr()
+
+
 class _SparcMixerFunction(torch.autograd.Function):
     """Autograd op around sparc_mixer_forward / sparc_mixer_backward.
 
@@ -116,7 +131,9 @@ class _SparcMixerFunction(torch.autograd.Function):
             _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
             carry.data_ptr(), controls.data_ptr(), _lib.ptr(nw), _lib.ptr(mask), _lib.ptr(gnw),
             *[g[n].data_ptr() for n in _PARAMS], None, 0,
-            ws.data_ptr(), ws.numel(), B, T, W, dt, ctx.max_spin)
+            workspace=ws.data_ptr(), workspace_bytes=ws.numel(), batch=B, length=T, width=W, dtype=dt,
+            max_spin=ctx.max_spin)
+        _exchange_fields(a, dev)
         _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_backward")
         return (dx, *[g[n] for n in _PARAMS],

@@ -108,7 +108,8 @@ def _core_backward(sv: _CoreSaved, dh, dlast_r, dlast_i):
         sv.carry.data_ptr(), sv.controls.data_ptr(), None, None, None,
         g[0].data_ptr(), g[1].data_ptr(), None, None, g[2].data_ptr(), g[5].data_ptr(),
         g[3].data_ptr(), g[4].data_ptr(), dp.data_ptr(), sv.lin,
-        ws.data_ptr(), ws.numel(), B, T, W, dt, sv.max_spin)
+        workspace=ws.data_ptr(), workspace_bytes=ws.numel(), batch=B, length=T, width=W, dtype=dt,
+        max_spin=sv.max_spin)
     _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
                "sparc_mixer_backward (projection mode)")
     return du, dp, g[:5], gh0

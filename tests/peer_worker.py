@@ -101,6 +101,46 @@ def main():
     out["timeout_seen"] = red2.timed_out()
     dist.barrier()
     red2.close()
+    # the fused exchange: the mixer / block backward returns gradients summed over the ranks
+    import sparc_b200
+    from sparc_b200.ddp import FusedGradExchange
+
+    torch.manual_seed(0)
+    mixer = sparc_b200.SPARCMixer(64).to(dev)
+    with torch.no_grad():
+        mixer.phase_direction.copy_(torch.randn(65) * 0.15)
+        mixer.radial_direction.copy_(torch.randn(65) * 0.15)
+    stack = sparc_b200.SPARCStack(64, 2).to(dev)
+    gx = torch.Generator().manual_seed(77 + rank)
+    x = torch.randn(2, 100, 64, generator=gx).to(dev)
+    gy = torch.randn(2, 100, 64, generator=gx).to(dev)
+    fworst, fident = 0.0, True
+    for model in (mixer, stack):
+        def run():
+            model.zero_grad(set_to_none=True)
+            y = model(x)
+            y = y[0] if isinstance(y, tuple) else y
+            y.backward(gy)
+            return [p.grad.clone() for p in model.parameters()]
+        ref = run()
+        for t in ref:
+            dist.all_reduce(t)
+        ex = FusedGradExchange()
+        for _ in range(3):  # several backward passes (epochs of the exchange slots)
+            got = run()
+        torch.cuda.synchronize()
+        out.setdefault("fused_status_ok", True)
+        out["fused_status_ok"] &= not ex.timed_out()
+        ex.close()
+        for r, g in zip(ref, got):
+            if r.abs().max() > 0:
+                fworst = max(fworst, float((g - r).double().norm() / r.double().norm()))
+        flat = torch.cat([g.reshape(-1) for g in got])
+        allf = [torch.empty_like(flat) for _ in range(world)]
+        dist.all_gather(allf, flat)
+        fident &= all(torch.equal(allf[0], f) for f in allf)
+    out["fused_rel_err"] = fworst
+    out["fused_identical"] = fident
     print("RESULT " + json.dumps(out), flush=True)
     dist.destroy_process_group()
 

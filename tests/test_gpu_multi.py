@@ -37,6 +37,8 @@ def test_peer_allreduce_multi_gpu():
         assert d["rel_err"] < 1e-6 and d["graph_rel_err"] < 1e-6, d
         assert d["identical"], d
         assert d["status_ok"], d
+        # the mixer / block backward with the fused exchange: the group's sums, on every rank alike
+        assert d["fused_rel_err"] < 1e-5 and d["fused_identical"] and d["fused_status_ok"], d
     # the rank that withheld its flags left the other's wait to run out
     assert any(d["timeout_seen"] for d in res), res
     print({d["rank"]: (round(d["peer_us"], 1), round(d["nccl_us"], 1)) for d in res})
