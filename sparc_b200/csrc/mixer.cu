@@ -202,14 +202,16 @@ struct TokenCoef2 {
   float2 num, gate, gain;
 };
 
-template <bool kFast>
+// kRotHw: the rotation from the hardware sin / cos of the whole angle (MUFU pipe), else from the
+// series of the bounded offset (FMA pipe); by default the fast path's choice.
+template <bool kFast, bool kRotHw = kFast>
 __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0,
                                                   float2 tau1, float2 keep) {
   TokenCoef2 k;
   k.z = mul2(mc.nu, E);
   k.rho = ex2_2(mul2(mc.nl2e_neg, E));
   const float2 rk = mul2(k.rho, keep);  // the transition's radius (0 at a reset)
-  if constexpr (kFast) {
+  if constexpr (kRotHw) {
     const float2 ph = sub2(add2(delta, mc.theta), mul2(k.rho, delta));  // theta + (1 - rho) delta
     float2 sn, cs;
     sincos_hw(ph.x, &sn.x, &cs.x);
@@ -239,9 +241,9 @@ __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E
 }
 
 // The same from a saved controls record.
-template <bool kFast>
+template <bool kFast, bool kRotHw = kFast>
 __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, const TokenCtl& c) {
-  return token_coef2<kFast>(mc, make_float2(c.ed.x, c.ed.y), make_float2(c.ed.z, c.ed.w),
+  return token_coef2<kFast, kRotHw>(mc, make_float2(c.ed.x, c.ed.y), make_float2(c.ed.z, c.ed.w),
                             make_float2(c.tau.x, c.tau.y), make_float2(c.tau.z, c.tau.w),
                             make_float2(c.keep.x, c.keep.y));
 }
@@ -296,6 +298,13 @@ __host__ __device__ constexpr int log2i() { return N <= 1 ? 0 : 1 + log2i<N / 2>
 // writing every chunk's v. No CTA waits on anything but the cluster barrier, and the composition
 // order is fixed, so the carries are bitwise reproducible.
 constexpr int kScanThreads = 256;
+// The forward tile kernels (summary, replay) are bound by the MUFU pipe: with
+// SPARC_FWD_HW_ROTATION 0 their bfloat16 instances rotate by the FMA-pipe series instead.
+#ifndef SPARC_FWD_HW_ROTATION
+#define SPARC_FWD_HW_ROTATION 1
+#endif
+constexpr bool kFwdHwRotation = SPARC_FWD_HW_ROTATION != 0;
+
 #ifndef SPARC_SCAN_Q
 #define SPARC_SCAN_Q 8
 #endif
