@@ -106,13 +106,18 @@ def mixer_kernel_bytes(B, T, W, s, chunk):
             "mixer_bwd_grad_kernel": 3 * act + ctl + 2 * car}
 
 
-def profile_traffic(kernel: str, workload: str):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, if there is one."""
+def profile_value(kernel: str, workload: str, key: str = "traffic_bytes_per_launch"):
+    """A per-launch figure of `kernel` (DRAM bytes, warp instructions) from the committed ncu
+    summary, if there is one."""
     path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
     if not os.path.exists(path):
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    m = re.search(key + r":\s*([0-9.eE+]+)", open(path).read())
     return float(m.group(1)) if m else None
+
+
+def profile_traffic(kernel: str, workload: str):
+    return profile_value(kernel, workload)
 
 
 class ClockSampler:
@@ -399,6 +404,16 @@ def run_layer(args, wl, world, rank, local):
                 "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": dom,
                 "peak_source": peak_kind, "kernels": kern,
                 "step_frac": round(5 * W * s * B * T / (ms / 1e3) / 1e9 / peak, 4)}
+    # the ceiling that binds these kernels: instruction issue (148 SMs x 4 schedulers x one
+    # warp-instruction per cycle), with the dominant kernel's instruction count from its ncu
+    # summary and the SM clock sampled under load
+    inst = profile_value(dom, f"layer_b{B}_t{T}_w{W}_{'fp32' if s == 4 else 'bf16'}", "warp_instructions_per_launch")
+    sm_mhz = (clocks.summary() or {}).get("sm_mhz")
+    if inst and sm_mhz and kern[dom]["ms"]:
+        issue_us = inst / (148 * 4) / (sm_mhz * 1e6) * 1e6
+        roofline["issue"] = {"kernel": dom, "warp_instructions": int(inst), "issue_bound_us": round(issue_us, 2),
+                             "measured_us": round(kern[dom]["ms"] * 1e3, 2),
+                             "frac": round(issue_us / (kern[dom]["ms"] * 1e3), 4), "sm_mhz": sm_mhz}
 
     # end to end through the public API: every step copies its x and g from pinned host memory
     # (on a copy stream, double-buffered, so that step i+1's copy overlaps step i's compute) and
