@@ -64,3 +64,23 @@ def proj_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, x=None
         msg = _lib.lib().sparc_proj_gemm_last_error()
         raise RuntimeError(f"sparc_proj_gemm failed ({_lib.ERR_NAMES.get(rc, rc)}): {msg.decode() if msg else ''}")
     return out
+
+
+def split3(t: torch.Tensor, role: str) -> torch.Tensor:
+    """A float32 operand as three bfloat16 terms along k for a float32-accurate product on the
+    bf16 tensor cores: t = hi + lo (hi = bf16(t), lo = bf16(t - hi), together 16 significand
+    bits); an A operand becomes [hi | hi | lo], a B operand [hi | lo | hi], so that one product
+    over 3k sums a_hi b_hi + a_hi b_lo + a_lo b_hi (the dropped a_lo b_lo is 2^-16 relative)."""
+    t = t.detach().float().contiguous()
+    hi = t.to(torch.bfloat16)
+    lo = (t - hi.float()).to(torch.bfloat16)
+    parts = (hi, hi, lo) if role == "a" else (hi, lo, hi)
+    return torch.cat(parts, dim=1).contiguous()
+
+
+def proj_gemm_f32(a: torch.Tensor, b: torch.Tensor, dp=None, c0=None, c1=None, b_split=None) -> torch.Tensor:
+    """float32 out[m, n] = sum_k a[m, k] b[n, k] (+ dp[m, 0] c0[n] + dp[m, 1] c1[n]) for float32
+    operands, through the three-term bf16 split (split3) in one tensor-core product; relative
+    error ~1e-5. `b_split` may pass a cached split3(b, "b")."""
+    return proj_gemm(split3(a, "a"), split3(b, "b") if b_split is None else b_split, torch.float32,
+                     dp=dp, c0=c0, c1=c1)

@@ -140,11 +140,13 @@ class _SparcCoreFunction(torch.autograd.Function):
 
 
 class _SequenceLayerTC(torch.autograd.Function):
-    """The whole layer for bfloat16 activations with the products on the tensor cores
-    (sparc_proj_gemm, tcgen05): u = x Wc and the readout with its fused skip in the forward;
-    dh = dy Ro and dx = du Wc^T + dp c^T + skip dy (one fused product) in the backward. The
-    weight gradients (x^T du, dy^T h) and the two controller projections stay torch products
-    (float32 for the projections, whose tanh sets every mode's controls)."""
+    """The whole layer with its activation products on the tensor cores (sparc_proj_gemm,
+    tcgen05): u = x Wc and the readout in the forward; dh = dy Ro and dx = du Wc^T + dp c^T +
+    skip dy in the backward. bfloat16 activations: bf16 operands, the skip and rank-2 terms fused
+    into the products' epilogues. float32 activations: each product through the three-term bf16
+    split (gemm.split3, relative error ~1e-5), the skip terms as torch adds. The weight gradients
+    (x^T du, dy^T h) and the two controller projections stay torch products (float32 for the
+    projections, whose tanh sets every mode's controls)."""
 
     @staticmethod
     def forward(ctx, x, content_real, content_imag, phase_controller, retention_controller, decay_log,
@@ -154,19 +156,26 @@ class _SequenceLayerTC(torch.autograd.Function):
 
         B, T, W = x.shape
         M = content_real.shape[1]
+        f32 = x.dtype == torch.float32
         xf = x.reshape(B * T, W)
-        wc = torch.cat((content_real, content_imag), dim=1).detach()               # [W, 2M]
-        ro = torch.cat((readout_real, -readout_imag), dim=1).detach()              # [W, 2M]
+        wc = torch.cat((content_real, content_imag), dim=1).detach().float()       # [W, 2M]
+        ro = torch.cat((readout_real, -readout_imag), dim=1).detach().float()      # [W, 2M]
         ctl = torch.stack((phase_controller, retention_controller), dim=1).detach().float()  # [W+1, 2]
-        u = gemm.proj_gemm(xf, wc.t().to(torch.bfloat16).contiguous()).view(B, T, 2 * M)
         p = torch.addmm(ctl[W], xf.float(), ctl[:W]).view(B, T, 2)
+        if f32:
+            u = gemm.proj_gemm_f32(xf, wc.t()).view(B, T, 2 * M)
+        else:
+            u = gemm.proj_gemm(xf, wc.t().to(torch.bfloat16).contiguous()).view(B, T, 2 * M)
         h0 = None if h0_r is None else (h0_r, h0_i)
         h, lr, li, sv = _core_forward(u, p, (decay_log, frequency_log, write_log_gain, write_phase_response,
                                              write_retention_response), h0, reset, lin, max_spin)
-        ro16 = ro.to(torch.bfloat16).contiguous()
-        y = gemm.proj_gemm(h.view(B * T, 2 * M), ro16, x=xf, skip=skip).view(B, T, W)
+        skipf = skip.detach().float()
+        if f32:
+            y = torch.addcmul(gemm.proj_gemm_f32(h.view(B * T, 2 * M), ro), skipf, xf).view(B, T, W)
+        else:
+            y = gemm.proj_gemm(h.view(B * T, 2 * M), ro.to(torch.bfloat16).contiguous(), x=xf, skip=skipf).view(B, T, W)
         ctx.sv = sv
-        ctx.save_for_backward(x, h, wc, ro16, ctl, skip.detach().float())
+        ctx.save_for_backward(x, h, wc, ro, ctl, skipf)
         ctx.set_materialize_grads(False)
         return y, lr, li
 
@@ -174,24 +183,36 @@ class _SequenceLayerTC(torch.autograd.Function):
     def backward(ctx, dy, dlast_r, dlast_i):
         from . import gemm
 
-        x, h, wc, ro16, ctl, skip = ctx.saved_tensors
+        x, h, wc, ro, ctl, skip = ctx.saved_tensors
         B, T, W = x.shape
         M2 = h.shape[-1]
+        f32 = x.dtype == torch.float32
         xf = x.reshape(B * T, W)
         hf = h.reshape(B * T, M2)
-        dyf = None if dy is None else dy.to(torch.bfloat16).reshape(B * T, W).contiguous()
-        dh = None if dyf is None else gemm.proj_gemm(dyf, ro16.t().contiguous()).view(B, T, M2)
+        dyf = None if dy is None else dy.to(x.dtype).reshape(B * T, W).contiguous()
+        if dyf is None:
+            dh = None
+        elif f32:
+            dh = gemm.proj_gemm_f32(dyf, ro.t()).view(B, T, M2)
+        else:
+            dh = gemm.proj_gemm(dyf, ro.t().to(torch.bfloat16).contiguous()).view(B, T, M2)
         du, dp, g, gh0 = _core_backward(ctx.sv, dh, dlast_r, dlast_i)
         ctx.sv = None
         du2 = du.view(B * T, M2)
         dp2 = dp.view(B * T, 2)
-        wc16 = wc.to(torch.bfloat16).contiguous()
+        c0, c1 = ctl[:W, 0].contiguous(), ctl[:W, 1].contiguous()
+        if f32:
+            dx = gemm.proj_gemm_f32(du2, wc, dp=dp2, c0=c0, c1=c1)
+            if dyf is not None:
+                dx = torch.addcmul(dx, skip, dyf)
+        elif dyf is not None:
+            dx = gemm.proj_gemm(du2, wc.to(torch.bfloat16).contiguous(), x=dyf, skip=skip, dp=dp2, c0=c0, c1=c1)
+        else:
+            dx = gemm.proj_gemm(du2, wc.to(torch.bfloat16).contiguous(), dp=dp2, c0=c0, c1=c1)
         if dyf is not None:
-            dx = gemm.proj_gemm(du2, wc16, x=dyf, skip=skip, dp=dp2, c0=ctl[:W, 0], c1=ctl[:W, 1])
             dro = (dyf.t() @ hf).float()                                           # [W, 2M]
             dskip = (dyf.float() * xf.float()).sum(0)
         else:
-            dx = gemm.proj_gemm(du2, wc16, dp=dp2, c0=ctl[:W, 0], c1=ctl[:W, 1])
             dro = torch.zeros((W, M2), dtype=torch.float32, device=x.device)
             dskip = torch.zeros(W, dtype=torch.float32, device=x.device)
         dwc = (xf.t() @ du2).float()                                               # [W, 2M]
@@ -234,14 +255,15 @@ def sparc_projection_states(x, params, content_activation: str = "tanh", state=N
 
 def sparc_sequence_layer(x, params, content_activation: str = "tanh", state=None, segment_pos=None,
                          reset_first: bool = False, max_spin: int = 0):
-    """Functional SPARCSequenceLayer: (y [B, T, W], (last_r, last_i)). For bfloat16 activations
-    (widths in whole 16-byte rows) the products run on the tensor cores (_SequenceLayerTC);
-    otherwise they are torch products around the same recurrence kernels."""
+    """Functional SPARCSequenceLayer: (y [B, T, W], (last_r, last_i)). When the widths are whole
+    16-byte rows of bf16 (W and 2M multiples of 8) the activation products run on the tensor
+    cores (_SequenceLayerTC; float32 through the three-term split); otherwise they are torch
+    products around the same recurrence kernels."""
     from . import gemm
 
     W = x.shape[-1]
     M = params["decay_log"].shape[0]
-    if x.dtype == torch.bfloat16 and gemm.supported(W, 2 * M):
+    if x.dtype in (torch.bfloat16, torch.float32) and gemm.supported(W, 2 * M):
         _lib.require_cuda(x, "x")
         lin = _check_activation(content_activation)
         h0_r, h0_i = (None, None) if state is None else state

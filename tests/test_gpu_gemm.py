@@ -46,3 +46,20 @@ def test_gemm_fused_terms():
     out = gemm.proj_gemm(a, b, torch.float32, x=x, skip=skip)
     assert _rel(out, a.float() @ b.float().t() + skip * x.float()) < 1e-5
     assert gemm.gemm_status("cuda") == 0
+
+
+@pytest.mark.parametrize("rows,n,k", [(300, 200, 520), (16384, 512, 512)])
+def test_gemm_f32_split(rows, n, k):
+    """float32 operands through the three-term bf16 split: ~1e-5 of a float64 product."""
+    from sparc_b200 import gemm
+
+    g = torch.Generator(device="cuda").manual_seed(rows + k)
+    a = torch.randn(rows, k, generator=g, device="cuda")
+    b = torch.randn(n, k, generator=g, device="cuda")
+    dp = torch.randn(rows, 2, generator=g, device="cuda")
+    c0 = torch.randn(n, generator=g, device="cuda")
+    c1 = torch.randn(n, generator=g, device="cuda")
+    ref = a.double() @ b.double().t() + dp[:, :1].double() * c0.double() + dp[:, 1:].double() * c1.double()
+    out = gemm.proj_gemm_f32(a, b, dp=dp, c0=c0, c1=c1)
+    assert _rel(out, ref) < 5e-5
+    assert gemm.gemm_status("cuda") == 0
