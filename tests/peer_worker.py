@@ -141,6 +141,10 @@ def main():
         fident &= all(torch.equal(allf[0], f) for f in allf)
     out["fused_rel_err"] = fworst
     out["fused_identical"] = fident
+    out_dir = os.environ.get("SPARC_PEER_RESULTS")
+    if out_dir:  # one file per rank (the ranks' stdout lines may interleave)
+        with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
+            json.dump(out, f)
     print("RESULT " + json.dumps(out), flush=True)
     dist.destroy_process_group()
 

@@ -22,16 +22,16 @@ def _free_port():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_peer_allreduce_multi_gpu():
+def test_peer_allreduce_multi_gpu(tmp_path):
     """One rank per visible GPU (2 to 8)."""
     n = min(torch.cuda.device_count(), 8)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT, SPARC_PEER_RESULTS=str(tmp_path))
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(ROOT, "tests", "peer_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    res = [json.loads(l.split("RESULT ", 1)[1]) for l in r.stdout.splitlines() if "RESULT " in l]
+    res = [json.load(open(os.path.join(tmp_path, f))) for f in sorted(os.listdir(tmp_path)) if f.endswith(".json")]
     assert len(res) == n, r.stdout[-2000:]
     for d in res:
         assert d["rel_err"] < 1e-6 and d["graph_rel_err"] < 1e-6, d
