@@ -114,17 +114,26 @@ struct TokenCoef {  // per-(token, mode) quantities shared by the forward and th
 // whole angle phi = theta + (1 - rho) delta, -expm1 from a shorter series, and the gate from the
 // hardware tanh (2 sigma(q) = 1 + tanh(q / 2)). Otherwise (float32) every factor is accurate to
 // a few ulp: series sin / cos of (1 - rho) delta rotate the precomputed e^{i theta}.
-template <bool kFast>
-__device__ __forceinline__ float2 transition_of(const ModeConst& mc, float rho, float delta) {
+// Rotation e^{i phi}, phi = theta + (1 - rho) delta, by kRot: 0 the series of the bounded offset
+// (1 - rho) delta (|.| <= pi/2) applied to the mode's e^{i theta}; 1 the hardware sin / cos of
+// the whole angle; 2 the hardware sin / cos of the offset (inside their accurate range) applied
+// to e^{i theta}.
+template <int kRot>
+__device__ __forceinline__ float2 transition_rot(const ModeConst& mc, float rho, float delta) {
   float s, c;
-  if constexpr (kFast) {
+  if constexpr (kRot == 1) {
     sincos_hw(fmaf(-rho, delta, delta) + mc.theta, &s, &c);
     return make_float2(rho * c, rho * s);
   } else {
-    sincos_halfpi(fmaf(-rho, delta, delta), &s, &c);  // (1 - rho) * delta, |.| <= pi/2
+    if constexpr (kRot == 2) sincos_hw(fmaf(-rho, delta, delta), &s, &c);
+    else sincos_halfpi(fmaf(-rho, delta, delta), &s, &c);
     const float rct = rho * mc.ct, rst = rho * mc.st;
     return make_float2(fmaf(rct, c, -rst * s), fmaf(rst, c, rct * s));
   }
+}
+template <bool kFast>
+__device__ __forceinline__ float2 transition_of(const ModeConst& mc, float rho, float delta) {
+  return transition_rot<kFast ? 1 : 0>(mc, rho, delta);
 }
 
 template <bool kFast>
@@ -202,16 +211,17 @@ struct TokenCoef2 {
   float2 num, gate, gain;
 };
 
-// kRotHw: the rotation from the hardware sin / cos of the whole angle (MUFU pipe), else from the
-// series of the bounded offset (FMA pipe); by default the fast path's choice.
-template <bool kFast, bool kRotHw = kFast>
+// kRot (see transition_rot): 1 the hardware sin / cos of the whole angle (MUFU pipe), 0 the
+// series of the bounded offset (FMA pipe), 2 the hardware sin / cos of the offset; by default
+// the fast path's choice (1 for bfloat16, 0 for float32).
+template <bool kFast, int kRot = kFast ? 1 : 0>
 __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0,
                                                   float2 tau1, float2 keep) {
   TokenCoef2 k;
   k.z = mul2(mc.nu, E);
   k.rho = ex2_2(mul2(mc.nl2e_neg, E));
   const float2 rk = mul2(k.rho, keep);  // the transition's radius (0 at a reset)
-  if constexpr (kRotHw) {
+  if constexpr (kRot == 1) {
     const float2 ph = sub2(add2(delta, mc.theta), mul2(k.rho, delta));  // theta + (1 - rho) delta
     float2 sn, cs;
     sincos_hw(ph.x, &sn.x, &cs.x);
@@ -219,7 +229,13 @@ __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E
     k.a = Cx2{mul2(rk, cs), mul2(rk, sn)};
   } else {
     float2 sn, cs;
-    sincos_halfpi2(sub2(delta, mul2(k.rho, delta)), &sn, &cs);  // (1 - rho) delta, |.| <= pi/2
+    const float2 off = sub2(delta, mul2(k.rho, delta));  // (1 - rho) delta, |.| <= pi/2
+    if constexpr (kRot == 2) {
+      sincos_hw(off.x, &sn.x, &cs.x);
+      sincos_hw(off.y, &sn.y, &cs.y);
+    } else {
+      sincos_halfpi2(off, &sn, &cs);
+    }
     const float2 rct = mul2(rk, mc.ct), rst = mul2(rk, mc.st);
     k.a = Cx2{sub2(mul2(rct, cs), mul2(rst, sn)), fma2(rst, cs, mul2(rct, sn))};
   }
@@ -241,17 +257,17 @@ __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E
 }
 
 // The same from a saved controls record.
-template <bool kFast, bool kRotHw = kFast>
+template <bool kFast, int kRot = kFast ? 1 : 0>
 __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, const TokenCtl& c) {
-  return token_coef2<kFast, kRotHw>(mc, make_float2(c.ed.x, c.ed.y), make_float2(c.ed.z, c.ed.w),
+  return token_coef2<kFast, kRot>(mc, make_float2(c.ed.x, c.ed.y), make_float2(c.ed.z, c.ed.w),
                             make_float2(c.tau.x, c.tau.y), make_float2(c.tau.z, c.tau.w),
                             make_float2(c.keep.x, c.keep.y));
 }
 
 // Transition a = rho e^{i(theta + (1-rho) delta)} alone (the reverse local pass needs no write).
-template <bool kFast>
+template <bool kFast, int kRot = kFast ? 1 : 0>
 __device__ __forceinline__ float2 token_transition(const ModeConst& mc, float E, float delta, float keep) {
-  const float2 a = transition_of<kFast>(mc, ex2_approx(-mc.nl2e * E), delta);
+  const float2 a = transition_rot<kRot>(mc, ex2_approx(-mc.nl2e * E), delta);
   return make_float2(a.x * keep, a.y * keep);
 }
 
@@ -298,12 +314,25 @@ __host__ __device__ constexpr int log2i() { return N <= 1 ? 0 : 1 + log2i<N / 2>
 // writing every chunk's v. No CTA waits on anything but the cluster barrier, and the composition
 // order is fixed, so the carries are bitwise reproducible.
 constexpr int kScanThreads = 256;
-// The forward tile kernels (summary, replay) are bound by the MUFU pipe: with
-// SPARC_FWD_HW_ROTATION 0 their bfloat16 instances rotate by the FMA-pipe series instead.
+// Rotation choice per kernel family and activation type (transition_rot): bfloat16 kernels use
+// the hardware sin / cos of the whole angle; the float32 forward the series of the bounded
+// offset (its outputs agree with the decode step's libm to ~1e-7); the float32 backward the
+// hardware sin / cos of the offset (absolute error ~5e-7, inside [-pi/2, pi/2], far below the
+// 1e-3 gradient tolerance; 4% faster gradient kernel). SPARC_F32_ROT_FWD / _BWD select 0 (series)
+// or 2 (hardware offset); SPARC_FWD_HW_ROTATION 0 makes the bfloat16 forward use the series.
 #ifndef SPARC_FWD_HW_ROTATION
 #define SPARC_FWD_HW_ROTATION 1
 #endif
-constexpr bool kFwdHwRotation = SPARC_FWD_HW_ROTATION != 0;
+#ifndef SPARC_F32_ROT_FWD
+#define SPARC_F32_ROT_FWD 0
+#endif
+#ifndef SPARC_F32_ROT_BWD
+#define SPARC_F32_ROT_BWD 2
+#endif
+template <bool kFast>
+__host__ __device__ constexpr int fwd_rot() { return kFast ? (SPARC_FWD_HW_ROTATION ? 1 : 0) : SPARC_F32_ROT_FWD; }
+template <bool kFast>
+__host__ __device__ constexpr int bwd_rot() { return kFast ? 1 : SPARC_F32_ROT_BWD; }
 
 #ifndef SPARC_SCAN_Q
 #define SPARC_SCAN_Q 8

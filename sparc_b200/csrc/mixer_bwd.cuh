@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
           }
           q.x += on_r ? gr : 0.0f;
           q.y += on_i ? gi : 0.0f;
-          const float2 a = token_transition<kFast>(mc, tc.ed.x, tc.ed.z, tc.keep.x);
+          const float2 a = token_transition<kFast, bwd_rot<kFast>()>(mc, tc.ed.x, tc.ed.z, tc.keep.x);
           q = make_float2(fmaf(a.x, q.x, a.y * q.y), fmaf(a.x, q.y, -a.y * q.x));
           P = cmul(a, P);
         }
@@ -233,7 +233,7 @@ __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& 
   const float2 delta = make_float2(tc.ed.z, tc.ed.w), tau0 = make_float2(tc.tau.x, tc.tau.y),
                tau1 = make_float2(tc.tau.z, tc.tau.w);
   // with a reset the transition (k.a) is zero, so every transition-gradient term below vanishes
-  const TokenCoef2 k = token_coef2<kFast>(mc, tc);
+  const TokenCoef2 k = token_coef2<kFast, bwd_rot<kFast>()>(mc, tc);
   const float2 gar = fma2(lam.re, pv.re, mul2(lam.im, pv.im));   // Re(lam conj(h_prev))
   const float2 gai = sub2(mul2(lam.im, pv.re), mul2(lam.re, pv.im));  // Im(lam conj(h_prev))
   const float2 pg = sub2(mul2(gai, k.a.re), mul2(gar, k.a.im));
@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
           if (kFull || t < nvalid) {
             float2 nr, ni;
             mixer_in(t, Pair<TIO>::load(&S.x[t][0][2 * tid]), Pair<TIO>::load(&S.x[t][1][2 * tid]), nr, ni);
-            const TokenCoef2 k = token_coef2<kFast>(mc, S.ctl[t]);
+            const TokenCoef2 k = token_coef2<kFast, bwd_rot<kFast>()>(mc, S.ctl[t]);
             h = cfma2(k.a, h, cx2(mul2(k.gain, content2<kFast, kMode>(nr, lin)), mul2(k.gain, content2<kFast, kMode>(ni, lin))));
             Pair<TIO>::store(&S.hr[t][2 * tid], h.re.x, h.re.y);
             Pair<TIO>::store(&S.hi[t][2 * tid], h.im.x, h.im.y);

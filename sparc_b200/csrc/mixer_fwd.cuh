@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
             xr = mul2(xr, mul2(rr, mc.wre));
             xi = mul2(xi, mul2(rr, mc.wim));
           }
-          const TokenCoef2 k = token_coef2<kFast, kFast && kFwdHwRotation>(mc, S.ctl[t]);
+          const TokenCoef2 k = token_coef2<kFast, fwd_rot<kFast>()>(mc, S.ctl[t]);
           Q = cfma2(k.a, Q, cx2(mul2(k.gain, content2<kFast, kMode>(xr, lin)), mul2(k.gain, content2<kFast, kMode>(xi, lin))));
           P = cmul2(k.a, P);
         }
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
         if (kFull || t < r.nvalid) {
           const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-          const TokenCoef2 k = token_coef2<kFast, kFast && kFwdHwRotation>(mc, ctl[t]);
+          const TokenCoef2 k = token_coef2<kFast, fwd_rot<kFast>()>(mc, ctl[t]);
           if constexpr (kBlock) {
             // mixer input x r w; block output x + relu(h); relu bits for the backward
             const float2 rr = make_float2(ctl[t].keep.z, ctl[t].keep.w);
