@@ -73,5 +73,39 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+TORCH_SRC = os.path.join(PKG, "csrc_torch", "torch_ops.cpp")
+TORCH_LIB = os.path.join(PKG, "libsparc_b200_torch.so")
+
+
+def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
+    """Build libsparc_b200_torch.so, the TORCH_LIBRARY registration of the C ABI
+    (torch.ops.sparc_b200.*), with PyTorch's extension builder into _build/torch_ops and copy it
+    in-tree. Its C-ABI symbols stay undefined: they resolve against libsparc_b200.so, which the
+    loader (sparc_b200.torch_ops) opens with global visibility first."""
+    deps = [TORCH_SRC, os.path.join(INCLUDE, "sparc_b200.h")]
+    if not force and os.path.exists(TORCH_LIB) and all(os.path.getmtime(d) <= os.path.getmtime(TORCH_LIB) for d in deps):
+        return TORCH_LIB
+    import ctypes
+
+    import torch.utils.cpp_extension as ce
+
+    # the extension builder loads what it built: the C ABI must be resolvable first
+    ctypes.CDLL(build(), mode=ctypes.RTLD_GLOBAL)
+    bdir = os.path.join(BUILD, "torch_ops")
+    os.makedirs(bdir, exist_ok=True)
+    path = ce.load(name="sparc_b200_torch_ops", sources=[TORCH_SRC], extra_include_paths=[INCLUDE],
+                   extra_cflags=["-O2"], build_directory=bdir, is_python_module=False, with_cuda=True,
+                   verbose=verbose)
+    built = os.path.join(bdir, "sparc_b200_torch_ops.so")
+    if isinstance(path, str) and os.path.exists(path):
+        built = path
+    tmp = TORCH_LIB + ".tmp"
+    shutil.copyfile(built, tmp)
+    os.replace(tmp, TORCH_LIB)
+    return TORCH_LIB
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose=True))
+    if "--torch" in sys.argv:
+        print(build_torch_ops(force="--force" in sys.argv, verbose=True))

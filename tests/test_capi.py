@@ -107,3 +107,17 @@ def test_module_api_matches_reference(golden):
     m.set_decode_backend("fused")
     m.prepare_inference()
     assert m._inference_fused
+
+
+def test_torch_operators_registered():
+    """The TORCH_LIBRARY registration exposes the C ABI as torch.ops.sparc_b200.* (schemas only:
+    no compute without a GPU)."""
+    from sparc_b200 import _build, torch_ops
+
+    _build.build_torch_ops()
+    ops = torch_ops.load()
+    names = {"mixer_forward", "mixer_backward", "decode_step", "real_scan_forward", "real_scan_backward"}
+    for n in names:
+        assert hasattr(ops, n), n
+    schema = str(ops.mixer_forward.default._schema)
+    assert "Tensor x" in schema and "Tensor write_radial_response" in schema
