@@ -1,5 +1,6 @@
 """The TORCH_LIBRARY operators (torch.ops.sparc_b200.*) give the same results as the module path
-over the same C ABI (same kernels: bitwise equal)."""
+over the same C ABI (same kernels: bitwise equal for the mixer and decode, to rounding for the
+real scan, whose lookback order can vary run to run)."""
 import pytest
 import torch
 
@@ -49,6 +50,7 @@ def test_real_scan_ops_match_module():
     out = sparc_b200.real_scan(a, b)
     out.backward(g)
     out2, carry, last = ops.real_scan_forward(a.detach(), b.detach())
-    assert torch.equal(out2, out.detach())
+    # (the real scan's decoupled lookback may compose its carries in another order run to run)
+    assert torch.allclose(out2, out.detach(), rtol=1e-6, atol=1e-6)
     ga, gb = ops.real_scan_backward(a.detach(), b.detach(), g, carry)
     assert torch.allclose(ga, a.grad, rtol=1e-6, atol=1e-6) and torch.allclose(gb, b.grad, rtol=1e-6, atol=1e-6)
