@@ -13,6 +13,11 @@
 //   the last CTA of every launch, so flags never need clearing between launches. Every wait
 //   is bounded; on timeout the kernel records an error bit in the launch status word and
 //   continues with a zero carry, so the launch still terminates.
+// * Packed f32x2 arithmetic (add/sub/mul/fma.rn.f32x2) and complex pairs on it.
+// * mbarrier, TMA tensor-map and 1-D bulk-copy wrappers (no multicast), programmatic dependent
+//   launch.
+// * warp_exchange: one warp's values summed over the ranks of a data-parallel group through
+//   NVLink peer memory (bounded waits).
 #pragma once
 
 #include <cuda.h>
@@ -45,11 +50,6 @@ template <> struct Io<__nv_bfloat16> {
 
 __device__ __forceinline__ float to_float(float v) { return v; }
 __device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
-template <typename T> __device__ __forceinline__ T from_float(float v);
-template <> __device__ __forceinline__ float from_float<float>(float v) { return v; }
-template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
-  return __float2bfloat16_rn(v);
-}
 
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -96,25 +96,6 @@ __device__ __forceinline__ float tanh_accurate(float x) {
   p = fmaf(p, x2, -3.3333333333333333e-1f);
   const float small = fmaf(p * x2, x, x);
   return ax < 0.5f ? small : copysignf(big, x);
-}
-
-template <bool kFast>
-__device__ __forceinline__ float tanh_t(float x) {
-  if constexpr (kFast) return tanh_hw(x);
-  else return tanh_accurate(x);
-}
-
-// -expm1(-u) = 1 - e^{-u} for u >= 0, given w = e^{-u}. Series below 1/4 (cancellation-free).
-__device__ __forceinline__ float one_minus_exp_neg(float u, float w) {
-  // u - u^2/2 + u^3/6 - u^4/24 + u^5/120 - u^6/720
-  float p = -1.3888888888888889e-3f;
-  p = fmaf(p, u, 8.3333333333333333e-3f);
-  p = fmaf(p, u, -4.1666666666666667e-2f);
-  p = fmaf(p, u, 1.6666666666666667e-1f);
-  p = fmaf(p, u, -0.5f);
-  p = fmaf(p, u, 1.0f);
-  const float small = p * u;
-  return u < 0.25f ? small : 1.0f - w;
 }
 
 // sin and cos of |x| <= pi/2 (Maclaurin series through x^13 / x^12).
@@ -266,6 +247,8 @@ __device__ __forceinline__ float2 tanh_t2(float2 x) {
   if constexpr (kFast) return tanh_hw2(x);
   else return tanh_accurate2(x);
 }
+// -expm1(-u) = 1 - e^{-u} for u >= 0, given w = e^{-u}, per lane: the series
+// u - u^2/2 + u^3/6 - u^4/24 + u^5/120 - u^6/720 below 1/4 (cancellation-free), else 1 - w.
 __device__ __forceinline__ float2 one_minus_exp_neg2(float2 u, float2 w) {
   float2 p = bcast2(-1.3888888888888889e-3f);
   p = fma2(p, u, bcast2(8.3333333333333333e-3f));
@@ -370,14 +353,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
           smem_addr(dst)),
       "l"(reinterpret_cast<unsigned long long>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
       : "memory");
-}
-
-// Cluster barrier split into arrive (release) and wait (acquire), for every thread of every CTA.
-__device__ __forceinline__ void cluster_arrive() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- peer exchange (N GPUs)

@@ -104,16 +104,6 @@ __device__ __forceinline__ ModeConst load_mode(const MixerParamPtrs& pp, int m, 
   return mc;
 }
 
-struct TokenCoef {  // per-(token, mode) quantities shared by the forward and the backward
-  float z, rho;
-  float2 a;
-  float num, gate, gain;
-};
-
-// kFast (bfloat16 activations): the rotation e^{i phi} comes from the hardware sin / cos of the
-// whole angle phi = theta + (1 - rho) delta, -expm1 from a shorter series, and the gate from the
-// hardware tanh (2 sigma(q) = 1 + tanh(q / 2)). Otherwise (float32) every factor is accurate to
-// a few ulp: series sin / cos of (1 - rho) delta rotate the precomputed e^{i theta}.
 // Rotation e^{i phi}, phi = theta + (1 - rho) delta, by kRot: 0 the series of the bounded offset
 // (1 - rho) delta (|.| <= pi/2) applied to the mode's e^{i theta}; 1 the hardware sin / cos of
 // the whole angle; 2 the hardware sin / cos of the offset (inside their accurate range) applied
@@ -131,36 +121,13 @@ __device__ __forceinline__ float2 transition_rot(const ModeConst& mc, float rho,
     return make_float2(fmaf(rct, c, -rst * s), fmaf(rst, c, rct * s));
   }
 }
-template <bool kFast>
-__device__ __forceinline__ float2 transition_of(const ModeConst& mc, float rho, float delta) {
-  return transition_rot<kFast ? 1 : 0>(mc, rho, delta);
-}
 
-template <bool kFast>
-__device__ __forceinline__ TokenCoef token_coef(const ModeConst& mc, float E, float delta,
-                                                float tau0, float tau1) {
-  TokenCoef k;
-  k.z = mc.nu * E;
-  k.rho = ex2_approx(-mc.nl2e * E);
-  k.a = transition_of<kFast>(mc, k.rho, delta);
-  const float q = fmaf(tau0, mc.wpr, tau1 * mc.wrr);
-  if constexpr (kFast) {
-    // -expm1(-2z): u - u^2/2 + u^3/6 - u^4/24 below 1/4 (truncation below 1e-4 relative)
-    const float u = 2.0f * k.z;
-    const float ser = u * fmaf(fmaf(fmaf(-4.1666666666666667e-2f, u, 1.6666666666666667e-1f), u, -0.5f), u, 1.0f);
-    k.num = u < 0.25f ? ser : fmaf(-k.rho, k.rho, 1.0f);
-    k.gate = 1.0f + tanh_hw(0.5f * q);
-  } else {
-    k.num = one_minus_exp_neg(2.0f * k.z, k.rho * k.rho);
-    k.gate = 2.0f * rcp_approx(1.0f + ex2_approx(-kLog2e * q));
-  }
-  k.gain = mc.gconst * sqrt_approx(k.num) * k.gate;
-  return k;
-}
-
-// Two modes at once (the lanes are the thread's modes m and m+1): the arithmetic of token_coef
-// with the float operations packed into f32x2 instructions; the hardware approximations stay per
-// lane. The token's controls come as pairs (E, E), (delta, delta), (tau0, tau0), (tau1, tau1).
+// The per-(token, mode) coefficients, two modes at once (the lanes are the thread's modes m and
+// m+1), with the float operations packed into f32x2 instructions; the hardware approximations
+// stay per lane. The token's controls come as pairs (E, E), (delta, delta), (tau0, tau0),
+// (tau1, tau1). kFast (bfloat16 activations): -expm1 from a shorter series and the gate from
+// the hardware tanh (2 sigma(q) = 1 + tanh(q / 2)); otherwise (float32) every factor is accurate
+// to a few ulp. The rotation follows kRot (transition_rot).
 struct ModeConst2 {
   float2 nu, nl2e_neg, theta, ct, st, gconst, stat, wpr, wrr;
   float2 wpr_h, wrr_l;  // wpr * 2/pi, wrr / ln 16 (the gate's chain factors in the backward)
