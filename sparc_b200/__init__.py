@@ -18,7 +18,10 @@ def library_path() -> str:
 
 
 def check_status(clear: bool = True) -> None:
-    """Raise if any kernel launch on a cached workspace recorded a lookback timeout.
+    """Raise if any kernel launch on a cached workspace recorded a bounded wait that ran out (a
+    tile kernel's wait on its TMA copies, or the real scan's lookback). The tensor-core product
+    and the multi-GPU exchanges keep their own status words (gemm.gemm_status, the reducers'
+    timed_out()).
 
     Synchronises the streams that own the workspaces."""
     for ws in _lib.WORKSPACES.all():
@@ -26,7 +29,7 @@ def check_status(clear: bool = True) -> None:
         if st:
             if clear:
                 _lib.clear_status(ws)
-            raise RuntimeError(f"sparc_b200: a chunk-carry wait timed out (status {st:#x})")
+            raise RuntimeError(f"sparc_b200: a bounded wait in a kernel timed out (status {st:#x})")
 
 
 __all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack", "sparc_decode_step",
