@@ -285,12 +285,25 @@ def _dist():
     return world, rank, local
 
 
-def _time_steps(step_fn, steps, flush, world, device):
+def _time_steps(step_fn, steps, flush, world, device, soak_s=0.3):
     """Per-step CUDA event times (ms) of `step_fn`, L2 flushed before each step; max over
-    ranks of the summed time."""
+    ranks of the summed time. Untimed steps for about `soak_s` seconds come first (the same
+    count on every rank), so that the clock sampler around this call sees the GPU under load."""
     import torch
     import torch.distributed as dist
 
+    if soak_s > 0:
+        torch.cuda.synchronize(device)
+        t0 = time.time()
+        flush()
+        step_fn()
+        torch.cuda.synchronize(device)
+        n = torch.tensor([int(min(4000, soak_s / max(time.time() - t0, 1e-5)))], device=device)
+        if world > 1:
+            dist.all_reduce(n, op=dist.ReduceOp.MAX)
+        for _ in range(int(n.item())):
+            flush()
+            step_fn()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     if world > 1:
