@@ -18,6 +18,7 @@
 //   launch.
 // * warp_exchange: one warp's values summed over the ranks of a data-parallel group through
 //   NVLink peer memory (bounded waits).
+// * fail(): the host-side error report of the mixer, decode and real-scan entry points.
 #pragma once
 
 #include <cuda.h>
@@ -26,6 +27,10 @@
 #include <stdint.h>
 
 namespace sparc {
+
+// Host: records `msg` as the thread-local message sparc_last_error() returns and returns
+// `code` (defined in mixer.cu).
+int fail(int code, const char* msg);
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn16 = 2.772588722239781f;

@@ -136,16 +136,19 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodePara
 using namespace sparc;
 
 extern "C" int sparc_decode_step(const SparcDecodeArgs* a, void* stream) {
-  if (a == nullptr || !a->x || !a->y || !a->state_r || !a->state_i || !a->new_state_r ||
-      !a->new_state_i || !a->nu_log || !a->theta_log || !a->phase_direction ||
-      !a->radial_direction || !a->write_log_gain || !a->write_phase_response ||
-      !a->write_radial_response) {
-    return SPARC_ERR_ARG;
+  if (a == nullptr) return fail(SPARC_ERR_ARG, "null args");
+  if (!a->x || !a->y || !a->state_r || !a->state_i || !a->new_state_r || !a->new_state_i || !a->nu_log ||
+      !a->theta_log || !a->phase_direction || !a->radial_direction || !a->write_log_gain ||
+      !a->write_phase_response || !a->write_radial_response) {
+    return fail(SPARC_ERR_ARG, "null tensor pointer");
   }
-  if (a->batch <= 0 || a->width <= 0 || (a->width % 2) != 0 || a->batch > 0x7fffffffLL) return SPARC_ERR_SHAPE;
-  if (a->width / 2 > kDecodeThreads * kDecodeModes) return SPARC_ERR_SHAPE;
-  if (a->new_state_r == a->state_r || a->new_state_i == a->state_i) return SPARC_ERR_ARG;
-  if (a->dtype != SPARC_DTYPE_BF16 && a->dtype != SPARC_DTYPE_F32) return SPARC_ERR_DTYPE;
+  if (a->batch <= 0 || a->width <= 0 || a->batch > 0x7fffffffLL)
+    return fail(SPARC_ERR_SHAPE, "batch and width must be positive");
+  if (a->width % 2) return fail(SPARC_ERR_SHAPE, "SPARC rnn_width must be even");
+  if (a->width / 2 > kDecodeThreads * kDecodeModes) return fail(SPARC_ERR_SHAPE, "width above the decode kernel's limit");
+  if (a->new_state_r == a->state_r || a->new_state_i == a->state_i)
+    return fail(SPARC_ERR_ARG, "the new state must not alias the old one");
+  if (a->dtype != SPARC_DTYPE_BF16 && a->dtype != SPARC_DTYPE_F32) return fail(SPARC_ERR_DTYPE, "unsupported dtype");
   DecodeParams p{a->x, a->y, a->state_r, a->state_i, a->new_state_r, a->new_state_i,
                  a->nu_log, a->theta_log, a->phase_direction, a->radial_direction,
                  a->write_log_gain, a->write_phase_response, a->write_radial_response,
@@ -163,5 +166,6 @@ extern "C" int sparc_decode_step(const SparcDecodeArgs* a, void* stream) {
   cfg.numAttrs = 1;
   void* args[] = {&p};
   const void* k = a->dtype == SPARC_DTYPE_BF16 ? (const void*)decode_kernel<__nv_bfloat16> : (const void*)decode_kernel<float>;
-  return cudaLaunchKernelExC(&cfg, k, args) == cudaSuccess ? SPARC_OK : SPARC_ERR_LAUNCH;
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, k, args);
+  return e == cudaSuccess ? SPARC_OK : fail(SPARC_ERR_LAUNCH, cudaGetErrorString(e));
 }

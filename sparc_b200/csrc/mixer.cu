@@ -506,6 +506,11 @@ struct Plan {
 static thread_local char g_err[512];
 static void set_err(const char* msg) { snprintf(g_err, sizeof(g_err), "%s", msg); }
 
+int fail(int code, const char* msg) {
+  set_err(msg);
+  return code;
+}
+
 static bool set_smem(const void* kernel, size_t dyn) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
     cudaGetLastError();

@@ -392,15 +392,15 @@ static int resident_blocks(K kernel) {
 }
 
 static int real_plan(long long B, long long T, long long D, int dtype, RealPlan* pl) {
-  if (B <= 0 || T <= 0 || D <= 0) return SPARC_ERR_SHAPE;
-  if (dtype != SPARC_DTYPE_F32 && dtype != SPARC_DTYPE_BF16) return SPARC_ERR_DTYPE;
+  if (B <= 0 || T <= 0 || D <= 0) return fail(SPARC_ERR_SHAPE, "batch, length and channels must be positive");
+  if (dtype != SPARC_DTYPE_F32 && dtype != SPARC_DTYPE_BF16) return fail(SPARC_ERR_DTYPE, "unsupported dtype");
   pl->V = (dtype == SPARC_DTYPE_BF16 && D % 2 == 0) ? 2 : 1;
   const long long per_cta = (long long)kRealThreads * pl->V;
   pl->nDB = (int)((D + per_cta - 1) / per_cta);
   pl->Dp = (int)(pl->nDB * per_cta);
   pl->chunks = (int)((T + kRealChunk - 1) / kRealChunk);
   pl->tiles = B * pl->chunks * (long long)pl->nDB;
-  if (pl->tiles >= (1LL << 31)) return SPARC_ERR_SHAPE;
+  if (pl->tiles >= (1LL << 31)) return fail(SPARC_ERR_SHAPE, "too many tiles");
   int gf, gb;
   if (dtype == SPARC_DTYPE_F32) {
     gf = resident_blocks(real_fwd_kernel<float, 1>);
@@ -412,7 +412,7 @@ static int real_plan(long long B, long long T, long long D, int dtype, RealPlan*
     gf = resident_blocks(real_fwd_kernel<__nv_bfloat16, 1>);
     gb = resident_blocks(real_bwd_kernel<__nv_bfloat16, 1>);
   }
-  if (gf <= 0 || gb <= 0) return SPARC_ERR_LAUNCH;
+  if (gf <= 0 || gb <= 0) return fail(SPARC_ERR_LAUNCH, "occupancy query failed");
   pl->grid_fwd = (int)std::min<long long>(gf, pl->tiles);
   pl->grid_bwd = (int)std::min<long long>(gb, pl->tiles);
   return SPARC_OK;
@@ -451,12 +451,13 @@ size_t sparc_real_workspace_bytes(long long batch, long long length, long long c
 }
 
 int sparc_real_scan_forward(const SparcRealFwdArgs* a, void* stream) {
-  if (a == nullptr || !a->a || !a->b || !a->out || !a->carry) return SPARC_ERR_ARG;
+  if (a == nullptr) return fail(SPARC_ERR_ARG, "null args");
+  if (!a->a || !a->b || !a->out || !a->carry) return fail(SPARC_ERR_ARG, "null tensor pointer");
   RealPlan pl;
   int rc = real_plan(a->batch, a->length, a->channels, a->dtype, &pl);
   if (rc != SPARC_OK) return rc;
   const RealWs L = real_ws(pl);
-  if (a->workspace == nullptr || a->workspace_bytes < L.total) return SPARC_ERR_WORKSPACE;
+  if (a->workspace == nullptr || a->workspace_bytes < L.total) return fail(SPARC_ERR_WORKSPACE, "workspace too small");
   char* ws = static_cast<char*>(a->workspace);
   RealParams p{};
   p.a = a->a;
@@ -482,17 +483,19 @@ int sparc_real_scan_forward(const SparcRealFwdArgs* a, void* stream) {
   if (a->dtype == SPARC_DTYPE_F32) real_fwd_kernel<float, 1><<<pl.grid_fwd, kRealThreads, 0, s>>>(p);
   else if (pl.V == 2) real_fwd_kernel<__nv_bfloat16, 2><<<pl.grid_fwd, kRealThreads, 0, s>>>(p);
   else real_fwd_kernel<__nv_bfloat16, 1><<<pl.grid_fwd, kRealThreads, 0, s>>>(p);
-  return cudaGetLastError() == cudaSuccess ? SPARC_OK : SPARC_ERR_LAUNCH;
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SPARC_OK : fail(SPARC_ERR_LAUNCH, cudaGetErrorString(e));
 }
 
 int sparc_real_scan_backward(const SparcRealBwdArgs* a, void* stream) {
-  if (a == nullptr || !a->a || !a->b || !a->grad_out || !a->carry || !a->grad_a || !a->grad_b)
-    return SPARC_ERR_ARG;
+  if (a == nullptr) return fail(SPARC_ERR_ARG, "null args");
+  if (!a->a || !a->b || !a->grad_out || !a->carry || !a->grad_a || !a->grad_b)
+    return fail(SPARC_ERR_ARG, "null tensor pointer");
   RealPlan pl;
   int rc = real_plan(a->batch, a->length, a->channels, a->dtype, &pl);
   if (rc != SPARC_OK) return rc;
   const RealWs L = real_ws(pl);
-  if (a->workspace == nullptr || a->workspace_bytes < L.total) return SPARC_ERR_WORKSPACE;
+  if (a->workspace == nullptr || a->workspace_bytes < L.total) return fail(SPARC_ERR_WORKSPACE, "workspace too small");
   char* ws = static_cast<char*>(a->workspace);
   RealParams p{};
   p.a = a->a;
@@ -519,7 +522,8 @@ int sparc_real_scan_backward(const SparcRealBwdArgs* a, void* stream) {
   if (a->dtype == SPARC_DTYPE_F32) real_bwd_kernel<float, 1><<<pl.grid_bwd, kRealThreads, 0, s>>>(p);
   else if (pl.V == 2) real_bwd_kernel<__nv_bfloat16, 2><<<pl.grid_bwd, kRealThreads, 0, s>>>(p);
   else real_bwd_kernel<__nv_bfloat16, 1><<<pl.grid_bwd, kRealThreads, 0, s>>>(p);
-  return cudaGetLastError() == cudaSuccess ? SPARC_OK : SPARC_ERR_LAUNCH;
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SPARC_OK : fail(SPARC_ERR_LAUNCH, cudaGetErrorString(e));
 }
 
 }  // extern "C"

@@ -37,11 +37,12 @@ def proj_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, x=None
 
     a [rows, k], b [n, k] bfloat16 (contiguous); float32 accumulation; out bfloat16 or float32.
     No autograd: the callers compose the products of the forward and backward themselves."""
-    _lib.require_cuda(a, "a")
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
         raise TypeError("proj_gemm takes bfloat16 operands")
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
         raise ValueError("proj_gemm expects a [rows, k] and b [n, k]")
+    _lib.require_cuda(a, "a")
+    _lib.require_cuda(b, "b")
     a = a.contiguous()
     b = b.contiguous()
     rows, k = a.shape

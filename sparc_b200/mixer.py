@@ -168,9 +168,9 @@ def sparc_block(x, params, norm_weight, eps: float = 1e-6, state=None, segment_p
                 reset_first: bool = False, max_spin: int = 0):
     """One block of the config-5 stack in the mixer's own kernels: (x + mixer(RMSNorm(x)),
     (last_r, last_i)), RMSNorm(x) = x * (mean(x^2) + eps)^(-1/2) * norm_weight per token."""
-    _lib.require_cuda(x, "x")
     if norm_weight.shape != (x.shape[-1],):
         raise ValueError("norm_weight must have shape [width]")
+    _lib.require_cuda(x, "x")
     h0_r, h0_i = (None, None) if state is None else state
     reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
     y, lr, li = _SparcMixerFunction.apply(
@@ -182,19 +182,19 @@ def sparc_block(x, params, norm_weight, eps: float = 1e-6, state=None, segment_p
 @torch.no_grad()
 def sparc_decode_step(x: torch.Tensor, params, state):
     """One fused decode step: (y [B, W] x.dtype, (new_r, new_i) [B, M] float32)."""
-    _lib.require_cuda(x, "x")
-    L = _lib.lib()
     if x.dim() != 2:
         raise ValueError("decode expects x of shape [batch, width]")
-    x = x.contiguous()
     B, W = x.shape
     if W % 2:
         raise ValueError("SPARC rnn_width must be even")
     M = W // 2
+    if tuple(state[0].shape) != (B, M) or tuple(state[1].shape) != (B, M):
+        raise ValueError("decode state must be a pair of [batch, width/2] tensors")
+    _lib.require_cuda(x, "x")
+    L = _lib.lib()
+    x = x.contiguous()
     dt = _lib.dtype_code(x.dtype)
     sr, si = _f32(state[0]), _f32(state[1])
-    if sr.shape != (B, M) or si.shape != (B, M):
-        raise ValueError("decode state must be a pair of [batch, width/2] tensors")
     p = [_f32(params[n]) for n in ("nu_log", "theta_log", "phase_direction", "radial_direction",
                                     "write_log_gain", "write_phase_response", "write_radial_response")]
     y = torch.empty_like(x)
@@ -243,7 +243,6 @@ class SPARCMixer(nn.Module):
 
     def forward(self, x: torch.Tensor, return_cache: bool = False, state=None, segment_pos=None,
                 reset_first: bool = False):
-        _lib.require_cuda(x, "x")
         if x.dim() != 3 or x.shape[-1] != self.width:
             raise ValueError(f"SPARCMixer expects x of shape [batch, length, {self.width}]")
         if x.dtype not in (torch.float32, torch.bfloat16):
@@ -252,6 +251,7 @@ class SPARCMixer(nn.Module):
             B = x.shape[0]
             if state[0].shape != (B, self.modes) or state[1].shape != (B, self.modes):
                 raise ValueError("initial SPARC states must have shape [B, M]")
+        _lib.require_cuda(x, "x")
         y, cache = sparc_mixer(x.contiguous(), self._params(), state, self.max_spin,
                                segment_pos=segment_pos, reset_first=reset_first)
         return y, (cache if return_cache else None)

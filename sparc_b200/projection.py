@@ -236,10 +236,10 @@ def sparc_projection_states(x, params, content_activation: str = "tanh", state=N
     (last_r, last_i) [B, M] float32) for x [B, T, W] and a mapping holding the JAX layer's
     recurrent parameters (content_real/imag [W, M], the two controllers [W+1], the five modal
     vectors [M])."""
-    _lib.require_cuda(x, "x")
     lin = _check_activation(content_activation)
     if x.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"supported activations are float32 and bfloat16, got {x.dtype}")
+    _lib.require_cuda(x, "x")
     W = x.shape[-1]
     M = params["decay_log"].shape[0]
     wc = torch.cat((params["content_real"], params["content_imag"]), dim=1)  # [W, 2M]
@@ -264,8 +264,8 @@ def sparc_sequence_layer(x, params, content_activation: str = "tanh", state=None
     W = x.shape[-1]
     M = params["decay_log"].shape[0]
     if x.dtype in (torch.bfloat16, torch.float32) and gemm.supported(W, 2 * M):
-        _lib.require_cuda(x, "x")
         lin = _check_activation(content_activation)
+        _lib.require_cuda(x, "x")
         h0_r, h0_i = (None, None) if state is None else state
         reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
         y, lr, li = _SequenceLayerTC.apply(

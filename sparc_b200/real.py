@@ -14,9 +14,12 @@ import torch
 from . import _lib
 
 
-def _check(a, b, what):
+def _check(a, b, what, chunk_size=None):
+    """Shape checks first (ValueError, as the reference's), then the device (no CPU path)."""
     if a.shape != b.shape or a.ndim != 3:
         raise ValueError(f"{what} expects matching [B, L, D] tensors")
+    if chunk_size is not None and (chunk_size not in (16, 32, 64, 128) or a.shape[1] % chunk_size):
+        raise ValueError("chunk size must be 16, 32, 64 or 128 and divide length")
     _lib.require_cuda(a, "a")
     _lib.require_cuda(b, "b")
 
@@ -76,9 +79,7 @@ def real_scan(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 
 def real_chunk_scan(a: torch.Tensor, b: torch.Tensor, chunk_size: int = 16) -> torch.Tensor:
     """Differentiable chunked real scan (backward/scan.py:825-884, 1647-1650)."""
-    _check(a, b, "real chunk scan")
-    if chunk_size not in (16, 32, 64, 128) or a.shape[1] % chunk_size:
-        raise ValueError("chunk size must be 16, 32, 64 or 128 and divide length")
+    _check(a, b, "real chunk scan", chunk_size)
     return _RealScanFunction.apply(a, b)
 
 

@@ -115,17 +115,17 @@ def rtrl_step(params, carry, inputs: torch.Tensor, reset=None, content_activatio
     """stored_rtrl_step (rtrl.py:204-209): ((next_state, next_traces), state) for a mapping of the
     nine recurrent parameters. next_state is the state with its gradient path (the traces give
     the parameters' gradients); the returned carry is detached."""
-    _lib.require_cuda(inputs, "inputs")
     if content_activation not in ("tanh", "linear"):
         raise ValueError(content_activation)
     state, traces = carry
-    x = inputs.float()
-    if x.dim() != 2:
+    if inputs.dim() != 2:
         raise ValueError("inputs must have shape [batch, input_size]")
-    B, W = x.shape
+    B, W = inputs.shape
     M = params["decay_log"].shape[0]
     if state.shape != (B, M):
         raise ValueError(f"state must have shape {(B, M)}")
+    _lib.require_cuda(inputs, "inputs")
+    x = inputs.float()
     wc = torch.cat((params["content_real"], params["content_imag"]), dim=1).detach().float()
     ctl = torch.stack((params["phase_controller"], params["retention_controller"]), dim=1).detach().float()
     u = x @ wc
