@@ -754,6 +754,19 @@ def run_rtrl(args, wl, world, rank, local):
 
 
 # ----------------------------------------------------------------------------- reference arm
+_PER_GPU_BATCH = ("layer", "layer5", "real", "decode", "projection", "projection16", "rtrl")
+
+
+def workload_config(workload: str, wl: dict, world: int) -> dict:
+    """The workload part of the JSON line's `config`, the same for both arms: the batch is the
+    job's global batch (per-GPU batch x ranks for the data-parallel workloads)."""
+    cfg = {"workload": wl["workload"], "baseline_config": wl["config_index"]}
+    for k in ("batch", "seq_len", "width", "modes", "channels", "layers", "steps"):
+        if k in wl:
+            cfg["global_batch" if k == "batch" else k] = wl[k] * (world if k == "batch" and workload in _PER_GPU_BATCH else 1)
+    return cfg
+
+
 def run_reference(args, wl):
     """The reference algorithm on the host cores: the float64 oracle restatement, one batch row
     per process over all host cores; each step is one round over min(cores, batch) rows."""
@@ -805,8 +818,7 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
                 "data": "synthetic", "impl": "reference",
-                "config": {"workload": wl["workload"], "global_batch": wl["batch"], "seq_len": wl["seq_len"],
-                           "width": wl["width"], "parallelism": "host cores"},
+                "config": {**workload_config(args.workload, wl, world), "parallelism": "host cores"},
                 "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
                                  "sample": f"{toks} tokens per step: {cores} batch rows of T={wl['seq_len']}, "
                                            f"W={wl['width']}, float64 numpy oracle fwd+bwd, one row per process"},
@@ -822,8 +834,8 @@ def main():
     r = runner(args, wl, world, rank, local)
     if rank == 0:
         unit = "tokens/s"
-        cfg = {"workload": wl["workload"], "baseline_config": wl["config_index"],
-               "parallelism": f"dp{world}" if world > 1 else "single"}
+        cfg = workload_config(args.workload, wl, world)
+        cfg["parallelism"] = f"dp{world}" if world > 1 else "single"
         if world > 1:
             cfg["gradient_exchange"] = {
                 "fused": "in the gradient reduction kernel over NVLink peer memory (CUDA IPC)",
@@ -831,10 +843,7 @@ def main():
                 "nccl": "NCCL all-reduce of the packed gradients"}[
                     args.allreduce if args.allreduce != "fused" or args.workload in ("layer", "layer5", "stack") else "peer"]
         if "chunk" in r:
-            wl["chunk"] = r["chunk"]
-        for k in ("batch", "seq_len", "width", "modes", "channels", "layers", "steps", "chunk"):
-            if k in wl:
-                cfg["global_batch" if k == "batch" else k] = wl[k] * (world if k == "batch" and args.workload in ("layer", "layer5", "real", "decode", "projection", "projection16", "rtrl") else 1)
+            cfg["chunk"] = r["chunk"]
         cfg["l2"] = ("flushed before every step (512 MiB write, outside the CUDA events)"
                      if args.workload in ("layer", "projection") else "inputs larger than L2")
         cfg["timing"] = ("per-step CUDA events, CUDA-graph replay"
@@ -842,7 +851,8 @@ def main():
                          else "per-step CUDA events")
         line = {"metric": METRIC, "value": round(r["value"], 1), "unit": unit, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "higher_is_better": True,
+                "scaling": "weak" if args.workload in _PER_GPU_BATCH else "strong", "vs_baseline": None,
                 "dtype": "f32" if wl["dtype"] == "float32" else "bf16", "data": "synthetic",
                 "config": cfg, "roofline": r["roofline"], "cpu_baseline": r["cpu"], "e2e": r["e2e"],
                 "clocks": r["clocks"], "gpu_launches": r["launches"]}
