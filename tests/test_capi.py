@@ -121,3 +121,25 @@ def test_torch_operators_registered():
         assert hasattr(ops, n), n
     schema = str(ops.mixer_forward.default._schema)
     assert "Tensor x" in schema and "Tensor write_radial_response" in schema
+
+
+def test_integration_stub_matches_the_header(lib):
+    """The ctypes stub INTEGRATION.md shows a maintainer has the header's struct layout and reads
+    error messages correctly (exec'd against the built library; no compute call is made)."""
+    import ctypes
+
+    from sparc_b200 import _lib
+
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    block = next(b for b in re.findall(r"```python\n(.*?)```", text, flags=re.S) if "class SparcMixerFwdArgs" in b)
+    block = block.replace('ctypes.CDLL("libsparc_b200.so")', f"ctypes.CDLL({_lib.LIB_PATH!r})")
+    ns = {}
+    exec(compile(block, "INTEGRATION.md", "exec"), ns)
+    stub, ours = ns["SparcMixerFwdArgs"], _lib.MixerFwdArgs
+    assert [f[0] for f in stub._fields_] == [f[0] for f in ours._fields_]
+    assert ctypes.sizeof(stub) == ctypes.sizeof(ours)
+    for name, _ in ours._fields_:
+        assert getattr(stub, name).offset == getattr(ours, name).offset, name
+    assert ns["lib"].sparc_mixer_forward(None, None) == -1  # SPARC_ERR_ARG
+    assert ns["lib"].sparc_last_error() == b"null args"
+    assert ns["lib"].sparc_mixer_carry_chunks(1 << 40, 0) == (1 << 40) // 8  # 64-bit return declared
