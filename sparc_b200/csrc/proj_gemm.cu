@@ -400,19 +400,33 @@ int sparc_proj_gemm(const SparcProjGemmArgs* a, void* stream) {
   p.max_spin = a->max_spin ? a->max_spin : (1u << 22);
   p.status = a->status;
   const size_t smem = sizeof(GemmSmem) + 1024;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [smem] {
-    attr_err = cudaFuncSetAttribute((const void*)proj_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  });
-  if (attr_err != cudaSuccess) return gemm_fail(SPARC_ERR_LAUNCH, cudaGetErrorString(attr_err));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaLaunchConfig_t cfg = {};
   int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return gemm_fail(SPARC_ERR_LAUNCH, "no current CUDA device");
+  }
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
     cudaGetLastError();
     sms = 148;
   }
+  {
+    // the shared-memory opt-in is a function attribute of each device's context: set it once
+    // per device (one process may drive several GPUs)
+    static std::mutex mu;
+    static unsigned long long opted_in = 0;  // bit per device ordinal
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 64 || !((opted_in >> dev) & 1ull)) {
+      const cudaError_t ae =
+          cudaFuncSetAttribute((const void*)proj_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (ae != cudaSuccess) {
+        cudaGetLastError();
+        return gemm_fail(SPARC_ERR_LAUNCH, cudaGetErrorString(ae));
+      }
+      if (dev < 64) opted_in |= 1ull << dev;
+    }
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)std::min<long long>(mt * nt, sms), 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
