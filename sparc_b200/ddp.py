@@ -137,23 +137,47 @@ class PeerGradAllReduce:
 
 def _map_peer_buffers(L, nbytes, group, check):
     """Allocate this rank's zeroed buffer, exchange CUDA IPC handles over `group` and open the
-    others': (own pointer, [opened pointers], [every rank's pointer in rank order])."""
+    others': (own pointer, [opened pointers], [every rank's pointer in rank order]).
+
+    All ranks succeed or all raise: each rank reports whether its allocation and openings
+    worked, and on any failure every rank closes what it opened, frees its buffer (after a
+    barrier, so that no peer still maps it) and raises the same error naming the failed ranks,
+    instead of leaving the others to wait for it in their next collective."""
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     handle = (ctypes.c_ubyte * 64)()
     own = ctypes.c_void_p()
-    check(L.sparc_peer_buffer_alloc(nbytes, ctypes.byref(own), handle), "sparc_peer_buffer_alloc")
+    err = None
+    try:
+        check(L.sparc_peer_buffer_alloc(nbytes, ctypes.byref(own), handle), "sparc_peer_buffer_alloc")
+    except RuntimeError as e:
+        err = str(e)
     handles = [None] * world
-    dist.all_gather_object(handles, bytes(handle), group=group)
+    dist.all_gather_object(handles, None if err else bytes(handle), group=group)
     opened, buffers = [], []
-    for r, h in enumerate(handles):
-        if r == rank:
-            buffers.append(own.value)
-            continue
-        ptr = ctypes.c_void_p()
-        check(L.sparc_peer_buffer_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(ptr)),
-              "sparc_peer_buffer_open")
-        opened.append(ptr.value)
-        buffers.append(ptr.value)
+    if err is None and all(h is not None for h in handles):
+        for r, h in enumerate(handles):
+            if r == rank:
+                buffers.append(own.value)
+                continue
+            ptr = ctypes.c_void_p()
+            try:
+                check(L.sparc_peer_buffer_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(ptr)),
+                      "sparc_peer_buffer_open")
+            except RuntimeError as e:
+                err = f"{e} (rank {r}'s buffer)"
+                break
+            opened.append(ptr.value)
+            buffers.append(ptr.value)
+    errors = [None] * world
+    dist.all_gather_object(errors, err, group=group)
+    failed = [(r, e) for r, e in enumerate(errors) if e is not None]
+    if failed:
+        for ptr in opened:
+            L.sparc_peer_buffer_close(ctypes.c_void_p(ptr))
+        dist.barrier(group=group)
+        if own.value:
+            L.sparc_peer_buffer_free(ctypes.c_void_p(own.value))
+        raise RuntimeError("mapping the peer buffers failed on " + "; ".join(f"rank {r}: {e}" for r, e in failed))
     return own.value, opened, buffers
 
 
