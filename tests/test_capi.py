@@ -143,3 +143,24 @@ def test_integration_stub_matches_the_header(lib):
     assert ns["lib"].sparc_mixer_forward(None, None) == -1  # SPARC_ERR_ARG
     assert ns["lib"].sparc_last_error() == b"null args"
     assert ns["lib"].sparc_mixer_carry_chunks(1 << 40, 0) == (1 << 40) // 8  # 64-bit return declared
+
+
+def test_header_compiles_as_c_and_cxx_and_the_c_host_links(lib, tmp_path):
+    """include/sparc_b200.h is plain C (and extern "C" under C++), and the C host program of the
+    GPU test builds warning-free against it and links against the library (not run here)."""
+    import subprocess
+
+    from sparc_b200 import _lib
+
+    inc = os.path.join(ROOT, "include")
+    for compiler, lang in (("gcc", "c"), ("g++", "c++")):
+        src = tmp_path / f"h.{lang}"
+        src.write_text('#include "sparc_b200.h"\nint main(void) { return sparc_last_error() == 0; }\n')
+        subprocess.run([compiler, "-x", lang, "-std=c11" if lang == "c" else "-std=c++17", "-Wall", "-Wextra",
+                        "-Werror", "-pedantic", "-I", inc, "-fsyntax-only", str(src)], check=True)
+    exe = tmp_path / "mixer_from_c"
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    subprocess.run(["gcc", "-O2", "-Wall", "-Werror", "-o", str(exe), os.path.join(ROOT, "tests", "c_abi", "mixer_from_c.c"),
+                    "-I", inc, "-I", "/usr/local/cuda/include", "-L", libdir, "-lsparc_b200",
+                    "-L", "/usr/local/cuda/lib64", "-lcudart", "-lm", f"-Wl,-rpath,{libdir}"], check=True)
+    assert exe.exists()
