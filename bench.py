@@ -536,9 +536,15 @@ def run_stack(args, wl, world, rank, local):
     value = gb * T / (ms / 1e3)
     peak, kind = measured_peaks()
     fused_min = L * 5 * W * 2 * gb * T / world
+    # as implemented: every block kernel's algorithmic bytes (saved controls, chunk maps and
+    # states included); the block's reverse summary reads the relu bits the replay wrote
+    # (W/8 bytes per token each way) instead of the mixer's output y
+    per_layer = sum(mixer_kernel_bytes(B, T, W, 2, 16).values()) - W * 2 * B * T + 2 * (W // 8) * B * T
     roofline = {"bound": "hbm", "achieved": round(fused_min / (ms / 1e3) / 1e9, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(fused_min / (ms / 1e3) / 1e9 / peak, 4), "traffic": None,
-                "kernel": "whole step (L*5*W*s bytes/token)", "peak_source": kind}
+                "kernel": "whole step (L*5*W*s bytes/token)", "peak_source": kind,
+                "bytes_per_token": {"fused_minimum": L * 5 * W * 2,
+                                    "as_implemented": round(L * per_layer / (B * T), 1)}}
     sparc_b200.check_status()
     return dict(value=value, ms=ms, roofline=roofline, e2e=None, cpu=None, clocks=clocks.summary(),
                 launches=MIXER_LAUNCHES * L * args.steps, per_step_ms=per, tokens_step=gb * T)
