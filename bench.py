@@ -803,6 +803,8 @@ def main():
                          "peer-memory all-reduce kernel, or by NCCL")
     ap.add_argument("--batch", type=int, default=None, help="override the per-GPU batch (profiling runs)")
     ap.add_argument("--seq-len", type=int, default=None, help="override the sequence length (profiling runs)")
+    ap.add_argument("--channels", type=int, default=None,
+                    help="real workload: override D (config 3 is quoted at D=16384 and D=1024)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     wl = dict(WORKLOADS[args.workload])
@@ -810,6 +812,10 @@ def main():
         wl["batch"] = args.batch
     if args.seq_len is not None:
         wl["seq_len"] = args.seq_len
+    if args.channels is not None:
+        if "channels" not in wl:
+            ap.error("--channels applies to the real workload")
+        wl["channels"] = args.channels
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
 
