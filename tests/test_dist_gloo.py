@@ -1,4 +1,4 @@
-"""Multi-process data parallelism on CPU (gloo, world size 2): the host-side logic of the
+"""Multi-process data parallelism on CPU (gloo, world sizes 2 and 4): the host-side logic of the
 batch-sharded training step. Each rank computes its shard's parameter gradients (with the float64
 oracle, since the kernels need a GPU) into the .grad of real SPARCMixer parameters, then
 GradAllReduce sums them across ranks; the result must equal the full-batch gradients."""
@@ -56,11 +56,12 @@ def _worker(rank, world, port, out_q):
         dist.destroy_process_group()
 
 
-def test_grad_allreduce_matches_full_batch():
+@pytest.mark.parametrize("world", [2, 4])
+def test_grad_allreduce_matches_full_batch(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for pr in procs:
         pr.start()
     got = q.get(timeout=120)
