@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodePara
 using namespace sparc;
 
 extern "C" int sparc_decode_step(const SparcDecodeArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) return fail(SPARC_ERR_ARG, "null args");
   if (!a->x || !a->y || !a->state_r || !a->state_i || !a->new_state_r || !a->new_state_i || !a->nu_log ||
       !a->theta_log || !a->phase_direction || !a->radial_direction || !a->write_log_gain ||

@@ -897,6 +897,7 @@ int sparc_mixer_mask_words(int width) {
 }
 
 int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   const int mode = fwd_mode(a);
   if (mode < 0) { set_err("norm_weight and projections exclude each other"); return SPARC_ERR_ARG; }
@@ -909,6 +910,7 @@ int sparc_mixer_forward(const SparcMixerFwdArgs* a, void* stream) {
 }
 
 int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   Plan pl;
   const bool block = a->norm_weight != nullptr;
@@ -1073,6 +1075,7 @@ extern "C" {
 size_t sparc_mixer_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 
 int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) { set_err("null args"); return SPARC_ERR_ARG; }
   const int mode = fwd_mode(a);
   if (mode < 0) { set_err("norm_weight and projections exclude each other"); return SPARC_ERR_ARG; }

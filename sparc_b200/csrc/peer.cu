@@ -189,6 +189,7 @@ int sparc_peer_buffer_close(void* ptr) { return peer_cuda(cudaIpcCloseMemHandle(
 int sparc_peer_buffer_free(void* ptr) { return peer_cuda(cudaFree(ptr)); }
 
 int sparc_peer_allreduce(const SparcPeerAllreduceArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) return peer_fail(SPARC_ERR_ARG, "null args");
   if (a->world < 1 || a->world > kPeerMax || a->rank < 0 || a->rank >= a->world)
     return peer_fail(SPARC_ERR_ARG, "world must be 1..8 and rank in [0, world)");

@@ -372,6 +372,7 @@ extern "C" {
 const char* sparc_proj_gemm_last_error(void) { return g_gemm_err; }
 
 int sparc_proj_gemm(const SparcProjGemmArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) return gemm_fail(SPARC_ERR_ARG, "null args");
   if (!a->a || !a->b || !a->out || !a->status) return gemm_fail(SPARC_ERR_ARG, "null tensor pointer");
   if (a->rows <= 0 || a->n <= 0 || a->k <= 0) return gemm_fail(SPARC_ERR_SHAPE, "rows, n and k must be positive");

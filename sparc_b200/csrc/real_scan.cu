@@ -451,6 +451,7 @@ size_t sparc_real_workspace_bytes(long long batch, long long length, long long c
 }
 
 int sparc_real_scan_forward(const SparcRealFwdArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) return fail(SPARC_ERR_ARG, "null args");
   if (!a->a || !a->b || !a->out || !a->carry) return fail(SPARC_ERR_ARG, "null tensor pointer");
   RealPlan pl;
@@ -488,6 +489,7 @@ int sparc_real_scan_forward(const SparcRealFwdArgs* a, void* stream) {
 }
 
 int sparc_real_scan_backward(const SparcRealBwdArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) return fail(SPARC_ERR_ARG, "null args");
   if (!a->a || !a->b || !a->grad_out || !a->carry || !a->grad_a || !a->grad_b)
     return fail(SPARC_ERR_ARG, "null tensor pointer");

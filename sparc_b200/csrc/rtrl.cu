@@ -344,6 +344,7 @@ const char* sparc_rtrl_last_error(void) { return g_rtrl_err; }
 int sparc_rtrl_saved_floats(void) { return kRtrlSavedFloats; }
 
 int sparc_rtrl_step(const SparcRtrlStepArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) return rtrl_fail(SPARC_ERR_ARG, "null args");
   if (a->batch <= 0 || a->input_size <= 0 || a->modes <= 0 || a->batch > 65535)
     return rtrl_fail(SPARC_ERR_SHAPE, "batch (1..65535), input_size and modes must be positive");
@@ -389,6 +390,7 @@ int sparc_rtrl_step(const SparcRtrlStepArgs* a, void* stream) {
 }
 
 int sparc_rtrl_grad(const SparcRtrlGradArgs* a, void* stream) {
+  NvtxRange nvtx(__func__);
   if (a == nullptr) return rtrl_fail(SPARC_ERR_ARG, "null args");
   if (a->batch <= 0 || a->input_size <= 0 || a->modes <= 0)
     return rtrl_fail(SPARC_ERR_SHAPE, "batch, input_size and modes must be positive");

@@ -164,3 +164,35 @@ def test_header_compiles_as_c_and_cxx_and_the_c_host_links(lib, tmp_path):
                     "-I", inc, "-I", "/usr/local/cuda/include", "-L", libdir, "-lsparc_b200",
                     "-L", "/usr/local/cuda/lib64", "-lcudart", "-lm", f"-Wl,-rpath,{libdir}"], check=True)
     assert exe.exists()
+
+
+def test_entry_points_open_nvtx_ranges(lib, tmp_path):
+    """Every compute entry point opens an NVTX range named after itself for the whole call (here
+    calls rejected by their argument checks, so no device is needed), recorded by a test
+    injection library (tests/c_abi/nvtx_recorder.c) that the library's NVTX client loads."""
+    import json
+    import subprocess
+    import sys
+
+    from sparc_b200 import _lib
+
+    rec = tmp_path / "libnvtx_recorder.so"
+    subprocess.run(["gcc", "-O2", "-Wall", "-Werror", "-shared", "-fPIC", "-o", str(rec),
+                    os.path.join(ROOT, "tests", "c_abi", "nvtx_recorder.c"), "-I", "/usr/local/cuda/include"],
+                   check=True)
+    names = ["sparc_mixer_forward", "sparc_mixer_backward", "sparc_mixer_forward_noalloc", "sparc_decode_step",
+             "sparc_real_scan_forward", "sparc_real_scan_backward", "sparc_rtrl_step", "sparc_rtrl_grad",
+             "sparc_proj_gemm", "sparc_peer_allreduce"]
+    code = (
+        "import ctypes, json, sys\n"
+        "lib = ctypes.CDLL(sys.argv[1])\n"
+        "rcs = [getattr(lib, n)(None, None) for n in json.loads(sys.argv[3])]\n"
+        "rec = ctypes.CDLL(sys.argv[2])\n"
+        "rec.nvtx_recorder_log.restype = ctypes.c_char_p\n"
+        "print(json.dumps({'rcs': rcs, 'log': rec.nvtx_recorder_log().decode()}))\n")
+    env = dict(os.environ, NVTX_INJECTION64_PATH=str(rec))
+    out = subprocess.run([sys.executable, "-c", code, _lib.LIB_PATH, str(rec), json.dumps(names)], env=env,
+                         capture_output=True, text=True, timeout=120, check=True)
+    res = json.loads(out.stdout.strip().splitlines()[-1])
+    assert res["rcs"] == [-1] * len(names)  # each rejected: null args
+    assert res["log"].split() == [x for n in names for x in (f"push:{n}", "pop")]
