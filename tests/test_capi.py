@@ -196,3 +196,28 @@ def test_entry_points_open_nvtx_ranges(lib, tmp_path):
     res = json.loads(out.stdout.strip().splitlines()[-1])
     assert res["rcs"] == [-1] * len(names)  # each rejected: null args
     assert res["log"].split() == [x for n in names for x in (f"push:{n}", "pop")]
+
+
+def test_state_dict_round_trips_with_the_reference_layout(golden):
+    """Checkpoint / resume: a reference SPARCMixer state dict (its names, shapes and values, from
+    the golden init.npz) loads strictly into ours and saves back unchanged, through torch.save."""
+    import io
+
+    import numpy as np
+    import torch
+
+    import sparc_b200
+
+    d = golden("init")
+    W = 64
+    ref_sd = {k[len(f"w{W}_"):]: torch.tensor(d[k], dtype=torch.float32) for k in d.files if k.startswith(f"w{W}_")}
+    torch.manual_seed(123)  # a different init, overwritten by the load
+    m = sparc_b200.SPARCMixer(W)
+    m.load_state_dict(ref_sd, strict=True)
+    buf = io.BytesIO()
+    torch.save(m.state_dict(), buf)
+    buf.seek(0)
+    m2 = sparc_b200.SPARCMixer(W)
+    m2.load_state_dict(torch.load(buf), strict=True)
+    for k, v in ref_sd.items():
+        np.testing.assert_array_equal(m2.state_dict()[k].numpy(), v.numpy(), err_msg=k)

@@ -171,3 +171,50 @@ def test_peer_buffer_mapping_fails_on_every_rank_and_releases(fail):
         allocated = any(e[0] == "alloc" for e in log)
         assert [e for e in log if e[0] == "free"] == ([("free", 0x10000 * (r + 1))] if allocated else [])
     assert len(msgs) == 1
+
+
+def _dead_peer_worker(rank, world, port, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import time
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    import sparc_b200
+    from sparc_b200.ddp import GradAllReduce
+
+    m = sparc_b200.SPARCMixer(8)
+    for p in m.parameters():
+        p.grad = torch.ones_like(p)
+    red = GradAllReduce(m.parameters())
+    red()  # one good step on every rank
+    dist.barrier()
+    if rank == world - 1:
+        os._exit(0)  # this rank leaves between steps, without its next collective
+    t0 = time.perf_counter()
+    try:
+        red()
+        out_q.put((rank, "no error", time.perf_counter() - t0))
+    except Exception as e:  # the survivors' next collective must fail, not hang
+        out_q.put((rank, type(e).__name__, time.perf_counter() - t0))
+    out_q.close()
+    out_q.join_thread()  # flush the result before leaving without the group's teardown
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_ends_the_others_next_collective_with_an_error():
+    """A rank that exits between steps: the other ranks' next gradient all-reduce raises within
+    the process group's timeout (10 s) instead of waiting for it forever."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world = 3
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    got = [q.get(timeout=120) for _ in range(world - 1)]
+    for pr in procs:
+        pr.join(timeout=60)
+    for rank, kind, seconds in got:
+        assert kind != "no error", rank
+        assert seconds < 60, (rank, seconds)
