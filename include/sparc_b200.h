@@ -275,6 +275,9 @@ int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* args, void* stream);
 
 int sparc_decode_step(const SparcDecodeArgs* args, void* stream);
 
+/* Tokens per saved carry of the real-mode scan (16); sparc_real_carry_chunks(length) is
+ * ceil(length / sparc_real_chunk_tokens()). */
+long long sparc_real_chunk_tokens(void);
 long long sparc_real_carry_chunks(long long length);
 size_t sparc_real_workspace_bytes(long long batch, long long length, long long channels, int dtype);
 int sparc_real_scan_forward(const SparcRealFwdArgs* args, void* stream);

@@ -136,6 +136,7 @@ SIGNATURES = {
     "sparc_mixer_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "sparc_mixer_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(MixerFwdArgs), _vp]),
     "sparc_decode_step": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
+    "sparc_real_chunk_tokens": (_ll, []),
     "sparc_real_carry_chunks": (_ll, [_ll]),
     "sparc_real_workspace_bytes": (ctypes.c_size_t, [_ll, _ll, _ll, ctypes.c_int]),
     "sparc_real_scan_forward": (ctypes.c_int, [ctypes.POINTER(RealFwdArgs), _vp]),

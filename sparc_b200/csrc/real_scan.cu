@@ -442,6 +442,8 @@ using namespace sparc;
 
 extern "C" {
 
+long long sparc_real_chunk_tokens(void) { return kRealChunk; }
+
 long long sparc_real_carry_chunks(long long length) { return (length + kRealChunk - 1) / kRealChunk; }
 
 size_t sparc_real_workspace_bytes(long long batch, long long length, long long channels, int dtype) {

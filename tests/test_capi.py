@@ -56,7 +56,7 @@ def test_host_only_queries(lib):
     assert lib.sparc_mixer_chunk_tokens(_lib.DTYPE_F32) == 8
     assert lib.sparc_mixer_carry_chunks(2048, _lib.DTYPE_BF16) == 128
     assert lib.sparc_mixer_carry_chunks(37, _lib.DTYPE_F32) == 5
-    assert lib.sparc_real_carry_chunks(17) == 2
+    assert lib.sparc_real_carry_chunks(17) == 2 and lib.sparc_real_chunk_tokens() == 16
     assert lib.sparc_mixer_controls_floats() == 16  # the per-token record the kernels write
     assert lib.sparc_mixer_mask_words(2048) == 64 and lib.sparc_mixer_mask_words(600) == 32
     assert lib.sparc_mixer_mask_words(7) == 0
