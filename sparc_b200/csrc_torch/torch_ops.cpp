@@ -83,6 +83,8 @@ std::vector<at::Tensor> mixer_backward(const at::Tensor& x_in, const at::Tensor&
                                        const at::Tensor& write_log_gain, const at::Tensor& write_phase_response,
                                        const at::Tensor& write_radial_response, const at::Tensor& carry,
                                        const at::Tensor& controls) {
+  TORCH_CHECK(x_in.is_cuda() && x_in.dim() == 3 && y.sizes() == x_in.sizes() && dy_in.sizes() == x_in.sizes(),
+              "mixer_backward: x, y and dy must be CUDA [batch, length, width] tensors of one shape");
   c10::cuda::CUDAGuard guard(x_in.device());
   const at::Tensor x = x_in.contiguous(), dy = dy_in.to(x.scalar_type()).contiguous(), yc = y.contiguous();
   const int64_t B = x.size(0), T = x.size(1), W = x.size(2), M = W / 2;
@@ -94,7 +96,7 @@ std::vector<at::Tensor> mixer_backward(const at::Tensor& x_in, const at::Tensor&
   std::vector<at::Tensor> g = {at::empty({M}, fo), at::empty({M}, fo), at::empty({W + 1}, fo), at::empty({W + 1}, fo),
                                at::empty({M}, fo), at::empty({M}, fo), at::empty({M}, fo), at::empty({M}, fo)};
   const size_t wsb = sparc_mixer_workspace_bytes(B, T, (int)W, dt);
-  TORCH_CHECK(wsb > 0, "mixer_backward: unsupported shape");
+  TORCH_CHECK(wsb > 0, "mixer_backward: unsupported shape (", sparc_last_error(), ")");
   at::Tensor ws = workspace(x, wsb);
   SparcMixerBwdArgs a = {};
   a.x = x.data_ptr();
@@ -136,6 +138,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> decode_step(
     const at::Tensor& x_in, const at::Tensor& state_r, const at::Tensor& state_i, const at::Tensor& nu_log,
     const at::Tensor& theta_log, const at::Tensor& phase_direction, const at::Tensor& radial_direction,
     const at::Tensor& write_log_gain, const at::Tensor& write_phase_response, const at::Tensor& write_radial_response) {
+  TORCH_CHECK(x_in.is_cuda() && x_in.dim() == 2, "decode_step: x must be a CUDA [batch, width] tensor");
   c10::cuda::CUDAGuard guard(x_in.device());
   const at::Tensor x = x_in.contiguous();
   const int64_t B = x.size(0), W = x.size(1), M = W / 2;
@@ -168,6 +171,8 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> decode_step(
 
 // real_scan / real_chunk_scan forward (backward/scan.py:793-884): (out, carry, last).
 std::tuple<at::Tensor, at::Tensor, at::Tensor> real_scan_forward(const at::Tensor& a_in, const at::Tensor& b_in) {
+  TORCH_CHECK(a_in.is_cuda() && a_in.dim() == 3 && b_in.sizes() == a_in.sizes(),
+              "real_scan_forward: a and b must be CUDA [batch, length, channels] tensors of one shape");
   c10::cuda::CUDAGuard guard(a_in.device());
   const at::Tensor a = a_in.contiguous(), b = b_in.to(a.scalar_type()).contiguous();
   const int64_t B = a.size(0), L = a.size(1), D = a.size(2);
@@ -177,7 +182,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> real_scan_forward(const at::Tenso
   at::Tensor carry = at::empty({B, sparc_real_carry_chunks(L), D}, fo);
   at::Tensor last = at::empty({B, D}, fo);
   const size_t wsb = sparc_real_workspace_bytes(B, L, D, dt);
-  TORCH_CHECK(wsb > 0, "real_scan_forward: unsupported shape");
+  TORCH_CHECK(wsb > 0, "real_scan_forward: unsupported shape (", sparc_last_error(), ")");
   at::Tensor ws = workspace(a, wsb);
   SparcRealFwdArgs r = {};
   r.a = a.data_ptr();
@@ -198,6 +203,8 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> real_scan_forward(const at::Tenso
 // Its backward: (grad_a, grad_b).
 std::tuple<at::Tensor, at::Tensor> real_scan_backward(const at::Tensor& a_in, const at::Tensor& b_in,
                                                       const at::Tensor& g_in, const at::Tensor& carry) {
+  TORCH_CHECK(a_in.is_cuda() && a_in.dim() == 3 && b_in.sizes() == a_in.sizes() && g_in.sizes() == a_in.sizes(),
+              "real_scan_backward: a, b and grad_out must be CUDA [batch, length, channels] tensors of one shape");
   c10::cuda::CUDAGuard guard(a_in.device());
   const at::Tensor a = a_in.contiguous(), b = b_in.to(a.scalar_type()).contiguous(),
                    g = g_in.to(a.scalar_type()).contiguous(), cc = carry.contiguous();
@@ -205,6 +212,7 @@ std::tuple<at::Tensor, at::Tensor> real_scan_backward(const at::Tensor& a_in, co
   const int dt = dtype_code(a);
   at::Tensor ga = at::empty_like(a), gb = at::empty_like(a);
   const size_t wsb = sparc_real_workspace_bytes(B, L, D, dt);
+  TORCH_CHECK(wsb > 0, "real_scan_backward: unsupported shape (", sparc_last_error(), ")");
   at::Tensor ws = workspace(a, wsb);
   SparcRealBwdArgs r = {};
   r.a = a.data_ptr();
