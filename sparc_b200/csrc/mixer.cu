@@ -161,7 +161,7 @@ __device__ __forceinline__ void load_norm_weight(ModeConst2& mc, const float* w,
   mc.wim = make_float2(a0 ? w[M + m0] : 0.0f, a1 ? w[M + m0 + 1] : 0.0f);
 }
 
-// Per-token controls as the forward saves them (48 bytes): every value twice, so that a
+// Per-token controls as the forward saves them (64 bytes): every value twice, so that a
 // thread's two modes load them as packed pairs; keep is 0 at a token where a segment reset cuts
 // the recurrence (its transition is zero), else 1.
 struct TokenCtl {
