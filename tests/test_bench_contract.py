@@ -60,3 +60,46 @@ def test_reference_arm_under_torchrun_prints_once():
                   "--impl", "reference", "--steps", "2", "--warmup", "1", "--batch", "2", "--seq-len", "64"])
     assert len(lines) == 1
     _check_line(lines[0], 2, 2, 3)  # warm-up is raised to the contract's minimum of 3
+
+
+def test_our_arm_line_assembly(monkeypatch, capsys):
+    """Our arm's JSON line from a stubbed runner (the kernels need a GPU): every key of the
+    contract, the shared workload config, weak scaling, and the runner's figures passed through."""
+    import bench
+
+    fake = dict(value=1.25e8, ms=0.131, roofline={"bound": "hbm", "achieved": 2000.0, "peak": 6555.2, "unit": "GB/s",
+                                                  "frac": 0.305, "traffic": 85891584.0},
+                e2e={"value": 1.3e7, "unit": "tokens/s", "h2d_bytes_per_step": 67108864, "d2h_bytes_per_step": 4},
+                cpu={"value": 3.5e4, "unit": "tokens/s", "cores": 8, "kind": "port", "sample": "s"},
+                clocks={"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": [], "samples": 3}, launches=140, chunk=8)
+    monkeypatch.setattr(bench, "_dist", lambda: (1, 0, 0))
+    monkeypatch.setattr(bench, "run_layer", lambda *a: fake)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--steps", "20", "--warmup", "5"])
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    monkeypatch.delenv("RANK", raising=False)
+    bench.main()
+    lines = [json.loads(l) for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    line = lines[0]
+    need = KEYS - {"impl"} | {"roofline", "clocks", "gpu_launches"}
+    assert need <= set(line), need - set(line)
+    assert line["value"] == 1.25e8 and line["ms_per_step"] == 0.131 and line["n_gpus"] == 1
+    assert line["steps"] == 20 and line["warmup"] == 5 and line["scaling"] == "weak" and line["dtype"] == "f32"
+    assert line["roofline"] == fake["roofline"] and line["e2e"] == fake["e2e"] and line["cpu_baseline"] == fake["cpu"]
+    assert line["gpu_launches"] == 140 and line["clocks"] == fake["clocks"] and line["vs_baseline"] is None
+    want = bench.workload_config("layer", bench.WORKLOADS["layer"], 1)
+    assert {k: line["config"][k] for k in want} == want and line["config"]["chunk"] == 8
+    assert line["config"]["global_batch"] == 8 and "l2" in line["config"] and line["config"]["parallelism"] == "single"
+
+
+def test_stack_line_reports_strong_scaling(monkeypatch, capsys):
+    import bench
+
+    fake = dict(value=1.5e7, ms=68.0, roofline={"bound": "hbm"}, e2e=None, cpu=None, clocks={}, launches=28)
+    monkeypatch.setattr(bench, "_dist", lambda: (1, 0, 0))
+    monkeypatch.setattr(bench, "run_stack", lambda *a: fake)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--workload", "stack", "--steps", "2", "--warmup", "3"])
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    bench.main()
+    line = json.loads([l for l in capsys.readouterr().out.splitlines() if l.startswith("{")][0])
+    assert line["scaling"] == "strong" and line["config"]["global_batch"] == 64 and line["dtype"] == "bf16"
