@@ -3,8 +3,10 @@
 (itself checked against the pinned oracle below): the change of variables, the plumbing, the
 output layout and the gradients through it against the reference's own sparc_tiled_serial_scan
 golden vectors (h0, segment resets, gradient of the last state), the routing of the dispatch,
-the reference's argument checks, and that real inputs on CPU still fail (no CPU path).
-The kernels themselves run in tests/test_gpu_scan_functions.py."""
+the reference's argument checks, and that real inputs on CPU still fail (no CPU path). One test
+goes through the real kernel call (scan._core and the projection-mode autograd function) with only
+the two ctypes wrappers underneath emulated. The kernels themselves run in
+tests/test_gpu_scan_functions.py."""
 import math
 
 import numpy as np
@@ -170,3 +172,63 @@ def test_reference_argument_checks():
         scan.sparc_chunk_scan(e, dl, nl, tl, b, b, controller_backward_cache=(e,) * 6)
     with pytest.raises(RuntimeError, match="CUDA"):  # well-formed CPU inputs: there is no CPU path
         scan.sparc_scan(e, dl, nl, tl, b, b)
+
+
+class _EmuSaved:
+    pass
+
+
+def _emu_core_forward(u, p, modal, h0, reset, lin, max_spin):
+    """Stands in for projection._core_forward (the sparc_mixer_forward call in projection mode)
+    with the float64 restatement, keeping its autograd graph for _emu_core_backward."""
+    nu_log, theta_log, wlg, wpr, wrr = modal
+    assert lin and not any(bool(t.abs().sum()) for t in (wlg, wpr, wrr))  # what the scan entry points pass
+    sv = _EmuSaved()
+    sv.leaves = [t.detach().double().requires_grad_(True) for t in (u, p, nu_log, theta_log)]
+    sv.h0 = None if h0 is None else [t.detach().double().requires_grad_(True) for t in h0]
+    sv.u_dtype = u.dtype
+    with torch.enable_grad():
+        sv.out = _standin_core(sv.leaves[0], sv.leaves[1], sv.leaves[2], sv.leaves[3], sv.h0, reset)
+    h, lr, li = sv.out
+    return h.detach().to(u.dtype), lr.detach(), li.detach(), sv
+
+
+def _emu_core_backward(sv, dh, dlast_r, dlast_i):
+    """Stands in for projection._core_backward: (du, dp, five modal gradients, gh0 or None)."""
+    h, lr, li = sv.out
+    gouts = [torch.zeros_like(h) if dh is None else dh.double(), torch.zeros_like(lr) if dlast_r is None else dlast_r,
+             torch.zeros_like(li) if dlast_i is None else dlast_i]
+    ins = sv.leaves + (sv.h0 or [])
+    gr = torch.autograd.grad([h, lr, li], ins, gouts, allow_unused=True)
+    gr = [torch.zeros_like(x) if g is None else g for g, x in zip(gr, ins)]
+    du, dp, dnu, dth = gr[0].to(sv.u_dtype), gr[1].float(), gr[2].float(), gr[3].float()
+    zeros = torch.zeros_like(dnu)
+    gh0 = None if sv.h0 is None else (gr[4].float(), gr[5].float())
+    return du, dp, [dnu, dth, zeros, zeros, zeros], gh0
+
+
+def test_real_core_call_with_emulated_kernels(monkeypatch, golden):
+    """The scan entry points through their real kernel call (scan._core -> the projection-mode
+    autograd function), with only the two ctypes wrappers underneath emulated: the argument
+    order, the zero write parameters, h0 / resets and the gradients' way back, against the
+    reference's golden vectors."""
+    from sparc_b200 import _lib, projection, scan
+
+    monkeypatch.setattr(projection, "_core_forward", _emu_core_forward)
+    monkeypatch.setattr(projection, "_core_backward", _emu_core_backward)
+    monkeypatch.setattr(_lib, "require_cuda", lambda t, name: None)
+    d = golden("tiled_h0_reset")
+    t = {k: torch.tensor(d[k], dtype=torch.float32).requires_grad_(True)
+         for k in ("eta", "delta", "write_r", "write_i", "h0_r", "h0_i", "p_nu_log", "p_theta_log")}
+    out_r, out_i, last_r, last_i = scan.sparc_tiled_serial_scan(
+        t["eta"], t["delta"], t["p_nu_log"], t["p_theta_log"], t["write_r"], t["write_i"],
+        segment_pos=torch.tensor(d["segment_pos"]), initial_state=(t["h0_r"], t["h0_i"]))
+    for got, ref in ((out_r, "out_r"), (out_i, "out_i"), (last_r, "last_r"), (last_i, "last_i")):
+        assert O.rel_l2(got.detach().double().numpy(), d[ref]) < 1e-5, ref
+    ((out_r.double() * torch.tensor(d["d_out_r"])).sum() + (out_i.double() * torch.tensor(d["d_out_i"])).sum()
+     + (last_r.double() * torch.tensor(d["d_last_r"])).sum() + (last_i.double() * torch.tensor(d["d_last_i"])).sum()
+     ).backward()
+    for k, ref in (("eta", "grad_eta"), ("delta", "grad_delta"), ("write_r", "grad_write_r"),
+                   ("write_i", "grad_write_i"), ("h0_r", "grad_h0_r"), ("h0_i", "grad_h0_i"),
+                   ("p_nu_log", "grad_nu_log"), ("p_theta_log", "grad_theta_log")):
+        assert O.rel_l2(t[k].grad.double().numpy(), d[ref]) < 1e-4, k
