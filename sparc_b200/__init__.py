@@ -6,13 +6,14 @@
 All compute runs in the sm_100a kernels of ``libsparc_b200.so`` (C ABI in
 ``include/sparc_b200.h``), loaded through ctypes on first use. There is no CPU path.
 """
-from .mixer import SPARCMixer, sparc_block, sparc_decode_step, sparc_mixer
+from .mixer import (SPARCMixer, prepare_decode, run_decode_step, run_sequence, sparc_block, sparc_decode_step,
+                    sparc_mixer)
 from .stack import SPARCBlock, SPARCStack
 from .projection import SPARCSequenceLayer, sparc_projection_states, sparc_sequence_layer
 from .rtrl import SPARCRTRLCell, initialize_carry, initialize_traces, rtrl_step
 from .real import real_chunk_scan, real_scan, real_scan_with_last
-from .scan import (sparc_chunk_scan, sparc_scan, sparc_scan_with_last, sparc_tiled_serial_scan,
-                   sparc_training_scan_dispatch)
+from .scan import (sparc_chunk_scan, sparc_scan, sparc_scan_precomputed_decay, sparc_scan_with_last,
+                   sparc_tiled_serial_scan, sparc_training_scan_dispatch)
 from . import _lib
 
 
@@ -39,5 +40,6 @@ __all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack
            "SPARCSequenceLayer", "sparc_sequence_layer", "sparc_projection_states",
            "SPARCRTRLCell", "rtrl_step", "initialize_carry", "initialize_traces",
            "real_scan", "real_chunk_scan", "real_scan_with_last", "sparc_scan", "sparc_chunk_scan",
-           "sparc_scan_with_last", "sparc_tiled_serial_scan", "sparc_training_scan_dispatch", "check_status",
+           "sparc_scan_with_last", "sparc_tiled_serial_scan", "sparc_training_scan_dispatch",
+           "sparc_scan_precomputed_decay", "run_sequence", "prepare_decode", "run_decode_step", "check_status",
            "library_path"]

@@ -206,6 +206,23 @@ def sparc_decode_step(x: torch.Tensor, params, state):
     return y, (nr, ni)
 
 
+def run_sequence(module, x: torch.Tensor, return_cache: bool = False):
+    """The reference's sequence entry as a function of the module (forward/scan.py:1398-1603,
+    which its SPARCMixer.forward calls): module(x, return_cache)."""
+    return module(x, return_cache)
+
+
+def prepare_decode(module) -> None:
+    """forward/decode.py:252-255: switch the module to its fused decode step."""
+    module.prepare_inference()
+
+
+def run_decode_step(module, x: torch.Tensor, state, segment_pos):
+    """forward/decode.py:273-306 (segment_pos is ignored there too): module.step(x, state,
+    segment_pos)."""
+    return module.step(x, state, segment_pos)
+
+
 class SPARCMixer(nn.Module):
     """Drop-in for the reference SPARCMixer (sparc-kernal/sparc.py:58-123)."""
 

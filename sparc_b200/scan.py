@@ -1,8 +1,8 @@
 """Scan-level functional entry points of the reference module: the SPARC recurrence from
 precomputed per-token controls (eta, delta) [B, L] and writes (br, bi) [B, L, M], as
-``sparc_scan``, ``sparc_chunk_scan``, ``sparc_scan_with_last``, ``sparc_tiled_serial_scan`` and
-``sparc_training_scan_dispatch`` (sparc-kernal/backward/scan.py:1658-1877, re-exported by
-sparc.py:17-29):
+``sparc_scan``, ``sparc_chunk_scan``, ``sparc_scan_with_last``, ``sparc_tiled_serial_scan``,
+``sparc_training_scan_dispatch`` and ``sparc_scan_precomputed_decay``
+(sparc-kernal/backward/scan.py:1658-1877, re-exported by sparc.py:17-29):
 
     rho = exp(-nu e^eta),  phi = theta + (1 - rho) delta,  h_t = rho e^{i phi} h_{t-1} + b_t
     (nu = e^{nu_log}, theta = e^{theta_log}; forward/scan.py:725-757).
@@ -225,3 +225,10 @@ def sparc_training_scan_dispatch(eta, delta, nu_log, theta_log, br, bi, *, chunk
                             compressed_transition, atomic_shared, two_stage_spectral, compact_control_cache,
                             precompute_spectral, mode_block_size=block_size, backward_chunk_group=backward_chunk_group,
                             fused_output_relu=fused_output_relu, prefix_group_size=prefix_group_size)
+
+
+def sparc_scan_precomputed_decay(eta, delta, nu_log, theta_log, br, bi):
+    """The reference's variant of sparc_scan that precomputes rho = exp(-nu e^eta) per
+    (token, mode) before its serial kernel (backward/scan.py:1073-1121, 1690-1700): the same
+    scan and gradients, so the same path here."""
+    return sparc_scan(eta, delta, nu_log, theta_log, br, bi)

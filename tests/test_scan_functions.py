@@ -232,3 +232,21 @@ def test_real_core_call_with_emulated_kernels(monkeypatch, golden):
                    ("write_i", "grad_write_i"), ("h0_r", "grad_h0_r"), ("h0_i", "grad_h0_i"),
                    ("p_nu_log", "grad_nu_log"), ("p_theta_log", "grad_theta_log")):
         assert O.rel_l2(t[k].grad.double().numpy(), d[ref]) < 1e-4, k
+
+
+def test_module_level_aliases(standin, golden):
+    import sparc_b200
+
+    d = golden("tiled_h0_reset")
+    args = [torch.tensor(d[k]).float() for k in ("eta", "delta", "p_nu_log", "p_theta_log", "write_r", "write_i")]
+    a, b = standin.sparc_scan_precomputed_decay(*args), standin.sparc_scan(*args)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    m = sparc_b200.SPARCMixer(8)
+    with pytest.raises(ValueError, match="batch, length, 8"):
+        sparc_b200.run_sequence(m, torch.randn(2, 3, 6))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sparc_b200.run_sequence(m, torch.randn(2, 3, 8), True)
+    sparc_b200.prepare_decode(m)
+    assert m._inference_fused
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sparc_b200.run_decode_step(m, torch.randn(2, 8), (torch.zeros(2, 4), torch.zeros(2, 4)), None)
