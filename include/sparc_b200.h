@@ -82,7 +82,7 @@ extern "C" {
  * backward then returns the block input's gradient in dx (the residual path included) and the
  * norm weight's in grad_norm_weight. */
 /* Projection mode (projections given): the recurrence core of the projection variant, the JAX
- * sequence layer and RTRL cell of sparc-impl (recurrence.py:20-63, layers.py:156-194), whose
+ * sequence layer and RTRL cell of sparc-impl (recurrence.py:20-63, layers.py:88-126), whose
  * content and controls come from matrix products the caller computes: x is the content input
  * u = [x_in content_real, x_in content_imag] ([batch, length, width], width = 2M), projections
  * the per-token controller projections p = [x_in, 1] phase_controller / retention_controller
@@ -298,7 +298,7 @@ int sparc_timing_read(double* ms, long long* launches, int n);
 int sparc_read_status(const void* workspace, unsigned* status, void* stream);
 int sparc_clear_status(void* workspace, void* stream);
 
-/* RTRL online traces of the SPARC cell (sparc-impl/sparc/training/rtrl.py:154-240, replaces the
+/* RTRL online traces of the SPARC cell (sparc-impl/sparc/training/rtrl.py:61-148, replaces the
  * JAX _trace_step / stored_rtrl_step). Traces and states are complex, stored as interleaved
  * float32 pairs (the layout of complex64): trace index 0-4 the modal parameters decay_log,
  * frequency_log, write_log_gain, write_phase_response, write_retention_response [batch, M];
@@ -306,7 +306,7 @@ int sparc_clear_status(void* workspace, void* stream);
  * retention_controller [batch, input_size + 1, M]. `content` is the caller's product
  * [x content_real, x content_imag] ([batch, 2M] float32) and `projections` [x, 1] phase_controller,
  * [x, 1] retention_controller ([batch, 2] float32). Where reset[b] is nonzero the carried state
- * and traces of row b are zeroed before the step (_reset_carry, rtrl.py:142-151). new_traces may
+ * and traces of row b are zeroed before the step (_reset_carry, rtrl.py:49-58). new_traces may
  * alias traces (each element is read and written by the same thread). `saved`
  * ([batch, M, sparc_rtrl_saved_floats()] float32) receives what sparc_rtrl_grad needs. */
 typedef struct SparcRtrlStepArgs {
@@ -330,7 +330,7 @@ typedef struct SparcRtrlStepArgs {
   int content_linear;                  /* content_activation "linear": content u, else tanh(u) */
 } SparcRtrlStepArgs;
 
-/* Gradients of a loss on the step's new state (stored_rtrl_step's backward, rtrl.py:220-240):
+/* Gradients of a loss on the step's new state (stored_rtrl_step's backward, rtrl.py:127-148):
  * grad_state holds (dL/dRe h', dL/dIm h') per mode; every parameter's gradient is
  * sum_b (dL/dRe h' Re(trace) + dL/dIm h' Im(trace)) over the step's NEW traces (summed over the
  * modes too for the controllers; grad_params in the trace order, shapes [M], [input_size, M],
@@ -355,7 +355,7 @@ int sparc_rtrl_grad(const SparcRtrlGradArgs* args, void* stream);
 const char* sparc_rtrl_last_error(void);
 
 /* Tensor-core product of the projection variant (content, readout and their adjoints; the JAX
- * layer's x @ content_real/imag and states @ readout^T, recurrence.py:39-40, layers.py:193-194):
+ * layer's x @ content_real/imag and states @ readout^T, recurrence.py:39-40, layers.py:125-126):
  *   out[m, n] = sum_k a[m, k] b[n, k] (+ skip[n] x[m, n]) (+ dp[m, 0] c0[n] + dp[m, 1] c1[n])
  * a [rows, k] and b [n, k] row-major bfloat16 (k a multiple of 8, 16-byte aligned bases),
  * float32 accumulation, out [rows, n] bfloat16 (or float32 with out_f32). x (bfloat16,

@@ -15,7 +15,7 @@ their distributions are restated (``init_layer``).
 
 All citations are paths inside the reference project (Botwwt/sparc).
 
-Layer math (sparc-impl/sparc/recurrence.py:20-63, layers.py:156-194), x: [B, T, W], M modes:
+Layer math (sparc-impl/sparc/recurrence.py:20-63, layers.py:88-126), x: [B, T, W], M modes:
     p0 = [x, 1] . phase_controller,  p1 = [x, 1] . retention_controller
     u_r = x @ content_real,  u_i = x @ content_imag             ([W, M] each)
     c = tanh(u) (or u for content_activation "linear")
@@ -60,7 +60,7 @@ def mixer_params(J) -> O.Params:
 
 
 def init_layer(model_width, modes, rng, r_min=0.9, r_max=0.999, max_phase=6.28):
-    """Parameter distributions of SPARCSequenceLayer (layers.py:85-126, 180-192;
+    """Parameter distributions of SPARCSequenceLayer (layers.py:17-58, 112-124;
     initialization.py:5-39), drawn from a numpy Generator (JAX's PRNG is not reproducible)."""
     W, M = model_width, modes
     u = rng.random(M)
@@ -130,7 +130,7 @@ def _content(u, activation):
 
 
 def layer_forward(x, J, h0=None, reset=None, content_activation="tanh"):
-    """SPARCSequenceLayer.__call__ (layers.py:164-194). Returns y [B, T, W], (last_r, last_i)
+    """SPARCSequenceLayer.__call__ (layers.py:97-126). Returns y [B, T, W], (last_r, last_i)
     and the saved intermediates."""
     x = _f64(x)
     P = mixer_params(J)
@@ -210,7 +210,7 @@ def layer_backward(x, J, dy, h0=None, grad_last=None, reset=None, content_activa
 
 # ------------------------------------------------------------------------------------ RTRL
 def init_cell(input_size, modes, rng, r_min=0.0, r_max=1.0, max_phase=6.28):
-    """Parameter distributions of SPARCRTRLCell (layers.py:129-150 with _parameters 85-126):
+    """Parameter distributions of SPARCRTRLCell (layers.py:61-85 with _parameters 17-58):
     the layer's recurrent parameters, no readout or skip."""
     J = init_layer(input_size, modes, rng, r_min, r_max, max_phase)
     for k in ("readout_real", "readout_imag", "skip"):
@@ -219,7 +219,7 @@ def init_cell(input_size, modes, rng, r_min=0.0, r_max=1.0, max_phase=6.28):
 
 
 def init_traces(batch, input_size, modes):
-    """rtrl.py:118-134: modal traces [B, M], content [B, W, M], controllers [B, W+1, M],
+    """rtrl.py:25-41: modal traces [B, M], content [B, W, M], controllers [B, W+1, M],
     complex, zero."""
     tr = {k: np.zeros((batch, modes), np.complex128) for k in MODAL_NAMES}
     tr.update({k: np.zeros((batch, input_size, modes), np.complex128) for k in CONTENT_NAMES})
@@ -240,7 +240,7 @@ def _step_terms(J, x, content_activation):
 
 
 def rtrl_step(J, state, traces, x, reset=None, content_activation="tanh"):
-    """One step of _trace_step (rtrl.py:154-201): the carry is zeroed where reset is set
+    """One step of _trace_step (rtrl.py:61-108): the carry is zeroed where reset is set
     (_reset_carry, 142-151), then every trace is advanced as trace' = a trace + direct, with
     direct the forward-mode derivative of this step's h' = a h + gain c with respect to the
     parameter (for the controllers: w.r.t. the bias entry, spread over the inputs by the
@@ -298,7 +298,7 @@ def rtrl_step(J, state, traces, x, reset=None, content_activation="tanh"):
 
 
 def rtrl_grads(J, state, traces, x, g_r, g_i, reset=None, content_activation="tanh"):
-    """Backward of stored_rtrl_step (rtrl.py:220-240) for a real loss of the step's new state:
+    """Backward of stored_rtrl_step (rtrl.py:127-148) for a real loss of the step's new state:
     g_r, g_i = dL/d Re h', dL/d Im h' [B, M] (JAX's cotangent is g_r - i g_i). Parameter
     gradients are Re(cot * trace) summed over the batch (and over the modes for the
     controllers), with `traces` the step's NEW traces; the input gradient is the one-step

@@ -1,7 +1,7 @@
 // Tensor-core matrix products of the SPARC projection variant for B200 (sm_100a): the content
 // product u = x [content_real | content_imag], the readout y = h readout^T + skip * x and, in
 // the backward, dh = dy readout and dx = du content^T + dp controller^T + skip * dy
-// (sparc-impl/sparc/recurrence.py:39-40, layers.py:193-194 and their adjoints).
+// (sparc-impl/sparc/recurrence.py:39-40, layers.py:125-126 and their adjoints).
 //
 //   C[m, n] = sum_k A[m, k] B[n, k]  (+ skip[n] X[m, n]) (+ dp[m, 0] c0[n] + dp[m, 1] c1[n])
 //

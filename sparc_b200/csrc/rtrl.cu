@@ -67,7 +67,7 @@ __device__ __forceinline__ float2 cmulf(float2 a, float2 b) {
 }
 
 // The step's transition, write and the forward-mode derivative of h' = a h + gain c w.r.t. each
-// parameter (rtrl.py:157-199; recurrence.py:28-63 for the terms). With z = nu e^eta,
+// parameter (rtrl.py:61-108; recurrence.py:28-63 for the terms). With z = nu e^eta,
 // rho = e^-z, s0 = 1 - tanh(p0)^2, s1 = 1 - tanh(p1)^2, dyn = z e^-2z / -expm1(-2z),
 // stat = nu e^-2nu / -expm1(-2nu), gq = gain (1 - gate / 2):
 //   decay_log:  z (i rho delta - 1) a h + gain (dyn - stat) c      frequency_log: i theta a h

@@ -1,5 +1,5 @@
 """The projection variant of SPARC on B200: the sequence layer of the JAX package ``sparc-impl``
-(``SPARCSequenceLayer``, layers.py:156-194 over recurrence.py:20-63) as a torch module.
+(``SPARCSequenceLayer``, layers.py:88-126 over recurrence.py:20-63) as a torch module.
 
 Unlike the torch ``SPARCMixer`` (whose content is x's two halves and whose output is
 relu([Re h, Im h])), this layer writes a content u = x content_{real,imag} into M modes of any
@@ -282,7 +282,7 @@ def sparc_sequence_layer(x, params, content_activation: str = "tanh", state=None
 
 
 class SPARCSequenceLayer(nn.Module):
-    """Torch counterpart of ``SPARCSequenceLayer`` (sparc-impl/sparc/layers.py:156-194).
+    """Torch counterpart of ``SPARCSequenceLayer`` (sparc-impl/sparc/layers.py:88-126).
 
     ``forward(x)`` returns y [B, T, model_width] like the JAX layer's ``__call__``; the optional
     ``state`` / ``segment_pos`` / ``reset_first`` / ``return_cache`` arguments mirror
@@ -296,7 +296,7 @@ class SPARCSequenceLayer(nn.Module):
         self.modes = M = modes
         self.content_activation = content_activation
         self.max_spin = 0
-        # draw order of _parameters (layers.py:86-115), then the readout and skip (180-192)
+        # draw order of _parameters (layers.py:17-58), then the readout and skip (layers.py:112-124)
         u = torch.rand(M)
         frequency_log = torch.log(max_phase * u)
         u = torch.rand(M)
@@ -321,7 +321,7 @@ class SPARCSequenceLayer(nn.Module):
     def forward(self, x: torch.Tensor, state=None, segment_pos=None, reset_first: bool = False,
                 return_cache: bool = False):
         if x.shape[-1] != self.model_width:
-            raise ValueError((x.shape[-1], self.model_width))  # layers.py:166-167
+            raise ValueError((x.shape[-1], self.model_width))  # layers.py:98-99
         if x.dim() != 3:
             raise ValueError("SPARCSequenceLayer expects x of shape [batch, length, model_width]")
         y, last = sparc_sequence_layer(x.contiguous(), self.parameters_dict(), self.content_activation,

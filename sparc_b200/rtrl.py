@@ -1,10 +1,10 @@
 """RTRL online training of the SPARC cell on B200: the torch counterpart of the JAX
-``SPARCRTRLCell`` (sparc-impl/sparc/layers.py:129-153) over ``stored_rtrl_step``
-(training/rtrl.py:154-247).
+``SPARCRTRLCell`` (sparc-impl/sparc/layers.py:61-85) over ``stored_rtrl_step``
+(training/rtrl.py:61-155).
 
 The carry is (state, traces): the state a complex64 [B, M] tensor, the traces a dict of complex64
 tensors, one per recurrent parameter (modal [B, M], content [B, W, M], controllers
-[B, W+1, M]), as ``initialize_carry`` (rtrl.py:118-139) makes them. One call advances state and
+[B, W+1, M]), as ``initialize_carry`` (rtrl.py:25-46) makes them. One call advances state and
 traces by one step in ``rtrl_step_kernel`` and returns (next_carry, output) with
 output = relu([Re h', Im h']) (or linear). As in the JAX custom VJP, the next carry carries no
 gradient, a loss on the output gives every recurrent parameter the gradient
@@ -29,7 +29,7 @@ TRACE_NAMES = MODAL_NAMES + CONTENT_NAMES + CONTROLLER_NAMES
 
 
 def initialize_traces(batch_size: int, input_size: int, modes: int, device=None, dtype=torch.complex64):
-    """Zero traces, rtrl.py:118-134."""
+    """Zero traces, rtrl.py:25-41."""
     tr = {n: torch.zeros((batch_size, modes), dtype=dtype, device=device) for n in MODAL_NAMES}
     tr.update({n: torch.zeros((batch_size, input_size, modes), dtype=dtype, device=device)
                for n in CONTENT_NAMES})
@@ -39,7 +39,7 @@ def initialize_traces(batch_size: int, input_size: int, modes: int, device=None,
 
 
 def initialize_carry(batch_size: int, input_size: int, modes: int, device=None, dtype=torch.complex64):
-    """(zero state [B, M], zero traces), rtrl.py:137-139."""
+    """(zero state [B, M], zero traces), rtrl.py:44-46."""
     return (torch.zeros((batch_size, modes), dtype=dtype, device=device),
             initialize_traces(batch_size, input_size, modes, device, dtype))
 
@@ -112,7 +112,7 @@ class _RTRLStepFunction(torch.autograd.Function):
 
 
 def rtrl_step(params, carry, inputs: torch.Tensor, reset=None, content_activation: str = "tanh"):
-    """stored_rtrl_step (rtrl.py:204-209): ((next_state, next_traces), state) for a mapping of the
+    """stored_rtrl_step (rtrl.py:111-116): ((next_state, next_traces), state) for a mapping of the
     nine recurrent parameters. next_state is the state with its gradient path (the traces give
     the parameters' gradients); the returned carry is detached."""
     if content_activation not in ("tanh", "linear"):
@@ -139,7 +139,7 @@ def rtrl_step(params, carry, inputs: torch.Tensor, reset=None, content_activatio
 
 
 class SPARCRTRLCell(nn.Module):
-    """Torch counterpart of ``SPARCRTRLCell`` (sparc-impl/sparc/layers.py:129-153):
+    """Torch counterpart of ``SPARCRTRLCell`` (sparc-impl/sparc/layers.py:61-85):
     ``forward(carry, inputs, reset) -> (next_carry, output)``, inputs [B, input_size]."""
 
     def __init__(self, input_size: int, modes: int, r_min: float = 0.0, r_max: float = 1.0,
@@ -148,12 +148,12 @@ class SPARCRTRLCell(nn.Module):
         if content_activation not in ("tanh", "linear"):
             raise ValueError(content_activation)
         if output_activation not in ("relu", "linear"):
-            raise ValueError(output_activation)  # layers.py:146-149
+            raise ValueError(output_activation)  # layers.py:78-81
         self.input_size = W = input_size
         self.modes = M = modes
         self.content_activation = content_activation
         self.output_activation = output_activation
-        # the draws of _parameters (layers.py:86-115; initialization.py:5-39)
+        # the draws of _parameters (layers.py:17-58; initialization.py:5-39)
         frequency_log = torch.log(max_phase * torch.rand(M))
         u = torch.rand(M)
         decay_log = torch.log(-0.5 * torch.log(u * (r_max ** 2 - r_min ** 2) + r_min ** 2))
