@@ -10,7 +10,7 @@ from .mixer import (SPARCMixer, prepare_decode, run_decode_step, run_sequence, s
                     sparc_mixer)
 from .stack import SPARCBlock, SPARCStack
 from .projection import SPARCSequenceLayer, sparc_projection_states, sparc_sequence_layer
-from .rtrl import SPARCRTRLCell, initialize_carry, initialize_traces, rtrl_step
+from .rtrl import SPARCRTRLCell, initialize_carry, initialize_traces, rtrl_step, stored_rtrl_step
 from .real import real_chunk_scan, real_scan, real_scan_with_last
 from .scan import (sparc_chunk_scan, sparc_scan, sparc_scan_precomputed_decay, sparc_scan_with_last,
                    sparc_tiled_serial_scan, sparc_training_scan_dispatch)
@@ -38,7 +38,7 @@ def check_status(clear: bool = True) -> None:
 
 __all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack", "sparc_decode_step",
            "SPARCSequenceLayer", "sparc_sequence_layer", "sparc_projection_states",
-           "SPARCRTRLCell", "rtrl_step", "initialize_carry", "initialize_traces",
+           "SPARCRTRLCell", "rtrl_step", "stored_rtrl_step", "initialize_carry", "initialize_traces",
            "real_scan", "real_chunk_scan", "real_scan_with_last", "sparc_scan", "sparc_chunk_scan",
            "sparc_scan_with_last", "sparc_tiled_serial_scan", "sparc_training_scan_dispatch",
            "sparc_scan_precomputed_decay", "run_sequence", "prepare_decode", "run_decode_step", "check_status",

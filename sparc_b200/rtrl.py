@@ -138,6 +138,10 @@ def rtrl_step(params, carry, inputs: torch.Tensor, reset=None, content_activatio
     return next_carry, new_state
 
 
+# the reference's name (training/rtrl.py:111-116): (parameters, carry, inputs, reset, content_activation)
+stored_rtrl_step = rtrl_step
+
+
 class SPARCRTRLCell(nn.Module):
     """Torch counterpart of ``SPARCRTRLCell`` (sparc-impl/sparc/layers.py:61-85):
     ``forward(carry, inputs, reset) -> (next_carry, output)``, inputs [B, input_size]."""
