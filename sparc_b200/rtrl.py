@@ -28,7 +28,7 @@ CONTROLLER_NAMES = ("phase_controller", "retention_controller")
 TRACE_NAMES = MODAL_NAMES + CONTENT_NAMES + CONTROLLER_NAMES
 
 
-def initialize_traces(batch_size: int, input_size: int, modes: int, device=None, dtype=torch.complex64):
+def initialize_traces(batch_size: int, input_size: int, modes: int, dtype=torch.complex64, device=None):
     """Zero traces, rtrl.py:25-41."""
     tr = {n: torch.zeros((batch_size, modes), dtype=dtype, device=device) for n in MODAL_NAMES}
     tr.update({n: torch.zeros((batch_size, input_size, modes), dtype=dtype, device=device)
@@ -38,10 +38,10 @@ def initialize_traces(batch_size: int, input_size: int, modes: int, device=None,
     return tr
 
 
-def initialize_carry(batch_size: int, input_size: int, modes: int, device=None, dtype=torch.complex64):
+def initialize_carry(batch_size: int, input_size: int, modes: int, dtype=torch.complex64, device=None):
     """(zero state [B, M], zero traces), rtrl.py:44-46."""
     return (torch.zeros((batch_size, modes), dtype=dtype, device=device),
-            initialize_traces(batch_size, input_size, modes, device, dtype))
+            initialize_traces(batch_size, input_size, modes, dtype, device))
 
 
 def _rtrl_check(rc: int, what: str):
@@ -171,12 +171,14 @@ class SPARCRTRLCell(nn.Module):
         self.write_phase_response = nn.Parameter(torch.zeros(M))
         self.write_retention_response = nn.Parameter(torch.zeros(M))
 
-    def initial_carry(self, batch_size: int, input_size: int | None = None, device=None,
-                      dtype=torch.complex64):
+    def initial_carry(self, batch_size: int, input_size: int | None = None, dtype=torch.complex64,
+                      device=None):
+        """(zero state, zero traces) with the reference's argument order (layers.py:84-85:
+        batch_size, input_size, dtype); on the cell's device unless `device` is given."""
         if device is None:
             device = self.decay_log.device
         return initialize_carry(batch_size, self.input_size if input_size is None else input_size,
-                                self.modes, device, dtype)
+                                self.modes, dtype, device)
 
     def forward(self, carry, inputs: torch.Tensor, reset=None):
         if inputs.shape[-1] != self.input_size:

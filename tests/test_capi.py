@@ -221,3 +221,27 @@ def test_state_dict_round_trips_with_the_reference_layout(golden):
     m2.load_state_dict(torch.load(buf), strict=True)
     for k, v in ref_sd.items():
         np.testing.assert_array_equal(m2.state_dict()[k].numpy(), v.numpy(), err_msg=k)
+
+
+def test_rtrl_carry_api_matches_reference():
+    """initialize_traces / initialize_carry (training/rtrl.py:25-46) and SPARCRTRLCell.initial_carry
+    (layers.py:84-85) take the reference's positional arguments (..., dtype) and build the same
+    shapes: modal traces [B, M], content [B, W, M], controllers [B, W + 1, M], complex64."""
+    import inspect
+
+    import torch
+
+    import sparc_b200
+    from sparc_b200 import rtrl
+
+    assert list(inspect.signature(rtrl.initialize_traces).parameters)[:4] == ["batch_size", "input_size", "modes", "dtype"]
+    assert list(inspect.signature(rtrl.initialize_carry).parameters)[:4] == ["batch_size", "input_size", "modes", "dtype"]
+    state, tr = sparc_b200.initialize_carry(2, 3, 4, torch.complex128)
+    assert state.shape == (2, 4) and state.dtype == torch.complex128
+    shapes = {n: tuple(t.shape) for n, t in tr.items()}
+    assert shapes["decay_log"] == (2, 4) and shapes["content_real"] == (2, 3, 4) and shapes["phase_controller"] == (2, 4, 4)
+    assert set(shapes) == set(rtrl.TRACE_NAMES) and len(shapes) == 9
+    cell = sparc_b200.SPARCRTRLCell(3, 4)
+    assert list(inspect.signature(cell.initial_carry).parameters)[:3] == ["batch_size", "input_size", "dtype"]
+    s2, tr2 = cell.initial_carry(2, 3, torch.complex64)
+    assert s2.dtype == torch.complex64 and tr2["retention_controller"].shape == (2, 4, 4)
