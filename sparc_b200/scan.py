@@ -18,7 +18,7 @@ nu_log, theta_log and the initial state.
 
 Domain: |eta| < ln 16 and |delta| < pi/2, the range of the reference's controller
 (forward/control.py:129-139: eta = ln16 tanh(p1), delta = (pi/2) tanh(p0)); values at or beyond
-it are clamped to the last float32 below the bound (and get no gradient there).
+it are clamped to (1 - 2^-23) times the bound (and get no gradient there).
 """
 from __future__ import annotations
 
@@ -30,7 +30,7 @@ from . import _lib
 
 LN16 = math.log(16.0)
 HALF_PI = 0.5 * math.pi
-_EDGE = 1.0 - 2.0 ** -23  # the largest float32 below 1 that atanh maps to a finite value
+_EDGE = 1.0 - 2.0 ** -23  # a float32 just below 1, where atanh is still finite (about 8.3)
 
 
 def _io_dtype(dtype: torch.dtype) -> torch.dtype:
