@@ -18,7 +18,7 @@ nu_log, theta_log and the initial state.
 
 Domain: |eta| < ln 16 and |delta| < pi/2, the range of the reference's controller
 (forward/control.py:129-139: eta = ln16 tanh(p1), delta = (pi/2) tanh(p0)); values at or beyond
-it are clamped to (1 - 2^-23) times the bound (and get no gradient there).
+it are clamped to (1 - 2^-23) times the bound (and get no gradient there); the writes stay b.
 """
 from __future__ import annotations
 
@@ -41,11 +41,11 @@ def _projection_inputs(eta, delta, nu_log, br, bi):
     """(u [B, L, 2M], p [B, L, 2] float32): the content input and controller projections for
     which the projection-mode kernels compute the scan with controls (eta, delta) and writes
     (br, bi). Differentiable in every argument."""
-    ef, df = eta.float(), delta.float()
-    p = torch.stack((torch.atanh((df / HALF_PI).clamp(-_EDGE, _EDGE)),
-                     torch.atanh((ef / LN16).clamp(-_EDGE, _EDGE))), dim=-1)
+    x0 = (delta.float() / HALF_PI).clamp(-_EDGE, _EDGE)  # tanh(p0), tanh(p1) as the kernels will form them
+    x1 = (eta.float() / LN16).clamp(-_EDGE, _EDGE)
+    p = torch.stack((torch.atanh(x0), torch.atanh(x1)), dim=-1)
     nu = torch.exp(nu_log.float())
-    z = nu * torch.exp(ef)[..., None]
+    z = nu * torch.exp(LN16 * x1)[..., None]  # (the clamped eta, so the writes are b also at the bound)
     s = torch.sqrt(torch.expm1(-2.0 * z) / torch.expm1(-2.0 * nu))
     u = torch.cat((br.float() / s, bi.float() / s), dim=-1).to(_io_dtype(br.dtype))
     return u, p

@@ -250,3 +250,28 @@ def test_module_level_aliases(standin, golden):
     assert m._inference_fused
     with pytest.raises(RuntimeError, match="CUDA"):
         sparc_b200.run_decode_step(m, torch.randn(2, 8), (torch.zeros(2, 4), torch.zeros(2, 4)), None)
+
+
+def test_controls_at_and_beyond_the_bound(standin):
+    """eta at or beyond ln16 (delta beyond pi/2) is clamped to just inside the bound: finite
+    states and gradients, the writes kept exactly, the transition of the clamped controls."""
+    B, L, M = 1, 6, 3
+    eta = torch.tensor([[LN16, -LN16, 5.0, 0.3, -9.0, 0.0]], requires_grad=True)
+    delta = torch.tensor([[HALF_PI, 2.0, -HALF_PI, 0.1, 0.0, -3.0]], requires_grad=True)
+    nl, tl = torch.full((M,), -1.0), torch.full((M,), 0.2)
+    br, bi = torch.randn(B, L, M), torch.randn(B, L, M)
+    out_r, out_i = standin.sparc_scan(eta, delta, nl, tl, br, bi)
+    assert bool(torch.isfinite(out_r).all()) and bool(torch.isfinite(out_i).all())
+    edge = 1.0 - 2.0 ** -23
+    ec = (eta.detach().double() / LN16).clamp(-edge, edge) * LN16
+    dc = (delta.detach().double() / HALF_PI).clamp(-edge, edge) * HALF_PI
+    P = O.Params.from_mapping({"nu_log": nl.double().numpy(), "theta_log": tl.double().numpy()} | {
+        k: np.zeros(2 * M + 1 if "direction" in k else M) for k in ("phase_direction", "radial_direction",
+                                                                    "write_log_gain", "energy_response",
+                                                                    "write_phase_response", "write_radial_response")})
+    ar, ai, _, _ = O.transition(ec.numpy(), dc.numpy(), P)
+    hr, hi = O._scan(ar, ai, br.double().numpy(), bi.double().numpy())
+    assert O.rel_l2(out_r.detach().double().numpy(), hr) < 1e-5 and O.rel_l2(out_i.detach().double().numpy(), hi) < 1e-5
+    (out_r.sum() + out_i.sum()).backward()
+    assert bool(torch.isfinite(eta.grad).all()) and bool(torch.isfinite(delta.grad).all())
+    assert float(eta.grad[0, 2]) == 0.0 and float(delta.grad[0, 5]) == 0.0  # clamped: no gradient
