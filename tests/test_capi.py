@@ -245,3 +245,27 @@ def test_rtrl_carry_api_matches_reference():
     assert list(inspect.signature(cell.initial_carry).parameters)[:3] == ["batch_size", "input_size", "dtype"]
     s2, tr2 = cell.initial_carry(2, 3, torch.complex64)
     assert s2.dtype == torch.complex64 and tr2["retention_controller"].shape == (2, 4, 4)
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """Without the built library every entry point raises (no CPU or Python fallback): a fresh
+    process whose loader points at a missing file."""
+    import subprocess
+    import sys
+
+    code = ("import torch, sparc_b200\n"
+            "from sparc_b200 import _lib\n"
+            f"_lib.LIB_PATH = {str(tmp_path / 'missing.so')!r}\n"
+            "_lib.load_library.__defaults__ = (_lib.LIB_PATH,)\n"
+            "try:\n"
+            "    sparc_b200.real_scan_with_last(torch.rand(1, 4, 3), torch.rand(1, 4, 3))\n"
+            "except RuntimeError as e:\n"
+            "    print('raised:', e)\n"
+            "try:\n"
+            "    _lib.lib()\n"
+            "except RuntimeError as e:\n"
+            "    print('raised:', e)\n")
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("raised:")]
+    assert len(lines) == 2 and "missing" in lines[1] and "no CPU or Python fallback" in lines[1]
