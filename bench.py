@@ -578,10 +578,57 @@ def run_real(args, wl, world, rank, local):
     ms = total_ms / args.steps
     peak, kind = measured_peaks()
     byts = 16 * D * B * T
-    roofline = {"bound": "hbm", "achieved": round(byts / (ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(byts / (ms / 1e3) / 1e9 / peak, 4), "traffic": None, "kernel": "fwd+bwd",
-                "peak_source": kind}
-    return dict(value=B * T * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=None, cpu=None,
+    # per-kernel device time from the library's CUDA-event timing, same inputs (larger than L2):
+    # forward 3 D s bytes per token (read a, b; write out), backward 5 D s (read a, b, grad_out;
+    # write grad_a, grad_b); the line's roofline is the dominant kernel's
+    from sparc_b200 import _lib
+
+    L = _lib.lib()
+    torch.cuda.synchronize(device)
+    L.sparc_timing_enable(1)
+    _lib.kernel_times(reset_only=True)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize(device)
+    times = _lib.kernel_times()
+    L.sparc_timing_enable(0)
+    kbytes = {"real_fwd_kernel": 3 * 2 * D * B * T, "real_bwd_kernel": 5 * 2 * D * B * T}
+    kern = {}
+    for name, (tot, cnt) in times.items():
+        kms = tot / cnt
+        kb = kbytes.get(name)
+        kern[name] = {"ms": round(kms, 4), "launches_per_step": round(cnt / args.steps, 2), "algorithmic_bytes": kb,
+                      "GBps": round(kb / (kms / 1e3) / 1e9, 1) if kb else None}
+    dom = max((k for k in kern if kern[k]["GBps"]), key=lambda k: kern[k]["ms"])
+    achieved = kern[dom]["GBps"]
+    traffic = profile_traffic(dom, f"real_b{B}_t{T}_c{D}_bf16")
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": traffic, "kernel": dom, "peak_source": kind, "kernels": kern,
+                "step_frac": round(byts / (ms / 1e3) / 1e9 / peak, 4)}
+    # end to end through real_chunk_scan: a, b and grad_out copied from pinned host memory every step,
+    # out's sum read back (the host link bounds it: 6 bytes per element cross PCIe)
+    ah, bh, gh = (t.detach().cpu().pin_memory() for t in (a, b, g))
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    ad, bd, gd = torch.empty_like(a), torch.empty_like(b), torch.empty_like(g)
+
+    def e2e_step():
+        ad.copy_(ah, non_blocking=True)
+        bd.copy_(bh, non_blocking=True)
+        gd.copy_(gh, non_blocking=True)
+        aa = ad.detach().requires_grad_(True)
+        bb = bd.detach().requires_grad_(True)
+        out = sparc_b200.real_chunk_scan(aa, bb, 128)
+        out.backward(gd)
+        loss_h.copy_(out.detach().float().sum(), non_blocking=True)
+
+    e2e_step()
+    e_steps = max(2, min(args.steps, 5))
+    e_ms, _ = _time_steps(e2e_step, e_steps, lambda: None, world, device)
+    e_ms /= e_steps
+    e2e = {"value": round(B * T * world / (e_ms / 1e3), 1), "unit": "tokens/s",
+           "h2d_bytes_per_step": 3 * 2 * B * T * D, "d2h_bytes_per_step": 4, "ms_per_step": round(e_ms, 4),
+           "path": "real_chunk_scan forward/backward from pinned host a, b, grad_out"}
+    return dict(value=B * T * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=e2e, cpu=None,
                 clocks=clocks.summary(), launches=2 * args.steps, per_step_ms=per, tokens_step=B * T * world)
 
 

@@ -206,10 +206,13 @@ typedef struct SparcDecodeArgs {
   int dtype;
 } SparcDecodeArgs;
 
-/* Real diagonal scan h_t = a_t h_{t-1} + b_t over [batch, length, channels] (a, b, out in
- * dtype; carries float32). `carry` ([batch, sparc_real_carry_chunks(length), channels]
- * float32) receives the state at the end of each chunk for the backward; `last` ([batch,
- * channels] float32) is optional. */
+/* Real diagonal scan h_t = a_t h_{t-1} + b_t over [batch, length, channels]
+ * (backward/scan.py:793-884, 1643-1650, 1821-1834; kernels forward/scan.py:622-698,
+ * backward/scan.py:35-128). As in the reference, a is read in its own dtype `a_dtype` and
+ * widened to float32, b and out are in `dtype` (b's), and the recurrence and its carries are
+ * float32; the backward writes grad_a in a_dtype and reads grad_out / writes grad_b in dtype.
+ * `carry` ([batch, sparc_real_carry_chunks(length), channels] float32) receives the state at
+ * the end of each chunk for the backward; `last` ([batch, channels] float32) is optional. */
 typedef struct SparcRealFwdArgs {
   const void* a;
   const void* b;
@@ -221,7 +224,8 @@ typedef struct SparcRealFwdArgs {
   long long batch;
   long long length;
   long long channels;
-  int dtype;
+  int dtype;                           /* b and out */
+  int a_dtype;                         /* a */
   unsigned max_spin;
   int inject_enable;                   /* test hook: 1 = tile inject_tile never publishes */
   long long inject_tile;               /*   (its successor's bounded wait runs out) */
@@ -239,7 +243,8 @@ typedef struct SparcRealBwdArgs {
   long long batch;
   long long length;
   long long channels;
-  int dtype;
+  int dtype;                           /* b, grad_out and grad_b */
+  int a_dtype;                         /* a and grad_a */
   unsigned max_spin;
 } SparcRealBwdArgs;
 
@@ -261,21 +266,30 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* args, void* stream);
  * that cannot allocate device memory: for example a plugin bound through an FFI into a host
  * process whose own memory pool has already claimed the GPU, or a serving loop that must not
  * call cudaMalloc after start-up because it can block the whole device. Its scratch is a
- * fixed array of sparc_mixer_noalloc_scratch_bytes() (32 MiB) inside the library, which every
- * GPU that loads the library holds until the process exits; a problem that needs more
- * (roughly batch * ceil(length/C) * (width/2 rounded up to 256) * 18 bytes, C = 16 tokens for
- * bfloat16 and 8 for float32) is rejected with
- * SPARC_ERR_WORKSPACE and a message. The first call on a device looks up that device's copy of the array
- * (cudaGetSymbolAddress), so make it before any stream capture. All calls share the array:
- * calls whose executions overlap on the GPU (other streams, other host threads) race and must
- * be serialised by the caller. The caller still provides x, y, carry, controls and the
- * parameters. */
+ * fixed array of sparc_mixer_noalloc_scratch_bytes() (32 MiB) inside the library. The array
+ * belongs to the library's mixer module, so every GPU on which any mixer kernel of this
+ * library runs (through this entry point or any other) holds it until the process exits.
+ * A problem whose forward scratch, sparc_mixer_noalloc_scratch_needed(batch, length, width,
+ * dtype) bytes (a 256-byte header plus 16 bytes per (batch row, chunk of C tokens, mode) with
+ * the modes rounded up to whole 256-mode tiles; C = 16 for bfloat16, 8 for float32), is
+ * larger is rejected with SPARC_ERR_WORKSPACE and a message. The first call on a device looks
+ * up that device's copy of the array (cudaGetSymbolAddress), so make it before any stream
+ * capture. All calls share the array: calls whose executions overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller. The caller still
+ * provides x, y, carry, controls and the parameters.
+ * The array's status word (SPARC_STATUS_* bits; a timed-out wait of a tile kernel sets
+ * SPARC_STATUS_TIMEOUT) is sticky: it stays set for every later call on that device until
+ * sparc_mixer_noalloc_clear_status clears it. sparc_mixer_noalloc_read_status reads it (and
+ * synchronises `stream`); neither allocates. */
 size_t sparc_mixer_noalloc_scratch_bytes(void);
+size_t sparc_mixer_noalloc_scratch_needed(long long batch, long long length, int width, int dtype);
 int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* args, void* stream);
+int sparc_mixer_noalloc_read_status(unsigned* status, void* stream);
+int sparc_mixer_noalloc_clear_status(void* stream);
 
 int sparc_decode_step(const SparcDecodeArgs* args, void* stream);
 
-/* Tokens per saved carry of the real-mode scan (16); sparc_real_carry_chunks(length) is
+/* Tokens per saved carry of the real-mode scan (32); sparc_real_carry_chunks(length) is
  * ceil(length / sparc_real_chunk_tokens()). */
 long long sparc_real_chunk_tokens(void);
 long long sparc_real_carry_chunks(long long length);

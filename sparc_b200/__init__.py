@@ -7,7 +7,7 @@ All compute runs in the sm_100a kernels of ``libsparc_b200.so`` (C ABI in
 ``include/sparc_b200.h``), loaded through ctypes on first use. There is no CPU path.
 """
 from .mixer import (SPARCMixer, prepare_decode, run_decode_step, run_sequence, sparc_block, sparc_decode_step,
-                    sparc_mixer)
+                    sparc_eager_step, sparc_mixer)
 from .stack import SPARCBlock, SPARCStack
 from .projection import SPARCSequenceLayer, sparc_projection_states, sparc_sequence_layer
 from .rtrl import SPARCRTRLCell, initialize_carry, initialize_traces, rtrl_step, stored_rtrl_step
@@ -36,7 +36,7 @@ def check_status(clear: bool = True) -> None:
             raise RuntimeError(f"sparc_b200: a bounded wait in a kernel timed out (status {st:#x})")
 
 
-__all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack", "sparc_decode_step",
+__all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack", "sparc_decode_step", "sparc_eager_step",
            "SPARCSequenceLayer", "sparc_sequence_layer", "sparc_projection_states",
            "SPARCRTRLCell", "rtrl_step", "stored_rtrl_step", "initialize_carry", "initialize_traces",
            "real_scan", "real_chunk_scan", "real_scan_with_last", "sparc_scan", "sparc_chunk_scan",

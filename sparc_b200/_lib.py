@@ -75,7 +75,7 @@ class RealFwdArgs(ctypes.Structure):
     _fields_ = [
         ("a", _vp), ("b", _vp), ("out", _vp), ("last", _vp), ("carry", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
-        ("batch", _ll), ("length", _ll), ("channels", _ll), ("dtype", ctypes.c_int),
+        ("batch", _ll), ("length", _ll), ("channels", _ll), ("dtype", ctypes.c_int), ("a_dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint),
         ("inject_enable", ctypes.c_int), ("inject_tile", _ll),
     ]
@@ -85,7 +85,7 @@ class RealBwdArgs(ctypes.Structure):
     _fields_ = [
         ("a", _vp), ("b", _vp), ("grad_out", _vp), ("carry", _vp), ("grad_a", _vp), ("grad_b", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
-        ("batch", _ll), ("length", _ll), ("channels", _ll), ("dtype", ctypes.c_int),
+        ("batch", _ll), ("length", _ll), ("channels", _ll), ("dtype", ctypes.c_int), ("a_dtype", ctypes.c_int),
         ("max_spin", ctypes.c_uint),
     ]
 
@@ -134,7 +134,10 @@ SIGNATURES = {
     "sparc_mixer_forward": (ctypes.c_int, [ctypes.POINTER(MixerFwdArgs), _vp]),
     "sparc_mixer_backward": (ctypes.c_int, [ctypes.POINTER(MixerBwdArgs), _vp]),
     "sparc_mixer_noalloc_scratch_bytes": (ctypes.c_size_t, []),
+    "sparc_mixer_noalloc_scratch_needed": (ctypes.c_size_t, [_ll, _ll, ctypes.c_int, ctypes.c_int]),
     "sparc_mixer_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(MixerFwdArgs), _vp]),
+    "sparc_mixer_noalloc_read_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), _vp]),
+    "sparc_mixer_noalloc_clear_status": (ctypes.c_int, [_vp]),
     "sparc_decode_step": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
     "sparc_real_chunk_tokens": (_ll, []),
     "sparc_real_carry_chunks": (_ll, [_ll]),
@@ -228,8 +231,11 @@ class _Workspaces:
     def __init__(self):
         self._ws = {}
 
-    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
-        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    def get(self, device: torch.device, nbytes: int, kind: str = "mixer") -> torch.Tensor:
+        """`kind` keeps the real-mode scan's status words apart from the mixer's scratch: a
+        scan recognises the words of its own earlier launches by their epoch, not arbitrary
+        data another family of kernels left behind."""
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream, kind)
         ws = self._ws.get(key)
         if ws is None or ws.numel() < nbytes:
             size = max(nbytes, 1 << 20)

@@ -1103,6 +1103,34 @@ int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
   return run_forward(a, pl, L, ws, s);
 }
 
+size_t sparc_mixer_noalloc_scratch_needed(long long batch, long long length, int width, int dtype) {
+  // the largest forward scratch over the three modes (plain, block, projection)
+  size_t need = 0;
+  for (int mode = kModePlain; mode <= kModeProj; ++mode) {
+    Plan pl;
+    if (make_plan(batch, length, width, dtype, mode, &pl) != SPARC_OK) return 0;
+    need = std::max(need, ws_layout(pl, batch, width / 2).kout);
+  }
+  return need;
+}
+
+int sparc_mixer_noalloc_read_status(unsigned* status, void* stream) {
+  if (status == nullptr) { set_err("null pointer"); return SPARC_ERR_ARG; }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); set_err("no current CUDA device"); return SPARC_ERR_LAUNCH; }
+  const void* ws = noalloc_scratch(dev);
+  if (ws == nullptr) { set_err("cudaGetSymbolAddress failed for the built-in scratch"); return SPARC_ERR_LAUNCH; }
+  return sparc_read_status(ws, status, stream);
+}
+
+int sparc_mixer_noalloc_clear_status(void* stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); set_err("no current CUDA device"); return SPARC_ERR_LAUNCH; }
+  void* ws = noalloc_scratch(dev);
+  if (ws == nullptr) { set_err("cudaGetSymbolAddress failed for the built-in scratch"); return SPARC_ERR_LAUNCH; }
+  return sparc_clear_status(ws, stream);
+}
+
 int sparc_read_status(const void* workspace, unsigned* status, void* stream) {
   if (workspace == nullptr || status == nullptr) { set_err("null pointer"); return SPARC_ERR_ARG; }
   const LaunchState* ls = static_cast<const LaunchState*>(workspace);

@@ -169,16 +169,17 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> decode_step(
   return {y, nr, ni};
 }
 
-// real_scan / real_chunk_scan forward (backward/scan.py:793-884): (out, carry, last).
+// real_scan / real_chunk_scan forward (backward/scan.py:793-884): (out, carry, last). a keeps
+// its own dtype (widened to float32 in the kernel); out has b's dtype.
 std::tuple<at::Tensor, at::Tensor, at::Tensor> real_scan_forward(const at::Tensor& a_in, const at::Tensor& b_in) {
   TORCH_CHECK(a_in.is_cuda() && a_in.dim() == 3 && b_in.sizes() == a_in.sizes(),
               "real_scan_forward: a and b must be CUDA [batch, length, channels] tensors of one shape");
   c10::cuda::CUDAGuard guard(a_in.device());
-  const at::Tensor a = a_in.contiguous(), b = b_in.to(a.scalar_type()).contiguous();
+  const at::Tensor a = a_in.contiguous(), b = b_in.contiguous();
   const int64_t B = a.size(0), L = a.size(1), D = a.size(2);
-  const int dt = dtype_code(a);
+  const int dt = dtype_code(b), adt = dtype_code(a);
   auto fo = a.options().dtype(at::kFloat);
-  at::Tensor out = at::empty_like(a);
+  at::Tensor out = at::empty_like(b);
   at::Tensor carry = at::empty({B, sparc_real_carry_chunks(L), D}, fo);
   at::Tensor last = at::empty({B, D}, fo);
   const size_t wsb = sparc_real_workspace_bytes(B, L, D, dt);
@@ -196,21 +197,22 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> real_scan_forward(const at::Tenso
   r.length = L;
   r.channels = D;
   r.dtype = dt;
+  r.a_dtype = adt;
   check(sparc_real_scan_forward(&r, stream_of(a)), "sparc_real_scan_forward");
   return {out, carry, last};
 }
 
-// Its backward: (grad_a, grad_b).
+// Its backward: (grad_a in a's dtype, grad_b in b's).
 std::tuple<at::Tensor, at::Tensor> real_scan_backward(const at::Tensor& a_in, const at::Tensor& b_in,
                                                       const at::Tensor& g_in, const at::Tensor& carry) {
   TORCH_CHECK(a_in.is_cuda() && a_in.dim() == 3 && b_in.sizes() == a_in.sizes() && g_in.sizes() == a_in.sizes(),
               "real_scan_backward: a, b and grad_out must be CUDA [batch, length, channels] tensors of one shape");
   c10::cuda::CUDAGuard guard(a_in.device());
-  const at::Tensor a = a_in.contiguous(), b = b_in.to(a.scalar_type()).contiguous(),
-                   g = g_in.to(a.scalar_type()).contiguous(), cc = carry.contiguous();
+  const at::Tensor a = a_in.contiguous(), b = b_in.contiguous(), g = g_in.to(b.scalar_type()).contiguous(),
+                   cc = carry.contiguous();
   const int64_t B = a.size(0), L = a.size(1), D = a.size(2);
-  const int dt = dtype_code(a);
-  at::Tensor ga = at::empty_like(a), gb = at::empty_like(a);
+  const int dt = dtype_code(b), adt = dtype_code(a);
+  at::Tensor ga = at::empty_like(a), gb = at::empty_like(b);
   const size_t wsb = sparc_real_workspace_bytes(B, L, D, dt);
   TORCH_CHECK(wsb > 0, "real_scan_backward: unsupported shape (", sparc_last_error(), ")");
   at::Tensor ws = workspace(a, wsb);
@@ -227,6 +229,7 @@ std::tuple<at::Tensor, at::Tensor> real_scan_backward(const at::Tensor& a_in, co
   r.length = L;
   r.channels = D;
   r.dtype = dt;
+  r.a_dtype = adt;
   check(sparc_real_scan_backward(&r, stream_of(a)), "sparc_real_scan_backward");
   return {ga, gb};
 }

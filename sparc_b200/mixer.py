@@ -206,6 +206,28 @@ def sparc_decode_step(x: torch.Tensor, params, state):
     return y, (nr, ni)
 
 
+def sparc_eager_step(x: torch.Tensor, params, state):
+    """The reference's decode step before ``prepare_inference()`` (forward/decode.py:296-306): one
+    token of the sequence path, differentiable with respect to x, the state and every parameter.
+
+    It runs the mixer kernels on the length-1 sequence x[:, None] with the state as the initial
+    state, so its gradients are the sequence adjoint's (the write keeps float32 here, where the
+    reference rounds it to x's dtype first, forward/control.py:163: with bfloat16 activations the
+    two differ by that rounding, well inside the bfloat16 tolerance).
+    Returns (y [B, W] x.dtype, (new_r, new_i) [B, M] float32)."""
+    if x.dim() != 2:
+        raise ValueError("decode expects x of shape [batch, width]")
+    B, W = x.shape
+    if W % 2:
+        raise ValueError("SPARC rnn_width must be even")
+    M = W // 2
+    if tuple(state[0].shape) != (B, M) or tuple(state[1].shape) != (B, M):
+        raise ValueError("decode state must be a pair of [batch, width/2] tensors")
+    _lib.require_cuda(x, "x")
+    y, last = sparc_mixer(x[:, None].contiguous(), params, state=(state[0], state[1]))
+    return y[:, 0], last
+
+
 def run_sequence(module, x: torch.Tensor, return_cache: bool = False):
     """The reference's sequence entry as a function of the module (forward/scan.py:1398-1603,
     which its SPARCMixer.forward calls): module(x, return_cache)."""
@@ -302,5 +324,9 @@ class SPARCMixer(nn.Module):
         self._decode_backend = backend
 
     def step(self, x: torch.Tensor, state, segment_pos):
+        """forward/decode.py:273-306: after prepare_inference() the fused decode kernel (no
+        autograd, as the reference's latest_sparc_decode); before it the differentiable step."""
         del segment_pos  # ignored, as in forward/decode.py:274
-        return sparc_decode_step(x, self._params(), state)
+        if self._inference_fused:
+            return sparc_decode_step(x, self._params(), state)
+        return sparc_eager_step(x, self._params(), state)

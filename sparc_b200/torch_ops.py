@@ -92,14 +92,14 @@ def _register_python_kernels():
     @torch.library.register_fake("sparc_b200::real_scan_forward")
     def _(a, b):
         B, T, D = a.shape
-        return (torch.empty_like(a, memory_format=torch.contiguous_format),
+        return (torch.empty_like(b, memory_format=torch.contiguous_format),
                 a.new_empty((B, _ceil_div(T, L.sparc_real_chunk_tokens()), D), dtype=f32),
                 a.new_empty((B, D), dtype=f32))
 
     @torch.library.register_fake("sparc_b200::real_scan_backward")
     def _(a, b, grad_out, carry):
         return (torch.empty_like(a, memory_format=torch.contiguous_format),
-                torch.empty_like(a, memory_format=torch.contiguous_format))
+                torch.empty_like(b, memory_format=torch.contiguous_format))
 
     def mixer_setup(ctx, inputs, output):
         y, last_r, last_i, carry, controls = output

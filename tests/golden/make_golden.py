@@ -2,8 +2,9 @@
 
 Run from the repository root, in a container where the reference is mounted:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /path/to/reference
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /path/to/reference [case ...]
 
+(no case names: every case).
 It imports the reference package ``sparc-kernal`` read-only and runs:
 
 * its Triton kernels (the chunked SPARC scan, the tiled serial scan with h0/resets, the fused
@@ -168,6 +169,84 @@ def decode_case(sparc):
     np.savez_compressed(os.path.join(HERE, "decode.npz"), **rec)
 
 
+def decode_grad_case(sparc):
+    """The eager step before prepare_inference (forward/decode.py:296-306) is differentiable:
+    several steps with a carried state, loss = sum_s y_s . g_s + last . g_last, gradients of the
+    inputs, the initial state and every parameter; in float32, with bfloat16 activations (the
+    write is rounded to bfloat16 there, forward/control.py:163), and after module.double()."""
+    B, W, steps, seed = 3, 16, 5, 17
+    torch.manual_seed(seed)
+    base = sparc.SPARCMixer(W)
+    gen = torch.Generator().manual_seed(seed + 1000)
+    _randomize(base, gen)
+    state = {k: v.clone() for k, v in base.state_dict().items()}
+    M = W // 2
+    xs = torch.randn(steps, B, W, generator=gen)
+    gs = torch.randn(steps, B, W, generator=gen)
+    s0 = (torch.randn(B, M, generator=gen) * 0.5, torch.randn(B, M, generator=gen) * 0.5)
+    gl = (torch.randn(B, M, generator=gen), torch.randn(B, M, generator=gen))
+    rec = {"xs": _np(xs), "gs": _np(gs), "state0_r": _np(s0[0]), "state0_i": _np(s0[1]),
+           "g_last_r": _np(gl[0]), "g_last_i": _np(gl[1])}
+    for n in PARAMS:
+        rec["p_" + n] = _np(state[n])
+    for tag, x_dtype, p_dtype in (("f32", torch.float32, torch.float32),
+                                  ("bf16", torch.bfloat16, torch.float32),
+                                  ("f64", torch.float64, torch.float64)):
+        m = sparc.SPARCMixer(W)
+        m.load_state_dict(state)
+        m = m.to(p_dtype)
+        x = xs.to(x_dtype).clone().requires_grad_(True)
+        st = (s0[0].to(p_dtype).clone().requires_grad_(True), s0[1].to(p_dtype).clone().requires_grad_(True))
+        cur = st
+        loss = 0.0
+        ys = []
+        for k in range(steps):
+            y, cur = m.step(x[k], cur, None)
+            ys.append(y)
+            loss = loss + (y.to(torch.float64) * gs[k].to(torch.float64)).sum()
+        loss = loss + (cur[0].to(torch.float64) * gl[0].to(torch.float64)).sum() \
+            + (cur[1].to(torch.float64) * gl[1].to(torch.float64)).sum()
+        loss.backward()
+        rec[tag + "_xs"] = _np(x.detach())
+        rec[tag + "_ys"] = _np(torch.stack(ys))
+        rec[tag + "_last_r"], rec[tag + "_last_i"] = _np(cur[0]), _np(cur[1])
+        rec[tag + "_grad_xs"] = _np(x.grad)
+        rec[tag + "_grad_state0_r"], rec[tag + "_grad_state0_i"] = _np(st[0].grad), _np(st[1].grad)
+        for n in PARAMS:
+            g = getattr(m, n).grad
+            rec[tag + "_grad_" + n] = _np(g) if g is not None else np.zeros(getattr(m, n).shape)
+    np.savez_compressed(os.path.join(HERE, "decode_grad.npz"), **rec)
+
+
+def real_mixed_case(sparc):
+    """The real scans with float32 retention a and bfloat16 writes b: the reference loads a in its
+    own dtype and widens it (forward/scan.py:631), writes out in b's dtype and grad_a in a's
+    (backward/scan.py:815, 880). a is close to 1 over a long sequence, where rounding a to
+    bfloat16 would change the recurrence."""
+    from backward.scan import real_chunk_scan, real_scan, real_scan_with_last
+
+    B, L, D = 2, 512, 24
+    gen = torch.Generator().manual_seed(23)
+    a = 0.99 + 0.0099 * torch.rand(B, L, D, generator=gen)
+    b = (0.5 * torch.randn(B, L, D, generator=gen)).to(torch.bfloat16)
+    g = torch.randn(B, L, D, generator=gen).to(torch.bfloat16)
+    rec = {"a": _np(a), "b": _np(b), "g": _np(g)}
+    for name, fn in (("chunk16", lambda a_, b_: real_chunk_scan(a_, b_, 16)),
+                     ("serial", real_scan)):
+        aa = a.clone().requires_grad_(True)
+        bb = b.clone().requires_grad_(True)
+        out = fn(aa, bb)
+        out.backward(g)
+        rec[name + "_out"] = _np(out)
+        rec[name + "_out_is_bf16"] = np.array(int(out.dtype == torch.bfloat16))
+        rec[name + "_grad_a"] = _np(aa.grad)
+        rec[name + "_grad_a_is_f32"] = np.array(int(aa.grad.dtype == torch.float32))
+        rec[name + "_grad_b"] = _np(bb.grad)
+    out, last = real_scan_with_last(a, b)
+    rec["with_last_out"], rec["with_last_last"] = _np(out), _np(last)
+    np.savez_compressed(os.path.join(HERE, "real_mixed.npz"), **rec)
+
+
 def real_case(sparc):
     from backward.scan import real_chunk_scan, real_scan, real_scan_with_last
 
@@ -249,23 +328,32 @@ def tiled_case(sparc):
     np.savez_compressed(os.path.join(HERE, "tiled_h0_reset.npz"), **rec)
 
 
-def main(reference_root: str):
+CASES = {
+    "init": init_case,
+    "mixer": lambda sparc: (
+        mixer_case(sparc, "mixer_b2_t64_w16", 2, 64, 16, seed=1),
+        mixer_case(sparc, "mixer_b3_t37_w10", 3, 37, 10, seed=2),
+        mixer_case(sparc, "mixer_b2_t96_w64_c32", 2, 96, 64, seed=3, chunk_backend="chunk32"),
+        mixer_case(sparc, "mixer_bf16_b2_t64_w32", 2, 64, 32, seed=4, x_dtype=torch.bfloat16)),
+    "decode": decode_case,
+    "decode_grad": decode_grad_case,
+    "real": real_case,
+    "real_mixed": real_mixed_case,
+    "tiled": tiled_case,
+}
+
+
+def main(reference_root: str, cases=()):
     sys.path.insert(0, os.path.join(reference_root, "sparc-kernal"))
     import sparc  # the reference module
 
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    init_case(sparc)
-    mixer_case(sparc, "mixer_b2_t64_w16", 2, 64, 16, seed=1)
-    mixer_case(sparc, "mixer_b3_t37_w10", 3, 37, 10, seed=2)
-    mixer_case(sparc, "mixer_b2_t96_w64_c32", 2, 96, 64, seed=3, chunk_backend="chunk32")
-    mixer_case(sparc, "mixer_bf16_b2_t64_w32", 2, 64, 32, seed=4, x_dtype=torch.bfloat16)
-    decode_case(sparc)
-    real_case(sparc)
-    tiled_case(sparc)
+    for name in (cases or CASES):
+        CASES[name](sparc)
     print("golden vectors written to", HERE)
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <reference checkout root>")
-    main(sys.argv[1])
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference checkout root> [case ...]  (cases: " + ", ".join(CASES) + ")")
+    main(sys.argv[1], tuple(sys.argv[2:]))

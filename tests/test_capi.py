@@ -56,7 +56,7 @@ def test_host_only_queries(lib):
     assert lib.sparc_mixer_chunk_tokens(_lib.DTYPE_F32) == 8
     assert lib.sparc_mixer_carry_chunks(2048, _lib.DTYPE_BF16) == 128
     assert lib.sparc_mixer_carry_chunks(37, _lib.DTYPE_F32) == 5
-    assert lib.sparc_real_carry_chunks(17) == 2 and lib.sparc_real_chunk_tokens() == 16
+    assert lib.sparc_real_carry_chunks(33) == 2 and lib.sparc_real_chunk_tokens() == 32
     assert lib.sparc_mixer_controls_floats() == 16  # the per-token record the kernels write
     assert lib.sparc_mixer_mask_words(2048) == 64 and lib.sparc_mixer_mask_words(600) == 32
     assert lib.sparc_mixer_mask_words(7) == 0
@@ -123,26 +123,28 @@ def test_torch_operators_registered():
     assert "Tensor x" in schema and "Tensor write_radial_response" in schema
 
 
-def test_integration_stub_matches_the_header(lib):
-    """The ctypes stub INTEGRATION.md shows a maintainer has the header's struct layout and reads
-    error messages correctly (exec'd against the built library; no compute call is made)."""
+def test_integration_stub_matches_the_header(lib, monkeypatch):
+    """The ctypes stub a maintainer would add (tests/c_abi/sparc_ctypes_stub.py, quoted in the
+    integration guide) has the header's struct layout and reads error messages correctly (loaded
+    against the built library; no compute call is made)."""
     import ctypes
+    import importlib.util
 
     from sparc_b200 import _lib
 
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    block = next(b for b in re.findall(r"```python\n(.*?)```", text, flags=re.S) if "class SparcMixerFwdArgs" in b)
-    block = block.replace('ctypes.CDLL("libsparc_b200.so")', f"ctypes.CDLL({_lib.LIB_PATH!r})")
-    ns = {}
-    exec(compile(block, "INTEGRATION.md", "exec"), ns)
-    stub, ours = ns["SparcMixerFwdArgs"], _lib.MixerFwdArgs
+    monkeypatch.setenv("SPARC_B200_LIBRARY", _lib.LIB_PATH)
+    spec = importlib.util.spec_from_file_location(
+        "sparc_ctypes_stub", os.path.join(ROOT, "tests", "c_abi", "sparc_ctypes_stub.py"))
+    ns = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ns)
+    stub, ours = ns.SparcMixerFwdArgs, _lib.MixerFwdArgs
     assert [f[0] for f in stub._fields_] == [f[0] for f in ours._fields_]
     assert ctypes.sizeof(stub) == ctypes.sizeof(ours)
     for name, _ in ours._fields_:
         assert getattr(stub, name).offset == getattr(ours, name).offset, name
-    assert ns["lib"].sparc_mixer_forward(None, None) == -1  # SPARC_ERR_ARG
-    assert ns["lib"].sparc_last_error() == b"null args"
-    assert ns["lib"].sparc_mixer_carry_chunks(1 << 40, 0) == (1 << 40) // 8  # 64-bit return declared
+    assert ns.lib.sparc_mixer_forward(None, None) == -1  # SPARC_ERR_ARG
+    assert ns.lib.sparc_last_error() == b"null args"
+    assert ns.lib.sparc_mixer_carry_chunks(1 << 40, 0) == (1 << 40) // 8  # 64-bit return declared
 
 
 def test_header_compiles_as_c_and_cxx_and_the_c_host_links(lib, tmp_path):

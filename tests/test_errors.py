@@ -196,15 +196,18 @@ def test_decode_rejects(L, change, code, words):
     (dict(batch=0), SHAPE, "positive"),
     (dict(channels=-3), SHAPE, "positive"),
     (dict(dtype=2), DTYPE, "dtype"),
+    (dict(a_dtype=5), DTYPE, "dtype"),
 ])
 def test_real_scan_rejects(L, change, code, words):
-    f = _lib.RealFwdArgs(FAKE, FAKE, FAKE, None, FAKE, FAKE, 1 << 30, 2, 32, 3, _lib.DTYPE_F32, 0, 0, 0)
+    f = _lib.RealFwdArgs(FAKE, FAKE, FAKE, None, FAKE, FAKE, 1 << 30, 2, 32, 3, _lib.DTYPE_F32, _lib.DTYPE_F32,
+                         0, 0, 0)
     for k, v in change.items():
         setattr(f, k, v)
     assert L.sparc_real_scan_forward(ctypes.byref(f), None) == code
     assert words in _msg(L.sparc_last_error)
     bwd = {"a": "grad_a"}.get(next(iter(change)), next(iter(change)))
-    r = _lib.RealBwdArgs(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1 << 30, 2, 32, 3, _lib.DTYPE_F32, 0)
+    r = _lib.RealBwdArgs(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1 << 30, 2, 32, 3, _lib.DTYPE_F32,
+                         _lib.DTYPE_F32, 0)
     setattr(r, bwd, change[next(iter(change))])
     assert L.sparc_real_scan_backward(ctypes.byref(r), None) == code
     assert words in _msg(L.sparc_last_error)

@@ -96,7 +96,7 @@ def test_real_scan_stays_in_bounds(B, L, D, dtype):
     lb, last = _guarded((B, D), torch.float32)
     ws = torch.zeros(lib.sparc_real_workspace_bytes(B, L, D, dt), dtype=torch.uint8, device="cuda")
     f = _lib.RealFwdArgs(a.data_ptr(), b.data_ptr(), out.data_ptr(), last.data_ptr(), carry.data_ptr(),
-                         ws.data_ptr(), ws.numel(), B, L, D, dt, 0, 0, -1)
+                         ws.data_ptr(), ws.numel(), B, L, D, dt, dt, 0, 0, -1)
     assert lib.sparc_real_scan_forward(ctypes.byref(f), torch.cuda.current_stream().cuda_stream) == 0
     torch.cuda.synchronize()
     assert _intact(ob, dtype) and _intact(cb, torch.float32) and _intact(lb, torch.float32)
@@ -104,7 +104,7 @@ def test_real_scan_stays_in_bounds(B, L, D, dtype):
     gab, ga = _guarded((B, L, D), dtype)
     gbb, gb = _guarded((B, L, D), dtype)
     r = _lib.RealBwdArgs(a.data_ptr(), b.data_ptr(), g.data_ptr(), carry.data_ptr(), ga.data_ptr(), gb.data_ptr(),
-                         ws.data_ptr(), ws.numel(), B, L, D, dt, 0)
+                         ws.data_ptr(), ws.numel(), B, L, D, dt, dt, 0)
     assert lib.sparc_real_scan_backward(ctypes.byref(r), torch.cuda.current_stream().cuda_stream) == 0
     torch.cuda.synchronize()
     assert _intact(gab, dtype) and _intact(gbb, dtype)

@@ -254,6 +254,7 @@ def test_decode_matches_oracle_and_sequence(golden):
 def test_decode_bf16_large():
     params = _random_params(2048, 3)
     m = _module(params, 2048)
+    m.prepare_inference()  # the fused decode kernel
     gen = torch.Generator().manual_seed(1)
     x = torch.randn(256, 2048, generator=gen).to(torch.bfloat16)
     s = (torch.randn(256, 1024, generator=gen), torch.randn(256, 1024, generator=gen))

@@ -85,8 +85,9 @@ def test_real_large_split_property():
 def test_lookback_timeout_sets_status():
     """A real-scan tile that never publishes (host-chosen test hook) makes its successor's
     bounded lookback wait run out: the kernel records the timeout in the workspace status word,
-    the launch completes, and the context stays usable. (B=2, 256 tokens of 16-token chunks,
-    64 channels: two tiles per chunk, so ticket 4 is chunk 2 of row 0 and chunk 3 waits on it.)"""
+    the launch completes, and the context stays usable. (B=2, 256 tokens of 32-token chunks,
+    64 channels in one channel block: two tiles per chunk, so ticket 4 is chunk 2 of row 0 and
+    chunk 3 of row 0 waits on it.)"""
     import sparc_b200
     from sparc_b200 import _lib
     from sparc_b200.real import _forward
@@ -104,3 +105,111 @@ def test_lookback_timeout_sets_status():
     ref, _ = O.real_scan_forward(a.double().cpu().numpy(), b.double().cpu().numpy())
     assert O.rel_l2(out.double().cpu().numpy(), ref) < 1e-4
     assert _lib.STATUS_TIMEOUT == 1
+
+
+def test_golden_real_mixed_dtypes(golden):
+    """float32 retention a with bfloat16 writes b against the reference's own run: out and grad_b
+    in bfloat16, grad_a in float32, a read at full precision (the reference's grad_a takes
+    h_{t-1} from its bfloat16 output, so grad_a agrees to that rounding)."""
+    import sparc_b200
+
+    d = golden("real_mixed")
+    a = torch.tensor(d["a"], dtype=torch.float32, device="cuda")
+    b = torch.tensor(d["b"], dtype=torch.float32, device="cuda").to(torch.bfloat16)
+    g = torch.tensor(d["g"], dtype=torch.float32, device="cuda").to(torch.bfloat16)
+    o_ref, _ = O.real_scan_forward(d["a"], d["b"])
+    ga_ref, gb_ref = O.real_scan_backward(d["a"], d["b"], d["g"])
+    for fn, src in ((lambda a_, b_: sparc_b200.real_chunk_scan(a_, b_, 16), "chunk16"),
+                    (sparc_b200.real_scan, "serial")):
+        aa = a.clone().requires_grad_(True)
+        bb = b.clone().requires_grad_(True)
+        out = fn(aa, bb)
+        out.backward(g)
+        assert out.dtype == torch.bfloat16 and aa.grad.dtype == torch.float32 and bb.grad.dtype == torch.bfloat16
+        o, ga, gb = (t.detach().double().cpu().numpy() for t in (out, aa.grad, bb.grad))
+        assert O.rel_l2(o, d[src + "_out"]) < 1e-2
+        assert O.rel_l2(gb, d[src + "_grad_b"]) < 1e-2
+        assert O.rel_l2(ga, d[src + "_grad_a"]) < 2e-2
+        # against the float64 oracle on the same inputs
+        assert O.rel_l2(o, o_ref) < 4e-3 and O.rel_l2(gb, gb_ref) < 4e-3 and O.rel_l2(ga, ga_ref) < 4e-3
+    _, last = sparc_b200.real_scan_with_last(a, b)
+    assert O.rel_l2(last.double().cpu().numpy(), d["with_last_last"]) < 1e-5
+
+
+def test_real_mixed_dtypes_long_sequence():
+    """a near 0.999 in float32 with bfloat16 b over T = 8192: the float32 retention decides the
+    recurrence (rounding a to bfloat16 changes the last state by percents), against the float64
+    oracle."""
+    import sparc_b200
+
+    B, L, D = 2, 8192, 64
+    gen = torch.Generator().manual_seed(3)
+    a = 0.998 + 0.0019 * torch.rand(B, L, D, generator=gen)
+    b = (0.5 * torch.randn(B, L, D, generator=gen)).to(torch.bfloat16)
+    g = torch.randn(B, L, D, generator=gen).to(torch.bfloat16)
+    aa = a.cuda().requires_grad_(True)
+    bb = b.cuda().requires_grad_(True)
+    out = sparc_b200.real_scan(aa, bb)
+    out.backward(g.cuda())
+    _, last = sparc_b200.real_scan_with_last(a.cuda(), b.cuda())
+    o_ref, last_ref = O.real_scan_forward(a.double().numpy(), b.double().numpy())
+    ga_ref, gb_ref = O.real_scan_backward(a.double().numpy(), b.double().numpy(), g.double().numpy())
+    assert O.rel_l2(last.double().cpu().numpy(), last_ref) < 1e-4
+    assert O.rel_l2(out.detach().double().cpu().numpy(), o_ref) < 2e-2
+    assert O.rel_l2(aa.grad.double().cpu().numpy(), ga_ref) < 1e-3
+    assert O.rel_l2(bb.grad.double().cpu().numpy(), gb_ref) < 2e-2
+    _, last16 = O.real_scan_forward(a.to(torch.bfloat16).double().numpy(), b.double().numpy())
+    assert O.rel_l2(last16, last_ref) > 1e-2  # the precision the float32 retention keeps
+
+
+@pytest.mark.parametrize("D,slices", [(1024, [slice(0, 16), slice(1000, 1024)]),
+                                      (16384, [slice(0, 8), slice(8190, 8198), slice(16376, 16384)])])
+def test_real_config3_full_shape_vs_oracle(D, slices):
+    """Config 3 at its full shape (B=16, L=8192, bfloat16, sigmoid(a) over [0.9, 0.999]): the whole
+    forward and backward on the GPU, compared with the float64 oracle on slices of channels (the
+    channels are independent recurrences)."""
+    import sparc_b200
+
+    B, L = 16, 8192
+    gen = torch.Generator(device="cuda").manual_seed(D)
+    a = torch.sigmoid(torch.logit(0.9 + 0.099 * torch.rand(B, L, D, generator=gen, device="cuda"))).to(torch.bfloat16)
+    b = (0.5 * torch.randn(B, L, D, generator=gen, device="cuda")).to(torch.bfloat16)
+    g = torch.randn(B, L, D, generator=gen, device="cuda").to(torch.bfloat16)
+    aa = a.requires_grad_(True)
+    bb = b.requires_grad_(True)
+    out = sparc_b200.real_chunk_scan(aa, bb, 128)
+    out.backward(g)
+    sparc_b200.check_status()
+    for sl in slices:
+        an, bn, gn = (t.detach()[:, :, sl].double().cpu().numpy() for t in (a, b, g))
+        o_ref, _ = O.real_scan_forward(an, bn)
+        ga_ref, gb_ref = O.real_scan_backward(an, bn, gn)
+        assert O.rel_l2(out.detach()[:, :, sl].double().cpu().numpy(), o_ref) < 2e-2
+        assert O.rel_l2(aa.grad[:, :, sl].double().cpu().numpy(), ga_ref) < 2e-2
+        assert O.rel_l2(bb.grad[:, :, sl].double().cpu().numpy(), gb_ref) < 2e-2
+    del out, aa, bb
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("D", [8, 6, 5])
+def test_real_unaligned_rows_and_views(D):
+    """Rows that are not whole 16-byte units (D * 2 bytes for bfloat16) and tensors at an odd
+    element offset are staged without bulk copies; results equal the oracle."""
+    import sparc_b200
+
+    B, L = 3, 300
+    gen = torch.Generator().manual_seed(D)
+    base_a = (torch.rand(B * L * D + 1, generator=gen) * 0.5 + 0.45).to(torch.bfloat16).cuda().requires_grad_(True)
+    base_b = torch.randn(B * L * D + 1, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
+    a = base_a[1:].view(B, L, D)  # odd element offset: 2-byte aligned data
+    b = base_b[1:].view(B, L, D)
+    assert a.is_contiguous() and a.data_ptr() % 16 != 0
+    g = torch.randn(B, L, D, generator=gen).to(torch.bfloat16).cuda()
+    out = sparc_b200.real_scan(a, b)
+    ga, gb = torch.autograd.grad(out, (base_a, base_b), g)
+    an, bn = a.detach().double().cpu().numpy(), b.detach().double().cpu().numpy()
+    o_ref, _ = O.real_scan_forward(an, bn)
+    ga_ref, gb_ref = O.real_scan_backward(an, bn, g.double().cpu().numpy())
+    assert O.rel_l2(out.detach().double().cpu().numpy(), o_ref) < 2e-2
+    assert O.rel_l2(ga[1:].view(B, L, D).double().cpu().numpy(), ga_ref) < 2e-2
+    assert O.rel_l2(gb[1:].view(B, L, D).double().cpu().numpy(), gb_ref) < 2e-2

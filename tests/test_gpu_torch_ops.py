@@ -34,6 +34,7 @@ def test_mixer_and_decode_ops_match_module():
     for n, t in zip(names, grads[1:]):
         assert torch.equal(t, getattr(m, n).grad), n
     st = (torch.zeros(2, 32, device="cuda"), torch.zeros(2, 32, device="cuda"))
+    m.prepare_inference()  # the fused decode kernel, which decode_step registers
     yd, sd = m.step(x.detach()[:, 0], st, None)
     yd2, nr, ni = ops.decode_step(x.detach()[:, 0].contiguous(), st[0], st[1], *p)
     assert torch.equal(yd2, yd) and torch.equal(nr, sd[0]) and torch.equal(ni, sd[1])

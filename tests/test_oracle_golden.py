@@ -140,3 +140,62 @@ def test_init_matches_reference(golden):
     assert int(d["odd_raises"]) == 1
     with pytest.raises(ValueError):
         O.init_params(7, lambda n: np.zeros(n))
+
+
+def _step_chain_grads(d, xs):
+    """The oracle's adjoint of a chain of decode steps: the sequence scan over the steps with h0
+    = the initial state and the gradient of the last state."""
+    p = _params(d)
+    x = np.transpose(xs, (1, 0, 2))  # [B, steps, W]
+    dy = np.transpose(d["gs"], (1, 0, 2))
+    h0 = (d["state0_r"], d["state0_i"])
+    y, last, _ = O.sparc_forward(x, p, h0=h0)
+    g = O.sparc_backward(x, p, dy, h0=h0, grad_last=(d["g_last_r"], d["g_last_i"]))
+    return np.transpose(y, (1, 0, 2)), last, g
+
+
+@pytest.mark.parametrize("src,tol", [("f64", 2e-6), ("f32", 1e-5)])
+def test_eager_step_gradients(golden, src, tol):
+    """The reference's differentiable eager step (forward/decode.py:296-306) chained over several
+    steps: outputs, last state and the gradients of the inputs, the initial state and every
+    parameter match the oracle's sequence adjoint with h0 and grad of the last state."""
+    d = golden("decode_grad")
+    ys, last, g = _step_chain_grads(d, d["xs"])
+    assert O.rel_l2(ys, d[src + "_ys"]) < tol
+    assert O.rel_l2(last[0], d[src + "_last_r"]) < tol and O.rel_l2(last[1], d[src + "_last_i"]) < tol
+    assert O.rel_l2(np.transpose(g["x"], (1, 0, 2)), d[src + "_grad_xs"]) < tol
+    assert O.rel_l2(g["h0_r"], d[src + "_grad_state0_r"]) < tol
+    assert O.rel_l2(g["h0_i"], d[src + "_grad_state0_i"]) < tol
+    for k in GRAD_NAMES:
+        assert O.rel_l2(g[k], d[src + "_grad_" + k]) < 3 * tol, k
+
+
+def test_eager_step_bf16_within_tolerance(golden):
+    """With bfloat16 activations the reference rounds the write to bfloat16 (forward/control.py:163);
+    its step then sits within the bf16 tolerance of the oracle on the same bf16 inputs."""
+    d = golden("decode_grad")
+    ys, last, g = _step_chain_grads(d, d["bf16_xs"])
+    assert O.rel_l2(ys, d["bf16_ys"]) < 2e-2
+    assert O.rel_l2(np.transpose(g["x"], (1, 0, 2)), d["bf16_grad_xs"]) < 2e-2
+    for k in GRAD_NAMES:
+        assert O.rel_l2(g[k], d["bf16_grad_" + k]) < 2e-2, k
+
+
+@pytest.mark.parametrize("src", ["chunk16", "serial"])
+def test_real_scan_mixed_dtypes(golden, src):
+    """float32 retention with bfloat16 writes: the reference widens a from its own dtype, writes
+    out (and grad_b) in b's dtype and grad_a in a's."""
+    d = golden("real_mixed")
+    out, last = O.real_scan_forward(d["a"], d["b"])
+    ga, gb = O.real_scan_backward(d["a"], d["b"], d["g"])
+    assert int(d[src + "_out_is_bf16"]) == 1 and int(d[src + "_grad_a_is_f32"]) == 1
+    assert O.rel_l2(out, d[src + "_out"]) < 4e-3        # out rounded to bfloat16
+    assert O.rel_l2(gb, d[src + "_grad_b"]) < 4e-3      # grad_b rounded to bfloat16
+    # grad_a = lambda_t h_{t-1}: the reference takes h_{t-1} from its bfloat16 output
+    assert O.rel_l2(ga, d[src + "_grad_a"]) < 1e-2
+    assert O.rel_l2(last, d["with_last_last"]) < 1e-5  # last state in float32
+    # rounding a to bfloat16 instead (what a same-dtype kernel would do) is far off
+    a16 = d["a"].astype(np.float32).view(np.uint32)
+    a16 = ((a16 + 0x7FFF + ((a16 >> 16) & 1)) & 0xFFFF0000).view(np.float32).astype(np.float64)
+    out16, last16 = O.real_scan_forward(a16, d["b"])
+    assert O.rel_l2(last16, d["with_last_last"]) > 1e-2
