@@ -217,7 +217,10 @@ def _oracle_rows(args):
 
     from oracle import sparc_oracle as O
 
-    x, g, params = args
+    seed, seq_len, width, params = args
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((1, seq_len, width))
+    g = rng.standard_normal((1, seq_len, width))
     with threadpool_limits(1):
         P = O.Params.from_mapping(params)
         y, _, _ = O.sparc_forward(x, P)
@@ -227,19 +230,17 @@ def _oracle_rows(args):
 
 class OraclePool:
     """Spawned worker processes that run the float64 oracle forward+backward, one batch row of
-    the layer workload per task (the pool starts before any timing and before GPU work)."""
+    the layer workload per task (each worker draws its row's x and g from the row's seed); a
+    round is every row of the batch (the pool starts before any timing and before GPU work)."""
 
     def __init__(self, batch, seq_len, width, workers, seed=0):
-        import numpy as np
         import torch
 
         from oracle import sparc_oracle as O
 
         torch.manual_seed(seed)
         params = O.init_params(width, lambda n: torch.rand(n).numpy())
-        rng = np.random.default_rng(seed)
-        self.rows = [(rng.standard_normal((1, seq_len, width)), rng.standard_normal((1, seq_len, width)), params)
-                     for _ in range(min(batch, workers))]
+        self.rows = [(seed * 1000003 + i, seq_len, width, params) for i in range(batch)]
         self.seq_len = seq_len
         self.ex = cf.ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn"))
         list(self.ex.map(_oracle_rows, self.rows[:1]))  # start the workers
@@ -820,11 +821,32 @@ def workload_config(workload: str, wl: dict, world: int) -> dict:
     return cfg
 
 
-def run_reference(args, wl):
+def line_config(args, wl: dict, world: int) -> dict:
+    """The JSON line's `config`, identical for both arms (the reference arm processes the same
+    global batch; how it runs is in its cpu_baseline block): the workload, its data-parallel
+    layout, how L2 is kept out of the timing and how steps are timed on the GPU arm."""
+    cfg = workload_config(args.workload, wl, world)
+    cfg["parallelism"] = f"dp{world}" if world > 1 else "single"
+    if world > 1:
+        cfg["gradient_exchange"] = {
+            "fused": "in the gradient reduction kernel over NVLink peer memory (CUDA IPC)",
+            "peer": "peer-memory all-reduce kernel (NVLink, CUDA IPC)",
+            "nccl": "NCCL all-reduce of the packed gradients"}[
+                args.allreduce if args.allreduce != "fused" or args.workload in ("layer", "layer5", "stack") else "peer"]
+    cfg["l2"] = ("flushed before every step (512 MiB write, outside the CUDA events)"
+                 if args.workload in ("layer", "projection") else "inputs larger than L2")
+    cfg["timing"] = ("per-step CUDA events, CUDA-graph replay"
+                     if args.workload in ("layer", "layer5", "decode", "projection", "projection16")
+                     else "per-step CUDA events")
+    return cfg
+
+
+def run_reference(args, wl, world=1):
     """The reference algorithm on the host cores: the float64 oracle restatement, one batch row
-    per process over all host cores; each step is one round over min(cores, batch) rows."""
+    per process over all host cores; each step is one round over the job's global batch
+    (per-GPU batch x ranks, the rows the GPU arm processes in one step)."""
     workers = os.cpu_count() or 1
-    B, T, W = wl["batch"], wl["seq_len"], wl["width"]
+    B, T, W = wl["batch"] * world, wl["seq_len"], wl["width"]
     pool = OraclePool(B, T, W, min(workers, B))
     times = []
     for i in range(args.warmup + args.steps):
@@ -872,15 +894,17 @@ def main():
         if args.workload != "layer":
             print(json.dumps({"impl": "reference", "unavailable": "reference arm covers the layer workload"}))
             return
-        value, ms, toks, cores = run_reference(args, wl)
+        value, ms, toks, cores = run_reference(args, wl, world)
         line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
                 "data": "synthetic", "impl": "reference",
-                "config": {**workload_config(args.workload, wl, world), "parallelism": "host cores"},
+                "config": line_config(args, wl, world),
                 "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-                                 "sample": f"{toks} tokens per step: {cores} batch rows of T={wl['seq_len']}, "
-                                           f"W={wl['width']}, float64 numpy oracle fwd+bwd, one row per process"},
+                                 "sample": f"{toks} tokens per step: {wl['batch'] * world} batch rows of "
+                                           f"T={wl['seq_len']}, W={wl['width']} (the job's global batch), float64 "
+                                           f"numpy oracle fwd+bwd on {cores} host cores, one row per process, "
+                                           f"wall clock per step"},
                 "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
@@ -891,23 +915,27 @@ def main():
               "decode": run_decode, "projection": run_projection, "projection16": run_projection,
               "rtrl": run_rtrl}[args.workload]
     r = runner(args, wl, world, rank, local)
+    # a bounded wait of the cross-GPU gradient exchange that ran out means wrong gradient sums:
+    # no number is published then (every rank learns of it through one collective)
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        bad = torch.tensor([int(any(x.timed_out() for x in _REDUCERS if hasattr(x, "timed_out")))],
+                           device=torch.device("cuda", local))
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        if int(bad.item()):
+            for x in _REDUCERS:
+                x.close()
+            dist.barrier()
+            dist.destroy_process_group()
+            raise RuntimeError("a gradient exchange's bounded wait for a peer ran out: the step's gradient sums "
+                               "are not valid, so no throughput is reported")
     if rank == 0:
         unit = "tokens/s"
-        cfg = workload_config(args.workload, wl, world)
-        cfg["parallelism"] = f"dp{world}" if world > 1 else "single"
-        if world > 1:
-            cfg["gradient_exchange"] = {
-                "fused": "in the gradient reduction kernel over NVLink peer memory (CUDA IPC)",
-                "peer": "peer-memory all-reduce kernel (NVLink, CUDA IPC)",
-                "nccl": "NCCL all-reduce of the packed gradients"}[
-                    args.allreduce if args.allreduce != "fused" or args.workload in ("layer", "layer5", "stack") else "peer"]
+        cfg = line_config(args, wl, world)
         if "chunk" in r:
-            cfg["chunk"] = r["chunk"]
-        cfg["l2"] = ("flushed before every step (512 MiB write, outside the CUDA events)"
-                     if args.workload in ("layer", "projection") else "inputs larger than L2")
-        cfg["timing"] = ("per-step CUDA events, CUDA-graph replay"
-                         if args.workload in ("layer", "layer5", "decode", "projection", "projection16")
-                         else "per-step CUDA events")
+            r["roofline"]["chunk"] = r["chunk"]
         line = {"metric": METRIC, "value": round(r["value"], 1), "unit": unit, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
                 "higher_is_better": True,

@@ -45,6 +45,10 @@ def _check_line(line, n_gpus, steps, warmup):
     want = bench.workload_config("layer", wl, n_gpus)
     assert {k: line["config"][k] for k in want} == want
     assert line["config"]["global_batch"] == 2 * n_gpus
+    # the same config our arm prints, and the sample covers the whole global batch
+    ns = bench.argparse.Namespace(workload="layer", allreduce="fused")
+    assert line["config"] == bench.line_config(ns, wl, n_gpus)
+    assert line["cpu_baseline"]["sample"].startswith(f"{2 * n_gpus * 64} tokens per step")
 
 
 def test_reference_arm_single_process():
@@ -88,7 +92,9 @@ def test_our_arm_line_assembly(monkeypatch, capsys):
     assert line["roofline"] == fake["roofline"] and line["e2e"] == fake["e2e"] and line["cpu_baseline"] == fake["cpu"]
     assert line["gpu_launches"] == 140 and line["clocks"] == fake["clocks"] and line["vs_baseline"] is None
     want = bench.workload_config("layer", bench.WORKLOADS["layer"], 1)
-    assert {k: line["config"][k] for k in want} == want and line["config"]["chunk"] == 8
+    assert {k: line["config"][k] for k in want} == want and line["roofline"]["chunk"] == 8
+    assert line["config"] == bench.line_config(bench.argparse.Namespace(workload="layer", allreduce="fused"),
+                                                bench.WORKLOADS["layer"], 1)
     assert line["config"]["global_batch"] == 8 and "l2" in line["config"] and line["config"]["parallelism"] == "single"
 
 
