@@ -92,6 +92,17 @@ extern "C" {
  * dy on the states and returns the content input's gradient in dx and the projections' in
  * grad_projections; the caller finishes x_in's and the matrices' gradients with the transposed
  * products. */
+/* Scan-level mode (projections given and content_linear == 2): the reference's scan-level
+ * functions (sparc_scan, sparc_chunk_scan, sparc_tiled_serial_scan, sparc_scan_with_last,
+ * sparc_training_scan_dispatch; backward/scan.py:922-1070, 1124-1372, 1658-1877, math at
+ * forward/scan.py:725-757), whose per-token controls and writes are given: projections holds
+ * (delta, eta) per token ([batch, length, 2] float32, any values), x the writes
+ * [b_r, b_i] ([batch, length, width]), and the recurrence is h_t = rho e^{i phi} h_{t-1} + b_t
+ * with rho = exp(-e^{nu_log} e^eta), phi = e^{theta_log} + (1 - rho) delta (no write gain; the
+ * write parameters are not read and their gradients come back zero). y receives the states
+ * [Re h, Im h] with no relu, or, with y_im given, Re h in y and Im h in y_im (each
+ * [batch, length, M]). The backward returns the writes' gradient in dx and (d delta, d eta)
+ * per token in grad_projections. */
 typedef struct SparcMixerFwdArgs {
   const void* x;                       /* [batch, length, width]  activations (dtype) */
   void* y;                             /* [batch, length, width]  output (dtype) */
@@ -113,7 +124,8 @@ typedef struct SparcMixerFwdArgs {
   float norm_eps;                      /* block: RMSNorm epsilon */
   unsigned* relu_mask;                 /* block: [batch, length, sparc_mixer_mask_words(width)] out */
   const float* projections;            /* [batch, length, 2]: projection mode (above), or NULL */
-  int content_linear;                  /* projection mode: content u instead of tanh(u) */
+  int content_linear;                  /* projection mode: 1 = content u instead of tanh(u);
+                                          2 = the scan-level mode (above) */
   void* workspace;
   size_t workspace_bytes;
   long long batch;
@@ -121,6 +133,8 @@ typedef struct SparcMixerFwdArgs {
   int width;
   int dtype;                           /* SPARC_DTYPE_* */
   unsigned max_spin;                   /* bound of the TMA waits (0 = default) */
+  void* y_im;                          /* scan-level mode: Im h [batch, length, M] out (y then
+                                          holds Re h [batch, length, M]), or NULL */
 } SparcMixerFwdArgs;
 
 /* Backward of sparc_mixer_forward for the loss gradient dy on y (and optionally grad_last on
@@ -160,7 +174,7 @@ typedef struct SparcMixerBwdArgs {
   float* grad_write_phase_response;    /* [M] */
   float* grad_write_radial_response;   /* [M] */
   float* grad_projections;             /* projection mode: [batch, length, 2] out, else NULL */
-  int content_linear;                  /* projection mode: as given to the forward */
+  int content_linear;                  /* projection / scan-level mode: as given to the forward */
   void* exchange_buffers[8];           /* data parallelism: every rank's exchange buffer (below) */
   int exchange_world;                  /* > 1: the parameter gradients are summed over the ranks */
   int exchange_rank;

@@ -50,15 +50,42 @@ constexpr int kModeBlock = 1;  // y = x + relu(SPARC(RMSNorm(x))) (a pre-norm re
 constexpr int kModeProj = 2;   // h = SPARC states from a content input u [B, T, 2M] and given
                                // per-token controller projections p [B, T, 2] (the projection
                                // variant: u = x Wc and p = [x, 1] c come from matrix products)
+constexpr int kModeScan = 3;   // h = SPARC states from given per-token controls (delta, eta)
+                               // [B, T, 2] and writes b [B, T, 2M] (the reference's scan-level
+                               // functions, sparc_scan and its kin): unit write gain, any eta and
+                               // delta (the rotation is range-reduced)
+// Modes whose output is the states themselves (no relu) from given per-token controls.
+template <int kMode>
+__host__ __device__ constexpr bool proj_like() { return kMode == kModeProj || kMode == kModeScan; }
 
 // Content of a token: tanh(u), or u itself for a projection-mode layer with a linear content
 // activation (lin, uniform over the launch).
 template <bool kFast, int kMode>
 __device__ __forceinline__ float2 content2(float2 u, bool lin) {
-  if constexpr (kMode == kModeProj) {
-    if (lin) return u;
+  if constexpr (kMode == kModeScan) {
+    return u;  // the write itself
+  } else {
+    if constexpr (kMode == kModeProj) {
+      if (lin) return u;
+    }
+    return tanh_t2<kFast>(u);
   }
-  return tanh_t2<kFast>(u);
+}
+
+// sin / cos of any float x by Cody and Waite's argument reduction: k = rint(x 2/pi),
+// r = x - k pi/2 with pi/2 split into three parts (c1, c2 exact in 12 bits, so k c1 and k c2 are
+// exact for |k| < 2^12; c3 the rest), |r| <= pi/4, then the series on [-pi/2, pi/2] and the
+// quadrant k mod 4. (The scan-level mode's phase offset (1 - rho) delta is unbounded.)
+__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+  const float k = rintf(x * 0.636619772f);
+  float r = fmaf(-k, 1.5703125f, x);
+  r = fmaf(-k, 4.8375129699707031e-4f, r);
+  r = fmaf(-k, 7.5497901264043321e-8f, r);
+  float sr, cr;
+  sincos_halfpi(r, &sr, &cr);
+  const int q = ((int)k) & 3;
+  *s = q == 0 ? sr : q == 1 ? cr : q == 2 ? -sr : -cr;
+  *c = q == 0 ? cr : q == 1 ? -sr : q == 2 ? -cr : sr;
 }
 
 struct ModeConst {
@@ -108,10 +135,14 @@ __device__ __forceinline__ ModeConst load_mode(const MixerParamPtrs& pp, int m, 
 // (1 - rho) delta (|.| <= pi/2) applied to the mode's e^{i theta}; 1 the hardware sin / cos of
 // the whole angle; 2 the hardware sin / cos of the offset (inside their accurate range) applied
 // to e^{i theta}.
-template <int kRot>
+template <int kRot, bool kScan = false>
 __device__ __forceinline__ float2 transition_rot(const ModeConst& mc, float rho, float delta) {
   float s, c;
-  if constexpr (kRot == 1) {
+  if constexpr (kScan) {  // any delta: the reduced offset applied to e^{i theta}
+    sincos_reduced(fmaf(-rho, delta, delta), &s, &c);
+    const float rct = rho * mc.ct, rst = rho * mc.st;
+    return make_float2(fmaf(rct, c, -rst * s), fmaf(rst, c, rct * s));
+  } else if constexpr (kRot == 1) {
     sincos_hw(fmaf(-rho, delta, delta) + mc.theta, &s, &c);
     return make_float2(rho * c, rho * s);
   } else {
@@ -181,14 +212,24 @@ struct TokenCoef2 {
 // kRot (see transition_rot): 1 the hardware sin / cos of the whole angle (MUFU pipe), 0 the
 // series of the bounded offset (FMA pipe), 2 the hardware sin / cos of the offset; by default
 // the fast path's choice (1 for bfloat16, 0 for float32).
-template <bool kFast, int kRot = kFast ? 1 : 0>
+template <bool kFast, int kRot = kFast ? 1 : 0, bool kScan = false>
 __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0,
                                                   float2 tau1, float2 keep) {
   TokenCoef2 k;
   k.z = mul2(mc.nu, E);
   k.rho = ex2_2(mul2(mc.nl2e_neg, E));
   const float2 rk = mul2(k.rho, keep);  // the transition's radius (0 at a reset)
-  if constexpr (kRot == 1) {
+  if constexpr (kScan) {
+    // scan-level mode: any delta (reduced offset), and the write is b itself (unit gain)
+    const float2 off = sub2(delta, mul2(k.rho, delta));
+    float2 sn, cs;
+    sincos_reduced(off.x, &sn.x, &cs.x);
+    sincos_reduced(off.y, &sn.y, &cs.y);
+    const float2 rct = mul2(rk, mc.ct), rst = mul2(rk, mc.st);
+    k.a = Cx2{sub2(mul2(rct, cs), mul2(rst, sn)), fma2(rst, cs, mul2(rct, sn))};
+    k.num = k.gate = k.gain = bcast2(1.0f);
+    return k;
+  } else if constexpr (kRot == 1) {
     const float2 ph = sub2(add2(delta, mc.theta), mul2(k.rho, delta));  // theta + (1 - rho) delta
     float2 sn, cs;
     sincos_hw(ph.x, &sn.x, &cs.x);
@@ -224,17 +265,17 @@ __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E
 }
 
 // The same from a saved controls record.
-template <bool kFast, int kRot = kFast ? 1 : 0>
+template <bool kFast, int kRot = kFast ? 1 : 0, bool kScan = false>
 __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, const TokenCtl& c) {
-  return token_coef2<kFast, kRot>(mc, make_float2(c.ed.x, c.ed.y), make_float2(c.ed.z, c.ed.w),
-                            make_float2(c.tau.x, c.tau.y), make_float2(c.tau.z, c.tau.w),
-                            make_float2(c.keep.x, c.keep.y));
+  return token_coef2<kFast, kRot, kScan>(mc, make_float2(c.ed.x, c.ed.y), make_float2(c.ed.z, c.ed.w),
+                                         make_float2(c.tau.x, c.tau.y), make_float2(c.tau.z, c.tau.w),
+                                         make_float2(c.keep.x, c.keep.y));
 }
 
 // Transition a = rho e^{i(theta + (1-rho) delta)} alone (the reverse local pass needs no write).
-template <bool kFast, int kRot = kFast ? 1 : 0>
+template <bool kFast, int kRot = kFast ? 1 : 0, bool kScan = false>
 __device__ __forceinline__ float2 token_transition(const ModeConst& mc, float E, float delta, float keep) {
-  const float2 a = transition_rot<kRot>(mc, ex2_approx(-mc.nl2e * E), delta);
+  const float2 a = transition_rot<kRot, kScan>(mc, ex2_approx(-mc.nl2e * E), delta);
   return make_float2(a.x * keep, a.y * keep);
 }
 
@@ -493,7 +534,7 @@ __global__ void __launch_bounds__(32 * kReduceWarps) mixer_reduce_kernel(const R
 // ------------------------------------------------------------------------------ host side
 struct Plan {
   int dtype, C, chunks;
-  int mode;                // kModePlain, kModeBlock or kModeProj
+  int mode;                // kModePlain, kModeBlock, kModeProj or kModeScan
   long long tiles;         // B * chunks
   int G, Mp;               // CTAs of 256 modes per tile; modes padded to G * 256
   bool vec, tma;
@@ -556,7 +597,7 @@ static int max_blocks(const void* kernel, int NT, size_t dyn_smem) {
 }
 
 // Kernel instances per activation type (bfloat16 uses the hardware tanh; float32 the accurate
-// one) and mode (kModePlain, kModeBlock, kModeProj).
+// one) and mode (kModePlain, kModeBlock, kModeProj, kModeScan).
 template <typename TIO>
 struct Kernels {
   static constexpr bool kFast = std::is_same<TIO, __nv_bfloat16>::value;
@@ -576,16 +617,20 @@ struct Kernels {
                : (const void*)mixer_bwd_grad_kernel<TIO, C, kFast, false, kM>;
   }
   static const void* sum(int mode) {
-    return mode == kModeBlock ? sum_m<kModeBlock>() : mode == kModeProj ? sum_m<kModeProj>() : sum_m<kModePlain>();
+    return mode == kModeBlock ? sum_m<kModeBlock>() : mode == kModeProj ? sum_m<kModeProj>()
+         : mode == kModeScan ? sum_m<kModeScan>() : sum_m<kModePlain>();
   }
   static const void* rep(bool vec, int mode) {
-    return mode == kModeBlock ? rep_m<kModeBlock>(vec) : mode == kModeProj ? rep_m<kModeProj>(vec) : rep_m<kModePlain>(vec);
+    return mode == kModeBlock ? rep_m<kModeBlock>(vec) : mode == kModeProj ? rep_m<kModeProj>(vec)
+         : mode == kModeScan ? rep_m<kModeScan>(vec) : rep_m<kModePlain>(vec);
   }
   static const void* rsum(int mode) {
-    return mode == kModeBlock ? rsum_m<kModeBlock>() : mode == kModeProj ? rsum_m<kModeProj>() : rsum_m<kModePlain>();
+    return mode == kModeBlock ? rsum_m<kModeBlock>() : mode == kModeProj ? rsum_m<kModeProj>()
+         : mode == kModeScan ? rsum_m<kModeScan>() : rsum_m<kModePlain>();
   }
   static const void* grad(bool vec, int mode) {
-    return mode == kModeBlock ? grad_m<kModeBlock>(vec) : mode == kModeProj ? grad_m<kModeProj>(vec) : grad_m<kModePlain>(vec);
+    return mode == kModeBlock ? grad_m<kModeBlock>(vec) : mode == kModeProj ? grad_m<kModeProj>(vec)
+         : mode == kModeScan ? grad_m<kModeScan>(vec) : grad_m<kModePlain>(vec);
   }
   static size_t sum_smem() { return sizeof(SumSmem<TIO, C>); }
   static size_t rep_smem() { return sizeof(RepSmem<TIO, C>); }
@@ -792,13 +837,14 @@ static int launch_error(cudaError_t e) {
 
 // The kernels' mode from which optional inputs are given (-1: both a norm weight and projections).
 static int fwd_mode(const SparcMixerFwdArgs* a) {
-  if (a->projections != nullptr) return a->norm_weight != nullptr ? -1 : kModeProj;
+  if (a->projections != nullptr)
+    return a->norm_weight != nullptr ? -1 : a->content_linear == 2 ? kModeScan : kModeProj;
   return a->norm_weight != nullptr ? kModeBlock : kModePlain;
 }
 
 // Validate the forward arguments and enqueue summary -> scan -> replay (scratch at `ws`).
 static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayout& L, char* ws, cudaStream_t s) {
-  const bool proj = pl.mode == kModeProj;
+  const bool proj = pl.mode == kModeProj || pl.mode == kModeScan;
   if (!a->x || !a->y || !a->carry || !a->controls || !a->nu_log || !a->theta_log ||
       (!proj && (!a->phase_direction || !a->radial_direction)) || !a->write_log_gain ||
       !a->write_phase_response || !a->write_radial_response) {
@@ -822,6 +868,10 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
                         a->write_radial_response};
   p.proj_in = reinterpret_cast<const float2*>(a->projections);
   p.content_linear = a->content_linear;
+  if (a->y_im != nullptr && pl.mode != kModeScan) {
+    set_err("y_im is an output of the scan-level mode only"); return SPARC_ERR_ARG;
+  }
+  p.y_im = a->y_im;
   p.h0_r = a->h0_r;
   p.h0_i = a->h0_i;
   p.ctl = reinterpret_cast<TokenCtl*>(a->controls);
@@ -877,7 +927,7 @@ long long sparc_mixer_carry_chunks(long long length, int dtype) {
 size_t sparc_mixer_workspace_bytes(long long batch, long long length, int width, int dtype) {
   // one size for every mode (their gradient kernels' occupancy may differ)
   size_t total = 0;
-  for (int mode = kModePlain; mode <= kModeProj; ++mode) {
+  for (int mode = kModePlain; mode <= kModeScan; ++mode) {
     Plan pl;
     if (make_plan(batch, length, width, dtype, mode, &pl) != SPARC_OK) return 0;
     total = std::max(total, ws_layout(pl, batch, width / 2).total);
@@ -916,7 +966,8 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   const bool block = a->norm_weight != nullptr;
   const bool proj = a->grad_projections != nullptr;
   if (block && proj) { set_err("norm_weight and grad_projections exclude each other"); return SPARC_ERR_ARG; }
-  int rc = make_plan(a->batch, a->length, a->width, a->dtype, proj ? kModeProj : block ? kModeBlock : kModePlain, &pl);
+  const int mode = proj ? (a->content_linear == 2 ? kModeScan : kModeProj) : block ? kModeBlock : kModePlain;
+  int rc = make_plan(a->batch, a->length, a->width, a->dtype, mode, &pl);
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
@@ -1106,7 +1157,7 @@ int sparc_mixer_forward_noalloc(const SparcMixerFwdArgs* a, void* stream) {
 size_t sparc_mixer_noalloc_scratch_needed(long long batch, long long length, int width, int dtype) {
   // the largest forward scratch over the three modes (plain, block, projection)
   size_t need = 0;
-  for (int mode = kModePlain; mode <= kModeProj; ++mode) {
+  for (int mode = kModePlain; mode <= kModeScan; ++mode) {
     Plan pl;
     if (make_plan(batch, length, width, dtype, mode, &pl) != SPARC_OK) return 0;
     need = std::max(need, ws_layout(pl, batch, width / 2).kout);

@@ -79,7 +79,8 @@ struct BwdParams {
 // ------------------------------------------------------------------------------ reverse summary
 template <typename TIO, int C, bool kFast, int kMode>
 __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __grid_constant__ BwdParams p) {
-  constexpr bool kBlock = kMode == kModeBlock, kProj = kMode == kModeProj;  // (projection mode: no relu)
+  constexpr bool kBlock = kMode == kModeBlock, kProj = proj_like<kMode>();  // (projection / scan modes: no relu)
+  constexpr bool kScan = kMode == kModeScan;
   const int g = blockIdx.x;
   const int tid = threadIdx.x;
   const int M = p.M, W = p.W;
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
           }
           q.x += on_r ? gr : 0.0f;
           q.y += on_i ? gi : 0.0f;
-          const float2 a = token_transition<kFast, bwd_rot<kFast>()>(mc, tc.ed.x, tc.ed.z, tc.keep.x);
+          const float2 a = token_transition<kFast, bwd_rot<kFast>(), kScan>(mc, tc.ed.x, tc.ed.z, tc.keep.x);
           q = make_float2(fmaf(a.x, q.x, a.y * q.y), fmaf(a.x, q.y, -a.y * q.x));
           P = cmul(a, P);
         }
@@ -233,12 +234,23 @@ __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& 
   const float2 delta = make_float2(tc.ed.z, tc.ed.w), tau0 = make_float2(tc.tau.x, tc.tau.y),
                tau1 = make_float2(tc.tau.z, tc.tau.w);
   // with a reset the transition (k.a) is zero, so every transition-gradient term below vanishes
-  const TokenCoef2 k = token_coef2<kFast, bwd_rot<kFast>()>(mc, tc);
+  constexpr bool kScan = kMode == kModeScan;
+  const TokenCoef2 k = token_coef2<kFast, bwd_rot<kFast>(), kScan>(mc, tc);
   const float2 gar = fma2(lam.re, pv.re, mul2(lam.im, pv.im));   // Re(lam conj(h_prev))
   const float2 gai = sub2(mul2(lam.im, pv.re), mul2(lam.re, pv.im));  // Im(lam conj(h_prev))
   const float2 pg = sub2(mul2(gai, k.a.re), mul2(gar, k.a.im));
   const float2 radial = mul2(k.z, sub2(mul2(mul2(k.rho, delta), pg), fma2(gar, k.a.re, mul2(gai, k.a.im))));
   const float2 dscan = sub2(pg, mul2(k.rho, pg));
+  if constexpr (kScan) {
+    // scan-level mode: the writes are inputs (unit gain), so only the transition's terms remain
+    ve = radial;
+    vd = dscan;
+    fa[0] = add2(fa[0], radial);
+    fa[1] = add2(fa[1], pg);
+    const Cx2 dxc = lam;  // the writes' gradient
+    lam = Cx2{fma2(k.a.re, lam.re, mul2(k.a.im, lam.im)), sub2(mul2(k.a.re, lam.im), mul2(k.a.im, lam.re))};
+    return dxc;
+  }
   const float2 cr = content2<kFast, kMode>(cx, lin);
   const float2 ci = content2<kFast, kMode>(cy, lin);
   const float2 gg = mul2(k.gain, fma2(lam.re, cr, mul2(lam.im, ci)));
@@ -266,7 +278,7 @@ __device__ __forceinline__ Cx2 grad_step2(const ModeConst2& mc, const TokenCtl& 
 template <typename TIO, int C, bool kFast, bool kVec, int kMode>
 __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const __grid_constant__ BwdParams p) {
   static_assert(C % kGroup == 0, "the reverse walk runs in groups of kGroup tokens");
-  constexpr bool kBlock = kMode == kModeBlock, kProj = kMode == kModeProj;
+  constexpr bool kBlock = kMode == kModeBlock, kProj = proj_like<kMode>(), kScan = kMode == kModeScan;
   const bool lin = kProj && p.content_linear != 0;
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
@@ -382,7 +394,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
           if (kFull || t < nvalid) {
             float2 nr, ni;
             mixer_in(t, Pair<TIO>::load(&S.x[t][0][2 * tid]), Pair<TIO>::load(&S.x[t][1][2 * tid]), nr, ni);
-            const TokenCoef2 k = token_coef2<kFast, bwd_rot<kFast>()>(mc, S.ctl[t]);
+            const TokenCoef2 k = token_coef2<kFast, bwd_rot<kFast>(), kScan>(mc, S.ctl[t]);
             h = cfma2(k.a, h, cx2(mul2(k.gain, content2<kFast, kMode>(nr, lin)), mul2(k.gain, content2<kFast, kMode>(ni, lin))));
             Pair<TIO>::store(&S.hr[t][2 * tid], h.re.x, h.re.y);
             Pair<TIO>::store(&S.hi[t][2 * tid], h.im.x, h.im.y);
@@ -492,8 +504,10 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       if (tid < C) {
         const TokenCtl& tc = S.ctl[tid];
         const float tau0 = tc.tau.x, tau1 = tc.tau.z;
-        const float dp1 = tid < nvalid ? S.tot[tid] * kLn16 * fmaf(-tau1, tau1, 1.0f) : 0.0f;
-        const float dp0 = tid < nvalid ? S.tot[C + tid] * kHalfPi * fmaf(-tau0, tau0, 1.0f) : 0.0f;
+        // d/dp of eta = ln16 tanh(p1), delta = pi/2 tanh(p0); the scan-level mode returns the
+        // gradients of (delta, eta) themselves
+        const float dp1 = tid < nvalid ? (kScan ? S.tot[tid] : S.tot[tid] * kLn16 * fmaf(-tau1, tau1, 1.0f)) : 0.0f;
+        const float dp0 = tid < nvalid ? (kScan ? S.tot[C + tid] : S.tot[C + tid] * kHalfPi * fmaf(-tau0, tau0, 1.0f)) : 0.0f;
         S.dp[tid] = make_float4(dp0, dp0, dp1, dp1);
         if constexpr (kProj) {  // the projections' gradient (finished by the caller's matrix products)
           if (g == 0 && tid < nvalid) p.dp_out[b * T + r.t0 + tid] = make_float2(dp0, dp1);

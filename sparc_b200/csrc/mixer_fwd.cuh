@@ -55,8 +55,10 @@ struct FwdParams {
   int mask_words;       // 16 per CTA of 256 modes: four words per 64 modes (store_relu_bits)
   const float2* carry;  // [B, chunks, M] inclusive chunk states (replay input)
   float4* agg;          // [B, chunks, Mp] chunk aggregates (P, Q)
-  const float2* proj_in;  // [B*T] controller projections (p0, p1), bias included (kModeProj)
+  const float2* proj_in;  // [B*T] controller projections (p0, p1), bias included (kModeProj), or
+                          // the controls (delta, eta) themselves (kModeScan)
   int content_linear;     // kModeProj: the content is u itself instead of tanh(u)
+  void* y_im;             // kModeScan: Im h [B*T, M] (y then holds Re h [B*T, M]), or null
   LaunchState* ls;
   long long B, T;
   int W, M, Mp, chunks;
@@ -190,7 +192,7 @@ __host__ __device__ constexpr unsigned act_box_bytes() {
 template <typename TIO, int C, bool kFast, int kMode>
 __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __grid_constant__ FwdParams p) {
   constexpr int NW = kFwdThreads / 32;
-  constexpr bool kBlock = kMode == kModeBlock, kProj = kMode == kModeProj;
+  constexpr bool kBlock = kMode == kModeBlock, kProj = proj_like<kMode>(), kScan = kMode == kModeScan;
   cg::cluster_group cluster = cg::this_cluster();
   const int g = (int)cluster.block_rank();
   const int G = (int)cluster.num_blocks();
@@ -328,9 +330,11 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
     }
     {
       if (tid < C) {
-        const float tau0 = tanh_accurate(fmaf(rs, p0, bias0));
-        const float tau1 = tanh_accurate(fmaf(rs, p1, bias1));
-        const float E = expf(kLn16 * tau1), delta = kHalfPi * tau0;
+        // controls: eta = ln16 tanh(p1), delta = pi/2 tanh(p0); the scan-level mode takes
+        // (p0, p1) = (delta, eta) as given (no gate: tau = 0)
+        const float tau0 = kScan ? 0.0f : tanh_accurate(fmaf(rs, p0, bias0));
+        const float tau1 = kScan ? 0.0f : tanh_accurate(fmaf(rs, p1, bias1));
+        const float E = kScan ? expf(p1) : expf(kLn16 * tau1), delta = kScan ? p0 : kHalfPi * tau0;
         const float keep = (p.reset != nullptr && tid < r.nvalid && p.reset[r.b * T + r.t0 + tid]) ? 0.0f : 1.0f;
         TokenCtl tc;
         tc.ed = make_float4(E, E, delta, delta);
@@ -358,7 +362,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
             xr = mul2(xr, mul2(rr, mc.wre));
             xi = mul2(xi, mul2(rr, mc.wim));
           }
-          const TokenCoef2 k = token_coef2<kFast, fwd_rot<kFast>()>(mc, S.ctl[t]);
+          const TokenCoef2 k = token_coef2<kFast, fwd_rot<kFast>(), kScan>(mc, S.ctl[t]);
           Q = cfma2(k.a, Q, cx2(mul2(k.gain, content2<kFast, kMode>(xr, lin)), mul2(k.gain, content2<kFast, kMode>(xi, lin))));
           P = cmul2(k.a, P);
         }
@@ -378,7 +382,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
 // ------------------------------------------------------------------------------ replay
 template <typename TIO, int C, bool kFast, bool kVec, int kMode>
 __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __grid_constant__ FwdParams p) {
-  constexpr bool kBlock = kMode == kModeBlock, kProj = kMode == kModeProj;
+  constexpr bool kBlock = kMode == kModeBlock, kProj = proj_like<kMode>(), kScan = kMode == kModeScan;
   const bool lin = kProj && p.content_linear != 0;
   const int g = blockIdx.x;
   const int tid = threadIdx.x;
@@ -463,7 +467,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
         if (kFull || t < r.nvalid) {
           const float2 xr = Pair<TIO>::load(&xt[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&xt[t][1][2 * tid]);
-          const TokenCoef2 k = token_coef2<kFast, fwd_rot<kFast>()>(mc, ctl[t]);
+          const TokenCoef2 k = token_coef2<kFast, fwd_rot<kFast>(), kScan>(mc, ctl[t]);
           if constexpr (kBlock) {
             // mixer input x r w; block output x + relu(h); relu bits for the backward
             const float2 rr = make_float2(ctl[t].keep.z, ctl[t].keep.w);
@@ -474,8 +478,22 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
                             h, lane);
           } else {
             h = cfma2(k.a, h, cx2(mul2(k.gain, content2<kFast, kMode>(xr, lin)), mul2(k.gain, content2<kFast, kMode>(xi, lin))));
-            store_y_pair<TIO, kVec, !kProj>(yrow + (long long)t * W, M, m0, act0, act1, make_float2(h.re.x, h.im.x),
-                                    make_float2(h.re.y, h.im.y));
+            if (kScan && p.y_im != nullptr) {
+              // separate real and imaginary outputs, [B*T, M] each
+              const long long o = (r.b * T + r.t0 + t) * (long long)M + m0;
+              TIO* yr = static_cast<TIO*>(p.y) + o;
+              TIO* yi = static_cast<TIO*>(p.y_im) + o;
+              if (kVec && act1) {
+                Pair<TIO>::store(yr, h.re.x, h.re.y);
+                Pair<TIO>::store(yi, h.im.x, h.im.y);
+              } else {
+                if (act0) { Io<TIO>::store(yr, h.re.x); Io<TIO>::store(yi, h.im.x); }
+                if (act1) { Io<TIO>::store(yr + 1, h.re.y); Io<TIO>::store(yi + 1, h.im.y); }
+              }
+            } else {
+              store_y_pair<TIO, kVec, !kProj>(yrow + (long long)t * W, M, m0, act0, act1,
+                                              make_float2(h.re.x, h.im.x), make_float2(h.re.y, h.im.y));
+            }
           }
         }
       }

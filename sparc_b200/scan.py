@@ -7,67 +7,136 @@ precomputed per-token controls (eta, delta) [B, L] and writes (br, bi) [B, L, M]
     rho = exp(-nu e^eta),  phi = theta + (1 - rho) delta,  h_t = rho e^{i phi} h_{t-1} + b_t
     (nu = e^{nu_log}, theta = e^{theta_log}; forward/scan.py:725-757).
 
-They run the mixer's projection-mode kernels (the ones behind SPARCSequenceLayer) through a
-change of variables, with no kernel of their own. Those kernels take per-token controller
-projections p and a content input u and form eta' = ln16 tanh(p1), delta' = (pi/2) tanh(p0) and
-the write gain(u) = e^{wlg} sqrt(expm1(-2 nu e^eta') / expm1(-2 nu)) 2 sigma(tau0 wpr + tau1 wrr) u.
-With p = (atanh(delta / (pi/2)), atanh(eta / ln16)), wlg = wpr = wrr = 0 and a linear content
-u = b / sqrt(expm1(-2 nu e^eta) / expm1(-2 nu)), they compute exactly the scan above, and
-autograd through the change of variables gives the gradients of eta, delta, the writes,
-nu_log, theta_log and the initial state.
-
-Domain: |eta| < ln 16 and |delta| < pi/2, the range of the reference's controller
-(forward/control.py:129-139: eta = ln16 tanh(p1), delta = (pi/2) tanh(p0)); values at or beyond
-it are clamped to (1 - 2^-23) times the bound (and get no gradient there); the writes stay b.
+They run the mixer kernels in their scan-level mode (``content_linear = 2`` of the C ABI): the
+controls (delta, eta) and the writes are read as given, for any values (the phase offset is
+range-reduced before its sine and cosine), with no write gain; the outputs are written as two
+contiguous [B, L, M] tensors. The only copies are the writes and, in the backward, the output
+gradients laid side by side as [b_r | b_i] [B, L, 2M] rows for the kernels' tile loads, and the
+controls stacked as float32 pairs [B, L, 2]. The gradients of eta, delta, the writes, nu_log,
+theta_log and the initial state come from the mixer's backward kernels.
 """
 from __future__ import annotations
 
-import math
+import ctypes
 
 import torch
 
 from . import _lib
-
-LN16 = math.log(16.0)
-HALF_PI = 0.5 * math.pi
-_EDGE = 1.0 - 2.0 ** -23  # a float32 just below 1, where atanh is still finite (about 8.3)
 
 
 def _io_dtype(dtype: torch.dtype) -> torch.dtype:
     return dtype if dtype in (torch.float32, torch.bfloat16) else torch.float32
 
 
-def _projection_inputs(eta, delta, nu_log, br, bi):
-    """(u [B, L, 2M], p [B, L, 2] float32): the content input and controller projections for
-    which the projection-mode kernels compute the scan with controls (eta, delta) and writes
-    (br, bi). Differentiable in every argument."""
-    x0 = (delta.float() / HALF_PI).clamp(-_EDGE, _EDGE)  # tanh(p0), tanh(p1) as the kernels will form them
-    x1 = (eta.float() / LN16).clamp(-_EDGE, _EDGE)
-    p = torch.stack((torch.atanh(x0), torch.atanh(x1)), dim=-1)
-    nu = torch.exp(nu_log.float())
-    z = nu * torch.exp(LN16 * x1)[..., None]  # (the clamped eta, so the writes are b also at the bound)
-    s = torch.sqrt(torch.expm1(-2.0 * z) / torch.expm1(-2.0 * nu))
-    u = torch.cat((br.float() / s, bi.float() / s), dim=-1).to(_io_dtype(br.dtype))
-    return u, p
+def _scan_forward(eta, delta, nu_log, theta_log, br, bi, h0, reset):
+    """sparc_mixer_forward in the scan-level mode: (out_r, out_i) [B, L, M] (the writes' dtype),
+    the last state (float32) and what the backward needs."""
+    L = _lib.lib()
+    B, T, M = br.shape
+    W = 2 * M
+    io = _io_dtype(br.dtype)
+    dev = br.device
+    dt = _lib.dtype_code(io)
+    u = torch.cat((br.to(io), bi.to(io)), dim=-1).contiguous()  # writes as [b_r | b_i] rows
+    p = torch.stack((delta.detach().float(), eta.detach().float()), dim=-1).contiguous()
+    nl = nu_log.detach().float().contiguous()
+    tl = theta_log.detach().float().contiguous()
+    zeros = torch.zeros(M, dtype=torch.float32, device=dev)  # write gain parameters: not read
+    h0 = None if h0 is None else (h0[0].detach().float().contiguous(), h0[1].detach().float().contiguous())
+    out_r = torch.empty((B, T, M), dtype=io, device=dev)
+    out_i = torch.empty((B, T, M), dtype=io, device=dev)
+    chunks = L.sparc_mixer_carry_chunks(T, dt)
+    carry = torch.empty((B, chunks, M, 2), dtype=torch.float32, device=dev)
+    controls = torch.empty((B, T, L.sparc_mixer_controls_floats()), dtype=torch.float32, device=dev)
+    last_r = torch.empty((B, M), dtype=torch.float32, device=dev)
+    last_i = torch.empty((B, M), dtype=torch.float32, device=dev)
+    nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
+    if nbytes == 0:
+        _lib.check(-2, "sparc_mixer_workspace_bytes")
+    ws = _lib.WORKSPACES.get(dev, nbytes)
+    a = _lib.MixerFwdArgs(
+        u.data_ptr(), out_r.data_ptr(), nl.data_ptr(), tl.data_ptr(), None, None,
+        zeros.data_ptr(), zeros.data_ptr(), zeros.data_ptr(),
+        _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
+        last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
+        None, 0.0, None, p.data_ptr(), 2,
+        ws.data_ptr(), ws.numel(), B, T, W, dt, 0, out_i.data_ptr())
+    _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
+               "sparc_mixer_forward (scan-level mode)")
+    return out_r, out_i, last_r, last_i, (u, nl, tl, zeros, h0, carry, controls)
 
 
-def _core(u, p, nu_log, theta_log, h0, reset):
-    """The projection-mode recurrence (sparc_mixer_forward / _backward through
-    projection._SparcCoreFunction): (h [B, L, 2M], last_r, last_i)."""
-    from .projection import _SparcCoreFunction
+def _scan_backward(saved, g_r, g_i, g_last_r, g_last_i):
+    """sparc_mixer_backward in the scan-level mode: (d eta, d delta [B, L] float32, d nu_log,
+    d theta_log [M], d b_r, d b_i [B, L, M] (views of one [B, L, 2M] buffer), d h0 or None)."""
+    L = _lib.lib()
+    u, nl, tl, zeros, h0, carry, controls = saved
+    B, T, W = u.shape
+    M = W // 2
+    dev = u.device
+    dt = _lib.dtype_code(u.dtype)
+    zr = None
+    if g_r is None or g_i is None:
+        zr = torch.zeros((B, T, M), dtype=u.dtype, device=dev)
+    dh = torch.cat(((zr if g_r is None else g_r).to(u.dtype), (zr if g_i is None else g_i).to(u.dtype)), dim=-1)
+    dh = dh.contiguous()
+    gl = None
+    if g_last_r is not None or g_last_i is not None:
+        gl = (torch.zeros((B, M), device=dev) if g_last_r is None else g_last_r.float().contiguous(),
+              torch.zeros((B, M), device=dev) if g_last_i is None else g_last_i.float().contiguous())
+    du = torch.empty_like(u)
+    dp = torch.empty((B, T, 2), dtype=torch.float32, device=dev)
+    g = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(6)]
+    gh0 = None
+    if h0 is not None:
+        gh0 = (torch.empty((B, M), dtype=torch.float32, device=dev),
+               torch.empty((B, M), dtype=torch.float32, device=dev))
+    ws = _lib.WORKSPACES.get(dev, L.sparc_mixer_workspace_bytes(B, T, W, dt))
+    a = _lib.MixerBwdArgs(
+        u.data_ptr(), None, dh.data_ptr(), du.data_ptr(),
+        nl.data_ptr(), tl.data_ptr(), None, None, zeros.data_ptr(), zeros.data_ptr(), zeros.data_ptr(),
+        _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
+        _lib.ptr(gl[0] if gl else None), _lib.ptr(gl[1] if gl else None),
+        _lib.ptr(gh0[0] if gh0 else None), _lib.ptr(gh0[1] if gh0 else None),
+        carry.data_ptr(), controls.data_ptr(), None, None, None,
+        g[0].data_ptr(), g[1].data_ptr(), None, None, g[2].data_ptr(), g[5].data_ptr(),
+        g[3].data_ptr(), g[4].data_ptr(), dp.data_ptr(), 2,
+        workspace=ws.data_ptr(), workspace_bytes=ws.numel(), batch=B, length=T, width=W, dtype=dt, max_spin=0)
+    _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
+               "sparc_mixer_backward (scan-level mode)")
+    return dp[..., 1], dp[..., 0], g[0], g[1], du[..., :M], du[..., M:], gh0
 
-    _lib.require_cuda(u, "the writes")
-    zeros = torch.zeros_like(nu_log, dtype=torch.float32)
-    h0_r, h0_i = (None, None) if h0 is None else h0
-    return _SparcCoreFunction.apply(u, p, nu_log, theta_log, zeros, zeros, zeros, h0_r, h0_i, 0, reset, True)
+
+class _SparcScanFunction(torch.autograd.Function):
+    """Autograd op of the scan-level entry points: (out_r, out_i, last_r, last_i) from
+    (eta, delta, nu_log, theta_log, br, bi) and an optional initial state; every input gets its
+    gradient, including the initial state, and the last state's gradient flows back."""
+
+    @staticmethod
+    def forward(ctx, eta, delta, nu_log, theta_log, br, bi, h0_r, h0_i, reset):
+        h0 = None if h0_r is None else (h0_r, h0_i)
+        out_r, out_i, last_r, last_i, saved = _scan_forward(eta, delta, nu_log, theta_log, br, bi, h0, reset)
+        ctx.saved = saved
+        ctx.dtypes = (eta.dtype, delta.dtype, nu_log.dtype, theta_log.dtype, br.dtype, bi.dtype)
+        ctx.set_materialize_grads(False)
+        if out_r.dtype != br.dtype:
+            out_r, out_i = out_r.to(br.dtype), out_i.to(bi.dtype)
+        return out_r, out_i, last_r, last_i
+
+    @staticmethod
+    def backward(ctx, g_r, g_i, g_last_r, g_last_i):
+        ge, gd, gn, gt, gbr, gbi, gh0 = _scan_backward(ctx.saved, g_r, g_i, g_last_r, g_last_i)
+        ctx.saved = None
+        grads = [t.to(d) for t, d in zip((ge, gd, gn, gt, gbr, gbi), ctx.dtypes)]
+        return (*grads, gh0[0] if gh0 else None, gh0[1] if gh0 else None, None)
 
 
 def _run(eta, delta, nu_log, theta_log, br, bi, h0=None, reset=None):
-    """(out_r, out_i) in br's dtype and (last_r, last_i) float32."""
-    M = br.shape[-1]
-    u, p = _projection_inputs(eta, delta, nu_log, br, bi)
-    h, last_r, last_i = _core(u, p, nu_log, theta_log, h0, reset)
-    return (h[..., :M].to(br.dtype).contiguous(), h[..., M:].to(bi.dtype).contiguous()), (last_r, last_i)
+    """((out_r, out_i) in br's dtype, (last_r, last_i) float32)."""
+    _lib.require_cuda(br, "the writes")
+    h0_r, h0_i = (None, None) if h0 is None else h0
+    out_r, out_i, last_r, last_i = _SparcScanFunction.apply(eta, delta, nu_log, theta_log, br, bi, h0_r, h0_i, reset)
+    return (out_r, out_i), (last_r, last_i)
 
 
 def _check(eta, delta, nu_log, theta_log, br, bi):

@@ -2,7 +2,8 @@
 sparc_chunk_scan, sparc_scan_with_last, sparc_training_scan_dispatch) on the GPU: the reference's
 own sparc_tiled_serial_scan golden vectors (h0, segment resets, gradient of the last state;
 float32: 1e-4 forward, 1e-3 gradients) and the float64 oracle's scan and adjoint for other
-shapes (two CTAs of modes, bfloat16 writes at 2e-2)."""
+shapes (two and four CTAs of modes, bfloat16 writes at 2e-2), with controls inside the module
+controller's range and far outside it (the scan-level functions take any eta and delta)."""
 import numpy as np
 import pytest
 import torch
@@ -35,10 +36,13 @@ def test_tiled_serial_scan_matches_reference_golden(golden):
         assert O.rel_l2(t[k].grad.double().cpu().numpy(), d[ref]) < 1e-3, k
 
 
-def _problem(B, L, M, seed):
+def _problem(B, L, M, seed, wide=False):
     rng = np.random.default_rng(seed)
     p = rng.standard_normal((B, L, 2)) * 0.8
     eta, delta = np.log(16.0) * np.tanh(p[..., 1]), 0.5 * np.pi * np.tanh(p[..., 0])
+    if wide:  # controls far outside the module controller's range: the scan takes any values
+        eta = rng.uniform(-6.0, 4.0, (B, L))
+        delta = rng.standard_normal((B, L)) * 6.0
     P = O.Params.from_mapping({"nu_log": rng.standard_normal(M) * 0.5 - 1.5, "theta_log": rng.standard_normal(M) * 0.5,
                                "phase_direction": np.zeros(2 * M + 1), "radial_direction": np.zeros(2 * M + 1),
                                "write_log_gain": np.zeros(M), "energy_response": np.zeros(M),
@@ -48,12 +52,16 @@ def _problem(B, L, M, seed):
     return eta, delta, P, br, bi, gr, gi
 
 
+@pytest.mark.parametrize("wide", [False, True], ids=["module_range", "wide_controls"])
 @pytest.mark.parametrize("B,L,M,dtype,tol", [(2, 50, 300, torch.float32, (1e-4, 1e-3)),
-                                             (2, 64, 40, torch.bfloat16, (2e-2, 2e-2))])
-def test_sparc_scan_matches_oracle(B, L, M, dtype, tol):
+                                             (2, 64, 40, torch.bfloat16, (2e-2, 2e-2)),
+                                             (3, 200, 1024, torch.float32, (1e-4, 1e-3))])
+def test_sparc_scan_matches_oracle(B, L, M, dtype, tol, wide):
+    """The scan against the float64 oracle, with controls inside the module controller's range
+    (|eta| < ln16, |delta| < pi/2) and far outside it (eta in [-6, 4], delta ~ 6 N(0, 1))."""
     from sparc_b200 import scan
 
-    eta, delta, P, br, bi, gr, gi = _problem(B, L, M, M)
+    eta, delta, P, br, bi, gr, gi = _problem(B, L, M, M, wide)
     dev = "cuda"
     te = torch.tensor(eta, dtype=torch.float32, device=dev, requires_grad=True)
     td = torch.tensor(delta, dtype=torch.float32, device=dev, requires_grad=True)
@@ -62,7 +70,7 @@ def test_sparc_scan_matches_oracle(B, L, M, dtype, tol):
     tbr = torch.tensor(br, device=dev).to(dtype).requires_grad_(True)
     tbi = torch.tensor(bi, device=dev).to(dtype).requires_grad_(True)
     out_r, out_i = scan.sparc_scan(te, td, tn, tt, tbr, tbi)
-    assert out_r.dtype == dtype and out_r.shape == (B, L, M)
+    assert out_r.dtype == dtype and out_r.shape == (B, L, M) and out_r.is_contiguous() and out_i.is_contiguous()
     ar, ai, _, _ = O.transition(eta, delta, P)
     brd, bid = tbr.detach().double().cpu().numpy(), tbi.detach().double().cpu().numpy()
     hr, hi = O._scan(ar, ai, brd, bid)
