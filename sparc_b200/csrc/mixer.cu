@@ -314,14 +314,15 @@ __host__ __device__ constexpr int log2i() { return N <= 1 ? 0 : 1 + log2i<N / 2>
 // state; else 0). out[chunk] receives every v; `final` (optional) the last one (the forward's
 // last state, the backward's gradient of h0).
 //
-// One thread-block cluster of kScanQ CTAs per (row, 256 modes): CTA q owns the span of chunks
-// [q L, (q+1) L), L = ceil(chunks / kScanQ), and one mode per thread. It composes its span's maps
-// (loads batched kScanBatch at a time so their latencies overlap), leaves the span's map in
-// shared memory, and after one cluster barrier composes the maps of the spans before it, read
-// from the peers' shared memory in order, into its carry-in; then it walks its span again
-// writing every chunk's v. No CTA waits on anything but the cluster barrier, and the composition
-// order is fixed, so the carries are bitwise reproducible.
-constexpr int kScanThreads = 256;
+// One thread-block cluster of kScanQ CTAs of kScanWarps warps per (row, 32 modes): lane l owns
+// mode m0 + l, and the cluster's kScanQ x kScanWarps warps own consecutive spans of
+// L = ceil(chunks / spans) chunks (warp w of CTA q: span q kScanWarps + w). Each lane composes its
+// span's maps (the first kScanHold of them kept in registers), leaves the span's map in shared
+// memory, and after one cluster barrier composes the earlier spans' maps in order (its own CTA's
+// from shared memory, the earlier CTAs' through distributed shared memory) into its carry-in;
+// then it walks its span writing every chunk's v. A warp's 32 lanes read 32 consecutive maps
+// (512 contiguous bytes) per chunk. The composition order is fixed, so the carries are bitwise
+// reproducible; nothing waits but the cluster barriers.
 // Rotation choice per kernel family and activation type (transition_rot): bfloat16 kernels use
 // the hardware sin / cos of the whole angle; the float32 forward the series of the bounded
 // offset (its outputs agree with the decode step's libm to ~1e-7); the float32 backward the
@@ -343,13 +344,16 @@ template <bool kFast>
 __host__ __device__ constexpr int bwd_rot() { return kFast ? 1 : SPARC_F32_ROT_BWD; }
 
 #ifndef SPARC_SCAN_Q
-#define SPARC_SCAN_Q 8
+#define SPARC_SCAN_Q 4
 #endif
-#ifndef SPARC_SCAN_BATCH
-#define SPARC_SCAN_BATCH 16
+#ifndef SPARC_SCAN_WARPS
+#define SPARC_SCAN_WARPS 4
 #endif
-constexpr int kScanQ = SPARC_SCAN_Q;          // CTAs per row (portable cluster size)
-constexpr int kScanBatch = SPARC_SCAN_BATCH;  // chunk maps in flight per thread
+constexpr int kScanQ = SPARC_SCAN_Q;            // CTAs per (row, 32 modes): a portable cluster
+constexpr int kScanWarps = SPARC_SCAN_WARPS;    // spans per CTA
+constexpr int kScanSpans = kScanQ * kScanWarps;
+constexpr int kScanThreads = 32 * kScanWarps;
+constexpr int kScanHold = 8;                    // span maps held in registers (longer spans reload)
 
 struct ScanParams {
   const float4* agg;     // [B, chunks, Mp] per-chunk maps (A, B)
@@ -358,65 +362,85 @@ struct ScanParams {
   const float* init_i;
   float* final_r;        // [B, M] or null
   float* final_i;
-  int G;                 // 256-mode groups per row
   int M, Mp, chunks, span;
   int reverse;
 };
 
 __global__ void __launch_bounds__(kScanThreads) mixer_carry_scan_kernel(const ScanParams p) {
-  __shared__ float4 s_map[kScanThreads];  // this span's map per mode (peers read it)
+  __shared__ float4 s_map[kScanWarps][32];  // this CTA's span maps per mode (peers read them)
   cg::cluster_group cluster = cg::this_cluster();
   const int q = (int)cluster.block_rank();
-  const int tid = threadIdx.x;
-  const long long row = blockIdx.y;
-  const long long b = row / p.G;
-  const int g = (int)(row - b * p.G);
-  const int m = g * kScanThreads + tid;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int sp = q * kScanWarps + w;  // this warp's span
+  const long long b = blockIdx.y;
+  const int m = (blockIdx.x / kScanQ) * 32 + lane;
   const bool act = m < p.M;
-  const int j0 = min(q * p.span, p.chunks), j1 = min(j0 + p.span, p.chunks);
-  auto map_at = [&](int j) {  // chunk map of processing index j (identity for idle lanes)
-    const int c = p.reverse ? p.chunks - 1 - j : j;
-    return act ? __ldcg(p.agg + (b * p.chunks + c) * (long long)p.Mp + m) : make_float4(1.0f, 0.0f, 0.0f, 0.0f);
-  };
+  const int j0 = min(sp * p.span, p.chunks), j1 = min(j0 + p.span, p.chunks);
+  // chunk maps and outputs of processing index j: strided pointers from the span's first chunk
+  const long long c0 = p.reverse ? p.chunks - 1 - j0 : j0;
+  const long long step = p.reverse ? -1 : 1;
+  const float4* ap = p.agg + (b * p.chunks + c0) * (long long)p.Mp + m;
+  float2* op = p.out + (b * p.chunks + c0) * (long long)p.M + m;
+  const long long astep = step * p.Mp, ostep = step * p.M;
+  const float4 ident = make_float4(1.0f, 0.0f, 0.0f, 0.0f);
   pdl_wait();  // the chunk maps (summary) are complete from here on
 
-  // the span's map
+  // the span's map; its first kScanHold maps stay in registers for the walk
+  float4 held[kScanHold];
+#pragma unroll
+  for (int u = 0; u < kScanHold; ++u) held[u] = (act && j0 + u < j1) ? __ldcg(ap + u * astep) : ident;
   float2 A = make_float2(1.0f, 0.0f), Bv = make_float2(0.0f, 0.0f);
-  for (int j = j0; j < j1; j += kScanBatch) {
-    float4 a[kScanBatch];
 #pragma unroll
-    for (int u = 0; u < kScanBatch; ++u) a[u] = j + u < j1 ? map_at(j + u) : make_float4(1.0f, 0.0f, 0.0f, 0.0f);
+  for (int u = 0; u < kScanHold; ++u) {
+    Bv = cfma(make_float2(held[u].x, held[u].y), Bv, make_float2(held[u].z, held[u].w));
+    A = cmul(make_float2(held[u].x, held[u].y), A);
+  }
+  for (int j = j0 + kScanHold; j < j1; j += kScanHold) {
+    float4 a[kScanHold];
 #pragma unroll
-    for (int u = 0; u < kScanBatch; ++u) {
+    for (int u = 0; u < kScanHold; ++u) a[u] = (act && j + u < j1) ? __ldcg(ap + (j - j0 + u) * astep) : ident;
+#pragma unroll
+    for (int u = 0; u < kScanHold; ++u) {
       Bv = cfma(make_float2(a[u].x, a[u].y), Bv, make_float2(a[u].z, a[u].w));
       A = cmul(make_float2(a[u].x, a[u].y), A);
     }
   }
-  s_map[tid] = make_float4(A.x, A.y, Bv.x, Bv.y);
+  s_map[w][lane] = make_float4(A.x, A.y, Bv.x, Bv.y);
   cluster.sync();
 
   // carry into the span: init, then the earlier spans' maps in order
   float2 v = make_float2(0.0f, 0.0f);
   if (p.init_r != nullptr && act) v = make_float2(p.init_r[b * p.M + m], p.init_i[b * p.M + m]);
-  {
-    float4 mk[kScanQ];
+  for (int k = 0; k < q; ++k) {  // the earlier CTAs' spans (their loads together)
+    const float4* peer = cluster.map_shared_rank(&s_map[0][0], k);
+    float4 mk[kScanWarps];
 #pragma unroll
-    for (int k = 0; k < kScanQ; ++k) mk[k] = k < q ? cluster.map_shared_rank(s_map, k)[tid] : make_float4(1.0f, 0.0f, 0.0f, 0.0f);
+    for (int u = 0; u < kScanWarps; ++u) mk[u] = peer[u * 32 + lane];
 #pragma unroll
-    for (int k = 0; k < kScanQ; ++k) v = cfma(make_float2(mk[k].x, mk[k].y), v, make_float2(mk[k].z, mk[k].w));
+    for (int u = 0; u < kScanWarps; ++u) v = cfma(make_float2(mk[u].x, mk[u].y), v, make_float2(mk[u].z, mk[u].w));
+  }
+  for (int u = 0; u < w; ++u) {  // this CTA's earlier spans
+    const float4 mk = s_map[u][lane];
+    v = cfma(make_float2(mk.x, mk.y), v, make_float2(mk.z, mk.w));
   }
 
   // walk the span
-  for (int j = j0; j < j1; j += kScanBatch) {
-    float4 a[kScanBatch];
 #pragma unroll
-    for (int u = 0; u < kScanBatch; ++u) a[u] = j + u < j1 ? map_at(j + u) : make_float4(1.0f, 0.0f, 0.0f, 0.0f);
+  for (int u = 0; u < kScanHold; ++u) {
+    if (j0 + u < j1) {
+      v = cfma(make_float2(held[u].x, held[u].y), v, make_float2(held[u].z, held[u].w));
+      if (act) op[u * ostep] = v;
+    }
+  }
+  for (int j = j0 + kScanHold; j < j1; j += kScanHold) {
+    float4 a[kScanHold];
 #pragma unroll
-    for (int u = 0; u < kScanBatch; ++u) {
+    for (int u = 0; u < kScanHold; ++u) a[u] = (act && j + u < j1) ? __ldcg(ap + (j - j0 + u) * astep) : ident;
+#pragma unroll
+    for (int u = 0; u < kScanHold; ++u) {
       if (j + u < j1) {
         v = cfma(make_float2(a[u].x, a[u].y), v, make_float2(a[u].z, a[u].w));
-        const int c = p.reverse ? p.chunks - 1 - (j + u) : j + u;
-        if (act) p.out[(b * p.chunks + c) * (long long)p.M + m] = v;
+        if (act) op[(j - j0 + u) * ostep] = v;
       }
     }
   }
@@ -424,7 +448,7 @@ __global__ void __launch_bounds__(kScanThreads) mixer_carry_scan_kernel(const Sc
     p.final_r[b * p.M + m] = v.x;
     p.final_i[b * p.M + m] = v.y;
   }
-  cluster.sync();  // no CTA leaves while a peer may still read its span map
+  cluster.sync();  // no CTA leaves while a peer may still read its span maps
 }
 
 #include "mixer_fwd.cuh"
@@ -540,8 +564,8 @@ struct Plan {
   bool vec, tma;
   int sum_clusters, rep_rows, rsum_rows, grad_clusters;
   size_t sum_smem, rep_smem, rsum_smem, grad_smem;
-  long long scan_rows;     // carry-scan clusters: B * G
-  int scan_span;           // chunks per carry-scan CTA
+  long long scan_rows;     // carry-scan grid rows: B
+  int scan_span;           // chunks per carry-scan span (warp)
 };
 
 static thread_local char g_err[512];
@@ -668,9 +692,9 @@ static int make_plan(long long B, long long T, int W, int dtype, int mode, Plan*
   pl->vec = (M % 2) == 0;
   const size_t s = dtype == SPARC_DTYPE_BF16 ? 2 : 4;
   pl->tma = ((size_t)W * s) % 16 == 0 && ((size_t)M * s) % 16 == 0 && B * T < (1LL << 31);
-  pl->scan_rows = B * pl->G;
-  pl->scan_span = (pl->chunks + kScanQ - 1) / kScanQ;
-  if (pl->scan_rows > 65535) { set_err("batch x width too large for the carry scan's grid"); return SPARC_ERR_SHAPE; }
+  pl->scan_rows = B;
+  pl->scan_span = (pl->chunks + kScanSpans - 1) / kScanSpans;
+  if (pl->scan_rows > 65535) { set_err("batch too large for the carry scan's grid"); return SPARC_ERR_SHAPE; }
 
   const void* k[4];
   if (dtype == SPARC_DTYPE_BF16) plan_kernels<__nv_bfloat16>(pl, k);
@@ -816,7 +840,7 @@ static ScanParams scan_params(const Plan& pl, const WsLayout& L, char* ws, int M
   sp.init_i = init_i;
   sp.final_r = final_r;
   sp.final_i = final_i;
-  sp.G = pl.G;
+
   sp.M = M;
   sp.Mp = pl.Mp;
   sp.chunks = pl.chunks;
@@ -826,7 +850,9 @@ static ScanParams scan_params(const Plan& pl, const WsLayout& L, char* ws, int M
 }
 
 static cudaError_t launch_scan(const Plan& pl, const ScanParams& sp, cudaStream_t s) {
-  return launch_cluster((const void*)mixer_carry_scan_kernel, kScanQ, kScanThreads, (int)pl.scan_rows, 0, s, sp);
+  // grid: kScanQ CTAs per 32 modes (x), rows (y); one cluster per (row, 32 modes)
+  return launch_ex((const void*)mixer_carry_scan_kernel, dim3(kScanQ * ((sp.M + 31) / 32), (unsigned)pl.scan_rows),
+                   dim3(kScanThreads, 1, 1), kScanQ, 0, s, sp);
 }
 
 static int launch_error(cudaError_t e) {
