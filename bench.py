@@ -741,14 +741,22 @@ def run_projection(args, wl, world, rank, local):
                 "frac": round(byts / (rec_ms / 1e3) / 1e9 / peak, 4), "traffic": None,
                 "kernel": "the seven recurrence kernels (projection mode), 5 x 2M x s bytes per token",
                 "peak_source": kind, "kernels_ms": kern, "recurrence_ms": round(rec_ms, 4)}
-    if "proj_gemm_kernel" in kern:  # tensor-core products: 2 x 2M x W flops per token each, four per step
-        gms = kern["proj_gemm_kernel"]
-        tf = 2.0 * 2 * M * W * B * T / (gms / 1e3) / 1e12
-        roofline["tensor"] = {"kernel": "proj_gemm_kernel", "ms_per_launch": gms, "TFLOPs": round(tf, 1),
-                              "peak_TFLOPs": _bf16_peak(), "frac": round(tf / _bf16_peak(), 4)}
+    if "proj_gemm_kernel" in times:  # tensor-core products: 2 x 2M x W flops per token each, six per step
+        # a product's time includes its split-k finish launch where it has one
+        tot, n = times["proj_gemm_kernel"]
+        tot += times.get("proj_gemm_finish_kernel", (0.0, 0))[0]
+        gms = tot / n
+        split = 3 if x.dtype == torch.float32 else 1  # float32 operands: three bf16 terms along k
+        tf = 2.0 * 2 * M * W * B * T * split / (gms / 1e3) / 1e12
+        roofline["tensor"] = {"kernel": "proj_gemm_kernel (+ proj_gemm_finish_kernel)", "ms_per_launch": round(gms, 4),
+                              "TFLOPs": round(tf, 1), "peak_TFLOPs": _bf16_peak(), "frac": round(tf / _bf16_peak(), 4),
+                              "flops": "2 x tokens x 2M x W per product" + (" x 3 (bf16 split of float32)" if split == 3 else "")}
     del graph
+    # every launch of the library in the timed steps (the colsum entry times its two launches
+    # as one pair)
+    launches = sum(n for _, n in times.values()) + times.get("proj_colsum_kernel", (0, 0))[1]
     return dict(value=B * T * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=None, cpu=None,
-                clocks=clocks.summary(), launches=MIXER_LAUNCHES * args.steps, per_step_ms=per,
+                clocks=clocks.summary(), launches=launches, per_step_ms=per,
                 tokens_step=B * T * world)
 
 

@@ -311,13 +311,67 @@ size_t sparc_real_workspace_bytes(long long batch, long long length, long long c
 int sparc_real_scan_forward(const SparcRealFwdArgs* args, void* stream);
 int sparc_real_scan_backward(const SparcRealBwdArgs* args, void* stream);
 
+/* Generic complex diagonal scan h_t = a_t h_{t-1} + b_t (h_{-1} = 0) over [batch, length,
+ * modes], each part a separate contiguous array (backward/scan.py:887-919, 1653-1656, 1838-1855;
+ * kernels forward/scan.py:701-722, backward/scan.py:131-160). ar, ai are read in a_dtype and br,
+ * bi in b_dtype, widened to float32; out_r, out_i are written in b_dtype; last_r, last_i
+ * ([batch, modes] float32, optional) receive the final state. The backward reads the forward's
+ * outputs (b_dtype) as the previous states and grad_out_r/_i in b_dtype, and writes grad_ar,
+ * grad_ai, grad_br, grad_bi in a_dtype (grad_ar = Re(adj) Re(h_{t-1}) + Im(adj) Im(h_{t-1}),
+ * grad_ai = Im(adj) Re(h_{t-1}) - Re(adj) Im(h_{t-1}), grad_b = adj, with
+ * adj_t = grad_t + conj(a_{t+1}) adj_{t+1}). `workspace`: sparc_complex_workspace_bytes bytes,
+ * 16-byte aligned, no initial contents needed. Shapes: batch <= 65535, ceil(length / 32) <=
+ * 65535, batch x ceil(length / 32) x modes < 2^31. */
+typedef struct SparcComplexFwdArgs {
+  const void* ar;
+  const void* ai;
+  const void* br;
+  const void* bi;
+  void* out_r;
+  void* out_i;
+  float* last_r;                       /* or NULL (with last_i) */
+  float* last_i;
+  void* workspace;
+  size_t workspace_bytes;
+  long long batch;
+  long long length;
+  long long modes;
+  int a_dtype;
+  int b_dtype;
+} SparcComplexFwdArgs;
+
+typedef struct SparcComplexBwdArgs {
+  const void* ar;
+  const void* ai;
+  const void* out_r;                   /* the forward's outputs */
+  const void* out_i;
+  const void* grad_out_r;
+  const void* grad_out_i;
+  void* grad_ar;
+  void* grad_ai;
+  void* grad_br;
+  void* grad_bi;
+  void* workspace;
+  size_t workspace_bytes;
+  long long batch;
+  long long length;
+  long long modes;
+  int a_dtype;
+  int b_dtype;
+} SparcComplexBwdArgs;
+
+long long sparc_complex_chunk_tokens(void);
+size_t sparc_complex_workspace_bytes(long long batch, long long length, long long modes);
+int sparc_complex_scan_forward(const SparcComplexFwdArgs* args, void* stream);
+int sparc_complex_scan_backward(const SparcComplexBwdArgs* args, void* stream);
+
 /* Diagnostics: per-kernel device time. While enabled, every kernel launch of this library is
  * bracketed by CUDA events on its stream (launches inside a stream capture are not timed).
  * sparc_timing_read waits for the recorded launches, writes per-kernel totals (milliseconds) and
  * launch counts for up to n kernel kinds (either pointer may be NULL), resets them, and returns
  * the number of kernel kinds, SPARC_TIMING_KERNELS; sparc_timing_kernel_name names kind `id`.
  * sparc_timing_enable returns the previous setting. */
-#define SPARC_TIMING_KERNELS 10
+#define SPARC_TIMING_KERNELS 23
 int sparc_timing_enable(int on);
 const char* sparc_timing_kernel_name(int id);
 int sparc_timing_read(double* ms, long long* launches, int n);
@@ -388,7 +442,50 @@ const char* sparc_rtrl_last_error(void);
  * a [rows, k] and b [n, k] row-major bfloat16 (k a multiple of 8, 16-byte aligned bases),
  * float32 accumulation, out [rows, n] bfloat16 (or float32 with out_f32). x (bfloat16,
  * [rows, n]) with skip ([n] float32), and dp ([rows, 2] float32) with c0, c1 ([n] float32),
- * are optional fused terms. `status` (device word) is or'ed with 4 if a bounded wait ran out. */
+ * are optional fused terms. `status` (device word) is or'ed with 4 if a bounded wait ran out.
+ * With a_mn (b_mn) the operand is stored transposed, a as [k, rows] (b as [k, n]), with rows
+ * (n) a multiple of 8 instead of k: the weight gradients x^T du and dy^T h, which contract over
+ * the tokens, run on x [tokens, width] and du [tokens, 2M] as they are (no transposed copies).
+ * Products with fewer output tiles (128 x 256) than SMs and a long k (the weight gradients of
+ * narrow layers) are split along k when `workspace` holds sparc_proj_gemm_workspace_bytes(rows,
+ * n, k) bytes (16-byte aligned; 0 bytes needed means no split): each k range's partial product
+ * is written there and a second launch adds them in order with the fused terms. A null or
+ * smaller workspace gives the unsplit product (same value to rounding).
+ *
+ * Column sums of the layer's backward (the controller projections' and the skip's gradients,
+ * layers.py:112-126): for x [rows, w] (dtype), dp [rows, 2] float32 and, optionally, dy
+ * [rows, w] (dtype), sparc_proj_colsum writes d_ctl [w + 1, 2] float32 (column j < w:
+ * sum_r x[r, j] dp[r, :], row w: sum_r dp[r, :]) and, with dy, d_skip [w] float32
+ * (sum_r dy[r, j] x[r, j]), in a fixed order (bitwise reproducible). `workspace` holds the
+ * partial sums: sparc_proj_colsum_workspace_bytes(rows, w) bytes. */
+typedef struct SparcProjColsumArgs {
+  const void* x;
+  const float* dp;
+  const void* dy;                      /* or NULL (no d_skip) */
+  float* d_ctl;
+  float* d_skip;                       /* or NULL */
+  void* workspace;
+  size_t workspace_bytes;
+  long long rows;
+  int w;
+  int dtype;
+} SparcProjColsumArgs;
+size_t sparc_proj_colsum_workspace_bytes(long long rows, int w);
+int sparc_proj_colsum(const SparcProjColsumArgs* args, void* stream);
+
+/* The layer forward's controller projections (layers.py:112-117, recurrence.py:20-38):
+ * p[r, :] = sum_j x[r, j] c[j, :] + c[w, :] for x [rows, w] (dtype) and c [w + 1, 2] float32
+ * (phase and retention controllers side by side, the biases in row w); p [rows, 2] float32. */
+typedef struct SparcProjRowdotArgs {
+  const void* x;
+  const float* c;
+  float* p;
+  long long rows;
+  int w;
+  int dtype;
+} SparcProjRowdotArgs;
+int sparc_proj_rowdot(const SparcProjRowdotArgs* args, void* stream);
+
 typedef struct SparcProjGemmArgs {
   const void* a;
   const void* b;
@@ -404,8 +501,13 @@ typedef struct SparcProjGemmArgs {
   int k;
   int out_f32;
   unsigned max_spin;                   /* bound of the mbarrier waits (0 = default) */
+  int a_mn;                            /* 1: a is stored transposed, [k, rows] (M-major) */
+  int b_mn;                            /* 1: b is stored transposed, [k, n] (N-major) */
+  void* workspace;                     /* split-k partials, or NULL */
+  size_t workspace_bytes;
 } SparcProjGemmArgs;
 
+size_t sparc_proj_gemm_workspace_bytes(long long rows, int n, int k);
 int sparc_proj_gemm(const SparcProjGemmArgs* args, void* stream);
 const char* sparc_proj_gemm_last_error(void);
 

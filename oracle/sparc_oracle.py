@@ -312,6 +312,36 @@ def real_scan_backward(a, b, g):
     return ga, gb
 
 
+def complex_scan_forward(ar, ai, br, bi):
+    """Generic complex diagonal scan h_t = a_t h_{t-1} + b_t (h_{-1} = 0) along axis 1,
+    forward/scan.py:701-722 (_complex_forward). Returns (out_r, out_i, last_r, last_i)."""
+    hr, hi = _scan(_f64(ar), _f64(ai), _f64(br), _f64(bi))
+    return hr, hi, hr[:, -1].copy(), hi[:, -1].copy()
+
+
+def complex_scan_backward(ar, ai, out_r, out_i, g_r, g_i):
+    """Adjoint of complex_scan_forward as backward/scan.py:131-160 (_complex_backward) computes
+    it, from the forward's outputs as the previous states: adj += g_t; grad_ar = Re(adj)
+    Re(h_{t-1}) + Im(adj) Im(h_{t-1}); grad_ai = Im(adj) Re(h_{t-1}) - Re(adj) Im(h_{t-1});
+    grad_b = adj; then adj = conj(a_t) adj. Returns (grad_ar, grad_ai, grad_br, grad_bi)."""
+    ar, ai, out_r, out_i, g_r, g_i = (_f64(t) for t in (ar, ai, out_r, out_i, g_r, g_i))
+    B, L, M = ar.shape
+    adj_r = np.zeros((B, M))
+    adj_i = np.zeros((B, M))
+    gar, gai, gbr, gbi = (np.empty((B, L, M)) for _ in range(4))
+    for t in range(L - 1, -1, -1):
+        adj_r = adj_r + g_r[:, t]
+        adj_i = adj_i + g_i[:, t]
+        pr = out_r[:, t - 1] if t > 0 else np.zeros((B, M))
+        pi = out_i[:, t - 1] if t > 0 else np.zeros((B, M))
+        gar[:, t] = adj_r * pr + adj_i * pi
+        gai[:, t] = -adj_r * pi + adj_i * pr
+        gbr[:, t] = adj_r
+        gbi[:, t] = adj_i
+        adj_r, adj_i = ar[:, t] * adj_r + ai[:, t] * adj_i, -ai[:, t] * adj_r + ar[:, t] * adj_i
+    return gar, gai, gbr, gbi
+
+
 def rms_norm(x, weight, eps=1e-6):
     """RMSNorm used by the 4-layer stack workload (no reference counterpart)."""
     x = _f64(x)

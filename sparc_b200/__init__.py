@@ -1,6 +1,7 @@
 """B200-native SPARC hot path: a drop-in for the reference ``sparc-kernal`` PyTorch API.
 
     from sparc_b200 import SPARCMixer, real_scan, real_chunk_scan, real_scan_with_last
+    from sparc_b200 import complex_scan, complex_scan_with_last
     from sparc_b200 import sparc_scan, sparc_chunk_scan, sparc_tiled_serial_scan  # scan level
 
 All compute runs in the sm_100a kernels of ``libsparc_b200.so`` (C ABI in
@@ -12,6 +13,7 @@ from .stack import SPARCBlock, SPARCStack
 from .projection import SPARCSequenceLayer, sparc_projection_states, sparc_sequence_layer
 from .rtrl import SPARCRTRLCell, initialize_carry, initialize_traces, rtrl_step, stored_rtrl_step
 from .real import real_chunk_scan, real_scan, real_scan_with_last
+from .complex import complex_scan, complex_scan_with_last
 from .scan import (sparc_chunk_scan, sparc_scan, sparc_scan_precomputed_decay, sparc_scan_with_last,
                    sparc_tiled_serial_scan, sparc_training_scan_dispatch)
 from . import _lib
@@ -39,7 +41,8 @@ def check_status(clear: bool = True) -> None:
 __all__ = ["SPARCMixer", "sparc_mixer", "sparc_block", "SPARCBlock", "SPARCStack", "sparc_decode_step", "sparc_eager_step",
            "SPARCSequenceLayer", "sparc_sequence_layer", "sparc_projection_states",
            "SPARCRTRLCell", "rtrl_step", "stored_rtrl_step", "initialize_carry", "initialize_traces",
-           "real_scan", "real_chunk_scan", "real_scan_with_last", "sparc_scan", "sparc_chunk_scan",
+           "real_scan", "real_chunk_scan", "real_scan_with_last", "complex_scan", "complex_scan_with_last",
+           "sparc_scan", "sparc_chunk_scan",
            "sparc_scan_with_last", "sparc_tiled_serial_scan", "sparc_training_scan_dispatch",
            "sparc_scan_precomputed_decay", "run_sequence", "prepare_decode", "run_decode_step", "check_status",
            "library_path"]

@@ -90,6 +90,23 @@ class RealBwdArgs(ctypes.Structure):
     ]
 
 
+class ComplexFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("ar", _vp), ("ai", _vp), ("br", _vp), ("bi", _vp), ("out_r", _vp), ("out_i", _vp),
+        ("last_r", _vp), ("last_i", _vp), ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("batch", _ll), ("length", _ll), ("modes", _ll), ("a_dtype", ctypes.c_int), ("b_dtype", ctypes.c_int),
+    ]
+
+
+class ComplexBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("ar", _vp), ("ai", _vp), ("out_r", _vp), ("out_i", _vp), ("grad_out_r", _vp), ("grad_out_i", _vp),
+        ("grad_ar", _vp), ("grad_ai", _vp), ("grad_br", _vp), ("grad_bi", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("batch", _ll), ("length", _ll), ("modes", _ll), ("a_dtype", ctypes.c_int), ("b_dtype", ctypes.c_int),
+    ]
+
+
 class RtrlStepArgs(ctypes.Structure):
     _fields_ = [
         ("x", _vp), ("content", _vp), ("projections", _vp), ("reset", _vp), ("state", _vp), ("new_state", _vp),
@@ -111,7 +128,19 @@ class ProjGemmArgs(ctypes.Structure):
     _fields_ = [
         ("a", _vp), ("b", _vp), ("out", _vp), ("x", _vp), ("skip", _vp), ("dp", _vp), ("c0", _vp), ("c1", _vp),
         ("status", _vp), ("rows", _ll), ("n", ctypes.c_int), ("k", ctypes.c_int), ("out_f32", ctypes.c_int),
-        ("max_spin", ctypes.c_uint),
+        ("max_spin", ctypes.c_uint), ("a_mn", ctypes.c_int), ("b_mn", ctypes.c_int),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class ProjRowdotArgs(ctypes.Structure):
+    _fields_ = [("x", _vp), ("c", _vp), ("p", _vp), ("rows", _ll), ("w", ctypes.c_int), ("dtype", ctypes.c_int)]
+
+
+class ProjColsumArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("dp", _vp), ("dy", _vp), ("d_ctl", _vp), ("d_skip", _vp), ("workspace", _vp),
+        ("workspace_bytes", ctypes.c_size_t), ("rows", _ll), ("w", ctypes.c_int), ("dtype", ctypes.c_int),
     ]
 
 
@@ -144,6 +173,10 @@ SIGNATURES = {
     "sparc_real_workspace_bytes": (ctypes.c_size_t, [_ll, _ll, _ll, ctypes.c_int]),
     "sparc_real_scan_forward": (ctypes.c_int, [ctypes.POINTER(RealFwdArgs), _vp]),
     "sparc_real_scan_backward": (ctypes.c_int, [ctypes.POINTER(RealBwdArgs), _vp]),
+    "sparc_complex_chunk_tokens": (_ll, []),
+    "sparc_complex_workspace_bytes": (ctypes.c_size_t, [_ll, _ll, _ll]),
+    "sparc_complex_scan_forward": (ctypes.c_int, [ctypes.POINTER(ComplexFwdArgs), _vp]),
+    "sparc_complex_scan_backward": (ctypes.c_int, [ctypes.POINTER(ComplexBwdArgs), _vp]),
     "sparc_read_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint), _vp]),
     "sparc_clear_status": (ctypes.c_int, [_vp, _vp]),
     "sparc_rtrl_saved_floats": (ctypes.c_int, []),
@@ -152,6 +185,10 @@ SIGNATURES = {
     "sparc_rtrl_last_error": (ctypes.c_char_p, []),
     "sparc_proj_gemm": (ctypes.c_int, [ctypes.POINTER(ProjGemmArgs), _vp]),
     "sparc_proj_gemm_last_error": (ctypes.c_char_p, []),
+    "sparc_proj_colsum_workspace_bytes": (ctypes.c_size_t, [_ll, ctypes.c_int]),
+    "sparc_proj_gemm_workspace_bytes": (ctypes.c_size_t, [_ll, ctypes.c_int, ctypes.c_int]),
+    "sparc_proj_colsum": (ctypes.c_int, [ctypes.POINTER(ProjColsumArgs), _vp]),
+    "sparc_proj_rowdot": (ctypes.c_int, [ctypes.POINTER(ProjRowdotArgs), _vp]),
     "sparc_exchange_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int]),
     "sparc_peer_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int, _ll]),
     "sparc_peer_buffer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
@@ -245,8 +282,11 @@ class _Workspaces:
             self._ws[key] = ws
         return ws
 
-    def all(self):
-        return list(self._ws.values())
+    def all(self, kinds=("mixer", "real")):
+        """The cached workspaces of the given kinds: by default those that begin with the
+        library's launch state and status word (the "gemm" and "complex" kinds hold scratch
+        values from their first byte)."""
+        return [ws for (_, _, kind), ws in self._ws.items() if kind in kinds]
 
 
 WORKSPACES = _Workspaces()
@@ -267,7 +307,7 @@ def kernel_times(reset_only: bool = False):
     """Per-kernel device time recorded since the last call while timing was enabled
     (sparc_timing_enable): {kernel name: (total ms, launches)} for kernels that ran."""
     L = lib()
-    n = 16
+    n = 32
     ms = (ctypes.c_double * n)()
     cnt = (ctypes.c_longlong * n)()
     k = L.sparc_timing_read(ms, cnt, n)

@@ -855,6 +855,26 @@ static cudaError_t launch_scan(const Plan& pl, const ScanParams& sp, cudaStream_
                    dim3(kScanThreads, 1, 1), kScanQ, 0, s, sp);
 }
 
+// The carry scan for other users of chunk maps (the generic complex scan): maps [rows, chunks,
+// M] float4, no initial state, spans as the mixer plans them.
+cudaError_t launch_chunk_carry_scan(const float4* maps, float2* out, int rows, int M, int chunks, int reverse,
+                                    float* final_r, float* final_i, cudaStream_t s) {
+  ScanParams sp;
+  sp.agg = maps;
+  sp.out = out;
+  sp.init_r = nullptr;
+  sp.init_i = nullptr;
+  sp.final_r = final_r;
+  sp.final_i = final_i;
+  sp.M = M;
+  sp.Mp = M;
+  sp.chunks = chunks;
+  sp.span = (chunks + kScanSpans - 1) / kScanSpans;
+  sp.reverse = reverse;
+  return launch_ex((const void*)mixer_carry_scan_kernel, dim3(kScanQ * ((M + 31) / 32), (unsigned)rows),
+                   dim3(kScanThreads, 1, 1), kScanQ, 0, s, sp);
+}
+
 static int launch_error(cudaError_t e) {
   if (e == cudaSuccess) return SPARC_OK;
   set_err(cudaGetErrorString(e));

@@ -28,7 +28,10 @@ const char* const kNames[kTimeKernels] = {
     "mixer_bwd_summary_kernel", "mixer_carry_scan_kernel(bwd)", "mixer_bwd_grad_kernel",
     "mixer_reduce_kernel",      "real_fwd_kernel",              "real_bwd_kernel",
     "decode_kernel",            "rtrl_step_kernel",             "rtrl_grad_kernel",
-    "proj_gemm_kernel",         "peer_allreduce_kernel"};
+    "proj_gemm_kernel",         "peer_allreduce_kernel",        "proj_rowdot_kernel",
+    "proj_colsum_kernel",       "proj_gemm_finish_kernel",      "complex_fwd_summary_kernel",
+    "complex_carry_scan(fwd)",  "complex_fwd_replay_kernel",    "complex_bwd_summary_kernel",
+    "complex_carry_scan(bwd)",  "complex_bwd_grad_kernel"};
 
 cudaEvent_t take_event() {
   if (!g_pool.empty()) {

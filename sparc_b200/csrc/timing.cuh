@@ -34,6 +34,15 @@ enum KernelId {
   kTimeRtrlGrad,
   kTimeProjGemm,
   kTimePeerAllreduce,
+  kTimeProjRowdot,
+  kTimeProjColsum,
+  kTimeProjGemmFinish,
+  kTimeComplexFwdSummary,
+  kTimeComplexFwdScan,
+  kTimeComplexFwdReplay,
+  kTimeComplexBwdSummary,
+  kTimeComplexBwdScan,
+  kTimeComplexBwdGrad,
   kTimeKernels
 };
 

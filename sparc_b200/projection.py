@@ -140,13 +140,16 @@ class _SparcCoreFunction(torch.autograd.Function):
 
 
 class _SequenceLayerTC(torch.autograd.Function):
-    """The whole layer with its activation products on the tensor cores (sparc_proj_gemm,
-    tcgen05): u = x Wc and the readout in the forward; dh = dy Ro and dx = du Wc^T + dp c^T +
-    skip dy in the backward. bfloat16 activations: bf16 operands, the skip and rank-2 terms fused
-    into the products' epilogues. float32 activations: each product through the three-term bf16
-    split (gemm.split3, relative error ~1e-5), the skip terms as torch adds. The weight gradients
-    (x^T du, dy^T h) and the two controller projections stay torch products (float32 for the
-    projections, whose tanh sets every mode's controls)."""
+    """The whole layer on the library's kernels: the controller projections p = [x, 1] c
+    (sparc_proj_rowdot), the content product u = x Wc and the readout on the tensor cores
+    (sparc_proj_gemm, tcgen05) around the recurrence (the mixer kernels' projection mode); in the
+    backward dh = dy Ro, dx = du Wc^T + dp c^T + skip dy and the weight gradients x^T du and
+    dy^T h on the tensor cores (the last two with the token-major operands as stored), and the
+    controllers' and skip's gradients as column sums (sparc_proj_colsum). bfloat16 activations:
+    bf16 operands, the skip and rank-2 terms fused into the products' epilogues. float32
+    activations: each product through the three-term bf16 split (gemm.split3, relative error
+    ~1e-5), the skip terms as adds. Widths that are not multiples of 8 are zero-padded to whole
+    16-byte rows for the tensor maps (the padding contributes zeros and is cut from the results)."""
 
     @staticmethod
     def forward(ctx, x, content_real, content_imag, phase_controller, retention_controller, decay_log,
@@ -158,22 +161,26 @@ class _SequenceLayerTC(torch.autograd.Function):
         M = content_real.shape[1]
         f32 = x.dtype == torch.float32
         xf = x.reshape(B * T, W)
+        xp = gemm.pad8(xf)                                                          # [BT, W8]
         wc = torch.cat((content_real, content_imag), dim=1).detach().float()       # [W, 2M]
         ro = torch.cat((readout_real, -readout_imag), dim=1).detach().float()      # [W, 2M]
         ctl = torch.stack((phase_controller, retention_controller), dim=1).detach().float()  # [W+1, 2]
-        p = torch.addmm(ctl[W], xf.float(), ctl[:W]).view(B, T, 2)
+        p = gemm.proj_rowdot(xf, ctl).view(B, T, 2)
+        wct = gemm.pad8(wc.t().contiguous())                                       # [2M, W8]
         if f32:
-            u = gemm.proj_gemm_f32(xf, wc.t()).view(B, T, 2 * M)
+            u = gemm.proj_gemm_f32(xp, wct).view(B, T, 2 * M)
         else:
-            u = gemm.proj_gemm(xf, wc.t().to(torch.bfloat16).contiguous()).view(B, T, 2 * M)
+            u = gemm.proj_gemm(xp, wct.to(torch.bfloat16).contiguous()).view(B, T, 2 * M)
         h0 = None if h0_r is None else (h0_r, h0_i)
         h, lr, li, sv = _core_forward(u, p, (decay_log, frequency_log, write_log_gain, write_phase_response,
                                              write_retention_response), h0, reset, lin, max_spin)
         skipf = skip.detach().float()
+        hp = gemm.pad8(h.view(B * T, 2 * M))                                       # [BT, 2M8]
+        rop = gemm.pad8(ro)                                                        # [W, 2M8]
         if f32:
-            y = torch.addcmul(gemm.proj_gemm_f32(h.view(B * T, 2 * M), ro), skipf, xf).view(B, T, W)
+            y = torch.addcmul(gemm.proj_gemm_f32(hp, rop), skipf, xf).view(B, T, W)
         else:
-            y = gemm.proj_gemm(h.view(B * T, 2 * M), ro.to(torch.bfloat16).contiguous(), x=xf, skip=skipf).view(B, T, W)
+            y = gemm.proj_gemm(hp, rop.to(torch.bfloat16).contiguous(), x=xf, skip=skipf).view(B, T, W)
         ctx.sv = sv
         ctx.save_for_backward(x, h, wc, ro, ctl, skipf)
         ctx.set_materialize_grads(False)
@@ -190,35 +197,40 @@ class _SequenceLayerTC(torch.autograd.Function):
         xf = x.reshape(B * T, W)
         hf = h.reshape(B * T, M2)
         dyf = None if dy is None else dy.to(x.dtype).reshape(B * T, W).contiguous()
-        if dyf is None:
-            dh = None
-        elif f32:
-            dh = gemm.proj_gemm_f32(dyf, ro.t()).view(B, T, M2)
-        else:
-            dh = gemm.proj_gemm(dyf, ro.t().to(torch.bfloat16).contiguous()).view(B, T, M2)
+        dh = None
+        if dyf is not None:
+            dyp = gemm.pad8(dyf)                                                   # [BT, W8]
+            rot = gemm.pad8(ro.t().contiguous())                                   # [2M, W8]
+            if f32:
+                dh = gemm.proj_gemm_f32(dyp, rot).view(B, T, M2)
+            else:
+                dh = gemm.proj_gemm(dyp, rot.to(torch.bfloat16).contiguous()).view(B, T, M2)
         du, dp, g, gh0 = _core_backward(ctx.sv, dh, dlast_r, dlast_i)
         ctx.sv = None
         du2 = du.view(B * T, M2)
         dp2 = dp.view(B * T, 2)
+        dup = gemm.pad8(du2)                                                       # [BT, 2M8]
+        wcp = gemm.pad8(wc)                                                        # [W, 2M8]
         c0, c1 = ctl[:W, 0].contiguous(), ctl[:W, 1].contiguous()
         if f32:
-            dx = gemm.proj_gemm_f32(du2, wc, dp=dp2, c0=c0, c1=c1)
+            dx = gemm.proj_gemm_f32(dup, wcp, dp=dp2, c0=c0, c1=c1)
             if dyf is not None:
                 dx = torch.addcmul(dx, skip, dyf)
         elif dyf is not None:
-            dx = gemm.proj_gemm(du2, wc.to(torch.bfloat16).contiguous(), x=dyf, skip=skip, dp=dp2, c0=c0, c1=c1)
+            dx = gemm.proj_gemm(dup, wcp.to(torch.bfloat16).contiguous(), x=dyf, skip=skip, dp=dp2, c0=c0, c1=c1)
         else:
-            dx = gemm.proj_gemm(du2, wc.to(torch.bfloat16).contiguous(), dp=dp2, c0=c0, c1=c1)
+            dx = gemm.proj_gemm(dup, wcp.to(torch.bfloat16).contiguous(), dp=dp2, c0=c0, c1=c1)
+        # weight gradients over the tokens, the operands token-major as stored: x^T du, dy^T h
+        xp = gemm.pad8(xf)
+        prod = gemm.proj_gemm_f32 if f32 else (lambda a, b, **kw: gemm.proj_gemm(a, b, torch.float32, **kw))
+        dwc = prod(xp, dup, a_mn=True, b_mn=True)[:W, :M2]                        # [W, 2M]
         if dyf is not None:
-            dro = (dyf.t() @ hf).float()                                           # [W, 2M]
-            dskip = (dyf.float() * xf.float()).sum(0)
+            dro = prod(dyp, gemm.pad8(hf), a_mn=True, b_mn=True)[:W, :M2]
         else:
             dro = torch.zeros((W, M2), dtype=torch.float32, device=x.device)
+        dctl, dskip = gemm.proj_colsum(xf, dp2, dyf)
+        if dskip is None:
             dskip = torch.zeros(W, dtype=torch.float32, device=x.device)
-        dwc = (xf.t() @ du2).float()                                               # [W, 2M]
-        dctl = torch.empty((W + 1, 2), dtype=torch.float32, device=x.device)
-        dctl[:W] = xf.float().t() @ dp2
-        dctl[W] = dp2.sum(0)
         M = M2 // 2
         return (dx.view(B, T, W), dwc[:, :M], dwc[:, M:], dctl[:, 0], dctl[:, 1], *g, dro[:, :M], -dro[:, M:],
                 dskip, gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None)
@@ -230,22 +242,77 @@ def _check_activation(content_activation: str) -> bool:
     return content_activation == "linear"
 
 
+class _ProjectionInputs(torch.autograd.Function):
+    """(u [B, T, 2M] x.dtype, p [B, T, 2] float32) = (x [content_real | content_imag],
+    [x, 1] [phase_controller | retention_controller]) on the library's kernels (tcgen05 product,
+    row dots), with their adjoints (dx = du Wc^T + dp c^T, x^T du token-major, column sums)."""
+
+    @staticmethod
+    def forward(ctx, x, content_real, content_imag, phase_controller, retention_controller):
+        from . import gemm
+
+        B, T, W = x.shape
+        M = content_real.shape[1]
+        xf = x.reshape(B * T, W)
+        wc = torch.cat((content_real, content_imag), dim=1).detach().float()       # [W, 2M]
+        ctl = torch.stack((phase_controller, retention_controller), dim=1).detach().float()
+        p = gemm.proj_rowdot(xf, ctl).view(B, T, 2)
+        wct = gemm.pad8(wc.t().contiguous())
+        if x.dtype == torch.float32:
+            u = gemm.proj_gemm_f32(gemm.pad8(xf), wct).view(B, T, 2 * M)
+        else:
+            u = gemm.proj_gemm(gemm.pad8(xf), wct.to(torch.bfloat16).contiguous()).view(B, T, 2 * M)
+        ctx.save_for_backward(x, wc, ctl)
+        ctx.set_materialize_grads(False)
+        return u, p
+
+    @staticmethod
+    def backward(ctx, du, dp):
+        from . import gemm
+
+        x, wc, ctl = ctx.saved_tensors
+        B, T, W = x.shape
+        M2 = wc.shape[1]
+        M = M2 // 2
+        f32 = x.dtype == torch.float32
+        xf = x.reshape(B * T, W)
+        du2 = torch.zeros((B * T, M2), dtype=x.dtype, device=x.device) if du is None else \
+            du.to(x.dtype).reshape(B * T, M2).contiguous()
+        dp2 = torch.zeros((B * T, 2), dtype=torch.float32, device=x.device) if dp is None else \
+            dp.float().reshape(B * T, 2).contiguous()
+        dup, wcp = gemm.pad8(du2), gemm.pad8(wc)
+        c0, c1 = ctl[:W, 0].contiguous(), ctl[:W, 1].contiguous()
+        need = ctx.needs_input_grad
+        dx = dwc = dctl = None
+        if need[0]:
+            if f32:
+                dx = gemm.proj_gemm_f32(dup, wcp, dp=dp2, c0=c0, c1=c1).view(B, T, W)
+            else:
+                dx = gemm.proj_gemm(dup, wcp.to(torch.bfloat16).contiguous(), dp=dp2, c0=c0, c1=c1).view(B, T, W)
+        if need[1] or need[2]:
+            if f32:
+                dwc = gemm.proj_gemm_f32(gemm.pad8(xf), dup, a_mn=True, b_mn=True)[:W, :M2]
+            else:
+                dwc = gemm.proj_gemm(gemm.pad8(xf), dup, torch.float32, a_mn=True, b_mn=True)[:W, :M2]
+        if need[3] or need[4]:
+            dctl, _ = gemm.proj_colsum(xf, dp2)
+        return (dx, None if dwc is None else dwc[:, :M], None if dwc is None else dwc[:, M:],
+                None if dctl is None else dctl[:, 0], None if dctl is None else dctl[:, 1])
+
+
 def sparc_projection_states(x, params, content_activation: str = "tanh", state=None, segment_pos=None,
                             reset_first: bool = False, max_spin: int = 0):
     """The recurrent core of the projection variant: ((h_r, h_i) [B, T, M] each in x.dtype,
     (last_r, last_i) [B, M] float32) for x [B, T, W] and a mapping holding the JAX layer's
     recurrent parameters (content_real/imag [W, M], the two controllers [W+1], the five modal
-    vectors [M])."""
+    vectors [M]); differentiable in x and every parameter."""
     lin = _check_activation(content_activation)
     if x.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"supported activations are float32 and bfloat16, got {x.dtype}")
     _lib.require_cuda(x, "x")
-    W = x.shape[-1]
     M = params["decay_log"].shape[0]
-    wc = torch.cat((params["content_real"], params["content_imag"]), dim=1)  # [W, 2M]
-    u = torch.matmul(x, wc.to(x.dtype)).contiguous()
-    ctl = torch.stack((params["phase_controller"], params["retention_controller"]), dim=1)  # [W+1, 2]
-    p = torch.addmm(ctl[W], x.reshape(-1, W).float(), ctl[:W]).reshape(*x.shape[:2], 2)
+    u, p = _ProjectionInputs.apply(x.contiguous(), params["content_real"], params["content_imag"],
+                                   params["phase_controller"], params["retention_controller"])
     h0_r, h0_i = (None, None) if state is None else state
     reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
     h, lr, li = _SparcCoreFunction.apply(
@@ -255,30 +322,19 @@ def sparc_projection_states(x, params, content_activation: str = "tanh", state=N
 
 def sparc_sequence_layer(x, params, content_activation: str = "tanh", state=None, segment_pos=None,
                          reset_first: bool = False, max_spin: int = 0):
-    """Functional SPARCSequenceLayer: (y [B, T, W], (last_r, last_i)). When the widths are whole
-    16-byte rows of bf16 (W and 2M multiples of 8) the activation products run on the tensor
-    cores (_SequenceLayerTC; float32 through the three-term split); otherwise they are torch
-    products around the same recurrence kernels."""
-    from . import gemm
-
-    W = x.shape[-1]
-    M = params["decay_log"].shape[0]
-    if x.dtype in (torch.bfloat16, torch.float32) and gemm.supported(W, 2 * M):
-        lin = _check_activation(content_activation)
-        _lib.require_cuda(x, "x")
-        h0_r, h0_i = (None, None) if state is None else state
-        reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
-        y, lr, li = _SequenceLayerTC.apply(
-            x.contiguous(), params["content_real"], params["content_imag"], params["phase_controller"],
-            params["retention_controller"], *[params[n] for n in _CORE_PARAMS], params["readout_real"],
-            params["readout_imag"], params["skip"], h0_r, h0_i, reset, lin, int(max_spin))
-        return y, (lr, li)
-    (hr, hi), last = sparc_projection_states(x, params, content_activation, state, segment_pos,
-                                             reset_first, max_spin)
-    ro = torch.cat((params["readout_real"], -params["readout_imag"]), dim=1).to(x.dtype)  # [W, 2M]
-    h = torch.cat((hr, hi), dim=-1)
-    y = torch.addcmul(torch.matmul(h, ro.t()), params["skip"].to(x.dtype), x)
-    return y, last
+    """Functional SPARCSequenceLayer: (y [B, T, W], (last_r, last_i)), every product and the
+    recurrence in the library's kernels (_SequenceLayerTC)."""
+    lin = _check_activation(content_activation)
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"supported activations are float32 and bfloat16, got {x.dtype}")
+    _lib.require_cuda(x, "x")
+    h0_r, h0_i = (None, None) if state is None else state
+    reset = reset_mask(segment_pos, reset_first, x.shape[:2], x.device)
+    y, lr, li = _SequenceLayerTC.apply(
+        x.contiguous(), params["content_real"], params["content_imag"], params["phase_controller"],
+        params["retention_controller"], *[params[n] for n in _CORE_PARAMS], params["readout_real"],
+        params["readout_imag"], params["skip"], h0_r, h0_i, reset, lin, int(max_spin))
+    return y, (lr, li)
 
 
 class SPARCSequenceLayer(nn.Module):

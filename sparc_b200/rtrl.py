@@ -126,10 +126,14 @@ def rtrl_step(params, carry, inputs: torch.Tensor, reset=None, content_activatio
         raise ValueError(f"state must have shape {(B, M)}")
     _lib.require_cuda(inputs, "inputs")
     x = inputs.float()
-    wc = torch.cat((params["content_real"], params["content_imag"]), dim=1).detach().float()
-    ctl = torch.stack((params["phase_controller"], params["retention_controller"]), dim=1).detach().float()
-    u = x @ wc
-    p = torch.addmm(ctl[W], x, ctl[:W])
+    # the content product and controller projections on the library's kernels (weights detached:
+    # as in the JAX custom VJP, the parameters' gradients come from the traces)
+    from .projection import _ProjectionInputs
+
+    u, p = _ProjectionInputs.apply(x[:, None].contiguous(), params["content_real"].detach(),
+                                   params["content_imag"].detach(), params["phase_controller"].detach(),
+                                   params["retention_controller"].detach())
+    u, p = u[:, 0], p[:, 0]
     r = None if reset is None else reset.to(device=x.device, dtype=torch.bool).to(torch.uint8).contiguous()
     out = _RTRLStepFunction.apply(u, p, x, r, state, content_activation == "linear",
                                   *[traces[n] for n in TRACE_NAMES], *[params[n] for n in TRACE_NAMES])

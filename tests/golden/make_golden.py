@@ -8,7 +8,8 @@ Run from the repository root, in a container where the reference is mounted:
 It imports the reference package ``sparc-kernal`` read-only and runs:
 
 * its Triton kernels (the chunked SPARC scan, the tiled serial scan with h0/resets, the fused
-  decode kernel, the write kernel and the real scans) under the Triton CPU interpreter
+  decode kernel, the write kernel, the real scans and the generic complex scan) under the Triton
+  CPU interpreter
   (``TRITON_INTERPRET=1``), in float32 / bfloat16 exactly as they would run on a GPU;
 * its eager torch path (``framework_eager`` backend) after ``module.double()``. Note that the
   reference casts the controller projection and the write path to float32 even then
@@ -247,6 +248,41 @@ def real_mixed_case(sparc):
     np.savez_compressed(os.path.join(HERE, "real_mixed.npz"), **rec)
 
 
+def complex_case(sparc):
+    """The generic complex scans (complex_scan forward and backward, complex_scan_with_last):
+    float32 throughout, and bfloat16 b with float32 a (out in b's dtype, every gradient in a's,
+    the backward reading the bfloat16 outputs as the previous states). |a| close to 1 with a
+    rotation, a ragged length, and modes beyond one 128-mode block."""
+    from backward.scan import complex_scan, complex_scan_with_last
+
+    B, L, M = 2, 40, 136
+    gen = torch.Generator().manual_seed(31)
+    rad = 0.9 + 0.099 * torch.rand(B, L, M, generator=gen)
+    ang = 0.3 * torch.randn(B, L, M, generator=gen)
+    ar, ai = rad * torch.cos(ang), rad * torch.sin(ang)
+    br, bi = 0.5 * torch.randn(B, L, M, generator=gen), 0.5 * torch.randn(B, L, M, generator=gen)
+    gr, gi = torch.randn(B, L, M, generator=gen), torch.randn(B, L, M, generator=gen)
+    rec = {"ar": _np(ar), "ai": _np(ai), "br": _np(br), "bi": _np(bi), "gr": _np(gr), "gi": _np(gi)}
+    for name, dt in (("f32", torch.float32), ("bf16b", torch.bfloat16)):
+        t = [ar.clone().requires_grad_(True), ai.clone().requires_grad_(True),
+             br.to(dt).clone().requires_grad_(True), bi.to(dt).clone().requires_grad_(True)]
+        out_r, out_i = complex_scan(*t)
+        (out_r.float() * gr).sum().backward(retain_graph=True)
+        (out_i.float() * gi).sum().backward()
+        rec[name + "_out_r"], rec[name + "_out_i"] = _np(out_r), _np(out_i)
+        rec[name + "_out_dtype_is_b"] = np.array(int(out_r.dtype == dt))
+        for k, tt in zip(("ar", "ai", "br", "bi"), t):
+            rec[name + "_grad_" + k] = _np(tt.grad)
+        if name == "bf16b":
+            rec["bf16b_br"], rec["bf16b_bi"] = _np(t[2].detach()), _np(t[3].detach())
+    o_r, o_i, l_r, l_i = complex_scan_with_last(ar, ai, br, bi)
+    rec["with_last_out_r"], rec["with_last_out_i"] = _np(o_r), _np(o_i)
+    rec["with_last_last_r"], rec["with_last_last_i"] = _np(l_r), _np(l_i)
+    # every value here is a float32 (or bfloat16) value: stored as float32, exactly
+    np.savez_compressed(os.path.join(HERE, "complex.npz"),
+                        **{k: (v.astype(np.float32) if v.dtype == np.float64 else v) for k, v in rec.items()})
+
+
 def real_case(sparc):
     from backward.scan import real_chunk_scan, real_scan, real_scan_with_last
 
@@ -339,6 +375,7 @@ CASES = {
     "decode_grad": decode_grad_case,
     "real": real_case,
     "real_mixed": real_mixed_case,
+    "complex": complex_case,
     "tiled": tiled_case,
 }
 

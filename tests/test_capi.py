@@ -43,7 +43,9 @@ def test_struct_layouts_match_header():
                       ("SparcDecodeArgs", _lib.DecodeArgs), ("SparcRealFwdArgs", _lib.RealFwdArgs),
                       ("SparcRealBwdArgs", _lib.RealBwdArgs), ("SparcRtrlStepArgs", _lib.RtrlStepArgs),
                       ("SparcRtrlGradArgs", _lib.RtrlGradArgs), ("SparcProjGemmArgs", _lib.ProjGemmArgs),
-                      ("SparcPeerAllreduceArgs", _lib.PeerAllreduceArgs)):
+                      ("SparcPeerAllreduceArgs", _lib.PeerAllreduceArgs),
+                      ("SparcComplexFwdArgs", _lib.ComplexFwdArgs), ("SparcComplexBwdArgs", _lib.ComplexBwdArgs),
+                      ("SparcProjColsumArgs", _lib.ProjColsumArgs), ("SparcProjRowdotArgs", _lib.ProjRowdotArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\}" % cname, src, flags=re.S).group(1)
         fields = re.findall(r"(\w+)\s*(?:\[\w+\])?\s*;", body)
         assert fields == [f[0] for f in py._fields_], cname
@@ -57,6 +59,9 @@ def test_host_only_queries(lib):
     assert lib.sparc_mixer_carry_chunks(2048, _lib.DTYPE_BF16) == 128
     assert lib.sparc_mixer_carry_chunks(37, _lib.DTYPE_F32) == 5
     assert lib.sparc_real_carry_chunks(33) == 2 and lib.sparc_real_chunk_tokens() == 32
+    assert lib.sparc_complex_chunk_tokens() == 32
+    assert lib.sparc_complex_workspace_bytes(2, 33, 5) == 256 + 2 * 2 * 5 * 24
+    assert lib.sparc_complex_workspace_bytes(70000, 8, 8) == 0  # beyond the launch grid
     assert lib.sparc_mixer_controls_floats() == 16  # the per-token record the kernels write
     assert lib.sparc_mixer_mask_words(2048) == 64 and lib.sparc_mixer_mask_words(600) == 32
     assert lib.sparc_mixer_mask_words(7) == 0

@@ -106,8 +106,12 @@ def test_gemm_operand_errors_precede_the_device_check():
     a = torch.randn(4, 8).bfloat16()
     with pytest.raises(TypeError, match="bfloat16"):
         gemm.proj_gemm(a.float(), a)
-    with pytest.raises(ValueError, match=r"\[rows, k\]"):
+    with pytest.raises(ValueError, match="contraction lengths"):
         gemm.proj_gemm(a, a[:, :4])
+    with pytest.raises(ValueError, match="contraction lengths"):
+        gemm.proj_gemm(a, a, a_mn=True)  # a [k=4, rows=8] against b [n=4, k=8]
+    with pytest.raises(ValueError, match="two matrices"):
+        gemm.proj_gemm(a[0], a)
     with pytest.raises(RuntimeError, match="CUDA"):
         gemm.proj_gemm(a, a)
 

@@ -125,6 +125,82 @@ def test_gemm_stays_in_bounds(rows, n, k):
         assert float((out.float() - ref).norm() / ref.norm()) < 1e-2
 
 
+@pytest.mark.parametrize("rows,n,k", [(72, 200, 24000), (136, 72, 24)])
+def test_gemm_split_and_fused_stay_in_bounds(rows, n, k):
+    """The split-k path (few output tiles, long k: the partials in the workspace, the finish
+    launch writing the output) and the fused epilogue's staged vectors at ragged tile edges."""
+    from sparc_b200 import gemm
+
+    at = torch.randn(k, rows, device="cuda").bfloat16()  # token-major operands
+    bt = torch.randn(k, n, device="cuda").bfloat16()
+    x = torch.randn(rows, n, device="cuda").bfloat16()
+    skip, c0, c1 = (torch.randn(n, device="cuda") for _ in range(3))
+    dp = torch.randn(rows, 2, device="cuda")
+    ref = at.float().t() @ bt.float() + skip * x.float() + dp[:, :1] * c0 + dp[:, 1:] * c1
+    for dtype in (torch.float32, torch.bfloat16):
+        ob, out = _guarded((rows, n), dtype)
+        gemm.proj_gemm(at, bt, dtype, x=x, skip=skip, dp=dp, c0=c0, c1=c1, out=out, a_mn=True, b_mn=True)
+        torch.cuda.synchronize()
+        assert _intact(ob, dtype)
+        assert float((out.float() - ref).norm() / ref.norm()) < 1e-2
+    assert gemm.gemm_status("cuda") == 0
+
+
+@pytest.mark.parametrize("rows,w,dtype", [(37, 2048, torch.bfloat16), (5, 700, torch.float32),
+                                          (300, 10, torch.bfloat16)])
+def test_rowdot_colsum_stay_in_bounds(rows, w, dtype):
+    from sparc_b200 import _lib
+
+    lib = _lib.lib()
+    x = torch.randn(rows, w, device="cuda").to(dtype)
+    dy = torch.randn(rows, w, device="cuda").to(dtype)
+    dp = torch.randn(rows, 2, device="cuda")
+    c = torch.randn(w + 1, 2, device="cuda")
+    pb, p = _guarded((rows, 2), torch.float32)
+    a = _lib.ProjRowdotArgs(x.data_ptr(), c.data_ptr(), p.data_ptr(), rows, w, _lib.dtype_code(dtype))
+    assert lib.sparc_proj_rowdot(ctypes.byref(a), torch.cuda.current_stream().cuda_stream) == 0
+    db, d_ctl = _guarded((w + 1, 2), torch.float32)
+    sb, d_skip = _guarded((w,), torch.float32)
+    wb, ws = _guarded((lib.sparc_proj_colsum_workspace_bytes(rows, w) // 4,), torch.float32)
+    a = _lib.ProjColsumArgs(x.data_ptr(), dp.data_ptr(), dy.data_ptr(), d_ctl.data_ptr(), d_skip.data_ptr(),
+                            ws.data_ptr(), ws.numel() * 4, rows, w, _lib.dtype_code(dtype))
+    assert lib.sparc_proj_colsum(ctypes.byref(a), torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert _intact(pb, torch.float32) and _intact(db, torch.float32) and _intact(sb, torch.float32)
+    assert _intact(wb, torch.float32)
+    xd = x.double()
+    assert float((p.double() - (xd @ c[:w].double() + c[w].double())).norm()) < 1e-3 * float(p.double().norm())
+
+
+@pytest.mark.parametrize("B,L,M,dtype", [(2, 37, 300, torch.float32), (1, 1, 1, torch.float32),
+                                         (3, 70, 130, torch.bfloat16)])
+def test_complex_scan_stays_in_bounds(B, L, M, dtype):
+    from sparc_b200 import _lib
+
+    lib = _lib.lib()
+    dt = _lib.dtype_code(dtype)
+    ar, ai = (torch.rand(B, L, M, device="cuda") * 0.6).to(dtype), (torch.rand(B, L, M, device="cuda") * 0.3).to(dtype)
+    br, bi = torch.randn(B, L, M, device="cuda").to(dtype), torch.randn(B, L, M, device="cuda").to(dtype)
+    orb, o_r = _guarded((B, L, M), dtype)
+    oib, o_i = _guarded((B, L, M), dtype)
+    lrb, l_r = _guarded((B, M), torch.float32)
+    lib_, l_i = _guarded((B, M), torch.float32)
+    wsb, ws = _guarded((lib.sparc_complex_workspace_bytes(B, L, M) // 4 + 4,), torch.float32)
+    f = _lib.ComplexFwdArgs(ar.data_ptr(), ai.data_ptr(), br.data_ptr(), bi.data_ptr(), o_r.data_ptr(), o_i.data_ptr(),
+                            l_r.data_ptr(), l_i.data_ptr(), ws.data_ptr(), ws.numel() * 4, B, L, M, dt, dt)
+    assert lib.sparc_complex_scan_forward(ctypes.byref(f), torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    for buf, t in ((orb, dtype), (oib, dtype), (lrb, torch.float32), (lib_, torch.float32), (wsb, torch.float32)):
+        assert _intact(buf, t)
+    gr, gi = torch.randn(B, L, M, device="cuda").to(dtype), torch.randn(B, L, M, device="cuda").to(dtype)
+    gbufs = [_guarded((B, L, M), dtype) for _ in range(4)]
+    r = _lib.ComplexBwdArgs(ar.data_ptr(), ai.data_ptr(), o_r.data_ptr(), o_i.data_ptr(), gr.data_ptr(), gi.data_ptr(),
+                            *(v.data_ptr() for _, v in gbufs), ws.data_ptr(), ws.numel() * 4, B, L, M, dt, dt)
+    assert lib.sparc_complex_scan_backward(ctypes.byref(r), torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert all(_intact(b, dtype) for b, _ in gbufs) and _intact(wsb, torch.float32)
+
+
 def test_rtrl_stays_in_bounds():
     import sparc_b200
     from sparc_b200 import _lib

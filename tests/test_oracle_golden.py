@@ -7,6 +7,7 @@ so agreement is expected at the float32 level, not float64. A formula error show
 """
 import numpy as np
 import pytest
+import torch
 
 from oracle import sparc_oracle as O
 
@@ -199,3 +200,32 @@ def test_real_scan_mixed_dtypes(golden, src):
     a16 = ((a16 + 0x7FFF + ((a16 >> 16) & 1)) & 0xFFFF0000).view(np.float32).astype(np.float64)
     out16, last16 = O.real_scan_forward(a16, d["b"])
     assert O.rel_l2(last16, d["with_last_last"]) > 1e-2
+
+
+def test_complex_scan(golden):
+    """The generic complex scan against the reference's float32 Triton kernels: forward, the
+    last state and every gradient (the backward reading the forward's outputs as the previous
+    states)."""
+    d = golden("complex")
+    out_r, out_i, last_r, last_i = O.complex_scan_forward(d["ar"], d["ai"], d["br"], d["bi"])
+    assert O.rel_l2(out_r, d["f32_out_r"]) < 1e-5 and O.rel_l2(out_i, d["f32_out_i"]) < 1e-5
+    assert O.rel_l2(last_r, d["with_last_last_r"]) < 1e-5 and O.rel_l2(last_i, d["with_last_last_i"]) < 1e-5
+    assert np.array_equal(d["with_last_out_r"], d["f32_out_r"])
+    grads = O.complex_scan_backward(d["ar"], d["ai"], d["f32_out_r"], d["f32_out_i"], d["gr"], d["gi"])
+    for k, g in zip(("ar", "ai", "br", "bi"), grads):
+        assert O.rel_l2(g, d["f32_grad_" + k]) < 1e-5, k
+
+
+def test_complex_scan_bf16_writes(golden):
+    """bfloat16 b with float32 a: out in bfloat16 (the reference's outputs are b's dtype), the
+    gradients computed against those bfloat16 outputs and returned in a's dtype (float32)."""
+    d = golden("complex")
+    assert int(d["bf16b_out_dtype_is_b"]) == 1
+    out_r, out_i, _, _ = O.complex_scan_forward(d["ar"], d["ai"], d["bf16b_br"], d["bf16b_bi"])
+    assert O.rel_l2(out_r, d["bf16b_out_r"]) < 4e-3 and O.rel_l2(out_i, d["bf16b_out_i"]) < 4e-3
+    # the output gradients reach the scan in the outputs' dtype (bfloat16)
+    g16 = [torch.from_numpy(d[k]).to(torch.bfloat16).double().numpy() for k in ("gr", "gi")]
+    grads = O.complex_scan_backward(d["ar"], d["ai"], d["bf16b_out_r"], d["bf16b_out_i"], *g16)
+    # grad_b is returned in a's dtype (float32) and cast to b's by autograd
+    for k, g, tol in zip(("ar", "ai", "br", "bi"), grads, (1e-5, 1e-5, 4e-3, 4e-3)):
+        assert O.rel_l2(g, d["bf16b_grad_" + k]) < tol, k
