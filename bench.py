@@ -5,7 +5,7 @@ SPARCMixer(512) layer, forward + backward of sum(y * g), B=8 x T=2048 tokens per
 parameters from the default init under torch.manual_seed(0), synthetic x, g ~ N(0, 1).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload layer|layer5|stack|real|decode|projection|projection16|rtrl]
+                    [--workload layer|layer5|stack|real|decode|projection|projection16|rtrl|complex]
 
 Multi-GPU: one process per GPU (torchrun), batch-sharded data parallelism (each rank runs the
 per-GPU batch: weak scaling), parameter gradients summed every step by the library's
@@ -57,6 +57,10 @@ WORKLOADS = {
     # the same in bfloat16: the products on the tensor cores (tcgen05)
     "projection16": dict(workload="sparc_sequence_layer_fwd_bwd_bf16", batch=8, seq_len=16384, width=2048,
                          modes=1024, dtype="bfloat16", config_index=0),
+    # the generic complex scan (the reference's complex_scan, its "triton" backend for more than
+    # 512 modes) at the config-5 layer's mode count, float32
+    "complex": dict(workload="complex_scan_fwd_bwd", batch=8, seq_len=8192, modes=1024, dtype="float32",
+                    config_index=4),
     # one RTRL cell step (trace update + trace gradients) at a size whose traces exceed L2
     "rtrl": dict(workload="sparc_rtrl_cell_step_fwd_bwd", batch=64, width=512, modes=512,
                  dtype="float32", config_index=0),
@@ -551,6 +555,75 @@ def run_stack(args, wl, world, rank, local):
                 launches=MIXER_LAUNCHES * L * args.steps, per_step_ms=per, tokens_step=gb * T)
 
 
+def run_complex(args, wl, world, rank, local):
+    """complex_scan forward + backward (sparc_b200.complex: chunk maps, cluster carry scan,
+    replay; the backward in reverse) on [B, L, M] float32 operands larger than L2."""
+    import torch
+
+    import sparc_b200
+    from sparc_b200 import _lib
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    B, T, M = wl["batch"], wl["seq_len"], wl["modes"]
+    gen = torch.Generator(device=device).manual_seed(rank)
+    rad = 0.99 + 0.0099 * torch.rand(B, T, M, generator=gen, device=device)
+    ang = 0.3 * torch.randn(B, T, M, generator=gen, device=device)
+    ops = [(rad * torch.cos(ang)), (rad * torch.sin(ang)), 0.5 * torch.randn(B, T, M, generator=gen, device=device),
+           0.5 * torch.randn(B, T, M, generator=gen, device=device)]
+    del rad, ang
+    gr, gi = torch.randn(B, T, M, generator=gen, device=device), torch.randn(B, T, M, generator=gen, device=device)
+    for t in ops:
+        t.requires_grad_(True)
+
+    def step():
+        for t in ops:
+            t.grad = None
+        out_r, out_i = sparc_b200.complex_scan(*ops)
+        torch.autograd.backward((out_r, out_i), (gr, gi))
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    with ClockSampler(local) as clocks:
+        total_ms, per = _time_steps(step, args.steps, lambda: None, world, device)
+    ms = total_ms / args.steps
+    peak, kind = measured_peaks()
+    L = _lib.lib()
+    torch.cuda.synchronize(device)
+    L.sparc_timing_enable(1)
+    _lib.kernel_times(reset_only=True)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize(device)
+    times = _lib.kernel_times()
+    L.sparc_timing_enable(0)
+    n = B * T * M * 4  # bytes of one float32 [B, L, M] array
+    # algorithmic bytes per launch: summaries read a, b (fwd) / a, grad_out (bwd): 4 arrays;
+    # the replay reads a, b and writes out: 6; the gradient kernel reads a, grad_out, out and
+    # writes four gradients: 10; the carry scans read the chunk maps (16 bytes per (row, chunk,
+    # mode)) and write the carries (8)
+    maps = B * -(-T // 32) * M * 24
+    kbytes = {"complex_fwd_summary_kernel": 4 * n, "complex_fwd_replay_kernel": 6 * n,
+              "complex_bwd_summary_kernel": 4 * n, "complex_bwd_grad_kernel": 10 * n,
+              "complex_carry_scan(fwd)": maps, "complex_carry_scan(bwd)": maps}
+    kern = {}
+    for name, (tot, cnt) in times.items():
+        kms = tot / cnt
+        kb = kbytes.get(name)
+        kern[name] = {"ms": round(kms, 4), "launches_per_step": round(cnt / args.steps, 2), "algorithmic_bytes": kb,
+                      "GBps": round(kb / (kms / 1e3) / 1e9, 1) if kb else None}
+    dom = max((k for k in kern if kern[k]["GBps"]), key=lambda k: kern[k]["ms"])
+    achieved = kern[dom]["GBps"]
+    # the step's minimum: forward reads a, b and writes out (6 arrays), backward reads a, out,
+    # grad_out and writes four gradients (10)
+    step_bytes = 16 * n
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": None, "kernel": dom, "peak_source": kind, "kernels": kern,
+                "step_frac": round(step_bytes / (ms / 1e3) / 1e9 / peak, 4)}
+    return dict(value=B * T * world / (ms / 1e3), ms=ms, roofline=roofline, e2e=None, cpu=None,
+                clocks=clocks.summary(), launches=6 * args.steps, per_step_ms=per, tokens_step=B * T * world)
+
+
 def run_real(args, wl, world, rank, local):
     import torch
 
@@ -816,7 +889,7 @@ def run_rtrl(args, wl, world, rank, local):
 
 
 # ----------------------------------------------------------------------------- reference arm
-_PER_GPU_BATCH = ("layer", "layer5", "real", "decode", "projection", "projection16", "rtrl")
+_PER_GPU_BATCH = ("layer", "layer5", "real", "decode", "projection", "projection16", "rtrl", "complex")
 
 
 def workload_config(workload: str, wl: dict, world: int) -> dict:
@@ -921,7 +994,7 @@ def main():
     world, rank, local = _dist()
     runner = {"layer": run_layer, "layer5": run_layer, "stack": run_stack, "real": run_real,
               "decode": run_decode, "projection": run_projection, "projection16": run_projection,
-              "rtrl": run_rtrl}[args.workload]
+              "rtrl": run_rtrl, "complex": run_complex}[args.workload]
     r = runner(args, wl, world, rank, local)
     # a bounded wait of the cross-GPU gradient exchange that ran out means wrong gradient sums:
     # no number is published then (every rank learns of it through one collective)

@@ -17,7 +17,9 @@
 // turns the maps into the value leaving every chunk; a replay kernel runs the recurrence through
 // each chunk from its carried-in value, writing the outputs and the last state (forward) or the
 // gradients (backward). Thread per mode, 128 modes per CTA, one CTA per (mode block, chunk, batch row);
-// each thread issues a group of kCxUnroll tokens' loads before using them.
+// each thread issues a group of kCxUnroll tokens' loads before using them (the replay kernel is
+// held to six CTAs' worth of registers: left alone it takes 143 and three CTAs per SM, too few
+// loads in flight).
 #include <algorithm>
 
 #include "common.cuh"
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(kCxModes) complex_fwd_summary_kernel(const CxP
 
 // Forward replay: h from the state entering the chunk, outputs in b's dtype.
 template <typename TA, typename TB>
-__global__ void __launch_bounds__(kCxModes) complex_fwd_replay_kernel(const CxParams p) {
+__global__ void __launch_bounds__(kCxModes, 6) complex_fwd_replay_kernel(const CxParams p) {
   pdl_wait();
   const int m = blockIdx.x * kCxModes + threadIdx.x;
   if (m >= p.M) return;
