@@ -94,7 +94,9 @@ MIXER_LAUNCHES = 7
 def mixer_kernel_bytes(B, T, W, s, chunk):
     """Algorithmic DRAM bytes of each mixer kernel per launch: every input it must read once and
     every output it must write once (activations W*s bytes per token, saved controls 32 bytes
-    per token, chunk maps 16 bytes and chunk states 8 bytes per chunk and mode)."""
+    per token, chunk maps 16 bytes and chunk states 8 bytes per chunk and mode). The replay also
+    writes every token's state (W*s per token) for the gradient kernel, which reads them with x
+    and dy instead of replaying the recurrence."""
     M = W // 2
     bt = B * T
     chunks = -(-T // chunk)
@@ -104,10 +106,10 @@ def mixer_kernel_bytes(B, T, W, s, chunk):
     car = 8 * B * chunks * M
     return {"mixer_fwd_summary_kernel": act + ctl + agg,
             "mixer_carry_scan_kernel(fwd)": agg + car,
-            "mixer_fwd_replay_kernel": 2 * act + ctl + car,
+            "mixer_fwd_replay_kernel": 3 * act + ctl + car,
             "mixer_bwd_summary_kernel": 2 * act + ctl + agg,
             "mixer_carry_scan_kernel(bwd)": agg + car,
-            "mixer_bwd_grad_kernel": 3 * act + ctl + 2 * car}
+            "mixer_bwd_grad_kernel": 4 * act + ctl + 2 * car}
 
 
 def profile_value(kernel: str, workload: str, key: str = "traffic_bytes_per_launch"):

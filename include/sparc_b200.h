@@ -135,6 +135,13 @@ typedef struct SparcMixerFwdArgs {
   unsigned max_spin;                   /* bound of the TMA waits (0 = default) */
   void* y_im;                          /* scan-level mode: Im h [batch, length, M] out (y then
                                           holds Re h [batch, length, M]), or NULL */
+  void* states;                        /* [batch, length, width] out (dtype): every token's state,
+                                          Re h in columns [0, M), Im h in [M, width) (the layout of
+                                          y), for the backward's `states`; or NULL. Plain and block
+                                          mode only (the other modes' y holds the states). Costs
+                                          one activation-sized write here and saves the backward
+                                          its replay of the states (the reference's backward
+                                          likewise reads saved states, backward/scan.py:1375-1640) */
 } SparcMixerFwdArgs;
 
 /* Backward of sparc_mixer_forward for the loss gradient dy on y (and optionally grad_last on
@@ -186,6 +193,9 @@ typedef struct SparcMixerBwdArgs {
   int width;
   int dtype;
   unsigned max_spin;
+  const void* states;                  /* the forward's `states` output (in projection mode: its
+                                          output y), or NULL: the gradient kernel then replays the
+                                          states from the chunk carries */
 } SparcMixerBwdArgs;
 
 /* Fused cross-GPU gradient sum (batch-sharded data parallelism, up to 8 ranks of one node):

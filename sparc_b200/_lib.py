@@ -37,7 +37,7 @@ class MixerFwdArgs(ctypes.Structure):
         ("projections", _vp), ("content_linear", ctypes.c_int),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
-        ("max_spin", ctypes.c_uint), ("y_im", _vp),
+        ("max_spin", ctypes.c_uint), ("y_im", _vp), ("states", _vp),
     ]
 
 
@@ -57,7 +57,7 @@ class MixerBwdArgs(ctypes.Structure):
         ("exchange_status", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("batch", _ll), ("length", _ll), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
-        ("max_spin", ctypes.c_uint),
+        ("max_spin", ctypes.c_uint), ("states", _vp),
     ]
 
 

@@ -918,6 +918,10 @@ static int run_forward(const SparcMixerFwdArgs* a, const Plan& pl, const WsLayou
     set_err("y_im is an output of the scan-level mode only"); return SPARC_ERR_ARG;
   }
   p.y_im = a->y_im;
+  if (a->states != nullptr && proj) {
+    set_err("states: in projection and scan-level mode the output y holds the states"); return SPARC_ERR_ARG;
+  }
+  p.states = a->states;
   p.h0_r = a->h0_r;
   p.h0_i = a->h0_i;
   p.ctl = reinterpret_cast<TokenCtl*>(a->controls);
@@ -1017,8 +1021,9 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   if (rc != SPARC_OK) return rc;
   const WsLayout L = ws_layout(pl, a->batch, a->width / 2);
   if (a->workspace == nullptr || a->workspace_bytes < L.total) { set_err("workspace too small"); return SPARC_ERR_WORKSPACE; }
-  if (block ? (a->relu_mask == nullptr || a->grad_norm_weight == nullptr) : (!proj && a->y == nullptr)) {
-    set_err(block ? "a block needs relu_mask and grad_norm_weight" : "the forward's output y is needed");
+  if (block ? (a->relu_mask == nullptr || a->grad_norm_weight == nullptr)
+            : (!proj && a->y == nullptr && a->states == nullptr)) {
+    set_err(block ? "a block needs relu_mask and grad_norm_weight" : "the forward's output y (or its states) is needed");
     return SPARC_ERR_ARG;
   }
   if (!a->x || !a->dy || !a->dx || !a->carry || !a->controls || !a->grad_nu_log || !a->grad_theta_log ||
@@ -1035,9 +1040,10 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   char* ws = static_cast<char*>(a->workspace);
   BwdParams p;
   p.x = a->x;
-  p.y = a->y;
+  p.y = a->states != nullptr ? a->states : a->y;  // (the relu mask: sign(h) = sign(y) where y > 0)
   p.dy = a->dy;
   p.dx = a->dx;
+  p.states = a->states;
   p.pp = MixerParamPtrs{a->nu_log, a->theta_log, proj ? nullptr : a->phase_direction,
                         proj ? nullptr : a->radial_direction, a->write_log_gain, a->write_phase_response,
                         a->write_radial_response};
@@ -1066,10 +1072,11 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   p.max_spin = a->max_spin ? a->max_spin : (1u << 20);
   const long long rows = p.B * p.T;
   // (a block reads no y: its relu mask comes as bits; the projection mode has no relu)
-  p.use_tma = pl.tma && aligned16(a->x) && aligned16(a->y) && aligned16(a->dy) && aligned16(a->controls) &&
-                      aligned16(a->carry) && aligned16(a->relu_mask) &&
+  p.use_tma = pl.tma && aligned16(a->x) && aligned16(p.y) && aligned16(a->dy) && aligned16(a->controls) &&
+                      aligned16(a->carry) && aligned16(a->relu_mask) && aligned16(a->states) &&
                       act_tensor_map(&p.map_x, a->x, a->dtype, rows, p.M, p.W, pl.C) &&
-                      (block || proj || act_tensor_map(&p.map_y, a->y, a->dtype, rows, p.M, p.W, pl.C)) &&
+                      (block || proj || act_tensor_map(&p.map_y, p.y, a->dtype, rows, p.M, p.W, pl.C)) &&
+                      (a->states == nullptr || act_tensor_map(&p.map_h, a->states, a->dtype, rows, p.M, p.W, pl.C)) &&
                       act_tensor_map(&p.map_dy, a->dy, a->dtype, rows, p.M, p.W, pl.C) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf = a->dtype == SPARC_DTYPE_BF16;

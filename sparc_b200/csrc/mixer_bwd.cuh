@@ -9,8 +9,10 @@
 //                             P = prod a_t and q the same walk from k_in = 0.
 //   mixer_carry_scan_kernel   (mixer.cu) the same scan as the forward's, from the last chunk
 //                             backwards: the adjoint carry leaving every chunk.
-//   mixer_bwd_grad_kernel     per tile (cluster of G CTAs): pass 0 replays the states from the
-//                             forward's chunk carry into shared memory and masks dy; pass B
+//   mixer_bwd_grad_kernel     per tile (cluster of G CTAs): the states come into shared memory
+//                             with x and dy when the forward saved them (one more TMA box per
+//                             tile instead of the recomputation), else pass 0 replays them from
+//                             the forward's chunk carry; pass B
 //                             walks the true adjoint backwards with every gradient: transition
 //                             (dEta, dDelta per token, dNu, dTheta per mode), write path (dx of
 //                             the content, dEta, dDelta, dNu, write-gain / response gradients);
@@ -47,10 +49,12 @@ struct BwdParams {
   CUtensorMap map_x;     // x, y, dy as [B*T rows][re|im][M], box {256, 2, C} (when use_tma)
   CUtensorMap map_y;
   CUtensorMap map_dy;
+  CUtensorMap map_h;     // the forward's saved states, same layout and box (when use_tma and states)
   const void* x;
   const void* y;
   const void* dy;
   void* dx;
+  const void* states;    // [B*T, W] the forward's states [Re | Im] (dtype), or null: replayed
   MixerParamPtrs pp;
   const float* h0_r;
   const float* h0_i;
@@ -207,10 +211,11 @@ template <typename TIO, int C>
 struct GradSmem {
   TIO x[C][2][kBwdModes];
   TIO dy[C][2][kBwdModes];     // the output gradient as given (the relu mask applies in pass B)
-  TIO hr[C][kBwdModes];        // replayed states (real plane), then the write-path dx (pass B);
-  TIO hi[C][kBwdModes];        // imaginary plane. In the activation dtype: for bfloat16 that keeps
-                               // the CTA within four per SM (the reference's bf16 path likewise
-                               // saves its states in bf16); float32 keeps them exact
+  TIO h[C][2][kBwdModes];      // the states (real, imaginary plane): the forward's saved states
+                               // (TMA box like x) or replayed (pass 0); then the write-path dx
+                               // (pass B). In the activation dtype: for bfloat16 that keeps the
+                               // CTA within four per SM (the reference's bf16 path likewise saves
+                               // its states in bf16); float32 keeps them exact
   float2 hin[kBwdModes];       // state entering the chunk, (re, im) per mode
   float2 kin[kBwdModes];       // adjoint carry entering the chunk from the later chunks
   TokenCtl ctl[C];
@@ -303,7 +308,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
 
   {
     unsigned* z = reinterpret_cast<unsigned*>(&S.x[0][0][0]);
-    for (int i = tid; i < (int)((sizeof(S.x) + sizeof(S.dy)) / 4); i += kGradThreads) z[i] = 0u;
+    for (int i = tid; i < (int)((sizeof(S.x) + sizeof(S.dy) + sizeof(S.h)) / 4); i += kGradThreads) z[i] = 0u;
   }
   if (tid == 0) {
     mbar_init(&S.bar, 1);
@@ -334,16 +339,19 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       const TokenCtl* cs = p.ctl + b * T + r.t0;
       const float2* hs = c > 0 ? p.carry + (b * chunks + (c - 1)) * (long long)M + mbase : nullptr;
       const float2* ks = c < chunks - 1 ? p.kout + (b * chunks + (c + 1)) * (long long)M + mbase : nullptr;
+      const bool saved = p.states != nullptr;
       if (p.use_tma) {
         if (tid == 0) {
           fence_proxy_async_smem();
-          unsigned bytes = 2u * act_box_bytes<TIO, C, kBwdModes>() + (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
+          unsigned bytes = (saved ? 3u : 2u) * act_box_bytes<TIO, C, kBwdModes>() +
+                           (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
           if (hs != nullptr) bytes += (unsigned)ncols * 8u;
           if (ks != nullptr) bytes += (unsigned)ncols * 8u;
           mbar_arrive_expect_tx(&S.bar, bytes);
           const int row = (int)(b * T + r.t0);
           tma_load_3d(&S.x[0][0][0], &p.map_x, mbase, 0, row, &S.bar);
           tma_load_3d(&S.dy[0][0][0], &p.map_dy, mbase, 0, row, &S.bar);
+          if (saved) tma_load_3d(&S.h[0][0][0], &p.map_h, mbase, 0, row, &S.bar);
           bulk_copy_g2s(&S.ctl[0], cs, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar);
           if (hs != nullptr) bulk_copy_g2s(&S.hin[0], hs, (unsigned)ncols * 8u, &S.bar);
           if (ks != nullptr) bulk_copy_g2s(&S.kin[0], ks, (unsigned)ncols * 8u, &S.bar);
@@ -352,6 +360,8 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       } else {
         load_act_rows<TIO, kBwdModes>(xs, W, M, mbase, r.nvalid, S.x, kGradThreads);
         load_act_rows<TIO, kBwdModes>(ds, W, M, mbase, r.nvalid, S.dy, kGradThreads);
+        if (saved) load_act_rows<TIO, kBwdModes>(static_cast<const TIO*>(p.states) + row0, W, M, mbase, r.nvalid, S.h,
+                                                 kGradThreads);
         for (int t = tid; t < r.nvalid; t += kGradThreads) S.ctl[t] = cs[t];
         for (int mm = tid; mm < ncols; mm += kGradThreads) {
           if (hs != nullptr) S.hin[mm] = hs[mm];
@@ -377,7 +387,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
           ni = xi;
         }
       };
-      // pass 0: replay the states from the forward's carry
+      // pass 0 (without saved states): replay the states from the forward's carry
       float2 hin0 = make_float2(0.0f, 0.0f), hin1 = hin0;
       if (c > 0) {
         if (act0) hin0 = S.hin[2 * tid];
@@ -387,7 +397,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
         if (act1) hin1 = make_float2(p.h0_r[b * M + m0 + 1], p.h0_i[b * M + m0 + 1]);
       }
       const Cx2 hin = cx2(make_float2(hin0.x, hin1.x), make_float2(hin0.y, hin1.y));
-      {
+      if (p.states == nullptr) {  // (else the forward's saved states are in S.h)
         Cx2 h = hin;
 #pragma unroll kU
         for (int t = 0; t < C; ++t) {
@@ -396,8 +406,8 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
             mixer_in(t, Pair<TIO>::load(&S.x[t][0][2 * tid]), Pair<TIO>::load(&S.x[t][1][2 * tid]), nr, ni);
             const TokenCoef2 k = token_coef2<kFast, bwd_rot<kFast>(), kScan>(mc, S.ctl[t]);
             h = cfma2(k.a, h, cx2(mul2(k.gain, content2<kFast, kMode>(nr, lin)), mul2(k.gain, content2<kFast, kMode>(ni, lin))));
-            Pair<TIO>::store(&S.hr[t][2 * tid], h.re.x, h.re.y);
-            Pair<TIO>::store(&S.hi[t][2 * tid], h.im.x, h.im.y);
+            Pair<TIO>::store(&S.h[t][0][2 * tid], h.re.x, h.re.y);
+            Pair<TIO>::store(&S.h[t][1][2 * tid], h.im.x, h.im.y);
           }
         }
       }
@@ -429,8 +439,8 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
           if (kFull || t < nvalid) {
             const TokenCtl& tc = S.ctl[t];
             // relu mask of the output gradient from this token's state (the slot still holds h_t)
-            const float2 hcr = Pair<TIO>::load(&S.hr[t][2 * tid]);
-            const float2 hci = Pair<TIO>::load(&S.hi[t][2 * tid]);
+            const float2 hcr = Pair<TIO>::load(&S.h[t][0][2 * tid]);
+            const float2 hci = Pair<TIO>::load(&S.h[t][1][2 * tid]);
             const float2 gr = Pair<TIO>::load(&S.dy[t][0][2 * tid]);
             const float2 gi = Pair<TIO>::load(&S.dy[t][1][2 * tid]);
             if constexpr (kProj) {  // the states are the output: no relu
@@ -440,7 +450,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
               lam.re = add2(lam.re, make_float2(hcr.x > 0.0f ? gr.x : 0.0f, hcr.y > 0.0f ? gr.y : 0.0f));
               lam.im = add2(lam.im, make_float2(hci.x > 0.0f ? gi.x : 0.0f, hci.y > 0.0f ? gi.y : 0.0f));
             }
-            const Cx2 pv = t > 0 ? cx2(Pair<TIO>::load(&S.hr[t - 1][2 * tid]), Pair<TIO>::load(&S.hi[t - 1][2 * tid]))
+            const Cx2 pv = t > 0 ? cx2(Pair<TIO>::load(&S.h[t - 1][0][2 * tid]), Pair<TIO>::load(&S.h[t - 1][1][2 * tid]))
                                  : hin;
             const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
             const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
@@ -450,8 +460,8 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
             const Cx2 dxc = grad_step2<kFast, kMode>(mc, tc, lam, pv, nr, ni, ve2, vd2, fa, lin);
             // h[t] was last read as the previous state at step t+1 and as this step's mask: its
             // slots now hold the write-path dx
-            Pair<TIO>::store(&S.hr[t][2 * tid], dxc.re.x, dxc.re.y);
-            Pair<TIO>::store(&S.hi[t][2 * tid], dxc.im.x, dxc.im.y);
+            Pair<TIO>::store(&S.h[t][0][2 * tid], dxc.re.x, dxc.re.y);
+            Pair<TIO>::store(&S.h[t][1][2 * tid], dxc.im.x, dxc.im.y);
             ve = (act0 ? ve2.x : 0.0f) + (act1 ? ve2.y : 0.0f);
             vd = (act0 ? vd2.x : 0.0f) + (act1 ? vd2.y : 0.0f);
             if constexpr (kBlock) {  // sum_j x_j w_j dxc_j (the norm backward's write-path part)
@@ -532,8 +542,8 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
           const float2 xr = Pair<TIO>::load(&S.x[t][0][2 * tid]);
           const float2 xi = Pair<TIO>::load(&S.x[t][1][2 * tid]);
           // the mixer's input gradient
-          const float2 dnr = fma2(dp0, mc.d0r, fma2(dp1, mc.d1r, Pair<TIO>::load(&S.hr[t][2 * tid])));
-          const float2 dni = fma2(dp0, mc.d0i, fma2(dp1, mc.d1i, Pair<TIO>::load(&S.hi[t][2 * tid])));
+          const float2 dnr = fma2(dp0, mc.d0r, fma2(dp1, mc.d1r, Pair<TIO>::load(&S.h[t][0][2 * tid])));
+          const float2 dni = fma2(dp0, mc.d0i, fma2(dp1, mc.d1i, Pair<TIO>::load(&S.h[t][1][2 * tid])));
           float2 dre, dim, nr, ni;
           if constexpr (kBlock) {
             const float2 rr = make_float2(S.ctl[t].keep.z, S.ctl[t].keep.w);

@@ -44,6 +44,7 @@ struct FwdParams {
   CUtensorMap map_x;    // x as [B*T rows][re|im][M], box {256, 2, C} (when use_tma)
   const void* x;
   void* y;
+  void* states;         // [B*T, W] every token's state [Re | Im] (dtype) for the backward, or null
   MixerParamPtrs pp;
   const float* h0_r;
   const float* h0_i;
@@ -474,6 +475,9 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
             const float2 nr = mul2(xr, mul2(rr, mc.wre)), ni = mul2(xi, mul2(rr, mc.wim));
             h = cfma2(k.a, h, cx2(mul2(k.gain, tanh_t2<kFast>(nr)), mul2(k.gain, tanh_t2<kFast>(ni))));
             store_sum_pair<TIO, kVec>(yrow + (long long)t * W, M, m0, act0, act1, xr, xi, h);
+            if (p.states != nullptr)
+              store_y_pair<TIO, kVec, false>(static_cast<TIO*>(p.states) + (r.b * T + r.t0 + t) * W, M, m0, act0,
+                                             act1, make_float2(h.re.x, h.im.x), make_float2(h.re.y, h.im.y));
             store_relu_bits(p.mask + (r.b * T + r.t0 + t) * (long long)p.mask_words + (mbase >> 6) * 4 + warp * 4,
                             h, lane);
           } else {
@@ -493,6 +497,9 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
             } else {
               store_y_pair<TIO, kVec, !kProj>(yrow + (long long)t * W, M, m0, act0, act1,
                                               make_float2(h.re.x, h.im.x), make_float2(h.re.y, h.im.y));
+              if (!kProj && p.states != nullptr)
+                store_y_pair<TIO, kVec, false>(static_cast<TIO*>(p.states) + (r.b * T + r.t0 + t) * W, M, m0, act0,
+                                               act1, make_float2(h.re.x, h.im.x), make_float2(h.re.y, h.im.y));
             }
           }
         }

@@ -8,6 +8,7 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
 
+#include <optional>
 #include <tuple>
 
 #include "sparc_b200.h"
@@ -32,8 +33,9 @@ at::Tensor workspace(const at::Tensor& like, size_t bytes) {
   return at::zeros({(int64_t)bytes}, like.options().dtype(at::kByte));
 }
 
-// SPARCMixer forward (sparc-kernal/forward/scan.py:1398-1603): (y, last_r, last_i, carry, controls).
-std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> mixer_forward(
+// SPARCMixer forward (sparc-kernal/forward/scan.py:1398-1603): (y, last_r, last_i, carry, controls,
+// states).
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> mixer_forward(
     const at::Tensor& x_in, const at::Tensor& nu_log, const at::Tensor& theta_log, const at::Tensor& phase_direction,
     const at::Tensor& radial_direction, const at::Tensor& write_log_gain, const at::Tensor& write_phase_response,
     const at::Tensor& write_radial_response) {
@@ -45,6 +47,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> mixer_for
   const at::Tensor p[7] = {f32(nu_log), f32(theta_log), f32(phase_direction), f32(radial_direction),
                            f32(write_log_gain), f32(write_phase_response), f32(write_radial_response)};
   at::Tensor y = at::empty_like(x);
+  at::Tensor states = at::empty_like(x);  // every token's state, for mixer_backward
   auto fo = x.options().dtype(at::kFloat);
   at::Tensor last_r = at::empty({B, M}, fo), last_i = at::empty({B, M}, fo);
   at::Tensor carry = at::empty({B, sparc_mixer_carry_chunks(T, dt), M, 2}, fo);
@@ -72,17 +75,19 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> mixer_for
   a.length = T;
   a.width = (int)W;
   a.dtype = dt;
+  a.states = states.data_ptr();
   check(sparc_mixer_forward(&a, stream_of(x)), "sparc_mixer_forward");
-  return {y, last_r, last_i, carry, controls};
+  return {y, last_r, last_i, carry, controls, states};
 }
 
-// Its backward: (dx, grad of each of the eight parameters in the module's order).
+// Its backward: (dx, grad of each of the eight parameters in the module's order). With the
+// forward's states (its sixth output) the gradient kernel reads them instead of replaying them.
 std::vector<at::Tensor> mixer_backward(const at::Tensor& x_in, const at::Tensor& y, const at::Tensor& dy_in,
                                        const at::Tensor& nu_log, const at::Tensor& theta_log,
                                        const at::Tensor& phase_direction, const at::Tensor& radial_direction,
                                        const at::Tensor& write_log_gain, const at::Tensor& write_phase_response,
                                        const at::Tensor& write_radial_response, const at::Tensor& carry,
-                                       const at::Tensor& controls) {
+                                       const at::Tensor& controls, const std::optional<at::Tensor>& states) {
   TORCH_CHECK(x_in.is_cuda() && x_in.dim() == 3 && y.sizes() == x_in.sizes() && dy_in.sizes() == x_in.sizes(),
               "mixer_backward: x, y and dy must be CUDA [batch, length, width] tensors of one shape");
   c10::cuda::CUDAGuard guard(x_in.device());
@@ -113,6 +118,13 @@ std::vector<at::Tensor> mixer_backward(const at::Tensor& x_in, const at::Tensor&
   const at::Tensor cc = carry.contiguous(), ct = controls.contiguous();
   a.carry = cc.data_ptr<float>();
   a.controls = ct.data_ptr<float>();
+  at::Tensor st;
+  if (states.has_value()) {
+    TORCH_CHECK(states->sizes() == x.sizes() && states->scalar_type() == x.scalar_type(),
+                "mixer_backward: states must be the forward's [batch, length, width] states");
+    st = states->contiguous();
+    a.states = st.data_ptr();
+  }
   a.grad_nu_log = g[0].data_ptr<float>();
   a.grad_theta_log = g[1].data_ptr<float>();
   a.grad_phase_direction = g[2].data_ptr<float>();
@@ -239,10 +251,10 @@ std::tuple<at::Tensor, at::Tensor> real_scan_backward(const at::Tensor& a_in, co
 TORCH_LIBRARY(sparc_b200, m) {
   m.def("mixer_forward(Tensor x, Tensor nu_log, Tensor theta_log, Tensor phase_direction, Tensor radial_direction, "
         "Tensor write_log_gain, Tensor write_phase_response, Tensor write_radial_response) "
-        "-> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+        "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)");
   m.def("mixer_backward(Tensor x, Tensor y, Tensor dy, Tensor nu_log, Tensor theta_log, Tensor phase_direction, "
         "Tensor radial_direction, Tensor write_log_gain, Tensor write_phase_response, Tensor write_radial_response, "
-        "Tensor carry, Tensor controls) -> Tensor[]");
+        "Tensor carry, Tensor controls, Tensor? states=None) -> Tensor[]");
   m.def("decode_step(Tensor x, Tensor state_r, Tensor state_i, Tensor nu_log, Tensor theta_log, "
         "Tensor phase_direction, Tensor radial_direction, Tensor write_log_gain, Tensor write_phase_response, "
         "Tensor write_radial_response) -> (Tensor, Tensor, Tensor)");

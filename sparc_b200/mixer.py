@@ -50,9 +50,10 @@ class _SparcMixerFunction(torch.autograd.Function):
     """Autograd op around sparc_mixer_forward / sparc_mixer_backward.
 
     Outputs y [B, T, W] (x.dtype) and the final state (last_r, last_i) [B, M] float32; both
-    are differentiable. Saved for backward: x, y, the parameters, the per-chunk carries and the
-    per-token controls. With a norm weight the call is a block: y = x + mixer(RMSNorm(x)) in the
-    same kernels, and the relu bits are saved instead of y."""
+    are differentiable. Saved for backward: x, every token's state (the forward writes them when
+    a gradient can be asked for; their sign is y's relu mask), the parameters, the per-chunk
+    carries and the per-token controls. With a norm weight the call is a block:
+    y = x + mixer(RMSNorm(x)) in the same kernels, and the relu bits are saved as well."""
 
     @staticmethod
     def forward(ctx, x, nu_log, theta_log, phase_direction, radial_direction, write_log_gain,
@@ -69,6 +70,9 @@ class _SparcMixerFunction(torch.autograd.Function):
         if h0_r is not None:
             h0 = (_f32(h0_r), _f32(h0_i))
         y = torch.empty_like(x)
+        # every token's state for the backward (saves its gradient kernel the state replay);
+        # only when a gradient can be asked for
+        states = torch.empty_like(x) if any(ctx.needs_input_grad) else None
         block = norm_weight is not None
         nw = _f32(norm_weight) if block else None
         mask = (torch.empty((B, T, L.sparc_mixer_mask_words(W)), dtype=torch.int32, device=dev)
@@ -87,11 +91,11 @@ class _SparcMixerFunction(torch.autograd.Function):
             _lib.ptr(h0[0] if h0 else None), _lib.ptr(h0[1] if h0 else None),
             last_r.data_ptr(), last_i.data_ptr(), carry.data_ptr(), controls.data_ptr(), _lib.ptr(reset),
             _lib.ptr(nw), float(norm_eps), _lib.ptr(mask), None, 0,
-            ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin)
+            ws.data_ptr(), ws.numel(), B, T, W, dt, max_spin, None, _lib.ptr(states))
         _lib.check(L.sparc_mixer_forward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_forward")
-        ctx.save_for_backward(x, None if block else y, *params, carry, controls, *(h0 if h0 else (None, None)),
-                              nw, mask)
+        # the states stand in for y in the backward (their sign is y's relu mask)
+        ctx.save_for_backward(x, states, *params, carry, controls, *(h0 if h0 else (None, None)), nw, mask)
         ctx.has_h0 = h0 is not None
         ctx.max_spin = max_spin
         ctx.set_materialize_grads(False)
@@ -100,7 +104,7 @@ class _SparcMixerFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy, dlast_r, dlast_i):
         L = _lib.lib()
-        x, y, nu_log, theta_log, pd, rd, wlg, wpr, wrr, carry, controls, h0_r, h0_i, nw, mask = ctx.saved_tensors
+        x, states, nu_log, theta_log, pd, rd, wlg, wpr, wrr, carry, controls, h0_r, h0_i, nw, mask = ctx.saved_tensors
         B, T, W = x.shape
         M = W // 2
         dev = x.device
@@ -123,7 +127,7 @@ class _SparcMixerFunction(torch.autograd.Function):
         nbytes = L.sparc_mixer_workspace_bytes(B, T, W, dt)
         ws = _lib.WORKSPACES.get(dev, nbytes)
         a = _lib.MixerBwdArgs(
-            x.data_ptr(), _lib.ptr(y), dy.data_ptr(), dx.data_ptr(),
+            x.data_ptr(), None, dy.data_ptr(), dx.data_ptr(),
             nu_log.data_ptr(), theta_log.data_ptr(), pd.data_ptr(), rd.data_ptr(),
             wlg.data_ptr(), wpr.data_ptr(), wrr.data_ptr(),
             _lib.ptr(h0_r), _lib.ptr(h0_i),
@@ -132,7 +136,7 @@ class _SparcMixerFunction(torch.autograd.Function):
             carry.data_ptr(), controls.data_ptr(), _lib.ptr(nw), _lib.ptr(mask), _lib.ptr(gnw),
             *[g[n].data_ptr() for n in _PARAMS], None, 0,
             workspace=ws.data_ptr(), workspace_bytes=ws.numel(), batch=B, length=T, width=W, dtype=dt,
-            max_spin=ctx.max_spin)
+            max_spin=ctx.max_spin, states=_lib.ptr(states))
         _exchange_fields(a, dev)
         _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
                    "sparc_mixer_backward")

@@ -76,8 +76,10 @@ def _core_forward(u, p, modal, h0, reset, lin, max_spin):
     return h, last_r, last_i, _CoreSaved(u, params, carry, controls, h0, int(lin), max_spin)
 
 
-def _core_backward(sv: _CoreSaved, dh, dlast_r, dlast_i):
-    """sparc_mixer_backward in projection mode: (du, dp, five modal gradients, gh0 or None)."""
+def _core_backward(sv: _CoreSaved, dh, dlast_r, dlast_i, states=None):
+    """sparc_mixer_backward in projection mode: (du, dp, five modal gradients, gh0 or None).
+    ``states``: the forward's output h (the states), read by the gradient kernel instead of
+    replaying them."""
     L = _lib.lib()
     u = sv.u
     B, T, W = u.shape
@@ -109,7 +111,7 @@ def _core_backward(sv: _CoreSaved, dh, dlast_r, dlast_i):
         g[0].data_ptr(), g[1].data_ptr(), None, None, g[2].data_ptr(), g[5].data_ptr(),
         g[3].data_ptr(), g[4].data_ptr(), dp.data_ptr(), sv.lin,
         workspace=ws.data_ptr(), workspace_bytes=ws.numel(), batch=B, length=T, width=W, dtype=dt,
-        max_spin=sv.max_spin)
+        max_spin=sv.max_spin, states=_lib.ptr(states))
     _lib.check(L.sparc_mixer_backward(ctypes.byref(a), _lib.stream_handle(dev)),
                "sparc_mixer_backward (projection mode)")
     return du, dp, g[:5], gh0
@@ -129,12 +131,14 @@ class _SparcCoreFunction(torch.autograd.Function):
         h, lr, li, sv = _core_forward(u, p, (decay_log, frequency_log, write_log_gain, write_phase_response,
                                              write_retention_response), h0, reset, content_linear, max_spin)
         ctx.sv = sv
+        ctx.save_for_backward(h)
         ctx.set_materialize_grads(False)
         return h, lr, li
 
     @staticmethod
     def backward(ctx, dh, dlast_r, dlast_i):
-        du, dp, g, gh0 = _core_backward(ctx.sv, dh, dlast_r, dlast_i)
+        (h,) = ctx.saved_tensors
+        du, dp, g, gh0 = _core_backward(ctx.sv, dh, dlast_r, dlast_i, states=h)
         ctx.sv = None
         return (du, dp, *g, gh0[0] if gh0 else None, gh0[1] if gh0 else None, None, None, None)
 
@@ -205,7 +209,7 @@ class _SequenceLayerTC(torch.autograd.Function):
                 dh = gemm.proj_gemm_f32(dyp, rot).view(B, T, M2)
             else:
                 dh = gemm.proj_gemm(dyp, rot.to(torch.bfloat16).contiguous()).view(B, T, M2)
-        du, dp, g, gh0 = _core_backward(ctx.sv, dh, dlast_r, dlast_i)
+        du, dp, g, gh0 = _core_backward(ctx.sv, dh, dlast_r, dlast_i, states=h)
         ctx.sv = None
         du2 = du.view(B * T, M2)
         dp2 = dp.view(B * T, 2)

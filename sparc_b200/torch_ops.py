@@ -7,8 +7,8 @@ return CUDA tensors and run on PyTorch's current stream; `load()` makes them ava
 library's host-only queries, symbolic lengths included), so that torch.compile / make_fx can
 trace calls to them, and autograd formulas for ``mixer_forward`` (through ``mixer_backward``)
 and ``real_scan_forward`` (through ``real_scan_backward``): their first output is
-differentiable with respect to the activations and parameters; the saved carries, controls and
-last states are marked non-differentiable."""
+differentiable with respect to the activations and parameters; the saved carries, controls,
+states and last states are marked non-differentiable."""
 from __future__ import annotations
 
 import ctypes
@@ -71,11 +71,12 @@ def _register_python_kernels():
         chunk = L.sparc_mixer_chunk_tokens(_lib.dtype_code(x.dtype))
         return (torch.empty_like(x, memory_format=torch.contiguous_format), x.new_empty((B, M), dtype=f32),
                 x.new_empty((B, M), dtype=f32), x.new_empty((B, _ceil_div(T, chunk), M, 2), dtype=f32),
-                x.new_empty((B, T, L.sparc_mixer_controls_floats()), dtype=f32))
+                x.new_empty((B, T, L.sparc_mixer_controls_floats()), dtype=f32),
+                torch.empty_like(x, memory_format=torch.contiguous_format))
 
     @torch.library.register_fake("sparc_b200::mixer_backward")
     def _(x, y, dy, nu_log, theta_log, phase_direction, radial_direction, write_log_gain, write_phase_response,
-          write_radial_response, carry, controls):
+          write_radial_response, carry, controls, states=None):
         W = x.shape[2]
         M = W // 2
         sizes = (M, M, W + 1, W + 1, M, M, M, M)  # energy_response's (zero) gradient sixth
@@ -102,15 +103,16 @@ def _register_python_kernels():
                 torch.empty_like(b, memory_format=torch.contiguous_format))
 
     def mixer_setup(ctx, inputs, output):
-        y, last_r, last_i, carry, controls = output
-        ctx.mark_non_differentiable(last_r, last_i, carry, controls)
-        ctx.save_for_backward(inputs[0], y, *inputs[1:], carry, controls)
+        y, last_r, last_i, carry, controls, states = output
+        ctx.mark_non_differentiable(last_r, last_i, carry, controls, states)
+        ctx.save_for_backward(inputs[0], y, *inputs[1:], carry, controls, states)
         ctx.dtypes = [t.dtype for t in inputs]
 
-    def mixer_backward(ctx, gy, g_last_r, g_last_i, g_carry, g_controls):
+    def mixer_backward(ctx, gy, g_last_r, g_last_i, g_carry, g_controls, g_states):
         x, y, *rest = ctx.saved_tensors
         params, carry, controls = rest[:_MIXER_PARAMS], rest[_MIXER_PARAMS], rest[_MIXER_PARAMS + 1]
-        g = torch.ops.sparc_b200.mixer_backward(x, y, gy, *params, carry, controls)
+        states = rest[_MIXER_PARAMS + 2]
+        g = torch.ops.sparc_b200.mixer_backward(x, y, gy, *params, carry, controls, states)
         grads = [g[0]] + g[1:6] + g[7:9]  # (the operator takes no energy_response)
         return tuple(t.to(d) for t, d in zip(grads, ctx.dtypes))
 

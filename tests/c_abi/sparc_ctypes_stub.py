@@ -24,7 +24,7 @@ class SparcMixerFwdArgs(ctypes.Structure):   # field order of include/sparc_b200
         ("workspace", ctypes.c_void_p)] + [
         ("workspace_bytes", ctypes.c_size_t), ("batch", ctypes.c_longlong),
         ("length", ctypes.c_longlong), ("width", ctypes.c_int), ("dtype", ctypes.c_int),
-        ("max_spin", ctypes.c_uint), ("y_im", ctypes.c_void_p)]
+        ("max_spin", ctypes.c_uint), ("y_im", ctypes.c_void_p), ("states", ctypes.c_void_p)]
 
 def run_sequence(module, x, return_cache=False):
     B, T, W = x.shape

@@ -25,14 +25,18 @@ def test_mixer_and_decode_ops_match_module():
     y, cache = m(x, return_cache=True)
     y.backward(g)
     p = [getattr(m, n).detach() for n in PARAMS]
-    y2, lr, li, carry, controls = ops.mixer_forward(x.detach(), *p)
+    y2, lr, li, carry, controls, states = ops.mixer_forward(x.detach(), *p)
     assert torch.equal(y2, y.detach()) and torch.equal(lr, cache[0]) and torch.equal(li, cache[1])
-    grads = ops.mixer_backward(x.detach(), y2, g, *p, carry, controls)
+    grads = ops.mixer_backward(x.detach(), y2, g, *p, carry, controls, states)
     assert torch.equal(grads[0], x.grad)
     names = ("nu_log", "theta_log", "phase_direction", "radial_direction", "write_log_gain",
              "energy_response", "write_phase_response", "write_radial_response")
     for n, t in zip(names, grads[1:]):
         assert torch.equal(t, getattr(m, n).grad), n
+    # without the saved states the gradient kernel replays them: the same gradients to rounding
+    replayed = ops.mixer_backward(x.detach(), y2, g, *p, carry, controls)
+    for t, r in zip(grads, replayed):
+        assert torch.allclose(r, t, rtol=1e-4, atol=1e-5)
     st = (torch.zeros(2, 32, device="cuda"), torch.zeros(2, 32, device="cuda"))
     m.prepare_inference()  # the fused decode kernel, which decode_step registers
     yd, sd = m.step(x.detach()[:, 0], st, None)

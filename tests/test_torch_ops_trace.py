@@ -37,12 +37,13 @@ def test_fake_shapes(ops, dtype, T):
     with FakeTensorMode():
         x = torch.randn(B, T, W, device="cuda").to(dtype)
         p = _params(W, "cuda")
-        y, lr, li, carry, ctl = ops.mixer_forward(x, *p)
+        y, lr, li, carry, ctl, st = ops.mixer_forward(x, *p)
         assert y.shape == x.shape and y.dtype == dtype and y.device == x.device
         assert lr.shape == li.shape == (B, M) and lr.dtype == torch.float32
         assert carry.shape == (B, L.sparc_mixer_carry_chunks(T, dt), M, 2)
         assert ctl.shape == (B, T, L.sparc_mixer_controls_floats())
-        g = ops.mixer_backward(x, y, y, *p, carry, ctl)
+        assert st.shape == x.shape and st.dtype == dtype
+        g = ops.mixer_backward(x, y, y, *p, carry, ctl, st)
         assert [t.shape for t in g] == [x.shape] + [(n,) for n in (M, M, W + 1, W + 1, M, M, M, M)]
         yd, nr, ni = ops.decode_step(x[:, 0], lr, li, *p)
         assert yd.shape == (B, W) and yd.dtype == dtype and nr.shape == ni.shape == (B, M)
@@ -61,8 +62,9 @@ def test_autograd_through_the_operators(ops):
     with FakeTensorMode():
         x = torch.randn(B, T, W, requires_grad=True)
         p = _params(W, "cpu", requires_grad=True)
-        y, lr, li, carry, ctl = ops.mixer_forward(x, *p)
+        y, lr, li, carry, ctl, st = ops.mixer_forward(x, *p)
         assert y.requires_grad and not lr.requires_grad and not carry.requires_grad and not ctl.requires_grad
+        assert not st.requires_grad
         (y * y).sum().backward()
         assert x.grad is not None and x.grad.shape == x.shape
         for t in p:
@@ -79,7 +81,7 @@ def test_make_fx_symbolic(ops):
     from torch.fx.experimental.proxy_tensor import make_fx
 
     def f(x, *p):
-        y, lr, li, carry, ctl = torch.ops.sparc_b200.mixer_forward(x, *p)
+        y, lr, li, carry, ctl, st = torch.ops.sparc_b200.mixer_forward(x, *p)
         return y, carry
 
     # (real CPU inputs: make_fx fakes them with symbolic sizes and never runs a kernel)
