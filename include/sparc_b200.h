@@ -194,8 +194,11 @@ typedef struct SparcMixerBwdArgs {
   int dtype;
   unsigned max_spin;
   const void* states;                  /* the forward's `states` output (in projection mode: its
-                                          output y), or NULL: the gradient kernel then replays the
-                                          states from the chunk carries */
+                                          output y), or NULL. With it (and 16-byte aligned rows:
+                                          the condition of the tensor maps) the gradient kernel
+                                          reads the states instead of replaying them from the
+                                          chunk carries; its sign stands in for y's relu mask,
+                                          so y may then be NULL. Not used in the scan-level mode */
 } SparcMixerBwdArgs;
 
 /* Fused cross-GPU gradient sum (batch-sharded data parallelism, up to 8 ranks of one node):

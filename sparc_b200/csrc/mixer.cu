@@ -562,8 +562,8 @@ struct Plan {
   long long tiles;         // B * chunks
   int G, Mp;               // CTAs of 256 modes per tile; modes padded to G * 256
   bool vec, tma;
-  int sum_clusters, rep_rows, rsum_rows, grad_clusters;
-  size_t sum_smem, rep_smem, rsum_smem, grad_smem;
+  int sum_clusters, rep_rows, rsum_rows, grad_clusters, saved_clusters;
+  size_t sum_smem, rep_smem, rsum_smem, grad_smem, saved_smem;
   long long scan_rows;     // carry-scan grid rows: B
   int scan_span;           // chunks per carry-scan span (warp)
 };
@@ -656,10 +656,25 @@ struct Kernels {
     return mode == kModeBlock ? grad_m<kModeBlock>(vec) : mode == kModeProj ? grad_m<kModeProj>(vec)
          : mode == kModeScan ? grad_m<kModeScan>(vec) : grad_m<kModePlain>(vec);
   }
+  template <int kM, int kSplit>
+  static const void* saved_s(bool vec) {
+    return vec ? (const void*)mixer_bwd_grad_saved_kernel<TIO, C, kSplit, kFast, true, kM>
+               : (const void*)mixer_bwd_grad_saved_kernel<TIO, C, kSplit, kFast, false, kM>;
+  }
+  template <int kM>
+  static const void* saved_m(bool vec, int G) { return G == 1 ? saved_s<kM, 2>(vec) : saved_s<kM, 1>(vec); }
+  // halves for a CTA of its own (G == 1), whole tiles in clusters; (the scan-level mode has no
+  // saved states: its outputs are two separate planes)
+  static const void* saved(bool vec, int mode, int G) {
+    return mode == kModeBlock ? saved_m<kModeBlock>(vec, G) : mode == kModeProj ? saved_m<kModeProj>(vec, G)
+         : mode == kModeScan ? nullptr : saved_m<kModePlain>(vec, G);
+  }
+  static int saved_split(int G) { return G == 1 ? 2 : 1; }
   static size_t sum_smem() { return sizeof(SumSmem<TIO, C>); }
   static size_t rep_smem() { return sizeof(RepSmem<TIO, C>); }
   static size_t rsum_smem() { return sizeof(RsumSmem<TIO, C>); }
   static size_t grad_smem() { return sizeof(GradSmem<TIO, C>); }
+  static size_t saved_smem(int G) { return G == 1 ? sizeof(GradSavedSmem<TIO, C, 2>) : sizeof(GradSavedSmem<TIO, C, 1>); }
 };
 
 template <typename TIO>
@@ -669,10 +684,12 @@ static void plan_kernels(Plan* pl, const void** k) {
   pl->rep_smem = K::rep_smem();
   pl->rsum_smem = K::rsum_smem();
   pl->grad_smem = K::grad_smem();
+  pl->saved_smem = K::saved_smem(pl->G);
   k[0] = K::sum(pl->mode);
   k[1] = K::rep(pl->vec, pl->mode);
   k[2] = K::rsum(pl->mode);
   k[3] = K::grad(pl->vec, pl->mode);
+  k[4] = K::saved(pl->vec, pl->mode, pl->G);
 }
 
 static int make_plan(long long B, long long T, int W, int dtype, int mode, Plan* pl) {
@@ -696,13 +713,13 @@ static int make_plan(long long B, long long T, int W, int dtype, int mode, Plan*
   pl->scan_span = (pl->chunks + kScanSpans - 1) / kScanSpans;
   if (pl->scan_rows > 65535) { set_err("batch too large for the carry scan's grid"); return SPARC_ERR_SHAPE; }
 
-  const void* k[4];
+  const void* k[5];
   if (dtype == SPARC_DTYPE_BF16) plan_kernels<__nv_bfloat16>(pl, k);
   else plan_kernels<float>(pl, k);
 
   int dev = 0;
   cudaGetDevice(&dev);
-  struct Key { int dev, dtype, G, vec, mode; int sum, rep, rsum, grad; };
+  struct Key { int dev, dtype, G, vec, mode; int sum, rep, rsum, grad, saved; };
   static std::mutex mu;
   static Key cache[64];
   static int ncache = 0;
@@ -716,12 +733,13 @@ static int make_plan(long long B, long long T, int W, int dtype, int mode, Plan*
   if (hit != nullptr) {
     key = *hit;
   } else {
-    key = Key{dev, dtype, pl->G, (int)pl->vec, mode, 0, 0, 0, 0};
+    key = Key{dev, dtype, pl->G, (int)pl->vec, mode, 0, 0, 0, 0, 0};
     key.sum = max_clusters(k[0], pl->G, kFwdThreads, pl->sum_smem);
     key.rep = max_blocks(k[1], kFwdThreads, pl->rep_smem);
     key.rsum = max_blocks(k[2], kBwdThreads, pl->rsum_smem);
     key.grad = max_clusters(k[3], pl->G, kGradThreads, pl->grad_smem);
-    if (key.sum <= 0 || key.rep <= 0 || key.rsum <= 0 || key.grad <= 0) {
+    key.saved = k[4] != nullptr ? max_clusters(k[4], pl->G, kGradThreads, pl->saved_smem) : 1;
+    if (key.sum <= 0 || key.rep <= 0 || key.rsum <= 0 || key.grad <= 0 || key.saved <= 0) {
       set_err("occupancy query failed");
       return SPARC_ERR_LAUNCH;
     }
@@ -732,6 +750,7 @@ static int make_plan(long long B, long long T, int W, int dtype, int mode, Plan*
   pl->rep_rows = clamp(key.rep / pl->G, pl->tiles);
   pl->rsum_rows = clamp(key.rsum / pl->G, pl->tiles);
   pl->grad_clusters = clamp(key.grad, pl->tiles);
+  pl->saved_clusters = clamp(key.saved, pl->tiles);
   return SPARC_OK;
 }
 
@@ -749,7 +768,8 @@ static WsLayout ws_layout(const Plan& pl, long long B, int M) {
   L.kout = off;
   off = align256(off + (size_t)B * pl.chunks * M * sizeof(float2));
   L.part = off;
-  off = align256(off + ((size_t)pl.grad_clusters * kPartModes * pl.Mp + 2 * (size_t)pl.grad_clusters) * sizeof(double));
+  const size_t clusters = (size_t)std::max(pl.grad_clusters, pl.saved_clusters);  // (either gradient kernel)
+  off = align256(off + (clusters * kPartModes * pl.Mp + 2 * clusters) * sizeof(double));
   L.total = off;
   return L;
 }
@@ -1073,15 +1093,23 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   const long long rows = p.B * p.T;
   // (a block reads no y: its relu mask comes as bits; the projection mode has no relu)
   p.use_tma = pl.tma && aligned16(a->x) && aligned16(p.y) && aligned16(a->dy) && aligned16(a->controls) &&
-                      aligned16(a->carry) && aligned16(a->relu_mask) && aligned16(a->states) &&
+                      aligned16(a->carry) && aligned16(a->relu_mask) &&
                       act_tensor_map(&p.map_x, a->x, a->dtype, rows, p.M, p.W, pl.C) &&
                       (block || proj || act_tensor_map(&p.map_y, p.y, a->dtype, rows, p.M, p.W, pl.C)) &&
-                      (a->states == nullptr || act_tensor_map(&p.map_h, a->states, a->dtype, rows, p.M, p.W, pl.C)) &&
                       act_tensor_map(&p.map_dy, a->dy, a->dtype, rows, p.M, p.W, pl.C) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf = a->dtype == SPARC_DTYPE_BF16;
   const void* krsum = bf ? Kernels<__nv_bfloat16>::rsum(pl.mode) : Kernels<float>::rsum(pl.mode);
   const void* kgrad = bf ? Kernels<__nv_bfloat16>::grad(pl.vec, pl.mode) : Kernels<float>::grad(pl.vec, pl.mode);
+  // With the forward's states (and tensor maps) the gradient kernel reads them in half-tile
+  // stages instead of replaying the recurrence; its maps have boxes of C/2 (C/2 + 1) rows.
+  const void* ksaved = bf ? Kernels<__nv_bfloat16>::saved(pl.vec, pl.mode, pl.G) : Kernels<float>::saved(pl.vec, pl.mode, pl.G);
+  const int part = pl.C / Kernels<float>::saved_split(pl.G);  // tokens per stage
+  BwdParams ps = p;
+  const bool saved = ksaved != nullptr && a->states != nullptr && p.use_tma && aligned16(a->states) &&
+                     act_tensor_map(&ps.map_x, a->x, a->dtype, rows, p.M, p.W, part) &&
+                     act_tensor_map(&ps.map_dy, a->dy, a->dtype, rows, p.M, p.W, part) &&
+                     act_tensor_map(&ps.map_h, a->states, a->dtype, rows, p.M, p.W, part + 1);
   {
     TimedLaunch tl(kTimeBwdSummary, s);
     rc = launch_error(launch_plain(krsum, dim3(pl.G, pl.rsum_rows), kBwdThreads, pl.rsum_smem, s, p));
@@ -1096,12 +1124,13 @@ int sparc_mixer_backward(const SparcMixerBwdArgs* a, void* stream) {
   if (rc != SPARC_OK) return rc;
   {
     TimedLaunch tl(kTimeBwdGrad, s);
-    rc = launch_error(launch_cluster(kgrad, pl.G, kGradThreads, pl.grad_clusters, pl.grad_smem, s, p));
+    rc = launch_error(saved ? launch_cluster(ksaved, pl.G, kGradThreads, pl.saved_clusters, pl.saved_smem, s, ps)
+                            : launch_cluster(kgrad, pl.G, kGradThreads, pl.grad_clusters, pl.grad_smem, s, p));
   }
   if (rc != SPARC_OK) return rc;
   ReduceParams r;
   r.part = p.part;
-  r.clusters = pl.grad_clusters;
+  r.clusters = saved ? pl.saved_clusters : pl.grad_clusters;
   r.Mp = pl.Mp;
   r.M = p.M;
   r.W = p.W;

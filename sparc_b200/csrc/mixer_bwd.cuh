@@ -9,10 +9,8 @@
 //                             P = prod a_t and q the same walk from k_in = 0.
 //   mixer_carry_scan_kernel   (mixer.cu) the same scan as the forward's, from the last chunk
 //                             backwards: the adjoint carry leaving every chunk.
-//   mixer_bwd_grad_kernel     per tile (cluster of G CTAs): the states come into shared memory
-//                             with x and dy when the forward saved them (one more TMA box per
-//                             tile instead of the recomputation), else pass 0 replays them from
-//                             the forward's chunk carry; pass B
+//   mixer_bwd_grad_kernel     per tile (cluster of G CTAs): pass 0 replays the states from the
+//                             forward's chunk carry into shared memory; pass B
 //                             walks the true adjoint backwards with every gradient: transition
 //                             (dEta, dDelta per token, dNu, dTheta per mode), write path (dx of
 //                             the content, dEta, dDelta, dNu, write-gain / response gradients);
@@ -21,6 +19,14 @@
 //                             transpose-reduce per group of tokens during the walk, then shared
 //                             and distributed shared memory) into the controller gradients dp0,
 //                             dp1, which finish dx and the direction gradients.
+//   mixer_bwd_grad_saved_kernel  the same gradients when the forward saved every token's state:
+//                             no replay. Without a cluster (W <= 512) each tile is walked as two
+//                             halves of C/2 tokens (the later half first, the adjoint carried
+//                             between them in registers), each half's x, dy and states arriving
+//                             by TMA into one of two stages, so that the next half's copies run
+//                             under this half's arithmetic; in clusters, where every part costs a
+//                             cross-CTA reduction, as whole tiles. The cluster's per-token sums
+//                             are pushed into every CTA with asynchronous stores on an mbarrier.
 // The reverse summary runs one mode per thread (256 threads per CTA); the gradient kernel two
 // adjacent modes per thread with packed f32x2 arithmetic (128 threads). Per-mode parameter
 // gradients accumulate per cluster; mixer_reduce_kernel sums the clusters in float64 in a fixed
@@ -49,12 +55,13 @@ struct BwdParams {
   CUtensorMap map_x;     // x, y, dy as [B*T rows][re|im][M], box {256, 2, C} (when use_tma)
   CUtensorMap map_y;
   CUtensorMap map_dy;
-  CUtensorMap map_h;     // the forward's saved states, same layout and box (when use_tma and states)
+  CUtensorMap map_h;     // the forward's saved states, box {256, 2, S + 1} (saved-state kernel,
+                         // S tokens per stage; its map_x and map_dy then have box {256, 2, S})
   const void* x;
   const void* y;
   const void* dy;
   void* dx;
-  const void* states;    // [B*T, W] the forward's states [Re | Im] (dtype), or null: replayed
+  const void* states;    // [B*T, W] the forward's states [Re | Im] (dtype) (saved-state kernel)
   MixerParamPtrs pp;
   const float* h0_r;
   const float* h0_i;
@@ -211,8 +218,7 @@ template <typename TIO, int C>
 struct GradSmem {
   TIO x[C][2][kBwdModes];
   TIO dy[C][2][kBwdModes];     // the output gradient as given (the relu mask applies in pass B)
-  TIO h[C][2][kBwdModes];      // the states (real, imaginary plane): the forward's saved states
-                               // (TMA box like x) or replayed (pass 0); then the write-path dx
+  TIO h[C][2][kBwdModes];      // replayed states (real, imaginary plane), then the write-path dx
                                // (pass B). In the activation dtype: for bfloat16 that keeps the
                                // CTA within four per SM (the reference's bf16 path likewise saves
                                // its states in bf16); float32 keeps them exact
@@ -308,7 +314,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
 
   {
     unsigned* z = reinterpret_cast<unsigned*>(&S.x[0][0][0]);
-    for (int i = tid; i < (int)((sizeof(S.x) + sizeof(S.dy) + sizeof(S.h)) / 4); i += kGradThreads) z[i] = 0u;
+    for (int i = tid; i < (int)((sizeof(S.x) + sizeof(S.dy)) / 4); i += kGradThreads) z[i] = 0u;
   }
   if (tid == 0) {
     mbar_init(&S.bar, 1);
@@ -339,19 +345,16 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       const TokenCtl* cs = p.ctl + b * T + r.t0;
       const float2* hs = c > 0 ? p.carry + (b * chunks + (c - 1)) * (long long)M + mbase : nullptr;
       const float2* ks = c < chunks - 1 ? p.kout + (b * chunks + (c + 1)) * (long long)M + mbase : nullptr;
-      const bool saved = p.states != nullptr;
       if (p.use_tma) {
         if (tid == 0) {
           fence_proxy_async_smem();
-          unsigned bytes = (saved ? 3u : 2u) * act_box_bytes<TIO, C, kBwdModes>() +
-                           (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
+          unsigned bytes = 2u * act_box_bytes<TIO, C, kBwdModes>() + (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
           if (hs != nullptr) bytes += (unsigned)ncols * 8u;
           if (ks != nullptr) bytes += (unsigned)ncols * 8u;
           mbar_arrive_expect_tx(&S.bar, bytes);
           const int row = (int)(b * T + r.t0);
           tma_load_3d(&S.x[0][0][0], &p.map_x, mbase, 0, row, &S.bar);
           tma_load_3d(&S.dy[0][0][0], &p.map_dy, mbase, 0, row, &S.bar);
-          if (saved) tma_load_3d(&S.h[0][0][0], &p.map_h, mbase, 0, row, &S.bar);
           bulk_copy_g2s(&S.ctl[0], cs, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar);
           if (hs != nullptr) bulk_copy_g2s(&S.hin[0], hs, (unsigned)ncols * 8u, &S.bar);
           if (ks != nullptr) bulk_copy_g2s(&S.kin[0], ks, (unsigned)ncols * 8u, &S.bar);
@@ -360,8 +363,6 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       } else {
         load_act_rows<TIO, kBwdModes>(xs, W, M, mbase, r.nvalid, S.x, kGradThreads);
         load_act_rows<TIO, kBwdModes>(ds, W, M, mbase, r.nvalid, S.dy, kGradThreads);
-        if (saved) load_act_rows<TIO, kBwdModes>(static_cast<const TIO*>(p.states) + row0, W, M, mbase, r.nvalid, S.h,
-                                                 kGradThreads);
         for (int t = tid; t < r.nvalid; t += kGradThreads) S.ctl[t] = cs[t];
         for (int mm = tid; mm < ncols; mm += kGradThreads) {
           if (hs != nullptr) S.hin[mm] = hs[mm];
@@ -387,7 +388,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
           ni = xi;
         }
       };
-      // pass 0 (without saved states): replay the states from the forward's carry
+      // pass 0: replay the states from the forward's carry
       float2 hin0 = make_float2(0.0f, 0.0f), hin1 = hin0;
       if (c > 0) {
         if (act0) hin0 = S.hin[2 * tid];
@@ -397,7 +398,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
         if (act1) hin1 = make_float2(p.h0_r[b * M + m0 + 1], p.h0_i[b * M + m0 + 1]);
       }
       const Cx2 hin = cx2(make_float2(hin0.x, hin1.x), make_float2(hin0.y, hin1.y));
-      if (p.states == nullptr) {  // (else the forward's saved states are in S.h)
+      {
         Cx2 h = hin;
 #pragma unroll kU
         for (int t = 0; t < C; ++t) {
@@ -602,6 +603,376 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
       acc_b1 += s1;
     }
     __syncthreads();  // every shared array is free for the next tile
+  }
+  // per-cluster partial parameter gradients (reduced in a fixed order by mixer_reduce_kernel)
+  const long long kc = blockIdx.y;
+  double* part = p.part + kc * (long long)kPartModes * Mp;
+#pragma unroll
+  for (int q = 0; q < kPartModes; ++q) {
+    part[(long long)q * Mp + m0] = act0 ? (double)acc[q].x : 0.0;
+    part[(long long)q * Mp + m0 + 1] = act1 ? (double)acc[q].y : 0.0;
+  }
+  if (g == 0 && tid == 0) {
+    double* pb = p.part + (long long)gridDim.y * kPartModes * Mp + 2 * kc;
+    pb[0] = acc_b0;
+    pb[1] = acc_b1;
+  }
+  if (timed_out) atomicOr(&p.ls->status, kStatusTimeout);
+  cluster.sync();
+}
+
+
+// ------------------------------------------------------------------------------ gradients from saved states
+// One stage of the saved-state gradient kernel: one of kSplit parts of a tile, S = C / kSplit
+// tokens of x, dy and the states, and one more state row in front (the state before the part's
+// first token).
+template <typename TIO, int C, int kSplit>
+struct GradSavedStage {
+  static constexpr int S = C / kSplit;
+  TIO x[S][2][kBwdModes];
+  TIO dy[S][2][kBwdModes];
+  TIO h[S + 1][2][kBwdModes];  // h[0] the state before the part, h[1 + u] the state of its token u,
+                               // which the reverse walk replaces with that token's write-path dx
+  TokenCtl ctl[S];
+};
+
+template <typename TIO, int C, int kSplit>
+struct GradSavedSmem {
+  static constexpr int S = C / kSplit;
+  GradSavedStage<TIO, C, kSplit> st[kSplit];
+  float4 dp[S];                // controller gradients per token as pairs (dp0, dp0, dp1, dp1)
+  float2 kap[S];               // a block's RMSNorm backward coefficient, as a pair
+  float part_all[2][8][3 * S]; // every cluster CTA's partials of the per-token sums (pushed by the
+                               // peers), by item parity
+  float warp_part[kGradWarps][3 * S];
+  unsigned long long bar[kSplit];
+  unsigned long long red[2];   // completes when all G CTAs' partials of an item have arrived
+};
+
+// Work item w of a CTA is part kSplit - 1 - w % kSplit of its tile w / kSplit (the later part
+// first); stage w % kSplit holds it. With kSplit = 2 (halves) thread 0 issues item w + 2 into
+// the stage as soon as item w has finished with it, so one item's copies are always in flight
+// under the other's arithmetic; with kSplit = 1 (whole tiles, one stage: the variant for
+// clusters, where each part costs a cross-CTA reduction) the next tile's copies follow the
+// current tile.
+template <typename TIO, int C, int kSplit, bool kFast, bool kVec, int kMode>
+__global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_saved_kernel(const __grid_constant__ BwdParams p) {
+  constexpr int S = C / kSplit;
+  static_assert((kSplit == 1 || kSplit == 2) && C % kSplit == 0 && S % kGroup == 0,
+                "whole tiles or halves of whole reverse-walk groups");
+  constexpr bool kBlock = kMode == kModeBlock, kProj = proj_like<kMode>(), kScan = kMode == kModeScan;
+  const bool lin = kProj && p.content_linear != 0;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int g = (int)cluster.block_rank();
+  const int G = (int)cluster.num_blocks();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int M = p.M, W = p.W;
+  const int mbase = g * kBwdModes;
+  const int m0 = mbase + 2 * tid;
+  const int Mp = p.Mp;
+  const bool act0 = m0 < M, act1 = m0 + 1 < M;
+  const long long B = p.B, T = p.T;
+  const int chunks = p.chunks;
+  const long long k0 = blockIdx.y, nk = gridDim.y;
+  constexpr int kVals = kBlock ? 3 * S : 2 * S;
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  GradSavedSmem<TIO, C, kSplit>& Q = *reinterpret_cast<GradSavedSmem<TIO, C, kSplit>*>(smem_raw);
+
+  ModeConst2 mc = pair_modes(load_mode(p.pp, m0, M, act0), load_mode(p.pp, m0 + 1, M, act1));
+  if constexpr (kBlock) load_norm_weight(mc, p.norm_w, m0, M, act0, act1);
+
+  const long long ntile = k0 < p.tiles ? (p.tiles - 1 - k0) / nk + 1 : 0;
+  const long long items = kSplit * ntile;
+  const unsigned red_bytes = (unsigned)(G * kVals) * 4u;  // per item: kVals floats from each CTA
+  if (tid == 0) {
+#pragma unroll
+    for (int k = 0; k < kSplit; ++k) mbar_init(&Q.bar[k], 1);
+    mbar_init(&Q.red[0], 1);
+    mbar_init(&Q.red[1], 1);
+    mbar_init_fence();
+    if (G > 1) {  // armed for items 0 and 1 before any peer can push
+      mbar_arrive_expect_tx(&Q.red[0], red_bytes);
+      mbar_arrive_expect_tx(&Q.red[1], red_bytes);
+    }
+  }
+  if (G > 1) cluster.sync();  // every CTA's barriers are initialised and armed
+  else __syncthreads();
+
+  float2 acc[kPartModes];
+#pragma unroll
+  for (int q = 0; q < kPartModes; ++q) acc[q] = bcast2(0.0f);
+  double acc_b0 = 0.0, acc_b1 = 0.0;
+  bool timed_out = false;
+  pdl_wait();  // the adjoint carries (scan) are complete from here on
+
+  auto issue = [&](long long w) {  // (thread 0)
+    const TileRef r = tile_ref(k0 + (w / kSplit) * nk, B, T, C);
+    const int part = kSplit - 1 - (int)(w % kSplit);
+    const int nv = max(0, min(S, r.nvalid - part * S));
+    GradSavedStage<TIO, C, kSplit>& st = Q.st[w % kSplit];
+    unsigned long long* bar = &Q.bar[w % kSplit];
+    const int row = (int)(r.b * T + r.t0 + part * S);
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar, 2u * act_box_bytes<TIO, S, kBwdModes>() + act_box_bytes<TIO, S + 1, kBwdModes>() +
+                                   (unsigned)sizeof(TokenCtl) * (unsigned)nv);
+    tma_load_3d(&st.x[0][0][0], &p.map_x, mbase, 0, row, bar);
+    tma_load_3d(&st.dy[0][0][0], &p.map_dy, mbase, 0, row, bar);
+    tma_load_3d(&st.h[0][0][0], &p.map_h, mbase, 0, row - 1, bar);  // (row -1 reads zeros)
+    if (nv > 0) bulk_copy_g2s(&st.ctl[0], p.ctl + r.b * T + r.t0 + part * S, (unsigned)sizeof(TokenCtl) * (unsigned)nv, bar);
+  };
+  // the adjoint entering a tile from the later chunks (the scan's output), or the gradient of the
+  // returned last state at the last chunk
+  auto tile_kin = [&](long long i) -> Cx2 {
+    const TileRef r = tile_ref(i, B, T, C);
+    float2 a = make_float2(0.0f, 0.0f), c = a;
+    if (r.c < chunks - 1) {
+      const float2* ks = p.kout + (r.b * chunks + (r.c + 1)) * (long long)M;
+      if (act0) a = __ldcg(ks + m0);
+      if (act1) c = __ldcg(ks + m0 + 1);
+    } else if (p.glast_r != nullptr) {
+      if (act0) a = make_float2(p.glast_r[r.b * M + m0], p.glast_i[r.b * M + m0]);
+      if (act1) c = make_float2(p.glast_r[r.b * M + m0 + 1], p.glast_i[r.b * M + m0 + 1]);
+    }
+    return cx2(make_float2(a.x, c.x), make_float2(a.y, c.y));
+  };
+  if (tid == 0) {
+    for (int k = 0; k < kSplit; ++k)
+      if (k < items) issue(k);
+  }
+  Cx2 kin_next = ntile > 0 ? tile_kin(k0) : cx2(bcast2(0.0f), bcast2(0.0f));
+  Cx2 lam = kin_next;
+
+  for (long long w = 0; w < items; ++w) {
+    const long long i = k0 + (w / kSplit) * nk;
+    const TileRef r = tile_ref(i, B, T, C);
+    const long long b = r.b;
+    const int part = kSplit - 1 - (int)(w % kSplit);
+    const int tb = part * S;  // the part's first token within the chunk
+    const int nv = max(0, min(S, r.nvalid - tb));
+    const int par = (int)(w & 1);
+    GradSavedStage<TIO, C, kSplit>& st = Q.st[w % kSplit];
+    if (part == kSplit - 1) {
+      lam = kin_next;  // a new tile: the adjoint from the later chunks
+      if (w / kSplit + 1 < ntile) kin_next = tile_kin(i + nk);  // (in flight under this tile)
+    }
+    if (!mbar_wait(&Q.bar[w % kSplit], (unsigned)((w / kSplit) & 1), p.max_spin << 4)) timed_out = true;
+    // the state before token 0 of the sequence: h0 (else zero), not the row in front of it
+    const bool first = r.c == 0 && part == 0;
+    Cx2 hfirst = cx2(bcast2(0.0f), bcast2(0.0f));
+    if (first && p.h0_r != nullptr) {
+      hfirst = cx2(make_float2(act0 ? p.h0_r[b * M + m0] : 0.0f, act1 ? p.h0_r[b * M + m0 + 1] : 0.0f),
+                   make_float2(act0 ? p.h0_i[b * M + m0] : 0.0f, act1 ? p.h0_i[b * M + m0 + 1] : 0.0f));
+    }
+    const long long row0 = (b * T + r.t0 + tb) * W;
+
+    auto body = [&](auto full_tag) {
+      constexpr bool kFull = decltype(full_tag)::value;
+      auto mixer_in = [&](int u, float2 xr, float2 xi, float2& nr, float2& ni) {
+        if constexpr (kBlock) {
+          const float2 rr = make_float2(st.ctl[u].keep.z, st.ctl[u].keep.w);
+          nr = mul2(xr, mul2(rr, mc.wre));
+          ni = mul2(xi, mul2(rr, mc.wim));
+        } else {
+          nr = xr;
+          ni = xi;
+        }
+      };
+      // pass B: the true adjoint with every gradient, kGroup tokens at a time (lane 4u+j of the
+      // warp ends up with value u of the group, as in the replaying kernel)
+      float2 fa[5];
+#pragma unroll
+      for (int q = 0; q < 5; ++q) fa[q] = bcast2(0.0f);
+      // the state of the token being walked (the later neighbour's previous state, carried)
+      Cx2 hc = cx2(Pair<TIO>::load(&st.h[S][0][2 * tid]), Pair<TIO>::load(&st.h[S][1][2 * tid]));
+      if (!kFull && nv < S && nv > 0) hc = cx2(Pair<TIO>::load(&st.h[nv][0][2 * tid]), Pair<TIO>::load(&st.h[nv][1][2 * tid]));
+#pragma unroll 1
+      for (int u1 = S - 1; u1 >= 0; u1 -= kGroup) {
+        float v[2 * kGroup];
+        float v3[kGroup];
+#pragma unroll
+        for (int j = 0; j < kGroup; ++j) {
+          const int u = u1 - j;
+          float ve = 0.0f, vd = 0.0f, vs = 0.0f;
+          if (kFull || u < nv) {
+            const TokenCtl& tc = st.ctl[u];
+            const float2 gr = Pair<TIO>::load(&st.dy[u][0][2 * tid]);
+            const float2 gi = Pair<TIO>::load(&st.dy[u][1][2 * tid]);
+            if constexpr (kProj) {
+              lam.re = add2(lam.re, gr);
+              lam.im = add2(lam.im, gi);
+            } else {  // relu mask of the output gradient from this token's state
+              lam.re = add2(lam.re, make_float2(hc.re.x > 0.0f ? gr.x : 0.0f, hc.re.y > 0.0f ? gr.y : 0.0f));
+              lam.im = add2(lam.im, make_float2(hc.im.x > 0.0f ? gi.x : 0.0f, hc.im.y > 0.0f ? gi.y : 0.0f));
+            }
+            const Cx2 pv = (u > 0 || !first) ? cx2(Pair<TIO>::load(&st.h[u][0][2 * tid]), Pair<TIO>::load(&st.h[u][1][2 * tid]))
+                                             : hfirst;
+            const float2 xr = Pair<TIO>::load(&st.x[u][0][2 * tid]);
+            const float2 xi = Pair<TIO>::load(&st.x[u][1][2 * tid]);
+            float2 nr, ni;
+            mixer_in(u, xr, xi, nr, ni);
+            float2 ve2, vd2;
+            const Cx2 dxc = grad_step2<kFast, kMode>(mc, tc, lam, pv, nr, ni, ve2, vd2, fa, lin);
+            Pair<TIO>::store(&st.h[u + 1][0][2 * tid], dxc.re.x, dxc.re.y);  // (h[u + 1] was last read above)
+            Pair<TIO>::store(&st.h[u + 1][1][2 * tid], dxc.im.x, dxc.im.y);
+            hc = pv;
+            ve = (act0 ? ve2.x : 0.0f) + (act1 ? ve2.y : 0.0f);
+            vd = (act0 ? vd2.x : 0.0f) + (act1 ? vd2.y : 0.0f);
+            if constexpr (kBlock) {
+              const float2 sx = fma2(mul2(xr, mc.wre), dxc.re, mul2(mul2(xi, mc.wim), dxc.im));
+              vs = (act0 ? sx.x : 0.0f) + (act1 ? sx.y : 0.0f);
+            }
+          }
+          v[j] = ve;
+          v[kGroup + j] = vd;
+          v3[j] = vs;
+        }
+        {
+          constexpr int kShift = 5 - log2i<2 * kGroup>();
+          const float total = transpose_reduce<2 * kGroup>(v, lane);
+          if ((lane & ((1 << kShift) - 1)) == 0) {
+            const int j = lane >> kShift;
+            Q.warp_part[warp][(j < kGroup ? 0 : S) + u1 - (j % kGroup)] = total;
+          }
+        }
+        if constexpr (kBlock) {
+          constexpr int kShift = 5 - log2i<kGroup>();
+          const float total = transpose_reduce<kGroup>(v3, lane);
+          if ((lane & ((1 << kShift) - 1)) == 0) Q.warp_part[warp][2 * S + u1 - (lane >> kShift)] = total;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 5; ++q) acc[q] = add2(acc[q], fa[q]);
+
+      // per-token sums over all modes: the CTA's warps, then (G > 1) the cluster's CTAs, each of
+      // which pushes its partials into every CTA's part_all (asynchronous stores completing on
+      // the receiver's `red` barrier: no cluster barrier in the loop)
+      __syncthreads();
+      if (G > 1) {
+        if (tid < kVals) {
+          float sum = 0.0f;
+#pragma unroll
+          for (int ww = 0; ww < kGradWarps; ++ww) sum += Q.warp_part[ww][tid];
+          for (int rr = 0; rr < G; ++rr)
+            st_async_f32(cluster_smem_addr(&Q.part_all[par][g][tid], (unsigned)rr), sum,
+                         cluster_smem_addr(&Q.red[par], (unsigned)rr));
+        }
+        if (!mbar_wait_cluster(&Q.red[par], (unsigned)((w >> 1) & 1), p.max_spin << 4)) timed_out = true;
+        // (re-armed for item w + 2: no peer can push that item before this CTA has pushed item w + 1)
+        if (tid == 0 && w + 2 < items) mbar_arrive_expect_tx(&Q.red[par], red_bytes);
+      }
+      if (tid < S) {
+        const int u = tid;
+        float te = 0.0f, td = 0.0f, ts = 0.0f;
+        if (G > 1) {
+#pragma unroll
+          for (int rr = 0; rr < 8; ++rr) {
+            if (rr < G) {  // fixed rank order: the same sums in every CTA
+              te += Q.part_all[par][rr][u];
+              td += Q.part_all[par][rr][S + u];
+              if constexpr (kBlock) ts += Q.part_all[par][rr][2 * S + u];
+            }
+          }
+        } else {
+#pragma unroll
+          for (int ww = 0; ww < kGradWarps; ++ww) {
+            te += Q.warp_part[ww][u];
+            td += Q.warp_part[ww][S + u];
+            if constexpr (kBlock) ts += Q.warp_part[ww][2 * S + u];
+          }
+        }
+        const TokenCtl& tc = st.ctl[u];
+        const bool ok = u < nv;
+        const float tau0 = ok ? tc.tau.x : 0.0f, tau1 = ok ? tc.tau.z : 0.0f;
+        // d/dp of eta = ln16 tanh(p1), delta = pi/2 tanh(p0); the scan-level mode returns the
+        // gradients of (delta, eta) themselves
+        const float dp1 = ok ? (kScan ? te : te * kLn16 * fmaf(-tau1, tau1, 1.0f)) : 0.0f;
+        const float dp0 = ok ? (kScan ? td : td * kHalfPi * fmaf(-tau0, tau0, 1.0f)) : 0.0f;
+        Q.dp[u] = make_float4(dp0, dp0, dp1, dp1);
+        if constexpr (kProj) {
+          if (g == 0 && ok) p.dp_out[b * T + r.t0 + tb + u] = make_float2(dp0, dp1);
+        }
+        if constexpr (kBlock) {
+          const float rs = ok ? tc.keep.z : 0.0f;
+          const float sxn = ok ? fmaf(dp0, tc.proj.x, fmaf(dp1, tc.proj.y, ts)) : 0.0f;
+          const float kappa = rs * rs * rs * sxn / (float)W;
+          Q.kap[u] = make_float2(kappa, kappa);
+        }
+      }
+      __syncthreads();
+
+      // pass C: dx (the write path plus the controllers' and, in a block, the norm's terms)
+      TIO* dxrow = static_cast<TIO*>(p.dx) + row0;
+      float2 fd[4] = {bcast2(0.0f), bcast2(0.0f), bcast2(0.0f), bcast2(0.0f)};
+      float2 fw[2] = {bcast2(0.0f), bcast2(0.0f)};
+#pragma unroll
+      for (int u = 0; u < S; ++u) {
+        if (kFull || u < nv) {
+          const float4 dpv = Q.dp[u];
+          const float2 dp0 = make_float2(dpv.x, dpv.y), dp1 = make_float2(dpv.z, dpv.w);
+          const float2 xr = Pair<TIO>::load(&st.x[u][0][2 * tid]);
+          const float2 xi = Pair<TIO>::load(&st.x[u][1][2 * tid]);
+          const float2 dnr = fma2(dp0, mc.d0r, fma2(dp1, mc.d1r, Pair<TIO>::load(&st.h[u + 1][0][2 * tid])));
+          const float2 dni = fma2(dp0, mc.d0i, fma2(dp1, mc.d1i, Pair<TIO>::load(&st.h[u + 1][1][2 * tid])));
+          float2 dre, dim, nr, ni;
+          if constexpr (kBlock) {
+            const float2 rr = make_float2(st.ctl[u].keep.z, st.ctl[u].keep.w);
+            const float2 kap = Q.kap[u];
+            const float2 rwr = mul2(rr, mc.wre), rwi = mul2(rr, mc.wim);
+            dre = sub2(fma2(rwr, dnr, Pair<TIO>::load(&st.dy[u][0][2 * tid])), mul2(kap, xr));
+            dim = sub2(fma2(rwi, dni, Pair<TIO>::load(&st.dy[u][1][2 * tid])), mul2(kap, xi));
+            nr = mul2(xr, rwr);
+            ni = mul2(xi, rwi);
+            fw[0] = fma2(mul2(xr, rr), dnr, fw[0]);
+            fw[1] = fma2(mul2(xi, rr), dni, fw[1]);
+          } else {
+            dre = dnr;
+            dim = dni;
+            nr = xr;
+            ni = xi;
+          }
+          TIO* row = dxrow + (long long)u * W;
+          if (kVec && act1) {
+            Pair<TIO>::store(row + m0, dre.x, dre.y);
+            Pair<TIO>::store(row + M + m0, dim.x, dim.y);
+          } else {
+            if (act0) {
+              Io<TIO>::store(row + m0, dre.x);
+              Io<TIO>::store(row + M + m0, dim.x);
+            }
+            if (act1) {
+              Io<TIO>::store(row + m0 + 1, dre.y);
+              Io<TIO>::store(row + M + m0 + 1, dim.y);
+            }
+          }
+          if constexpr (!kProj) {
+            fd[0] = fma2(nr, dp0, fd[0]);
+            fd[1] = fma2(ni, dp0, fd[1]);
+            fd[2] = fma2(nr, dp1, fd[2]);
+            fd[3] = fma2(ni, dp1, fd[3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[5 + q] = add2(acc[5 + q], fd[q]);
+      if constexpr (kBlock) {
+        acc[9] = add2(acc[9], fw[0]);
+        acc[10] = add2(acc[10], fw[1]);
+      }
+    };
+    if (nv == S) body(std::true_type{});
+    else body(std::false_type{});
+    if (g == 0 && tid == 0) {
+      float s0 = 0.0f, s1 = 0.0f;
+      for (int u = 0; u < S; ++u) {
+        s0 += Q.dp[u].x;
+        s1 += Q.dp[u].z;
+      }
+      acc_b0 += s0;
+      acc_b1 += s1;
+    }
+    __syncthreads();  // the stage, dp and kap are free
+    if (tid == 0 && w + kSplit < items) issue(w + kSplit);
   }
   // per-cluster partial parameter gradients (reduced in a fixed order by mixer_reduce_kernel)
   const long long kc = blockIdx.y;
