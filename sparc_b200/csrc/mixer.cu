@@ -212,32 +212,26 @@ struct TokenCoef2 {
 // kRot (see transition_rot): 1 the hardware sin / cos of the whole angle (MUFU pipe), 0 the
 // series of the bounded offset (FMA pipe), 2 the hardware sin / cos of the offset; by default
 // the fast path's choice (1 for bfloat16, 0 for float32).
-template <bool kFast, int kRot = kFast ? 1 : 0, bool kScan = false>
-__device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0,
-                                                  float2 tau1, float2 keep) {
-  TokenCoef2 k;
-  k.z = mul2(mc.nu, E);
-  k.rho = ex2_2(mul2(mc.nl2e_neg, E));
-  const float2 rk = mul2(k.rho, keep);  // the transition's radius (0 at a reset)
+// The transition a = rk e^{i(theta + (1 - rho) delta)} of two modes (rk = rho keep: 0 at a
+// reset), the rotation by kRot; the scan-level mode (kScan) takes any delta (reduced offset).
+template <int kRot, bool kScan>
+__device__ __forceinline__ Cx2 transition2(const ModeConst2& mc, float2 rho, float2 rk, float2 delta) {
   if constexpr (kScan) {
-    // scan-level mode: any delta (reduced offset), and the write is b itself (unit gain)
-    const float2 off = sub2(delta, mul2(k.rho, delta));
+    const float2 off = sub2(delta, mul2(rho, delta));
     float2 sn, cs;
     sincos_reduced(off.x, &sn.x, &cs.x);
     sincos_reduced(off.y, &sn.y, &cs.y);
     const float2 rct = mul2(rk, mc.ct), rst = mul2(rk, mc.st);
-    k.a = Cx2{sub2(mul2(rct, cs), mul2(rst, sn)), fma2(rst, cs, mul2(rct, sn))};
-    k.num = k.gate = k.gain = bcast2(1.0f);
-    return k;
+    return Cx2{sub2(mul2(rct, cs), mul2(rst, sn)), fma2(rst, cs, mul2(rct, sn))};
   } else if constexpr (kRot == 1) {
-    const float2 ph = sub2(add2(delta, mc.theta), mul2(k.rho, delta));  // theta + (1 - rho) delta
+    const float2 ph = sub2(add2(delta, mc.theta), mul2(rho, delta));  // theta + (1 - rho) delta
     float2 sn, cs;
     sincos_hw(ph.x, &sn.x, &cs.x);
     sincos_hw(ph.y, &sn.y, &cs.y);
-    k.a = Cx2{mul2(rk, cs), mul2(rk, sn)};
+    return Cx2{mul2(rk, cs), mul2(rk, sn)};
   } else {
     float2 sn, cs;
-    const float2 off = sub2(delta, mul2(k.rho, delta));  // (1 - rho) delta, |.| <= pi/2
+    const float2 off = sub2(delta, mul2(rho, delta));  // (1 - rho) delta, |.| <= pi/2
     if constexpr (kRot == 2) {
       sincos_hw(off.x, &sn.x, &cs.x);
       sincos_hw(off.y, &sn.y, &cs.y);
@@ -245,7 +239,20 @@ __device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E
       sincos_halfpi2(off, &sn, &cs);
     }
     const float2 rct = mul2(rk, mc.ct), rst = mul2(rk, mc.st);
-    k.a = Cx2{sub2(mul2(rct, cs), mul2(rst, sn)), fma2(rst, cs, mul2(rct, sn))};
+    return Cx2{sub2(mul2(rct, cs), mul2(rst, sn)), fma2(rst, cs, mul2(rct, sn))};
+  }
+}
+
+template <bool kFast, int kRot = kFast ? 1 : 0, bool kScan = false>
+__device__ __forceinline__ TokenCoef2 token_coef2(const ModeConst2& mc, float2 E, float2 delta, float2 tau0,
+                                                  float2 tau1, float2 keep) {
+  TokenCoef2 k;
+  k.z = mul2(mc.nu, E);
+  k.rho = ex2_2(mul2(mc.nl2e_neg, E));
+  k.a = transition2<kRot, kScan>(mc, k.rho, mul2(k.rho, keep), delta);
+  if constexpr (kScan) {  // the write is b itself (unit gain)
+    k.num = k.gate = k.gain = bcast2(1.0f);
+    return k;
   }
   const float2 q = fma2(tau0, mc.wpr, mul2(tau1, mc.wrr));
   const float2 u = add2(k.z, k.z);
@@ -353,7 +360,7 @@ constexpr int kScanQ = SPARC_SCAN_Q;            // CTAs per (row, 32 modes): a p
 constexpr int kScanWarps = SPARC_SCAN_WARPS;    // spans per CTA
 constexpr int kScanSpans = kScanQ * kScanWarps;
 constexpr int kScanThreads = 32 * kScanWarps;
-constexpr int kScanHold = 8;                    // span maps held in registers (longer spans reload)
+constexpr int kScanHold = 16;                   // span maps held in registers (longer spans reload)
 
 struct ScanParams {
   const float4* agg;     // [B, chunks, Mp] per-chunk maps (A, B)
@@ -411,13 +418,24 @@ __global__ void __launch_bounds__(kScanThreads) mixer_carry_scan_kernel(const Sc
   // carry into the span: init, then the earlier spans' maps in order
   float2 v = make_float2(0.0f, 0.0f);
   if (p.init_r != nullptr && act) v = make_float2(p.init_r[b * p.M + m], p.init_i[b * p.M + m]);
-  for (int k = 0; k < q; ++k) {  // the earlier CTAs' spans (their loads together)
-    const float4* peer = cluster.map_shared_rank(&s_map[0][0], k);
-    float4 mk[kScanWarps];
+  {  // the earlier CTAs' spans: every read issued before the first composition
+    float4 mk[kScanQ - 1][kScanWarps];
 #pragma unroll
-    for (int u = 0; u < kScanWarps; ++u) mk[u] = peer[u * 32 + lane];
+    for (int k = 0; k < kScanQ - 1; ++k) {
+      if (k < q) {
+        const float4* peer = cluster.map_shared_rank(&s_map[0][0], k);
 #pragma unroll
-    for (int u = 0; u < kScanWarps; ++u) v = cfma(make_float2(mk[u].x, mk[u].y), v, make_float2(mk[u].z, mk[u].w));
+        for (int u = 0; u < kScanWarps; ++u) mk[k][u] = peer[u * 32 + lane];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kScanQ - 1; ++k) {
+      if (k < q) {
+#pragma unroll
+        for (int u = 0; u < kScanWarps; ++u)
+          v = cfma(make_float2(mk[k][u].x, mk[k][u].y), v, make_float2(mk[k][u].z, mk[k][u].w));
+      }
+    }
   }
   for (int u = 0; u < w; ++u) {  // this CTA's earlier spans
     const float4 mk = s_map[u][lane];
