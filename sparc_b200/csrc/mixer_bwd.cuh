@@ -704,8 +704,6 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_saved_kernel(c
   for (int q = 0; q < kPartModes; ++q) acc[q] = bcast2(0.0f);
   double acc_b0 = 0.0, acc_b1 = 0.0;
   bool timed_out = false;
-  pdl_wait();  // the adjoint carries (scan) are complete from here on
-
   auto issue = [&](long long w) {  // (thread 0)
     const TileRef r = tile_ref(k0 + (w / kSplit) * nk, B, T, C);
     const int part = kSplit - 1 - (int)(w % kSplit);
@@ -736,10 +734,14 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_saved_kernel(c
     }
     return cx2(make_float2(a.x, c.x), make_float2(a.y, c.y));
   };
+  // The first stages' copies go out before the wait: x, dy, the states and the controls come from
+  // kernels before the carry scan, which have completed when this kernel starts (see pdl_wait);
+  // only the adjoint carries need the wait.
   if (tid == 0) {
     for (int k = 0; k < kSplit; ++k)
       if (k < items) issue(k);
   }
+  pdl_wait();  // the adjoint carries (scan) are complete from here on
   Cx2 kin_next = ntile > 0 ? tile_kin(k0) : cx2(bcast2(0.0f), bcast2(0.0f));
   Cx2 lam = kin_next;
 

@@ -409,24 +409,34 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
   }
   __syncthreads();
 
-  pdl_wait();  // the controls (summary) and the carries (scan) are complete from here on
+  // Tile inputs: x rows, the C token controls and (for c > 0) the carried-in chunk state. With
+  // `carried` false only x and the controls are issued (and the carry is expected), for the first
+  // tile before the wait: x and the controls come from kernels before the carry scan, which have
+  // completed when this kernel starts (see pdl_wait).
+  auto issue_tma = [&](long long i, int buf, bool inputs, bool carried) {  // (thread 0)
+    const TileRef r = tile_ref(i, B, T, C);
+    const float2* hsrc = r.c > 0 ? p.carry + (r.b * p.chunks + (r.c - 1)) * (long long)M + mbase : nullptr;
+    if (inputs) {
+      fence_proxy_async_smem();
+      unsigned bytes = act_box_bytes<TIO, C, kFwdModes>() + (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
+      if (hsrc != nullptr) bytes += (unsigned)ncols * 8u;
+      mbar_arrive_expect_tx(&S.bar[buf], bytes);
+      tma_load_3d(&S.x[buf][0][0][0], &p.map_x, mbase, 0, (int)(r.b * T + r.t0), &S.bar[buf]);
+      bulk_copy_g2s(&S.ctl[buf][0], p.ctl + r.b * T + r.t0, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar[buf]);
+    }
+    if (carried && hsrc != nullptr) bulk_copy_g2s(&S.hin[buf][0], hsrc, (unsigned)ncols * 8u, &S.bar[buf]);
+  };
+  if (p.use_tma && tid == 0 && k0 < p.tiles) issue_tma(k0, 0, true, false);
 
-  // Tile inputs: x rows, the C token controls and (for c > 0) the carried-in chunk state.
+  pdl_wait();  // the carries (scan) are complete from here on
+
   auto issue = [&](long long i, int buf) {
     const TileRef r = tile_ref(i, B, T, C);
     const TIO* src = static_cast<const TIO*>(p.x) + (r.b * T + r.t0) * W;
     const TokenCtl* csrc = p.ctl + r.b * T + r.t0;
     const float2* hsrc = r.c > 0 ? p.carry + (r.b * p.chunks + (r.c - 1)) * (long long)M + mbase : nullptr;
     if (p.use_tma) {
-      if (tid == 0) {
-        fence_proxy_async_smem();
-        unsigned bytes = act_box_bytes<TIO, C, kFwdModes>() + (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
-        if (hsrc != nullptr) bytes += (unsigned)ncols * 8u;
-        mbar_arrive_expect_tx(&S.bar[buf], bytes);
-        tma_load_3d(&S.x[buf][0][0][0], &p.map_x, mbase, 0, (int)(r.b * T + r.t0), &S.bar[buf]);
-        bulk_copy_g2s(&S.ctl[buf][0], csrc, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar[buf]);
-        if (hsrc != nullptr) bulk_copy_g2s(&S.hin[buf][0], hsrc, (unsigned)ncols * 8u, &S.bar[buf]);
-      }
+      if (tid == 0) issue_tma(i, buf, true, true);
     } else {
       load_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], kFwdThreads);
       for (int t = tid; t < r.nvalid; t += kFwdThreads) S.ctl[buf][t] = csrc[t];
@@ -434,7 +444,13 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
         for (int mm = tid; mm < ncols; mm += kFwdThreads) S.hin[buf][mm] = hsrc[mm];
     }
   };
-  if (k0 < p.tiles) issue(k0, 0);
+  if (k0 < p.tiles) {
+    if (p.use_tma) {
+      if (tid == 0) issue_tma(k0, 0, false, true);  // (x and the controls are on their way)
+    } else {
+      issue(k0, 0);
+    }
+  }
   bool timed_out = false;
 
   for (long long n = 0;; ++n) {
