@@ -531,10 +531,11 @@ const char* sparc_proj_gemm_last_error(void);
  * collective), and each rank opens the others' (sparc_peer_buffer_open). sparc_peer_allreduce
  * then sums the float32 gradient segments (in order, `total` floats) over the ranks in place:
  * every rank gets the identical sum in rank order, times `scale`. One kernel: each CTA pushes
- * its slice into every rank's buffer, publishes an epoch flag per rank and waits (bounded by
- * max_spin polls; a wait that runs out or's 8 into *status) for every rank's slice. Every rank
- * must call it the same number of times with the same total. inject_skip_publish (tests only)
- * withholds this rank's flags so that the peers' waits run out. */
+ * its slice into every rank's buffer, every value stored with the launch's epoch as one 8-byte
+ * word, and waits (bounded by max_spin polls; a wait that runs out or's 8 into *status) until
+ * its words from every rank carry the epoch. Every rank must call it the same number of times
+ * with the same total. inject_skip_publish (tests only) withholds this rank's push so that the
+ * peers' waits run out. */
 #define SPARC_PEER_MAX_RANKS 8
 #define SPARC_PEER_MAX_SEGMENTS 64
 typedef struct SparcPeerAllreduceArgs {

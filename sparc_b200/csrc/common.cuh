@@ -392,13 +392,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 // One warp's values summed over the ranks of a data-parallel group through NVLink peer memory,
 // inside the kernel that computed them (the parameter-gradient reduction). Every rank holds an
 // exchange buffer mapped into every rank (CUDA IPC):
-//   flags [8][kXchgSlots] u32, epoch [kXchgSlots] u32, inbox [2][world][kXchgSlots][32] f32.
+//   epoch [kXchgSlots] u32, inbox [2][world][kXchgSlots][32] u64.
 // A slot is one warp-sized group of values of one launch geometry; its epoch counts the
-// launches that used it. The warp stores its 32 values into inbox[e & 1][rank][slot] of every
-// rank, publishes e in every rank's flags[rank][slot] (release, system scope), waits (bounded)
-// until every rank's flag for the slot reaches e (acquire), and sums the ranks' values in rank
-// order: every rank gets the identical sum. A peer can run one exchange ahead on a slot (the
-// parity double-buffers the inbox) but not two (it needs this rank's next push first).
+// launches that used it. Each lane stores its value together with the epoch e as one 8-byte word
+// (value in the low half, e in the high half: a naturally aligned 8-byte store is single-copy
+// atomic, so a reader that sees e sees the value stored with it) into inbox[e & 1][rank][slot]
+// of every rank, then waits (bounded) until the word from every rank carries e in its own inbox,
+// and sums the ranks' values in rank order: every rank gets the identical sum. No fence and no
+// separate flag: one NVLink write per value is the whole exchange. A peer can run one exchange
+// ahead on a slot (the parity double-buffers the inbox) but not two (it needs this rank's next
+// push first), so a word of the other parity is never overwritten while it is awaited.
 constexpr int kXchgSlots = 1024;
 constexpr int kXchgMaxRanks = 8;
 constexpr unsigned kStatusXchgTimeout = 16u;
@@ -410,10 +413,9 @@ struct PeerExchange {
   unsigned max_spin;
 };
 
-__host__ __device__ constexpr size_t xchg_flags_bytes() { return (size_t)kXchgMaxRanks * kXchgSlots * 4; }
-__host__ __device__ constexpr size_t xchg_inbox_offset() { return xchg_flags_bytes() + (size_t)kXchgSlots * 4; }
+__host__ __device__ constexpr size_t xchg_inbox_offset() { return (size_t)kXchgSlots * 4; }
 __host__ __device__ constexpr size_t xchg_buffer_bytes(int world) {
-  return xchg_inbox_offset() + 2 * (size_t)world * kXchgSlots * 32 * 4;
+  return xchg_inbox_offset() + 2 * (size_t)world * kXchgSlots * 32 * 8;
 }
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
@@ -424,40 +426,55 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // Called by all 32 lanes of one warp with the lane's value; returns the sum over the ranks.
 __device__ __forceinline__ float warp_exchange(const PeerExchange& x, int slot, float val) {
   const int lane = threadIdx.x & 31;
-  unsigned* flags_own = reinterpret_cast<unsigned*>(x.base[x.rank]);
-  unsigned* epoch = reinterpret_cast<unsigned*>(x.base[x.rank] + xchg_flags_bytes()) + slot;
+  unsigned* epoch = reinterpret_cast<unsigned*>(x.base[x.rank]) + slot;
   unsigned e = 0;
   if (lane == 0) e = *epoch + 1u;
   e = __shfl_sync(0xffffffffu, e, 0);
   const long long par = e & 1u;
+  const unsigned long long word = ((unsigned long long)e << 32) | (unsigned long long)__float_as_uint(val);
   for (int r = 0; r < x.world; ++r) {
-    float* in = reinterpret_cast<float*>(x.base[r] + xchg_inbox_offset());
-    in[((par * x.world + x.rank) * kXchgSlots + slot) * 32 + lane] = val;
+    unsigned long long* in = reinterpret_cast<unsigned long long*>(x.base[r] + xchg_inbox_offset());
+    st_relaxed_sys_u64(in + ((par * x.world + x.rank) * kXchgSlots + slot) * 32 + lane, word);
   }
-  __syncwarp();  // the warp's peer stores precede the release below (cumulativity)
-  if (lane < x.world)
-    st_release_sys(reinterpret_cast<unsigned*>(x.base[lane]) + (long long)x.rank * kXchgSlots + slot, e);
+  const unsigned long long* own = reinterpret_cast<const unsigned long long*>(x.base[x.rank] + xchg_inbox_offset());
+  float v[kXchgMaxRanks];
   bool late = false;
-  if (lane < x.world) {
-    const unsigned* f = flags_own + (long long)lane * kXchgSlots + slot;
-    unsigned it = 0;
-    while ((int)(ld_acquire_sys(f) - e) < 0) {
-      if (++it >= x.max_spin) {
-        late = true;
-        break;
+#pragma unroll
+  for (int r = 0; r < kXchgMaxRanks; ++r) {
+    v[r] = 0.0f;
+    if (r < x.world) {
+      const unsigned long long* w = own + ((par * x.world + r) * kXchgSlots + slot) * 32 + lane;
+      unsigned long long got = ld_relaxed_sys_u64(w);
+      unsigned it = 0;
+      while ((unsigned)(got >> 32) != e) {
+        if (++it >= x.max_spin) {
+          late = true;
+          break;
+        }
+        __nanosleep(32);
+        got = ld_relaxed_sys_u64(w);
       }
-      __nanosleep(64);
+      v[r] = __uint_as_float((unsigned)got);
     }
   }
   if (late) atomicOr(x.status, kStatusXchgTimeout);
-  __syncwarp();
-  const float* own = reinterpret_cast<const float*>(x.base[x.rank] + xchg_inbox_offset());
   float s = 0.0f;
-  for (int r = 0; r < x.world; ++r) s += __ldcv(own + ((par * x.world + r) * kXchgSlots + slot) * 32 + lane);
+#pragma unroll
+  for (int r = 0; r < kXchgMaxRanks; ++r)
+    if (r < x.world) s += v[r];
+  __syncwarp();
   if (lane == 0) *epoch = e;
   return s;
 }

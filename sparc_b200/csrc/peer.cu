@@ -3,21 +3,21 @@
 // layer: a latency-bound collective).
 //
 // Every rank holds one buffer, mapped into every other rank's address space by CUDA IPC:
-//   flags [kMaxPeers][ctas] u32   flags[src][c]: the epoch of src's last push of slice c
 //   epoch [ctas] u32              this rank's launch count, one word per CTA
-//   inbox [2][world][cap] f32     inbox[e & 1][src]: src's gradients of epoch e
+//   inbox [2][world][cap] u64     inbox[e & 1][src]: src's gradients of epoch e, each float in
+//                                 the low half of an 8-byte word whose high half holds e
 // One launch, grid = ceil(total / 1024) CTAs of 256 threads, CTA c owning the flat gradient
 // elements [1024 c, 1024 c + 1024): it gathers its slice from the gradient tensors (up to 64
-// segments), stores it into inbox[e & 1][rank] of EVERY rank's buffer (peer stores over
-// NVLink), and after a CTA barrier its threads 0..world-1 publish the epoch e in the flags of
-// every rank (st.release.sys). Then threads 0..world-1 poll their own flags[r][c] until every
-// rank's slice c of epoch e has arrived (ld.acquire.sys, bounded: a wait that runs out sets a
-// status bit and the sum proceeds), and the CTA sums inbox[e & 1][0..world-1] in rank order into
-// the gradient tensors: every rank computes the identical sum (deterministic, rank-independent).
-// Epoch parity double-buffers the inbox: a peer can be one launch ahead (it has seen this rank's
-// push of epoch e) but not two (epoch e+2 needs this rank's push of e+1, which starts only after
-// this launch, including its reads of inbox[e & 1], has finished on this stream).
-// Each CTA keeps its own epoch word, so no CTA of a launch can see another's update.
+// segments) and stores each value with the epoch e as one 8-byte word into inbox[e & 1][rank] of
+// EVERY rank's buffer (peer stores over NVLink; a naturally aligned 8-byte store is single-copy
+// atomic, so a reader that sees e in a word sees the value stored with it: no fence, no flag).
+// Then every thread polls, in its own inbox, its elements' words from every rank until they carry
+// e (bounded: a wait that runs out sets a status bit and the sum proceeds), and sums them in rank
+// order into the gradient tensors: every rank computes the identical sum (deterministic,
+// rank-independent). Epoch parity double-buffers the inbox: a peer can be one launch ahead (it
+// has seen this rank's push of epoch e) but not two (epoch e+2 needs this rank's push of e+1,
+// which starts only after this launch, including its reads of inbox[e & 1], has finished on this
+// stream). Each CTA keeps its own epoch word, so no CTA of a launch can see another's update.
 #include "common.cuh"
 #include "sparc_b200.h"
 #include "timing.cuh"
@@ -36,17 +36,16 @@ constexpr unsigned kStatusPeerTimeout = 8u;
 
 struct PeerLayout {
   long long ctas, cap;
-  size_t flags, epoch, inbox, total;
+  size_t epoch, inbox, total;
 };
 
 static PeerLayout peer_layout(int world, long long total) {
   PeerLayout L;
   L.ctas = (total + kPeerSlice - 1) / kPeerSlice;
   L.cap = L.ctas * kPeerSlice;
-  L.flags = 0;
-  L.epoch = (size_t)kPeerMax * (size_t)L.ctas * 4;
-  L.inbox = (L.epoch + (size_t)L.ctas * 4 + 255) & ~size_t(255);
-  L.total = L.inbox + 2 * (size_t)world * (size_t)L.cap * 4;
+  L.epoch = 0;
+  L.inbox = ((size_t)L.ctas * 4 + 255) & ~size_t(255);
+  L.total = L.inbox + 2 * (size_t)world * (size_t)L.cap * 8;
   return L;
 }
 
@@ -57,12 +56,12 @@ struct PeerParams {
   long long total;
   unsigned char* base[kPeerMax];   // every rank's buffer, as mapped here (own included)
   long long ctas, cap;
-  unsigned long long flags_off, epoch_off, inbox_off;
+  unsigned long long epoch_off, inbox_off;
   int world, rank;
   float scale;
   unsigned max_spin;
   unsigned* status;
-  int skip_publish;                // failure test: do not publish (peers' waits run out)
+  int skip_publish;                // failure test: push nothing (peers' waits run out)
 };
 
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const __grid_constant__ PeerParams p) {
@@ -95,42 +94,43 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const __gr
       v[u] = p.seg[s][loc[u]];
     }
   }
-  // push into inbox[par][rank] of every rank
-  for (int r = 0; r < p.world; ++r) {
-    float* dst = reinterpret_cast<float*>(p.base[r] + p.inbox_off) + ((long long)par * p.world + p.rank) * p.cap + first;
+  // push each value with the epoch into inbox[par][rank] of every rank
+  const unsigned long long tag = (unsigned long long)e << 32;
+  if (!p.skip_publish) {
+    for (int r = 0; r < p.world; ++r) {
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(p.base[r] + p.inbox_off) +
+                                ((long long)par * p.world + p.rank) * p.cap + first;
 #pragma unroll
-    for (int u = 0; u < kPeerPerThread; ++u)
-      if (segi[u] >= 0) dst[u * kPeerThreads + tid] = v[u];
-  }
-  __syncthreads();  // every thread's peer stores precede the release below (cumulativity)
-  if (tid < p.world && !p.skip_publish) {
-    unsigned* flag = reinterpret_cast<unsigned*>(p.base[tid] + p.flags_off) + (long long)p.rank * p.ctas + c;
-    st_release_sys(flag, e);
-  }
-  // wait for every rank's slice c of epoch e (thread r watches rank r)
-  bool late = false;
-  if (tid < p.world) {
-    const unsigned* flag = reinterpret_cast<const unsigned*>(p.base[p.rank] + p.flags_off) + (long long)tid * p.ctas + c;
-    unsigned it = 0;
-    while ((int)(ld_acquire_sys(flag) - e) < 0) {
-      if (++it >= p.max_spin) {
-        late = true;
-        break;
-      }
-      __nanosleep(64);
+      for (int u = 0; u < kPeerPerThread; ++u)
+        if (segi[u] >= 0) st_relaxed_sys_u64(dst + u * kPeerThreads + tid, tag | __float_as_uint(v[u]));
     }
   }
-  if (late) atomicOr(p.status, kStatusPeerTimeout);
-  __syncthreads();
-  // the sum in rank order (identical on every rank)
-  const float* in = reinterpret_cast<const float*>(p.base[p.rank] + p.inbox_off) + (long long)par * p.world * p.cap + first;
+  // wait for every rank's words of epoch e and sum them in rank order (identical on every rank)
+  const unsigned long long* in =
+      reinterpret_cast<const unsigned long long*>(p.base[p.rank] + p.inbox_off) + (long long)par * p.world * p.cap + first;
+  bool late = false;
 #pragma unroll
   for (int u = 0; u < kPeerPerThread; ++u) {
     if (segi[u] < 0) continue;
     float s = 0.0f;
-    for (int r = 0; r < p.world; ++r) s += __ldcv(in + (long long)r * p.cap + u * kPeerThreads + tid);
+    for (int r = 0; r < p.world; ++r) {
+      const unsigned long long* w = in + (long long)r * p.cap + u * kPeerThreads + tid;
+      unsigned long long got = ld_relaxed_sys_u64(w);
+      unsigned it = 0;
+      while (!late && (unsigned)(got >> 32) != e) {
+        if (++it >= p.max_spin) {
+          late = true;  // (later words of this thread do not wait again)
+          break;
+        }
+        __nanosleep(32);
+        got = ld_relaxed_sys_u64(w);
+      }
+      s += __uint_as_float((unsigned)got);
+    }
     p.seg[segi[u]][loc[u]] = s * p.scale;
   }
+  if (late) atomicOr(p.status, kStatusPeerTimeout);
+  __syncthreads();  // every thread of the CTA is done with this epoch's words
   if (tid == 0) *my_epoch = e;
 }
 
@@ -214,7 +214,6 @@ int sparc_peer_allreduce(const SparcPeerAllreduceArgs* a, void* stream) {
   p.total = total;
   p.ctas = L.ctas;
   p.cap = L.cap;
-  p.flags_off = L.flags;
   p.epoch_off = L.epoch;
   p.inbox_off = L.inbox;
   p.world = a->world;

@@ -1,7 +1,7 @@
 """Worker of tests/test_gpu_multi.py (one process per GPU, launched by torch.distributed.run):
 the peer-memory gradient all-reduce against a float64 sum, identical results on every rank,
 several epochs eager and from a CUDA graph, the bounded wait running out when a rank withholds
-its flags, and the latency against NCCL's all-reduce of the same gradients."""
+its push, and the latency against NCCL's all-reduce of the same gradients."""
 import datetime
 import json
 import os
@@ -94,7 +94,7 @@ def main():
     out["nccl_us"] = timeit(nccl)
     out["status_ok"] = not red.timed_out()
     red.close()
-    # a rank that withholds its flags: the others' bounded waits run out, the launch completes
+    # a rank that withholds its push: the others' bounded waits run out, the launch completes
     red2 = PeerGradAllReduce(params, max_spin=2000)
     red2(inject_skip_publish=(rank == world - 1))
     torch.cuda.synchronize()
