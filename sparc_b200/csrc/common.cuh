@@ -364,6 +364,14 @@ __device__ __forceinline__ void st_async_f32(unsigned raddr, float v, unsigned r
                "r"(rbar)
                : "memory");
 }
+// A cluster barrier for CTA lifetime only (no CTA leaves while a peer may still access its
+// shared memory), with no memory ordering: the peers' accesses before it have completed (their
+// values were used before the arrive issued), and nothing written before it needs to be seen by a
+// peer, so the arrive does not wait for this CTA's outstanding global stores as the ordered
+// (release) form does.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kScanThreads) mixer_carry_scan_kernel(const Sc
     p.final_r[b * p.M + m] = v.x;
     p.final_i[b * p.M + m] = v.y;
   }
-  cluster.sync();  // no CTA leaves while a peer may still read its span maps
+  cluster_sync_relaxed();  // no CTA leaves while a peer may still read its span maps
 }
 
 #include "mixer_fwd.cuh"

@@ -618,7 +618,7 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_kernel(const _
     pb[1] = acc_b1;
   }
   if (timed_out) atomicOr(&p.ls->status, kStatusTimeout);
-  cluster.sync();
+  cluster_sync_relaxed();
 }
 
 
@@ -990,5 +990,5 @@ __global__ void __launch_bounds__(kGradThreads, 4) mixer_bwd_grad_saved_kernel(c
     pb[1] = acc_b1;
   }
   if (timed_out) atomicOr(&p.ls->status, kStatusTimeout);
-  cluster.sync();
+  cluster_sync_relaxed();
 }

@@ -27,9 +27,11 @@ template <typename TIO, int C>
 struct SumSmem {
   TIO x[2][C][2][kFwdModes];  // [buffer][token][re|im][mode]
   TokenCtl ctl[C];
-  float part[2][3 * C];       // this CTA's projection / sum-of-squares partials (peers read), by tile parity
+  float part_all[2][8][3 * C];  // every cluster CTA's projection / sum-of-squares partials (pushed
+                                // by the peers), by tile parity
   float warp_part[kFwdThreads / 32][3 * C];
   unsigned long long bar[2];
+  unsigned long long red[2];    // completes when all G CTAs' partials of a tile have arrived
 };
 
 template <typename TIO, int C>
@@ -222,12 +224,21 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
     unsigned* xs = reinterpret_cast<unsigned*>(&S.x[0][0][0][0]);
     for (int i = tid; i < (int)(sizeof(S.x) / 4); i += kFwdThreads) xs[i] = 0u;
   }
+  constexpr int kVals = kBlock ? 3 * C : 2 * C;  // reduced per-token values
+  const unsigned red_bytes = (unsigned)(G * kVals) * 4u;
   if (tid == 0) {
     mbar_init(&S.bar[0], 1);
     mbar_init(&S.bar[1], 1);
+    mbar_init(&S.red[0], 1);
+    mbar_init(&S.red[1], 1);
     mbar_init_fence();
+    if (!kProj && G > 1) {  // armed for tiles 0 and 1 before any peer can push
+      mbar_arrive_expect_tx(&S.red[0], red_bytes);
+      mbar_arrive_expect_tx(&S.red[1], red_bytes);
+    }
   }
-  __syncthreads();
+  if (G > 1) cluster.sync();  // every CTA's barriers are initialised and armed
+  else __syncthreads();
 
   auto issue = [&](long long i, int buf) {
     const TileRef r = tile_ref(i, B, T, C);
@@ -294,26 +305,38 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
         const float total = transpose_reduce<C>(vs, lane);
         if ((lane & ((1 << kShift) - 1)) == 0) S.warp_part[warp][2 * C + (lane >> kShift)] = total;
       }
-      constexpr int kVals = kBlock ? 3 * C : 2 * C;
+      // the CTA's sums, then (G > 1) every cluster CTA pushes them into every CTA's part_all
+      // with asynchronous stores completing on the receiver's `red` barrier (no cluster barrier
+      // in the loop; a barrier is re-armed for tile n + 2 once tile n's sums have arrived, and no
+      // peer can push tile n + 2 before this CTA has pushed tile n + 1)
       __syncthreads();
       if (tid < kVals) {
         float sum = 0.0f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) sum += S.warp_part[w][tid];
-        S.part[buf][tid] = sum;
+        if (G > 1) {
+          for (int rr = 0; rr < G; ++rr)
+            st_async_f32(cluster_smem_addr(&S.part_all[buf][g][tid], (unsigned)rr), sum,
+                         cluster_smem_addr(&S.red[buf], (unsigned)rr));
+        } else {
+          S.part_all[buf][0][tid] = sum;
+        }
       }
-      if (G > 1) cluster.sync();
-      else __syncthreads();
+      if (G > 1) {
+        if (!mbar_wait_cluster(&S.red[buf], (unsigned)((n >> 1) & 1), p.max_spin << 4)) timed_out = true;
+        if (tid == 0 && i + 2 * nk < p.tiles) mbar_arrive_expect_tx(&S.red[buf], red_bytes);
+      } else {
+        __syncthreads();
+      }
       if (tid < C) {
-        // the peers' partials are read together (their latencies overlap)
+        // the cluster CTAs' partials in rank order (the same sums in every CTA)
         float q0[8], q1[8], qs[8];
 #pragma unroll
         for (int rr = 0; rr < 8; ++rr) {
           if (rr < G) {
-            const float* peer = cluster.map_shared_rank(&S.part[buf][0], rr);
-            q0[rr] = peer[tid];
-            q1[rr] = peer[C + tid];
-            qs[rr] = kBlock ? peer[2 * C + tid] : 0.0f;
+            q0[rr] = S.part_all[buf][rr][tid];
+            q1[rr] = S.part_all[buf][rr][C + tid];
+            qs[rr] = kBlock ? S.part_all[buf][rr][2 * C + tid] : 0.0f;
           } else {
             q0[rr] = q1[rr] = qs[rr] = 0.0f;
           }
@@ -377,7 +400,7 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_summary_kernel(const __
     __syncthreads();  // the buffer and the shared arrays are free for the tile after next
   }
   if (timed_out) atomicOr(&p.ls->status, kStatusTimeout);
-  cluster.sync();  // no CTA leaves while a peer may still read its shared memory
+  cluster_sync_relaxed();  // no CTA leaves while a peer may still read its shared memory
 }
 
 // ------------------------------------------------------------------------------ replay
