@@ -690,7 +690,9 @@ struct Kernels {
   static int saved_split(int G) { return G == 1 ? 2 : 1; }
   static size_t sum_smem() { return sizeof(SumSmem<TIO, C>); }
   static size_t rep_smem() { return sizeof(RepSmem<TIO, C>); }
-  static size_t rsum_smem() { return sizeof(RsumSmem<TIO, C>); }
+  static size_t rsum_smem(int mode) {
+    return mode == kModePlain ? sizeof(RsumSmem<TIO, C, true>) : sizeof(RsumSmem<TIO, C, false>);
+  }
   static size_t grad_smem() { return sizeof(GradSmem<TIO, C>); }
   static size_t saved_smem(int G) { return G == 1 ? sizeof(GradSavedSmem<TIO, C, 2>) : sizeof(GradSavedSmem<TIO, C, 1>); }
 };
@@ -700,7 +702,7 @@ static void plan_kernels(Plan* pl, const void** k) {
   using K = Kernels<TIO>;
   pl->sum_smem = K::sum_smem();
   pl->rep_smem = K::rep_smem();
-  pl->rsum_smem = K::rsum_smem();
+  pl->rsum_smem = K::rsum_smem(pl->mode);
   pl->grad_smem = K::grad_smem();
   pl->saved_smem = K::saved_smem(pl->G);
   k[0] = K::sum(pl->mode);

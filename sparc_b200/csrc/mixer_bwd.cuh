@@ -41,10 +41,13 @@ constexpr int kPartModes = 11;  // nu, theta (sum of phase grads), wlg, wpr, wrr
                                 // norm weight at the real / imaginary column (blocks only)
 constexpr int kGroup = 4;      // tokens per unrolled group of the reverse walk
 
-template <typename TIO, int C>
+// kY: the relu mask comes from a tile of the forward's output (or states); a block reads its
+// relu bits and the projection mode has no relu, and they hold a minimal placeholder instead.
+template <typename TIO, int C, bool kY>
 struct RsumSmem {
+  static constexpr int YB = kY ? 2 : 1, YC = kY ? C : 1;
   TIO dy[2][C][2][kBwdModes];
-  TIO y[2][C][2][kBwdModes];     // the forward's output (not used by blocks)
+  TIO y[YB][YC][2][kBwdModes];    // the forward's output or states (kY)
   TokenCtl ctl[2][C];
   unsigned mask[2][C][16];        // a block's relu bits for the CTA's 256 modes
   unsigned long long bar[2];
@@ -103,7 +106,8 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
   pdl_wait();  // the first launch of the backward: dy comes from the previous kernel
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  RsumSmem<TIO, C>& S = *reinterpret_cast<RsumSmem<TIO, C>*>(smem_raw);
+  constexpr bool kY = !kBlock && !kProj;
+  RsumSmem<TIO, C, kY>& S = *reinterpret_cast<RsumSmem<TIO, C, kY>*>(smem_raw);
 
   const ModeConst mc = load_mode(p.pp, m, M, act);
 
@@ -166,7 +170,7 @@ __global__ void __launch_bounds__(kBwdThreads) mixer_bwd_summary_kernel(const __
       __syncthreads();
     }
     const TIO(*dyt)[2][kBwdModes] = S.dy[buf];
-    const TIO(*yt)[2][kBwdModes] = S.y[buf];
+    const TIO(*yt)[2][kBwdModes] = S.y[kY ? buf : 0];
     const TokenCtl* ctl = S.ctl[buf];
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
