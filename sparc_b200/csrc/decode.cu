@@ -1,15 +1,19 @@
 // Fused single-step SPARC decode for B200 (sm_100a).
 //
-// One CTA of 512 threads per batch row: the controller projection needs the whole row (a block
-// reduction over `width` columns), then every thread updates its modes (up to four; widths up to
-// 4096). Everything a thread needs that does not depend on the token's controls is loaded and
-// computed first, in flight with the projection: its x values for the write, its old state and
-// its modes' constants (e^nu_log, the rotation e^{i theta}, the write gain's constant part), so
-// after the block reduction only the control-dependent arithmetic remains. Launches carry the
+// Grid (batch, S) of 512-thread CTAs, S = ceil(M / 512): CTA (b, s) updates modes
+// [512 s, 512 s + 512) of batch row b, one mode per thread, so that more CTAs share a step's
+// short latency chain. The controller projection needs the whole row: every CTA of the row
+// computes it (a block reduction over `width` columns; the row is a few KB in L2) instead of
+// exchanging it. Everything a thread needs that does not depend on the token's controls is
+// loaded and computed first, in flight with the projection: its x values for the write, its old
+// state and its mode's constants (e^nu_log, the rotation e^{i theta}, the write gain's constant
+// part), so after the reduction only the control-dependent arithmetic remains, in the same
+// approximations as the sequence kernels (hardware exp2 / reciprocal / square root, the series
+// of the bounded phase offset and of 1 - e^{-2z} for small z, tanh as 1 - 2 / (e^{2x} + 1)): the
+// decode trajectory follows the sequence scan to rounding. Launches carry the
 // programmatic-stream-serialisation attribute, so a step's launch overlaps the previous step's
 // tail (pdl_wait comes first: the previous kernel may write x, the state or the parameters).
-// Parity target: _latest_sparc_decode, forward/decode.py:11-55 (Botwwt/sparc). Decode is
-// latency-bound (a few KB per row), so the accurate libm functions are used throughout.
+// Parity target: _latest_sparc_decode, forward/decode.py:11-55 (Botwwt/sparc).
 #include "common.cuh"
 #include "sparc_b200.h"
 #include "timing.cuh"
@@ -17,7 +21,7 @@
 namespace sparc {
 
 constexpr int kDecodeThreads = 512;
-constexpr int kDecodeModes = 4;  // modes per thread at most (M <= 2048)
+constexpr int kDecodeMaxSplit = 4;  // CTAs per row at most (M <= 2048)
 
 struct DecodeParams {
   const void* x;
@@ -36,33 +40,32 @@ struct DecodeParams {
   int W, M;
 };
 
+__device__ __forceinline__ float tanh_exp(float x) { return fmaf(-2.0f, rcp_approx(ex2_approx(2.0f * kLog2e * x) + 1.0f), 1.0f); }
+
 template <typename TIO>
 __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeParams p) {
   pdl_wait();
   const long long b = blockIdx.x;
   const int W = p.W, M = p.M;
   const int tid = threadIdx.x;
+  const int m = blockIdx.y * kDecodeThreads + tid;
+  const bool act = m < M;
   const TIO* xrow = static_cast<const TIO*>(p.x) + b * W;
 
-  // control-independent work first: the thread's modes' x values, old states and constants
-  float xr[kDecodeModes], xi[kDecodeModes], hr[kDecodeModes], hi[kDecodeModes];
-  float nu[kDecodeModes], ct[kDecodeModes], st[kDecodeModes], gconst[kDecodeModes], den[kDecodeModes];
-  float wpr[kDecodeModes], wrr[kDecodeModes];
-#pragma unroll
-  for (int j = 0; j < kDecodeModes; ++j) {
-    const int m = tid + j * kDecodeThreads;
-    if (m < M) {
-      xr[j] = Io<TIO>::load(xrow + m);
-      xi[j] = Io<TIO>::load(xrow + M + m);
-      hr[j] = p.state_r[b * M + m];
-      hi[j] = p.state_i[b * M + m];
-      nu[j] = expf(p.nu_log[m]);
-      sincosf(expf(p.theta_log[m]), &st[j], &ct[j]);
-      den[j] = expm1f(-2.0f * nu[j]);
-      gconst[j] = expf(p.wlg[m]);
-      wpr[j] = p.wpr[m];
-      wrr[j] = p.wrr[m];
-    }
+  // control-independent work first: the mode's x values, old state and constants
+  float xr = 0.0f, xi = 0.0f, hr = 0.0f, hi = 0.0f, nu = 0.0f, ct = 1.0f, st = 0.0f, gconst = 0.0f, iden = 0.0f;
+  float wpr = 0.0f, wrr = 0.0f;
+  if (act) {
+    xr = Io<TIO>::load(xrow + m);
+    xi = Io<TIO>::load(xrow + M + m);
+    hr = p.state_r[b * M + m];
+    hi = p.state_i[b * M + m];
+    nu = expf(p.nu_log[m]);
+    sincosf(expf(p.theta_log[m]), &st, &ct);
+    iden = 1.0f / -expm1f(-2.0f * nu);
+    gconst = expf(p.wlg[m]);
+    wpr = p.wpr[m];
+    wrr = p.wrr[m];
   }
 
   // controller projection of the row
@@ -96,8 +99,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodePara
       t1 += __shfl_xor_sync(0xffffffffu, t1, o);
     }
     if (lane == 0) {
-      const float tau0 = tanhf(t0 + p.phase_dir[W]);
-      const float tau1 = tanhf(t1 + p.radial_dir[W]);
+      const float tau0 = tanh_accurate(t0 + p.phase_dir[W]);
+      const float tau1 = tanh_accurate(t1 + p.radial_dir[W]);
       ctl[0] = tau0;
       ctl[1] = tau1;
       ctl[2] = kHalfPi * tau0;      // delta
@@ -105,30 +108,29 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodePara
     }
   }
   __syncthreads();
+  if (!act) return;
   const float tau0 = ctl[0], tau1 = ctl[1], delta = ctl[2], E = ctl[3];
+  const float z = nu * E;
+  const float rho = ex2_approx(-kLog2e * z);
+  float s, c;
+  sincos_halfpi(fmaf(-rho, delta, delta), &s, &c);  // rotate e^{i theta} by (1 - rho) delta, |.| <= pi/2
+  const float pc = ct * c - st * s, ps = st * c + ct * s;
+  // 1 - e^{-2z}: its series below u = 2z = 1/4 (no cancellation), else 1 - rho^2
+  const float u = 2.0f * z;
+  const float ser = u * fmaf(fmaf(fmaf(fmaf(fmaf(-1.3888888888888889e-3f, u, 8.3333333333333333e-3f), u,
+                                           -4.1666666666666667e-2f), u, 1.6666666666666667e-1f), u, -0.5f), u, 1.0f);
+  const float num = u < 0.25f ? ser : fmaf(-rho, rho, 1.0f);
+  const float q = fmaf(tau0, wpr, tau1 * wrr);
+  const float gate = 2.0f * rcp_approx(1.0f + ex2_approx(-kLog2e * q));
+  const float gain = gconst * sqrt_approx(num * iden) * gate;
+  const float ar = rho * pc, ai = rho * ps;
+  const float nr = fmaf(ar, hr, fmaf(-ai, hi, gain * tanh_exp(xr)));
+  const float ni = fmaf(ai, hr, fmaf(ar, hi, gain * tanh_exp(xi)));
+  p.new_r[b * M + m] = nr;
+  p.new_i[b * M + m] = ni;
   TIO* yrow = static_cast<TIO*>(p.y) + b * W;
-#pragma unroll
-  for (int j = 0; j < kDecodeModes; ++j) {
-    const int m = tid + j * kDecodeThreads;
-    if (m < M) {
-      const float z = nu[j] * E;
-      const float rho = expf(-z);
-      float s, c;
-      sincosf((1.0f - rho) * delta, &s, &c);  // rotate e^{i theta} by the token's phase offset
-      const float pc = ct[j] * c - st[j] * s, ps = st[j] * c + ct[j] * s;
-      const float ratio = sqrtf(expm1f(-2.0f * z) / den[j]);
-      const float q = tau0 * wpr[j] + tau1 * wrr[j];
-      const float gate = 2.0f / (1.0f + expf(-q));
-      const float gain = gconst[j] * ratio * gate;
-      const float ar = rho * pc, ai = rho * ps;
-      const float nr = fmaf(ar, hr[j], fmaf(-ai, hi[j], gain * tanhf(xr[j])));
-      const float ni = fmaf(ai, hr[j], fmaf(ar, hi[j], gain * tanhf(xi[j])));
-      p.new_r[b * M + m] = nr;
-      p.new_i[b * M + m] = ni;
-      Io<TIO>::store(yrow + m, fmaxf(nr, 0.0f));
-      Io<TIO>::store(yrow + M + m, fmaxf(ni, 0.0f));
-    }
-  }
+  Io<TIO>::store(yrow + m, fmaxf(nr, 0.0f));
+  Io<TIO>::store(yrow + M + m, fmaxf(ni, 0.0f));
 }
 
 }  // namespace sparc
@@ -146,7 +148,7 @@ extern "C" int sparc_decode_step(const SparcDecodeArgs* a, void* stream) {
   if (a->batch <= 0 || a->width <= 0 || a->batch > 0x7fffffffLL)
     return fail(SPARC_ERR_SHAPE, "batch and width must be positive");
   if (a->width % 2) return fail(SPARC_ERR_SHAPE, "SPARC rnn_width must be even");
-  if (a->width / 2 > kDecodeThreads * kDecodeModes) return fail(SPARC_ERR_SHAPE, "width above the decode kernel's limit");
+  if (a->width / 2 > kDecodeThreads * kDecodeMaxSplit) return fail(SPARC_ERR_SHAPE, "width above the decode kernel's limit");
   if (a->new_state_r == a->state_r || a->new_state_i == a->state_i)
     return fail(SPARC_ERR_ARG, "the new state must not alias the old one");
   if (a->dtype != SPARC_DTYPE_BF16 && a->dtype != SPARC_DTYPE_F32) return fail(SPARC_ERR_DTYPE, "unsupported dtype");
@@ -157,7 +159,7 @@ extern "C" int sparc_decode_step(const SparcDecodeArgs* a, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   TimedLaunch tl(kTimeDecode, s);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)a->batch, 1, 1);
+  cfg.gridDim = dim3((unsigned)a->batch, (unsigned)((a->width / 2 + kDecodeThreads - 1) / kDecodeThreads), 1);
   cfg.blockDim = dim3(kDecodeThreads, 1, 1);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
