@@ -92,3 +92,31 @@ def test_operator_autograd_matches_module():
     b2 = b.detach().clone().requires_grad_(True)
     ga2, gb2 = torch.autograd.grad(ops.real_scan_forward(a2, b2)[0], (a2, b2), gr)
     assert torch.allclose(ga2, ga_, rtol=1e-6, atol=1e-6) and torch.allclose(gb2, gb_, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("dtype,W,T", [(torch.float32, 512, 37), (torch.float32, 1024, 100),
+                                       (torch.bfloat16, 2048, 70), (torch.bfloat16, 512, 49)])
+def test_saved_state_and_replaying_gradient_kernels_agree(dtype, W, T):
+    """The gradient kernel that reads the forward's saved states (halves in a two-stage ring
+    without a cluster, whole tiles with the cluster's sums pushed between CTAs at W >= 1024) and
+    the one that replays the states from the chunk carries give the same gradients (float32 to
+    1e-4; bfloat16, whose replayed and saved states are both rounded to bfloat16, to 1e-2),
+    with ragged last chunks."""
+    from sparc_b200 import torch_ops
+
+    ops = torch_ops.load()
+    torch.manual_seed(1)
+    p = [torch.randn(W // 2, device="cuda") * 0.3 - 1.0, torch.randn(W // 2, device="cuda") * 0.3,
+         torch.randn(W + 1, device="cuda") / W ** 0.5, torch.randn(W + 1, device="cuda") / W ** 0.5,
+         torch.randn(W // 2, device="cuda") * 0.1, torch.randn(W // 2, device="cuda") * 0.5,
+         torch.randn(W // 2, device="cuda") * 0.5]
+    x = torch.randn(3, T, W, device="cuda").to(dtype)
+    g = torch.randn(3, T, W, device="cuda").to(dtype)
+    y, lr, li, carry, controls, states = ops.mixer_forward(x, *p)
+    saved = ops.mixer_backward(x, y, g, *p, carry, controls, states)
+    replayed = ops.mixer_backward(x, y, g, *p, carry, controls)
+    tol = 1e-4 if dtype == torch.float32 else 1e-2
+    for k, (s, r) in enumerate(zip(saved, replayed)):
+        s, r = s.double(), r.double()
+        err = ((s - r).norm() / r.norm().clamp_min(1e-30)).item()
+        assert err < tol, (k, err)
