@@ -78,12 +78,17 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def _bf16_peak():
+def _bf16_peak(sustained=False):
+    """Measured dense bf16 TFLOP/s: the burst figure (a product timed alone) or, with `sustained`,
+    the figure of back-to-back products under the power cap (a product inside a long step)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
-            return float(json.load(f)["bf16_tflops"])
-    return 1590.0
+            d = json.load(f)
+        if sustained and "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"])
+        return float(d["bf16_tflops"])
+    return 1400.0 if sustained else 1590.0
 
 
 # Kernels one mixer fwd+bwd launches: fwd summary, carry scan, replay; bwd summary, carry scan,
@@ -823,8 +828,12 @@ def run_projection(args, wl, world, rank, local):
         gms = tot / n
         split = 3 if x.dtype == torch.float32 else 1  # float32 operands: three bf16 terms along k
         tf = 2.0 * 2 * M * W * B * T * split / (gms / 1e3) / 1e12
+        # the products run back to back inside the step (milliseconds long, under the power cap):
+        # the sustained measured peak is the denominator; the burst one is reported beside it
         roofline["tensor"] = {"kernel": "proj_gemm_kernel (+ proj_gemm_finish_kernel)", "ms_per_launch": round(gms, 4),
-                              "TFLOPs": round(tf, 1), "peak_TFLOPs": _bf16_peak(), "frac": round(tf / _bf16_peak(), 4),
+                              "TFLOPs": round(tf, 1), "peak_TFLOPs": _bf16_peak(sustained=True),
+                              "peak_kind": "sustained (measured)", "frac": round(tf / _bf16_peak(sustained=True), 4),
+                              "peak_burst_TFLOPs": _bf16_peak(), "frac_of_burst": round(tf / _bf16_peak(), 4),
                               "flops": "2 x tokens x 2M x W per product" + (" x 3 (bf16 split of float32)" if split == 3 else "")}
     del graph
     # every launch of the library in the timed steps (the colsum entry times its two launches

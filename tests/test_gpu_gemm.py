@@ -12,7 +12,9 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("rows,n,k", [(128, 128, 64), (300, 200, 520), (1000, 64, 64), (16384, 512, 512),
-                                      (7, 9, 8), (4096, 1024, 128)])
+                                      (7, 9, 8), (4096, 1024, 128),
+                                      # several output tiles per CTA (the tensor-memory reuse)
+                                      (65536, 1024, 256), (40000, 777, 136)])
 def test_gemm_matches_torch(rows, n, k):
     from sparc_b200 import gemm
 
@@ -28,10 +30,10 @@ def test_gemm_matches_torch(rows, n, k):
     assert _rel(out16.float(), ref) < 1e-2
 
 
-def test_gemm_fused_terms():
+@pytest.mark.parametrize("rows,n,k", [(777, 320, 192), (30001, 1000, 64)])
+def test_gemm_fused_terms(rows, n, k):
     from sparc_b200 import gemm
 
-    rows, n, k = 777, 320, 192
     g = torch.Generator(device="cuda").manual_seed(0)
     a = torch.randn(rows, k, generator=g, device="cuda").bfloat16()
     b = torch.randn(n, k, generator=g, device="cuda").bfloat16()
