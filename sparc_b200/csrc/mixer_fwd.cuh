@@ -38,7 +38,6 @@ template <typename TIO, int C>
 struct RepSmem {
   TIO x[2][C][2][kFwdModes];
   TokenCtl ctl[2][C];
-  float2 hin[2][kFwdModes];  // carried-in state of the tile's modes
   unsigned long long bar[2];
 };
 
@@ -416,7 +415,6 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
   const bool act0 = m0 < M, act1 = m0 + 1 < M;
   const long long B = p.B, T = p.T;
   const long long k0 = blockIdx.y, nk = gridDim.y;
-  const int ncols = min(kFwdModes, M - mbase);
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   RepSmem<TIO, C>& S = *reinterpret_cast<RepSmem<TIO, C>*>(smem_raw);
@@ -432,24 +430,17 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
   }
   __syncthreads();
 
-  // Tile inputs: x rows, the C token controls and (for c > 0) the carried-in chunk state. With
-  // `carried` false only x and the controls are issued (and the carry is expected), for the first
-  // tile before the wait: x and the controls come from kernels before the carry scan, which have
-  // completed when this kernel starts (see pdl_wait).
-  auto issue_tma = [&](long long i, int buf, bool inputs, bool carried) {  // (thread 0)
+  // Tile inputs in shared memory: x rows and the C token controls (thread 0's copies). The first
+  // tile's go out before the wait: x and the controls come from kernels before the carry scan,
+  // which have completed when this kernel starts (see pdl_wait).
+  auto issue_tma = [&](long long i, int buf) {  // (thread 0)
     const TileRef r = tile_ref(i, B, T, C);
-    const float2* hsrc = r.c > 0 ? p.carry + (r.b * p.chunks + (r.c - 1)) * (long long)M + mbase : nullptr;
-    if (inputs) {
-      fence_proxy_async_smem();
-      unsigned bytes = act_box_bytes<TIO, C, kFwdModes>() + (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid;
-      if (hsrc != nullptr) bytes += (unsigned)ncols * 8u;
-      mbar_arrive_expect_tx(&S.bar[buf], bytes);
-      tma_load_3d(&S.x[buf][0][0][0], &p.map_x, mbase, 0, (int)(r.b * T + r.t0), &S.bar[buf]);
-      bulk_copy_g2s(&S.ctl[buf][0], p.ctl + r.b * T + r.t0, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar[buf]);
-    }
-    if (carried && hsrc != nullptr) bulk_copy_g2s(&S.hin[buf][0], hsrc, (unsigned)ncols * 8u, &S.bar[buf]);
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&S.bar[buf], act_box_bytes<TIO, C, kFwdModes>() + (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid);
+    tma_load_3d(&S.x[buf][0][0][0], &p.map_x, mbase, 0, (int)(r.b * T + r.t0), &S.bar[buf]);
+    bulk_copy_g2s(&S.ctl[buf][0], p.ctl + r.b * T + r.t0, (unsigned)sizeof(TokenCtl) * (unsigned)r.nvalid, &S.bar[buf]);
   };
-  if (p.use_tma && tid == 0 && k0 < p.tiles) issue_tma(k0, 0, true, false);
+  if (p.use_tma && tid == 0 && k0 < p.tiles) issue_tma(k0, 0);
 
   pdl_wait();  // the carries (scan) are complete from here on
 
@@ -457,23 +448,37 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
     const TileRef r = tile_ref(i, B, T, C);
     const TIO* src = static_cast<const TIO*>(p.x) + (r.b * T + r.t0) * W;
     const TokenCtl* csrc = p.ctl + r.b * T + r.t0;
-    const float2* hsrc = r.c > 0 ? p.carry + (r.b * p.chunks + (r.c - 1)) * (long long)M + mbase : nullptr;
     if (p.use_tma) {
-      if (tid == 0) issue_tma(i, buf, true, true);
+      if (tid == 0) issue_tma(i, buf);
     } else {
       load_act_rows<TIO, kFwdModes>(src, W, M, mbase, r.nvalid, S.x[buf], kFwdThreads);
       for (int t = tid; t < r.nvalid; t += kFwdThreads) S.ctl[buf][t] = csrc[t];
-      if (hsrc != nullptr)
-        for (int mm = tid; mm < ncols; mm += kFwdThreads) S.hin[buf][mm] = hsrc[mm];
     }
   };
-  if (k0 < p.tiles) {
-    if (p.use_tma) {
-      if (tid == 0) issue_tma(k0, 0, false, true);  // (x and the controls are on their way)
-    } else {
-      issue(k0, 0);
+  if (k0 < p.tiles && !p.use_tma) issue(k0, 0);
+  // the state carried into tile i at the thread's two modes: the scan's state at the end of the
+  // previous chunk (h0 or zero at chunk 0), loaded straight into registers a tile ahead
+  const bool carry16 = (reinterpret_cast<uintptr_t>(p.carry) & 15u) == 0;
+  auto tile_hin = [&](long long i) -> Cx2 {
+    const TileRef r = tile_ref(i, B, T, C);
+    float2 h0 = make_float2(0.0f, 0.0f), h1 = h0;
+    if (r.c > 0) {
+      const float2* hs = p.carry + (r.b * p.chunks + (r.c - 1)) * (long long)M + m0;
+      if (kVec && act1 && carry16) {  // (M even: the pair starts on a 16-byte boundary)
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(hs));
+        h0 = make_float2(v.x, v.y);
+        h1 = make_float2(v.z, v.w);
+      } else {
+        if (act0) h0 = __ldcg(hs);
+        if (act1) h1 = __ldcg(hs + 1);
+      }
+    } else if (p.h0_r != nullptr) {
+      if (act0) h0 = make_float2(p.h0_r[r.b * M + m0], p.h0_i[r.b * M + m0]);
+      if (act1) h1 = make_float2(p.h0_r[r.b * M + m0 + 1], p.h0_i[r.b * M + m0 + 1]);
     }
-  }
+    return cx2(make_float2(h0.x, h1.x), make_float2(h0.y, h1.y));
+  };
+  Cx2 hin_next = k0 < p.tiles ? tile_hin(k0) : cx2(bcast2(0.0f), bcast2(0.0f));
   bool timed_out = false;
 
   for (long long n = 0;; ++n) {
@@ -481,6 +486,8 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
     if (i >= p.tiles) break;
     const int buf = (int)(n & 1);
     if (i + nk < p.tiles) issue(i + nk, buf ^ 1);
+    Cx2 h = hin_next;
+    if (i + nk < p.tiles) hin_next = tile_hin(i + nk);  // (in flight under this tile)
     const TileRef r = tile_ref(i, B, T, C);
     if (p.use_tma) {
       if (!mbar_wait(&S.bar[buf], (unsigned)((n >> 1) & 1), p.max_spin << 4)) timed_out = true;
@@ -489,15 +496,6 @@ __global__ void __launch_bounds__(kFwdThreads) mixer_fwd_replay_kernel(const __g
     }
     const TIO(*xt)[2][kFwdModes] = S.x[buf];
     const TokenCtl* ctl = S.ctl[buf];
-    float2 h0 = make_float2(0.0f, 0.0f), h1 = h0;
-    if (r.c > 0) {
-      if (act0) h0 = S.hin[buf][2 * tid];
-      if (act1) h1 = S.hin[buf][2 * tid + 1];
-    } else if (p.h0_r != nullptr) {
-      if (act0) h0 = make_float2(p.h0_r[r.b * M + m0], p.h0_i[r.b * M + m0]);
-      if (act1) h1 = make_float2(p.h0_r[r.b * M + m0 + 1], p.h0_i[r.b * M + m0 + 1]);
-    }
-    Cx2 h = cx2(make_float2(h0.x, h1.x), make_float2(h0.y, h1.y));
     TIO* yrow = static_cast<TIO*>(p.y) + (r.b * T + r.t0) * W;
     auto body = [&](auto full_tag) {
       constexpr bool kFull = decltype(full_tag)::value;
